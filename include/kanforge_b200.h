@@ -1,0 +1,165 @@
+/*
+ * kanforge_b200 -- C ABI of the B200 (sm_100a) KAN-layer kernels.
+ *
+ * Every pointer is a device pointer owned by the caller (torch allocates; the
+ * library allocates nothing).  Every compute entry point takes the CUDA stream
+ * to launch on (a cudaStream_t passed as void*), is stream-ordered, never
+ * synchronises the host and returns KF_OK or an error code; kf_last_error()
+ * returns the message of the last failure on the calling thread.  The only
+ * process-wide state is per-device initialisation done once.
+ *
+ * Reference interfaces replaced (fx-xf/kanforge v0.8.0, paths within the project):
+ *   kanforge/torch/kernels.py:19-28    available(device)      -> kf_query
+ *   kanforge/torch/kernels.py:39-55    _raw(op, plan, m, ...) -> kf_prim
+ *   kanforge/kernels/triton_kernels.py:225-242 launch(...)     -> kf_prim
+ *   kanforge/torch/kernels.py:143-150  spline_forward + the SiLU/bias epilogue of
+ *   kanforge/torch/layers.py:177-191   KANLinear.forward      -> kf_pack_coef + kf_fwd
+ *   kanforge/torch/kernels.py:79-87    _F.backward (m = 0)    -> kf_dgrad + kf_wgrad
+ *   kanforge/torch/layers.py:206-226   edge_derivative        -> kf_edge_derivative
+ *   kanforge/bases/rational.py:84-101  Rational._eval (GRKAN) -> kf_rational_act,
+ *                                                               kf_rational_bwd
+ */
+#ifndef KANFORGE_B200_H
+#define KANFORGE_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KF_ABI_VERSION 1
+
+/* status codes */
+#define KF_OK 0
+#define KF_ERR_ARG 1         /* bad argument: null pointer, size, alignment */
+#define KF_ERR_UNSUPPORTED 2 /* basis / order / dtype without a kernel */
+#define KF_ERR_CUDA 3        /* a CUDA runtime call failed */
+#define KF_ERR_DEVICE 4      /* a kernel reported a bounded wait that ran out */
+
+/* basis kinds (kanforge/kernels/plan.py:39-72 plan kinds, plus the rational) */
+#define KF_BASIS_BSPLINE 1   /* native derivative order, per-input grid */
+#define KF_BASIS_CHEB 2      /* Chebyshev features T_j(g(x)), derivatives folded */
+#define KF_BASIS_RATIONAL 3  /* KAT P(x) / (1 + |Q(x)|), per-group parameters */
+
+#define KF_MAP_TANH 0
+#define KF_MAP_IDENTITY 1
+
+#define KF_DTYPE_F32 0
+#define KF_DTYPE_BF16 1
+
+/* primitive ops of the closed family (kanforge/kernels/__init__.py:5-13) */
+#define KF_OP_F 0
+#define KF_OP_G 1
+#define KF_OP_P 2
+
+typedef struct kf_basis_desc {
+  int32_t kind;       /* KF_BASIS_* */
+  int32_t size;       /* basis functions per edge: G+k, d+1, or 1 */
+  int32_t grid_size;  /* B-spline: intervals G */
+  int32_t order;      /* B-spline: spline order k */
+  int32_t degree;     /* Chebyshev: degree d; rational: numerator degree */
+  int32_t den_degree; /* rational: denominator degree */
+  int32_t input_map;  /* Chebyshev: KF_MAP_* */
+  int32_t groups;     /* rational: parameter groups (inputs per group = I / groups) */
+} kf_basis_desc;
+
+/* Library ABI version (KF_ABI_VERSION). */
+int kf_version(void);
+
+/* Message of the last error on this thread ("" if none). */
+const char* kf_last_error(void);
+
+/* 1 if a kernel exists for (basis, op, dtype), else 0.  op: KF_OP_* for the
+ * primitives, 16 = fused fwd/dgrad/wgrad, 17 = edge_derivative.
+ * Replaces available() + plan_for() (kanforge/torch/kernels.py:19-28,
+ * kanforge/kernels/plan.py:104-121). */
+int kf_query(const kf_basis_desc* basis, int op, int dtype);
+
+/* Reads and clears the device-side error word of the current device (set by a
+ * kernel whose bounded wait ran out).  Synchronises the device.  *flags = 0 when
+ * clean. */
+int kf_device_status(int32_t* flags);
+
+/* One launch of the closed primitive family, float32, any derivative order m
+ * (kanforge/torch/kernels.py:39-55, triton_kernels.py:128-191):
+ *   op F: a = w (B,I),  b = c (O,I,nf) -> out (B,O)    = sum_{i,j} w c phi_j^(m)
+ *   op G: a = w (B,I),  b = g (B,O)    -> out (O,I,nf) = sum_b w g phi_j^(m)
+ *   op P: a = g (B,O),  b = c (O,I,nf) -> out (B,I)    = sum_{o,j} g c phi_j^(m)
+ * For KF_BASIS_CHEB the features are T_0..T_{nf-1}(g(x)) and the caller folds
+ * the derivative into c (plan.fold); B-splines evaluate order m natively.
+ * grid: (I, G+1) per-input grids for B-splines, else ignored. */
+int kf_prim(int op, int m, const float* x, const float* a, const float* b, const float* grid, float* out,
+            int64_t B, int32_t I, int32_t O, int32_t nf, const kf_basis_desc* basis, void* stream);
+
+/* Builds the bf16 tensor-core operand of the fused layer kernels:
+ *   packed[o, i, j] = sum_k coef_eff[o,i,k] fold[k,j]   (j < nt; fold = null: j = k)
+ *   packed[o, i, nt] = base_eff[o, i]                   (if base_eff != null)
+ *   zero up to f_pad.
+ * coef_eff (O,I,K), base_eff (O,I) in `dtype`; fold (K, nt) float32 row-major.
+ * packed is (O, I*f_pad) bf16, 16-byte aligned. */
+int kf_pack_coef(const void* coef_eff, const void* base_eff, const float* fold, void* packed,
+                 int32_t O, int32_t I, int32_t K, int32_t nt, int32_t f_pad, int dtype, void* stream);
+
+/* Fused KANLinear forward on tcgen05 (bf16 operands, f32 accumulation):
+ *   y[b,o] = sum_{i,j} feat_j(x[b,i]) packed[o,i,j] + bias[o]
+ * feat = basis features (B-spline values or T_j(g(x))) and, at column nt,
+ * silu(x) when has_base.  x (B,I) bf16, y (B,O) bf16, bias (O) bf16 or null,
+ * grid (I, G+1) float32 for B-splines.  Requires I*f_pad % 64 == 0, O % 16 == 0,
+ * B >= 1.  (kanforge/torch/layers.py:171-192 with kernels.py:143-150.) */
+int kf_fwd(const void* x, const void* packed, const void* bias, const float* grid, void* y, int64_t B,
+           int32_t I, int32_t O, int32_t nt, int32_t f_pad, int32_t has_base, const kf_basis_desc* basis,
+           void* stream);
+
+/* Fused input gradient on tcgen05:
+ *   dx[b,i] = sum_j (sum_o dy[b,o] packed[o,i,j]) dfeat_j(x[b,i])
+ * dfeat = d/dx of the forward features (the SiLU column included).
+ * dy (B,O) bf16, dx (B,I) bf16.  (kanforge/torch/kernels.py:84 gx = w * P_{m+1}.) */
+int kf_dgrad(const void* x, const void* dy, const void* packed, const float* grid, void* dx, int64_t B,
+             int32_t I, int32_t O, int32_t nt, int32_t f_pad, int32_t has_base, const kf_basis_desc* basis,
+             void* stream);
+
+/* Fused coefficient gradient on tcgen05:
+ *   dpacked[o,i,j] = sum_b dy[b,o] feat_j(x[b,i])
+ *   dcoef_eff[o,i,k] = sum_{j<nt} dpacked[o,i,j] fold[k,j]   (fold null: k = j)
+ *   dbase[o,i] = dpacked[o,i,nt]                              (if dbase != null)
+ * dcoef_eff (O,I,K) and dbase (O,I) in bf16.  (kanforge/torch/kernels.py:85, 97-98.) */
+int kf_wgrad(const void* x, const void* dy, const float* grid, const float* fold, void* dcoef_eff,
+             void* dbase, int64_t B, int32_t I, int32_t O, int32_t K, int32_t nt, int32_t f_pad,
+             const kf_basis_desc* basis, void* stream);
+
+/* edge_derivative (kanforge/torch/layers.py:206-226), float32:
+ *   out[b,o,i] = sum_j phi_j^(order)(x[b,i]) coef[o,i,j] + s(x[b,i]) base_eff[o,i]
+ * coef (O,I,nf): for KF_BASIS_CHEB the caller passes coef_eff @ fold(order)
+ * and phi_j = T_j(g(x)); otherwise coef_eff and the native derivative.
+ * s = silu^(order) given by the polynomials h_order(sigma), h_{order-1}(sigma):
+ * silu^(m)(x) = x h_m(s) + m h_{m-1}(s) (kanforge/_calculus.py:90-96), passed as
+ * silu_poly = [h_m coefficients (n_poly) , h_{m-1} coefficients (n_poly)];
+ * base_eff null: no base term.  out (B,O,I). */
+int kf_edge_derivative(const float* x, const float* coef, const float* base_eff, const float* grid,
+                       const float* basis_num, const float* basis_den, float* out, int64_t B, int32_t I,
+                       int32_t O, int32_t nf, int32_t order, const kf_basis_desc* basis,
+                       const float* silu_poly, int32_t n_poly, void* stream);
+
+/* KAT group rational activation and its order-m derivative, elementwise
+ * (kanforge/bases/rational.py:84-101):  out[b,i] = R_g(i)^(m)(x[b,i]).
+ * num (groups, p+1), den (groups, q) float32; x, out in `dtype`. */
+int kf_rational_act(const void* x, const float* num, const float* den, void* out, int64_t B, int32_t I,
+                    int32_t m, const kf_basis_desc* basis, int dtype, void* stream);
+
+/* Backward of the rational activation: dx[b,i] = dr[b,i] R'(x[b,i]) and the
+ * per-group parameter gradients dnum (groups, p+1), dden (groups, q), float32,
+ * reduced deterministically through `workspace` (float32, at least
+ * kf_rational_workspace(B, I, basis) elements). */
+int kf_rational_bwd(const void* x, const void* dr, const float* num, const float* den, void* dx, float* dnum,
+                    float* dden, float* workspace, int64_t B, int32_t I, const kf_basis_desc* basis,
+                    int dtype, void* stream);
+
+/* Workspace (float32 elements) that kf_rational_bwd needs. */
+int64_t kf_rational_workspace(int64_t B, int32_t I, const kf_basis_desc* basis);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KANFORGE_B200_H */

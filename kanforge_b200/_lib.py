@@ -1,0 +1,116 @@
+"""ctypes binding of libkanb200.so (the C ABI declared in include/kanforge_b200.h).
+
+The library is built in-tree by ``kanforge_b200.build``.  Loading fails loudly
+when it is missing: this package has no CPU fallback.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libkanb200.so"
+
+KF_OK = 0
+KF_BASIS_BSPLINE, KF_BASIS_CHEB, KF_BASIS_RATIONAL = 1, 2, 3
+KF_MAP_TANH, KF_MAP_IDENTITY = 0, 1
+KF_DTYPE_F32, KF_DTYPE_BF16 = 0, 1
+KF_OP_F, KF_OP_G, KF_OP_P = 0, 1, 2
+KF_QUERY_FUSED, KF_QUERY_EDGE = 16, 17
+
+_c_i32, _c_i64, _vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p
+
+
+class BasisDesc(ctypes.Structure):
+    """``kf_basis_desc`` (include/kanforge_b200.h)."""
+
+    _fields_ = [
+        ("kind", _c_i32),
+        ("size", _c_i32),
+        ("grid_size", _c_i32),
+        ("order", _c_i32),
+        ("degree", _c_i32),
+        ("den_degree", _c_i32),
+        ("input_map", _c_i32),
+        ("groups", _c_i32),
+    ]
+
+
+# name -> (restype, argtypes)
+PROTOTYPES = {
+    "kf_version": (ctypes.c_int, []),
+    "kf_last_error": (ctypes.c_char_p, []),
+    "kf_query": (ctypes.c_int, [ctypes.POINTER(BasisDesc), ctypes.c_int, ctypes.c_int]),
+    "kf_device_status": (ctypes.c_int, [ctypes.POINTER(_c_i32)]),
+    "kf_prim": (
+        ctypes.c_int,
+        [ctypes.c_int, ctypes.c_int, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i32, _c_i32, _c_i32, ctypes.POINTER(BasisDesc), _vp],
+    ),
+    "kf_pack_coef": (ctypes.c_int, [_vp, _vp, _vp, _vp, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, ctypes.c_int, _vp]),
+    "kf_fwd": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _vp, _vp, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, ctypes.POINTER(BasisDesc), _vp],
+    ),
+    "kf_dgrad": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _vp, _vp, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, ctypes.POINTER(BasisDesc), _vp],
+    ),
+    "kf_wgrad": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, ctypes.POINTER(BasisDesc), _vp],
+    ),
+    "kf_edge_derivative": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, ctypes.POINTER(BasisDesc), _vp, _c_i32, _vp],
+    ),
+    "kf_rational_act": (ctypes.c_int, [_vp, _vp, _vp, _vp, _c_i64, _c_i32, _c_i32, ctypes.POINTER(BasisDesc), ctypes.c_int, _vp]),
+    "kf_rational_bwd": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i32, ctypes.POINTER(BasisDesc), ctypes.c_int, _vp],
+    ),
+    "kf_rational_workspace": (_c_i64, [_c_i64, _c_i32, ctypes.POINTER(BasisDesc)]),
+}
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+def load() -> ctypes.CDLL:
+    """The loaded library (RuntimeError if it was not built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise RuntimeError(
+                    f"{LIB_PATH} is missing: build the sm_100a kernels first (python -m kanforge_b200.build); "
+                    "kanforge_b200 has no CPU fallback"
+                )
+            lib = ctypes.CDLL(str(LIB_PATH))
+            for name, (res, args) in PROTOTYPES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+    return _lib
+
+
+def last_error() -> str:
+    msg = load().kf_last_error()
+    return msg.decode() if msg else ""
+
+
+def call(name: str, *args) -> None:
+    """Call an entry point; a non-zero status becomes RuntimeError with the library's message."""
+    rc = getattr(load(), name)(*args)
+    if rc != KF_OK:
+        raise RuntimeError(f"{name} failed (status {rc}): {last_error()}")
+
+
+def device_status() -> int:
+    """Reads and clears the device error word (synchronises the device)."""
+    flags = _c_i32(0)
+    call("kf_device_status", ctypes.byref(flags))
+    return int(flags.value)

@@ -1,0 +1,1138 @@
+// Fused KANLinear forward / input-gradient / coefficient-gradient kernels on
+// the 5th-generation tensor cores (tcgen05, sm_100a).
+//
+// A KANLinear of basis size K with the SiLU base branch is one contraction
+// over I * F features, F = f_pad >= nt + 1 (kanforge/torch/layers.py:184-186
+// folded together):
+//
+//   FWD   y[b,o]       = sum_{i,j} feat_j(x[b,i]) packed[o,i,j]         M=B    N=O    K=I*F
+//   DGRAD dx[b,i]      = sum_j dfeat_j(x[b,i]) sum_o dy[b,o] packed[o,i,j]  M=B  N=I*F  K=O
+//   WGRAD dpacked[o,i,j] = sum_b feat_j(x[b,i]) dy[b,o]                  M=I*F  N=O    K=B
+//
+// (reference F/G/P closure, kanforge/kernels/__init__.py:5-13, at m = 0 with
+// w = 1; dx is P_1, the coefficient gradient G_0 followed by the fold
+// transpose of kanforge/torch/kernels.py:97-98).
+//
+// The basis operand feat is never written to HBM: producer warps evaluate it
+// from x into shared memory in the canonical 128-byte swizzled K-major layout
+// the tensor core reads, fence it into the async proxy and signal an mbarrier.
+// Coefficients / dy arrive by TMA (no multicast).  One thread issues
+// tcgen05.mma into one of two 128x256 f32 accumulators in tensor memory while
+// the epilogue warps drain the other (persistent CTAs, one per SM).
+//
+// Tiles: BM = 128 rows, BN = 256 columns, BK = 64 bf16 (128 B), 4 stages.
+#include "basis.cuh"
+#include "umma.cuh"
+
+namespace kf {
+
+namespace {
+
+using namespace umma;
+
+constexpr int kBM = 128;
+constexpr int kBN = 256;
+constexpr int kBK = 64;  // bf16 elements per stage row = 128 bytes
+constexpr int kStages = 4;
+constexpr int kATile = kBM * 128;  // 16 KB
+constexpr int kBTile = kBN * 128;  // 32 KB
+constexpr int kTabStride = 64;     // floats per knot/inverse-difference row
+constexpr int kMaxOrder = 5;
+
+struct TileMap {
+  int m_tiles, n_tiles, gm;
+  __device__ __forceinline__ void get(int t, int& m, int& n) const {
+    const int per_super = gm * n_tiles;
+    const int sup = t / per_super, local = t % per_super;
+    const int rows = min(gm, m_tiles - sup * gm);
+    m = sup * gm + local % rows;
+    n = local / rows;
+  }
+  __device__ __forceinline__ int count() const { return m_tiles * n_tiles; }
+};
+
+struct BasisDev {
+  int map;       // KF_MAP_* (Chebyshev)
+  int nt;        // basis feature columns (Chebyshev: T_0..T_{nt-1}; B-spline: size)
+  int has_base;  // SiLU column at index nt
+  int G, nk;     // B-spline grid intervals and extended knots
+  const float* grid;
+};
+
+struct Ctl {
+  uint64_t full_a[kStages];
+  uint64_t full_b[kStages];
+  uint64_t empty[kStages];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+__device__ __forceinline__ void named_bar(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Knot table of one input: row 0 = extended knots t_r (r < nk), row q = 1/(t_{r+q} - t_r).
+template <int BK>
+__device__ __forceinline__ float knot_table_entry(const BasisDev& bd, int i, int q, int r) {
+  const float* g = bd.grid + (size_t)i * (bd.G + 1);
+  if (q == 0) return r < bd.nk ? extended_knot(g, bd.G, BK, r) : 0.0f;
+  if (r > bd.nk - 1 - q) return 0.0f;
+  return 1.0f / (extended_knot(g, bd.G, BK, r + q) - extended_knot(g, bd.G, BK, r));
+}
+
+// Abort path of the TMA thread: wait for the last load issued on every stage
+// (iterations < `issued`) so that no bulk copy targets shared memory after exit.
+__device__ __forceinline__ void drain_tma(Ctl* ctl, int issued) {
+  for (int s = 0; s < kStages; ++s) {
+    int last = issued - 1 - ((issued - 1 - s) % kStages + kStages) % kStages;
+    if (issued <= 0 || last < 0) continue;
+    mbar_drain(&ctl->full_b[s], (last / kStages) & 1);
+  }
+}
+
+// Cox-de Boor / derivative levels of bspline_local (basis.cuh) with the
+// reciprocal knot differences read from the table.
+template <int K>
+__device__ __forceinline__ void bspline_local_tab(float x, const float* tab, int nk, int j, int m, float (&v)[K + 1]) {
+  const float* t = tab;
+#pragma unroll
+  for (int r = 0; r <= K; ++r) v[r] = 0.0f;
+  v[0] = 1.0f;
+#pragma unroll
+  for (int q = 1; q <= K; ++q) {
+    float nv[K + 1];
+    const bool deriv = q > K - m;
+    const float* inv = tab + q * kTabStride;
+#pragma unroll
+    for (int rp = 0; rp <= q; ++rp) {
+      const int r = j - q + rp;
+      const float left = rp >= 1 ? v[rp - 1] : 0.0f;
+      const float right = rp <= q - 1 ? v[rp] : 0.0f;
+      float out = 0.0f;
+      if (r >= 0 && r <= nk - 2 - q) {
+        const float i1 = inv[r], i2 = inv[r + 1];
+        out = deriv ? (float)q * (left * i1 - right * i2) : (x - t[r]) * i1 * left + (t[r + q + 1] - x) * i2 * right;
+      }
+      nv[rp] = out;
+    }
+#pragma unroll
+    for (int rp = 0; rp <= K; ++rp) v[rp] = rp <= q ? nv[rp] : 0.0f;
+  }
+}
+
+// Chebyshev feature row of one input, F values.
+template <int F>
+__device__ __forceinline__ void cheb_row(float x, const BasisDev& bd, float (&f)[F]) {
+  const float z = bd.map == KF_MAP_TANH ? tanh_exp(x) : x;
+  float tm2 = 1.0f, tm1 = z;
+  f[0] = 1.0f;
+  f[1] = bd.nt > 1 ? z : 0.0f;
+#pragma unroll
+  for (int j = 2; j < F; ++j) {
+    const float tj = 2.0f * z * tm1 - tm2;
+    f[j] = j < bd.nt ? tj : 0.0f;
+    tm2 = tm1;
+    tm1 = tj;
+  }
+  if (bd.has_base) {
+    const float s = silu_fast(x);
+#pragma unroll
+    for (int j = 0; j < F; ++j)
+      if (j == bd.nt) f[j] = s;
+  }
+}
+
+// d/dx of the Chebyshev feature row: j U_{j-1}(z) g'(x), and silu' at nt.
+template <int F>
+__device__ __forceinline__ void cheb_drow(float x, const BasisDev& bd, float (&f)[F]) {
+  float z, gp;
+  if (bd.map == KF_MAP_TANH) {
+    z = tanhf(x);
+    gp = 1.0f - z * z;
+  } else {
+    z = x;
+    gp = 1.0f;
+  }
+  float um2 = 0.0f, um1 = 1.0f;  // U_{-1} = 0, U_0 = 1
+  f[0] = 0.0f;
+#pragma unroll
+  for (int j = 1; j < F; ++j) {
+    f[j] = j < bd.nt ? (float)j * um1 * gp : 0.0f;
+    const float u = 2.0f * z * um1 - um2;
+    um2 = um1;
+    um1 = u;
+  }
+  if (bd.has_base) {
+    const float ds = dsilu_acc(x);
+#pragma unroll
+    for (int j = 0; j < F; ++j)
+      if (j == bd.nt) f[j] = ds;
+  }
+}
+
+// ===========================================================================
+// FWD
+// ===========================================================================
+
+struct FwdParams {
+  const __nv_bfloat16* x;
+  const __nv_bfloat16* bias;
+  __nv_bfloat16* y;
+  int64_t B;
+  int I, O;
+  int k_steps;
+  TileMap tiles;
+  BasisDev bd;
+};
+
+constexpr int kFwdThreads = 512;  // w0 TMA, w1 MMA, w4-7 epilogue, w8-15 producers (2 groups)
+
+template <int BK, int F>
+__global__ void __launch_bounds__(kFwdThreads, 1) fused_fwd_kernel(const __grid_constant__ CUtensorMap tmap_c, FwdParams p) {
+  constexpr int IPK = kBK / F;  // inputs per K-step
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = align1024(smem_raw);
+  uint8_t* sa = base;                                   // kStages x 16 KB
+  uint8_t* sb = sa + kStages * kATile;                  // kStages x 32 KB
+  Ctl* ctl = reinterpret_cast<Ctl*>(sb + kStages * kBTile);
+  float* tabs = reinterpret_cast<float*>(ctl + 1);      // B-spline: [group][buf][IPK][(BK+1) * 64]
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  volatile int* abort = &ctl->abort;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&ctl->full_a[s], 4);
+      mbar_init(&ctl->full_b[s], 1);
+      mbar_init(&ctl->empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&ctl->acc_full[a], 1);
+      mbar_init(&ctl->acc_empty[a], 4);
+    }
+    mbar_init(&ctl->drain, 1);
+    ctl->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&ctl->tmem_base, 512);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) prefetch_tmap(&tmap_c);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+  const int n_tiles = p.tiles.count();
+
+  if (warp == 0) {
+    // ---------------- TMA producer: coefficient tiles ----------------
+    if (lane == 0) {
+      int it = 0;
+      for (int t = blockIdx.x; t < n_tiles && !*abort; t += gridDim.x) {
+        int m, n;
+        p.tiles.get(t, m, n);
+        for (int k = 0; k < p.k_steps; ++k, ++it) {
+          const int s = it % kStages;
+          const uint32_t ph = (it / kStages) & 1;
+          if (!mbar_wait(&ctl->empty[s], ph ^ 1, abort)) break;
+          mbar_arrive_expect_tx(&ctl->full_b[s], kBTile);
+          tma_load_2d(sb + s * kBTile, &tmap_c, &ctl->full_b[s], k * kBK, n * kBN);
+        }
+      }
+      if (*abort) drain_tma(ctl, it);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(kBM, kBN, false, false);
+      int it = 0, tc = 0;
+      for (int t = blockIdx.x; t < n_tiles && !*abort; t += gridDim.x, ++tc) {
+        const int acc = tc & 1;
+        if (!mbar_wait(&ctl->acc_empty[acc], ((tc >> 1) & 1) ^ 1, abort)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + acc * kBN;
+        bool ok = true;
+        for (int k = 0; k < p.k_steps; ++k, ++it) {
+          const int s = it % kStages;
+          const uint32_t ph = (it / kStages) & 1;
+          if (!mbar_wait(&ctl->full_a[s], ph, abort) || !mbar_wait(&ctl->full_b[s], ph, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sa + s * kATile), b0 = smem_u32(sb + s * kBTile);
+#pragma unroll
+          for (int j = 0; j < kBK / 16; ++j) {
+            mma_bf16(d_tmem, smem_desc_sw128(a0 + 32 * j, 16, 1024), smem_desc_sw128(b0 + 32 * j, 16, 1024), idesc,
+                     (k > 0 || j > 0) ? 1u : 0u);
+          }
+          mma_commit(&ctl->empty[s]);
+        }
+        if (!ok) break;
+        mma_commit(&ctl->acc_full[acc]);
+      }
+      if (*abort) {
+        mma_commit(&ctl->drain);
+        mbar_drain(&ctl->drain, 0);
+      }
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // ---------------- epilogue: TMEM -> +bias -> bf16 -> y ----------------
+    const int q = warp - 4;
+    const int row = q * 32 + lane;
+    int tc = 0;
+    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++tc) {
+      int m, n;
+      p.tiles.get(t, m, n);
+      const int acc = tc & 1;
+      if (!mbar_wait_warp(&ctl->acc_full[acc], (tc >> 1) & 1, abort)) break;
+      tc_fence_after();
+      const int64_t b = (int64_t)m * kBM + row;
+      const int o_base = n * kBN;
+#pragma unroll 1
+      for (int c = 0; c < kBN / 32; ++c) {
+        float v[32];
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + acc * kBN + c * 32, v);
+        if (c == kBN / 32 - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&ctl->acc_empty[acc]);
+        }
+        const int o0 = o_base + c * 32;
+        if (b < p.B && o0 < p.O) {
+          if (p.bias) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] += (o0 + j < p.O) ? __bfloat162float(p.bias[o0 + j]) : 0.0f;
+          }
+          __nv_bfloat16* dst = p.y + b * p.O + o0;
+          if (o0 + 32 <= p.O) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              uint4 pk;
+              pk.x = pack_bf16x2(v[8 * u + 0], v[8 * u + 1]);
+              pk.y = pack_bf16x2(v[8 * u + 2], v[8 * u + 3]);
+              pk.z = pack_bf16x2(v[8 * u + 4], v[8 * u + 5]);
+              pk.w = pack_bf16x2(v[8 * u + 6], v[8 * u + 7]);
+              *reinterpret_cast<uint4*>(dst + 8 * u) = pk;
+            }
+          } else {
+            for (int j = 0; j < 32 && o0 + j < p.O; ++j) dst[j] = __float2bfloat16_rn(v[j]);
+          }
+        }
+      }
+    }
+  } else if (warp >= 8) {
+    // ---------------- feature producers: x -> basis rows in smem ----------------
+    const int grp = (warp - 8) / 4;        // handles K-steps of parity grp
+    const int row = ((warp - 8) % 4) * 32 + lane;
+    const int gtid = (warp - 8) % 4 * 32 + lane;  // 0..127 inside the group
+    int it = 0, local_step = 0;
+    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {  // abort is seen (uniformly) by the waits
+      int m, n;
+      p.tiles.get(t, m, n);
+      const int64_t b = (int64_t)m * kBM + row;
+      const bool row_ok = b < p.B;
+      const __nv_bfloat16* xrow = p.x + (row_ok ? b : 0) * p.I;
+      for (int k = 0; k < p.k_steps; ++k, ++it) {
+        if ((it & 1) != grp) continue;
+        const int s = it % kStages;
+        const uint32_t ph = (it / kStages) & 1;
+        const int i0 = k * IPK;
+        // x values of this row for the IPK inputs of the step
+        float xv[IPK];
+#pragma unroll
+        for (int u = 0; u < IPK; ++u) xv[u] = (row_ok && i0 + u < p.I) ? __bfloat162float(xrow[i0 + u]) : 0.0f;
+        float* tab = nullptr;
+        if constexpr (BK > 0) {
+          tab = tabs + ((grp * 2 + (local_step & 1)) * IPK) * ((BK + 1) * kTabStride);
+          const int per_in = (BK + 1) * kTabStride;
+          for (int e = gtid; e < IPK * per_in; e += 128) {
+            const int u = e / per_in, rem = e % per_in;
+            const int qq = rem / kTabStride, r = rem % kTabStride;
+            tab[e] = (i0 + u < p.I && r < p.bd.nk) ? knot_table_entry<BK>(p.bd, i0 + u, qq, r) : 0.0f;
+          }
+        }
+        ++local_step;
+        bool ok = mbar_wait_warp(&ctl->empty[s], ph ^ 1, abort);
+        // B-spline: the group barrier publishes the tables and makes the exit decision common
+        if constexpr (BK > 0) ok = named_bar_and(1 + grp, 128, ok);
+        if (!ok) break;
+        uint8_t* arow = sa + s * kATile;
+        if constexpr (BK == 0) {
+#pragma unroll
+          for (int u = 0; u < IPK; ++u) {
+            float f[F];
+            cheb_row<F>(xv[u], p.bd, f);
+            if (i0 + u >= p.I) {
+#pragma unroll
+              for (int j = 0; j < F; ++j) f[j] = 0.0f;
+            }
+#pragma unroll
+            for (int c = 0; c < F / 8; ++c) {
+              uint4 pk;
+              pk.x = pack_bf16x2(f[8 * c + 0], f[8 * c + 1]);
+              pk.y = pack_bf16x2(f[8 * c + 2], f[8 * c + 3]);
+              pk.z = pack_bf16x2(f[8 * c + 4], f[8 * c + 5]);
+              pk.w = pack_bf16x2(f[8 * c + 6], f[8 * c + 7]);
+              *reinterpret_cast<uint4*>(arow + sw128_offset(row, u * (F / 8) + c)) = pk;
+            }
+          }
+        } else {
+#pragma unroll
+          for (int u = 0; u < IPK; ++u) {
+            // zero the input's F columns, then scatter the BK+1 supported splines and silu
+#pragma unroll
+            for (int c = 0; c < F / 8; ++c) *reinterpret_cast<uint4*>(arow + sw128_offset(row, u * (F / 8) + c)) = make_uint4(0, 0, 0, 0);
+            if (i0 + u >= p.I) continue;
+            const float* tu = tab + u * ((BK + 1) * kTabStride);
+            const int j0 = knot_interval(xv[u], tu, p.bd.nk);
+            if (j0 >= 0) {
+              float v[BK + 1];
+              bspline_local_tab<BK>(xv[u], tu, p.bd.nk, j0, 0, v);
+#pragma unroll
+              for (int rp = 0; rp <= BK; ++rp) {
+                const int r = j0 - BK + rp;
+                if (r >= 0 && r < p.bd.nt) {
+                  const int col = u * F + r;
+                  *reinterpret_cast<__nv_bfloat16*>(arow + sw128_offset(row, col >> 3) + (col & 7) * 2) = __float2bfloat16_rn(v[rp]);
+                }
+              }
+            }
+            if (p.bd.has_base) {
+              const int col = u * F + p.bd.nt;
+              *reinterpret_cast<__nv_bfloat16*>(arow + sw128_offset(row, col >> 3) + (col & 7) * 2) = __float2bfloat16_rn(silu_fast(xv[u]));
+            }
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ctl->full_a[s]);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ===========================================================================
+// DGRAD
+// ===========================================================================
+
+struct DgradParams {
+  const __nv_bfloat16* x;
+  __nv_bfloat16* dx;
+  int64_t B;
+  int I, O;
+  int k_steps;
+  TileMap tiles;
+  BasisDev bd;
+};
+
+constexpr int kDgradThreads = 256;  // w0 TMA, w1 MMA, w4-7 epilogue
+
+template <int BK, int F>
+__global__ void __launch_bounds__(kDgradThreads, 1) fused_dgrad_kernel(const __grid_constant__ CUtensorMap tmap_dy,
+                                                                       const __grid_constant__ CUtensorMap tmap_c, DgradParams p) {
+  constexpr int IPT = kBN / F;  // inputs per tile
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = align1024(smem_raw);
+  uint8_t* sa = base;
+  uint8_t* sb = sa + kStages * kATile;
+  Ctl* ctl = reinterpret_cast<Ctl*>(sb + kStages * kBTile);
+  float* tabs = reinterpret_cast<float*>(ctl + 1);      // B-spline knots: [IPT][64]
+  float* stage = tabs + IPT * kTabStride;               // B-spline: per-warp [32][33]
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  volatile int* abort = &ctl->abort;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&ctl->full_a[s], 1);
+      mbar_init(&ctl->full_b[s], 1);
+      mbar_init(&ctl->empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&ctl->acc_full[a], 1);
+      mbar_init(&ctl->acc_empty[a], 4);
+    }
+    mbar_init(&ctl->drain, 1);
+    ctl->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&ctl->tmem_base, 512);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmap_dy);
+    prefetch_tmap(&tmap_c);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+  const int n_tiles = p.tiles.count();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int it = 0;
+      for (int t = blockIdx.x; t < n_tiles && !*abort; t += gridDim.x) {
+        int m, n;
+        p.tiles.get(t, m, n);
+        for (int k = 0; k < p.k_steps; ++k, ++it) {
+          const int s = it % kStages;
+          const uint32_t ph = (it / kStages) & 1;
+          if (!mbar_wait(&ctl->empty[s], ph ^ 1, abort)) break;
+          mbar_arrive_expect_tx(&ctl->full_b[s], kATile + kBTile);
+          // A: dy rows m*128.., K = o (K-major, 128 x 64)
+          tma_load_2d(sa + s * kATile, &tmap_dy, &ctl->full_b[s], k * kBK, m * kBM);
+          // B: packed[o, n*256 + 0..255] as N-major (MN-major) 64 x 64 boxes
+#pragma unroll
+          for (int c = 0; c < kBN / 64; ++c)
+            tma_load_2d(sb + s * kBTile + c * 8192, &tmap_c, &ctl->full_b[s], n * kBN + c * 64, k * kBK);
+        }
+      }
+      if (*abort) drain_tma(ctl, it);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(kBM, kBN, false, true);
+      int it = 0, tc = 0;
+      for (int t = blockIdx.x; t < n_tiles && !*abort; t += gridDim.x, ++tc) {
+        const int acc = tc & 1;
+        if (!mbar_wait(&ctl->acc_empty[acc], ((tc >> 1) & 1) ^ 1, abort)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + acc * kBN;
+        bool ok = true;
+        for (int k = 0; k < p.k_steps; ++k, ++it) {
+          const int s = it % kStages;
+          const uint32_t ph = (it / kStages) & 1;
+          if (!mbar_wait(&ctl->full_b[s], ph, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sa + s * kATile), b0 = smem_u32(sb + s * kBTile);
+#pragma unroll
+          for (int j = 0; j < kBK / 16; ++j) {
+            mma_bf16(d_tmem, smem_desc_sw128(a0 + 32 * j, 16, 1024), smem_desc_sw128(b0 + 2048 * j, 8192, 1024), idesc,
+                     (k > 0 || j > 0) ? 1u : 0u);
+          }
+          mma_commit(&ctl->empty[s]);
+        }
+        if (!ok) break;
+        mma_commit(&ctl->acc_full[acc]);
+      }
+      if (*abort) {
+        mma_commit(&ctl->drain);
+        mbar_drain(&ctl->drain, 0);
+      }
+    }
+  } else if (warp >= 4) {
+    const int q = warp - 4;
+    const int row = q * 32 + lane;
+    const int etid = q * 32 + lane;
+    float* wst = stage + q * (32 * 33);
+    int tc = 0;
+    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++tc) {
+      int m, n;
+      p.tiles.get(t, m, n);
+      const int i_base = n * IPT;
+      const int acc = tc & 1;
+      bool ok = mbar_wait_warp(&ctl->acc_full[acc], (tc >> 1) & 1, abort);
+      if constexpr (BK > 0) {
+        // all four warps are past the previous tile (its table readers are done) and agree
+        ok = named_bar_and(1, 128, ok);
+        if (ok) {
+          for (int e = etid; e < IPT * kTabStride; e += 128) {
+            const int u = e / kTabStride, r = e % kTabStride;
+            tabs[e] = (i_base + u < p.I && r < p.bd.nk) ? knot_table_entry<BK>(p.bd, i_base + u, 0, r) : 0.0f;
+          }
+        }
+        named_bar(1, 128);
+      }
+      if (!ok) break;
+      tc_fence_after();
+      const int64_t b = (int64_t)m * kBM + row;
+      const bool row_ok = b < p.B;
+      float dxv[IPT];
+#pragma unroll 1
+      for (int c = 0; c < kBN / 32; ++c) {
+        float v[32];
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + acc * kBN + c * 32, v);
+        if (c == kBN / 32 - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&ctl->acc_empty[acc]);
+        }
+        if constexpr (BK == 0) {
+#pragma unroll
+          for (int h = 0; h < 32 / F + (F > 32 ? 1 : 0); ++h) {
+            // F == 16: two inputs per chunk; F == 32: one input per chunk
+            const int u = (c * 32) / F + h;
+            const int i = i_base + u;
+            float xval = (row_ok && i < p.I) ? __bfloat162float(p.x[b * p.I + i]) : 0.0f;
+            float df[F];
+            cheb_drow<F>(xval, p.bd, df);
+            float s = 0.0f;
+#pragma unroll
+            for (int j = 0; j < F; ++j) s = fmaf(v[h * F + j], df[j], s);
+#pragma unroll
+            for (int uu = 0; uu < IPT; ++uu)
+              if (uu == u) dxv[uu] = s;
+          }
+        } else {
+          // stage the 32 columns of this row, then dot with the local derivative window
+#pragma unroll
+          for (int j = 0; j < 32; ++j) wst[lane * 33 + j] = v[j];
+          __syncwarp();
+#pragma unroll
+          for (int h = 0; h < 32 / F; ++h) {
+            const int u = (c * 32) / F + h;
+            const int i = i_base + u;
+            float s = 0.0f;
+            if (row_ok && i < p.I) {
+              const float xval = __bfloat162float(p.x[b * p.I + i]);
+              const float* tu = tabs + u * kTabStride;
+              const int j0 = knot_interval(xval, tu, p.bd.nk);
+              if (j0 >= 0) {
+                float dv[BK + 1];
+                // reference derivative step with plain division (spline.py:86-91)
+                bspline_local<BK>(xval, tu, p.bd.nk, j0, 1, dv);
+#pragma unroll
+                for (int rp = 0; rp <= BK; ++rp) {
+                  const int r = j0 - BK + rp;
+                  if (r >= 0 && r < p.bd.nt) s = fmaf(wst[lane * 33 + h * F + r], dv[rp], s);
+                }
+              }
+              if (p.bd.has_base) s = fmaf(wst[lane * 33 + h * F + p.bd.nt], dsilu_acc(xval), s);
+            }
+#pragma unroll
+            for (int uu = 0; uu < IPT; ++uu)
+              if (uu == u) dxv[uu] = s;
+          }
+          __syncwarp();
+        }
+      }
+      if (row_ok) {
+        __nv_bfloat16* dst = p.dx + b * p.I + i_base;
+        if (i_base + IPT <= p.I && (p.I % 8) == 0) {
+#pragma unroll
+          for (int u = 0; u < IPT / 8; ++u) {
+            uint4 pk;
+            pk.x = pack_bf16x2(dxv[8 * u + 0], dxv[8 * u + 1]);
+            pk.y = pack_bf16x2(dxv[8 * u + 2], dxv[8 * u + 3]);
+            pk.z = pack_bf16x2(dxv[8 * u + 4], dxv[8 * u + 5]);
+            pk.w = pack_bf16x2(dxv[8 * u + 6], dxv[8 * u + 7]);
+            *reinterpret_cast<uint4*>(dst + 8 * u) = pk;
+          }
+        } else {
+#pragma unroll
+          for (int u = 0; u < IPT; ++u)
+            if (i_base + u < p.I) dst[u] = __float2bfloat16_rn(dxv[u]);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ===========================================================================
+// WGRAD
+// ===========================================================================
+
+struct WgradParams {
+  const __nv_bfloat16* x;
+  const float* fold;     // (K, nt) or null
+  __nv_bfloat16* dcoef;  // (O, I, K)
+  __nv_bfloat16* dbase;  // (O, I) or null
+  int64_t B;
+  int I, O, K;
+  int k_steps;
+  TileMap tiles;
+  BasisDev bd;
+};
+
+constexpr int kWgradThreads = 512;  // w0 TMA, w1 MMA, w4-7 epilogue, w8-15 producers
+
+template <int BK, int F>
+__global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __grid_constant__ CUtensorMap tmap_dy, WgradParams p) {
+  constexpr int IPT = kBM / F;  // inputs per tile (rows of the feature operand)
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = align1024(smem_raw);
+  uint8_t* sa = base;
+  uint8_t* sb = sa + kStages * kATile;
+  Ctl* ctl = reinterpret_cast<Ctl*>(sb + kStages * kBTile);
+  float* stg = reinterpret_cast<float*>(ctl + 1);   // epilogue staging [128][33]
+  float* tabs = stg + 128 * 33;                      // B-spline: per producer warp [(BK+1) * 64]
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  volatile int* abort = &ctl->abort;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&ctl->full_a[s], 8);
+      mbar_init(&ctl->full_b[s], 1);
+      mbar_init(&ctl->empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&ctl->acc_full[a], 1);
+      mbar_init(&ctl->acc_empty[a], 4);
+    }
+    mbar_init(&ctl->drain, 1);
+    ctl->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&ctl->tmem_base, 512);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) prefetch_tmap(&tmap_dy);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+  const int n_tiles = p.tiles.count();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int it = 0;
+      for (int t = blockIdx.x; t < n_tiles && !*abort; t += gridDim.x) {
+        int m, n;
+        p.tiles.get(t, m, n);
+        for (int k = 0; k < p.k_steps; ++k, ++it) {
+          const int s = it % kStages;
+          const uint32_t ph = (it / kStages) & 1;
+          if (!mbar_wait(&ctl->empty[s], ph ^ 1, abort)) break;
+          mbar_arrive_expect_tx(&ctl->full_b[s], kBTile);
+#pragma unroll
+          for (int c = 0; c < kBN / 64; ++c)
+            tma_load_2d(sb + s * kBTile + c * 8192, &tmap_dy, &ctl->full_b[s], n * kBN + c * 64, k * kBK);
+        }
+      }
+      if (*abort) drain_tma(ctl, it);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(kBM, kBN, false, true);
+      int it = 0, tc = 0;
+      for (int t = blockIdx.x; t < n_tiles && !*abort; t += gridDim.x, ++tc) {
+        const int acc = tc & 1;
+        if (!mbar_wait(&ctl->acc_empty[acc], ((tc >> 1) & 1) ^ 1, abort)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + acc * kBN;
+        bool ok = true;
+        for (int k = 0; k < p.k_steps; ++k, ++it) {
+          const int s = it % kStages;
+          const uint32_t ph = (it / kStages) & 1;
+          if (!mbar_wait(&ctl->full_a[s], ph, abort) || !mbar_wait(&ctl->full_b[s], ph, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sa + s * kATile), b0 = smem_u32(sb + s * kBTile);
+#pragma unroll
+          for (int j = 0; j < kBK / 16; ++j) {
+            mma_bf16(d_tmem, smem_desc_sw128(a0 + 32 * j, 16, 1024), smem_desc_sw128(b0 + 2048 * j, 8192, 1024), idesc,
+                     (k > 0 || j > 0) ? 1u : 0u);
+          }
+          mma_commit(&ctl->empty[s]);
+        }
+        if (!ok) break;
+        mma_commit(&ctl->acc_full[acc]);
+      }
+      if (*abort) {
+        mma_commit(&ctl->drain);
+        mbar_drain(&ctl->drain, 0);
+      }
+    }
+  } else if (warp >= 4 && warp < 8) {
+    const int q = warp - 4;
+    const int mrow = q * 32 + lane;  // feature row (il, f) of this thread
+    const int etid = mrow;
+    int tc = 0;
+    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++tc) {
+      int m, n;
+      p.tiles.get(t, m, n);
+      const int i_base = m * IPT;
+      const int acc = tc & 1;
+      bool ok = mbar_wait_warp(&ctl->acc_full[acc], (tc >> 1) & 1, abort);
+      if (!named_bar_and(1, 128, ok)) break;  // the four epilogue warps leave together
+      tc_fence_after();
+#pragma unroll 1
+      for (int c = 0; c < kBN / 32; ++c) {
+        float v[32];
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + acc * kBN + c * 32, v);
+        if (c == kBN / 32 - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&ctl->acc_empty[acc]);
+        }
+        named_bar(1, 128);  // staging free
+#pragma unroll
+        for (int j = 0; j < 32; ++j) stg[mrow * 33 + j] = v[j];
+        named_bar(1, 128);
+        // 32 outputs x IPT inputs, 128 threads
+        for (int pr = etid; pr < 32 * IPT; pr += 128) {
+          const int ol = pr % 32, u = pr / 32;
+          const int o = n * kBN + c * 32 + ol;
+          const int i = i_base + u;
+          if (o >= p.O || i >= p.I) continue;
+          const float* dcol = stg + (u * F) * 33 + ol;  // dpacked[o, i, j] = dcol[j * 33]
+          __nv_bfloat16* dst = p.dcoef + ((int64_t)o * p.I + i) * p.K;
+          if (p.fold) {
+            for (int kk = 0; kk < p.K; ++kk) {
+              float s = 0.0f;
+              for (int j = 0; j < p.bd.nt; ++j) s = fmaf(dcol[j * 33], __ldg(p.fold + kk * p.bd.nt + j), s);
+              dst[kk] = __float2bfloat16_rn(s);
+            }
+          } else {
+            for (int kk = 0; kk < p.K; ++kk) dst[kk] = __float2bfloat16_rn(dcol[kk * 33]);
+          }
+          if (p.dbase) p.dbase[(int64_t)o * p.I + i] = __float2bfloat16_rn(dcol[p.bd.nt * 33]);
+        }
+      }
+    }
+  } else if (warp >= 8) {
+    // producers: warp w handles input u = w - 8 of the tile's IPT inputs (F == 16: 8 inputs)
+    const int pw = warp - 8;
+    float* tab = tabs + pw * ((BK + 1) * kTabStride);
+    int it = 0;
+    bool alive = true;
+    for (int t = blockIdx.x; t < n_tiles && alive; t += gridDim.x) {  // abort is seen (uniformly) by the waits
+      int m, n;
+      p.tiles.get(t, m, n);
+      const int i_base = m * IPT;
+      if constexpr (BK > 0) {
+        __syncwarp();
+        if (pw < IPT) {
+          const int i = i_base + pw;
+          for (int e = lane; e < (BK + 1) * kTabStride; e += 32) {
+            const int qq = e / kTabStride, r = e % kTabStride;
+            tab[e] = (i < p.I && r < p.bd.nk) ? knot_table_entry<BK>(p.bd, i, qq, r) : 0.0f;
+          }
+        }
+        __syncwarp();
+      }
+      for (int k = 0; k < p.k_steps; ++k, ++it) {
+        const int s = it % kStages;
+        const uint32_t ph = (it / kStages) & 1;
+        // rows (inputs, features) handled by this warp: F == 16 -> warp pw owns input pw;
+        // F == 32 -> 4 inputs, warps 2u and 2u+1 split the 64 batch columns.
+        const int u = (F == 16) ? pw : pw / 2;
+        const int bsub = (F == 16) ? lane * 2 : (pw % 2) * 32 + lane;  // first batch column
+        const int nb = (F == 16) ? 2 : 1;
+        const int i = i_base + u;
+        float xv[2] = {0.0f, 0.0f};
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const int64_t b = (int64_t)k * kBK + bsub + r;
+          if (r < nb && b < p.B && i < p.I) xv[r] = __bfloat162float(p.x[b * p.I + i]);
+        }
+        if (!mbar_wait_warp(&ctl->empty[s], ph ^ 1, abort)) {
+          alive = false;
+          break;
+        }
+        uint8_t* at = sa + s * kATile;
+        float f[2][F];
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const int64_t b = (int64_t)k * kBK + bsub + r;
+          const bool ok = r < nb && b < p.B && i < p.I;
+#pragma unroll
+          for (int j = 0; j < F; ++j) f[r][j] = 0.0f;
+          if (!ok) continue;
+          if constexpr (BK == 0) {
+            cheb_row<F>(xv[r], p.bd, f[r]);
+          } else {
+            const int j0 = knot_interval(xv[r], tab, p.bd.nk);
+            float vv[BK + 1];
+#pragma unroll
+            for (int rp = 0; rp <= BK; ++rp) vv[rp] = 0.0f;
+            if (j0 >= 0) bspline_local_tab<BK>(xv[r], tab, p.bd.nk, j0, 0, vv);
+#pragma unroll
+            for (int j = 0; j < F; ++j) {
+              float val = 0.0f;
+#pragma unroll
+              for (int rp = 0; rp <= BK; ++rp)
+                if (j == j0 - BK + rp) val = vv[rp];
+              f[r][j] = j < p.bd.nt ? val : 0.0f;
+            }
+            if (p.bd.has_base) {
+              const float sv = silu_fast(xv[r]);
+#pragma unroll
+              for (int j = 0; j < F; ++j)
+                if (j == p.bd.nt) f[r][j] = sv;
+            }
+          }
+        }
+        // A[m = u*F + j][k = bsub (+1)]: K-major swizzled rows
+#pragma unroll
+        for (int j = 0; j < F; ++j) {
+          const int mr = u * F + j;
+          if (nb == 2) {
+            const uint32_t off = sw128_offset(mr, bsub >> 3) + (bsub & 7) * 2;
+            *reinterpret_cast<uint32_t*>(at + off) = pack_bf16x2(f[0][j], f[1][j]);
+          } else {
+            const uint32_t off = sw128_offset(mr, bsub >> 3) + (bsub & 7) * 2;
+            *reinterpret_cast<__nv_bfloat16*>(at + off) = __float2bfloat16_rn(f[0][j]);
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ctl->full_a[s]);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ===========================================================================
+// host side
+// ===========================================================================
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// 2-D bf16 tensor map: `rows` x `cols` row-major (cols contiguous), box box_cols x box_rows, 128-byte swizzle.
+int make_tmap_bf16(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int box_cols, int box_rows) {
+  auto enc = get_encode();
+  if (!enc) {
+    set_error("cuTensorMapEncodeTiled is not available from the driver");
+    return KF_ERR_CUDA;
+  }
+  KF_CHECK_ARG(((uintptr_t)ptr % 16) == 0, "TMA operand must be 16-byte aligned");
+  KF_CHECK_ARG((cols * 2) % 16 == 0, "TMA operand row pitch (%lld bf16) must be a multiple of 16 bytes", (long long)cols);
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(cols * 2)};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d) for %lldx%lld box %dx%d", (int)r, (long long)rows, (long long)cols,
+              box_rows, box_cols);
+    return KF_ERR_CUDA;
+  }
+  return KF_OK;
+}
+
+int sm_count() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+int fill_basis(const kf_basis_desc* d, const float* grid, int nt, int has_base, int f_pad, BasisDev& bd) {
+  KF_CHECK_ARG(d != nullptr, "basis is null");
+  KF_CHECK_ARG(f_pad == 16 || f_pad == 32, "f_pad must be 16 or 32 (got %d)", f_pad);
+  KF_CHECK_ARG(nt >= 1 && nt + (has_base ? 1 : 0) <= f_pad, "nt %d (+ base) exceeds f_pad %d", nt, f_pad);
+  bd.map = d->input_map;
+  bd.nt = nt;
+  bd.has_base = has_base;
+  bd.grid = grid;
+  if (d->kind == KF_BASIS_BSPLINE) {
+    KF_CHECK_ARG(grid != nullptr, "B-spline needs its grid");
+    KF_CHECK_ARG(d->order >= 1 && d->order <= kMaxOrder, "B-spline order %d unsupported", d->order);
+    bd.G = d->grid_size;
+    bd.nk = d->grid_size + 2 * d->order + 1;
+    KF_CHECK_ARG(bd.nk <= kTabStride, "B-spline with %d knots exceeds %d", bd.nk, kTabStride);
+    KF_CHECK_ARG(nt == d->size, "B-spline nt %d must equal the basis size %d", nt, d->size);
+  } else if (d->kind != KF_BASIS_CHEB) {
+    set_error("fused kernels support B-spline and Chebyshev-feature bases");
+    return KF_ERR_UNSUPPORTED;
+  }
+  return KF_OK;
+}
+
+template <typename Fn>
+int dispatch_fused(const kf_basis_desc* d, int f_pad, Fn&& fn) {
+  if (d->kind == KF_BASIS_CHEB) return f_pad == 16 ? fn.template go<0, 16>() : fn.template go<0, 32>();
+  switch (d->order) {
+    case 1: return f_pad == 16 ? fn.template go<1, 16>() : fn.template go<1, 32>();
+    case 2: return f_pad == 16 ? fn.template go<2, 16>() : fn.template go<2, 32>();
+    case 3: return f_pad == 16 ? fn.template go<3, 16>() : fn.template go<3, 32>();
+    case 4: return f_pad == 16 ? fn.template go<4, 16>() : fn.template go<4, 32>();
+    case 5: return f_pad == 16 ? fn.template go<5, 16>() : fn.template go<5, 32>();
+    default: break;
+  }
+  set_error("B-spline order %d unsupported", d->order);
+  return KF_ERR_UNSUPPORTED;
+}
+
+constexpr size_t kMainSmem = 1024 + kStages * (kATile + kBTile) + sizeof(Ctl);
+
+struct FwdLaunch {
+  const CUtensorMap* tmap;
+  FwdParams p;
+  cudaStream_t stream;
+  template <int BK, int F>
+  int go() const {
+    constexpr int IPK = kBK / F;
+    const size_t smem = kMainSmem + (BK > 0 ? sizeof(float) * 4 * IPK * (BK + 1) * kTabStride : 0);
+    auto kern = fused_fwd_kernel<BK, F>;
+    KF_CUDA_RET(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    const int grid = (int)std::min<int64_t>(p.tiles.m_tiles * (int64_t)p.tiles.n_tiles, sm_count());
+    kern<<<grid, kFwdThreads, smem, stream>>>(*tmap, p);
+    return check_launch("kf_fwd");
+  }
+};
+
+struct DgradLaunch {
+  const CUtensorMap *tmap_dy, *tmap_c;
+  DgradParams p;
+  cudaStream_t stream;
+  template <int BK, int F>
+  int go() const {
+    constexpr int IPT = kBN / F;
+    const size_t smem = kMainSmem + (BK > 0 ? sizeof(float) * (IPT * kTabStride + 4 * 32 * 33) : 0);
+    auto kern = fused_dgrad_kernel<BK, F>;
+    KF_CUDA_RET(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    const int grid = (int)std::min<int64_t>(p.tiles.m_tiles * (int64_t)p.tiles.n_tiles, sm_count());
+    kern<<<grid, kDgradThreads, smem, stream>>>(*tmap_dy, *tmap_c, p);
+    return check_launch("kf_dgrad");
+  }
+};
+
+struct WgradLaunch {
+  const CUtensorMap* tmap_dy;
+  WgradParams p;
+  cudaStream_t stream;
+  template <int BK, int F>
+  int go() const {
+    const size_t smem = kMainSmem + sizeof(float) * (128 * 33 + (BK > 0 ? 8 * (BK + 1) * kTabStride : 0));
+    auto kern = fused_wgrad_kernel<BK, F>;
+    KF_CUDA_RET(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    const int grid = (int)std::min<int64_t>(p.tiles.m_tiles * (int64_t)p.tiles.n_tiles, sm_count());
+    kern<<<grid, kWgradThreads, smem, stream>>>(*tmap_dy, p);
+    return check_launch("kf_wgrad");
+  }
+};
+
+}  // namespace
+
+}  // namespace kf
+
+extern "C" int kf_fwd(const void* x, const void* packed, const void* bias, const float* grid, void* y, int64_t B,
+                      int32_t I, int32_t O, int32_t nt, int32_t f_pad, int32_t has_base, const kf_basis_desc* basis,
+                      void* stream) {
+  using namespace kf;
+  clear_error();
+  KF_CHECK_ARG(x && packed && y, "kf_fwd: null tensor pointer");
+  KF_CHECK_ARG(B >= 0 && I >= 1 && O >= 1, "kf_fwd: bad sizes");
+  KF_CHECK_ARG(O % 8 == 0, "kf_fwd: O (%d) must be a multiple of 8", O);
+  FwdParams p{};
+  if (int rc = fill_basis(basis, grid, nt, has_base, f_pad, p.bd)) return rc;
+  if (B == 0) return KF_OK;
+  p.x = (const __nv_bfloat16*)x;
+  p.bias = (const __nv_bfloat16*)bias;
+  p.y = (__nv_bfloat16*)y;
+  p.B = B;
+  p.I = I;
+  p.O = O;
+  const int ipk = kBK / f_pad;
+  p.k_steps = (int)cdiv(I, ipk);
+  p.tiles.m_tiles = (int)cdiv(B, kBM);
+  p.tiles.n_tiles = (int)cdiv(O, kBN);
+  p.tiles.gm = p.tiles.m_tiles;  // M fastest: concurrent CTAs share one coefficient column block
+  CUtensorMap tmap;
+  if (int rc = make_tmap_bf16(&tmap, packed, O, (int64_t)I * f_pad, kBK, kBN)) return rc;
+  FwdLaunch L{&tmap, p, (cudaStream_t)stream};
+  return dispatch_fused(basis, f_pad, L);
+}
+
+extern "C" int kf_dgrad(const void* x, const void* dy, const void* packed, const float* grid, void* dx, int64_t B,
+                        int32_t I, int32_t O, int32_t nt, int32_t f_pad, int32_t has_base, const kf_basis_desc* basis,
+                        void* stream) {
+  using namespace kf;
+  clear_error();
+  KF_CHECK_ARG(x && dy && packed && dx, "kf_dgrad: null tensor pointer");
+  KF_CHECK_ARG(B >= 0 && I >= 1 && O >= 1, "kf_dgrad: bad sizes");
+  KF_CHECK_ARG(O % 8 == 0, "kf_dgrad: O (%d) must be a multiple of 8", O);
+  DgradParams p{};
+  if (int rc = fill_basis(basis, grid, nt, has_base, f_pad, p.bd)) return rc;
+  if (B == 0) return KF_OK;
+  p.x = (const __nv_bfloat16*)x;
+  p.dx = (__nv_bfloat16*)dx;
+  p.B = B;
+  p.I = I;
+  p.O = O;
+  p.k_steps = (int)cdiv(O, kBK);
+  p.tiles.m_tiles = (int)cdiv(B, kBM);
+  p.tiles.n_tiles = (int)cdiv((int64_t)I * f_pad, kBN);
+  p.tiles.gm = std::min(p.tiles.m_tiles, 16);
+  CUtensorMap tdy, tc;
+  if (int rc = make_tmap_bf16(&tdy, dy, B, O, kBK, kBM)) return rc;
+  if (int rc = make_tmap_bf16(&tc, packed, O, (int64_t)I * f_pad, 64, kBK)) return rc;
+  DgradLaunch L{&tdy, &tc, p, (cudaStream_t)stream};
+  return dispatch_fused(basis, f_pad, L);
+}
+
+extern "C" int kf_wgrad(const void* x, const void* dy, const float* grid, const float* fold, void* dcoef_eff,
+                        void* dbase, int64_t B, int32_t I, int32_t O, int32_t K, int32_t nt, int32_t f_pad,
+                        const kf_basis_desc* basis, void* stream) {
+  using namespace kf;
+  clear_error();
+  KF_CHECK_ARG(x && dy && dcoef_eff, "kf_wgrad: null tensor pointer");
+  KF_CHECK_ARG(B >= 0 && I >= 1 && O >= 1 && K >= 1, "kf_wgrad: bad sizes");
+  KF_CHECK_ARG(O % 8 == 0, "kf_wgrad: O (%d) must be a multiple of 8", O);
+  KF_CHECK_ARG(fold != nullptr || K == nt, "kf_wgrad: without a fold K must equal nt");
+  WgradParams p{};
+  if (int rc = fill_basis(basis, grid, nt, dbase != nullptr, f_pad, p.bd)) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (B == 0) {
+    KF_CUDA_RET(cudaMemsetAsync(dcoef_eff, 0, sizeof(__nv_bfloat16) * (size_t)O * I * K, s));
+    if (dbase) KF_CUDA_RET(cudaMemsetAsync(dbase, 0, sizeof(__nv_bfloat16) * (size_t)O * I, s));
+    return KF_OK;
+  }
+  p.x = (const __nv_bfloat16*)x;
+  p.fold = fold;
+  p.dcoef = (__nv_bfloat16*)dcoef_eff;
+  p.dbase = (__nv_bfloat16*)dbase;
+  p.B = B;
+  p.I = I;
+  p.O = O;
+  p.K = K;
+  p.k_steps = (int)cdiv(B, kBK);
+  const int ipt = kBM / f_pad;
+  p.tiles.m_tiles = (int)cdiv(I, ipt);
+  p.tiles.n_tiles = (int)cdiv(O, kBN);
+  p.tiles.gm = p.tiles.m_tiles;  // M fastest: concurrent CTAs share the dy column block
+  CUtensorMap tdy;
+  if (int rc = make_tmap_bf16(&tdy, dy, B, O, 64, kBK)) return rc;
+  WgradLaunch L{&tdy, p, s};
+  return dispatch_fused(basis, f_pad, L);
+}

@@ -1,0 +1,82 @@
+// Builds the bf16 coefficient operand of the fused tensor-core kernels.
+//
+//   packed[o, i, j]  = sum_k coef_eff[o,i,k] fold[k,j]   j < nt   (fold null: j = k)
+//   packed[o, i, nt] = base_eff[o,i]                     (SiLU column)
+//   packed[o, i, j]  = 0                                 up to f_pad
+//
+// For folded plans this is the reference's `ct = c @ R` (kanforge/torch/kernels.py:75-77,
+// kanforge/kernels/plan.py:75-101) with the base branch of
+// kanforge/torch/layers.py:185-186 appended as one more feature column, so the
+// layer forward becomes a single contraction over I * f_pad.
+#include "common.cuh"
+
+namespace kf {
+
+namespace {
+
+constexpr int kPackThreads = 256;
+constexpr int kMaxFold = 64;
+
+template <typename T>
+__global__ void __launch_bounds__(kPackThreads) pack_kernel(const T* __restrict__ coef, const T* __restrict__ base,
+                                                            const float* __restrict__ fold, __nv_bfloat16* __restrict__ packed,
+                                                            int64_t n_edges, int K, int nt, int f_pad, int has_fold) {
+  __shared__ float R[kMaxFold * kMaxFold];
+  if (has_fold)
+    for (int e = threadIdx.x; e < K * nt; e += blockDim.x) R[e] = fold[e];
+  __syncthreads();
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n_edges; e += (int64_t)gridDim.x * blockDim.x) {
+    const T* c = coef + e * K;
+    float cv[kMaxFold];
+    for (int k = 0; k < K; ++k) cv[k] = to_f32(c[k]);
+    __nv_bfloat16* dst = packed + e * f_pad;
+    for (int j0 = 0; j0 < f_pad; j0 += 8) {
+      __align__(16) __nv_bfloat16 tmp[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int j = j0 + u;
+        float v = 0.0f;
+        if (j < nt) {
+          if (has_fold) {
+            for (int k = 0; k < K; ++k) v = fmaf(cv[k], R[k * nt + j], v);
+          } else {
+            v = j < K ? cv[j] : 0.0f;
+          }
+        } else if (j == nt && base != nullptr) {
+          v = to_f32(base[e]);
+        }
+        tmp[u] = __float2bfloat16_rn(v);
+      }
+      *reinterpret_cast<uint4*>(dst + j0) = *reinterpret_cast<const uint4*>(tmp);
+    }
+  }
+}
+
+}  // namespace
+
+}  // namespace kf
+
+extern "C" int kf_pack_coef(const void* coef_eff, const void* base_eff, const float* fold, void* packed, int32_t O,
+                            int32_t I, int32_t K, int32_t nt, int32_t f_pad, int dtype, void* stream) {
+  using namespace kf;
+  clear_error();
+  KF_CHECK_ARG(coef_eff && packed, "kf_pack_coef: null pointer");
+  KF_CHECK_ARG(O >= 1 && I >= 1 && K >= 1 && nt >= 1 && K <= kMaxFold && nt <= kMaxFold, "kf_pack_coef: bad sizes");
+  KF_CHECK_ARG(f_pad % 8 == 0 && f_pad >= nt + (base_eff ? 1 : 0), "kf_pack_coef: f_pad %d too small", f_pad);
+  KF_CHECK_ARG(fold != nullptr || nt <= K, "kf_pack_coef: without a fold nt must be <= K");
+  KF_CHECK_ARG(((uintptr_t)packed % 16) == 0, "kf_pack_coef: packed must be 16-byte aligned");
+  const int64_t n = (int64_t)O * I;
+  const unsigned grid = (unsigned)std::min<int64_t>(cdiv(n, kPackThreads), 148 * 16);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (dtype == KF_DTYPE_F32) {
+    pack_kernel<float><<<grid, kPackThreads, 0, s>>>((const float*)coef_eff, (const float*)base_eff, fold,
+                                                     (__nv_bfloat16*)packed, n, K, nt, f_pad, fold != nullptr);
+  } else if (dtype == KF_DTYPE_BF16) {
+    pack_kernel<__nv_bfloat16><<<grid, kPackThreads, 0, s>>>((const __nv_bfloat16*)coef_eff, (const __nv_bfloat16*)base_eff,
+                                                             fold, (__nv_bfloat16*)packed, n, K, nt, f_pad, fold != nullptr);
+  } else {
+    set_error("kf_pack_coef: dtype %d unsupported", dtype);
+    return KF_ERR_UNSUPPORTED;
+  }
+  return check_launch("kf_pack_coef");
+}

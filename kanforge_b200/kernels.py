@@ -1,0 +1,410 @@
+"""Torch side of the sm_100a kernels: launchers and differentiable primitives.
+
+Mirrors the reference module ``kanforge.torch.kernels`` (kanforge/torch/kernels.py):
+``available``, ``_raw``, the closed autograd family ``prim_F / prim_G / prim_P``
+and ``spline_forward`` keep their names and argument meaning, so code written
+against the reference's kernel layer runs unchanged.  Every launch goes
+through the C ABI of ``libkanb200`` (include/kanforge_b200.h) on torch's
+current CUDA stream; there is no CPU or Triton path.
+
+On top of the reference's primitives this module adds the fused training op
+of the layer (``kan_linear_fused``: basis features, SiLU base branch and bias in
+one tensor-core contraction per pass), the streaming ``edge_derivative`` and
+the KAT rational activation.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from ._init import silu_derivative_polys
+from .plan import KernelPlan
+
+_BF16 = torch.bfloat16
+
+# Optional observer of kernel launches: a callable(name) returning a context
+# manager entered around every compute entry point (bench.py records CUDA
+# events with it); LAUNCH_COUNT counts library compute launches.
+_observer = None
+LAUNCH_COUNT = 0
+
+
+def set_launch_observer(fn) -> None:
+    global _observer
+    _observer = fn
+
+
+def _launch(name: str, *args) -> None:
+    global LAUNCH_COUNT
+    LAUNCH_COUNT += 1
+    if _observer is None:
+        _lib.call(name, *args)
+        return
+    with _observer(name):
+        _lib.call(name, *args)
+
+
+def available(device: torch.device) -> bool:
+    """True on CUDA devices with the library loaded (kanforge/torch/kernels.py:19-28)."""
+    if torch.device(device).type != "cuda":
+        return False
+    _lib.load()
+    return True
+
+
+def _stream(t: torch.Tensor) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _ptr(t: torch.Tensor | None) -> ctypes.c_void_p:
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+def _check_cuda(*ts) -> None:
+    for t in ts:
+        if t is not None and t.device.type != "cuda":
+            raise RuntimeError(f"kanforge_b200 kernels run on CUDA tensors only (got a {t.device} tensor)")
+
+
+# --- raw launches (no autograd) ---------------------------------------------
+
+
+def _prep(t: torch.Tensor) -> torch.Tensor:
+    return t.contiguous().float()
+
+
+def _raw(op: str, plan: KernelPlan, m: int, x, a, b, grid, n_out: int, nf: int) -> torch.Tensor:
+    """op F: (x, w, cT) -> y; G: (x, w, g) -> GT; P: (x, g, cT) -> p (kanforge/torch/kernels.py:39-55)."""
+    _check_cuda(x, a, b, grid)
+    batch, n_in = x.shape
+    code = {"F": _lib.KF_OP_F, "G": _lib.KF_OP_G, "P": _lib.KF_OP_P}[op]
+    if op == "F":
+        out = torch.empty(batch, n_out, device=x.device, dtype=torch.float32)
+    elif op == "G":
+        out = torch.empty(n_out, n_in, nf, device=x.device, dtype=torch.float32)
+    else:
+        out = torch.empty(batch, n_in, device=x.device, dtype=torch.float32)
+    desc = plan.desc()
+    _launch("kf_prim", code, m, _ptr(x), _ptr(a), _ptr(b), _ptr(grid), _ptr(out), batch, n_in, n_out, nf,
+              ctypes.byref(desc), _stream(x))
+    return out
+
+
+def _fold(plan: KernelPlan, m: int, like: torch.Tensor):
+    r = plan.fold(m)
+    return None if r is None else torch.tensor(r, dtype=like.dtype, device=like.device)
+
+
+# --- differentiable primitives (kanforge/torch/kernels.py:70-140) -------------
+
+
+class _F(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, c, w, grid, plan, m):
+        ctx.save_for_backward(x, c, w, grid)
+        ctx.plan, ctx.m = plan, m
+        r = _fold(plan, m, c)
+        ct = c if r is None else c @ r
+        return _raw("F", plan, plan.native_order(m), _prep(x), _prep(w), _prep(ct), _prep(grid), c.shape[0], ct.shape[-1])
+
+    @staticmethod
+    def backward(ctx, gy):
+        x, c, w, grid = ctx.saved_tensors
+        plan, m = ctx.plan, ctx.m
+        need = ctx.needs_input_grad
+        gx = w * prim_P(x, gy, c, grid, plan, m + 1) if need[0] else None
+        gc = prim_G(x, gy, w, grid, plan, m) if need[1] else None
+        gw = prim_P(x, gy, c, grid, plan, m) if need[2] else None
+        return gx, gc, gw, None, None, None
+
+
+class _G(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, g, w, grid, plan, m):
+        ctx.save_for_backward(x, g, w, grid)
+        ctx.plan, ctx.m = plan, m
+        nf = plan.n_features(m)
+        gt = _raw("G", plan, plan.native_order(m), _prep(x), _prep(w), _prep(g), _prep(grid), g.shape[1], nf)
+        r = _fold(plan, m, gt)
+        return gt if r is None else gt @ r.T
+
+    @staticmethod
+    def backward(ctx, gg_out):
+        x, g, w, grid = ctx.saved_tensors
+        plan, m = ctx.plan, ctx.m
+        need = ctx.needs_input_grad
+        gx = w * prim_P(x, g, gg_out, grid, plan, m + 1) if need[0] else None
+        gg = prim_F(x, gg_out, w, grid, plan, m) if need[1] else None
+        gw = prim_P(x, g, gg_out, grid, plan, m) if need[2] else None
+        return gx, gg, gw, None, None, None
+
+
+class _P(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, g, c, grid, plan, m):
+        ctx.save_for_backward(x, g, c, grid)
+        ctx.plan, ctx.m = plan, m
+        r = _fold(plan, m, c)
+        ct = c if r is None else c @ r
+        return _raw("P", plan, plan.native_order(m), _prep(x), _prep(g), _prep(ct), _prep(grid), c.shape[0], ct.shape[-1])
+
+    @staticmethod
+    def backward(ctx, gp):
+        x, g, c, grid = ctx.saved_tensors
+        plan, m = ctx.plan, ctx.m
+        need = ctx.needs_input_grad
+        gx = gp * prim_P(x, g, c, grid, plan, m + 1) if need[0] else None
+        gg = prim_F(x, c, gp, grid, plan, m) if need[1] else None
+        gc = prim_G(x, g, gp, grid, plan, m) if need[2] else None
+        return gx, gg, gc, None, None, None
+
+
+def prim_F(x, c, w, grid, plan, m=0):
+    return _F.apply(x, c, w, grid, plan, m)
+
+
+def prim_G(x, g, w, grid, plan, m=0):
+    return _G.apply(x, g, w, grid, plan, m)
+
+
+def prim_P(x, g, c, grid, plan, m=0):
+    return _P.apply(x, g, c, grid, plan, m)
+
+
+def spline_forward(x: torch.Tensor, coef: torch.Tensor, grid: torch.Tensor | None, plan: KernelPlan) -> torch.Tensor:
+    """sum_{i,k} coef[o,i,k] phi_k(x[..., i]) through the float32 primitive (kernels.py:143-150)."""
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, x.shape[-1])
+    if grid is None:
+        grid = x2.new_zeros(1, dtype=torch.float32)
+    y = prim_F(x2.float(), coef.float(), torch.ones_like(x2, dtype=torch.float32), grid.float(), plan, 0)
+    return y.to(x.dtype).reshape(*lead, coef.shape[0])
+
+
+# --- fused layer op (tcgen05) ------------------------------------------------
+
+
+def fused_layout(plan: KernelPlan, has_base: bool) -> tuple[int, int]:
+    """(nt, f_pad): basis feature columns per input and the padded width (16 or 32)."""
+    nt = plan.n_features(0)
+    width = nt + (1 if has_base else 0)
+    return nt, (16 if width <= 16 else 32)
+
+
+def fused_ok(plan: KernelPlan | None, x: torch.Tensor, n_out: int, has_base: bool) -> bool:
+    """Whether the tensor-core path serves this call: bf16, CUDA, a B-spline or
+    Chebyshev-feature plan with <= 31 feature columns, outputs a multiple of 8."""
+    if plan is None or plan.kind not in ("cheb", "bspline") or x.dtype != _BF16 or x.device.type != "cuda":
+        return False
+    nt, _ = fused_layout(plan, has_base)
+    if nt + (1 if has_base else 0) > 32 or n_out % 8:
+        return False
+    return plan.supported(_lib.KF_QUERY_FUSED, _lib.KF_DTYPE_BF16)
+
+
+def pack_coef(coef_eff: torch.Tensor, base_eff: torch.Tensor | None, plan: KernelPlan, f_pad: int) -> torch.Tensor:
+    """The bf16 tensor-core operand (O, I * f_pad): folded coefficients and the SiLU column."""
+    n_out, n_in, k = coef_eff.shape
+    nt = plan.n_features(0)
+    coef_eff = coef_eff.detach().contiguous()
+    dt = _lib.KF_DTYPE_BF16 if coef_eff.dtype == _BF16 else _lib.KF_DTYPE_F32
+    if dt == _lib.KF_DTYPE_F32:
+        coef_eff = coef_eff.float()
+    base = None if base_eff is None else base_eff.detach().to(coef_eff.dtype).contiguous()
+    fold = None
+    if plan.folded and not plan.is_identity_fold():
+        fold = torch.tensor(plan.fold(0), dtype=torch.float32, device=coef_eff.device)
+    packed = torch.empty(n_out, n_in * f_pad, device=coef_eff.device, dtype=_BF16)
+    _launch("kf_pack_coef", _ptr(coef_eff), _ptr(base), _ptr(fold), _ptr(packed), n_out, n_in, k, nt, f_pad, dt,
+              _stream(coef_eff))
+    return packed
+
+
+class _FusedKANLinear(torch.autograd.Function):
+    """y = sum_{i,j} feat_j(x_i) C_eff[o,i,j] + silu(x_i) W_eff[o,i] + b_o in one
+    tcgen05 contraction per pass (forward, input gradient, coefficient gradient).
+
+    When the backward itself is differentiated (create_graph), the gradients are
+    built from the closed float32 primitives instead, so every order works as in
+    the reference (kanforge/torch/kernels.py:79-87)."""
+
+    @staticmethod
+    def forward(ctx, x, coef_eff, base_eff, bias, grid, plan):
+        n_out, n_in, _ = coef_eff.shape
+        has_base = base_eff is not None
+        nt, f_pad = fused_layout(plan, has_base)
+        x = x.contiguous()
+        packed = pack_coef(coef_eff, base_eff, plan, f_pad)
+        y = torch.empty(x.shape[0], n_out, device=x.device, dtype=_BF16)
+        b = None if bias is None else bias.detach().to(_BF16).contiguous()
+        g = None if grid is None else grid.detach().float().contiguous()
+        desc = plan.desc()
+        _launch("kf_fwd", _ptr(x), _ptr(packed), _ptr(b), _ptr(g), _ptr(y), x.shape[0], n_in, n_out, nt, f_pad,
+                  int(has_base), ctypes.byref(desc), _stream(x))
+        ctx.save_for_backward(x, coef_eff, base_eff, g)
+        ctx.packed, ctx.plan, ctx.has_bias = packed, plan, bias is not None
+        ctx.layout = (nt, f_pad)
+        return y
+
+    @staticmethod
+    def backward(ctx, gy):
+        x, coef_eff, base_eff, grid = ctx.saved_tensors
+        plan = ctx.plan
+        need = ctx.needs_input_grad
+        if torch.is_grad_enabled():
+            return _fused_backward_differentiable(x, gy, coef_eff, base_eff, grid, plan, need, ctx.has_bias)
+        nt, f_pad = ctx.layout
+        n_out, n_in, k = coef_eff.shape
+        gy = gy.to(_BF16).contiguous()
+        desc = plan.desc()
+        stream = _stream(x)
+        gx = gc = gb = gbias = None
+        if need[1] or need[2]:
+            gc = torch.empty(n_out, n_in, k, device=x.device, dtype=_BF16)
+            gb = torch.empty(n_out, n_in, device=x.device, dtype=_BF16) if base_eff is not None else None
+            fold = None
+            if plan.folded and not plan.is_identity_fold():
+                fold = torch.tensor(plan.fold(0), dtype=torch.float32, device=x.device)
+            _launch("kf_wgrad", _ptr(x), _ptr(gy), _ptr(grid), _ptr(fold), _ptr(gc), _ptr(gb), x.shape[0], n_in, n_out,
+                      k, nt, f_pad, ctypes.byref(desc), stream)
+            gc = gc.to(coef_eff.dtype) if need[1] else None
+            gb = gb.to(base_eff.dtype) if (gb is not None and need[2]) else None
+        if need[0]:
+            gx = torch.empty_like(x)
+            _launch("kf_dgrad", _ptr(x), _ptr(gy), _ptr(ctx.packed), _ptr(grid), _ptr(gx), x.shape[0], n_in, n_out, nt,
+                      f_pad, int(base_eff is not None), ctypes.byref(desc), stream)
+        if need[3]:
+            gbias = gy.float().sum(0)
+        ctx.packed = None
+        return gx, gc, gb, gbias, None, None
+
+
+def _fused_backward_differentiable(x, gy, coef_eff, base_eff, grid, plan, need, has_bias):
+    """Gradients of the fused op as a graph of float32 primitives (create_graph=True)."""
+    xf = x.float()
+    gyf = gy.float()
+    ones = torch.ones_like(xf)
+    g = grid if grid is not None else xf.new_zeros(1)
+    cf = coef_eff.float()
+    gx = gc = gb = gbias = None
+    if need[0]:
+        gx = prim_P(xf, gyf, cf, g, plan, 1)
+        if base_eff is not None:
+            s = torch.sigmoid(xf)
+            gx = gx + (gyf @ base_eff.float()) * (s * (1 + xf * (1 - s)))
+        gx = gx.to(x.dtype)
+    if need[1]:
+        gc = prim_G(xf, gyf, ones, g, plan, 0).to(coef_eff.dtype)
+    if need[2] and base_eff is not None:
+        gb = (gyf.T @ torch.nn.functional.silu(xf)).to(base_eff.dtype)
+    if need[3] and has_bias:
+        gbias = gyf.sum(0)
+    return gx, gc, gb, gbias, None, None
+
+
+def kan_linear_fused(x, coef_eff, base_eff, bias, grid, plan):
+    """Fused KANLinear on (..., I) bf16 inputs; see ``_FusedKANLinear``."""
+    lead = x.shape[:-1]
+    y = _FusedKANLinear.apply(x.reshape(-1, x.shape[-1]), coef_eff, base_eff, bias, grid, plan)
+    return y.reshape(*lead, coef_eff.shape[0])
+
+
+# --- edge_derivative ---------------------------------------------------------
+
+
+def edge_derivative(x, coef_eff, base_eff, grid, plan: KernelPlan, order: int, basis_params: dict | None = None,
+                    groups: int = 1) -> torch.Tensor:
+    """(B, O, I) d^m phi_oi / dx_i^m + silu^(m) W_eff, float32 (kanforge/torch/layers.py:206-226)."""
+    _check_cuda(x)
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, x.shape[-1]).float().contiguous()
+    n_out, n_in, _ = coef_eff.shape
+    c = coef_eff.detach().float()
+    num = den = None
+    if plan.kind == "cheb":
+        c = c @ torch.tensor(plan.fold(order), dtype=torch.float32, device=x.device)
+    elif plan.kind == "rational":
+        num = basis_params["numerator"].detach().float().contiguous()
+        den = basis_params["denominator"].detach().float().contiguous()
+    nf = c.shape[-1]
+    coef_t = c.permute(0, 2, 1).contiguous()  # (O, nf, I)
+    base = None if base_eff is None else base_eff.detach().float().contiguous()
+    g = None if grid is None else grid.detach().float().contiguous()
+    polys = torch.as_tensor(silu_derivative_polys(order), dtype=torch.float32).flatten().contiguous()
+    out = torch.empty(x2.shape[0], n_out, n_in, device=x.device, dtype=torch.float32)
+    desc = plan.desc(groups)
+    poly_buf = (ctypes.c_float * polys.numel())(*polys.tolist())
+    _launch("kf_edge_derivative", _ptr(x2), _ptr(coef_t), _ptr(base), _ptr(g), _ptr(num), _ptr(den), _ptr(out),
+              x2.shape[0], n_in, n_out, nf, order, ctypes.byref(desc), ctypes.cast(poly_buf, ctypes.c_void_p),
+              polys.numel() // 2, _stream(x2))
+    return out.reshape(*lead, n_out, n_in)
+
+
+# --- KAT rational ------------------------------------------------------------
+
+
+def _rat_dtype(t: torch.Tensor) -> int:
+    if t.dtype == _BF16:
+        return _lib.KF_DTYPE_BF16
+    if t.dtype == torch.float32:
+        return _lib.KF_DTYPE_F32
+    raise RuntimeError(f"rational kernels take float32 or bfloat16, not {t.dtype}")
+
+
+class _RationalAct(torch.autograd.Function):
+    """R_g^(m)(x) of the group rational; d/dx is R^(m+1) (closed in x), the
+    parameter gradient of order 0 comes from the fused backward kernel."""
+
+    @staticmethod
+    def forward(ctx, x, num, den, plan, groups, m):
+        _check_cuda(x)
+        x = x.contiguous()
+        if x.dtype not in (torch.float32, _BF16):
+            x = x.float()
+        numf, denf = num.detach().float().contiguous(), den.detach().float().contiguous()
+        out = torch.empty_like(x)
+        desc = plan.desc(groups)
+        _launch("kf_rational_act", _ptr(x), _ptr(numf), _ptr(denf), _ptr(out), x.shape[0], x.shape[1], m,
+                  ctypes.byref(desc), _rat_dtype(x), _stream(x))
+        ctx.save_for_backward(x, num, den)
+        ctx.plan, ctx.groups, ctx.m = plan, groups, m
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        x, num, den = ctx.saved_tensors
+        plan, groups, m = ctx.plan, ctx.groups, ctx.m
+        need = ctx.needs_input_grad
+        if m == 0 and not torch.is_grad_enabled():
+            g = g.to(x.dtype).contiguous()
+            dx = torch.empty_like(x)
+            dnum = torch.empty(num.shape, device=x.device, dtype=torch.float32)
+            dden = torch.empty(den.shape, device=x.device, dtype=torch.float32)
+            desc = plan.desc(groups)
+            ws_n = _lib.load().kf_rational_workspace(x.shape[0], x.shape[1], ctypes.byref(desc))
+            ws = torch.empty(max(int(ws_n), 1), device=x.device, dtype=torch.float32)
+            _launch("kf_rational_bwd", _ptr(x), _ptr(g), _ptr(num.detach().float().contiguous()),
+                      _ptr(den.detach().float().contiguous()), _ptr(dx), _ptr(dnum), _ptr(dden), _ptr(ws), x.shape[0],
+                      x.shape[1], ctypes.byref(desc), _rat_dtype(x), _stream(x))
+            return (dx if need[0] else None, dnum.to(num.dtype) if need[1] else None,
+                    dden.to(den.dtype) if need[2] else None, None, None, None)
+        if need[1] or need[2]:
+            raise NotImplementedError(
+                "gradients of higher derivatives of the rational activation into its parameters are not available"
+            )
+        dx = g * _RationalAct.apply(x, num, den, plan, groups, m + 1) if need[0] else None
+        return dx, None, None, None, None, None
+
+
+def rational_act(x2, num, den, plan, groups, m=0):
+    return _RationalAct.apply(x2, num, den, plan, groups, m)
+
+
+def check_device_errors() -> None:
+    """Raise if a kernel recorded a bounded wait that ran out (synchronises)."""
+    flags = _lib.device_status()
+    if flags:
+        raise RuntimeError(f"a kanforge_b200 kernel reported device error flags {flags:#x}")

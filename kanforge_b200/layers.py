@@ -1,0 +1,361 @@
+"""KAN layers on the sm_100a kernels: KANLinear, KAN, GRKAN.
+
+Same constructor arguments, parameter names, shapes, buffers and state-dict
+layout as the reference torch layers (kanforge/torch/layers.py:28-398), so
+state dicts and ``.npz`` files move between the two unchanged.  The compute
+differs: every forward and backward runs ``libkanb200`` kernels on CUDA.
+
+Dispatch of ``KANLinear.forward`` (reference kanforge/torch/layers.py:171-192):
+
+* bfloat16 B-spline / polynomial layers -> one fused tcgen05 contraction per
+  pass (basis features + SiLU base branch + bias, ``kernels.kan_linear_fused``);
+* other dtypes and shapes -> the closed float32 primitive family
+  (``kernels.spline_forward``) plus the base branch and bias;
+* rational (GRKAN) layers -> the group-rational kernel, then the contraction
+  with the layer coefficients.
+
+CPU tensors raise: there is no CPU fallback.
+"""
+
+from __future__ import annotations
+
+import math
+from collections.abc import Callable, Sequence
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from . import kernels as _kernels
+from ._init import basis_param_values, init_stds, resolve_groups
+from .bases import Basis, Rational, make_basis
+from .plan import plan_for
+
+BACKENDS = ("auto", "ops", "kernel")
+
+
+def _require_cuda(x: torch.Tensor) -> None:
+    if x.device.type != "cuda":
+        raise RuntimeError(
+            f"kanforge_b200 layers run on CUDA devices only (got a {x.device} tensor); there is no CPU fallback"
+        )
+
+
+class _EdgeDerivativeNoGrad(torch.autograd.Function):
+    """Marks a kernel-computed edge derivative as non-differentiable, loudly."""
+
+    @staticmethod
+    def forward(ctx, out, *inputs):
+        return out
+
+    @staticmethod
+    def backward(ctx, *grads):
+        raise NotImplementedError("backward through KANLinear.edge_derivative is not available; use autograd on forward")
+
+
+class KANLinear(nn.Module):
+    """One KAN layer: y_o = sum_i s_oi phi_oi(x_i) + sum_i w_oi act(x_i) + b_o.
+
+    Parameters (reference names): ``coef`` (out, in, basis.size), ``base_weight``
+    (out, in), ``bias`` (out,), ``edge_scale`` (out, in), trainable basis
+    parameters ``basis_<name>`` (groups, *shape).  Buffers: ``basis_<name>``
+    grids (in, *shape), ``edge_mask``, ``sym_code``, ``sym_params``.
+
+    ``backend`` is accepted for compatibility ("auto", "ops", "kernel"); every
+    value runs the CUDA kernels.  ``"kernel"`` raises for a basis without one.
+    """
+
+    def __init__(
+        self,
+        in_features: int,
+        out_features: int,
+        basis: str | dict | Basis = "bspline",
+        *,
+        bias: bool = True,
+        base_activation: Callable[[torch.Tensor], torch.Tensor] | None = F.silu,
+        groups: int | None = None,
+        edge_scale: bool = False,
+        grid_ranges=None,
+        coef_init: str = "normal",
+        coef_init_std: float = 0.1,
+        edge_dropout: float = 0.0,
+        backend: str = "auto",
+        device=None,
+        dtype=None,
+    ):
+        super().__init__()
+        if not 0 <= edge_dropout < 1:
+            raise ValueError("edge_dropout must be in [0, 1)")
+        if backend not in BACKENDS:
+            raise ValueError(f"backend must be one of {BACKENDS}")
+        factory = {"device": device, "dtype": dtype}
+        self.in_features = in_features
+        self.out_features = out_features
+        self.basis = make_basis(basis)
+        self.base_activation = base_activation
+        self.groups = resolve_groups(in_features, groups)
+        self.coef_init = coef_init
+        self.coef_init_std = coef_init_std
+        self.edge_dropout = edge_dropout
+        self.backend = backend
+        self._grid_ranges = grid_ranges
+        self._init_kwargs = {
+            "basis": self.basis,
+            "bias": bias,
+            "base_activation": base_activation,
+            "groups": groups,
+            "edge_scale": edge_scale,
+            "coef_init": coef_init,
+            "coef_init_std": coef_init_std,
+            "edge_dropout": edge_dropout,
+            "backend": backend,
+        }
+        init_stds(self.basis, in_features, out_features, coef_init, coef_init_std, base_activation is not None)
+        self.coef = nn.Parameter(torch.empty(out_features, in_features, self.basis.size, **factory))
+        if base_activation is not None:
+            self.base_weight = nn.Parameter(torch.empty(out_features, in_features, **factory))
+        else:
+            self.register_parameter("base_weight", None)
+        if bias:
+            self.bias = nn.Parameter(torch.empty(out_features, **factory))
+        else:
+            self.register_parameter("bias", None)
+        if edge_scale:
+            self.edge_scale = nn.Parameter(torch.empty(out_features, in_features, **factory))
+        else:
+            self.register_parameter("edge_scale", None)
+        self.register_buffer("edge_mask", torch.empty(out_features, in_features, **factory))
+        self.register_buffer("sym_code", torch.empty(out_features, in_features, dtype=torch.int32, device=device))
+        self.register_buffer("sym_params", torch.empty(out_features, in_features, 4, **factory))
+        self._trainable_names: list[str] = []
+        self._buffer_names: list[str] = []
+        self.reset_parameters()
+        if backend == "kernel" and self._plan is None:
+            raise RuntimeError(f"no fused kernel for this basis: {self.basis!r}")
+
+    # --- parameters (reference layers.py:120-167) -----------------------------
+
+    def _set_basis_state(self, trainable: dict, buffers: dict) -> None:
+        for name in self._trainable_names + self._buffer_names:
+            delattr(self, f"basis_{name}")
+        like = {"dtype": self.coef.dtype, "device": self.coef.device}
+        for name, value in trainable.items():
+            self.register_parameter(f"basis_{name}", nn.Parameter(torch.as_tensor(np.ascontiguousarray(value), **like)))
+        for name, value in buffers.items():
+            self.register_buffer(f"basis_{name}", torch.as_tensor(np.ascontiguousarray(value), **like))
+        self._trainable_names, self._buffer_names = list(trainable), list(buffers)
+        self._plan = plan_for(self.basis)
+
+    def reset_parameters(self) -> None:
+        coef_std, base_std = init_stds(
+            self.basis, self.in_features, self.out_features, self.coef_init, self.coef_init_std, self.base_weight is not None
+        )
+        nn.init.normal_(self.coef, std=coef_std) if coef_std else nn.init.zeros_(self.coef)
+        if self.base_weight is not None:
+            if base_std is None:
+                nn.init.kaiming_uniform_(self.base_weight, a=math.sqrt(5))
+            else:
+                nn.init.normal_(self.base_weight, std=base_std)
+        if self.bias is not None:
+            nn.init.zeros_(self.bias)
+        if self.edge_scale is not None:
+            nn.init.ones_(self.edge_scale)
+        self.edge_mask.fill_(1.0)
+        self.sym_code.fill_(-1)
+        self.sym_params.zero_()
+        self._sym_codes = ()
+        self._set_basis_state(*basis_param_values(self.basis, self.groups, self.in_features, self._grid_ranges))
+
+    def basis_params(self) -> dict[str, torch.Tensor]:
+        """Basis parameters and buffers expanded to (in, *shape) (layers.py:151-160)."""
+        rep = self.in_features // self.groups
+        out = {}
+        for name in self._trainable_names:
+            p = getattr(self, f"basis_{name}")
+            out[name] = p if self.groups in (1, self.in_features) else p.repeat_interleave(rep, dim=0)
+        for name in self._buffer_names:
+            out[name] = getattr(self, f"basis_{name}")
+        return out
+
+    def effective_coef(self) -> torch.Tensor:
+        scale = self.edge_mask if self.edge_scale is None else self.edge_scale * self.edge_mask
+        return self.coef * scale[..., None]
+
+    def effective_base_weight(self) -> torch.Tensor | None:
+        return None if self.base_weight is None else self.base_weight * self.edge_mask
+
+    # --- computation ------------------------------------------------------------
+
+    def _grid(self):
+        return getattr(self, "basis_grid", None) if self._plan is not None and self._plan.grid else None
+
+    def _check_supported(self) -> None:
+        if self._plan is None:
+            raise RuntimeError(f"no fused kernel for this basis: {self.basis!r}")
+        if self._sym_codes:
+            raise NotImplementedError("symbolic edges are not part of the kanforge_b200 kernel path")
+        if self.base_weight is not None and self.base_activation is not F.silu:
+            raise NotImplementedError("the fused base branch is SiLU; other base activations are not supported")
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        _require_cuda(x)
+        self._check_supported()
+        if self.training and self.edge_dropout > 0:
+            raise NotImplementedError("edge_dropout (DropKAN) is not part of the kanforge_b200 kernel path")
+        plan = self._plan
+        coef_eff = self.effective_coef()
+        base_eff = self.effective_base_weight()
+        if plan.kind == "rational":
+            lead = x.shape[:-1]
+            x2 = x.reshape(-1, self.in_features)
+            r = _kernels.rational_act(x2, self.basis_numerator, self.basis_denominator, plan, self.groups)
+            y = F.linear(r.to(coef_eff.dtype), coef_eff[..., 0], self.bias)
+            if base_eff is not None:
+                y = y + F.linear(F.silu(x2), base_eff)
+            return y.reshape(*lead, self.out_features)
+        if _kernels.fused_ok(plan, x, self.out_features, base_eff is not None):
+            return _kernels.kan_linear_fused(x, coef_eff, base_eff, self.bias, self._grid(), plan)
+        y = _kernels.spline_forward(x, coef_eff, self._grid(), plan)
+        if base_eff is not None:
+            y = y + F.linear(self.base_activation(x), base_eff)
+        if self.bias is not None:
+            y = y + self.bias
+        return y
+
+    def uses_kernel(self, device: torch.device) -> bool:
+        """Whether forward runs the CUDA kernels on ``device`` (layers.py:194-204)."""
+        ok = self._plan is not None and _kernels.available(torch.device(device))
+        if self.backend == "kernel" and not ok:
+            why = "basis" if self._plan is None else f"device {device}"
+            raise RuntimeError(f"no fused kernel for this {why}: {self.basis!r}")
+        return ok
+
+    def edge_derivative(self, x: torch.Tensor, order: int = 1) -> torch.Tensor:
+        """d^order phi_oi / dx_i^order of every edge, (..., out, in) (layers.py:206-226)."""
+        if order < 0:
+            raise ValueError("order must be >= 0")
+        _require_cuda(x)
+        self._check_supported()
+        plan = self._plan
+        coef_eff = self.effective_coef()
+        base_eff = self.effective_base_weight()
+        params = None
+        if plan.kind == "rational":
+            params = {"numerator": self.basis_numerator, "denominator": self.basis_denominator}
+        out = _kernels.edge_derivative(x, coef_eff, base_eff, self._grid(), plan, order, params, self.groups)
+        out = out.to(x.dtype) if x.dtype != torch.float32 else out
+        if torch.is_grad_enabled() and (x.requires_grad or any(p.requires_grad for p in self.parameters())):
+            out = _EdgeDerivativeNoGrad.apply(out, x)
+        return out
+
+    # --- state export / import (.npz layout, layers.py:230-267) -----------------
+
+    @staticmethod
+    def _to_numpy(x) -> np.ndarray:
+        return x.detach().cpu().double().numpy() if isinstance(x, torch.Tensor) else np.asarray(x)
+
+    def _export_full(self) -> dict:
+        own = {**dict(self.named_parameters(recurse=False)), **dict(self.named_buffers(recurse=False))}
+        out = {k: self._to_numpy(v) for k, v in own.items()}
+        out.update({k: None for k in ("base_weight", "bias", "edge_scale") if getattr(self, k) is None})
+        return out
+
+    @torch.no_grad()
+    def _import_full(self, state: dict) -> None:
+        for name, value in state.items():
+            t = getattr(self, name, None)
+            if value is None or t is None:
+                continue
+            if t.shape != value.shape:
+                raise ValueError(f"{name}: shape {value.shape} does not fit {tuple(t.shape)}")
+            t.copy_(torch.as_tensor(value, dtype=t.dtype, device=t.device))
+        self._refresh_symbolic()
+
+    def _refresh_symbolic(self) -> None:
+        codes = np.unique(self.sym_code.detach().cpu().numpy().astype(int))
+        self._sym_codes = tuple(int(c) for c in codes if c >= 0)
+
+    def _load_from_state_dict(self, *args, **kwargs):
+        super()._load_from_state_dict(*args, **kwargs)
+        self._refresh_symbolic()
+
+    def extra_repr(self) -> str:
+        groups = "" if self.groups == self.in_features else f", groups={self.groups}"
+        return f"in_features={self.in_features}, out_features={self.out_features}, basis={self.basis!r}{groups}"
+
+
+class GRKAN(KANLinear):
+    """Group-rational KAN layer of KAT (layers.py:335-363): rational activations
+    shared by ``groups`` of inputs, the coefficients act as the linear weight."""
+
+    def __init__(
+        self,
+        in_features: int,
+        out_features: int,
+        *,
+        groups: int = 8,
+        num_degree: int = 5,
+        den_degree: int = 4,
+        init: str = "gelu",
+        bias: bool = True,
+        device=None,
+        dtype=None,
+    ):
+        super().__init__(
+            in_features,
+            out_features,
+            Rational(num_degree, den_degree, init),
+            bias=bias,
+            base_activation=None,
+            groups=groups,
+            coef_init="variance",
+            device=device,
+            dtype=dtype,
+        )
+
+
+class KAN(nn.Sequential):
+    """Stack of KANLinear layers, e.g. ``KAN([2, 5, 1], basis="chebyshev")`` (layers.py:366-398)."""
+
+    def __init__(self, widths: Sequence[int], basis: str | dict | Basis = "bspline", grid_ranges=None, **layer_kwargs):
+        if len(widths) < 2:
+            raise ValueError("widths needs at least input and output size")
+        super().__init__(
+            *(
+                KANLinear(a, b, basis, grid_ranges=grid_ranges if k == 0 else None, **layer_kwargs)
+                for k, (a, b) in enumerate(zip(widths[:-1], widths[1:]))
+            )
+        )
+        self.widths = list(widths)
+
+    def edge_derivative(self, x: torch.Tensor, order: int = 1) -> list[torch.Tensor]:
+        """Per-layer edge derivatives at the activations each layer receives."""
+        return [layer.edge_derivative(h, order) for layer, h in layer_inputs(self, x)]
+
+
+def rebuild_kan(layers: Sequence[KANLinear]) -> KAN:
+    """A KAN made of existing layers."""
+    model = KAN.__new__(KAN)
+    nn.Sequential.__init__(model, *layers)
+    model.widths = [layers[0].in_features] + [layer.out_features for layer in layers]
+    return model
+
+
+def layer_inputs(model: nn.Module, x: torch.Tensor) -> list[tuple[KANLinear, torch.Tensor]]:
+    """(KANLinear, its input) for every KAN layer of ``model`` (layers.py:446-467)."""
+    out = []
+
+    def walk(m, h):
+        if isinstance(m, KANLinear):
+            out.append((m, h))
+            return m(h)
+        if isinstance(m, nn.Sequential):
+            for sub in m:
+                h = walk(sub, h)
+            return h
+        return m(h)
+
+    with torch.no_grad():
+        walk(model, x)
+    return out

@@ -1,0 +1,403 @@
+"""Parity of the sm_100a kernels with the oracle and the reference's golden vectors.
+
+Tolerances (metric max|a-b| / max(1, max|b|), reference tests/test_kernels.py:96-99):
+  float32 kernels vs float64 oracle ........ 1e-5 (layer values and gradients)
+  float32 primitives vs reference Triton ... 2e-5 (both float32)
+  bf16 fused tensor-core path .............. 2e-2, against the float64 oracle evaluated
+                                             on the same bf16-valued inputs and parameters
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+from conftest import load_golden, params_of, spec_of
+
+import kan_oracle as ko
+import kanforge_b200 as kb
+
+pytestmark = pytest.mark.gpu
+
+FP32_TOL = 1e-5
+BF16_TOL = 2e-2
+DEV = "cuda"
+
+
+def close(got, want, tol, what=""):
+    got = got.detach().double().cpu().numpy() if isinstance(got, torch.Tensor) else np.asarray(got)
+    err = ko.max_rel_err(got, want)
+    assert got.shape == np.shape(want), (what, got.shape, np.shape(want))
+    assert err <= tol, f"{what}: max rel err {err:.3e} > {tol:.0e}"
+
+
+def spec_of_basis(basis) -> dict:
+    cfg = basis.config()
+    if cfg["name"] == "bspline":
+        return {"kind": "bspline", "grid_size": cfg["grid_size"], "order": cfg["order"], "grid_range": cfg["grid_range"]}
+    if cfg["name"] == "rational":
+        return {"kind": "rational", "num_degree": cfg["num_degree"], "den_degree": cfg["den_degree"]}
+    out = {"kind": "poly", "family": cfg["name"], "degree": cfg["degree"], "input_map": cfg["input_map"]}
+    for k in ("alpha", "beta", "lam"):
+        if k in cfg:
+            out[k] = cfg[k]
+    return out
+
+
+def layer_numpy(layer) -> dict:
+    n_in = layer.in_features
+    params = {}
+    for k, v in layer.basis_params().items():
+        v = v.detach().double().cpu().numpy()
+        params[k] = v if v.shape[0] == n_in else np.repeat(v, n_in // v.shape[0], axis=0)
+    g = lambda t: None if t is None else t.detach().double().cpu().numpy()  # noqa: E731
+    return dict(coef=g(layer.coef), base_weight=g(layer.base_weight), bias=g(layer.bias), spec=spec_of_basis(layer.basis),
+                params=params, edge_scale=g(layer.edge_scale), edge_mask=g(layer.edge_mask))
+
+
+# ---------------------------------------------------------------------------
+# primitives F/G/P vs the reference's own Triton kernels and the oracle
+# ---------------------------------------------------------------------------
+
+PRIMS = load_golden("prims.npz")
+PRIM_BASES = {"bspline_5_3": kb.BSpline(5, 3), "chebyshev_5": kb.Chebyshev(5), "jacobi_4": kb.Jacobi(4, 0.5, 1.5)}
+
+
+@pytest.mark.parametrize("case", sorted(PRIM_BASES))
+@pytest.mark.parametrize("m", [0, 1, 2])
+def test_primitives_match_reference_triton(case, m):
+    plan = kb.plan_for(PRIM_BASES[case])
+    t = {k.split("/", 1)[1]: torch.as_tensor(v, device=DEV) for k, v in PRIMS.items() if k.startswith(case + "/")}
+    with torch.no_grad():
+        f = kb.kernels.prim_F(t["x"], t["c"], t["w"], t["grid"], plan, m)
+        g = kb.kernels.prim_G(t["x"], t["g"], t["w"], t["grid"], plan, m)
+        p = kb.kernels.prim_P(t["x"], t["g"], t["c"], t["grid"], plan, m)
+    for got, key in [(f, "F"), (g, "G"), (p, "P")]:
+        close(got, PRIMS[f"{case}/{key}{m}"], 2e-5, f"{case} {key}{m}")
+
+
+PRIM_SWEEP = [
+    (kb.BSpline(8, 3), 300, 37, 70),
+    (kb.BSpline(4, 1), 65, 5, 3),
+    (kb.BSpline(3, 2), 129, 9, 65),
+    (kb.BSpline(6, 5), 40, 6, 9),
+    (kb.Chebyshev(12), 200, 33, 66),
+    (kb.Chebyshev(4, input_map="identity"), 17, 3, 2),
+    (kb.Jacobi(6, 0.5, 0.5), 99, 12, 31),
+]
+
+
+@pytest.mark.parametrize("basis,n_b,n_in,n_out", PRIM_SWEEP, ids=lambda v: repr(v) if isinstance(v, kb.Basis) else str(v))
+@pytest.mark.parametrize("m", [0, 1, 2, 3])
+def test_primitives_match_oracle_ragged_shapes(basis, n_b, n_in, n_out, m):
+    plan = kb.plan_for(basis)
+    spec = spec_of_basis(basis)
+    rng = np.random.default_rng(7 + m)
+    lo, hi = spec.get("grid_range", (-1.0, 1.0))
+    x = rng.uniform(1.3 * lo - 0.2, 1.3 * hi + 0.2, (n_b, n_in))
+    w = rng.uniform(0.5, 1.5, (n_b, n_in))
+    g = rng.standard_normal((n_b, n_out))
+    c = rng.standard_normal((n_out, n_in, basis.size)) * 0.3
+    params = None
+    grid = np.zeros(1)
+    if spec["kind"] == "bspline":
+        grid = ko.default_grid(spec, n_in)
+        grid[:, 1:-1] += rng.uniform(-0.2, 0.2, (n_in, grid.shape[1] - 2)) * (grid[0, 1] - grid[0, 0])
+        params = {"grid": grid}
+    T = lambda a: torch.as_tensor(a, dtype=torch.float32, device=DEV)  # noqa: E731
+    x32 = x.astype(np.float32).astype(np.float64)
+    grid32 = grid.astype(np.float32).astype(np.float64)
+    p64 = None if params is None else {"grid": grid32}
+    with torch.no_grad():
+        f = kb.kernels.prim_F(T(x), T(c), T(w), T(grid), plan, m)
+        gg = kb.kernels.prim_G(T(x), T(g), T(w), T(grid), plan, m)
+        p = kb.kernels.prim_P(T(x), T(g), T(c), T(grid), plan, m)
+    close(f, ko.prim_F(x32, c, w, spec, m, p64), 5e-5, "F")
+    close(gg, ko.prim_G(x32, g, w, spec, m, p64), 5e-5, "G")
+    close(p, ko.prim_P(x32, g, c, spec, m, p64), 5e-5, "P")
+
+
+# ---------------------------------------------------------------------------
+# float32 layers: forward, all gradients, edge_derivative vs golden + oracle
+# ---------------------------------------------------------------------------
+
+LAYERS = load_golden("layers.npz")
+LAYER_BASES = {
+    "bspline_5_3": (kb.BSpline(5, 3), {}),
+    "bspline_8_3": (kb.BSpline(8, 3), {}),
+    "chebyshev_12": (kb.Chebyshev(12), {}),
+    "jacobi_6": (kb.Jacobi(6, 0.5, 0.5), {}),
+    "chebyshev_4_id_nobase": (kb.Chebyshev(4, input_map="identity"), {"base_activation": None}),
+    "rational_gelu_g2": (kb.Rational(5, 4, "gelu"), {"base_activation": None, "groups": 2}),
+    "rational_identity_g1": (kb.Rational(5, 4, "identity"), {"base_activation": None, "groups": 1}),
+}
+
+
+def golden_layer(case, dtype=torch.float32):
+    pre = f"{case}/state/"
+    state = {k[len(pre):]: v for k, v in LAYERS.items() if k.startswith(pre)}
+    basis, kw = LAYER_BASES[case]
+    n_out, n_in = state["coef"].shape[:2]
+    layer = kb.KANLinear(n_in, n_out, basis, edge_scale="edge_scale" in state, **kw)
+    layer.load_state_dict({k: torch.as_tensor(v) for k, v in state.items()})
+    return layer.to(device=DEV, dtype=dtype)
+
+
+@pytest.mark.parametrize("case", sorted(LAYER_BASES))
+def test_float32_layer_matches_reference_values_and_gradients(case):
+    layer = golden_layer(case)
+    x = torch.as_tensor(LAYERS[f"{case}/x"], dtype=torch.float32, device=DEV).requires_grad_()
+    y = layer(x)
+    close(y, LAYERS[f"{case}/y"], FP32_TOL, "y")
+    dy = torch.as_tensor(LAYERS[f"{case}/dy"], dtype=torch.float32, device=DEV)
+    names = [n for n, _ in layer.named_parameters()]
+    grads = torch.autograd.grad((y * dy).sum(), [x] + [p for _, p in layer.named_parameters()])
+    close(grads[0], LAYERS[f"{case}/grad/x"], FP32_TOL, "dx")
+    for n, gr in zip(names, grads[1:]):
+        close(gr, LAYERS[f"{case}/grad/{n}"], FP32_TOL, f"d{n}")
+
+
+@pytest.mark.parametrize("case", sorted(LAYER_BASES))
+@pytest.mark.parametrize("order", [0, 1, 2])
+def test_edge_derivative_matches_reference(case, order):
+    layer = golden_layer(case)
+    x = torch.as_tensor(LAYERS[f"{case}/x"], dtype=torch.float32, device=DEV)
+    with torch.no_grad():
+        d = layer.edge_derivative(x, order)
+    close(d, LAYERS[f"{case}/edge{order}"], FP32_TOL, f"edge{order}")
+
+
+@pytest.mark.parametrize("basis", [kb.Jacobi(6, 0.5, 0.5), kb.BSpline(8, 3), kb.Chebyshev(5)], ids=repr)
+@pytest.mark.parametrize("order", [0, 2, 3])
+def test_edge_derivative_vector_path_matches_oracle(basis, order):
+    """I % 4 == 0 takes the float4 streaming kernel; ragged batch."""
+    torch.manual_seed(0)
+    layer = kb.KANLinear(64, 24, basis, edge_scale=True, device=DEV)
+    with torch.no_grad():
+        layer.edge_scale.uniform_(0.5, 1.5)
+        layer.edge_mask[3, 5] = 0
+        layer.coef.normal_(0, 0.3)
+    x = torch.rand(301, 64, device=DEV) * 2.4 - 1.2
+    with torch.no_grad():
+        d = layer.edge_derivative(x, order)
+    n = layer_numpy(layer)
+    want = ko.edge_derivative(x.double().cpu().numpy(), n["coef"], n["base_weight"], n["spec"], n["params"], order,
+                              n["edge_scale"], n["edge_mask"])
+    close(d, want, FP32_TOL, "edge")
+
+
+def test_higher_order_input_derivatives_and_gradient_penalty():
+    """Closure of F/G/P: 1st-3rd input derivatives and the double backward into
+    coef (reference tests/test_kernels.py:102-121), against the oracle."""
+    torch.manual_seed(0)
+    for basis in (kb.BSpline(5, 3), kb.Chebyshev(5), kb.Jacobi(4, 0.5, 1.5)):
+        layer = kb.KANLinear(4, 5, basis, edge_scale=True, device=DEV)
+        with torch.no_grad():
+            layer.coef.normal_(0, 0.5)
+            layer.edge_scale.uniform_(0.5, 1.5)
+            layer.bias.normal_()
+        x0 = torch.rand(37, 4, device=DEV) * 1.8 - 0.9
+        wts = torch.linspace(-1, 1, 5, device=DEV)
+        x = x0.clone().requires_grad_()
+        y = layer(x)
+        loss = (y * wts).sum()
+        (gx,) = torch.autograd.grad(loss, x, create_graph=True)
+        (gxx,) = torch.autograd.grad(gx.sum(), x, create_graph=True)
+        (gxxx,) = torch.autograd.grad(gxx.sum(), x, create_graph=True)
+        (gc,) = torch.autograd.grad((gx**2).sum(), layer.coef)
+        n = layer_numpy(layer)
+        xs = x0.double().cpu().numpy()
+        w = wts.double().cpu().numpy()
+        eds = [ko.edge_derivative(xs, n["coef"], n["base_weight"], n["spec"], n["params"], m, n["edge_scale"], n["edge_mask"])
+               for m in (1, 2, 3)]
+        for got, ed, what in zip((gx, gxx, gxxx), eds, ("gx", "gxx", "gxxx")):
+            close(got, np.einsum("boi,o->bi", ed, w), 2e-5, f"{basis!r} {what}")
+        # d/dcoef sum_b,i gx^2 = 2 sum_b gx[b,i] w_o phi'_k(x_bi) s_oi m_oi
+        gx_np = np.einsum("boi,o->bi", eds[0], w)
+        dphi = ko.basis_eval(n["spec"], xs, 1, n["params"])
+        scale = n["edge_scale"] * n["edge_mask"]
+        want = 2 * np.einsum("bi,o,bik->oik", gx_np, w, dphi) * scale[..., None]
+        close(gc, want, 2e-5, f"{basis!r} gradient penalty")
+
+
+def test_reference_model_file_forward():
+    import kanforge_b200.convert as cv
+    from conftest import GOLDEN
+
+    model = cv.load(GOLDEN / "ref_model.npz").to(DEV)
+    io = load_golden("ref_model_io.npz")
+    with torch.no_grad():
+        y = model(torch.as_tensor(io["x"], device=DEV))
+    close(y, io["y"], FP32_TOL, "model file")
+
+
+# ---------------------------------------------------------------------------
+# bf16 fused tensor-core path
+# ---------------------------------------------------------------------------
+
+FUSED_CASES = [
+    # basis, B, I, O, base, bias, edge_scale
+    (kb.Chebyshev(12), 300, 40, 264, True, True, False),
+    (kb.BSpline(8, 3), 257, 37, 136, True, True, True),
+    (kb.Jacobi(6, 0.5, 0.5), 130, 64, 256, True, True, False),
+    (kb.Chebyshev(20), 200, 20, 64, True, True, False),         # f_pad 32
+    (kb.Chebyshev(5), 129, 9, 24, False, False, False),          # no base, no bias
+    (kb.BSpline(5, 3, (-2.0, 2.0)), 1030, 16, 520, True, True, False),
+    (kb.BSpline(4, 1), 64, 8, 8, True, True, False),
+    (kb.Chebyshev(4, input_map="identity"), 77, 12, 40, True, True, False),
+]
+
+
+def make_bf16_layer(basis, n_in, n_out, base, bias, scale, seed=0):
+    torch.manual_seed(seed)
+    kw = {} if base else {"base_activation": None}
+    layer = kb.KANLinear(n_in, n_out, basis, bias=bias, edge_scale=scale, **kw)
+    with torch.no_grad():
+        layer.coef.normal_(0, 1.0 / np.sqrt(n_in * basis.size))
+        if layer.bias is not None:
+            layer.bias.normal_(0, 0.1)
+        if scale:
+            layer.edge_scale.uniform_(0.5, 1.5)
+        layer.edge_mask[0, -1] = 0
+        if hasattr(layer, "basis_grid"):  # non-uniform per-input grids
+            g = layer.basis_grid
+            step = (g[:, 1] - g[:, 0])[:, None]
+            g[:, 1:-1] += (torch.rand_like(g[:, 1:-1]) - 0.5) * 0.4 * step
+    return layer.to(device=DEV, dtype=torch.bfloat16)
+
+
+@pytest.mark.parametrize("basis,n_b,n_in,n_out,base,bias,scale", FUSED_CASES, ids=lambda v: repr(v) if isinstance(v, kb.Basis) else str(v))
+def test_bf16_fused_layer_forward_and_gradients(basis, n_b, n_in, n_out, base, bias, scale):
+    layer = make_bf16_layer(basis, n_in, n_out, base, bias, scale)
+    x0 = (torch.randn(n_b, n_in, device=DEV) * 1.2).clamp(-3, 3).to(torch.bfloat16)
+    assert kb.kernels.fused_ok(layer._plan, x0, n_out, base)
+    x = x0.clone().requires_grad_()
+    y = layer(x)
+    assert y.dtype == torch.bfloat16
+    dy = (torch.randn(n_b, n_out, device=DEV) * 0.5).to(torch.bfloat16)
+    params = [p for _, p in layer.named_parameters()]
+    names = [n for n, _ in layer.named_parameters()]
+    grads = torch.autograd.grad(y, [x] + params, dy)
+    n = layer_numpy(layer)
+    xs = x0.double().cpu().numpy()
+    kw = dict(coef=n["coef"], base_weight=n["base_weight"], bias=n["bias"], spec=n["spec"], params=n["params"],
+              edge_scale=n["edge_scale"], edge_mask=n["edge_mask"])
+    close(y, ko.kan_linear(xs, **kw), BF16_TOL, "y")
+    want = ko.kan_linear_backward(xs, dy.double().cpu().numpy(), **kw)
+    close(grads[0], want["dx"], BF16_TOL, "dx")
+    key = {"coef": "dcoef", "base_weight": "dbase_weight", "bias": "dbias", "edge_scale": "dedge_scale"}
+    for nme, gr in zip(names, grads[1:]):
+        close(gr, want[key[nme]], BF16_TOL, f"d{nme}")
+
+
+def test_bf16_fused_multi_tile_persistent_against_float32_primitives():
+    """Enough tiles that every persistent CTA runs several (both TMEM accumulators,
+    every pipeline phase); checked against the float32 primitive kernels."""
+    torch.manual_seed(1)
+    n_b, n_in, n_out = 16384 + 77, 64, 1024
+    layer = make_bf16_layer(kb.Chebyshev(12), n_in, n_out, True, True, False, seed=1)
+    x0 = torch.randn(n_b, n_in, device=DEV).clamp(-3, 3).to(torch.bfloat16)
+    x = x0.clone().requires_grad_()
+    y = layer(x)
+    dy = (torch.randn(n_b, n_out, device=DEV) * 0.1).to(torch.bfloat16)
+    gx, gc, gb = torch.autograd.grad(y, [x, layer.coef, layer.base_weight], dy)
+    plan = layer._plan
+    xf, dyf = x0.float(), dy.float()
+    ce, be = layer.effective_coef().float().detach(), layer.effective_base_weight().float().detach()
+    ones = torch.ones_like(xf)
+    g0 = xf.new_zeros(1)
+    with torch.no_grad():
+        y_ref = kb.kernels.prim_F(xf, ce, ones, g0, plan, 0) + torch.nn.functional.silu(xf) @ be.T + layer.bias.float()
+        s = torch.sigmoid(xf)
+        gx_ref = kb.kernels.prim_P(xf, dyf, ce, g0, plan, 1) + (dyf @ be) * (s * (1 + xf * (1 - s)))
+        gc_ref = kb.kernels.prim_G(xf, dyf, ones, g0, plan, 0)
+        gb_ref = dyf.T @ torch.nn.functional.silu(xf)
+    for got, ref, what in ((y, y_ref, "y"), (gx, gx_ref, "dx"), (gc, gc_ref, "dcoef"), (gb, gb_ref, "dbase")):
+        close(got.float(), ref.double().cpu().numpy(), BF16_TOL, what)
+    kb.kernels.check_device_errors()
+
+
+def test_bf16_layer_double_backward_uses_differentiable_path():
+    layer = make_bf16_layer(kb.Chebyshev(6), 8, 16, True, True, False)
+    x = (torch.rand(33, 8, device=DEV) * 2 - 1).to(torch.bfloat16).requires_grad_()
+    y = layer(x)
+    (gx,) = torch.autograd.grad(y.float().sum(), x, create_graph=True)
+    (gc,) = torch.autograd.grad((gx.float() ** 2).sum(), layer.coef)
+    assert gc.shape == layer.coef.shape and torch.isfinite(gc).all()
+    n = layer_numpy(layer)
+    xs = x.detach().double().cpu().numpy()
+    ed = ko.edge_derivative(xs, n["coef"], n["base_weight"], n["spec"], n["params"], 1, n["edge_scale"], n["edge_mask"])
+    close(gx, ed.sum(1), BF16_TOL, "gx")
+
+
+# ---------------------------------------------------------------------------
+# GR-KAN (rational) and KAN blocks
+# ---------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, FP32_TOL), (torch.bfloat16, BF16_TOL)])
+def test_grkan_forward_and_gradients(dtype, tol):
+    torch.manual_seed(0)
+    layer = kb.GRKAN(64, 48, groups=8)
+    with torch.no_grad():
+        layer.basis_numerator.add_(0.05 * torch.randn_like(layer.basis_numerator))
+        layer.basis_denominator.add_(0.05 * torch.randn_like(layer.basis_denominator))
+    layer = layer.to(device=DEV, dtype=dtype)
+    x0 = (torch.randn(513, 64, device=DEV) * 1.5).to(dtype)
+    x = x0.clone().requires_grad_()
+    y = layer(x)
+    dy = torch.randn_like(y)
+    names = [n for n, _ in layer.named_parameters()]
+    grads = torch.autograd.grad(y, [x] + [p for _, p in layer.named_parameters()], dy)
+    n = layer_numpy(layer)
+    xs = x0.double().cpu().numpy()
+    kw = dict(coef=n["coef"], base_weight=None, bias=n["bias"], spec=n["spec"], params=n["params"], edge_scale=None,
+              edge_mask=n["edge_mask"])
+    close(y, ko.kan_linear(xs, **kw), tol, "y")
+    want = ko.kan_linear_backward(xs, dy.double().cpu().numpy(), groups=8, **kw)
+    close(grads[0], want["dx"], tol, "dx")
+    key = {"coef": "dcoef", "bias": "dbias", "basis_numerator": "dnumerator", "basis_denominator": "ddenominator"}
+    for nme, gr in zip(names, grads[1:]):
+        # parameter gradients are sums over 513 x 8 inputs: scale the bf16 bound by their size
+        close(gr, want[key[nme]], tol if dtype == torch.float32 else 5e-2, f"d{nme}")
+
+
+def test_grkan_starts_as_gelu_and_keeps_variance():
+    """reference tests/test_layers.py:84-96, on the CUDA kernels."""
+    torch.manual_seed(0)
+    layer = kb.GRKAN(64, 64, groups=8).to(DEV)
+    x = torch.randn(4096, 64, device=DEV)
+    with torch.no_grad():
+        assert 0.7 < layer(x).std().item() < 1.4
+        z = torch.linspace(-3, 3, 301, device=DEV)[:, None].expand(301, 64).contiguous()
+        acts = kb.kernels.rational_act(z, layer.basis_numerator, layer.basis_denominator, layer._plan, 8)
+    assert (acts[:, 0] - torch.nn.functional.gelu(z[:, 0])).abs().max() < 2e-2
+
+
+def test_kanffn_and_conv2d_match_oracle():
+    torch.manual_seed(0)
+    ffn = kb.KANFFN(32, 64, kind="grkan", groups=8).to(DEV)
+    x = torch.randn(3, 5, 32, device=DEV)
+    with torch.no_grad():
+        y = ffn(x)
+        h = ffn.fc1(x)
+    n1, n2 = layer_numpy(ffn.fc1), layer_numpy(ffn.fc2)
+    xs = x.double().cpu().numpy()
+    h_ref = ko.kan_linear(xs, n1["coef"], None, n1["bias"], n1["spec"], n1["params"], None, n1["edge_mask"])
+    close(h, h_ref, FP32_TOL, "fc1")
+    y_ref = ko.kan_linear(h.double().cpu().numpy(), n2["coef"], None, n2["bias"], n2["spec"], n2["params"], None, n2["edge_mask"])
+    close(y, y_ref, FP32_TOL, "fc2")
+
+    conv = kb.KANConv2d(3, 4, 3, padding=1, basis=kb.BSpline(5, 3)).to(DEV)
+    img = torch.rand(2, 3, 6, 7, device=DEV) * 2 - 1
+    with torch.no_grad():
+        out = conv(img)
+    assert out.shape == (2, 4, 6, 7)
+    n = layer_numpy(conv.kans[0])
+    patches = torch.nn.functional.unfold(img, 3, padding=1).transpose(1, 2).double().cpu().numpy()  # (2, 42, 27)
+    ref = ko.kan_linear(patches, n["coef"], n["base_weight"], n["bias"], n["spec"], n["params"], None, n["edge_mask"])
+    close(out.permute(0, 2, 3, 1).reshape(2, 42, 4), ref, FP32_TOL, "conv2d")
+
+
+def test_no_device_errors_recorded():
+    kb.kernels.check_device_errors()
