@@ -41,6 +41,21 @@ int check_launch(const char* what) {
 
 }  // namespace kf
 
+int kf::bind_device(const void* ptr) {
+  cudaPointerAttributes attr;
+  cudaError_t err = cudaPointerGetAttributes(&attr, ptr);
+  if (err != cudaSuccess || (attr.type != cudaMemoryTypeDevice && attr.type != cudaMemoryTypeManaged)) {
+    cudaGetLastError();
+    set_error("operand %p is not CUDA device memory", ptr);
+    return KF_ERR_ARG;
+  }
+  // Since CUDA 12, cudaSetDevice initialises the device's primary context and
+  // makes it current on this thread immediately, which the driver calls of
+  // the tensor-map encoder need.
+  KF_CUDA_RET(cudaSetDevice(attr.device));
+  return KF_OK;
+}
+
 extern "C" int kf_version(void) { return KF_ABI_VERSION; }
 
 extern "C" const char* kf_last_error(void) { return kf::g_msg; }

@@ -39,6 +39,13 @@ void clear_error();
 // Checks the launch that was just enqueued.
 int check_launch(const char* what);
 
+// Makes the device that owns `ptr` current for this host thread in the
+// library's (statically linked) CUDA runtime and binds its primary context.
+// Every entry point calls it: callers such as torch's autograd engine launch
+// from worker threads on which this runtime has never run, and a process may
+// drive several GPUs.
+int bind_device(const void* ptr);
+
 // ---- device error word ----------------------------------------------------
 // Bit set by a kernel whose bounded wait ran out; read and cleared by
 // kf_device_status().  Kernels never trap: they record and return.

@@ -142,8 +142,6 @@ struct EdgeLaunch {
 
 }  // namespace
 
-int edge_derivative_launch(EdgeArgs& A, const kf_basis_desc* basis, cudaStream_t stream);
-
 }  // namespace kf
 
 extern "C" int kf_edge_derivative(const float* x, const float* coef, const float* base_eff, const float* grid,
@@ -156,6 +154,7 @@ extern "C" int kf_edge_derivative(const float* x, const float* coef, const float
   KF_CHECK_ARG(B >= 0 && I >= 1 && O >= 1 && nf >= 1 && order >= 0, "kf_edge_derivative: bad sizes");
   KF_CHECK_ARG(nf <= KF_NF_MAX, "kf_edge_derivative: %d features exceed the limit %d", nf, KF_NF_MAX);
   KF_CHECK_ARG(x && coef && out, "kf_edge_derivative: null tensor pointer");
+  if (int rc = bind_device(x)) return rc;
   KF_CHECK_ARG(base_eff == nullptr || (silu_poly != nullptr && n_poly >= 1 && n_poly <= 8),
                "kf_edge_derivative: the base term needs 1..8 SiLU polynomial coefficients");
   EdgeArgs A{};

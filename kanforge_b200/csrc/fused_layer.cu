@@ -1052,6 +1052,7 @@ extern "C" int kf_fwd(const void* x, const void* packed, const void* bias, const
   using namespace kf;
   clear_error();
   KF_CHECK_ARG(x && packed && y, "kf_fwd: null tensor pointer");
+  if (int rc = bind_device(x)) return rc;
   KF_CHECK_ARG(B >= 0 && I >= 1 && O >= 1, "kf_fwd: bad sizes");
   KF_CHECK_ARG(O % 8 == 0, "kf_fwd: O (%d) must be a multiple of 8", O);
   FwdParams p{};
@@ -1080,6 +1081,7 @@ extern "C" int kf_dgrad(const void* x, const void* dy, const void* packed, const
   using namespace kf;
   clear_error();
   KF_CHECK_ARG(x && dy && packed && dx, "kf_dgrad: null tensor pointer");
+  if (int rc = bind_device(x)) return rc;
   KF_CHECK_ARG(B >= 0 && I >= 1 && O >= 1, "kf_dgrad: bad sizes");
   KF_CHECK_ARG(O % 8 == 0, "kf_dgrad: O (%d) must be a multiple of 8", O);
   DgradParams p{};
@@ -1107,6 +1109,7 @@ extern "C" int kf_wgrad(const void* x, const void* dy, const float* grid, const 
   using namespace kf;
   clear_error();
   KF_CHECK_ARG(x && dy && dcoef_eff, "kf_wgrad: null tensor pointer");
+  if (int rc = bind_device(x)) return rc;
   KF_CHECK_ARG(B >= 0 && I >= 1 && O >= 1 && K >= 1, "kf_wgrad: bad sizes");
   KF_CHECK_ARG(O % 8 == 0, "kf_wgrad: O (%d) must be a multiple of 8", O);
   KF_CHECK_ARG(fold != nullptr || K == nt, "kf_wgrad: without a fold K must equal nt");

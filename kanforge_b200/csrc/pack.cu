@@ -61,6 +61,7 @@ extern "C" int kf_pack_coef(const void* coef_eff, const void* base_eff, const fl
   using namespace kf;
   clear_error();
   KF_CHECK_ARG(coef_eff && packed, "kf_pack_coef: null pointer");
+  if (int rc = bind_device(packed)) return rc;
   KF_CHECK_ARG(O >= 1 && I >= 1 && K >= 1 && nt >= 1 && K <= kMaxFold && nt <= kMaxFold, "kf_pack_coef: bad sizes");
   KF_CHECK_ARG(f_pad % 8 == 0 && f_pad >= nt + (base_eff ? 1 : 0), "kf_pack_coef: f_pad %d too small", f_pad);
   KF_CHECK_ARG(fold != nullptr || nt <= K, "kf_pack_coef: without a fold nt must be <= K");

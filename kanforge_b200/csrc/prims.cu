@@ -280,6 +280,7 @@ extern "C" int kf_prim(int op, int m, const float* x, const float* a, const floa
                (long long)B, I, O, nf, m);
   KF_CHECK_ARG(nf <= KF_NF_MAX, "kf_prim: %d features exceed the limit %d", nf, KF_NF_MAX);
   KF_CHECK_ARG(x && a && b && out, "kf_prim: null tensor pointer");
+  if (int rc = bind_device(x)) return rc;
   FeatArgs fa{};
   fa.m = m;
   fa.nf = nf;

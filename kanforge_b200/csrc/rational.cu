@@ -156,6 +156,7 @@ extern "C" int kf_rational_act(const void* x, const float* num, const float* den
   RatParams p{};
   if (int rc = rat_params(basis, I, p)) return rc;
   KF_CHECK_ARG(x && num && den && out && B >= 0 && m >= 0 && m <= KF_RAT_MAX_ORDER, "kf_rational_act: bad arguments");
+  if (int rc = bind_device(x)) return rc;
   if (B == 0) return KF_OK;
   const int64_t n = B * I;
   const size_t smem = sizeof(float) * p.groups * (p.na + p.nb);
@@ -181,6 +182,7 @@ extern "C" int kf_rational_bwd(const void* x, const void* dr, const float* num, 
   RatParams p{};
   if (int rc = rat_params(basis, I, p)) return rc;
   KF_CHECK_ARG(x && dr && num && den && dx && dnum && dden && workspace && B >= 0, "kf_rational_bwd: bad arguments");
+  if (int rc = bind_device(x)) return rc;
   cudaStream_t s = (cudaStream_t)stream;
   if (B == 0) {
     KF_CUDA_RET(cudaMemsetAsync(dnum, 0, sizeof(float) * p.groups * p.na, s));

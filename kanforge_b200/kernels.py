@@ -386,9 +386,10 @@ class _RationalAct(torch.autograd.Function):
             desc = plan.desc(groups)
             ws_n = _lib.load().kf_rational_workspace(x.shape[0], x.shape[1], ctypes.byref(desc))
             ws = torch.empty(max(int(ws_n), 1), device=x.device, dtype=torch.float32)
-            _launch("kf_rational_bwd", _ptr(x), _ptr(g), _ptr(num.detach().float().contiguous()),
-                      _ptr(den.detach().float().contiguous()), _ptr(dx), _ptr(dnum), _ptr(dden), _ptr(ws), x.shape[0],
-                      x.shape[1], ctypes.byref(desc), _rat_dtype(x), _stream(x))
+            # keep the float32 copies alive until the launch is enqueued
+            numf, denf = num.detach().float().contiguous(), den.detach().float().contiguous()
+            _launch("kf_rational_bwd", _ptr(x), _ptr(g), _ptr(numf), _ptr(denf), _ptr(dx), _ptr(dnum), _ptr(dden),
+                    _ptr(ws), x.shape[0], x.shape[1], ctypes.byref(desc), _rat_dtype(x), _stream(x))
             return (dx if need[0] else None, dnum.to(num.dtype) if need[1] else None,
                     dden.to(den.dtype) if need[2] else None, None, None, None)
         if need[1] or need[2]:

@@ -310,8 +310,9 @@ def test_bf16_fused_multi_tile_persistent_against_float32_primitives():
         y_ref = kb.kernels.prim_F(xf, ce, ones, g0, plan, 0) + torch.nn.functional.silu(xf) @ be.T + layer.bias.float()
         s = torch.sigmoid(xf)
         gx_ref = kb.kernels.prim_P(xf, dyf, ce, g0, plan, 1) + (dyf @ be) * (s * (1 + xf * (1 - s)))
-        gc_ref = kb.kernels.prim_G(xf, dyf, ones, g0, plan, 0)
-        gb_ref = dyf.T @ torch.nn.functional.silu(xf)
+        mask = layer.edge_mask.float()
+        gc_ref = kb.kernels.prim_G(xf, dyf, ones, g0, plan, 0) * mask[..., None]
+        gb_ref = (dyf.T @ torch.nn.functional.silu(xf)) * mask
     for got, ref, what in ((y, y_ref, "y"), (gx, gx_ref, "dx"), (gc, gc_ref, "dcoef"), (gb, gb_ref, "dbase")):
         close(got.float(), ref.double().cpu().numpy(), BF16_TOL, what)
     kb.kernels.check_device_errors()
