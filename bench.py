@@ -70,7 +70,7 @@ def dist_env():
 # ---------------------------------------------------------------------------
 
 
-def build_workload(cfg: int, dtype_name: str, device, seed: int):
+def build_workload(cfg: int, dtype_name: str, device, seed: int, tokens: int | None = None):
     """(model, x, step_fn, params, flops_per_step, unit_per_step, per-kernel work)."""
     import torch
 
@@ -93,20 +93,22 @@ def build_workload(cfg: int, dtype_name: str, device, seed: int):
         with torch.no_grad():
             model.coef.normal_(0, 0.1 / np.sqrt(1024 * 11))
         model = model.to(dtype)
-        x = torch.randn(65536, 1024, generator=g).clamp(-3, 3).to(device=device, dtype=dtype)
+        nb = tokens or 65536
+        x = torch.randn(nb, 1024, generator=g).clamp(-3, 3).to(device=device, dtype=dtype)
         loss_fn = lambda y: y.float().square().mean()  # noqa: E731
-        flops = 6 * 65536 * 1024 * 1024 * 12
-        kwork = {n: 2.0 * 65536 * 1024 * 1024 * 12 for n in ("kf_fwd", "kf_dgrad", "kf_wgrad")}
+        flops = 6 * nb * 1024 * 1024 * 12
+        kwork = {n: 2.0 * nb * 1024 * 1024 * 12 for n in ("kf_fwd", "kf_dgrad", "kf_wgrad")}
     elif cfg == 2:
         dtype = torch.bfloat16
         model = kb.KANLinear(4096, 4096, kb.Chebyshev(12), device=device)
         with torch.no_grad():
             model.coef.normal_(0, 1.0 / np.sqrt(4096 * 13))
         model = model.to(dtype)
-        x = torch.randn(16384, 4096, generator=g).to(device=device, dtype=dtype)
+        nb = tokens or 16384
+        x = torch.randn(nb, 4096, generator=g).to(device=device, dtype=dtype)
         loss_fn = lambda y: y.float().square().mean()  # noqa: E731
-        flops = 6 * 16384 * 4096 * 4096 * 14
-        kwork = {n: 2.0 * 16384 * 4096 * 4096 * 14 for n in ("kf_fwd", "kf_dgrad", "kf_wgrad")}
+        flops = 6 * nb * 4096 * 4096 * 14
+        kwork = {n: 2.0 * nb * 4096 * 4096 * 14 for n in ("kf_fwd", "kf_dgrad", "kf_wgrad")}
     elif cfg == 3:
         dtype = torch.bfloat16
         model = kb.KANFFN(768, 3072, kind="grkan", groups=8).to(device=device, dtype=dtype)
@@ -141,7 +143,7 @@ def build_workload(cfg: int, dtype_name: str, device, seed: int):
         loss.backward()
         return loss
 
-    return model, x, step, params, flops, CONFIGS[cfg]["tokens"], kwork, dtype
+    return model, x, step, params, flops, x.shape[0] if cfg in (1, 2) else CONFIGS[cfg]["tokens"], kwork, dtype
 
 
 # ---------------------------------------------------------------------------
@@ -323,7 +325,8 @@ def run_ours(args, world, rank, local):
         dist.init_process_group("nccl", device_id=device, timeout=__import__("datetime").timedelta(seconds=120))
         pg = dist.group.WORLD
     cfg = args.config
-    model, x, step, params, flops, units, kwork, dtype = build_workload(cfg, args.dtype, device, seed=1234 + rank)
+    model, x, step, params, flops, units, kwork, dtype = build_workload(cfg, args.dtype, device, seed=1234 + rank,
+                                                                        tokens=args.tokens)
 
     def full_step():
         out = step()
@@ -483,6 +486,8 @@ def main(argv=None):
     ap.add_argument("--dtype", default="bf16", choices=["bf16", "fp32"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tokens", type=int, default=None,
+                    help="profiling case: override the batch of configs 1-2 (not a bench line)")
     args = ap.parse_args(argv)
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

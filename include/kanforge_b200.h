@@ -101,13 +101,20 @@ int kf_prim(int op, int m, const float* x, const float* a, const float* b, const
 int kf_pack_coef(const void* coef_eff, const void* base_eff, const float* fold, void* packed,
                  int32_t O, int32_t I, int32_t K, int32_t nt, int32_t f_pad, int dtype, void* stream);
 
+/* Knot tables of per-input B-spline grids, read by the fused kernels: for each
+ * input i, tab[i, 0, r] = extended knot t_r (r < G + 2 order + 1, order mean
+ * steps per side, kanforge/bases/spline.py:22-30) and tab[i, q, r] =
+ * 1 / (t_{r+q} - t_r) (q = 1..order); rows of 64 floats, zero-padded.
+ * grid (I, G+1) float32, tab (I, order+1, 64) float32, 16-byte aligned. */
+int kf_knot_tables(const float* grid, float* tab, int32_t I, int32_t grid_size, int32_t order, void* stream);
+
 /* Fused KANLinear forward on tcgen05 (bf16 operands, f32 accumulation):
  *   y[b,o] = sum_{i,j} feat_j(x[b,i]) packed[o,i,j] + bias[o]
  * feat = basis features (B-spline values or T_j(g(x))) and, at column nt,
  * silu(x) when has_base.  x (B,I) bf16, y (B,O) bf16, bias (O) bf16 or null,
- * grid (I, G+1) float32 for B-splines.  Requires I*f_pad % 64 == 0, O % 16 == 0,
- * B >= 1.  (kanforge/torch/layers.py:171-192 with kernels.py:143-150.) */
-int kf_fwd(const void* x, const void* packed, const void* bias, const float* grid, void* y, int64_t B,
+ * knot_tab: kf_knot_tables output for B-splines, else null.  Requires O % 8 == 0.
+ * (kanforge/torch/layers.py:171-192 with kernels.py:143-150.) */
+int kf_fwd(const void* x, const void* packed, const void* bias, const float* knot_tab, void* y, int64_t B,
            int32_t I, int32_t O, int32_t nt, int32_t f_pad, int32_t has_base, const kf_basis_desc* basis,
            void* stream);
 
@@ -115,7 +122,7 @@ int kf_fwd(const void* x, const void* packed, const void* bias, const float* gri
  *   dx[b,i] = sum_j (sum_o dy[b,o] packed[o,i,j]) dfeat_j(x[b,i])
  * dfeat = d/dx of the forward features (the SiLU column included).
  * dy (B,O) bf16, dx (B,I) bf16.  (kanforge/torch/kernels.py:84 gx = w * P_{m+1}.) */
-int kf_dgrad(const void* x, const void* dy, const void* packed, const float* grid, void* dx, int64_t B,
+int kf_dgrad(const void* x, const void* dy, const void* packed, const float* knot_tab, void* dx, int64_t B,
              int32_t I, int32_t O, int32_t nt, int32_t f_pad, int32_t has_base, const kf_basis_desc* basis,
              void* stream);
 
@@ -124,7 +131,7 @@ int kf_dgrad(const void* x, const void* dy, const void* packed, const float* gri
  *   dcoef_eff[o,i,k] = sum_{j<nt} dpacked[o,i,j] fold[k,j]   (fold null: k = j)
  *   dbase[o,i] = dpacked[o,i,nt]                              (if dbase != null)
  * dcoef_eff (O,I,K) and dbase (O,I) in bf16.  (kanforge/torch/kernels.py:85, 97-98.) */
-int kf_wgrad(const void* x, const void* dy, const float* grid, const float* fold, void* dcoef_eff,
+int kf_wgrad(const void* x, const void* dy, const float* knot_tab, const float* fold, void* dcoef_eff,
              void* dbase, int64_t B, int32_t I, int32_t O, int32_t K, int32_t nt, int32_t f_pad,
              const kf_basis_desc* basis, void* stream);
 

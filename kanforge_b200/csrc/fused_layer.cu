@@ -56,7 +56,7 @@ struct BasisDev {
   int nt;        // basis feature columns (Chebyshev: T_0..T_{nt-1}; B-spline: size)
   int has_base;  // SiLU column at index nt
   int G, nk;     // B-spline grid intervals and extended knots
-  const float* grid;
+  const float* tab;  // B-spline knot tables (I, order + 1, 64), see kf_knot_tables
 };
 
 struct Ctl {
@@ -78,13 +78,24 @@ __device__ __forceinline__ void named_bar(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
-// Knot table of one input: row 0 = extended knots t_r (r < nk), row q = 1/(t_{r+q} - t_r).
+// Knot table of one input (kTabStride floats per row): row 0 = extended knots
+// t_r (r < nk), row q = 1 / (t_{r+q} - t_r) for r <= nk - 1 - q; zero elsewhere.
 template <int BK>
-__device__ __forceinline__ float knot_table_entry(const BasisDev& bd, int i, int q, int r) {
-  const float* g = bd.grid + (size_t)i * (bd.G + 1);
-  if (q == 0) return r < bd.nk ? extended_knot(g, bd.G, BK, r) : 0.0f;
-  if (r > bd.nk - 1 - q) return 0.0f;
-  return 1.0f / (extended_knot(g, bd.G, BK, r + q) - extended_knot(g, bd.G, BK, r));
+__global__ void __launch_bounds__(256) knot_table_kernel(const float* __restrict__ grid, float* __restrict__ tab, int I, int G) {
+  const int nk = G + 2 * BK + 1;
+  const int per_in = (BK + 1) * kTabStride;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < (int64_t)I * per_in; e += (int64_t)gridDim.x * blockDim.x) {
+    const int i = (int)(e / per_in), rem = (int)(e % per_in);
+    const int q = rem / kTabStride, r = rem % kTabStride;
+    const float* g = grid + (size_t)i * (G + 1);
+    float v = 0.0f;
+    if (q == 0) {
+      if (r < nk) v = extended_knot(g, G, BK, r);
+    } else if (r <= nk - 1 - q) {
+      v = 1.0f / (extended_knot(g, G, BK, r + q) - extended_knot(g, G, BK, r));
+    }
+    tab[e] = v;
+  }
 }
 
 // Abort path of the TMA thread: wait for the last load issued on every stage
@@ -202,7 +213,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fused_fwd_kernel(const __grid_
   uint8_t* sa = base;                                   // kStages x 16 KB
   uint8_t* sb = sa + kStages * kATile;                  // kStages x 32 KB
   Ctl* ctl = reinterpret_cast<Ctl*>(sb + kStages * kBTile);
-  float* tabs = reinterpret_cast<float*>(ctl + 1);      // B-spline: [group][buf][IPK][(BK+1) * 64]
+  constexpr int kTabIn = (BK + 1) * kTabStride;          // floats of one input's knot table
+  float* tabs = reinterpret_cast<float*>(align1024(reinterpret_cast<uint8_t*>(ctl + 1)));  // B-spline: [stage][IPK][kTabIn]
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   volatile int* abort = &ctl->abort;
 
@@ -242,7 +254,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fused_fwd_kernel(const __grid_
           const int s = it % kStages;
           const uint32_t ph = (it / kStages) & 1;
           if (!mbar_wait(&ctl->empty[s], ph ^ 1, abort)) break;
-          mbar_arrive_expect_tx(&ctl->full_b[s], kBTile);
+          if constexpr (BK > 0) {
+            // the knot tables of the step's inputs travel with the coefficient tile
+            const int n_in = min(IPK, p.I - k * IPK);
+            const uint32_t tb = (uint32_t)(n_in * kTabIn * sizeof(float));
+            mbar_arrive_expect_tx(&ctl->full_b[s], kBTile + tb);
+            bulk_load(tabs + s * IPK * kTabIn, p.bd.tab + (size_t)k * IPK * kTabIn, tb, &ctl->full_b[s]);
+          } else {
+            mbar_arrive_expect_tx(&ctl->full_b[s], kBTile);
+          }
           tma_load_2d(sb + s * kBTile, &tmap_c, &ctl->full_b[s], k * kBK, n * kBN);
         }
       }
@@ -330,40 +350,39 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fused_fwd_kernel(const __grid_
     }
   } else if (warp >= 8) {
     // ---------------- feature producers: x -> basis rows in smem ----------------
-    const int grp = (warp - 8) / 4;        // handles K-steps of parity grp
+    // Group grp owns the K-steps of global parity grp; each thread owns one row.
+    // The x values of a thread's next step are loaded one step ahead so global
+    // latency overlaps the current step.
+    const int grp = (warp - 8) / 4;
     const int row = ((warp - 8) % 4) * 32 + lane;
-    const int gtid = (warp - 8) % 4 * 32 + lane;  // 0..127 inside the group
-    int it = 0, local_step = 0;
-    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {  // abort is seen (uniformly) by the waits
+    int it = 0;
+    bool alive = true;
+    for (int t = blockIdx.x; t < n_tiles && alive; t += gridDim.x) {  // abort is seen (warp-uniformly) by the waits
       int m, n;
       p.tiles.get(t, m, n);
       const int64_t b = (int64_t)m * kBM + row;
       const bool row_ok = b < p.B;
-      const __nv_bfloat16* xrow = p.x + (row_ok ? b : 0) * p.I;
-      for (int k = 0; k < p.k_steps; ++k, ++it) {
-        if ((it & 1) != grp) continue;
-        const int s = it % kStages;
-        const uint32_t ph = (it / kStages) & 1;
+      const unsigned short* xrow = reinterpret_cast<const unsigned short*>(p.x) + (row_ok ? b : 0) * p.I;
+      int k = ((it & 1) == grp) ? 0 : 1;
+      unsigned short xa[IPK], xb[IPK];
+#pragma unroll
+      for (int u = 0; u < IPK; ++u) xa[u] = (row_ok && k < p.k_steps && k * IPK + u < p.I) ? __ldg(xrow + k * IPK + u) : 0;
+      for (; k < p.k_steps; k += 2) {
+        const int git = it + k;
+        const int s = git % kStages;
+        const uint32_t ph = (git / kStages) & 1;
         const int i0 = k * IPK;
-        // x values of this row for the IPK inputs of the step
+#pragma unroll
+        for (int u = 0; u < IPK; ++u) xb[u] = (row_ok && k + 2 < p.k_steps && i0 + 2 * IPK + u < p.I) ? __ldg(xrow + i0 + 2 * IPK + u) : 0;
+        bool ok = mbar_wait_warp(&ctl->empty[s], ph ^ 1, abort);
+        if constexpr (BK > 0) ok = ok && mbar_wait_warp(&ctl->full_b[s], ph, abort);  // tables landed
+        if (!ok) {
+          alive = false;
+          break;
+        }
         float xv[IPK];
 #pragma unroll
-        for (int u = 0; u < IPK; ++u) xv[u] = (row_ok && i0 + u < p.I) ? __bfloat162float(xrow[i0 + u]) : 0.0f;
-        float* tab = nullptr;
-        if constexpr (BK > 0) {
-          tab = tabs + ((grp * 2 + (local_step & 1)) * IPK) * ((BK + 1) * kTabStride);
-          const int per_in = (BK + 1) * kTabStride;
-          for (int e = gtid; e < IPK * per_in; e += 128) {
-            const int u = e / per_in, rem = e % per_in;
-            const int qq = rem / kTabStride, r = rem % kTabStride;
-            tab[e] = (i0 + u < p.I && r < p.bd.nk) ? knot_table_entry<BK>(p.bd, i0 + u, qq, r) : 0.0f;
-          }
-        }
-        ++local_step;
-        bool ok = mbar_wait_warp(&ctl->empty[s], ph ^ 1, abort);
-        // B-spline: the group barrier publishes the tables and makes the exit decision common
-        if constexpr (BK > 0) ok = named_bar_and(1 + grp, 128, ok);
-        if (!ok) break;
+        for (int u = 0; u < IPK; ++u) xv[u] = __uint_as_float((uint32_t)xa[u] << 16);
         uint8_t* arow = sa + s * kATile;
         if constexpr (BK == 0) {
 #pragma unroll
@@ -385,13 +404,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fused_fwd_kernel(const __grid_
             }
           }
         } else {
+          const float* tab_s = tabs + s * IPK * kTabIn;
 #pragma unroll
           for (int u = 0; u < IPK; ++u) {
             // zero the input's F columns, then scatter the BK+1 supported splines and silu
 #pragma unroll
             for (int c = 0; c < F / 8; ++c) *reinterpret_cast<uint4*>(arow + sw128_offset(row, u * (F / 8) + c)) = make_uint4(0, 0, 0, 0);
             if (i0 + u >= p.I) continue;
-            const float* tu = tab + u * ((BK + 1) * kTabStride);
+            const float* tu = tab_s + u * kTabIn;
             const int j0 = knot_interval(xv[u], tu, p.bd.nk);
             if (j0 >= 0) {
               float v[BK + 1];
@@ -414,7 +434,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fused_fwd_kernel(const __grid_
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&ctl->full_a[s]);
+#pragma unroll
+        for (int u = 0; u < IPK; ++u) xa[u] = xb[u];
       }
+      it += p.k_steps;
     }
   }
 
@@ -557,7 +580,7 @@ __global__ void __launch_bounds__(kDgradThreads, 1) fused_dgrad_kernel(const __g
         if (ok) {
           for (int e = etid; e < IPT * kTabStride; e += 128) {
             const int u = e / kTabStride, r = e % kTabStride;
-            tabs[e] = (i_base + u < p.I && r < p.bd.nk) ? knot_table_entry<BK>(p.bd, i_base + u, 0, r) : 0.0f;
+            tabs[e] = (i_base + u < p.I) ? __ldg(p.bd.tab + (size_t)(i_base + u) * ((BK + 1) * kTabStride) + r) : 0.0f;
           }
         }
         named_bar(1, 128);
@@ -666,22 +689,26 @@ struct WgradParams {
   int64_t B;
   int I, O, K;
   int k_steps;
+  int x_tma;  // x tiles arrive by TMA with the dy tile (row pitch 16-byte aligned)
   TileMap tiles;
   BasisDev bd;
 };
 
 constexpr int kWgradThreads = 512;  // w0 TMA, w1 MMA, w4-7 epilogue, w8-15 producers
+constexpr int kXTile = kBK * 8 * 2;  // x tile per stage: 64 rows x 8 inputs bf16 = 1 KB
 
 template <int BK, int F>
-__global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __grid_constant__ CUtensorMap tmap_dy, WgradParams p) {
+__global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __grid_constant__ CUtensorMap tmap_dy,
+                                                                       const __grid_constant__ CUtensorMap tmap_x, WgradParams p) {
   constexpr int IPT = kBM / F;  // inputs per tile (rows of the feature operand)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = align1024(smem_raw);
   uint8_t* sa = base;
   uint8_t* sb = sa + kStages * kATile;
   Ctl* ctl = reinterpret_cast<Ctl*>(sb + kStages * kBTile);
-  float* stg = reinterpret_cast<float*>(ctl + 1);   // epilogue staging [128][33]
-  float* tabs = stg + 128 * 33;                      // B-spline: per producer warp [(BK+1) * 64]
+  uint8_t* sx = align1024(reinterpret_cast<uint8_t*>(ctl + 1));  // x tiles [stage][64 rows][8 inputs]
+  float* stg = reinterpret_cast<float*>(sx + kStages * kXTile);  // epilogue staging [128][33]
+  float* tabs = stg + 128 * 33;                                   // B-spline: per producer warp [(BK+1) * 64]
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   volatile int* abort = &ctl->abort;
 
@@ -703,7 +730,10 @@ __global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __g
     tmem_alloc(&ctl->tmem_base, 512);
     tmem_relinquish();
   }
-  if (warp == 0 && lane == 0) prefetch_tmap(&tmap_dy);
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmap_dy);
+    if (p.x_tma) prefetch_tmap(&tmap_x);
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -716,14 +746,16 @@ __global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __g
       for (int t = blockIdx.x; t < n_tiles && !*abort; t += gridDim.x) {
         int m, n;
         p.tiles.get(t, m, n);
+        const int x0 = (m * IPT) & ~7;  // TMA x coordinate rounded down to 16 bytes
         for (int k = 0; k < p.k_steps; ++k, ++it) {
           const int s = it % kStages;
           const uint32_t ph = (it / kStages) & 1;
           if (!mbar_wait(&ctl->empty[s], ph ^ 1, abort)) break;
-          mbar_arrive_expect_tx(&ctl->full_b[s], kBTile);
+          mbar_arrive_expect_tx(&ctl->full_b[s], kBTile + (p.x_tma ? kXTile : 0));
 #pragma unroll
           for (int c = 0; c < kBN / 64; ++c)
             tma_load_2d(sb + s * kBTile + c * 8192, &tmap_dy, &ctl->full_b[s], n * kBN + c * 64, k * kBK);
+          if (p.x_tma) tma_load_2d(sx + s * kXTile, &tmap_x, &ctl->full_b[s], x0, k * kBK);
         }
       }
       if (*abort) drain_tma(ctl, it);
@@ -810,54 +842,58 @@ __global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __g
       }
     }
   } else if (warp >= 8) {
-    // producers: warp w handles input u = w - 8 of the tile's IPT inputs (F == 16: 8 inputs)
+    // producers: F == 16 -> warp w owns input u = w - 8 of the tile's 8 inputs, each
+    // lane two batch columns; F == 32 -> 4 inputs, warps 2u and 2u+1 split the 64 columns.
     const int pw = warp - 8;
+    const int u = (F == 16) ? pw : pw / 2;
+    const int bsub = (F == 16) ? lane * 2 : (pw % 2) * 32 + lane;  // first batch column of this lane
+    constexpr int NB = (F == 16) ? 2 : 1;
     float* tab = tabs + pw * ((BK + 1) * kTabStride);
     int it = 0;
     bool alive = true;
-    for (int t = blockIdx.x; t < n_tiles && alive; t += gridDim.x) {  // abort is seen (uniformly) by the waits
+    for (int t = blockIdx.x; t < n_tiles && alive; t += gridDim.x) {  // abort is seen (warp-uniformly) by the waits
       int m, n;
       p.tiles.get(t, m, n);
       const int i_base = m * IPT;
+      const int i = i_base + u;
+      const int xoff = i_base - (i_base & ~7) + u;  // column of input i inside the TMA x tile
       if constexpr (BK > 0) {
         __syncwarp();
-        if (pw < IPT) {
-          const int i = i_base + pw;
-          for (int e = lane; e < (BK + 1) * kTabStride; e += 32) {
-            const int qq = e / kTabStride, r = e % kTabStride;
-            tab[e] = (i < p.I && r < p.bd.nk) ? knot_table_entry<BK>(p.bd, i, qq, r) : 0.0f;
-          }
-        }
+        for (int e = lane; e < (BK + 1) * kTabStride; e += 32)
+          tab[e] = i < p.I ? __ldg(p.bd.tab + (size_t)i * ((BK + 1) * kTabStride) + e) : 0.0f;
         __syncwarp();
       }
       for (int k = 0; k < p.k_steps; ++k, ++it) {
         const int s = it % kStages;
         const uint32_t ph = (it / kStages) & 1;
-        // rows (inputs, features) handled by this warp: F == 16 -> warp pw owns input pw;
-        // F == 32 -> 4 inputs, warps 2u and 2u+1 split the 64 batch columns.
-        const int u = (F == 16) ? pw : pw / 2;
-        const int bsub = (F == 16) ? lane * 2 : (pw % 2) * 32 + lane;  // first batch column
-        const int nb = (F == 16) ? 2 : 1;
-        const int i = i_base + u;
         float xv[2] = {0.0f, 0.0f};
+        if (!p.x_tma) {
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
-          const int64_t b = (int64_t)k * kBK + bsub + r;
-          if (r < nb && b < p.B && i < p.I) xv[r] = __bfloat162float(p.x[b * p.I + i]);
+          for (int r = 0; r < NB; ++r) {
+            const int64_t b = (int64_t)k * kBK + bsub + r;
+            if (b < p.B && i < p.I) xv[r] = __bfloat162float(p.x[b * p.I + i]);
+          }
         }
-        if (!mbar_wait_warp(&ctl->empty[s], ph ^ 1, abort)) {
+        bool ok = mbar_wait_warp(&ctl->empty[s], ph ^ 1, abort);
+        if (p.x_tma) ok = ok && mbar_wait_warp(&ctl->full_b[s], ph, abort);  // x tile landed
+        if (!ok) {
           alive = false;
           break;
+        }
+        if (p.x_tma) {
+          const __nv_bfloat16* xt = reinterpret_cast<const __nv_bfloat16*>(sx + s * kXTile);
+#pragma unroll
+          for (int r = 0; r < NB; ++r) xv[r] = __bfloat162float(xt[(bsub + r) * 8 + xoff]);
         }
         uint8_t* at = sa + s * kATile;
         float f[2][F];
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
           const int64_t b = (int64_t)k * kBK + bsub + r;
-          const bool ok = r < nb && b < p.B && i < p.I;
+          const bool okr = r < NB && b < p.B && i < p.I;
 #pragma unroll
           for (int j = 0; j < F; ++j) f[r][j] = 0.0f;
-          if (!ok) continue;
+          if (!okr) continue;
           if constexpr (BK == 0) {
             cheb_row<F>(xv[r], p.bd, f[r]);
           } else {
@@ -886,11 +922,10 @@ __global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __g
 #pragma unroll
         for (int j = 0; j < F; ++j) {
           const int mr = u * F + j;
-          if (nb == 2) {
-            const uint32_t off = sw128_offset(mr, bsub >> 3) + (bsub & 7) * 2;
+          const uint32_t off = sw128_offset(mr, bsub >> 3) + (bsub & 7) * 2;
+          if (NB == 2) {
             *reinterpret_cast<uint32_t*>(at + off) = pack_bf16x2(f[0][j], f[1][j]);
           } else {
-            const uint32_t off = sw128_offset(mr, bsub >> 3) + (bsub & 7) * 2;
             *reinterpret_cast<__nv_bfloat16*>(at + off) = __float2bfloat16_rn(f[0][j]);
           }
         }
@@ -925,8 +960,10 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   return fn;
 }
 
-// 2-D bf16 tensor map: `rows` x `cols` row-major (cols contiguous), box box_cols x box_rows, 128-byte swizzle.
-int make_tmap_bf16(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int box_cols, int box_rows) {
+// 2-D bf16 tensor map: `rows` x `cols` row-major (cols contiguous), box box_cols x box_rows,
+// 128-byte swizzle (or none).
+int make_tmap_bf16(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int box_cols, int box_rows,
+                   bool swizzle = true) {
   auto enc = get_encode();
   if (!enc) {
     set_error("cuTensorMapEncodeTiled is not available from the driver");
@@ -939,7 +976,8 @@ int make_tmap_bf16(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols
   cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_error("cuTensorMapEncodeTiled failed (%d) for %lldx%lld box %dx%d", (int)r, (long long)rows, (long long)cols,
@@ -956,16 +994,17 @@ int sm_count() {
   return n > 0 ? n : 148;
 }
 
-int fill_basis(const kf_basis_desc* d, const float* grid, int nt, int has_base, int f_pad, BasisDev& bd) {
+int fill_basis(const kf_basis_desc* d, const float* knot_tab, int nt, int has_base, int f_pad, BasisDev& bd) {
   KF_CHECK_ARG(d != nullptr, "basis is null");
   KF_CHECK_ARG(f_pad == 16 || f_pad == 32, "f_pad must be 16 or 32 (got %d)", f_pad);
   KF_CHECK_ARG(nt >= 1 && nt + (has_base ? 1 : 0) <= f_pad, "nt %d (+ base) exceeds f_pad %d", nt, f_pad);
   bd.map = d->input_map;
   bd.nt = nt;
   bd.has_base = has_base;
-  bd.grid = grid;
+  bd.tab = knot_tab;
   if (d->kind == KF_BASIS_BSPLINE) {
-    KF_CHECK_ARG(grid != nullptr, "B-spline needs its grid");
+    KF_CHECK_ARG(knot_tab != nullptr, "B-spline needs its knot tables (kf_knot_tables)");
+    KF_CHECK_ARG(((uintptr_t)knot_tab % 16) == 0, "knot tables must be 16-byte aligned");
     KF_CHECK_ARG(d->order >= 1 && d->order <= kMaxOrder, "B-spline order %d unsupported", d->order);
     bd.G = d->grid_size;
     bd.nk = d->grid_size + 2 * d->order + 1;
@@ -1002,7 +1041,7 @@ struct FwdLaunch {
   template <int BK, int F>
   int go() const {
     constexpr int IPK = kBK / F;
-    const size_t smem = kMainSmem + (BK > 0 ? sizeof(float) * 4 * IPK * (BK + 1) * kTabStride : 0);
+    const size_t smem = kMainSmem + (BK > 0 ? 1024 + sizeof(float) * kStages * IPK * (BK + 1) * kTabStride : 0);
     auto kern = fused_fwd_kernel<BK, F>;
     KF_CUDA_RET(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     const int grid = (int)std::min<int64_t>(p.tiles.m_tiles * (int64_t)p.tiles.n_tiles, sm_count());
@@ -1028,16 +1067,16 @@ struct DgradLaunch {
 };
 
 struct WgradLaunch {
-  const CUtensorMap* tmap_dy;
+  const CUtensorMap *tmap_dy, *tmap_x;
   WgradParams p;
   cudaStream_t stream;
   template <int BK, int F>
   int go() const {
-    const size_t smem = kMainSmem + sizeof(float) * (128 * 33 + (BK > 0 ? 8 * (BK + 1) * kTabStride : 0));
+    const size_t smem = kMainSmem + 1024 + kStages * kXTile + sizeof(float) * (128 * 33 + (BK > 0 ? 8 * (BK + 1) * kTabStride : 0));
     auto kern = fused_wgrad_kernel<BK, F>;
     KF_CUDA_RET(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     const int grid = (int)std::min<int64_t>(p.tiles.m_tiles * (int64_t)p.tiles.n_tiles, sm_count());
-    kern<<<grid, kWgradThreads, smem, stream>>>(*tmap_dy, p);
+    kern<<<grid, kWgradThreads, smem, stream>>>(*tmap_dy, *tmap_x, p);
     return check_launch("kf_wgrad");
   }
 };
@@ -1046,7 +1085,7 @@ struct WgradLaunch {
 
 }  // namespace kf
 
-extern "C" int kf_fwd(const void* x, const void* packed, const void* bias, const float* grid, void* y, int64_t B,
+extern "C" int kf_fwd(const void* x, const void* packed, const void* bias, const float* knot_tab, void* y, int64_t B,
                       int32_t I, int32_t O, int32_t nt, int32_t f_pad, int32_t has_base, const kf_basis_desc* basis,
                       void* stream) {
   using namespace kf;
@@ -1056,7 +1095,7 @@ extern "C" int kf_fwd(const void* x, const void* packed, const void* bias, const
   KF_CHECK_ARG(B >= 0 && I >= 1 && O >= 1, "kf_fwd: bad sizes");
   KF_CHECK_ARG(O % 8 == 0, "kf_fwd: O (%d) must be a multiple of 8", O);
   FwdParams p{};
-  if (int rc = fill_basis(basis, grid, nt, has_base, f_pad, p.bd)) return rc;
+  if (int rc = fill_basis(basis, knot_tab, nt, has_base, f_pad, p.bd)) return rc;
   if (B == 0) return KF_OK;
   p.x = (const __nv_bfloat16*)x;
   p.bias = (const __nv_bfloat16*)bias;
@@ -1075,7 +1114,7 @@ extern "C" int kf_fwd(const void* x, const void* packed, const void* bias, const
   return dispatch_fused(basis, f_pad, L);
 }
 
-extern "C" int kf_dgrad(const void* x, const void* dy, const void* packed, const float* grid, void* dx, int64_t B,
+extern "C" int kf_dgrad(const void* x, const void* dy, const void* packed, const float* knot_tab, void* dx, int64_t B,
                         int32_t I, int32_t O, int32_t nt, int32_t f_pad, int32_t has_base, const kf_basis_desc* basis,
                         void* stream) {
   using namespace kf;
@@ -1085,7 +1124,7 @@ extern "C" int kf_dgrad(const void* x, const void* dy, const void* packed, const
   KF_CHECK_ARG(B >= 0 && I >= 1 && O >= 1, "kf_dgrad: bad sizes");
   KF_CHECK_ARG(O % 8 == 0, "kf_dgrad: O (%d) must be a multiple of 8", O);
   DgradParams p{};
-  if (int rc = fill_basis(basis, grid, nt, has_base, f_pad, p.bd)) return rc;
+  if (int rc = fill_basis(basis, knot_tab, nt, has_base, f_pad, p.bd)) return rc;
   if (B == 0) return KF_OK;
   p.x = (const __nv_bfloat16*)x;
   p.dx = (__nv_bfloat16*)dx;
@@ -1103,7 +1142,7 @@ extern "C" int kf_dgrad(const void* x, const void* dy, const void* packed, const
   return dispatch_fused(basis, f_pad, L);
 }
 
-extern "C" int kf_wgrad(const void* x, const void* dy, const float* grid, const float* fold, void* dcoef_eff,
+extern "C" int kf_wgrad(const void* x, const void* dy, const float* knot_tab, const float* fold, void* dcoef_eff,
                         void* dbase, int64_t B, int32_t I, int32_t O, int32_t K, int32_t nt, int32_t f_pad,
                         const kf_basis_desc* basis, void* stream) {
   using namespace kf;
@@ -1114,7 +1153,7 @@ extern "C" int kf_wgrad(const void* x, const void* dy, const float* grid, const 
   KF_CHECK_ARG(O % 8 == 0, "kf_wgrad: O (%d) must be a multiple of 8", O);
   KF_CHECK_ARG(fold != nullptr || K == nt, "kf_wgrad: without a fold K must equal nt");
   WgradParams p{};
-  if (int rc = fill_basis(basis, grid, nt, dbase != nullptr, f_pad, p.bd)) return rc;
+  if (int rc = fill_basis(basis, knot_tab, nt, dbase != nullptr, f_pad, p.bd)) return rc;
   cudaStream_t s = (cudaStream_t)stream;
   if (B == 0) {
     KF_CUDA_RET(cudaMemsetAsync(dcoef_eff, 0, sizeof(__nv_bfloat16) * (size_t)O * I * K, s));
@@ -1134,8 +1173,34 @@ extern "C" int kf_wgrad(const void* x, const void* dy, const float* grid, const 
   p.tiles.m_tiles = (int)cdiv(I, ipt);
   p.tiles.n_tiles = (int)cdiv(O, kBN);
   p.tiles.gm = p.tiles.m_tiles;  // M fastest: concurrent CTAs share the dy column block
-  CUtensorMap tdy;
+  CUtensorMap tdy, tx;
   if (int rc = make_tmap_bf16(&tdy, dy, B, O, 64, kBK)) return rc;
-  WgradLaunch L{&tdy, p, s};
+  p.x_tma = (I % 8 == 0) && ((uintptr_t)x % 16 == 0);
+  if (p.x_tma) {
+    if (int rc = make_tmap_bf16(&tx, x, B, I, 8, kBK, false)) return rc;
+  } else {
+    tx = tdy;  // unused
+  }
+  WgradLaunch L{&tdy, &tx, p, s};
   return dispatch_fused(basis, f_pad, L);
+}
+
+extern "C" int kf_knot_tables(const float* grid, float* tab, int32_t I, int32_t grid_size, int32_t order, void* stream) {
+  using namespace kf;
+  clear_error();
+  KF_CHECK_ARG(grid && tab && I >= 1 && grid_size >= 1, "kf_knot_tables: bad arguments");
+  KF_CHECK_ARG(order >= 1 && order <= kMaxOrder && grid_size + 2 * order + 1 <= kTabStride,
+               "kf_knot_tables: order %d / grid %d beyond the kernel limits", order, grid_size);
+  if (int rc = bind_device(grid)) return rc;
+  const int64_t n = (int64_t)I * (order + 1) * kTabStride;
+  const unsigned blocks = (unsigned)std::min<int64_t>(cdiv(n, 256), 148 * 8);
+  cudaStream_t s = (cudaStream_t)stream;
+  switch (order) {
+    case 1: knot_table_kernel<1><<<blocks, 256, 0, s>>>(grid, tab, I, grid_size); break;
+    case 2: knot_table_kernel<2><<<blocks, 256, 0, s>>>(grid, tab, I, grid_size); break;
+    case 3: knot_table_kernel<3><<<blocks, 256, 0, s>>>(grid, tab, I, grid_size); break;
+    case 4: knot_table_kernel<4><<<blocks, 256, 0, s>>>(grid, tab, I, grid_size); break;
+    default: knot_table_kernel<5><<<blocks, 256, 0, s>>>(grid, tab, I, grid_size); break;
+  }
+  return check_launch("kf_knot_tables");
 }

@@ -187,6 +187,16 @@ def spline_forward(x: torch.Tensor, coef: torch.Tensor, grid: torch.Tensor | Non
 # --- fused layer op (tcgen05) ------------------------------------------------
 
 
+def knot_tables(grid: torch.Tensor, plan: KernelPlan) -> torch.Tensor:
+    """(I, order + 1, 64) knot / reciprocal-difference tables of the per-input grids."""
+    g = grid.detach().float().contiguous()
+    n_in = g.shape[0]
+    grid_size, order = plan.consts
+    tab = torch.empty(n_in, order + 1, 64, device=g.device, dtype=torch.float32)
+    _launch("kf_knot_tables", _ptr(g), _ptr(tab), n_in, grid_size, order, _stream(g))
+    return tab
+
+
 def fused_layout(plan: KernelPlan, has_base: bool) -> tuple[int, int]:
     """(nt, f_pad): basis feature columns per input and the padded width (16 or 32)."""
     nt = plan.n_features(0)
@@ -241,11 +251,12 @@ class _FusedKANLinear(torch.autograd.Function):
         y = torch.empty(x.shape[0], n_out, device=x.device, dtype=_BF16)
         b = None if bias is None else bias.detach().to(_BF16).contiguous()
         g = None if grid is None else grid.detach().float().contiguous()
+        tab = None if grid is None else knot_tables(g, plan)
         desc = plan.desc()
-        _launch("kf_fwd", _ptr(x), _ptr(packed), _ptr(b), _ptr(g), _ptr(y), x.shape[0], n_in, n_out, nt, f_pad,
-                  int(has_base), ctypes.byref(desc), _stream(x))
+        _launch("kf_fwd", _ptr(x), _ptr(packed), _ptr(b), _ptr(tab), _ptr(y), x.shape[0], n_in, n_out, nt, f_pad,
+                int(has_base), ctypes.byref(desc), _stream(x))
         ctx.save_for_backward(x, coef_eff, base_eff, g)
-        ctx.packed, ctx.plan, ctx.has_bias = packed, plan, bias is not None
+        ctx.packed, ctx.knot_tab, ctx.plan, ctx.has_bias = packed, tab, plan, bias is not None
         ctx.layout = (nt, f_pad)
         return y
 
@@ -268,17 +279,17 @@ class _FusedKANLinear(torch.autograd.Function):
             fold = None
             if plan.folded and not plan.is_identity_fold():
                 fold = torch.tensor(plan.fold(0), dtype=torch.float32, device=x.device)
-            _launch("kf_wgrad", _ptr(x), _ptr(gy), _ptr(grid), _ptr(fold), _ptr(gc), _ptr(gb), x.shape[0], n_in, n_out,
+            _launch("kf_wgrad", _ptr(x), _ptr(gy), _ptr(ctx.knot_tab), _ptr(fold), _ptr(gc), _ptr(gb), x.shape[0], n_in, n_out,
                       k, nt, f_pad, ctypes.byref(desc), stream)
             gc = gc.to(coef_eff.dtype) if need[1] else None
             gb = gb.to(base_eff.dtype) if (gb is not None and need[2]) else None
         if need[0]:
             gx = torch.empty_like(x)
-            _launch("kf_dgrad", _ptr(x), _ptr(gy), _ptr(ctx.packed), _ptr(grid), _ptr(gx), x.shape[0], n_in, n_out, nt,
+            _launch("kf_dgrad", _ptr(x), _ptr(gy), _ptr(ctx.packed), _ptr(ctx.knot_tab), _ptr(gx), x.shape[0], n_in, n_out, nt,
                       f_pad, int(base_eff is not None), ctypes.byref(desc), stream)
         if need[3]:
             gbias = gy.float().sum(0)
-        ctx.packed = None
+        ctx.packed = ctx.knot_tab = None
         return gx, gc, gb, gbias, None, None
 
 
