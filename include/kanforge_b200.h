@@ -94,8 +94,8 @@ int kf_prim(int op, int m, const float* x, const float* a, const float* b, const
 
 /* Builds the bf16 tensor-core operand of the fused layer kernels:
  *   packed[o, i, j] = sum_k coef_eff[o,i,k] fold[k,j]   (j < nt; fold = null: j = k)
- *   packed[o, i, nt] = base_eff[o, i]                   (if base_eff != null)
- *   zero up to f_pad.
+ *   packed[o, i, f_pad-1] = base_eff[o, i]              (if base_eff != null)
+ *   zero elsewhere; f_pad >= nt + 1.
  * coef_eff (O,I,K), base_eff (O,I) in `dtype`; fold (K, nt) float32 row-major.
  * packed is (O, I*f_pad) bf16, 16-byte aligned. */
 int kf_pack_coef(const void* coef_eff, const void* base_eff, const float* fold, void* packed,
@@ -110,8 +110,8 @@ int kf_knot_tables(const float* grid, float* tab, int32_t I, int32_t grid_size, 
 
 /* Fused KANLinear forward on tcgen05 (bf16 operands, f32 accumulation):
  *   y[b,o] = sum_{i,j} feat_j(x[b,i]) packed[o,i,j] + bias[o]
- * feat = basis features (B-spline values or T_j(g(x))) and, at column nt,
- * silu(x) when has_base.  x (B,I) bf16, y (B,O) bf16, bias (O) bf16 or null,
+ * feat = basis features (B-spline values or T_j(g(x))) and, in the last
+ * column f_pad-1, silu(x) when has_base.  x (B,I) bf16, y (B,O) bf16, bias (O) bf16 or null,
  * knot_tab: kf_knot_tables output for B-splines, else null.  Requires O % 8 == 0.
  * (kanforge/torch/layers.py:171-192 with kernels.py:143-150.) */
 int kf_fwd(const void* x, const void* packed, const void* bias, const float* knot_tab, void* y, int64_t B,
@@ -129,7 +129,7 @@ int kf_dgrad(const void* x, const void* dy, const void* packed, const float* kno
 /* Fused coefficient gradient on tcgen05:
  *   dpacked[o,i,j] = sum_b dy[b,o] feat_j(x[b,i])
  *   dcoef_eff[o,i,k] = sum_{j<nt} dpacked[o,i,j] fold[k,j]   (fold null: k = j)
- *   dbase[o,i] = dpacked[o,i,nt]                              (if dbase != null)
+ *   dbase[o,i] = dpacked[o,i,f_pad-1]                         (if dbase != null)
  * dcoef_eff (O,I,K) and dbase (O,I) in bf16.  (kanforge/torch/kernels.py:85, 97-98.) */
 int kf_wgrad(const void* x, const void* dy, const float* knot_tab, const float* fold, void* dcoef_eff,
              void* dbase, int64_t B, int32_t I, int32_t O, int32_t K, int32_t nt, int32_t f_pad,

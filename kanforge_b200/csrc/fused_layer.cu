@@ -54,7 +54,7 @@ struct TileMap {
 struct BasisDev {
   int map;       // KF_MAP_* (Chebyshev)
   int nt;        // basis feature columns (Chebyshev: T_0..T_{nt-1}; B-spline: size)
-  int has_base;  // SiLU column at index nt
+  int has_base;  // SiLU column at index F - 1 (the last padded column)
   int G, nk;     // B-spline grid intervals and extended knots
   const float* tab;  // B-spline knot tables (I, order + 1, 64), see kf_knot_tables
 };
@@ -111,7 +111,8 @@ __device__ __forceinline__ void drain_tma(Ctl* ctl, int issued) {
 // Cox-de Boor / derivative levels of bspline_local (basis.cuh) with the
 // reciprocal knot differences read from the table.
 template <int K>
-__device__ __forceinline__ void bspline_local_tab(float x, const float* tab, int nk, int j, int m, float (&v)[K + 1]) {
+__device__ __forceinline__ void bspline_local_tab(float x, const float* tab, int nk, int j, int m, float (&v)[K + 1],
+                                                  int ts = kTabStride) {
   const float* t = tab;
 #pragma unroll
   for (int r = 0; r <= K; ++r) v[r] = 0.0f;
@@ -120,7 +121,7 @@ __device__ __forceinline__ void bspline_local_tab(float x, const float* tab, int
   for (int q = 1; q <= K; ++q) {
     float nv[K + 1];
     const bool deriv = q > K - m;
-    const float* inv = tab + q * kTabStride;
+    const float* inv = tab + q * ts;
 #pragma unroll
     for (int rp = 0; rp <= q; ++rp) {
       const int r = j - q + rp;
@@ -138,54 +139,49 @@ __device__ __forceinline__ void bspline_local_tab(float x, const float* tab, int
   }
 }
 
-// Chebyshev feature row of one input, F values.
+// Chebyshev feature row of one input: T_0..T_{F-2}(g(x)) and silu(x) in the
+// last column.  Columns nt..F-2 meet zero coefficients (kf_pack_coef), so for
+// the tanh map (|T_j| <= 1) they need no masking; the identity map masks them
+// so that large |x| cannot produce inf * 0.
 template <int F>
 __device__ __forceinline__ void cheb_row(float x, const BasisDev& bd, float (&f)[F]) {
-  const float z = bd.map == KF_MAP_TANH ? tanh_exp(x) : x;
-  float tm2 = 1.0f, tm1 = z;
+  const bool tanh_map = bd.map == KF_MAP_TANH;
+  const float z = tanh_map ? tanh_exp(x) : x;
+  const float z2 = 2.0f * z;
   f[0] = 1.0f;
-  f[1] = bd.nt > 1 ? z : 0.0f;
+  f[1] = z;
 #pragma unroll
-  for (int j = 2; j < F; ++j) {
-    const float tj = 2.0f * z * tm1 - tm2;
-    f[j] = j < bd.nt ? tj : 0.0f;
-    tm2 = tm1;
-    tm1 = tj;
-  }
-  if (bd.has_base) {
-    const float s = silu_fast(x);
+  for (int j = 2; j < F - 1; ++j) f[j] = fmaf(z2, f[j - 1], -f[j - 2]);
+  if (!tanh_map) {
 #pragma unroll
-    for (int j = 0; j < F; ++j)
-      if (j == bd.nt) f[j] = s;
+    for (int j = 1; j < F - 1; ++j) f[j] = j < bd.nt ? f[j] : 0.0f;
   }
+  f[F - 1] = bd.has_base ? silu_fast(x) : 0.0f;
 }
 
-// d/dx of the Chebyshev feature row: j U_{j-1}(z) g'(x), and silu' at nt.
+// d/dx of the Chebyshev feature row: j U_{j-1}(z) g'(x), and silu' in the last column.
 template <int F>
 __device__ __forceinline__ void cheb_drow(float x, const BasisDev& bd, float (&f)[F]) {
+  const bool tanh_map = bd.map == KF_MAP_TANH;
   float z, gp;
-  if (bd.map == KF_MAP_TANH) {
+  if (tanh_map) {
     z = tanhf(x);
     gp = 1.0f - z * z;
   } else {
     z = x;
     gp = 1.0f;
   }
+  const float z2 = 2.0f * z;
   float um2 = 0.0f, um1 = 1.0f;  // U_{-1} = 0, U_0 = 1
   f[0] = 0.0f;
 #pragma unroll
-  for (int j = 1; j < F; ++j) {
-    f[j] = j < bd.nt ? (float)j * um1 * gp : 0.0f;
-    const float u = 2.0f * z * um1 - um2;
+  for (int j = 1; j < F - 1; ++j) {
+    f[j] = (tanh_map || j < bd.nt) ? (float)j * um1 * gp : 0.0f;
+    const float u = fmaf(z2, um1, -um2);
     um2 = um1;
     um1 = u;
   }
-  if (bd.has_base) {
-    const float ds = dsilu_acc(x);
-#pragma unroll
-    for (int j = 0; j < F; ++j)
-      if (j == bd.nt) f[j] = ds;
-  }
+  f[F - 1] = bd.has_base ? dsilu_acc(x) : 0.0f;
 }
 
 // ===========================================================================
@@ -389,7 +385,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fused_fwd_kernel(const __grid_
           for (int u = 0; u < IPK; ++u) {
             float f[F];
             cheb_row<F>(xv[u], p.bd, f);
-            if (i0 + u >= p.I) {
+            if (i0 + IPK > p.I && i0 + u >= p.I) {  // tail step only
 #pragma unroll
               for (int j = 0; j < F; ++j) f[j] = 0.0f;
             }
@@ -426,7 +422,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fused_fwd_kernel(const __grid_
               }
             }
             if (p.bd.has_base) {
-              const int col = u * F + p.bd.nt;
+              const int col = u * F + F - 1;
               *reinterpret_cast<__nv_bfloat16*>(arow + sw128_offset(row, col >> 3) + (col & 7) * 2) = __float2bfloat16_rn(silu_fast(xv[u]));
             }
           }
@@ -639,7 +635,7 @@ __global__ void __launch_bounds__(kDgradThreads, 1) fused_dgrad_kernel(const __g
                   if (r >= 0 && r < p.bd.nt) s = fmaf(wst[lane * 33 + h * F + r], dv[rp], s);
                 }
               }
-              if (p.bd.has_base) s = fmaf(wst[lane * 33 + h * F + p.bd.nt], dsilu_acc(xval), s);
+              if (p.bd.has_base) s = fmaf(wst[lane * 33 + h * F + F - 1], dsilu_acc(xval), s);
             }
 #pragma unroll
             for (int uu = 0; uu < IPT; ++uu)
@@ -690,11 +686,12 @@ struct WgradParams {
   int I, O, K;
   int k_steps;
   int x_tma;  // x tiles arrive by TMA with the dy tile (row pitch 16-byte aligned)
+  int tab_stride;  // B-spline: row stride of the producers' private knot tables (>= nk)
   TileMap tiles;
   BasisDev bd;
 };
 
-constexpr int kWgradThreads = 512;  // w0 TMA, w1 MMA, w4-7 epilogue, w8-15 producers
+constexpr int kWgradThreads = 768;  // w0 TMA, w1 MMA, w4-7 epilogue, w8-23 producers (2 groups)
 constexpr int kXTile = kBK * 8 * 2;  // x tile per stage: 64 rows x 8 inputs bf16 = 1 KB
 
 template <int BK, int F>
@@ -708,13 +705,13 @@ __global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __g
   Ctl* ctl = reinterpret_cast<Ctl*>(sb + kStages * kBTile);
   uint8_t* sx = align1024(reinterpret_cast<uint8_t*>(ctl + 1));  // x tiles [stage][64 rows][8 inputs]
   float* stg = reinterpret_cast<float*>(sx + kStages * kXTile);  // epilogue staging [128][33]
-  float* tabs = stg + 128 * 33;                                   // B-spline: per producer warp [(BK+1) * 64]
+  float* tabs = stg + 128 * 33;                                   // B-spline: per producer warp [(BK+1) * ts]
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   volatile int* abort = &ctl->abort;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&ctl->full_a[s], 8);
+      mbar_init(&ctl->full_a[s], 8);  // the 8 warps of the producer group that owns the step
       mbar_init(&ctl->full_b[s], 1);
       mbar_init(&ctl->empty[s], 1);
     }
@@ -837,18 +834,21 @@ __global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __g
           } else {
             for (int kk = 0; kk < p.K; ++kk) dst[kk] = __float2bfloat16_rn(dcol[kk * 33]);
           }
-          if (p.dbase) p.dbase[(int64_t)o * p.I + i] = __float2bfloat16_rn(dcol[p.bd.nt * 33]);
+          if (p.dbase) p.dbase[(int64_t)o * p.I + i] = __float2bfloat16_rn(dcol[(F - 1) * 33]);
         }
       }
     }
   } else if (warp >= 8) {
-    // producers: F == 16 -> warp w owns input u = w - 8 of the tile's 8 inputs, each
-    // lane two batch columns; F == 32 -> 4 inputs, warps 2u and 2u+1 split the 64 columns.
-    const int pw = warp - 8;
+    // producers: two groups of 8 warps own the K-steps of global parity 0 / 1.
+    // F == 16 -> warp pw owns input u = pw of the tile's 8 inputs, each lane two
+    // batch columns; F == 32 -> 4 inputs, warps 2u and 2u+1 split the 64 columns.
+    const int grp = (warp - 8) / 8;
+    const int pw = (warp - 8) % 8;
     const int u = (F == 16) ? pw : pw / 2;
     const int bsub = (F == 16) ? lane * 2 : (pw % 2) * 32 + lane;  // first batch column of this lane
     constexpr int NB = (F == 16) ? 2 : 1;
-    float* tab = tabs + pw * ((BK + 1) * kTabStride);
+    const int ts = p.tab_stride;
+    float* tab = tabs + (warp - 8) * ((BK + 1) * ts);
     int it = 0;
     bool alive = true;
     for (int t = blockIdx.x; t < n_tiles && alive; t += gridDim.x) {  // abort is seen (warp-uniformly) by the waits
@@ -859,13 +859,17 @@ __global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __g
       const int xoff = i_base - (i_base & ~7) + u;  // column of input i inside the TMA x tile
       if constexpr (BK > 0) {
         __syncwarp();
-        for (int e = lane; e < (BK + 1) * kTabStride; e += 32)
-          tab[e] = i < p.I ? __ldg(p.bd.tab + (size_t)i * ((BK + 1) * kTabStride) + e) : 0.0f;
+        for (int e = lane; e < (BK + 1) * ts; e += 32) {
+          const int q = e / ts, r = e % ts;
+          tab[e] = (i < p.I && r < kTabStride) ? __ldg(p.bd.tab + (size_t)i * ((BK + 1) * kTabStride) + q * kTabStride + r) : 0.0f;
+        }
         __syncwarp();
       }
-      for (int k = 0; k < p.k_steps; ++k, ++it) {
-        const int s = it % kStages;
-        const uint32_t ph = (it / kStages) & 1;
+      int k = ((it & 1) == grp) ? 0 : 1;
+      for (; k < p.k_steps; k += 2) {
+        const int git = it + k;
+        const int s = git % kStages;
+        const uint32_t ph = (git / kStages) & 1;
         float xv[2] = {0.0f, 0.0f};
         if (!p.x_tma) {
 #pragma unroll
@@ -901,7 +905,7 @@ __global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __g
             float vv[BK + 1];
 #pragma unroll
             for (int rp = 0; rp <= BK; ++rp) vv[rp] = 0.0f;
-            if (j0 >= 0) bspline_local_tab<BK>(xv[r], tab, p.bd.nk, j0, 0, vv);
+            if (j0 >= 0) bspline_local_tab<BK>(xv[r], tab, p.bd.nk, j0, 0, vv, ts);
 #pragma unroll
             for (int j = 0; j < F; ++j) {
               float val = 0.0f;
@@ -910,12 +914,7 @@ __global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __g
                 if (j == j0 - BK + rp) val = vv[rp];
               f[r][j] = j < p.bd.nt ? val : 0.0f;
             }
-            if (p.bd.has_base) {
-              const float sv = silu_fast(xv[r]);
-#pragma unroll
-              for (int j = 0; j < F; ++j)
-                if (j == p.bd.nt) f[r][j] = sv;
-            }
+            if (p.bd.has_base) f[r][F - 1] = silu_fast(xv[r]);
           }
         }
         // A[m = u*F + j][k = bsub (+1)]: K-major swizzled rows
@@ -933,6 +932,7 @@ __global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __g
         __syncwarp();
         if (lane == 0) mbar_arrive(&ctl->full_a[s]);
       }
+      it += p.k_steps;
     }
   }
 
@@ -997,7 +997,7 @@ int sm_count() {
 int fill_basis(const kf_basis_desc* d, const float* knot_tab, int nt, int has_base, int f_pad, BasisDev& bd) {
   KF_CHECK_ARG(d != nullptr, "basis is null");
   KF_CHECK_ARG(f_pad == 16 || f_pad == 32, "f_pad must be 16 or 32 (got %d)", f_pad);
-  KF_CHECK_ARG(nt >= 1 && nt + (has_base ? 1 : 0) <= f_pad, "nt %d (+ base) exceeds f_pad %d", nt, f_pad);
+  KF_CHECK_ARG(nt >= 1 && nt + 1 <= f_pad, "nt %d (+ the SiLU column) exceeds f_pad %d", nt, f_pad);
   bd.map = d->input_map;
   bd.nt = nt;
   bd.has_base = has_base;
@@ -1072,7 +1072,11 @@ struct WgradLaunch {
   cudaStream_t stream;
   template <int BK, int F>
   int go() const {
-    const size_t smem = kMainSmem + 1024 + kStages * kXTile + sizeof(float) * (128 * 33 + (BK > 0 ? 8 * (BK + 1) * kTabStride : 0));
+    const size_t smem = kMainSmem + 1024 + kStages * kXTile + sizeof(float) * (128 * 33 + (BK > 0 ? 16 * (BK + 1) * p.tab_stride : 0));
+    if (smem > 232448) {
+      set_error("kf_wgrad: B-spline order %d with %d knots needs %zu bytes of shared memory", BK, p.bd.nk, smem);
+      return KF_ERR_UNSUPPORTED;
+    }
     auto kern = fused_wgrad_kernel<BK, F>;
     KF_CUDA_RET(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     const int grid = (int)std::min<int64_t>(p.tiles.m_tiles * (int64_t)p.tiles.n_tiles, sm_count());
@@ -1176,6 +1180,7 @@ extern "C" int kf_wgrad(const void* x, const void* dy, const float* knot_tab, co
   CUtensorMap tdy, tx;
   if (int rc = make_tmap_bf16(&tdy, dy, B, O, 64, kBK)) return rc;
   p.x_tma = (I % 8 == 0) && ((uintptr_t)x % 16 == 0);
+  p.tab_stride = basis->kind == KF_BASIS_BSPLINE ? ((p.bd.nk + 15) & ~15) : 16;
   if (p.x_tma) {
     if (int rc = make_tmap_bf16(&tx, x, B, I, 8, kBK, false)) return rc;
   } else {

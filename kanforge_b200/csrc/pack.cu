@@ -1,8 +1,8 @@
 // Builds the bf16 coefficient operand of the fused tensor-core kernels.
 //
 //   packed[o, i, j]  = sum_k coef_eff[o,i,k] fold[k,j]   j < nt   (fold null: j = k)
-//   packed[o, i, nt] = base_eff[o,i]                     (SiLU column)
-//   packed[o, i, j]  = 0                                 up to f_pad
+//   packed[o, i, f_pad-1] = base_eff[o,i]                (SiLU column, the last one)
+//   packed[o, i, j]  = 0                                 elsewhere
 //
 // For folded plans this is the reference's `ct = c @ R` (kanforge/torch/kernels.py:75-77,
 // kanforge/kernels/plan.py:75-101) with the base branch of
@@ -42,7 +42,7 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(const T* __restrict_
           } else {
             v = j < K ? cv[j] : 0.0f;
           }
-        } else if (j == nt && base != nullptr) {
+        } else if (j == f_pad - 1 && base != nullptr) {
           v = to_f32(base[e]);
         }
         tmp[u] = __float2bfloat16_rn(v);
@@ -63,7 +63,7 @@ extern "C" int kf_pack_coef(const void* coef_eff, const void* base_eff, const fl
   KF_CHECK_ARG(coef_eff && packed, "kf_pack_coef: null pointer");
   if (int rc = bind_device(packed)) return rc;
   KF_CHECK_ARG(O >= 1 && I >= 1 && K >= 1 && nt >= 1 && K <= kMaxFold && nt <= kMaxFold, "kf_pack_coef: bad sizes");
-  KF_CHECK_ARG(f_pad % 8 == 0 && f_pad >= nt + (base_eff ? 1 : 0), "kf_pack_coef: f_pad %d too small", f_pad);
+  KF_CHECK_ARG(f_pad % 8 == 0 && f_pad >= nt + 1, "kf_pack_coef: f_pad %d too small", f_pad);
   KF_CHECK_ARG(fold != nullptr || nt <= K, "kf_pack_coef: without a fold nt must be <= K");
   KF_CHECK_ARG(((uintptr_t)packed % 16) == 0, "kf_pack_coef: packed must be 16-byte aligned");
   const int64_t n = (int64_t)O * I;

@@ -198,10 +198,10 @@ def knot_tables(grid: torch.Tensor, plan: KernelPlan) -> torch.Tensor:
 
 
 def fused_layout(plan: KernelPlan, has_base: bool) -> tuple[int, int]:
-    """(nt, f_pad): basis feature columns per input and the padded width (16 or 32)."""
+    """(nt, f_pad): basis feature columns per input and the padded width (16 or
+    32); the last padded column carries the SiLU base branch."""
     nt = plan.n_features(0)
-    width = nt + (1 if has_base else 0)
-    return nt, (16 if width <= 16 else 32)
+    return nt, (16 if nt + 1 <= 16 else 32)
 
 
 def fused_ok(plan: KernelPlan | None, x: torch.Tensor, n_out: int, has_base: bool) -> bool:
@@ -210,7 +210,7 @@ def fused_ok(plan: KernelPlan | None, x: torch.Tensor, n_out: int, has_base: boo
     if plan is None or plan.kind not in ("cheb", "bspline") or x.dtype != _BF16 or x.device.type != "cuda":
         return False
     nt, _ = fused_layout(plan, has_base)
-    if nt + (1 if has_base else 0) > 32 or n_out % 8:
+    if nt + 1 > 32 or n_out % 8:
         return False
     return plan.supported(_lib.KF_QUERY_FUSED, _lib.KF_DTYPE_BF16)
 
