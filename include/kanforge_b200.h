@@ -93,13 +93,16 @@ int kf_prim(int op, int m, const float* x, const float* a, const float* b, const
             int64_t B, int32_t I, int32_t O, int32_t nf, const kf_basis_desc* basis, void* stream);
 
 /* Builds the bf16 tensor-core operand of the fused layer kernels:
+ *   coef_eff = coef * edge_scale * edge_mask, base_eff = base * edge_mask
+ *   (kanforge/torch/layers.py:162-167; a null scale / mask is 1)
  *   packed[o, i, j] = sum_k coef_eff[o,i,k] fold[k,j]   (j < nt; fold = null: j = k)
- *   packed[o, i, f_pad-1] = base_eff[o, i]              (if base_eff != null)
+ *   packed[o, i, f_pad-1] = base_eff[o, i]              (if base != null)
  *   zero elsewhere; f_pad >= nt + 1.
- * coef_eff (O,I,K), base_eff (O,I) in `dtype`; fold (K, nt) float32 row-major.
- * packed is (O, I*f_pad) bf16, 16-byte aligned. */
-int kf_pack_coef(const void* coef_eff, const void* base_eff, const float* fold, void* packed,
-                 int32_t O, int32_t I, int32_t K, int32_t nt, int32_t f_pad, int dtype, void* stream);
+ * coef (O,I,K), base, edge_scale, edge_mask (O,I) in `dtype`; fold (K, nt)
+ * float32 row-major.  packed is (O, I*f_pad) bf16, 16-byte aligned. */
+int kf_pack_coef(const void* coef, const void* base, const void* edge_scale, const void* edge_mask,
+                 const float* fold, void* packed, int32_t O, int32_t I, int32_t K, int32_t nt, int32_t f_pad,
+                 int dtype, void* stream);
 
 /* Knot tables of per-input B-spline grids, read by the fused kernels: for each
  * input i, tab[i, 0, r] = extended knot t_r (r < G + 2 order + 1, order mean
@@ -126,14 +129,17 @@ int kf_dgrad(const void* x, const void* dy, const void* packed, const float* kno
              int32_t I, int32_t O, int32_t nt, int32_t f_pad, int32_t has_base, const kf_basis_desc* basis,
              void* stream);
 
-/* Fused coefficient gradient on tcgen05:
+/* Fused coefficient gradient on tcgen05, with the effective-coefficient chain rule:
  *   dpacked[o,i,j] = sum_b dy[b,o] feat_j(x[b,i])
- *   dcoef_eff[o,i,k] = sum_{j<nt} dpacked[o,i,j] fold[k,j]   (fold null: k = j)
- *   dbase[o,i] = dpacked[o,i,f_pad-1]                         (if dbase != null)
- * dcoef_eff (O,I,K) and dbase (O,I) in bf16.  (kanforge/torch/kernels.py:85, 97-98.) */
-int kf_wgrad(const void* x, const void* dy, const float* knot_tab, const float* fold, void* dcoef_eff,
-             void* dbase, int64_t B, int32_t I, int32_t O, int32_t K, int32_t nt, int32_t f_pad,
-             const kf_basis_desc* basis, void* stream);
+ *   dC[o,i,k]      = sum_{j<nt} dpacked[o,i,j] fold[k,j]      (fold null: k = j)
+ *   dcoef[o,i,k]   = dC[o,i,k] * edge_scale[o,i] * edge_mask[o,i]
+ *   dscale[o,i]    = sum_k dC[o,i,k] coef[o,i,k] edge_mask[o,i] (if dscale != null)
+ *   dbase[o,i]     = dpacked[o,i,f_pad-1] * edge_mask[o,i]       (if dbase != null)
+ * coef, edge_scale, edge_mask (null = 1) and the outputs are bf16.
+ * (kanforge/torch/kernels.py:85, 97-98; layers.py:162-167.) */
+int kf_wgrad(const void* x, const void* dy, const float* knot_tab, const float* fold, const void* coef,
+             const void* edge_scale, const void* edge_mask, void* dcoef, void* dbase, void* dscale, int64_t B,
+             int32_t I, int32_t O, int32_t K, int32_t nt, int32_t f_pad, const kf_basis_desc* basis, void* stream);
 
 /* edge_derivative (kanforge/torch/layers.py:206-226), float32:
  *   out[b,o,i] = sum_j phi_j^(order)(x[b,i]) coef[o,i,j] + s(x[b,i]) base_eff[o,i]

@@ -48,7 +48,7 @@ PROTOTYPES = {
         [ctypes.c_int, ctypes.c_int, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i32, _c_i32, _c_i32, ctypes.POINTER(BasisDesc), _vp],
     ),
     "kf_knot_tables": (ctypes.c_int, [_vp, _vp, _c_i32, _c_i32, _c_i32, _vp]),
-    "kf_pack_coef": (ctypes.c_int, [_vp, _vp, _vp, _vp, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, ctypes.c_int, _vp]),
+    "kf_pack_coef": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, ctypes.c_int, _vp]),
     "kf_fwd": (
         ctypes.c_int,
         [_vp, _vp, _vp, _vp, _vp, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, ctypes.POINTER(BasisDesc), _vp],
@@ -59,7 +59,8 @@ PROTOTYPES = {
     ),
     "kf_wgrad": (
         ctypes.c_int,
-        [_vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, ctypes.POINTER(BasisDesc), _vp],
+        [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
+         ctypes.POINTER(BasisDesc), _vp],
     ),
     "kf_edge_derivative": (
         ctypes.c_int,

@@ -199,7 +199,8 @@ struct FwdParams {
   BasisDev bd;
 };
 
-constexpr int kFwdThreads = 512;  // w0 TMA, w1 MMA, w4-7 epilogue, w8-15 producers (2 groups)
+constexpr int kFwdThreads = 768;  // w0 TMA, w1 MMA, w4-7 epilogue, w8-23 producers (4 groups)
+constexpr int kFwdGroups = 4;     // producer group g owns the K-steps it with it % 4 == g (stage g)
 
 template <int BK, int F>
 __global__ void __launch_bounds__(kFwdThreads, 1) fused_fwd_kernel(const __grid_constant__ CUtensorMap tmap_c, FwdParams p) {
@@ -346,9 +347,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fused_fwd_kernel(const __grid_
     }
   } else if (warp >= 8) {
     // ---------------- feature producers: x -> basis rows in smem ----------------
-    // Group grp owns the K-steps of global parity grp; each thread owns one row.
-    // The x values of a thread's next step are loaded one step ahead so global
-    // latency overlaps the current step.
+    // Group grp owns the K-steps it with it % 4 == grp, i.e. always stage grp;
+    // each thread owns one row.  The x values of a thread's next step are
+    // loaded one step ahead so global latency overlaps the current step.
+    static_assert(kStages % kFwdGroups == 0, "each producer group owns whole stages");
     const int grp = (warp - 8) / 4;
     const int row = ((warp - 8) % 4) * 32 + lane;
     int it = 0;
@@ -359,17 +361,18 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fused_fwd_kernel(const __grid_
       const int64_t b = (int64_t)m * kBM + row;
       const bool row_ok = b < p.B;
       const unsigned short* xrow = reinterpret_cast<const unsigned short*>(p.x) + (row_ok ? b : 0) * p.I;
-      int k = ((it & 1) == grp) ? 0 : 1;
+      int k = ((grp - it) % kFwdGroups + kFwdGroups) % kFwdGroups;
       unsigned short xa[IPK], xb[IPK];
 #pragma unroll
       for (int u = 0; u < IPK; ++u) xa[u] = (row_ok && k < p.k_steps && k * IPK + u < p.I) ? __ldg(xrow + k * IPK + u) : 0;
-      for (; k < p.k_steps; k += 2) {
+      for (; k < p.k_steps; k += kFwdGroups) {
         const int git = it + k;
         const int s = git % kStages;
         const uint32_t ph = (git / kStages) & 1;
         const int i0 = k * IPK;
+        const int inext = i0 + kFwdGroups * IPK;
 #pragma unroll
-        for (int u = 0; u < IPK; ++u) xb[u] = (row_ok && k + 2 < p.k_steps && i0 + 2 * IPK + u < p.I) ? __ldg(xrow + i0 + 2 * IPK + u) : 0;
+        for (int u = 0; u < IPK; ++u) xb[u] = (row_ok && k + kFwdGroups < p.k_steps && inext + u < p.I) ? __ldg(xrow + inext + u) : 0;
         bool ok = mbar_wait_warp(&ctl->empty[s], ph ^ 1, abort);
         if constexpr (BK > 0) ok = ok && mbar_wait_warp(&ctl->full_b[s], ph, abort);  // tables landed
         if (!ok) {
@@ -680,8 +683,12 @@ __global__ void __launch_bounds__(kDgradThreads, 1) fused_dgrad_kernel(const __g
 struct WgradParams {
   const __nv_bfloat16* x;
   const float* fold;     // (K, nt) or null
+  const __nv_bfloat16* coef;   // (O, I, K): needed for the edge_scale gradient
+  const __nv_bfloat16* scale;  // (O, I) edge_scale or null
+  const __nv_bfloat16* mask;   // (O, I) edge_mask or null
   __nv_bfloat16* dcoef;  // (O, I, K)
   __nv_bfloat16* dbase;  // (O, I) or null
+  __nv_bfloat16* dscale; // (O, I) or null
   int64_t B;
   int I, O, K;
   int k_steps;
@@ -824,17 +831,26 @@ __global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __g
           const int i = i_base + u;
           if (o >= p.O || i >= p.I) continue;
           const float* dcol = stg + (u * F) * 33 + ol;  // dpacked[o, i, j] = dcol[j * 33]
-          __nv_bfloat16* dst = p.dcoef + ((int64_t)o * p.I + i) * p.K;
-          if (p.fold) {
-            for (int kk = 0; kk < p.K; ++kk) {
-              float s = 0.0f;
-              for (int j = 0; j < p.bd.nt; ++j) s = fmaf(dcol[j * 33], __ldg(p.fold + kk * p.bd.nt + j), s);
-              dst[kk] = __float2bfloat16_rn(s);
+          const int64_t e = (int64_t)o * p.I + i;
+          __nv_bfloat16* dst = p.dcoef + e * p.K;
+          // C_eff = coef * scale * mask  =>  dcoef = dC_eff * scale * mask,
+          // dscale = sum_k dC_eff * coef * mask; base_eff = base * mask (kanforge/torch/layers.py:162-167)
+          const float mk = p.mask ? __bfloat162float(p.mask[e]) : 1.0f;
+          const float sm = mk * (p.scale ? __bfloat162float(p.scale[e]) : 1.0f);
+          float dsc = 0.0f;
+          for (int kk = 0; kk < p.K; ++kk) {
+            float dce;
+            if (p.fold) {
+              dce = 0.0f;
+              for (int j = 0; j < p.bd.nt; ++j) dce = fmaf(dcol[j * 33], __ldg(p.fold + kk * p.bd.nt + j), dce);
+            } else {
+              dce = dcol[kk * 33];
             }
-          } else {
-            for (int kk = 0; kk < p.K; ++kk) dst[kk] = __float2bfloat16_rn(dcol[kk * 33]);
+            dst[kk] = __float2bfloat16_rn(dce * sm);
+            if (p.dscale) dsc = fmaf(dce, __bfloat162float(p.coef[e * p.K + kk]), dsc);
           }
-          if (p.dbase) p.dbase[(int64_t)o * p.I + i] = __float2bfloat16_rn(dcol[(F - 1) * 33]);
+          if (p.dscale) p.dscale[e] = __float2bfloat16_rn(dsc * mk);
+          if (p.dbase) p.dbase[e] = __float2bfloat16_rn(dcol[(F - 1) * 33] * mk);
         }
       }
     }
@@ -1146,12 +1162,15 @@ extern "C" int kf_dgrad(const void* x, const void* dy, const void* packed, const
   return dispatch_fused(basis, f_pad, L);
 }
 
-extern "C" int kf_wgrad(const void* x, const void* dy, const float* knot_tab, const float* fold, void* dcoef_eff,
-                        void* dbase, int64_t B, int32_t I, int32_t O, int32_t K, int32_t nt, int32_t f_pad,
-                        const kf_basis_desc* basis, void* stream) {
+extern "C" int kf_wgrad(const void* x, const void* dy, const float* knot_tab, const float* fold, const void* coef,
+                        const void* edge_scale, const void* edge_mask, void* dcoef, void* dbase, void* dscale, int64_t B,
+                        int32_t I, int32_t O, int32_t K, int32_t nt, int32_t f_pad, const kf_basis_desc* basis,
+                        void* stream) {
   using namespace kf;
   clear_error();
-  KF_CHECK_ARG(x && dy && dcoef_eff, "kf_wgrad: null tensor pointer");
+  void* dcoef_eff = dcoef;
+  KF_CHECK_ARG(x && dy && dcoef, "kf_wgrad: null tensor pointer");
+  KF_CHECK_ARG(dscale == nullptr || (coef != nullptr && edge_scale != nullptr), "kf_wgrad: dscale needs coef and edge_scale");
   if (int rc = bind_device(x)) return rc;
   KF_CHECK_ARG(B >= 0 && I >= 1 && O >= 1 && K >= 1, "kf_wgrad: bad sizes");
   KF_CHECK_ARG(O % 8 == 0, "kf_wgrad: O (%d) must be a multiple of 8", O);
@@ -1162,12 +1181,17 @@ extern "C" int kf_wgrad(const void* x, const void* dy, const float* knot_tab, co
   if (B == 0) {
     KF_CUDA_RET(cudaMemsetAsync(dcoef_eff, 0, sizeof(__nv_bfloat16) * (size_t)O * I * K, s));
     if (dbase) KF_CUDA_RET(cudaMemsetAsync(dbase, 0, sizeof(__nv_bfloat16) * (size_t)O * I, s));
+    if (dscale) KF_CUDA_RET(cudaMemsetAsync(dscale, 0, sizeof(__nv_bfloat16) * (size_t)O * I, s));
     return KF_OK;
   }
   p.x = (const __nv_bfloat16*)x;
   p.fold = fold;
+  p.coef = (const __nv_bfloat16*)coef;
+  p.scale = (const __nv_bfloat16*)edge_scale;
+  p.mask = (const __nv_bfloat16*)edge_mask;
   p.dcoef = (__nv_bfloat16*)dcoef_eff;
   p.dbase = (__nv_bfloat16*)dbase;
+  p.dscale = (__nv_bfloat16*)dscale;
   p.B = B;
   p.I = I;
   p.O = O;

@@ -1,5 +1,6 @@
 // Builds the bf16 coefficient operand of the fused tensor-core kernels.
 //
+//   coef_eff = coef * edge_scale * edge_mask, base_eff = base * edge_mask
 //   packed[o, i, j]  = sum_k coef_eff[o,i,k] fold[k,j]   j < nt   (fold null: j = k)
 //   packed[o, i, f_pad-1] = base_eff[o,i]                (SiLU column, the last one)
 //   packed[o, i, j]  = 0                                 elsewhere
@@ -19,6 +20,7 @@ constexpr int kMaxFold = 64;
 
 template <typename T>
 __global__ void __launch_bounds__(kPackThreads) pack_kernel(const T* __restrict__ coef, const T* __restrict__ base,
+                                                            const T* __restrict__ scale, const T* __restrict__ mask,
                                                             const float* __restrict__ fold, __nv_bfloat16* __restrict__ packed,
                                                             int64_t n_edges, int K, int nt, int f_pad, int has_fold) {
   __shared__ float R[kMaxFold * kMaxFold];
@@ -27,8 +29,11 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(const T* __restrict_
   __syncthreads();
   for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n_edges; e += (int64_t)gridDim.x * blockDim.x) {
     const T* c = coef + e * K;
+    // effective coefficients coef * edge_scale * edge_mask (kanforge/torch/layers.py:162-167)
+    const float mk = mask ? to_f32(mask[e]) : 1.0f;
+    const float sm = mk * (scale ? to_f32(scale[e]) : 1.0f);
     float cv[kMaxFold];
-    for (int k = 0; k < K; ++k) cv[k] = to_f32(c[k]);
+    for (int k = 0; k < K; ++k) cv[k] = to_f32(c[k]) * sm;
     __nv_bfloat16* dst = packed + e * f_pad;
     for (int j0 = 0; j0 < f_pad; j0 += 8) {
       __align__(16) __nv_bfloat16 tmp[8];
@@ -43,7 +48,7 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(const T* __restrict_
             v = j < K ? cv[j] : 0.0f;
           }
         } else if (j == f_pad - 1 && base != nullptr) {
-          v = to_f32(base[e]);
+          v = to_f32(base[e]) * mk;
         }
         tmp[u] = __float2bfloat16_rn(v);
       }
@@ -56,8 +61,9 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(const T* __restrict_
 
 }  // namespace kf
 
-extern "C" int kf_pack_coef(const void* coef_eff, const void* base_eff, const float* fold, void* packed, int32_t O,
-                            int32_t I, int32_t K, int32_t nt, int32_t f_pad, int dtype, void* stream) {
+extern "C" int kf_pack_coef(const void* coef_eff, const void* base_eff, const void* edge_scale, const void* edge_mask,
+                            const float* fold, void* packed, int32_t O, int32_t I, int32_t K, int32_t nt, int32_t f_pad,
+                            int dtype, void* stream) {
   using namespace kf;
   clear_error();
   KF_CHECK_ARG(coef_eff && packed, "kf_pack_coef: null pointer");
@@ -70,11 +76,13 @@ extern "C" int kf_pack_coef(const void* coef_eff, const void* base_eff, const fl
   const unsigned grid = (unsigned)std::min<int64_t>(cdiv(n, kPackThreads), 148 * 16);
   cudaStream_t s = (cudaStream_t)stream;
   if (dtype == KF_DTYPE_F32) {
-    pack_kernel<float><<<grid, kPackThreads, 0, s>>>((const float*)coef_eff, (const float*)base_eff, fold,
+    pack_kernel<float><<<grid, kPackThreads, 0, s>>>((const float*)coef_eff, (const float*)base_eff,
+                                                     (const float*)edge_scale, (const float*)edge_mask, fold,
                                                      (__nv_bfloat16*)packed, n, K, nt, f_pad, fold != nullptr);
   } else if (dtype == KF_DTYPE_BF16) {
-    pack_kernel<__nv_bfloat16><<<grid, kPackThreads, 0, s>>>((const __nv_bfloat16*)coef_eff, (const __nv_bfloat16*)base_eff,
-                                                             fold, (__nv_bfloat16*)packed, n, K, nt, f_pad, fold != nullptr);
+    pack_kernel<__nv_bfloat16><<<grid, kPackThreads, 0, s>>>(
+        (const __nv_bfloat16*)coef_eff, (const __nv_bfloat16*)base_eff, (const __nv_bfloat16*)edge_scale,
+        (const __nv_bfloat16*)edge_mask, fold, (__nv_bfloat16*)packed, n, K, nt, f_pad, fold != nullptr);
   } else {
     set_error("kf_pack_coef: dtype %d unsupported", dtype);
     return KF_ERR_UNSUPPORTED;

@@ -204,10 +204,13 @@ def fused_layout(plan: KernelPlan, has_base: bool) -> tuple[int, int]:
     return nt, (16 if nt + 1 <= 16 else 32)
 
 
-def fused_ok(plan: KernelPlan | None, x: torch.Tensor, n_out: int, has_base: bool) -> bool:
-    """Whether the tensor-core path serves this call: bf16, CUDA, a B-spline or
-    Chebyshev-feature plan with <= 31 feature columns, outputs a multiple of 8."""
+def fused_ok(plan: KernelPlan | None, x: torch.Tensor, n_out: int, has_base: bool, coef_dtype=None) -> bool:
+    """Whether the tensor-core path serves this call: bf16 inputs and parameters,
+    CUDA, a B-spline or Chebyshev-feature plan with <= 31 feature columns,
+    outputs a multiple of 8."""
     if plan is None or plan.kind not in ("cheb", "bspline") or x.dtype != _BF16 or x.device.type != "cuda":
+        return False
+    if coef_dtype is not None and coef_dtype != _BF16:
         return False
     nt, _ = fused_layout(plan, has_base)
     if nt + 1 > 32 or n_out % 8:
@@ -215,112 +218,132 @@ def fused_ok(plan: KernelPlan | None, x: torch.Tensor, n_out: int, has_base: boo
     return plan.supported(_lib.KF_QUERY_FUSED, _lib.KF_DTYPE_BF16)
 
 
-def pack_coef(coef_eff: torch.Tensor, base_eff: torch.Tensor | None, plan: KernelPlan, f_pad: int) -> torch.Tensor:
-    """The bf16 tensor-core operand (O, I * f_pad): folded coefficients and the SiLU column."""
-    n_out, n_in, k = coef_eff.shape
+def _bf16_or_none(t):
+    return None if t is None else t.detach().to(_BF16).contiguous()
+
+
+def pack_coef(coef, base, edge_scale, edge_mask, plan: KernelPlan, f_pad: int) -> torch.Tensor:
+    """The bf16 tensor-core operand (O, I * f_pad): coef * edge_scale * edge_mask
+    folded into Chebyshev features, and the masked base weight in the last column."""
+    n_out, n_in, k = coef.shape
     nt = plan.n_features(0)
-    coef_eff = coef_eff.detach().contiguous()
-    dt = _lib.KF_DTYPE_BF16 if coef_eff.dtype == _BF16 else _lib.KF_DTYPE_F32
+    coef = coef.detach().contiguous()
+    dt = _lib.KF_DTYPE_BF16 if coef.dtype == _BF16 else _lib.KF_DTYPE_F32
     if dt == _lib.KF_DTYPE_F32:
-        coef_eff = coef_eff.float()
-    base = None if base_eff is None else base_eff.detach().to(coef_eff.dtype).contiguous()
+        coef = coef.float()
+    like = coef.dtype
+    conv = lambda t: None if t is None else t.detach().to(like).contiguous()  # noqa: E731
+    base, scale, mask = conv(base), conv(edge_scale), conv(edge_mask)
     fold = None
     if plan.folded and not plan.is_identity_fold():
-        fold = torch.tensor(plan.fold(0), dtype=torch.float32, device=coef_eff.device)
-    packed = torch.empty(n_out, n_in * f_pad, device=coef_eff.device, dtype=_BF16)
-    _launch("kf_pack_coef", _ptr(coef_eff), _ptr(base), _ptr(fold), _ptr(packed), n_out, n_in, k, nt, f_pad, dt,
-              _stream(coef_eff))
+        fold = torch.tensor(plan.fold(0), dtype=torch.float32, device=coef.device)
+    packed = torch.empty(n_out, n_in * f_pad, device=coef.device, dtype=_BF16)
+    _launch("kf_pack_coef", _ptr(coef), _ptr(base), _ptr(scale), _ptr(mask), _ptr(fold), _ptr(packed), n_out, n_in, k,
+            nt, f_pad, dt, _stream(coef))
     return packed
 
 
 class _FusedKANLinear(torch.autograd.Function):
     """y = sum_{i,j} feat_j(x_i) C_eff[o,i,j] + silu(x_i) W_eff[o,i] + b_o in one
-    tcgen05 contraction per pass (forward, input gradient, coefficient gradient).
+    tcgen05 contraction per pass (forward, input gradient, coefficient gradient),
+    with C_eff = coef * edge_scale * edge_mask and W_eff = base_weight * edge_mask
+    (kanforge/torch/layers.py:162-191) formed inside the kernels.
 
     When the backward itself is differentiated (create_graph), the gradients are
     built from the closed float32 primitives instead, so every order works as in
     the reference (kanforge/torch/kernels.py:79-87)."""
 
     @staticmethod
-    def forward(ctx, x, coef_eff, base_eff, bias, grid, plan):
-        n_out, n_in, _ = coef_eff.shape
-        has_base = base_eff is not None
+    def forward(ctx, x, coef, base_weight, bias, edge_scale, edge_mask, grid, plan):
+        n_out, n_in, _ = coef.shape
+        has_base = base_weight is not None
         nt, f_pad = fused_layout(plan, has_base)
         x = x.contiguous()
-        packed = pack_coef(coef_eff, base_eff, plan, f_pad)
+        packed = pack_coef(coef, base_weight, edge_scale, edge_mask, plan, f_pad)
         y = torch.empty(x.shape[0], n_out, device=x.device, dtype=_BF16)
-        b = None if bias is None else bias.detach().to(_BF16).contiguous()
+        b = _bf16_or_none(bias)
         g = None if grid is None else grid.detach().float().contiguous()
         tab = None if grid is None else knot_tables(g, plan)
         desc = plan.desc()
         _launch("kf_fwd", _ptr(x), _ptr(packed), _ptr(b), _ptr(tab), _ptr(y), x.shape[0], n_in, n_out, nt, f_pad,
                 int(has_base), ctypes.byref(desc), _stream(x))
-        ctx.save_for_backward(x, coef_eff, base_eff, g)
+        ctx.save_for_backward(x, coef, base_weight, edge_scale, edge_mask, g)
         ctx.packed, ctx.knot_tab, ctx.plan, ctx.has_bias = packed, tab, plan, bias is not None
         ctx.layout = (nt, f_pad)
         return y
 
     @staticmethod
     def backward(ctx, gy):
-        x, coef_eff, base_eff, grid = ctx.saved_tensors
+        x, coef, base_weight, edge_scale, edge_mask, grid = ctx.saved_tensors
         plan = ctx.plan
         need = ctx.needs_input_grad
         if torch.is_grad_enabled():
-            return _fused_backward_differentiable(x, gy, coef_eff, base_eff, grid, plan, need, ctx.has_bias)
+            ctx.packed = ctx.knot_tab = None
+            return _fused_backward_differentiable(x, gy, coef, base_weight, edge_scale, edge_mask, grid, plan, need,
+                                                  ctx.has_bias)
         nt, f_pad = ctx.layout
-        n_out, n_in, k = coef_eff.shape
+        n_out, n_in, k = coef.shape
         gy = gy.to(_BF16).contiguous()
         desc = plan.desc()
         stream = _stream(x)
-        gx = gc = gb = gbias = None
-        if need[1] or need[2]:
+        gx = gc = gb = gbias = gs = None
+        if need[1] or need[2] or need[4]:
             gc = torch.empty(n_out, n_in, k, device=x.device, dtype=_BF16)
-            gb = torch.empty(n_out, n_in, device=x.device, dtype=_BF16) if base_eff is not None else None
+            gb = torch.empty(n_out, n_in, device=x.device, dtype=_BF16) if base_weight is not None else None
+            gs = torch.empty(n_out, n_in, device=x.device, dtype=_BF16) if (edge_scale is not None and need[4]) else None
             fold = None
             if plan.folded and not plan.is_identity_fold():
                 fold = torch.tensor(plan.fold(0), dtype=torch.float32, device=x.device)
-            _launch("kf_wgrad", _ptr(x), _ptr(gy), _ptr(ctx.knot_tab), _ptr(fold), _ptr(gc), _ptr(gb), x.shape[0], n_in, n_out,
-                      k, nt, f_pad, ctypes.byref(desc), stream)
-            gc = gc.to(coef_eff.dtype) if need[1] else None
-            gb = gb.to(base_eff.dtype) if (gb is not None and need[2]) else None
+            cf, sc, mk = _bf16_or_none(coef), _bf16_or_none(edge_scale), _bf16_or_none(edge_mask)
+            _launch("kf_wgrad", _ptr(x), _ptr(gy), _ptr(ctx.knot_tab), _ptr(fold), _ptr(cf), _ptr(sc), _ptr(mk), _ptr(gc),
+                    _ptr(gb), _ptr(gs), x.shape[0], n_in, n_out, k, nt, f_pad, ctypes.byref(desc), stream)
+            gc = gc.to(coef.dtype) if need[1] else None
+            gb = gb.to(base_weight.dtype) if (gb is not None and need[2]) else None
+            gs = gs.to(edge_scale.dtype) if gs is not None else None
         if need[0]:
             gx = torch.empty_like(x)
-            _launch("kf_dgrad", _ptr(x), _ptr(gy), _ptr(ctx.packed), _ptr(ctx.knot_tab), _ptr(gx), x.shape[0], n_in, n_out, nt,
-                      f_pad, int(base_eff is not None), ctypes.byref(desc), stream)
+            _launch("kf_dgrad", _ptr(x), _ptr(gy), _ptr(ctx.packed), _ptr(ctx.knot_tab), _ptr(gx), x.shape[0], n_in, n_out,
+                    nt, f_pad, int(base_weight is not None), ctypes.byref(desc), stream)
         if need[3]:
             gbias = gy.float().sum(0)
         ctx.packed = ctx.knot_tab = None
-        return gx, gc, gb, gbias, None, None
+        return gx, gc, gb, gbias, gs, None, None, None
 
 
-def _fused_backward_differentiable(x, gy, coef_eff, base_eff, grid, plan, need, has_bias):
+def _fused_backward_differentiable(x, gy, coef, base_weight, edge_scale, edge_mask, grid, plan, need, has_bias):
     """Gradients of the fused op as a graph of float32 primitives (create_graph=True)."""
     xf = x.float()
     gyf = gy.float()
     ones = torch.ones_like(xf)
     g = grid if grid is not None else xf.new_zeros(1)
-    cf = coef_eff.float()
-    gx = gc = gb = gbias = None
+    mask = edge_mask.float() if edge_mask is not None else torch.ones(coef.shape[:2], device=x.device)
+    sm = mask if edge_scale is None else edge_scale.float() * mask
+    ce = coef.float() * sm[..., None]
+    gx = gc = gb = gbias = gs = None
     if need[0]:
-        gx = prim_P(xf, gyf, cf, g, plan, 1)
-        if base_eff is not None:
+        gx = prim_P(xf, gyf, ce, g, plan, 1)
+        if base_weight is not None:
             s = torch.sigmoid(xf)
-            gx = gx + (gyf @ base_eff.float()) * (s * (1 + xf * (1 - s)))
+            gx = gx + (gyf @ (base_weight.float() * mask)) * (s * (1 + xf * (1 - s)))
         gx = gx.to(x.dtype)
-    if need[1]:
-        gc = prim_G(xf, gyf, ones, g, plan, 0).to(coef_eff.dtype)
-    if need[2] and base_eff is not None:
-        gb = (gyf.T @ torch.nn.functional.silu(xf)).to(base_eff.dtype)
+    if need[1] or need[4]:
+        gce = prim_G(xf, gyf, ones, g, plan, 0)
+        if need[1]:
+            gc = (gce * sm[..., None]).to(coef.dtype)
+        if need[4] and edge_scale is not None:
+            gs = ((gce * coef.float()).sum(-1) * mask).to(edge_scale.dtype)
+    if need[2] and base_weight is not None:
+        gb = ((gyf.T @ torch.nn.functional.silu(xf)) * mask).to(base_weight.dtype)
     if need[3] and has_bias:
         gbias = gyf.sum(0)
-    return gx, gc, gb, gbias, None, None
+    return gx, gc, gb, gbias, gs, None, None, None
 
 
-def kan_linear_fused(x, coef_eff, base_eff, bias, grid, plan):
+def kan_linear_fused(x, coef, base_weight, bias, edge_scale, edge_mask, grid, plan):
     """Fused KANLinear on (..., I) bf16 inputs; see ``_FusedKANLinear``."""
     lead = x.shape[:-1]
-    y = _FusedKANLinear.apply(x.reshape(-1, x.shape[-1]), coef_eff, base_eff, bias, grid, plan)
-    return y.reshape(*lead, coef_eff.shape[0])
+    y = _FusedKANLinear.apply(x.reshape(-1, x.shape[-1]), coef, base_weight, bias, edge_scale, edge_mask, grid, plan)
+    return y.reshape(*lead, coef.shape[0])
 
 
 # --- edge_derivative ---------------------------------------------------------

@@ -204,6 +204,11 @@ class KANLinear(nn.Module):
         if self.training and self.edge_dropout > 0:
             raise NotImplementedError("edge_dropout (DropKAN) is not part of the kanforge_b200 kernel path")
         plan = self._plan
+        if plan.kind != "rational" and _kernels.fused_ok(plan, x, self.out_features, self.base_weight is not None,
+                                                          self.coef.dtype):
+            # coef * edge_scale * edge_mask and base_weight * edge_mask are formed inside the kernels
+            return _kernels.kan_linear_fused(x, self.coef, self.base_weight, self.bias, self.edge_scale, self.edge_mask,
+                                             self._grid(), plan)
         coef_eff = self.effective_coef()
         base_eff = self.effective_base_weight()
         if plan.kind == "rational":
@@ -214,8 +219,6 @@ class KANLinear(nn.Module):
             if base_eff is not None:
                 y = y + F.linear(F.silu(x2), base_eff)
             return y.reshape(*lead, self.out_features)
-        if _kernels.fused_ok(plan, x, self.out_features, base_eff is not None):
-            return _kernels.kan_linear_fused(x, coef_eff, base_eff, self.bias, self._grid(), plan)
         y = _kernels.spline_forward(x, coef_eff, self._grid(), plan)
         if base_eff is not None:
             y = y + F.linear(self.base_activation(x), base_eff)
