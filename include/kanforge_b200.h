@@ -171,6 +171,25 @@ int kf_rational_bwd(const void* x, const void* dr, const float* num, const float
 /* Workspace (float32 elements) that kf_rational_bwd needs. */
 int64_t kf_rational_workspace(int64_t B, int32_t I, const kf_basis_desc* basis);
 
+/* kf_rational_bwd for callers that cannot allocate device memory.  Some hosts
+ * of this library may not call cudaMalloc: code that runs inside a device
+ * memory allocator or pool callback (allocating there would re-enter the
+ * allocator), frameworks that own every byte of device memory and hand kernels
+ * only the buffers they planned, and runtimes that forbid allocation after
+ * start-up to keep latency and memory use fixed.  This entry point takes no
+ * workspace: the per-CTA partial sums live in a fixed array of
+ * KF_RATIONAL_NOALLOC_MAX_FLOATS floats (4 MiB) that is part of the library's
+ * device code, so every GPU that loads the library holds it until the process
+ * exits.  Requires I * (p + 1 + q) <= KF_RATIONAL_NOALLOC_MAX_FLOATS (else
+ * KF_ERR_ARG with a message) and allocates and frees nothing.  The first call
+ * on a device looks up the array's device address (cudaGetSymbolAddress) and
+ * must come before any stream capture.  All calls share the array: calls whose
+ * kernels overlap on the GPU race.  The caller still passes inputs and outputs.
+ * Has no counterpart in the reference. */
+#define KF_RATIONAL_NOALLOC_MAX_FLOATS (1 << 20)
+int kf_rational_bwd_noalloc(const void* x, const void* dr, const float* num, const float* den, void* dx, float* dnum,
+                            float* dden, int64_t B, int32_t I, const kf_basis_desc* basis, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

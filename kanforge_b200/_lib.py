@@ -72,6 +72,10 @@ PROTOTYPES = {
         [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i32, ctypes.POINTER(BasisDesc), ctypes.c_int, _vp],
     ),
     "kf_rational_workspace": (_c_i64, [_c_i64, _c_i32, ctypes.POINTER(BasisDesc)]),
+    "kf_rational_bwd_noalloc": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i32, ctypes.POINTER(BasisDesc), ctypes.c_int, _vp],
+    ),
 }
 
 _lock = threading.Lock()

@@ -9,6 +9,8 @@
 // The parameter gradients are reduced deterministically: each CTA writes
 // per-(CTA, input) partial sums into the caller's workspace, a second kernel
 // sums them in a fixed order.
+#include <mutex>
+
 #include "basis.cuh"
 
 namespace kf {
@@ -140,6 +142,38 @@ int rat_params(const kf_basis_desc* d, int I, RatParams& p) {
 
 int64_t rat_blocks(int64_t B) { return B <= 0 ? 1 : std::min<int64_t>(kRatMaxBlocks, B); }
 
+// ---------------------------------------------------------------------------
+// Scratch for kf_rational_bwd_noalloc: a fixed array in device memory, one per
+// GPU that loads this library, held until the process exits.  Host code must
+// not pass the symbol itself to a kernel (on the host it is only a stand-in);
+// the device address comes from cudaGetSymbolAddress, once per device.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) float g_rational_scratch[KF_RATIONAL_NOALLOC_MAX_FLOATS];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+float* g_scratch_ptr[kMaxDevices] = {};
+
+// Device address of g_rational_scratch on the current device (resolved on the
+// first call per device).
+int rational_scratch(float** out) {
+  int dev = -1;
+  KF_CUDA_RET(cudaGetDevice(&dev));
+  KF_CHECK_ARG(dev >= 0 && dev < kMaxDevices, "kf_rational_bwd_noalloc: device %d beyond %d", dev, kMaxDevices);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t err = cudaGetSymbolAddress(&p, g_rational_scratch);
+    if (err != cudaSuccess || p == nullptr) {
+      set_error("kf_rational_bwd_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev, cudaGetErrorString(err));
+      return KF_ERR_CUDA;
+    }
+    g_scratch_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_scratch_ptr[dev];
+  return KF_OK;
+}
+
 }  // namespace
 
 }  // namespace kf
@@ -206,4 +240,52 @@ extern "C" int kf_rational_bwd(const void* x, const void* dr, const float* num, 
   if (int rc = check_launch("kf_rational_bwd")) return rc;
   rational_reduce_kernel<<<(unsigned)(p.groups * (p.na + p.nb)), kRatThreads, 0, s>>>(workspace, dnum, dden, (int)used, I, p);
   return check_launch("kf_rational_bwd (reduce)");
+}
+
+// Same computation as kf_rational_bwd, with the per-CTA partial sums in the
+// library's fixed device array instead of a caller workspace.  The number of
+// partial rows is lowered until they fit the array (the final sums then run in
+// a different order than kf_rational_bwd, equal up to float32 rounding).
+// Every element the reduction reads is written by the same call first, so
+// nothing needs to start at zero; calls that overlap on the GPU share the array
+// and race.
+extern "C" int kf_rational_bwd_noalloc(const void* x, const void* dr, const float* num, const float* den, void* dx,
+                                       float* dnum, float* dden, int64_t B, int32_t I, const kf_basis_desc* basis,
+                                       int dtype, void* stream) {
+  using namespace kf;
+  clear_error();
+  RatParams p{};
+  if (int rc = rat_params(basis, I, p)) return rc;
+  KF_CHECK_ARG(x && dr && num && den && dx && dnum && dden && B >= 0, "kf_rational_bwd_noalloc: bad arguments");
+  const int64_t row = (int64_t)I * (p.na + p.nb);  // partial sums of one CTA
+  KF_CHECK_ARG(row <= KF_RATIONAL_NOALLOC_MAX_FLOATS,
+               "kf_rational_bwd_noalloc: I * (p + 1 + q) = %lld exceeds the fixed scratch of %d floats",
+               (long long)row, KF_RATIONAL_NOALLOC_MAX_FLOATS);
+  if (int rc = bind_device(x)) return rc;
+  float* ws = nullptr;
+  if (int rc = rational_scratch(&ws)) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (B == 0) {
+    KF_CUDA_RET(cudaMemsetAsync(dnum, 0, sizeof(float) * p.groups * p.na, s));
+    KF_CUDA_RET(cudaMemsetAsync(dden, 0, sizeof(float) * p.groups * p.nb, s));
+    return KF_OK;
+  }
+  const int64_t cap = std::max<int64_t>(1, KF_RATIONAL_NOALLOC_MAX_FLOATS / row);
+  const int64_t nblk = std::min<int64_t>(rat_blocks(B), cap);
+  const int64_t rows = cdiv(B, nblk);
+  const int64_t used = cdiv(B, rows);
+  const size_t smem = sizeof(float) * p.groups * (p.na + p.nb);
+  if (dtype == KF_DTYPE_F32) {
+    rational_bwd_kernel<float><<<(unsigned)used, kRatThreads, smem, s>>>((const float*)x, (const float*)dr, num, den,
+                                                                         (float*)dx, ws, B, I, rows, p);
+  } else if (dtype == KF_DTYPE_BF16) {
+    rational_bwd_kernel<__nv_bfloat16><<<(unsigned)used, kRatThreads, smem, s>>>(
+        (const __nv_bfloat16*)x, (const __nv_bfloat16*)dr, num, den, (__nv_bfloat16*)dx, ws, B, I, rows, p);
+  } else {
+    set_error("kf_rational_bwd_noalloc: dtype %d unsupported", dtype);
+    return KF_ERR_UNSUPPORTED;
+  }
+  if (int rc = check_launch("kf_rational_bwd_noalloc")) return rc;
+  rational_reduce_kernel<<<(unsigned)(p.groups * (p.na + p.nb)), kRatThreads, 0, s>>>(ws, dnum, dden, (int)used, I, p);
+  return check_launch("kf_rational_bwd_noalloc (reduce)");
 }
