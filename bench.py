@@ -143,6 +143,7 @@ def build_workload(cfg: int, dtype_name: str, device, seed: int, tokens: int | N
         loss.backward()
         return loss
 
+    step.loss_fn = loss_fn
     return model, x, step, params, flops, x.shape[0] if cfg in (1, 2) else CONFIGS[cfg]["tokens"], kwork, dtype
 
 
@@ -327,19 +328,14 @@ def run_ours(args, world, rank, local):
     cfg = args.config
     model, x, step, params, flops, units, kwork, dtype = build_workload(cfg, args.dtype, device, seed=1234 + rank,
                                                                         tokens=args.tokens)
+    loss_of = getattr(step, "loss_fn", None)
+
+    from kanforge_b200.data_parallel import allreduce_gradients, max_over_ranks
 
     def full_step():
         out = step()
         if pg is not None and params:
-            import torch.distributed as dist
-
-            flat = torch.cat([p.grad.reshape(-1) for p in params])
-            dist.all_reduce(flat, group=pg)
-            off = 0
-            for p in params:
-                n = p.numel()
-                p.grad.copy_(flat[off: off + n].view_as(p.grad))
-                off += n
+            allreduce_gradients(params, group=pg)
         return out
 
     def barrier():
@@ -377,11 +373,7 @@ def run_ours(args, world, rank, local):
     launches = (kb.kernels.LAUNCH_COUNT - launches0) // max(1, args.steps)
     elapsed_ms = start.elapsed_time(end)
     if pg is not None:
-        import torch.distributed as dist
-
-        t = torch.tensor([elapsed_ms], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=pg)
-        elapsed_ms = float(t.item())
+        elapsed_ms = max_over_ranks(elapsed_ms, device, pg)
     ms_per_step = elapsed_ms / args.steps
     value = world * units * args.steps / (elapsed_ms / 1e3)
     kb.kernels.check_device_errors()
@@ -401,14 +393,11 @@ def run_ours(args, world, rank, local):
         x_dev.requires_grad_(True)
         for p in params:
             p.grad = None
-        loss = (model(x_dev) - 0).float().square().mean() if cfg != 0 else step()
-        if cfg != 0:
-            loss.backward()
+        y = model(x_dev)
+        loss = loss_of(y)
+        loss.backward()
         if pg is not None and params:
-            import torch.distributed as dist
-
-            flat = torch.cat([p.grad.reshape(-1) for p in params])
-            dist.all_reduce(flat, group=pg)
+            allreduce_gradients(params, group=pg)
         loss_host.copy_(loss.detach().float().reshape(1), non_blocking=True)
         x_dev.requires_grad_(False)
 
@@ -424,11 +413,7 @@ def run_ours(args, world, rank, local):
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
     if pg is not None:
-        import torch.distributed as dist
-
-        t = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=pg)
-        e2e_ms = float(t.item())
+        e2e_ms = max_over_ranks(e2e_ms, device, pg)
     e2e_value = world * units * args.steps / (e2e_ms / 1e3)
 
     # ---- roofline of the dominant kernel ----
