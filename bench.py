@@ -120,15 +120,16 @@ def build_workload(cfg: int, dtype_name: str, device, seed: int, tokens: int | N
     elif cfg == 4:
         dtype = torch.float32
         model = kb.KANLinear(64, 64, kb.Jacobi(6, 0.5, 0.5), device=device)
-        x = (torch.rand(262144, 64, generator=g) * 2 - 1).to(device)
+        nb = tokens or 262144
+        x = (torch.rand(nb, 64, generator=g) * 2 - 1).to(device)
         flops = None
-        kwork = {"kf_edge_derivative": 4.0 * 262144 * (64 * 64 + 64)}
+        kwork = {"kf_edge_derivative": 4.0 * nb * (64 * 64 + 64)}
 
         def step():
             with torch.no_grad():
                 return model.edge_derivative(x, 2)
 
-        return model, x, step, [], flops, 262144, kwork, dtype
+        return model, x, step, [], flops, nb, kwork, dtype
     else:
         raise SystemExit(f"unknown config {cfg}")
 
@@ -472,7 +473,7 @@ def main(argv=None):
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tokens", type=int, default=None,
-                    help="profiling case: override the batch of configs 1-2 (not a bench line)")
+                    help="profiling case: override the batch of configs 1, 2, 4 (not a bench line)")
     args = ap.parse_args(argv)
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

@@ -142,14 +142,16 @@ int kf_wgrad(const void* x, const void* dy, const float* knot_tab, const float* 
              int32_t I, int32_t O, int32_t K, int32_t nt, int32_t f_pad, const kf_basis_desc* basis, void* stream);
 
 /* edge_derivative (kanforge/torch/layers.py:206-226), float32:
- *   out[b,o,i] = sum_j phi_j^(order)(x[b,i]) coef[o,i,j] + s(x[b,i]) base_eff[o,i]
- * coef (O,I,nf): for KF_BASIS_CHEB the caller passes coef_eff @ fold(order)
- * and phi_j = T_j(g(x)); otherwise coef_eff and the native derivative.
+ *   out[b,o,i] = sum_j phi_j^(order)(x[b,i]) coefT[o,j,i] + s(x[b,i]) base_eff[o,i]
+ * coefT (O,nf,I) -- the effective coefficients with the feature axis moved
+ * before the input axis: for KF_BASIS_CHEB the caller passes
+ * (coef_eff @ fold(order)) transposed and phi_j = T_j(g(x)); otherwise
+ * coef_eff transposed and the native derivative.
  * s = silu^(order) given by the polynomials h_order(sigma), h_{order-1}(sigma):
  * silu^(m)(x) = x h_m(s) + m h_{m-1}(s) (kanforge/_calculus.py:90-96), passed as
  * silu_poly = [h_m coefficients (n_poly) , h_{m-1} coefficients (n_poly)];
  * base_eff null: no base term.  out (B,O,I). */
-int kf_edge_derivative(const float* x, const float* coef, const float* base_eff, const float* grid,
+int kf_edge_derivative(const float* x, const float* coefT, const float* base_eff, const float* grid,
                        const float* basis_num, const float* basis_den, float* out, int64_t B, int32_t I,
                        int32_t O, int32_t nf, int32_t order, const kf_basis_desc* basis,
                        const float* silu_poly, int32_t n_poly, void* stream);

@@ -2,149 +2,272 @@
 // (reference kanforge/torch/layers.py:206-226).
 //
 // The output (B, O, I) is the whole cost (4.3 GB at the PINN configuration),
-// so the kernel is organised around writing it once at HBM speed: every thread
-// owns 4 consecutive inputs of NB rows, evaluates their features once into
-// registers, then streams over all outputs o with one 16-byte streaming store
-// per (row, o).  Coefficients are read in the transposed layout (O, nf, I) so
-// that the 4 inputs of a thread are one 16-byte load per feature; they stay in
-// L1/L2 (O*nf*I floats, 147 KB at the PINN configuration).
+// so the kernel is organised around writing it once at HBM speed: the
+// features of a (row, input) pair are evaluated once and kept in registers
+// while all outputs o stream past, and the coefficients (O*nf*I floats, read
+// in the (O, nf, I) layout so that a warp's load is one 128-byte line) stay in
+// L1/L2 and are reused over many rows per thread.
+#include <algorithm>
+
 #include "features.cuh"
 
 namespace kf {
 
 namespace {
 
-constexpr int kEdgeLanesI = 16;  // float4 lanes along i: 64 inputs per CTA
-constexpr int kEdgeLanesB = 8;   // row lanes
+constexpr int kEdgeThreads = 256;
+constexpr int kEdgeMaxNF = 16;  // features per input of the streaming kernel
 
 struct EdgeArgs {
   const float* x;
-  const float* coefT;  // (O, nf, I)
+  const float* coef;   // (O, nf, I)
   const float* base;   // (O, I) or null
   const float* num;    // rational: (groups, na)
   const float* den;    // rational: (groups, nb)
   float* out;
   int64_t B;
   int I, O, nf, m;
+  int kind, order;     // KF_BASIS_*, B-spline order
   int na, nb, in_per_group;
   float poly[2 * 8];   // h_m, h_{m-1} in sigmoid (silu derivatives)
   int n_poly;
   FeatArgs fa;
 };
 
-// Feature j of order m at x for input i (rational: j == 0 only).
-template <int BK>
-__device__ __forceinline__ void edge_features(const EdgeArgs& A, int i, float x, const float* t, float* f) {
-  if constexpr (BK < 0) {
-    const int g = i / A.in_per_group;
-    f[0] = rational_deriv(x, A.num + (size_t)g * A.na, A.na, A.den + (size_t)g * A.nb, A.nb, A.m);
-  } else {
-    eval_features<BK>(A.fa, x, 1.0f, t, f, 1);
+// Features j < nf of order m at x for input i; t: knots of input i (B-splines).
+__device__ __forceinline__ void edge_features_rt(const EdgeArgs& A, int i, float x, const float* t, float* f,
+                                                 int stride = 1) {
+  switch (A.kind == KF_BASIS_BSPLINE ? A.order : (A.kind == KF_BASIS_RATIONAL ? -1 : 0)) {
+    case -1: {
+      const int g = i / A.in_per_group;
+      f[0] = rational_deriv(x, A.num + (size_t)g * A.na, A.na, A.den + (size_t)g * A.nb, A.nb, A.m);
+      break;
+    }
+    case 0: eval_features<0>(A.fa, x, 1.0f, t, f, stride); break;
+    case 1: eval_features<1>(A.fa, x, 1.0f, t, f, stride); break;
+    case 2: eval_features<2>(A.fa, x, 1.0f, t, f, stride); break;
+    case 3: eval_features<3>(A.fa, x, 1.0f, t, f, stride); break;
+    case 4: eval_features<4>(A.fa, x, 1.0f, t, f, stride); break;
+    default: eval_features<5>(A.fa, x, 1.0f, t, f, stride); break;
   }
 }
 
-template <int BK, int NFM, int NB>
-__global__ void __launch_bounds__(kEdgeLanesI * kEdgeLanesB) edge_vec_kernel(EdgeArgs A) {
-  __shared__ float Ts[64 * KF_NK_MAX];
-  const int li = threadIdx.x % kEdgeLanesI;
-  const int lb = threadIdx.x / kEdgeLanesI;
-  const int i_base = blockIdx.y * 64;
-  const int i4 = i_base + li * 4;
-  const int64_t b_base = (int64_t)blockIdx.x * (kEdgeLanesB * NB) + lb * NB;
-  if constexpr (BK > 0) {
-    for (int e = threadIdx.x; e < 64 * A.fa.nk; e += blockDim.x) {
+__device__ __forceinline__ void load_knots_rt(const EdgeArgs& A, int i, float* t) {
+  if (A.kind != KF_BASIS_BSPLINE) return;
+  const float* g = A.fa.grid + (size_t)i * (A.fa.G + 1);
+  for (int r = 0; r < A.fa.nk; ++r) t[r] = extended_knot(g, A.fa.G, A.order, r);
+}
+
+// Row r of the paired feature registers (rows 2p and 2p+1 share the float2
+// feat[p][j]) from the thread's shared-memory column, for a run-time r: one
+// case per row keeps every register index static, so the caller's row loop
+// (and the basis code in it) is not unrolled.
+template <int NP, int NJ>
+__device__ __forceinline__ void copy_row(float2 (&feat)[NP][NJ], int r, const float* fs) {
+#pragma unroll
+  for (int rr = 0; rr < 2 * NP; ++rr)
+    if (rr == r) {
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) {
+        if (rr % 2 == 0)
+          feat[rr / 2][j].x = fs[j * kEdgeThreads];
+        else
+          feat[rr / 2][j].y = fs[j * kEdgeThreads];
+      }
+    }
+}
+
+// Rows per thread of the streaming kernel for NF features: an even number
+// that keeps NB x (NF + 1) feature registers near 170, so that the
+// coefficients of one output (NF + 1 loads) serve NB outputs.
+__host__ __device__ constexpr int edge_rows(int nf) {
+  return (168 / (nf + 1) < 2 ? 2 : (168 / (nf + 1) > 16 ? 16 : 168 / (nf + 1))) & ~1;
+}
+
+// One lane per input; a warp covers il consecutive inputs (il = 32, or the
+// power of two covering I when I < 32) times 32 / il consecutive outputs, so
+// each of its stores is one contiguous 128-byte run of the (B, O, I) output.
+// A warp owns NB rows at a time: it evaluates their features (the silu term
+// as feature NF) once, passing them through the thread's own shared-memory
+// column so that the run-time basis code is inlined once, into registers
+// paired by rows; then it streams over the outputs o: NF + 1 coalesced
+// coefficient loads (the next output's issued before this one's arithmetic)
+// feed NB outputs, two rows per packed f32x2 FMA.  Warps take row groups
+// independently (persistent, no barrier after the knot table), so one warp's
+// feature prologue overlaps the others' stores.
+template <int NF, int NB, int MINB, bool PF>
+__global__ void __launch_bounds__(kEdgeThreads, MINB) edge_vec_kernel(const __grid_constant__ EdgeArgs A, int il_log2) {
+  static_assert(NB % 2 == 0, "rows are processed in pairs");
+  constexpr int NJ = NF + 1, NP = NB / 2;
+  extern __shared__ float smem[];
+  float* Fs = smem;                          // [NJ][kEdgeThreads]: one row's features per thread
+  float* Ts = smem + NJ * kEdgeThreads;      // [il][KF_NK_MAX] (B-splines)
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int il = 1 << il_log2, ol = 32 / il;
+  const int i = blockIdx.y * il + (lane & (il - 1));
+  const int lo = lane >> il_log2;
+  const int i_base = blockIdx.y * il;
+  if (A.kind == KF_BASIS_BSPLINE) {
+    const int n_in = min(il, A.I - i_base);
+    for (int e = threadIdx.x; e < n_in * A.fa.nk; e += blockDim.x) {
       const int ii = e / A.fa.nk, r = e % A.fa.nk;
-      if (i_base + ii < A.I) Ts[ii * KF_NK_MAX + r] = extended_knot(A.fa.grid + (size_t)(i_base + ii) * (A.fa.G + 1), A.fa.G, BK, r);
+      Ts[ii * KF_NK_MAX + r] = extended_knot(A.fa.grid + (size_t)(i_base + ii) * (A.fa.G + 1), A.fa.G, A.order, r);
     }
     __syncthreads();
   }
-  if (i4 >= A.I) return;
-  float feat[NB][4][NFM];
-  float sb[NB][4];
-  bool row_ok[NB];
+  if (i >= A.I) return;
+  const float* ti = Ts + (i - i_base) * KF_NK_MAX;
+  float* fs = Fs + threadIdx.x;
+  const int64_t n_groups = (A.B + NB - 1) / NB;
+  const size_t c_step = (size_t)ol * NF * A.I, o_step = (size_t)ol * A.I, row_step = (size_t)A.O * A.I;
+  for (int64_t grp = (int64_t)blockIdx.x * (kEdgeThreads / 32) + warp; grp < n_groups;
+       grp += (int64_t)gridDim.x * (kEdgeThreads / 32)) {
+    const int64_t b0 = grp * NB;
+    const int nrows = (int)min((int64_t)NB, A.B - b0);
+    // Defined before the row loop: copy_row sets one row per trip, and an
+    // undefined start would let the compiler fold its selects away.
+    float2 feat[NP][NJ];
 #pragma unroll
-  for (int r = 0; r < NB; ++r) {
-    const int64_t b = b_base + r;
-    row_ok[r] = b < A.B;
-    const float4 xv = row_ok[r] ? *reinterpret_cast<const float4*>(A.x + b * A.I + i4) : make_float4(0, 0, 0, 0);
-    const float xs[4] = {xv.x, xv.y, xv.z, xv.w};
+    for (int p = 0; p < NP; ++p)
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      float tmp[KF_NF_MAX];
-      edge_features<BK>(A, i4 + c, xs[c], Ts + (li * 4 + c) * KF_NK_MAX, tmp);
-#pragma unroll
-      for (int j = 0; j < NFM; ++j) feat[r][c][j] = j < A.nf ? tmp[j] : 0.0f;
-      sb[r][c] = A.base ? silu_deriv(xs[c], A.m, A.poly, A.n_poly) : 0.0f;
-    }
-  }
-  for (int o = 0; o < A.O; ++o) {
-    float4 cf[NFM];
-    const float* crow = A.coefT + (size_t)o * A.nf * A.I + i4;
-#pragma unroll
-    for (int j = 0; j < NFM; ++j) cf[j] = j < A.nf ? __ldg(reinterpret_cast<const float4*>(crow + (size_t)j * A.I)) : make_float4(0, 0, 0, 0);
-    const float4 bw = A.base ? __ldg(reinterpret_cast<const float4*>(A.base + (size_t)o * A.I + i4)) : make_float4(0, 0, 0, 0);
-#pragma unroll
+      for (int j = 0; j < NJ; ++j) feat[p][j] = make_float2(0.0f, 0.0f);
+#pragma unroll 1
     for (int r = 0; r < NB; ++r) {
-      if (!row_ok[r]) continue;
-      float acc[4] = {sb[r][0] * bw.x, sb[r][1] * bw.y, sb[r][2] * bw.z, sb[r][3] * bw.w};
+      const float x = r < nrows ? __ldg(A.x + (b0 + r) * A.I + i) : 0.0f;
+      edge_features_rt(A, i, x, ti, fs, kEdgeThreads);
+      fs[NF * kEdgeThreads] = A.base ? silu_deriv(x, A.m, A.poly, A.n_poly) : 0.0f;
+      copy_row<NP, NJ>(feat, r, fs);
+    }
+
+    const float* cp = A.coef + (size_t)lo * NF * A.I + i;  // (O, NF, I)
+    const float* bp = A.base ? A.base + (size_t)lo * A.I + i : nullptr;
+    float* op = A.out + (b0 * A.O + lo) * A.I + i;
+    float qn[NJ];
+    if (PF && lo < A.O) {
 #pragma unroll
-      for (int j = 0; j < NFM; ++j) {
-        acc[0] = fmaf(feat[r][0][j], cf[j].x, acc[0]);
-        acc[1] = fmaf(feat[r][1][j], cf[j].y, acc[1]);
-        acc[2] = fmaf(feat[r][2][j], cf[j].z, acc[2]);
-        acc[3] = fmaf(feat[r][3][j], cf[j].w, acc[3]);
+      for (int j = 0; j < NF; ++j) qn[j] = __ldg(cp + (size_t)j * A.I);
+      qn[NF] = bp ? __ldg(bp) : 0.0f;
+    }
+    for (int o = lo; o < A.O; o += ol) {
+      float q[NJ];
+      if constexpr (PF) {
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) q[j] = qn[j];
+        if (o + ol < A.O) {
+#pragma unroll
+          for (int j = 0; j < NF; ++j) qn[j] = __ldg(cp + c_step + (size_t)j * A.I);
+          qn[NF] = bp ? __ldg(bp + o_step) : 0.0f;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < NF; ++j) q[j] = __ldg(cp + (size_t)j * A.I);
+        q[NF] = bp ? __ldg(bp) : 0.0f;
       }
-      __stcs(reinterpret_cast<float4*>(A.out + ((b_base + r) * A.O + o) * A.I + i4), make_float4(acc[0], acc[1], acc[2], acc[3]));
+      float2 acc[NP];
+      {
+        const float2 qq = make_float2(q[NF], q[NF]);
+#pragma unroll
+        for (int p = 0; p < NP; ++p) acc[p] = __fmul2_rn(feat[p][NF], qq);
+      }
+#pragma unroll
+      for (int j = 0; j < NF; ++j) {
+        const float2 qq = make_float2(q[j], q[j]);
+#pragma unroll
+        for (int p = 0; p < NP; ++p) acc[p] = __ffma2_rn(feat[p][j], qq, acc[p]);
+      }
+#pragma unroll
+      for (int p = 0; p < NP; ++p) {
+        if (2 * p < nrows) __stcs(op + (2 * p) * row_step, acc[p].x);
+        if (2 * p + 1 < nrows) __stcs(op + (2 * p + 1) * row_step, acc[p].y);
+      }
+      cp += c_step;
+      if (bp) bp += o_step;
+      op += o_step;
     }
   }
 }
 
 // Any I and nf <= KF_NF_MAX: one thread per (b, i), looping over o.
-template <int BK>
 __global__ void __launch_bounds__(256) edge_scalar_kernel(EdgeArgs A) {
   const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (e >= A.B * A.I) return;
   const int64_t b = e / A.I;
   const int i = (int)(e % A.I);
   float t[KF_NK_MAX];
-  if constexpr (BK > 0) load_knots<BK>(A.fa, i, t, 0, 1);
+  load_knots_rt(A, i, t);
   const float x = A.x[e];
   float f[KF_NF_MAX];
-  edge_features<BK>(A, i, x, t, f);
+  edge_features_rt(A, i, x, t, f);
   const float sb = A.base ? silu_deriv(x, A.m, A.poly, A.n_poly) : 0.0f;
   for (int o = 0; o < A.O; ++o) {
     float acc = A.base ? sb * A.base[(size_t)o * A.I + i] : 0.0f;
-    for (int j = 0; j < A.nf; ++j) acc = fmaf(f[j], A.coefT[((size_t)o * A.nf + j) * A.I + i], acc);
+    const float* c = A.coef + (size_t)o * A.nf * A.I + i;
+    for (int j = 0; j < A.nf; ++j) acc = fmaf(f[j], c[(size_t)j * A.I], acc);
     A.out[(b * A.O + o) * A.I + i] = acc;
   }
 }
 
-struct EdgeLaunch {
-  EdgeArgs A;
-  cudaStream_t stream;
-  bool vec;
-
-  template <int BK>
-  int operator()() const {
-    if (vec && A.nf <= 10) {
-      constexpr int NB = 2;
-      dim3 grid((unsigned)cdiv(A.B, kEdgeLanesB * NB), (unsigned)cdiv(A.I, 64));
-      edge_vec_kernel<BK, 10, NB><<<grid, kEdgeLanesI * kEdgeLanesB, 0, stream>>>(A);
-    } else if (vec && A.nf <= 16) {
-      dim3 grid((unsigned)cdiv(A.B, kEdgeLanesB), (unsigned)cdiv(A.I, 64));
-      edge_vec_kernel<BK, 16, 1><<<grid, kEdgeLanesI * kEdgeLanesB, 0, stream>>>(A);
-    } else {
-      edge_scalar_kernel<BK><<<(unsigned)cdiv(A.B * A.I, 256), 256, 0, stream>>>(A);
-    }
-    return check_launch("kf_edge_derivative");
+template <int NF, int NB, int MINB, bool PF>
+int launch_vec_cfg(const EdgeArgs& A, cudaStream_t stream) {
+  int il_log2 = 5;
+  while (il_log2 > 0 && (1 << (il_log2 - 1)) >= A.I) --il_log2;
+  const size_t smem = ((size_t)(NF + 1) * kEdgeThreads + (A.kind == KF_BASIS_BSPLINE ? (32 * KF_NK_MAX) : 0)) * sizeof(float);
+  int dev = 0, n_sm = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+  // The coefficients are read through L1: keep the shared-memory carve-out small.
+  cudaError_t e = cudaFuncSetAttribute(edge_vec_kernel<NF, NB, MINB, PF>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(edge_vec_kernel<NF, NB, MINB, PF>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             (int)cudaSharedmemCarveoutMaxL1);
+  if (e != cudaSuccess) {
+    set_error("kf_edge_derivative: shared memory attribute: %s", cudaGetErrorString(e));
+    return KF_ERR_CUDA;
   }
-};
+  const unsigned gy = (unsigned)cdiv(A.I, 1 << il_log2);
+  const int64_t n_groups = cdiv(A.B, (int64_t)NB);
+  const int64_t gx_need = cdiv(n_groups, (int64_t)(kEdgeThreads / 32));
+  const int slots = n_sm * MINB;
+  const unsigned gx = (unsigned)std::max<int64_t>(1, std::min<int64_t>(gx_need, std::max(1, slots / (int)std::min<unsigned>(gy, slots))));
+  edge_vec_kernel<NF, NB, MINB, PF><<<dim3(gx, gy), kEdgeThreads, smem, stream>>>(A, il_log2);
+  return check_launch("kf_edge_derivative");
+}
+
+template <int NF>
+int launch_vec(const EdgeArgs& A, cudaStream_t stream) {
+  return launch_vec_cfg<NF, edge_rows(NF), 1, false>(A, stream);
+}
+
+int launch_edge(const EdgeArgs& A, bool vec, cudaStream_t stream) {
+  if (vec) {
+    switch (A.nf) {
+      case 1: return launch_vec<1>(A, stream);
+      case 2: return launch_vec<2>(A, stream);
+      case 3: return launch_vec<3>(A, stream);
+      case 4: return launch_vec<4>(A, stream);
+      case 5: return launch_vec<5>(A, stream);
+      case 6: return launch_vec<6>(A, stream);
+      case 7: return launch_vec<7>(A, stream);
+      case 8: return launch_vec<8>(A, stream);
+      case 9: return launch_vec<9>(A, stream);
+      case 10: return launch_vec<10>(A, stream);
+      case 11: return launch_vec<11>(A, stream);
+      case 12: return launch_vec<12>(A, stream);
+      case 13: return launch_vec<13>(A, stream);
+      case 14: return launch_vec<14>(A, stream);
+      case 15: return launch_vec<15>(A, stream);
+      case kEdgeMaxNF: return launch_vec<kEdgeMaxNF>(A, stream);
+      default: break;
+    }
+  }
+  edge_scalar_kernel<<<(unsigned)cdiv(A.B * A.I, 256), 256, 0, stream>>>(A);
+  return check_launch("kf_edge_derivative");
+}
 
 }  // namespace
 
 }  // namespace kf
 
-extern "C" int kf_edge_derivative(const float* x, const float* coef, const float* base_eff, const float* grid,
+extern "C" int kf_edge_derivative(const float* x, const float* coefT, const float* base_eff, const float* grid,
                                   const float* basis_num, const float* basis_den, float* out, int64_t B, int32_t I,
                                   int32_t O, int32_t nf, int32_t order, const kf_basis_desc* basis,
                                   const float* silu_poly, int32_t n_poly, void* stream) {
@@ -153,13 +276,13 @@ extern "C" int kf_edge_derivative(const float* x, const float* coef, const float
   KF_CHECK_ARG(basis != nullptr, "kf_edge_derivative: basis is null");
   KF_CHECK_ARG(B >= 0 && I >= 1 && O >= 1 && nf >= 1 && order >= 0, "kf_edge_derivative: bad sizes");
   KF_CHECK_ARG(nf <= KF_NF_MAX, "kf_edge_derivative: %d features exceed the limit %d", nf, KF_NF_MAX);
-  KF_CHECK_ARG(x && coef && out, "kf_edge_derivative: null tensor pointer");
+  KF_CHECK_ARG(x && coefT && out, "kf_edge_derivative: null tensor pointer");
   if (int rc = bind_device(x)) return rc;
   KF_CHECK_ARG(base_eff == nullptr || (silu_poly != nullptr && n_poly >= 1 && n_poly <= 8),
                "kf_edge_derivative: the base term needs 1..8 SiLU polynomial coefficients");
   EdgeArgs A{};
   A.x = x;
-  A.coefT = coef;
+  A.coef = coefT;
   A.base = base_eff;
   A.out = out;
   A.B = B;
@@ -167,34 +290,36 @@ extern "C" int kf_edge_derivative(const float* x, const float* coef, const float
   A.O = O;
   A.nf = nf;
   A.m = order;
+  A.kind = basis->kind;
+  A.order = basis->order;
   A.n_poly = base_eff ? n_poly : 0;
   for (int e = 0; e < 2 * A.n_poly; ++e) A.poly[e] = silu_poly[e];
   A.fa.m = order;
   A.fa.nf = nf;
   A.fa.map = basis->input_map;
   if (B == 0) return KF_OK;
-  const bool vec = (I % 4 == 0) && ((uintptr_t)x % 16 == 0) && ((uintptr_t)coef % 16 == 0) && ((uintptr_t)out % 16 == 0) &&
-                   (base_eff == nullptr || (uintptr_t)base_eff % 16 == 0);
-  EdgeLaunch L{A, (cudaStream_t)stream, vec};
   if (basis->kind == KF_BASIS_RATIONAL) {
     KF_CHECK_ARG(basis_num && basis_den, "kf_edge_derivative: rational needs its parameters");
     KF_CHECK_ARG(nf == 1, "kf_edge_derivative: rational has one feature");
     KF_CHECK_ARG(basis->groups >= 1 && I % basis->groups == 0, "kf_edge_derivative: groups must divide I");
     KF_CHECK_ARG(basis->degree + 1 <= KF_RAT_MAX_NUM && basis->den_degree <= KF_RAT_MAX_DEN && order <= KF_RAT_MAX_ORDER,
                  "kf_edge_derivative: rational degree/order beyond the kernel limits");
-    L.A.num = basis_num;
-    L.A.den = basis_den;
-    L.A.na = basis->degree + 1;
-    L.A.nb = basis->den_degree;
-    L.A.in_per_group = I / basis->groups;
-    return L.template operator()<-1>();
-  }
-  if (basis->kind == KF_BASIS_BSPLINE) {
+    A.num = basis_num;
+    A.den = basis_den;
+    A.na = basis->degree + 1;
+    A.nb = basis->den_degree;
+    A.in_per_group = I / basis->groups;
+  } else if (basis->kind == KF_BASIS_BSPLINE) {
     KF_CHECK_ARG(grid != nullptr, "kf_edge_derivative: B-spline needs its grid");
-    L.A.fa.G = basis->grid_size;
-    L.A.fa.nk = basis->grid_size + 2 * basis->order + 1;
-    L.A.fa.grid = grid;
-    KF_CHECK_ARG(L.A.fa.nk <= KF_NK_MAX, "kf_edge_derivative: too many knots");
+    KF_CHECK_ARG(basis->order >= 1 && basis->order <= 5, "kf_edge_derivative: B-spline order %d unsupported", basis->order);
+    A.fa.G = basis->grid_size;
+    A.fa.nk = basis->grid_size + 2 * basis->order + 1;
+    A.fa.grid = grid;
+    KF_CHECK_ARG(A.fa.nk <= KF_NK_MAX, "kf_edge_derivative: too many knots");
+  } else if (basis->kind != KF_BASIS_CHEB) {
+    set_error("kf_edge_derivative: basis kind %d unsupported", basis->kind);
+    return KF_ERR_UNSUPPORTED;
   }
-  return dispatch_bk(basis, L);
+  const bool vec = nf <= kEdgeMaxNF;
+  return launch_edge(A, vec, (cudaStream_t)stream);
 }

@@ -16,6 +16,7 @@ the KAT rational activation.
 from __future__ import annotations
 
 import ctypes
+import functools
 
 import torch
 
@@ -93,9 +94,17 @@ def _raw(op: str, plan: KernelPlan, m: int, x, a, b, grid, n_out: int, nf: int) 
     return out
 
 
-def _fold(plan: KernelPlan, m: int, like: torch.Tensor):
+@functools.lru_cache(maxsize=256)
+def _fold_on(plan: KernelPlan, m: int, device: torch.device, dtype: torch.dtype = torch.float32):
+    """R_m as a read-only device tensor, made once per (plan, order, device,
+    dtype): building it is a pageable host-to-device copy, which would
+    otherwise stall the stream on every call."""
     r = plan.fold(m)
-    return None if r is None else torch.tensor(r, dtype=like.dtype, device=like.device)
+    return None if r is None else torch.tensor(r, dtype=dtype, device=device)
+
+
+def _fold(plan: KernelPlan, m: int, like: torch.Tensor):
+    return _fold_on(plan, m, like.device, like.dtype)
 
 
 # --- differentiable primitives (kanforge/torch/kernels.py:70-140) -------------
@@ -236,7 +245,7 @@ def pack_coef(coef, base, edge_scale, edge_mask, plan: KernelPlan, f_pad: int) -
     base, scale, mask = conv(base), conv(edge_scale), conv(edge_mask)
     fold = None
     if plan.folded and not plan.is_identity_fold():
-        fold = torch.tensor(plan.fold(0), dtype=torch.float32, device=coef.device)
+        fold = _fold_on(plan, 0, coef.device)
     packed = torch.empty(n_out, n_in * f_pad, device=coef.device, dtype=_BF16)
     _launch("kf_pack_coef", _ptr(coef), _ptr(base), _ptr(scale), _ptr(mask), _ptr(fold), _ptr(packed), n_out, n_in, k,
             nt, f_pad, dt, _stream(coef))
@@ -293,7 +302,7 @@ class _FusedKANLinear(torch.autograd.Function):
             gs = torch.empty(n_out, n_in, device=x.device, dtype=_BF16) if (edge_scale is not None and need[4]) else None
             fold = None
             if plan.folded and not plan.is_identity_fold():
-                fold = torch.tensor(plan.fold(0), dtype=torch.float32, device=x.device)
+                fold = _fold_on(plan, 0, x.device)
             cf, sc, mk = _bf16_or_none(coef), _bf16_or_none(edge_scale), _bf16_or_none(edge_mask)
             _launch("kf_wgrad", _ptr(x), _ptr(gy), _ptr(ctx.knot_tab), _ptr(fold), _ptr(cf), _ptr(sc), _ptr(mk), _ptr(gc),
                     _ptr(gb), _ptr(gs), x.shape[0], n_in, n_out, k, nt, f_pad, ctypes.byref(desc), stream)
@@ -359,19 +368,19 @@ def edge_derivative(x, coef_eff, base_eff, grid, plan: KernelPlan, order: int, b
     c = coef_eff.detach().float()
     num = den = None
     if plan.kind == "cheb":
-        c = c @ torch.tensor(plan.fold(order), dtype=torch.float32, device=x.device)
+        c = c @ _fold_on(plan, order, x.device)
     elif plan.kind == "rational":
         num = basis_params["numerator"].detach().float().contiguous()
         den = basis_params["denominator"].detach().float().contiguous()
     nf = c.shape[-1]
-    coef_t = c.permute(0, 2, 1).contiguous()  # (O, nf, I)
+    coef_c = c.permute(0, 2, 1).contiguous()  # (O, nf, I): the kernel's coalesced layout
     base = None if base_eff is None else base_eff.detach().float().contiguous()
     g = None if grid is None else grid.detach().float().contiguous()
     polys = torch.as_tensor(silu_derivative_polys(order), dtype=torch.float32).flatten().contiguous()
     out = torch.empty(x2.shape[0], n_out, n_in, device=x.device, dtype=torch.float32)
     desc = plan.desc(groups)
     poly_buf = (ctypes.c_float * polys.numel())(*polys.tolist())
-    _launch("kf_edge_derivative", _ptr(x2), _ptr(coef_t), _ptr(base), _ptr(g), _ptr(num), _ptr(den), _ptr(out),
+    _launch("kf_edge_derivative", _ptr(x2), _ptr(coef_c), _ptr(base), _ptr(g), _ptr(num), _ptr(den), _ptr(out),
               x2.shape[0], n_in, n_out, nf, order, ctypes.byref(desc), ctypes.cast(poly_buf, ctypes.c_void_p),
               polys.numel() // 2, _stream(x2))
     return out.reshape(*lead, n_out, n_in)

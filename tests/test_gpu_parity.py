@@ -167,17 +167,39 @@ def test_edge_derivative_matches_reference(case, order):
     close(d, LAYERS[f"{case}/edge{order}"], FP32_TOL, f"edge{order}")
 
 
+# (n_in, n_out, batch): one or several 32-input chunks, partial chunks, I < 32
+# (several outputs per warp, some idle when O is small), ragged row groups.
+EDGE_SHAPES = [(64, 24, 301), (37, 3, 133), (5, 7, 1000), (2, 1, 4096), (130, 9, 50)]
+
+
 @pytest.mark.parametrize("basis", [kb.Jacobi(6, 0.5, 0.5), kb.BSpline(8, 3), kb.Chebyshev(5)], ids=repr)
 @pytest.mark.parametrize("order", [0, 2, 3])
-def test_edge_derivative_vector_path_matches_oracle(basis, order):
-    """I % 4 == 0 takes the float4 streaming kernel; ragged batch."""
+@pytest.mark.parametrize("shape", EDGE_SHAPES, ids=str)
+def test_edge_derivative_streaming_kernel_matches_oracle(basis, order, shape):
+    n_in, n_out, n_b = shape
     torch.manual_seed(0)
-    layer = kb.KANLinear(64, 24, basis, edge_scale=True, device=DEV)
+    layer = kb.KANLinear(n_in, n_out, basis, edge_scale=True, device=DEV)
     with torch.no_grad():
         layer.edge_scale.uniform_(0.5, 1.5)
-        layer.edge_mask[3, 5] = 0
+        layer.edge_mask[n_out // 2, n_in // 2] = 0
         layer.coef.normal_(0, 0.3)
-    x = torch.rand(301, 64, device=DEV) * 2.4 - 1.2
+    x = torch.rand(n_b, n_in, device=DEV) * 2.4 - 1.2
+    with torch.no_grad():
+        d = layer.edge_derivative(x, order)
+    n = layer_numpy(layer)
+    want = ko.edge_derivative(x.double().cpu().numpy(), n["coef"], n["base_weight"], n["spec"], n["params"], order,
+                              n["edge_scale"], n["edge_mask"])
+    close(d, want, FP32_TOL, "edge")
+
+
+@pytest.mark.parametrize("order", [0, 2])
+def test_edge_derivative_many_features_scalar_kernel(order):
+    """More than 16 features per input takes the one-thread-per-(b, i) kernel."""
+    torch.manual_seed(0)
+    layer = kb.KANLinear(33, 6, kb.BSpline(20, 3), device=DEV)
+    with torch.no_grad():
+        layer.coef.normal_(0, 0.3)
+    x = torch.rand(77, 33, device=DEV) * 1.8 - 0.9
     with torch.no_grad():
         d = layer.edge_derivative(x, order)
     n = layer_numpy(layer)
