@@ -58,24 +58,18 @@ __device__ __forceinline__ void load_knots_rt(const EdgeArgs& A, int i, float* t
   for (int r = 0; r < A.fa.nk; ++r) t[r] = extended_knot(g, A.fa.G, A.order, r);
 }
 
-// Row r of the paired feature registers (rows 2p and 2p+1 share the float2
-// feat[p][j]) from the thread's shared-memory column, for a run-time r: one
-// case per row keeps every register index static, so the caller's row loop
-// (and the basis code in it) is not unrolled.
-template <int NP, int NJ>
-__device__ __forceinline__ void copy_row(float2 (&feat)[NP][NJ], int r, const float* fs) {
-#pragma unroll
-  for (int rr = 0; rr < 2 * NP; ++rr)
-    if (rr == r) {
-#pragma unroll
-      for (int j = 0; j < NJ; ++j) {
-        if (rr % 2 == 0)
-          feat[rr / 2][j].x = fs[j * kEdgeThreads];
-        else
-          feat[rr / 2][j].y = fs[j * kEdgeThreads];
-      }
-    }
+// 4-byte asynchronous global -> shared copy (zero-filled when !valid).
+__device__ __forceinline__ void cp_async4(float* dst, const float* src, bool valid) {
+  const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+  const int n = valid ? 4 : 0;
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(d), "l"(src), "r"(n) : "memory");
 }
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
+
+// Rows whose features are staged in shared memory at once (the basis code is
+// inlined NB / CH times).
+__host__ __device__ constexpr int edge_chunk(int nb) { return nb % 4 == 0 ? 4 : 2; }
 
 // Rows per thread of the streaming kernel for NF features: an even number
 // that keeps NB x (NF + 1) feature registers near 170, so that the
@@ -87,21 +81,22 @@ __host__ __device__ constexpr int edge_rows(int nf) {
 // One lane per input; a warp covers il consecutive inputs (il = 32, or the
 // power of two covering I when I < 32) times 32 / il consecutive outputs, so
 // each of its stores is one contiguous 128-byte run of the (B, O, I) output.
-// A warp owns NB rows at a time: it evaluates their features (the silu term
-// as feature NF) once, passing them through the thread's own shared-memory
-// column so that the run-time basis code is inlined once, into registers
-// paired by rows; then it streams over the outputs o: NF + 1 coalesced
-// coefficient loads (the next output's issued before this one's arithmetic)
-// feed NB outputs, two rows per packed f32x2 FMA.  Warps take row groups
+// A warp owns NB rows at a time.  Their x values arrive in the thread's
+// shared-memory column by cp.async, issued while the previous group streams.
+// The features (the silu term as feature NF) are evaluated CH rows at a time
+// into shared memory and moved into registers paired by rows; then the warp
+// streams over the outputs o: NF + 1 coalesced coefficient loads feed NB
+// outputs, two rows per packed f32x2 FMA.  Warps take row groups
 // independently (persistent, no barrier after the knot table), so one warp's
 // feature prologue overlaps the others' stores.
-template <int NF, int NB, int MINB, bool PF>
-__global__ void __launch_bounds__(kEdgeThreads, MINB) edge_vec_kernel(const __grid_constant__ EdgeArgs A, int il_log2) {
-  static_assert(NB % 2 == 0, "rows are processed in pairs");
-  constexpr int NJ = NF + 1, NP = NB / 2;
+template <int NF, int NB>
+__global__ void __launch_bounds__(kEdgeThreads, 1) edge_vec_kernel(const __grid_constant__ EdgeArgs A, int il_log2) {
+  constexpr int NJ = NF + 1, NP = NB / 2, CH = edge_chunk(NB);
+  static_assert(NB % 2 == 0 && NB % CH == 0, "rows are processed in pairs and chunks");
   extern __shared__ float smem[];
-  float* Fs = smem;                          // [NJ][kEdgeThreads]: one row's features per thread
-  float* Ts = smem + NJ * kEdgeThreads;      // [il][KF_NK_MAX] (B-splines)
+  float* Fs = smem;                            // [CH][NJ][kEdgeThreads]: features of CH rows
+  float* Xs = Fs + CH * NJ * kEdgeThreads;     // [NB][kEdgeThreads]: x of the group's rows
+  float* Ts = Xs + NB * kEdgeThreads;          // [il][KF_NK_MAX] (B-splines)
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int il = 1 << il_log2, ol = 32 / il;
   const int i = blockIdx.y * il + (lane & (il - 1));
@@ -118,51 +113,57 @@ __global__ void __launch_bounds__(kEdgeThreads, MINB) edge_vec_kernel(const __gr
   if (i >= A.I) return;
   const float* ti = Ts + (i - i_base) * KF_NK_MAX;
   float* fs = Fs + threadIdx.x;
+  float* xs = Xs + threadIdx.x;
   const int64_t n_groups = (A.B + NB - 1) / NB;
+  const int64_t g_step = (int64_t)gridDim.x * (kEdgeThreads / 32);
   const size_t c_step = (size_t)ol * NF * A.I, o_step = (size_t)ol * A.I, row_step = (size_t)A.O * A.I;
-  for (int64_t grp = (int64_t)blockIdx.x * (kEdgeThreads / 32) + warp; grp < n_groups;
-       grp += (int64_t)gridDim.x * (kEdgeThreads / 32)) {
+  auto fetch_x = [&](int64_t grp) {
+#pragma unroll
+    for (int r = 0; r < NB; ++r) {
+      const int64_t b = grp * NB + r;
+      cp_async4(xs + r * kEdgeThreads, A.x + (b < A.B ? b : 0) * A.I + i, b < A.B);
+    }
+    cp_async_commit();
+  };
+  int64_t grp = (int64_t)blockIdx.x * (kEdgeThreads / 32) + warp;
+  if (grp < n_groups) fetch_x(grp);
+  for (; grp < n_groups; grp += g_step) {
     const int64_t b0 = grp * NB;
     const int nrows = (int)min((int64_t)NB, A.B - b0);
-    // Defined before the row loop: copy_row sets one row per trip, and an
-    // undefined start would let the compiler fold its selects away.
+    cp_async_wait();
     float2 feat[NP][NJ];
 #pragma unroll
-    for (int p = 0; p < NP; ++p)
-#pragma unroll
-      for (int j = 0; j < NJ; ++j) feat[p][j] = make_float2(0.0f, 0.0f);
+    for (int c = 0; c < NB / CH; ++c) {
 #pragma unroll 1
-    for (int r = 0; r < NB; ++r) {
-      const float x = r < nrows ? __ldg(A.x + (b0 + r) * A.I + i) : 0.0f;
-      edge_features_rt(A, i, x, ti, fs, kEdgeThreads);
-      fs[NF * kEdgeThreads] = A.base ? silu_deriv(x, A.m, A.poly, A.n_poly) : 0.0f;
-      copy_row<NP, NJ>(feat, r, fs);
+      for (int rr = 0; rr < CH; ++rr) {
+        const float x = xs[(c * CH + rr) * kEdgeThreads];
+        float* f = fs + rr * NJ * kEdgeThreads;
+        edge_features_rt(A, i, x, ti, f, kEdgeThreads);
+        f[NF * kEdgeThreads] = A.base ? silu_deriv(x, A.m, A.poly, A.n_poly) : 0.0f;
+      }
+#pragma unroll
+      for (int rr = 0; rr < CH; ++rr) {
+        const int r = c * CH + rr;
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) {
+          const float v = fs[(rr * NJ + j) * kEdgeThreads];
+          if (r % 2 == 0)
+            feat[r / 2][j].x = v;
+          else
+            feat[r / 2][j].y = v;
+        }
+      }
     }
+    if (grp + g_step < n_groups) fetch_x(grp + g_step);
 
     const float* cp = A.coef + (size_t)lo * NF * A.I + i;  // (O, NF, I)
     const float* bp = A.base ? A.base + (size_t)lo * A.I + i : nullptr;
     float* op = A.out + (b0 * A.O + lo) * A.I + i;
-    float qn[NJ];
-    if (PF && lo < A.O) {
-#pragma unroll
-      for (int j = 0; j < NF; ++j) qn[j] = __ldg(cp + (size_t)j * A.I);
-      qn[NF] = bp ? __ldg(bp) : 0.0f;
-    }
     for (int o = lo; o < A.O; o += ol) {
       float q[NJ];
-      if constexpr (PF) {
 #pragma unroll
-        for (int j = 0; j < NJ; ++j) q[j] = qn[j];
-        if (o + ol < A.O) {
-#pragma unroll
-          for (int j = 0; j < NF; ++j) qn[j] = __ldg(cp + c_step + (size_t)j * A.I);
-          qn[NF] = bp ? __ldg(bp + o_step) : 0.0f;
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < NF; ++j) q[j] = __ldg(cp + (size_t)j * A.I);
-        q[NF] = bp ? __ldg(bp) : 0.0f;
-      }
+      for (int j = 0; j < NF; ++j) q[j] = __ldg(cp + (size_t)j * A.I);
+      q[NF] = bp ? __ldg(bp) : 0.0f;
       float2 acc[NP];
       {
         const float2 qq = make_float2(q[NF], q[NF]);
@@ -185,6 +186,7 @@ __global__ void __launch_bounds__(kEdgeThreads, MINB) edge_vec_kernel(const __gr
       op += o_step;
     }
   }
+  cp_async_wait();
 }
 
 // Any I and nf <= KF_NF_MAX: one thread per (b, i), looping over o.
@@ -207,17 +209,19 @@ __global__ void __launch_bounds__(256) edge_scalar_kernel(EdgeArgs A) {
   }
 }
 
-template <int NF, int NB, int MINB, bool PF>
-int launch_vec_cfg(const EdgeArgs& A, cudaStream_t stream) {
+template <int NF>
+int launch_vec(const EdgeArgs& A, cudaStream_t stream) {
+  constexpr int NB = edge_rows(NF);
   int il_log2 = 5;
   while (il_log2 > 0 && (1 << (il_log2 - 1)) >= A.I) --il_log2;
-  const size_t smem = ((size_t)(NF + 1) * kEdgeThreads + (A.kind == KF_BASIS_BSPLINE ? (32 * KF_NK_MAX) : 0)) * sizeof(float);
+  const size_t smem = ((size_t)(edge_chunk(NB) * (NF + 1) + NB) * kEdgeThreads +
+                       (A.kind == KF_BASIS_BSPLINE ? (32 * KF_NK_MAX) : 0)) * sizeof(float);
   int dev = 0, n_sm = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
   // The coefficients are read through L1: keep the shared-memory carve-out small.
-  cudaError_t e = cudaFuncSetAttribute(edge_vec_kernel<NF, NB, MINB, PF>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = cudaFuncSetAttribute(edge_vec_kernel<NF, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(edge_vec_kernel<NF, NB, MINB, PF>, cudaFuncAttributePreferredSharedMemoryCarveout,
+    e = cudaFuncSetAttribute(edge_vec_kernel<NF, NB>, cudaFuncAttributePreferredSharedMemoryCarveout,
                              (int)cudaSharedmemCarveoutMaxL1);
   if (e != cudaSuccess) {
     set_error("kf_edge_derivative: shared memory attribute: %s", cudaGetErrorString(e));
@@ -226,15 +230,9 @@ int launch_vec_cfg(const EdgeArgs& A, cudaStream_t stream) {
   const unsigned gy = (unsigned)cdiv(A.I, 1 << il_log2);
   const int64_t n_groups = cdiv(A.B, (int64_t)NB);
   const int64_t gx_need = cdiv(n_groups, (int64_t)(kEdgeThreads / 32));
-  const int slots = n_sm * MINB;
-  const unsigned gx = (unsigned)std::max<int64_t>(1, std::min<int64_t>(gx_need, std::max(1, slots / (int)std::min<unsigned>(gy, slots))));
-  edge_vec_kernel<NF, NB, MINB, PF><<<dim3(gx, gy), kEdgeThreads, smem, stream>>>(A, il_log2);
+  const unsigned gx = (unsigned)std::max<int64_t>(1, std::min<int64_t>(gx_need, std::max(1, n_sm / (int)std::min<unsigned>(gy, n_sm))));
+  edge_vec_kernel<NF, NB><<<dim3(gx, gy), kEdgeThreads, smem, stream>>>(A, il_log2);
   return check_launch("kf_edge_derivative");
-}
-
-template <int NF>
-int launch_vec(const EdgeArgs& A, cudaStream_t stream) {
-  return launch_vec_cfg<NF, edge_rows(NF), 1, false>(A, stream);
 }
 
 int launch_edge(const EdgeArgs& A, bool vec, cudaStream_t stream) {
