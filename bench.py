@@ -36,9 +36,13 @@ ROOT = Path(__file__).resolve().parent
 METRIC = "KANLinear fwd+bwd tokens/s per GPU and % of tensor/HBM roofline, 1-8 B200"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
-# DRAM bytes per launch of the dominant kernel, from the ncu captures summarised
-# in profiles/ (scaled to the full launch by the units it processes).
-TRAFFIC_PER_LAUNCH: dict[tuple[int, str], float] = {}
+# DRAM bytes (read + write) per launch, from one-pass ncu captures of the full
+# bench workload, summarised in profiles/ with the commands that made them.
+TRAFFIC_PER_LAUNCH: dict[tuple[int, str], float] = {
+    (2, "kf_fwd"): 2852525568 + 160925440,
+    (2, "kf_wgrad"): 2303037696 + 452308992,
+    (2, "kf_dgrad"): 4568498688 + 132800768,
+}
 
 CONFIGS = {
     0: {"workload": "KAN([2,5,1]) BSpline(5,3) grid [-2,2], fp32, batch 1024, MSE fwd+bwd", "tokens": 1024},
@@ -371,7 +375,7 @@ def run_ours(args, world, rank, local):
     timer.active = False
     barrier()
     clocks = sampler.stop()
-    launches = (kb.kernels.LAUNCH_COUNT - launches0) // max(1, args.steps)
+    launches = kb.kernels.LAUNCH_COUNT - launches0  # library kernels launched in the timed region
     elapsed_ms = start.elapsed_time(end)
     if pg is not None:
         elapsed_ms = max_over_ranks(elapsed_ms, device, pg)
@@ -380,16 +384,35 @@ def run_ours(args, world, rank, local):
     kb.kernels.check_device_errors()
 
     # ---- end to end through the public API with host buffers ----
+    # Every step copies its input from pinned host memory and reads its result
+    # (loss, or one value of the derivative tensor) back.  The input of step
+    # k + 1 is copied on a side stream into the other of two device buffers
+    # while step k computes; all copies lie between the two timing events.
     x_host = x.detach().cpu().pin_memory()
     loss_host = torch.empty(1, dtype=torch.float32).pin_memory()
-    x_dev = x.detach().clone()
+    bufs = [x.detach().clone(), x.detach().clone()]
+    copy_stream = torch.cuda.Stream(device)
+    ready = [torch.cuda.Event(), torch.cuda.Event()]
+    free = [torch.cuda.Event(), torch.cuda.Event()]
 
-    def e2e_step():
-        x_dev.copy_(x_host, non_blocking=True)
+    def issue_copy(k):
+        slot = k % 2
+        with torch.cuda.stream(copy_stream):
+            copy_stream.wait_event(free[slot])
+            bufs[slot].copy_(x_host, non_blocking=True)
+            ready[slot].record(copy_stream)
+
+    def e2e_step(k, last):
+        slot = k % 2
+        torch.cuda.current_stream().wait_event(ready[slot])
+        if not last:
+            issue_copy(k + 1)
+        x_dev = bufs[slot]
         if cfg == 4:
             with torch.no_grad():
                 out = model.edge_derivative(x_dev, 2)
             loss_host.copy_(out[0, 0, :1], non_blocking=True)
+            free[slot].record()
             return
         x_dev.requires_grad_(True)
         for p in params:
@@ -401,15 +424,20 @@ def run_ours(args, world, rank, local):
             allreduce_gradients(params, group=pg)
         loss_host.copy_(loss.detach().float().reshape(1), non_blocking=True)
         x_dev.requires_grad_(False)
+        free[slot].record()
 
-    for _ in range(max(1, args.warmup)):
-        e2e_step()
+    def e2e_run(n_steps):
+        issue_copy(0)
+        for k in range(n_steps):
+            e2e_step(k, k == n_steps - 1)
+
+    e2e_run(max(1, args.warmup))
     torch.cuda.synchronize()
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(args.steps):
-        e2e_step()
+    copy_stream.wait_event(e0)
+    e2e_run(args.steps)
     e1.record()
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
@@ -447,6 +475,7 @@ def run_ours(args, world, rank, local):
         "roofline": roofline,
         "kernels": ksum,
         "gpu_launches": launches,
+        "gpu_launches_per_step": launches / max(1, args.steps),
         "clocks": clocks,
         "e2e": {"value": e2e_value, "unit": "tokens/s" if cfg != 4 else "points/s",
                 "h2d_bytes_per_step": x.numel() * x.element_size(), "d2h_bytes_per_step": 4},

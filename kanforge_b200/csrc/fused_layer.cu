@@ -62,6 +62,7 @@ struct BasisDev {
 struct Ctl {
   uint64_t full_a[kStages];
   uint64_t full_b[kStages];
+  uint64_t tab_full[kStages];   // CTA pairs: this CTA's knot tables of the stage landed
   uint64_t empty[kStages];
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
@@ -199,52 +200,67 @@ struct FwdParams {
   BasisDev bd;
 };
 
-constexpr int kFwdThreads = 768;  // w0 TMA, w1 MMA, w4-7 epilogue, w8-23 producers (4 groups)
+constexpr int kFwdThreads = 768;  // w0 TMA, w1 MMA (CTA 0), w4-7 epilogue, w8-23 producers (4 groups)
 constexpr int kFwdGroups = 4;     // producer group g owns the K-steps it with it % 4 == g (stage g)
+constexpr int kPairM = 2 * kBM;   // rows of a CTA-pair tile
+constexpr int kBHalf = (kBN / 2) * 128;  // 16 KB: the half of a B stage one CTA of the pair holds
 
+// The forward runs on CTA pairs: a tile is 256 tokens x 256 outputs, CTA r of
+// the pair evaluates the feature rows of tokens 128 r .. 128 r + 127 (its half
+// of A) and loads coefficient rows 128 r .. 128 r + 127 of the tile (its half
+// of B), and CTA 0 issues tcgen05.mma.cta_group::2 with M = 256; each CTA's
+// tensor memory holds its own 128 accumulator rows.  Per CTA and K-step the
+// shared memory moves 16 KB of features, 16 KB of coefficients and 32 KB of
+// MMA operand reads.  The stage barriers that the MMA waits on live in CTA 0:
+// CTA 1's producers arrive there remotely and its coefficient TMA completes
+// there; the MMA completions are multicast to both CTAs' barriers.
 template <int BK, int F>
 __global__ void __launch_bounds__(kFwdThreads, 1) fused_fwd_kernel(const __grid_constant__ CUtensorMap tmap_c, FwdParams p) {
   constexpr int IPK = kBK / F;  // inputs per K-step
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = align1024(smem_raw);
   uint8_t* sa = base;                                   // kStages x 16 KB
-  uint8_t* sb = sa + kStages * kATile;                  // kStages x 32 KB
-  Ctl* ctl = reinterpret_cast<Ctl*>(sb + kStages * kBTile);
+  uint8_t* sb = sa + kStages * kATile;                  // kStages x 16 KB (this CTA's half of B)
+  Ctl* ctl = reinterpret_cast<Ctl*>(sb + kStages * kBHalf);
   constexpr int kTabIn = (BK + 1) * kTabStride;          // floats of one input's knot table
   float* tabs = reinterpret_cast<float*>(align1024(reinterpret_cast<uint8_t*>(ctl + 1)));  // B-spline: [stage][IPK][kTabIn]
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = blockIdx.x / 2, n_pairs = gridDim.x / 2;
   volatile int* abort = &ctl->abort;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&ctl->full_a[s], 4);
-      mbar_init(&ctl->full_b[s], 1);
+      mbar_init(&ctl->full_a[s], 8);    // 4 producer warps of each CTA (used in CTA 0)
+      mbar_init(&ctl->full_b[s], 1);    // CTA 0's expect_tx for both halves (used in CTA 0)
+      mbar_init(&ctl->tab_full[s], 1);  // this CTA's knot tables
       mbar_init(&ctl->empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&ctl->acc_full[a], 1);
-      mbar_init(&ctl->acc_empty[a], 4);
+      mbar_init(&ctl->acc_empty[a], 8);  // 4 epilogue warps of each CTA (used in CTA 0)
     }
     mbar_init(&ctl->drain, 1);
     ctl->abort = 0;
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc(&ctl->tmem_base, 512);
-    tmem_relinquish();
+    tmem_alloc_pair(&ctl->tmem_base, 512);
+    tmem_relinquish_pair();
   }
   if (warp == 0 && lane == 0) prefetch_tmap(&tmap_c);
   tc_fence_before();
   __syncthreads();
+  cluster_sync();  // both CTAs' barriers exist before any remote arrive
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
   const int n_tiles = p.tiles.count();
 
   if (warp == 0) {
-    // ---------------- TMA producer: coefficient tiles ----------------
+    // ---------------- TMA producer: this CTA's half of the coefficient tile ----------------
     if (lane == 0) {
       int it = 0;
-      for (int t = blockIdx.x; t < n_tiles && !*abort; t += gridDim.x) {
+      for (int t = pair; t < n_tiles && !*abort; t += n_pairs) {
         int m, n;
         p.tiles.get(t, m, n);
         for (int k = 0; k < p.k_steps; ++k, ++it) {
@@ -252,66 +268,72 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fused_fwd_kernel(const __grid_
           const uint32_t ph = (it / kStages) & 1;
           if (!mbar_wait(&ctl->empty[s], ph ^ 1, abort)) break;
           if constexpr (BK > 0) {
-            // the knot tables of the step's inputs travel with the coefficient tile
+            // the knot tables of the step's inputs, into this CTA
             const int n_in = min(IPK, p.I - k * IPK);
             const uint32_t tb = (uint32_t)(n_in * kTabIn * sizeof(float));
-            mbar_arrive_expect_tx(&ctl->full_b[s], kBTile + tb);
-            bulk_load(tabs + s * IPK * kTabIn, p.bd.tab + (size_t)k * IPK * kTabIn, tb, &ctl->full_b[s]);
-          } else {
-            mbar_arrive_expect_tx(&ctl->full_b[s], kBTile);
+            mbar_arrive_expect_tx(&ctl->tab_full[s], tb);
+            bulk_load(tabs + s * IPK * kTabIn, p.bd.tab + (size_t)k * IPK * kTabIn, tb, &ctl->tab_full[s]);
           }
-          tma_load_2d(sb + s * kBTile, &tmap_c, &ctl->full_b[s], k * kBK, n * kBN);
+          const int c_row = n * kBN + (int)rank * (kBN / 2);
+          if (rank == 0) {
+            mbar_arrive_expect_tx(&ctl->full_b[s], 2 * kBHalf);  // both halves complete here
+            tma_load_2d(sb + s * kBHalf, &tmap_c, &ctl->full_b[s], k * kBK, c_row);
+          } else {
+            tma_load_2d_pair(sb + s * kBHalf, &tmap_c, &ctl->full_b[s], 0, k * kBK, c_row);
+          }
         }
       }
-      if (*abort) drain_tma(ctl, it);
+      // Abort: CTA 0 drains the coefficient loads of both CTAs (they complete
+      // on its barriers) before the pair's final cluster barrier.
+      if (*abort && rank == 0) drain_tma(ctl, it);
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
-      const uint32_t idesc = idesc_bf16_f32(kBM, kBN, false, false);
+    // ---------------- MMA issuer (CTA 0 of the pair) ----------------
+    if (rank == 0 && lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(kPairM, kBN, false, false);
       int it = 0, tc = 0;
-      for (int t = blockIdx.x; t < n_tiles && !*abort; t += gridDim.x, ++tc) {
+      for (int t = pair; t < n_tiles && !*abort; t += n_pairs, ++tc) {
         const int acc = tc & 1;
-        if (!mbar_wait(&ctl->acc_empty[acc], ((tc >> 1) & 1) ^ 1, abort)) break;
+        if (!mbar_wait_cluster(&ctl->acc_empty[acc], ((tc >> 1) & 1) ^ 1, abort)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem + acc * kBN;
         bool ok = true;
         for (int k = 0; k < p.k_steps; ++k, ++it) {
           const int s = it % kStages;
           const uint32_t ph = (it / kStages) & 1;
-          if (!mbar_wait(&ctl->full_a[s], ph, abort) || !mbar_wait(&ctl->full_b[s], ph, abort)) {
+          if (!mbar_wait_cluster(&ctl->full_a[s], ph, abort) || !mbar_wait_cluster(&ctl->full_b[s], ph, abort)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(sa + s * kATile), b0 = smem_u32(sb + s * kBTile);
+          const uint32_t a0 = smem_u32(sa + s * kATile), b0 = smem_u32(sb + s * kBHalf);
 #pragma unroll
           for (int j = 0; j < kBK / 16; ++j) {
-            mma_bf16(d_tmem, smem_desc_sw128(a0 + 32 * j, 16, 1024), smem_desc_sw128(b0 + 32 * j, 16, 1024), idesc,
-                     (k > 0 || j > 0) ? 1u : 0u);
+            mma_bf16_pair(d_tmem, smem_desc_sw128(a0 + 32 * j, 16, 1024), smem_desc_sw128(b0 + 32 * j, 16, 1024), idesc,
+                          (k > 0 || j > 0) ? 1u : 0u);
           }
-          mma_commit(&ctl->empty[s]);
+          mma_commit_pair(&ctl->empty[s], 0x3);
         }
         if (!ok) break;
-        mma_commit(&ctl->acc_full[acc]);
+        mma_commit_pair(&ctl->acc_full[acc], 0x3);
       }
-      if (*abort) {
-        mma_commit(&ctl->drain);
-        mbar_drain(&ctl->drain, 0);
-      }
+      // Every MMA of this CTA has completed (and every commit above has
+      // arrived) once the drain barrier flips: the pair may then exit.
+      mma_commit_pair(&ctl->drain, 0x1);
+      mbar_drain(&ctl->drain, 0);
     }
   } else if (warp >= 4 && warp < 8) {
     // ---------------- epilogue: TMEM -> +bias -> bf16 -> y ----------------
     const int q = warp - 4;
     const int row = q * 32 + lane;
     int tc = 0;
-    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++tc) {
+    for (int t = pair; t < n_tiles; t += n_pairs, ++tc) {
       int m, n;
       p.tiles.get(t, m, n);
       const int acc = tc & 1;
       if (!mbar_wait_warp(&ctl->acc_full[acc], (tc >> 1) & 1, abort)) break;
       tc_fence_after();
-      const int64_t b = (int64_t)m * kBM + row;
+      const int64_t b = (int64_t)m * kPairM + (int64_t)rank * kBM + row;
       const int o_base = n * kBN;
 #pragma unroll 1
       for (int c = 0; c < kBN / 32; ++c) {
@@ -320,7 +342,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fused_fwd_kernel(const __grid_
         if (c == kBN / 32 - 1) {
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&ctl->acc_empty[acc]);
+          if (lane == 0) mbar_arrive_cluster(&ctl->acc_empty[acc], 0);
         }
         const int o0 = o_base + c * 32;
         if (b < p.B && o0 < p.O) {
@@ -355,10 +377,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fused_fwd_kernel(const __grid_
     const int row = ((warp - 8) % 4) * 32 + lane;
     int it = 0;
     bool alive = true;
-    for (int t = blockIdx.x; t < n_tiles && alive; t += gridDim.x) {  // abort is seen (warp-uniformly) by the waits
+    for (int t = pair; t < n_tiles && alive; t += n_pairs) {  // abort is seen (warp-uniformly) by the waits
       int m, n;
       p.tiles.get(t, m, n);
-      const int64_t b = (int64_t)m * kBM + row;
+      const int64_t b = (int64_t)m * kPairM + (int64_t)rank * kBM + row;
       const bool row_ok = b < p.B;
       const unsigned short* xrow = reinterpret_cast<const unsigned short*>(p.x) + (row_ok ? b : 0) * p.I;
       int k = ((grp - it) % kFwdGroups + kFwdGroups) % kFwdGroups;
@@ -374,7 +396,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fused_fwd_kernel(const __grid_
 #pragma unroll
         for (int u = 0; u < IPK; ++u) xb[u] = (row_ok && k + kFwdGroups < p.k_steps && inext + u < p.I) ? __ldg(xrow + inext + u) : 0;
         bool ok = mbar_wait_warp(&ctl->empty[s], ph ^ 1, abort);
-        if constexpr (BK > 0) ok = ok && mbar_wait_warp(&ctl->full_b[s], ph, abort);  // tables landed
+        if constexpr (BK > 0) ok = ok && mbar_wait_warp(&ctl->tab_full[s], ph, abort);  // tables landed
         if (!ok) {
           alive = false;
           break;
@@ -432,7 +454,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fused_fwd_kernel(const __grid_
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&ctl->full_a[s]);
+        if (lane == 0) {
+          if (rank == 0)
+            mbar_arrive(&ctl->full_a[s]);
+          else
+            mbar_arrive_peer(&ctl->full_a[s], 0);
+        }
 #pragma unroll
         for (int u = 0; u < IPK; ++u) xa[u] = xb[u];
       }
@@ -442,9 +469,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fused_fwd_kernel(const __grid_
 
   tc_fence_before();
   __syncthreads();
+  cluster_sync();  // no remote arrive or MMA of the pair is outstanding past this point
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc_pair(tmem, 512);
   }
 }
 
@@ -1050,6 +1078,24 @@ int dispatch_fused(const kf_basis_desc* d, int f_pad, Fn&& fn) {
 
 constexpr size_t kMainSmem = 1024 + kStages * (kATile + kBTile) + sizeof(Ctl);
 
+constexpr size_t kFwdSmem = 1024 + kStages * (kATile + kBHalf) + sizeof(Ctl);
+
+// Largest number of co-resident CTA pairs for a cluster launch of `kern`
+// (clusters of 2), cached per device in the caller's `cache`.
+template <typename K>
+int max_pairs(K kern, const cudaLaunchConfig_t& cfg, int (&cache)[64]) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && cache[dev] > 0) return cache[dev];
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    n = sm_count() / 2;
+  }
+  if (dev >= 0 && dev < 64) cache[dev] = n;
+  return n;
+}
+
 struct FwdLaunch {
   const CUtensorMap* tmap;
   FwdParams p;
@@ -1057,11 +1103,25 @@ struct FwdLaunch {
   template <int BK, int F>
   int go() const {
     constexpr int IPK = kBK / F;
-    const size_t smem = kMainSmem + (BK > 0 ? 1024 + sizeof(float) * kStages * IPK * (BK + 1) * kTabStride : 0);
+    const size_t smem = kFwdSmem + (BK > 0 ? 1024 + sizeof(float) * kStages * IPK * (BK + 1) * kTabStride : 0);
     auto kern = fused_fwd_kernel<BK, F>;
     KF_CUDA_RET(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    const int grid = (int)std::min<int64_t>(p.tiles.m_tiles * (int64_t)p.tiles.n_tiles, sm_count());
-    kern<<<grid, kFwdThreads, smem, stream>>>(*tmap, p);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(kFwdThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cfg.gridDim = dim3(2 * (unsigned)(sm_count() / 2));
+    static int pair_cache[64] = {0};  // per instantiation
+    const int pairs = (int)std::min<int64_t>(p.tiles.m_tiles * (int64_t)p.tiles.n_tiles, max_pairs(kern, cfg, pair_cache));
+    cfg.gridDim = dim3(2 * (unsigned)pairs);
+    KF_CUDA_RET(cudaLaunchKernelEx(&cfg, kern, *tmap, p));
     return check_launch("kf_fwd");
   }
 };
@@ -1125,11 +1185,11 @@ extern "C" int kf_fwd(const void* x, const void* packed, const void* bias, const
   p.O = O;
   const int ipk = kBK / f_pad;
   p.k_steps = (int)cdiv(I, ipk);
-  p.tiles.m_tiles = (int)cdiv(B, kBM);
+  p.tiles.m_tiles = (int)cdiv(B, kPairM);
   p.tiles.n_tiles = (int)cdiv(O, kBN);
-  p.tiles.gm = p.tiles.m_tiles;  // M fastest: concurrent CTAs share one coefficient column block
+  p.tiles.gm = p.tiles.m_tiles;  // M fastest: concurrent pairs share one coefficient column block
   CUtensorMap tmap;
-  if (int rc = make_tmap_bf16(&tmap, packed, O, (int64_t)I * f_pad, kBK, kBN)) return rc;
+  if (int rc = make_tmap_bf16(&tmap, packed, O, (int64_t)I * f_pad, kBK, kBN / 2)) return rc;
   FwdLaunch L{&tmap, p, (cudaStream_t)stream};
   return dispatch_fused(basis, f_pad, L);
 }

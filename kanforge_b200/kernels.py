@@ -38,9 +38,13 @@ def set_launch_observer(fn) -> None:
     _observer = fn
 
 
+# Entry points that launch more than one kernel (partial sums + their reduction).
+_KERNELS_PER_CALL = {"kf_rational_bwd": 2, "kf_rational_bwd_noalloc": 2}
+
+
 def _launch(name: str, *args) -> None:
     global LAUNCH_COUNT
-    LAUNCH_COUNT += 1
+    LAUNCH_COUNT += _KERNELS_PER_CALL.get(name, 1)
     if _observer is None:
         _lib.call(name, *args)
         return
