@@ -726,9 +726,15 @@ struct WgradParams {
   BasisDev bd;
 };
 
-constexpr int kWgradThreads = 768;  // w0 TMA, w1 MMA, w4-7 epilogue, w8-23 producers (2 groups)
+constexpr int kWgradThreads = 768;  // w0 TMA, w1 MMA (CTA 0), w4-7 epilogue, w8-23 producers (2 groups)
 constexpr int kXTile = kBK * 8 * 2;  // x tile per stage: 64 rows x 8 inputs bf16 = 1 KB
 
+// The coefficient gradient runs on CTA pairs like the forward: a tile is 256
+// feature rows (CTA r evaluates the features of inputs IPT r .. IPT r + IPT - 1
+// of the pair's 2 IPT) x 256 outputs (CTA r loads dy columns 128 r .. 128 r +
+// 127 of the tile), CTA 0 issues tcgen05.mma.cta_group::2 with M = 256, and
+// each CTA's epilogue folds its own 128 accumulator rows.  The x tile a CTA's
+// producers read completes on that CTA's own barrier (tab_full).
 template <int BK, int F>
 __global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __grid_constant__ CUtensorMap tmap_dy,
                                                                        const __grid_constant__ CUtensorMap tmap_x, WgradParams p) {
@@ -736,31 +742,34 @@ __global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __g
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = align1024(smem_raw);
   uint8_t* sa = base;
-  uint8_t* sb = sa + kStages * kATile;
-  Ctl* ctl = reinterpret_cast<Ctl*>(sb + kStages * kBTile);
+  uint8_t* sb = sa + kStages * kATile;                           // kStages x 16 KB (this CTA's half of dy)
+  Ctl* ctl = reinterpret_cast<Ctl*>(sb + kStages * kBHalf);
   uint8_t* sx = align1024(reinterpret_cast<uint8_t*>(ctl + 1));  // x tiles [stage][64 rows][8 inputs]
   float* stg = reinterpret_cast<float*>(sx + kStages * kXTile);  // epilogue staging [128][33]
   float* tabs = stg + 128 * 33;                                   // B-spline: per producer warp [(BK+1) * ts]
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = blockIdx.x / 2, n_pairs = gridDim.x / 2;
   volatile int* abort = &ctl->abort;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&ctl->full_a[s], 8);  // the 8 warps of the producer group that owns the step
-      mbar_init(&ctl->full_b[s], 1);
+      mbar_init(&ctl->full_a[s], 16);   // the 8 warps of the owning producer group, in each CTA (used in CTA 0)
+      mbar_init(&ctl->full_b[s], 1);    // CTA 0's expect_tx for both dy halves (used in CTA 0)
+      mbar_init(&ctl->tab_full[s], 1);  // this CTA's x tile
       mbar_init(&ctl->empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&ctl->acc_full[a], 1);
-      mbar_init(&ctl->acc_empty[a], 4);
+      mbar_init(&ctl->acc_empty[a], 8);  // 4 epilogue warps of each CTA (used in CTA 0)
     }
     mbar_init(&ctl->drain, 1);
     ctl->abort = 0;
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc(&ctl->tmem_base, 512);
-    tmem_relinquish();
+    tmem_alloc_pair(&ctl->tmem_base, 512);
+    tmem_relinquish_pair();
   }
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmap_dy);
@@ -768,6 +777,7 @@ __global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __g
   }
   tc_fence_before();
   __syncthreads();
+  cluster_sync();  // both CTAs' barriers exist before any remote arrive
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
   const int n_tiles = p.tiles.count();
@@ -775,66 +785,86 @@ __global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __g
   if (warp == 0) {
     if (lane == 0) {
       int it = 0;
-      for (int t = blockIdx.x; t < n_tiles && !*abort; t += gridDim.x) {
+      for (int t = pair; t < n_tiles && !*abort; t += n_pairs) {
         int m, n;
         p.tiles.get(t, m, n);
-        const int x0 = (m * IPT) & ~7;  // TMA x coordinate rounded down to 16 bytes
+        const int x0 = ((m * 2 + (int)rank) * IPT) & ~7;  // TMA x coordinate rounded down to 16 bytes
+        const int o0 = n * kBN + (int)rank * (kBN / 2);
         for (int k = 0; k < p.k_steps; ++k, ++it) {
           const int s = it % kStages;
           const uint32_t ph = (it / kStages) & 1;
           if (!mbar_wait(&ctl->empty[s], ph ^ 1, abort)) break;
-          mbar_arrive_expect_tx(&ctl->full_b[s], kBTile + (p.x_tma ? kXTile : 0));
+          if (p.x_tma) {
+            mbar_arrive_expect_tx(&ctl->tab_full[s], kXTile);
+            tma_load_2d(sx + s * kXTile, &tmap_x, &ctl->tab_full[s], x0, k * kBK);
+          }
+          if (rank == 0) {
+            mbar_arrive_expect_tx(&ctl->full_b[s], 2 * kBHalf);  // both dy halves complete here
 #pragma unroll
-          for (int c = 0; c < kBN / 64; ++c)
-            tma_load_2d(sb + s * kBTile + c * 8192, &tmap_dy, &ctl->full_b[s], n * kBN + c * 64, k * kBK);
-          if (p.x_tma) tma_load_2d(sx + s * kXTile, &tmap_x, &ctl->full_b[s], x0, k * kBK);
+            for (int c = 0; c < kBN / 128; ++c)
+              tma_load_2d(sb + s * kBHalf + c * 8192, &tmap_dy, &ctl->full_b[s], o0 + c * 64, k * kBK);
+          } else {
+#pragma unroll
+            for (int c = 0; c < kBN / 128; ++c)
+              tma_load_2d_pair(sb + s * kBHalf + c * 8192, &tmap_dy, &ctl->full_b[s], 0, o0 + c * 64, k * kBK);
+          }
         }
       }
-      if (*abort) drain_tma(ctl, it);
+      // Abort: CTA 0 drains the dy loads of both CTAs (they complete on its
+      // barriers); each CTA drains its own x tiles.
+      if (*abort) {
+        if (rank == 0) drain_tma(ctl, it);
+        if (p.x_tma) {
+          for (int s = 0; s < kStages; ++s) {
+            const int last = it - 1 - ((it - 1 - s) % kStages + kStages) % kStages;
+            if (it > 0 && last >= 0) mbar_drain(&ctl->tab_full[s], (last / kStages) & 1);
+          }
+        }
+      }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      const uint32_t idesc = idesc_bf16_f32(kBM, kBN, false, true);
+    if (rank == 0 && lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(kPairM, kBN, false, true);
       int it = 0, tc = 0;
-      for (int t = blockIdx.x; t < n_tiles && !*abort; t += gridDim.x, ++tc) {
+      for (int t = pair; t < n_tiles && !*abort; t += n_pairs, ++tc) {
         const int acc = tc & 1;
-        if (!mbar_wait(&ctl->acc_empty[acc], ((tc >> 1) & 1) ^ 1, abort)) break;
+        if (!mbar_wait_cluster(&ctl->acc_empty[acc], ((tc >> 1) & 1) ^ 1, abort)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem + acc * kBN;
         bool ok = true;
         for (int k = 0; k < p.k_steps; ++k, ++it) {
           const int s = it % kStages;
           const uint32_t ph = (it / kStages) & 1;
-          if (!mbar_wait(&ctl->full_a[s], ph, abort) || !mbar_wait(&ctl->full_b[s], ph, abort)) {
+          if (!mbar_wait_cluster(&ctl->full_a[s], ph, abort) || !mbar_wait_cluster(&ctl->full_b[s], ph, abort)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(sa + s * kATile), b0 = smem_u32(sb + s * kBTile);
+          const uint32_t a0 = smem_u32(sa + s * kATile), b0 = smem_u32(sb + s * kBHalf);
 #pragma unroll
           for (int j = 0; j < kBK / 16; ++j) {
-            mma_bf16(d_tmem, smem_desc_sw128(a0 + 32 * j, 16, 1024), smem_desc_sw128(b0 + 2048 * j, 8192, 1024), idesc,
-                     (k > 0 || j > 0) ? 1u : 0u);
+            mma_bf16_pair(d_tmem, smem_desc_sw128(a0 + 32 * j, 16, 1024), smem_desc_sw128(b0 + 2048 * j, 8192, 1024), idesc,
+                          (k > 0 || j > 0) ? 1u : 0u);
           }
-          mma_commit(&ctl->empty[s]);
+          mma_commit_pair(&ctl->empty[s], 0x3);
         }
         if (!ok) break;
-        mma_commit(&ctl->acc_full[acc]);
+        mma_commit_pair(&ctl->acc_full[acc], 0x3);
       }
-      if (*abort) {
-        mma_commit(&ctl->drain);
-        mbar_drain(&ctl->drain, 0);
-      }
+      // Every MMA of the pair has completed (and every commit above has
+      // arrived) once the drain barrier flips: the pair may then exit.
+      mma_commit_pair(&ctl->drain, 0x1);
+      mbar_drain(&ctl->drain, 0);
     }
   } else if (warp >= 4 && warp < 8) {
     const int q = warp - 4;
     const int mrow = q * 32 + lane;  // feature row (il, f) of this thread
     const int etid = mrow;
     int tc = 0;
-    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++tc) {
+    for (int t = pair; t < n_tiles; t += n_pairs, ++tc) {
       int m, n;
       p.tiles.get(t, m, n);
-      const int i_base = m * IPT;
+      const int i_base = (m * 2 + (int)rank) * IPT;
       const int acc = tc & 1;
       bool ok = mbar_wait_warp(&ctl->acc_full[acc], (tc >> 1) & 1, abort);
       if (!named_bar_and(1, 128, ok)) break;  // the four epilogue warps leave together
@@ -846,7 +876,7 @@ __global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __g
         if (c == kBN / 32 - 1) {
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&ctl->acc_empty[acc]);
+          if (lane == 0) mbar_arrive_cluster(&ctl->acc_empty[acc], 0);
         }
         named_bar(1, 128);  // staging free
 #pragma unroll
@@ -895,10 +925,10 @@ __global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __g
     float* tab = tabs + (warp - 8) * ((BK + 1) * ts);
     int it = 0;
     bool alive = true;
-    for (int t = blockIdx.x; t < n_tiles && alive; t += gridDim.x) {  // abort is seen (warp-uniformly) by the waits
+    for (int t = pair; t < n_tiles && alive; t += n_pairs) {  // abort is seen (warp-uniformly) by the waits
       int m, n;
       p.tiles.get(t, m, n);
-      const int i_base = m * IPT;
+      const int i_base = (m * 2 + (int)rank) * IPT;
       const int i = i_base + u;
       const int xoff = i_base - (i_base & ~7) + u;  // column of input i inside the TMA x tile
       if constexpr (BK > 0) {
@@ -923,7 +953,7 @@ __global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __g
           }
         }
         bool ok = mbar_wait_warp(&ctl->empty[s], ph ^ 1, abort);
-        if (p.x_tma) ok = ok && mbar_wait_warp(&ctl->full_b[s], ph, abort);  // x tile landed
+        if (p.x_tma) ok = ok && mbar_wait_warp(&ctl->tab_full[s], ph, abort);  // x tile landed
         if (!ok) {
           alive = false;
           break;
@@ -974,7 +1004,12 @@ __global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __g
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&ctl->full_a[s]);
+        if (lane == 0) {
+          if (rank == 0)
+            mbar_arrive(&ctl->full_a[s]);
+          else
+            mbar_arrive_peer(&ctl->full_a[s], 0);
+        }
       }
       it += p.k_steps;
     }
@@ -982,9 +1017,10 @@ __global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __g
 
   tc_fence_before();
   __syncthreads();
+  cluster_sync();  // no remote arrive or MMA of the pair is outstanding past this point
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc_pair(tmem, 512);
   }
 }
 
@@ -1148,15 +1184,29 @@ struct WgradLaunch {
   cudaStream_t stream;
   template <int BK, int F>
   int go() const {
-    const size_t smem = kMainSmem + 1024 + kStages * kXTile + sizeof(float) * (128 * 33 + (BK > 0 ? 16 * (BK + 1) * p.tab_stride : 0));
+    const size_t smem = kFwdSmem + 1024 + kStages * kXTile + sizeof(float) * (128 * 33 + (BK > 0 ? 16 * (BK + 1) * p.tab_stride : 0));
     if (smem > 232448) {
       set_error("kf_wgrad: B-spline order %d with %d knots needs %zu bytes of shared memory", BK, p.bd.nk, smem);
       return KF_ERR_UNSUPPORTED;
     }
     auto kern = fused_wgrad_kernel<BK, F>;
     KF_CUDA_RET(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    const int grid = (int)std::min<int64_t>(p.tiles.m_tiles * (int64_t)p.tiles.n_tiles, sm_count());
-    kern<<<grid, kWgradThreads, smem, stream>>>(*tmap_dy, *tmap_x, p);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(kWgradThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cfg.gridDim = dim3(2 * (unsigned)(sm_count() / 2));
+    static int pair_cache[64] = {0};  // per instantiation
+    const int pairs = (int)std::min<int64_t>(p.tiles.m_tiles * (int64_t)p.tiles.n_tiles, max_pairs(kern, cfg, pair_cache));
+    cfg.gridDim = dim3(2 * (unsigned)pairs);
+    KF_CUDA_RET(cudaLaunchKernelEx(&cfg, kern, *tmap_dy, *tmap_x, p));
     return check_launch("kf_wgrad");
   }
 };
@@ -1257,10 +1307,10 @@ extern "C" int kf_wgrad(const void* x, const void* dy, const float* knot_tab, co
   p.O = O;
   p.K = K;
   p.k_steps = (int)cdiv(B, kBK);
-  const int ipt = kBM / f_pad;
-  p.tiles.m_tiles = (int)cdiv(I, ipt);
+  const int ipt = kBM / f_pad;  // inputs per CTA of a pair tile
+  p.tiles.m_tiles = (int)cdiv(I, 2 * ipt);
   p.tiles.n_tiles = (int)cdiv(O, kBN);
-  p.tiles.gm = p.tiles.m_tiles;  // M fastest: concurrent CTAs share the dy column block
+  p.tiles.gm = p.tiles.m_tiles;  // M fastest: concurrent pairs share the dy column block
   CUtensorMap tdy, tx;
   if (int rc = make_tmap_bf16(&tdy, dy, B, O, 64, kBK)) return rc;
   p.x_tma = (I % 8 == 0) && ((uintptr_t)x % 16 == 0);
