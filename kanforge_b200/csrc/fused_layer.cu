@@ -196,6 +196,7 @@ struct FwdParams {
   int64_t B;
   int I, O;
   int k_steps;
+  int nblk;  // 256-output accumulator blocks per tile: kFwdNB, or 1 when O <= 256
   TileMap tiles;
   BasisDev bd;
 };
@@ -204,14 +205,17 @@ constexpr int kFwdThreads = 768;  // w0 TMA, w1 MMA (CTA 0), w4-7 epilogue, w8-2
 constexpr int kFwdGroups = 4;     // producer group g owns the K-steps it with it % 4 == g (stage g)
 constexpr int kPairM = 2 * kBM;   // rows of a CTA-pair tile
 constexpr int kBHalf = (kBN / 2) * 128;  // 16 KB: the half of a B stage one CTA of the pair holds
+constexpr int kFwdNB = 2;                 // forward: 256-column accumulator blocks per tile (all of TMEM)
 
-// The forward runs on CTA pairs: a tile is 256 tokens x 256 outputs, CTA r of
+// The forward runs on CTA pairs: a tile is 256 tokens x 512 outputs, CTA r of
 // the pair evaluates the feature rows of tokens 128 r .. 128 r + 127 (its half
-// of A) and loads coefficient rows 128 r .. 128 r + 127 of the tile (its half
-// of B), and CTA 0 issues tcgen05.mma.cta_group::2 with M = 256; each CTA's
-// tensor memory holds its own 128 accumulator rows.  Per CTA and K-step the
-// shared memory moves 16 KB of features, 16 KB of coefficients and 32 KB of
-// MMA operand reads.  The stage barriers that the MMA waits on live in CTA 0:
+// of A) and loads coefficient rows 128 r .. 128 r + 127 of each 256-output
+// block of the tile (its half of B), and CTA 0 issues
+// tcgen05.mma.cta_group::2 with M = 256 into two 256-column accumulators that
+// fill the tensor memory; each CTA's tensor memory holds its own 128 rows.
+// One feature stage thus feeds 512 outputs, halving the feature evaluation per
+// MMA, at the price of an epilogue that is not overlapped (about 1% of a
+// tile's K loop at 4096 inputs).  The stage barriers that the MMA waits on live in CTA 0:
 // CTA 1's producers arrive there remotely and its coefficient TMA completes
 // there; the MMA completions are multicast to both CTAs' barriers.
 template <int BK, int F>
@@ -220,8 +224,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fused_fwd_kernel(const __grid_
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = align1024(smem_raw);
   uint8_t* sa = base;                                   // kStages x 16 KB
-  uint8_t* sb = sa + kStages * kATile;                  // kStages x 16 KB (this CTA's half of B)
-  Ctl* ctl = reinterpret_cast<Ctl*>(sb + kStages * kBHalf);
+  uint8_t* sb = sa + kStages * kATile;                  // kStages x kFwdNB x 16 KB (this CTA's halves of B)
+  Ctl* ctl = reinterpret_cast<Ctl*>(sb + kStages * kFwdNB * kBHalf);
   constexpr int kTabIn = (BK + 1) * kTabStride;          // floats of one input's knot table
   float* tabs = reinterpret_cast<float*>(align1024(reinterpret_cast<uint8_t*>(ctl + 1)));  // B-spline: [stage][IPK][kTabIn]
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -274,12 +278,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fused_fwd_kernel(const __grid_
             mbar_arrive_expect_tx(&ctl->tab_full[s], tb);
             bulk_load(tabs + s * IPK * kTabIn, p.bd.tab + (size_t)k * IPK * kTabIn, tb, &ctl->tab_full[s]);
           }
-          const int c_row = n * kBN + (int)rank * (kBN / 2);
-          if (rank == 0) {
-            mbar_arrive_expect_tx(&ctl->full_b[s], 2 * kBHalf);  // both halves complete here
-            tma_load_2d(sb + s * kBHalf, &tmap_c, &ctl->full_b[s], k * kBK, c_row);
-          } else {
-            tma_load_2d_pair(sb + s * kBHalf, &tmap_c, &ctl->full_b[s], 0, k * kBK, c_row);
+          uint8_t* sbs = sb + s * (kFwdNB * kBHalf);
+          if (rank == 0) mbar_arrive_expect_tx(&ctl->full_b[s], 2 * p.nblk * kBHalf);  // both CTAs' halves complete here
+          for (int nb = 0; nb < p.nblk; ++nb) {
+            const int c_row = (n * p.nblk + nb) * kBN + (int)rank * (kBN / 2);
+            if (rank == 0)
+              tma_load_2d(sbs + nb * kBHalf, &tmap_c, &ctl->full_b[s], k * kBK, c_row);
+            else
+              tma_load_2d_pair(sbs + nb * kBHalf, &tmap_c, &ctl->full_b[s], 0, k * kBK, c_row);
           }
         }
       }
@@ -293,10 +299,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fused_fwd_kernel(const __grid_
       const uint32_t idesc = idesc_bf16_f32(kPairM, kBN, false, false);
       int it = 0, tc = 0;
       for (int t = pair; t < n_tiles && !*abort; t += n_pairs, ++tc) {
-        const int acc = tc & 1;
-        if (!mbar_wait_cluster(&ctl->acc_empty[acc], ((tc >> 1) & 1) ^ 1, abort)) break;
+        if (!mbar_wait_cluster(&ctl->acc_empty[0], (tc & 1) ^ 1, abort)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem + acc * kBN;
         bool ok = true;
         for (int k = 0; k < p.k_steps; ++k, ++it) {
           const int s = it % kStages;
@@ -306,16 +310,18 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fused_fwd_kernel(const __grid_
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(sa + s * kATile), b0 = smem_u32(sb + s * kBHalf);
+          const uint32_t a0 = smem_u32(sa + s * kATile), b0 = smem_u32(sb + s * (kFwdNB * kBHalf));
 #pragma unroll
           for (int j = 0; j < kBK / 16; ++j) {
-            mma_bf16_pair(d_tmem, smem_desc_sw128(a0 + 32 * j, 16, 1024), smem_desc_sw128(b0 + 32 * j, 16, 1024), idesc,
-                          (k > 0 || j > 0) ? 1u : 0u);
+            const uint64_t adesc = smem_desc_sw128(a0 + 32 * j, 16, 1024);
+            for (int nb = 0; nb < p.nblk; ++nb)
+              mma_bf16_pair(tmem + nb * kBN, adesc, smem_desc_sw128(b0 + nb * kBHalf + 32 * j, 16, 1024), idesc,
+                            (k > 0 || j > 0) ? 1u : 0u);
           }
           mma_commit_pair(&ctl->empty[s], 0x3);
         }
         if (!ok) break;
-        mma_commit_pair(&ctl->acc_full[acc], 0x3);
+        mma_commit_pair(&ctl->acc_full[0], 0x3);
       }
       // Every MMA of this CTA has completed (and every commit above has
       // arrived) once the drain barrier flips: the pair may then exit.
@@ -330,19 +336,19 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fused_fwd_kernel(const __grid_
     for (int t = pair; t < n_tiles; t += n_pairs, ++tc) {
       int m, n;
       p.tiles.get(t, m, n);
-      const int acc = tc & 1;
-      if (!mbar_wait_warp(&ctl->acc_full[acc], (tc >> 1) & 1, abort)) break;
+      if (!mbar_wait_warp(&ctl->acc_full[0], tc & 1, abort)) break;
       tc_fence_after();
       const int64_t b = (int64_t)m * kPairM + (int64_t)rank * kBM + row;
-      const int o_base = n * kBN;
+      const int o_base = n * (p.nblk * kBN);
+      const int n_chunks = p.nblk * kBN / 32;
 #pragma unroll 1
-      for (int c = 0; c < kBN / 32; ++c) {
+      for (int c = 0; c < n_chunks; ++c) {
         float v[32];
-        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + acc * kBN + c * 32, v);
-        if (c == kBN / 32 - 1) {
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + c * 32, v);
+        if (c == n_chunks - 1) {
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(&ctl->acc_empty[acc], 0);
+          if (lane == 0) mbar_arrive_cluster(&ctl->acc_empty[0], 0);
         }
         const int o0 = o_base + c * 32;
         if (b < p.B && o0 < p.O) {
@@ -1114,7 +1120,8 @@ int dispatch_fused(const kf_basis_desc* d, int f_pad, Fn&& fn) {
 
 constexpr size_t kMainSmem = 1024 + kStages * (kATile + kBTile) + sizeof(Ctl);
 
-constexpr size_t kFwdSmem = 1024 + kStages * (kATile + kBHalf) + sizeof(Ctl);
+constexpr size_t kFwdSmem = 1024 + kStages * (kATile + kFwdNB * kBHalf) + sizeof(Ctl);
+constexpr size_t kPairSmem = 1024 + kStages * (kATile + kBHalf) + sizeof(Ctl);
 
 // Largest number of co-resident CTA pairs for a cluster launch of `kern`
 // (clusters of 2), cached per device in the caller's `cache`.
@@ -1184,7 +1191,7 @@ struct WgradLaunch {
   cudaStream_t stream;
   template <int BK, int F>
   int go() const {
-    const size_t smem = kFwdSmem + 1024 + kStages * kXTile + sizeof(float) * (128 * 33 + (BK > 0 ? 16 * (BK + 1) * p.tab_stride : 0));
+    const size_t smem = kPairSmem + 1024 + kStages * kXTile + sizeof(float) * (128 * 33 + (BK > 0 ? 16 * (BK + 1) * p.tab_stride : 0));
     if (smem > 232448) {
       set_error("kf_wgrad: B-spline order %d with %d knots needs %zu bytes of shared memory", BK, p.bd.nk, smem);
       return KF_ERR_UNSUPPORTED;
@@ -1236,7 +1243,8 @@ extern "C" int kf_fwd(const void* x, const void* packed, const void* bias, const
   const int ipk = kBK / f_pad;
   p.k_steps = (int)cdiv(I, ipk);
   p.tiles.m_tiles = (int)cdiv(B, kPairM);
-  p.tiles.n_tiles = (int)cdiv(O, kBN);
+  p.nblk = O > kBN ? kFwdNB : 1;
+  p.tiles.n_tiles = (int)cdiv(O, p.nblk * kBN);
   p.tiles.gm = p.tiles.m_tiles;  // M fastest: concurrent pairs share one coefficient column block
   CUtensorMap tmap;
   if (int rc = make_tmap_bf16(&tmap, packed, O, (int64_t)I * f_pad, kBK, kBN / 2)) return rc;
