@@ -753,6 +753,8 @@ __global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __g
   uint8_t* sx = align1024(reinterpret_cast<uint8_t*>(ctl + 1));  // x tiles [stage][64 rows][8 inputs]
   float* stg = reinterpret_cast<float*>(sx + kStages * kXTile);  // epilogue staging [128][33]
   float* tabs = stg + 128 * 33;                                   // B-spline: per producer warp [(BK+1) * ts]
+  float* sfold = tabs + (BK > 0 ? 16 * (BK + 1) * p.tab_stride : 0);  // fold matrix [K][F], zero past nt
+  __nv_bfloat16* sout = reinterpret_cast<__nv_bfloat16*>(sfold + 32 * 32);  // dcoef of a chunk [32][IPT * K]
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const uint32_t rank = cluster_ctarank();
   const int pair = blockIdx.x / 2, n_pairs = gridDim.x / 2;
@@ -866,11 +868,18 @@ __global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __g
     const int q = warp - 4;
     const int mrow = q * 32 + lane;  // feature row (il, f) of this thread
     const int etid = mrow;
+    const int K = p.K;
+    for (int e = etid; e < K * F; e += 128) {
+      const int kk = e / F, j = e % F;
+      sfold[e] = (p.fold != nullptr && j < p.bd.nt) ? __ldg(p.fold + kk * p.bd.nt + j) : 0.0f;
+    }
     int tc = 0;
     for (int t = pair; t < n_tiles; t += n_pairs, ++tc) {
       int m, n;
       p.tiles.get(t, m, n);
       const int i_base = (m * 2 + (int)rank) * IPT;
+      const int n_u = min(IPT, p.I - i_base);  // inputs of this CTA's rows that exist
+      const int row_len = n_u * K;              // bf16 of one output's contiguous dcoef slice
       const int acc = tc & 1;
       bool ok = mbar_wait_warp(&ctl->acc_full[acc], (tc >> 1) & 1, abort);
       if (!named_bar_and(1, 128, ok)) break;  // the four epilogue warps leave together
@@ -884,37 +893,54 @@ __global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __g
           __syncwarp();
           if (lane == 0) mbar_arrive_cluster(&ctl->acc_empty[acc], 0);
         }
-        named_bar(1, 128);  // staging free
+        named_bar(1, 128);  // staging (stg, sout) free
 #pragma unroll
         for (int j = 0; j < 32; ++j) stg[mrow * 33 + j] = v[j];
         named_bar(1, 128);
-        // 32 outputs x IPT inputs, 128 threads
+        // 32 outputs x IPT inputs, 128 threads; the input index runs fastest so
+        // that neighbouring threads own neighbouring (o, i) edges.
         for (int pr = etid; pr < 32 * IPT; pr += 128) {
-          const int ol = pr % 32, u = pr / 32;
+          const int u = pr % IPT, ol = pr / IPT;
           const int o = n * kBN + c * 32 + ol;
           const int i = i_base + u;
           if (o >= p.O || i >= p.I) continue;
           const float* dcol = stg + (u * F) * 33 + ol;  // dpacked[o, i, j] = dcol[j * 33]
           const int64_t e = (int64_t)o * p.I + i;
-          __nv_bfloat16* dst = p.dcoef + e * p.K;
+          __nv_bfloat16* so = sout + ol * (IPT * K) + u * K;
           // C_eff = coef * scale * mask  =>  dcoef = dC_eff * scale * mask,
           // dscale = sum_k dC_eff * coef * mask; base_eff = base * mask (kanforge/torch/layers.py:162-167)
           const float mk = p.mask ? __bfloat162float(p.mask[e]) : 1.0f;
           const float sm = mk * (p.scale ? __bfloat162float(p.scale[e]) : 1.0f);
+          const __nv_bfloat16* ce = p.coef + e * K;
           float dsc = 0.0f;
-          for (int kk = 0; kk < p.K; ++kk) {
-            float dce;
-            if (p.fold) {
-              dce = 0.0f;
-              for (int j = 0; j < p.bd.nt; ++j) dce = fmaf(dcol[j * 33], __ldg(p.fold + kk * p.bd.nt + j), dce);
-            } else {
-              dce = dcol[kk * 33];
+          if (BK == 0 && p.fold) {  // only Chebyshev-feature plans fold
+            float d[F - 1];
+#pragma unroll
+            for (int j = 0; j < F - 1; ++j) d[j] = dcol[j * 33];
+            for (int kk = 0; kk < K; ++kk) {
+              const float* fr = sfold + kk * F;
+              float dce = 0.0f;
+#pragma unroll
+              for (int j = 0; j < F - 1; ++j) dce = fmaf(d[j], fr[j], dce);
+              so[kk] = __float2bfloat16_rn(dce * sm);
+              if (p.dscale) dsc = fmaf(dce, __bfloat162float(ce[kk]), dsc);
             }
-            dst[kk] = __float2bfloat16_rn(dce * sm);
-            if (p.dscale) dsc = fmaf(dce, __bfloat162float(p.coef[e * p.K + kk]), dsc);
+          } else {
+            for (int kk = 0; kk < K; ++kk) {
+              const float dce = dcol[kk * 33];
+              so[kk] = __float2bfloat16_rn(dce * sm);
+              if (p.dscale) dsc = fmaf(dce, __bfloat162float(ce[kk]), dsc);
+            }
           }
           if (p.dscale) p.dscale[e] = __float2bfloat16_rn(dsc * mk);
           if (p.dbase) p.dbase[e] = __float2bfloat16_rn(dcol[(F - 1) * 33] * mk);
+        }
+        named_bar(1, 128);  // sout complete
+        // each output's slice (o, i_base .. i_base + n_u - 1, 0 .. K - 1) is contiguous in dcoef
+        for (int idx = etid; idx < 32 * row_len; idx += 128) {
+          const int ol = idx / row_len, col = idx - ol * row_len;
+          const int o = n * kBN + c * 32 + ol;
+          if (o < p.O) p.dcoef[((int64_t)o * p.I + i_base) * K + col] = sout[ol * (IPT * K) + col];
         }
       }
     }
@@ -1191,7 +1217,9 @@ struct WgradLaunch {
   cudaStream_t stream;
   template <int BK, int F>
   int go() const {
-    const size_t smem = kPairSmem + 1024 + kStages * kXTile + sizeof(float) * (128 * 33 + (BK > 0 ? 16 * (BK + 1) * p.tab_stride : 0));
+    const size_t smem = kPairSmem + 1024 + kStages * kXTile +
+                        sizeof(float) * (128 * 33 + (BK > 0 ? 16 * (BK + 1) * p.tab_stride : 0) + 32 * 32) +
+                        sizeof(__nv_bfloat16) * 32 * 128;
     if (smem > 232448) {
       set_error("kf_wgrad: B-spline order %d with %d knots needs %zu bytes of shared memory", BK, p.bd.nk, smem);
       return KF_ERR_UNSUPPORTED;
