@@ -832,7 +832,7 @@ __global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __g
     }
   } else if (warp == 1) {
     if (rank == 0 && lane == 0) {
-      const uint32_t idesc = idesc_bf16_f32(kPairM, kBN, false, true);
+      const uint32_t idesc = idesc_bf16_f32(kPairM, kBN, true, true);  // both operands MN-major
       int it = 0, tc = 0;
       for (int t = pair; t < n_tiles && !*abort; t += n_pairs, ++tc) {
         const int acc = tc & 1;
@@ -851,7 +851,7 @@ __global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __g
           const uint32_t a0 = smem_u32(sa + s * kATile), b0 = smem_u32(sb + s * kBHalf);
 #pragma unroll
           for (int j = 0; j < kBK / 16; ++j) {
-            mma_bf16_pair(d_tmem, smem_desc_sw128(a0 + 32 * j, 16, 1024), smem_desc_sw128(b0 + 2048 * j, 8192, 1024), idesc,
+            mma_bf16_pair(d_tmem, smem_desc_sw128(a0 + 2048 * j, 8192, 1024), smem_desc_sw128(b0 + 2048 * j, 8192, 1024), idesc,
                           (k > 0 || j > 0) ? 1u : 0u);
           }
           mma_commit_pair(&ctl->empty[s], 0x3);
@@ -936,11 +936,21 @@ __global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __g
           if (p.dbase) p.dbase[e] = __float2bfloat16_rn(dcol[(F - 1) * 33] * mk);
         }
         named_bar(1, 128);  // sout complete
-        // each output's slice (o, i_base .. i_base + n_u - 1, 0 .. K - 1) is contiguous in dcoef
-        for (int idx = etid; idx < 32 * row_len; idx += 128) {
-          const int ol = idx / row_len, col = idx - ol * row_len;
+        // each output's slice (o, i_base .. i_base + n_u - 1, 0 .. K - 1) is
+        // contiguous in dcoef: warp q copies rows q, q + 4, ..., lanes along the
+        // row, in bf16 pairs when the row starts 4-byte aligned and is even.
+        for (int ol = q; ol < 32; ol += 4) {
           const int o = n * kBN + c * 32 + ol;
-          if (o < p.O) p.dcoef[((int64_t)o * p.I + i_base) * K + col] = sout[ol * (IPT * K) + col];
+          if (o >= p.O) break;
+          const int64_t g0 = ((int64_t)o * p.I + i_base) * K;
+          const __nv_bfloat16* src = sout + ol * (IPT * K);
+          if (((g0 | row_len | (IPT * K)) & 1) == 0) {
+            uint32_t* dst2 = reinterpret_cast<uint32_t*>(p.dcoef + g0);
+            const uint32_t* src2 = reinterpret_cast<const uint32_t*>(src);
+            for (int col = lane; col < row_len / 2; col += 32) dst2[col] = src2[col];
+          } else {
+            for (int col = lane; col < row_len; col += 32) p.dcoef[g0 + col] = src[col];
+          }
         }
       }
     }
@@ -1023,15 +1033,25 @@ __global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __g
             if (p.bd.has_base) f[r][F - 1] = silu_fast(xv[r]);
           }
         }
-        // A[m = u*F + j][k = bsub (+1)]: K-major swizzled rows
+        // A[m = u*F + j][k = token], MN-major: 64-row chunks of m (8 KB apart),
+        // each token a 128-byte swizzled row holding 64 consecutive m; the F
+        // features of one (token, input) are F / 8 consecutive 16-byte granules.
+        {
+          const int m0 = u * F;
+          uint8_t* chunk = at + (m0 / 64) * 8192;
+          const int gr0 = (m0 % 64) / 8;
 #pragma unroll
-        for (int j = 0; j < F; ++j) {
-          const int mr = u * F + j;
-          const uint32_t off = sw128_offset(mr, bsub >> 3) + (bsub & 7) * 2;
-          if (NB == 2) {
-            *reinterpret_cast<uint32_t*>(at + off) = pack_bf16x2(f[0][j], f[1][j]);
-          } else {
-            *reinterpret_cast<__nv_bfloat16*>(at + off) = __float2bfloat16_rn(f[0][j]);
+          for (int r = 0; r < NB; ++r) {
+            const int kt = bsub + r;
+#pragma unroll
+            for (int g = 0; g < F / 8; ++g) {
+              uint4 pk;
+              pk.x = pack_bf16x2(f[r][8 * g + 0], f[r][8 * g + 1]);
+              pk.y = pack_bf16x2(f[r][8 * g + 2], f[r][8 * g + 3]);
+              pk.z = pack_bf16x2(f[r][8 * g + 4], f[r][8 * g + 5]);
+              pk.w = pack_bf16x2(f[r][8 * g + 6], f[r][8 * g + 7]);
+              *reinterpret_cast<uint4*>(chunk + sw128_offset(kt, gr0 + g)) = pk;
+            }
           }
         }
         fence_proxy_async_smem();
