@@ -35,7 +35,6 @@ constexpr int kBN = 256;
 constexpr int kBK = 64;  // bf16 elements per stage row = 128 bytes
 constexpr int kStages = 4;
 constexpr int kATile = kBM * 128;  // 16 KB
-constexpr int kBTile = kBN * 128;  // 32 KB
 constexpr int kTabStride = 64;     // floats per knot/inverse-difference row
 constexpr int kMaxOrder = 5;
 
@@ -496,8 +495,13 @@ struct DgradParams {
   BasisDev bd;
 };
 
-constexpr int kDgradThreads = 256;  // w0 TMA, w1 MMA, w4-7 epilogue
+constexpr int kDgradThreads = 256;  // w0 TMA, w1 MMA (CTA 0), w4-7 epilogue
 
+// The input gradient runs on CTA pairs: a tile is 256 tokens x 256 feature
+// columns, CTA r loads dy rows 128 r .. 128 r + 127 (its half of A) and
+// packed columns 128 r .. 128 r + 127 (its half of B), both completing on CTA
+// 0's barrier, and each CTA's epilogue contracts its own 128 accumulator rows
+// with the derivative features.
 template <int BK, int F>
 __global__ void __launch_bounds__(kDgradThreads, 1) fused_dgrad_kernel(const __grid_constant__ CUtensorMap tmap_dy,
                                                                        const __grid_constant__ CUtensorMap tmap_c, DgradParams p) {
@@ -505,30 +509,31 @@ __global__ void __launch_bounds__(kDgradThreads, 1) fused_dgrad_kernel(const __g
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = align1024(smem_raw);
   uint8_t* sa = base;
-  uint8_t* sb = sa + kStages * kATile;
-  Ctl* ctl = reinterpret_cast<Ctl*>(sb + kStages * kBTile);
+  uint8_t* sb = sa + kStages * kATile;                  // kStages x 16 KB (this CTA's half of B)
+  Ctl* ctl = reinterpret_cast<Ctl*>(sb + kStages * kBHalf);
   float* tabs = reinterpret_cast<float*>(ctl + 1);      // B-spline knots: [IPT][64]
   float* stage = tabs + IPT * kTabStride;               // B-spline: per-warp [32][33]
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = blockIdx.x / 2, n_pairs = gridDim.x / 2;
   volatile int* abort = &ctl->abort;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&ctl->full_a[s], 1);
-      mbar_init(&ctl->full_b[s], 1);
+      mbar_init(&ctl->full_b[s], 1);  // CTA 0's expect_tx for both CTAs' A and B halves (used in CTA 0)
       mbar_init(&ctl->empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&ctl->acc_full[a], 1);
-      mbar_init(&ctl->acc_empty[a], 4);
+      mbar_init(&ctl->acc_empty[a], 8);  // 4 epilogue warps of each CTA (used in CTA 0)
     }
     mbar_init(&ctl->drain, 1);
     ctl->abort = 0;
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc(&ctl->tmem_base, 512);
-    tmem_relinquish();
+    tmem_alloc_pair(&ctl->tmem_base, 512);
+    tmem_relinquish_pair();
   }
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmap_dy);
@@ -536,6 +541,7 @@ __global__ void __launch_bounds__(kDgradThreads, 1) fused_dgrad_kernel(const __g
   }
   tc_fence_before();
   __syncthreads();
+  cluster_sync();  // both CTAs' barriers exist before any remote arrive
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
   const int n_tiles = p.tiles.count();
@@ -543,57 +549,68 @@ __global__ void __launch_bounds__(kDgradThreads, 1) fused_dgrad_kernel(const __g
   if (warp == 0) {
     if (lane == 0) {
       int it = 0;
-      for (int t = blockIdx.x; t < n_tiles && !*abort; t += gridDim.x) {
+      for (int t = pair; t < n_tiles && !*abort; t += n_pairs) {
         int m, n;
         p.tiles.get(t, m, n);
+        const int a_row = m * kPairM + (int)rank * kBM;
+        const int b_col = n * kBN + (int)rank * (kBN / 2);
         for (int k = 0; k < p.k_steps; ++k, ++it) {
           const int s = it % kStages;
           const uint32_t ph = (it / kStages) & 1;
           if (!mbar_wait(&ctl->empty[s], ph ^ 1, abort)) break;
-          mbar_arrive_expect_tx(&ctl->full_b[s], kATile + kBTile);
-          // A: dy rows m*128.., K = o (K-major, 128 x 64)
-          tma_load_2d(sa + s * kATile, &tmap_dy, &ctl->full_b[s], k * kBK, m * kBM);
-          // B: packed[o, n*256 + 0..255] as N-major (MN-major) 64 x 64 boxes
+          if (rank == 0) {
+            mbar_arrive_expect_tx(&ctl->full_b[s], 2 * (kATile + kBHalf));  // both CTAs' loads complete here
+            // A: dy rows, K = o (K-major, 128 x 64)
+            tma_load_2d(sa + s * kATile, &tmap_dy, &ctl->full_b[s], k * kBK, a_row);
+            // B: packed[o, feature columns] as MN-major 64 x 64 boxes
 #pragma unroll
-          for (int c = 0; c < kBN / 64; ++c)
-            tma_load_2d(sb + s * kBTile + c * 8192, &tmap_c, &ctl->full_b[s], n * kBN + c * 64, k * kBK);
+            for (int c = 0; c < kBN / 128; ++c)
+              tma_load_2d(sb + s * kBHalf + c * 8192, &tmap_c, &ctl->full_b[s], b_col + c * 64, k * kBK);
+          } else {
+            tma_load_2d_pair(sa + s * kATile, &tmap_dy, &ctl->full_b[s], 0, k * kBK, a_row);
+#pragma unroll
+            for (int c = 0; c < kBN / 128; ++c)
+              tma_load_2d_pair(sb + s * kBHalf + c * 8192, &tmap_c, &ctl->full_b[s], 0, b_col + c * 64, k * kBK);
+          }
         }
       }
-      if (*abort) drain_tma(ctl, it);
+      // Abort: CTA 0 drains the loads of both CTAs (they complete on its
+      // barriers) before the pair's final cluster barrier.
+      if (*abort && rank == 0) drain_tma(ctl, it);
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      const uint32_t idesc = idesc_bf16_f32(kBM, kBN, false, true);
+    if (rank == 0 && lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(kPairM, kBN, false, true);
       int it = 0, tc = 0;
-      for (int t = blockIdx.x; t < n_tiles && !*abort; t += gridDim.x, ++tc) {
+      for (int t = pair; t < n_tiles && !*abort; t += n_pairs, ++tc) {
         const int acc = tc & 1;
-        if (!mbar_wait(&ctl->acc_empty[acc], ((tc >> 1) & 1) ^ 1, abort)) break;
+        if (!mbar_wait_cluster(&ctl->acc_empty[acc], ((tc >> 1) & 1) ^ 1, abort)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem + acc * kBN;
         bool ok = true;
         for (int k = 0; k < p.k_steps; ++k, ++it) {
           const int s = it % kStages;
           const uint32_t ph = (it / kStages) & 1;
-          if (!mbar_wait(&ctl->full_b[s], ph, abort)) {
+          if (!mbar_wait_cluster(&ctl->full_b[s], ph, abort)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(sa + s * kATile), b0 = smem_u32(sb + s * kBTile);
+          const uint32_t a0 = smem_u32(sa + s * kATile), b0 = smem_u32(sb + s * kBHalf);
 #pragma unroll
           for (int j = 0; j < kBK / 16; ++j) {
-            mma_bf16(d_tmem, smem_desc_sw128(a0 + 32 * j, 16, 1024), smem_desc_sw128(b0 + 2048 * j, 8192, 1024), idesc,
-                     (k > 0 || j > 0) ? 1u : 0u);
+            mma_bf16_pair(d_tmem, smem_desc_sw128(a0 + 32 * j, 16, 1024), smem_desc_sw128(b0 + 2048 * j, 8192, 1024), idesc,
+                          (k > 0 || j > 0) ? 1u : 0u);
           }
-          mma_commit(&ctl->empty[s]);
+          mma_commit_pair(&ctl->empty[s], 0x3);
         }
         if (!ok) break;
-        mma_commit(&ctl->acc_full[acc]);
+        mma_commit_pair(&ctl->acc_full[acc], 0x3);
       }
-      if (*abort) {
-        mma_commit(&ctl->drain);
-        mbar_drain(&ctl->drain, 0);
-      }
+      // Every MMA of the pair has completed (and every commit above has
+      // arrived) once the drain barrier flips: the pair may then exit.
+      mma_commit_pair(&ctl->drain, 0x1);
+      mbar_drain(&ctl->drain, 0);
     }
   } else if (warp >= 4) {
     const int q = warp - 4;
@@ -601,7 +618,7 @@ __global__ void __launch_bounds__(kDgradThreads, 1) fused_dgrad_kernel(const __g
     const int etid = q * 32 + lane;
     float* wst = stage + q * (32 * 33);
     int tc = 0;
-    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++tc) {
+    for (int t = pair; t < n_tiles; t += n_pairs, ++tc) {
       int m, n;
       p.tiles.get(t, m, n);
       const int i_base = n * IPT;
@@ -620,7 +637,7 @@ __global__ void __launch_bounds__(kDgradThreads, 1) fused_dgrad_kernel(const __g
       }
       if (!ok) break;
       tc_fence_after();
-      const int64_t b = (int64_t)m * kBM + row;
+      const int64_t b = (int64_t)m * kPairM + (int64_t)rank * kBM + row;
       const bool row_ok = b < p.B;
       float dxv[IPT];
 #pragma unroll 1
@@ -630,7 +647,7 @@ __global__ void __launch_bounds__(kDgradThreads, 1) fused_dgrad_kernel(const __g
         if (c == kBN / 32 - 1) {
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&ctl->acc_empty[acc]);
+          if (lane == 0) mbar_arrive_cluster(&ctl->acc_empty[acc], 0);
         }
         if constexpr (BK == 0) {
 #pragma unroll
@@ -704,9 +721,10 @@ __global__ void __launch_bounds__(kDgradThreads, 1) fused_dgrad_kernel(const __g
 
   tc_fence_before();
   __syncthreads();
+  cluster_sync();  // no remote arrive or MMA of the pair is outstanding past this point
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc_pair(tmem, 512);
   }
 }
 
@@ -1164,7 +1182,6 @@ int dispatch_fused(const kf_basis_desc* d, int f_pad, Fn&& fn) {
   return KF_ERR_UNSUPPORTED;
 }
 
-constexpr size_t kMainSmem = 1024 + kStages * (kATile + kBTile) + sizeof(Ctl);
 
 constexpr size_t kFwdSmem = 1024 + kStages * (kATile + kFwdNB * kBHalf) + sizeof(Ctl);
 constexpr size_t kPairSmem = 1024 + kStages * (kATile + kBHalf) + sizeof(Ctl);
@@ -1222,11 +1239,25 @@ struct DgradLaunch {
   template <int BK, int F>
   int go() const {
     constexpr int IPT = kBN / F;
-    const size_t smem = kMainSmem + (BK > 0 ? sizeof(float) * (IPT * kTabStride + 4 * 32 * 33) : 0);
+    const size_t smem = kPairSmem + (BK > 0 ? sizeof(float) * (IPT * kTabStride + 4 * 32 * 33) : 0);
     auto kern = fused_dgrad_kernel<BK, F>;
     KF_CUDA_RET(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    const int grid = (int)std::min<int64_t>(p.tiles.m_tiles * (int64_t)p.tiles.n_tiles, sm_count());
-    kern<<<grid, kDgradThreads, smem, stream>>>(*tmap_dy, *tmap_c, p);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(kDgradThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cfg.gridDim = dim3(2 * (unsigned)(sm_count() / 2));
+    static int pair_cache[64] = {0};  // per instantiation
+    const int pairs = (int)std::min<int64_t>(p.tiles.m_tiles * (int64_t)p.tiles.n_tiles, max_pairs(kern, cfg, pair_cache));
+    cfg.gridDim = dim3(2 * (unsigned)pairs);
+    KF_CUDA_RET(cudaLaunchKernelEx(&cfg, kern, *tmap_dy, *tmap_c, p));
     return check_launch("kf_dgrad");
   }
 };
@@ -1318,9 +1349,9 @@ extern "C" int kf_dgrad(const void* x, const void* dy, const void* packed, const
   p.I = I;
   p.O = O;
   p.k_steps = (int)cdiv(O, kBK);
-  p.tiles.m_tiles = (int)cdiv(B, kBM);
+  p.tiles.m_tiles = (int)cdiv(B, kPairM);
   p.tiles.n_tiles = (int)cdiv((int64_t)I * f_pad, kBN);
-  p.tiles.gm = std::min(p.tiles.m_tiles, 16);
+  p.tiles.gm = std::min(p.tiles.m_tiles, 8);
   CUtensorMap tdy, tc;
   if (int rc = make_tmap_bf16(&tdy, dy, B, O, kBK, kBM)) return rc;
   if (int rc = make_tmap_bf16(&tc, packed, O, (int64_t)I * f_pad, 64, kBK)) return rc;

@@ -318,7 +318,7 @@ class _FusedKANLinear(torch.autograd.Function):
             _launch("kf_dgrad", _ptr(x), _ptr(gy), _ptr(ctx.packed), _ptr(ctx.knot_tab), _ptr(gx), x.shape[0], n_in, n_out,
                     nt, f_pad, int(base_weight is not None), ctypes.byref(desc), stream)
         if need[3]:
-            gbias = gy.float().sum(0)
+            gbias = gy.sum(0, dtype=torch.float32)
         ctx.packed = ctx.knot_tab = None
         return gx, gc, gb, gbias, gs, None, None, None
 
