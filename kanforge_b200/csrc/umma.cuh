@@ -41,14 +41,19 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
 
+// A try_wait may suspend the thread until the phase completes, for at most
+// this long (a hint to the hardware): waiting warps then leave the issue slots
+// to the warps that do the work instead of spinning.
+constexpr uint32_t kSuspendHintNs = 10000000u;  // 10 ms
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}\n"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
       : "memory");
   return ok != 0;
 }
@@ -59,15 +64,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
-  for (uint32_t it = 1;; ++it) {
+  for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 63) == 0) {
-      if (*abort) return false;
-      if (globaltimer() - t0 > kWaitLimitNs) {
-        *abort = 1;
-        report_device_error(KF_DEVERR_MBAR_TIMEOUT);
-        return false;
-      }
+    if (*abort) return false;
+    if (globaltimer() - t0 > kWaitLimitNs) {
+      *abort = 1;
+      report_device_error(KF_DEVERR_MBAR_TIMEOUT);
+      return false;
     }
   }
 }
@@ -232,10 +235,10 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t pa
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}\n"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
       : "memory");
   return ok != 0;
 }
@@ -244,15 +247,13 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t pa
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort) {
   if (mbar_try_wait_cluster(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
-  for (uint32_t it = 1;; ++it) {
+  for (;;) {
     if (mbar_try_wait_cluster(bar, parity)) return true;
-    if ((it & 63) == 0) {
-      if (*abort) return false;
-      if (globaltimer() - t0 > kWaitLimitNs) {
-        *abort = 1;
-        report_device_error(KF_DEVERR_MBAR_TIMEOUT);
-        return false;
-      }
+    if (*abort) return false;
+    if (globaltimer() - t0 > kWaitLimitNs) {
+      *abort = 1;
+      report_device_error(KF_DEVERR_MBAR_TIMEOUT);
+      return false;
     }
   }
 }
