@@ -129,6 +129,17 @@ int kf_dgrad(const void* x, const void* dy, const void* packed, const float* kno
              int32_t I, int32_t O, int32_t nt, int32_t f_pad, int32_t has_base, const kf_basis_desc* basis,
              void* stream);
 
+/* Basis feature matrix of the fused layer, bf16:
+ *   feat[b, i*f_pad + j] = feat_j(x[b,i])   (the forward's features: basis
+ *   columns 0..nt-1, zero up to f_pad-2, silu(x) in column f_pad-1 when has_base)
+ * x (B,I) bf16, feat (B, I*f_pad) bf16, 16-byte aligned.  Input of the fast
+ * path of kf_wgrad, which then reads the features by TMA instead of
+ * evaluating them once per 256-output tile.  (No reference counterpart: the
+ * reference evaluates the basis inside each Triton launch,
+ * kanforge/kernels/triton_kernels.py:122-124, 144, 166.) */
+int kf_features(const void* x, const float* knot_tab, void* feat, int64_t B, int32_t I, int32_t nt, int32_t f_pad,
+                int32_t has_base, const kf_basis_desc* basis, void* stream);
+
 /* Fused coefficient gradient on tcgen05, with the effective-coefficient chain rule:
  *   dpacked[o,i,j] = sum_b dy[b,o] feat_j(x[b,i])
  *   dC[o,i,k]      = sum_{j<nt} dpacked[o,i,j] fold[k,j]      (fold null: k = j)
@@ -136,8 +147,10 @@ int kf_dgrad(const void* x, const void* dy, const void* packed, const float* kno
  *   dscale[o,i]    = sum_k dC[o,i,k] coef[o,i,k] edge_mask[o,i] (if dscale != null)
  *   dbase[o,i]     = dpacked[o,i,f_pad-1] * edge_mask[o,i]       (if dbase != null)
  * coef, edge_scale, edge_mask (null = 1) and the outputs are bf16.
+ * feat: the kf_features matrix of x (fast path), or null (the kernel evaluates
+ * the features from x itself).
  * (kanforge/torch/kernels.py:85, 97-98; layers.py:162-167.) */
-int kf_wgrad(const void* x, const void* dy, const float* knot_tab, const float* fold, const void* coef,
+int kf_wgrad(const void* x, const void* feat, const void* dy, const float* knot_tab, const float* fold, const void* coef,
              const void* edge_scale, const void* edge_mask, void* dcoef, void* dbase, void* dscale, int64_t B,
              int32_t I, int32_t O, int32_t K, int32_t nt, int32_t f_pad, const kf_basis_desc* basis, void* stream);
 

@@ -57,9 +57,13 @@ PROTOTYPES = {
         ctypes.c_int,
         [_vp, _vp, _vp, _vp, _vp, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, ctypes.POINTER(BasisDesc), _vp],
     ),
+    "kf_features": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, ctypes.POINTER(BasisDesc), _vp],
+    ),
     "kf_wgrad": (
         ctypes.c_int,
-        [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
+        [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
          ctypes.POINTER(BasisDesc), _vp],
     ),
     "kf_edge_derivative": (

@@ -750,7 +750,8 @@ struct WgradParams {
   BasisDev bd;
 };
 
-constexpr int kWgradThreads = 768;  // w0 TMA, w1 MMA (CTA 0), w4-7 epilogue, w8-23 producers (2 groups)
+constexpr int kWgradThreads = 768;     // w0 TMA, w1 MMA (CTA 0), w4-7 epilogue, w8-23 producers (2 groups)
+constexpr int kWgradTmaThreads = 256;  // A_TMA: w0 TMA, w1 MMA (CTA 0), w4-7 epilogue
 constexpr int kXTile = kBK * 8 * 2;  // x tile per stage: 64 rows x 8 inputs bf16 = 1 KB
 
 // The coefficient gradient runs on CTA pairs like the forward: a tile is 256
@@ -759,9 +760,15 @@ constexpr int kXTile = kBK * 8 * 2;  // x tile per stage: 64 rows x 8 inputs bf1
 // 127 of the tile), CTA 0 issues tcgen05.mma.cta_group::2 with M = 256, and
 // each CTA's epilogue folds its own 128 accumulator rows.  The x tile a CTA's
 // producers read completes on that CTA's own barrier (tab_full).
-template <int BK, int F>
-__global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __grid_constant__ CUtensorMap tmap_dy,
-                                                                       const __grid_constant__ CUtensorMap tmap_x, WgradParams p) {
+//
+// A_TMA: the feature operand is not evaluated here but read by TMA from the
+// (B, I*F) feature matrix of kf_features (tmap_x then maps that matrix), in the
+// same MN-major swizzled layout; the kernel then has no producer warps and is
+// a TMA-fed GEMM with the fold / chain-rule epilogue.
+template <int BK, int F, bool A_TMA>
+__global__ void __launch_bounds__(A_TMA ? kWgradTmaThreads : kWgradThreads, 1)
+    fused_wgrad_kernel(const __grid_constant__ CUtensorMap tmap_dy, const __grid_constant__ CUtensorMap tmap_x,
+                       WgradParams p) {
   constexpr int IPT = kBM / F;  // inputs per tile (rows of the feature operand)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = align1024(smem_raw);
@@ -781,7 +788,7 @@ __global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __g
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&ctl->full_a[s], 16);   // the 8 warps of the owning producer group, in each CTA (used in CTA 0)
-      mbar_init(&ctl->full_b[s], 1);    // CTA 0's expect_tx for both dy halves (used in CTA 0)
+      mbar_init(&ctl->full_b[s], 1);    // CTA 0's expect_tx for both dy halves (and A_TMA: feature halves)
       mbar_init(&ctl->tab_full[s], 1);  // this CTA's x tile
       mbar_init(&ctl->empty[s], 1);
     }
@@ -799,7 +806,7 @@ __global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __g
   }
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmap_dy);
-    if (p.x_tma) prefetch_tmap(&tmap_x);
+    if (A_TMA || p.x_tma) prefetch_tmap(&tmap_x);
   }
   tc_fence_before();
   __syncthreads();
@@ -816,23 +823,35 @@ __global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __g
         p.tiles.get(t, m, n);
         const int x0 = ((m * 2 + (int)rank) * IPT) & ~7;  // TMA x coordinate rounded down to 16 bytes
         const int o0 = n * kBN + (int)rank * (kBN / 2);
+        const int f0 = (m * 2 + (int)rank) * kBM;         // A_TMA: first feature column of this CTA
         for (int k = 0; k < p.k_steps; ++k, ++it) {
           const int s = it % kStages;
           const uint32_t ph = (it / kStages) & 1;
           if (!mbar_wait(&ctl->empty[s], ph ^ 1, abort)) break;
-          if (p.x_tma) {
+          if (!A_TMA && p.x_tma) {
             mbar_arrive_expect_tx(&ctl->tab_full[s], kXTile);
             tma_load_2d(sx + s * kXTile, &tmap_x, &ctl->tab_full[s], x0, k * kBK);
           }
           if (rank == 0) {
-            mbar_arrive_expect_tx(&ctl->full_b[s], 2 * kBHalf);  // both dy halves complete here
+            // both CTAs' dy halves (and feature halves) complete here
+            mbar_arrive_expect_tx(&ctl->full_b[s], 2 * kBHalf + (A_TMA ? 2 * kATile : 0));
 #pragma unroll
             for (int c = 0; c < kBN / 128; ++c)
               tma_load_2d(sb + s * kBHalf + c * 8192, &tmap_dy, &ctl->full_b[s], o0 + c * 64, k * kBK);
+            if constexpr (A_TMA) {
+#pragma unroll
+              for (int c = 0; c < kBM / 64; ++c)
+                tma_load_2d(sa + s * kATile + c * 8192, &tmap_x, &ctl->full_b[s], f0 + c * 64, k * kBK);
+            }
           } else {
 #pragma unroll
             for (int c = 0; c < kBN / 128; ++c)
               tma_load_2d_pair(sb + s * kBHalf + c * 8192, &tmap_dy, &ctl->full_b[s], 0, o0 + c * 64, k * kBK);
+            if constexpr (A_TMA) {
+#pragma unroll
+              for (int c = 0; c < kBM / 64; ++c)
+                tma_load_2d_pair(sa + s * kATile + c * 8192, &tmap_x, &ctl->full_b[s], 0, f0 + c * 64, k * kBK);
+            }
           }
         }
       }
@@ -861,7 +880,7 @@ __global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __g
         for (int k = 0; k < p.k_steps; ++k, ++it) {
           const int s = it % kStages;
           const uint32_t ph = (it / kStages) & 1;
-          if (!mbar_wait_cluster(&ctl->full_a[s], ph, abort) || !mbar_wait_cluster(&ctl->full_b[s], ph, abort)) {
+          if ((!A_TMA && !mbar_wait_cluster(&ctl->full_a[s], ph, abort)) || !mbar_wait_cluster(&ctl->full_b[s], ph, abort)) {
             ok = false;
             break;
           }
@@ -972,7 +991,7 @@ __global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __g
         }
       }
     }
-  } else if (warp >= 8) {
+  } else if (!A_TMA && warp >= 8) {
     // producers: two groups of 8 warps own the K-steps of global parity 0 / 1.
     // F == 16 -> warp pw owns input u = pw of the tile's 8 inputs, each lane two
     // batch columns; F == 32 -> 4 inputs, warps 2u and 2u+1 split the 64 columns.
@@ -1091,6 +1110,61 @@ __global__ void __launch_bounds__(kWgradThreads, 1) fused_wgrad_kernel(const __g
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc_pair(tmem, 512);
+  }
+}
+
+// ===========================================================================
+// feature matrix for the coefficient gradient
+// ===========================================================================
+
+// feat[b, i*F + j] = feature j of x[b,i], bf16: the forward's basis row
+// (Chebyshev T_j(g(x)) or the B-spline values, zero past nt) with silu(x) in
+// column F - 1.  One thread per 16-byte chunk (8 features) of the output, so
+// that a warp's store is 512 contiguous bytes; the F / 8 threads of one
+// (b, i) each evaluate its row and keep their own chunk.
+template <int BK, int F>
+__global__ void __launch_bounds__(256) feature_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ feat,
+                                                      int64_t n, int I, BasisDev bd) {
+  constexpr int CH = F / 8;
+  const int64_t n_chunks = n * CH;
+  for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < n_chunks; c += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e = c / CH;
+    const int q = (int)(c % CH);
+    const float xv = __bfloat162float(x[e]);
+    float f[F];
+    if constexpr (BK == 0) {
+      cheb_row<F>(xv, bd, f);
+    } else {
+      const float* tu = bd.tab + (size_t)(e % I) * ((BK + 1) * kTabStride);
+      const int j0 = knot_interval(xv, tu, bd.nk);
+      float vv[BK + 1];
+#pragma unroll
+      for (int rp = 0; rp <= BK; ++rp) vv[rp] = 0.0f;
+      if (j0 >= 0) bspline_local_tab<BK>(xv, tu, bd.nk, j0, 0, vv);
+#pragma unroll
+      for (int j = 0; j < F; ++j) {
+        float val = 0.0f;
+#pragma unroll
+        for (int rp = 0; rp <= BK; ++rp)
+          if (j == j0 - BK + rp) val = vv[rp];
+        f[j] = j < bd.nt ? val : 0.0f;
+      }
+      f[F - 1] = bd.has_base ? silu_fast(xv) : 0.0f;
+    }
+    float g[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      g[u] = f[u];
+#pragma unroll
+      for (int qq = 1; qq < CH; ++qq)
+        if (q == qq) g[u] = f[8 * qq + u];
+    }
+    uint4 pk;
+    pk.x = pack_bf16x2(g[0], g[1]);
+    pk.y = pack_bf16x2(g[2], g[3]);
+    pk.z = pack_bf16x2(g[4], g[5]);
+    pk.w = pack_bf16x2(g[6], g[7]);
+    reinterpret_cast<uint4*>(feat)[c] = pk;
   }
 }
 
@@ -1263,11 +1337,16 @@ struct DgradLaunch {
 };
 
 struct WgradLaunch {
-  const CUtensorMap *tmap_dy, *tmap_x;
+  const CUtensorMap *tmap_dy, *tmap_x;  // tmap_x maps the feature matrix when a_tma
   WgradParams p;
+  bool a_tma;
   cudaStream_t stream;
   template <int BK, int F>
   int go() const {
+    return a_tma ? launch<BK, F, true>() : launch<BK, F, false>();
+  }
+  template <int BK, int F, bool A_TMA>
+  int launch() const {
     const size_t smem = kPairSmem + 1024 + kStages * kXTile +
                         sizeof(float) * (128 * 33 + (BK > 0 ? 16 * (BK + 1) * p.tab_stride : 0) + 32 * 32) +
                         sizeof(__nv_bfloat16) * 32 * 128;
@@ -1275,7 +1354,7 @@ struct WgradLaunch {
       set_error("kf_wgrad: B-spline order %d with %d knots needs %zu bytes of shared memory", BK, p.bd.nk, smem);
       return KF_ERR_UNSUPPORTED;
     }
-    auto kern = fused_wgrad_kernel<BK, F>;
+    auto kern = fused_wgrad_kernel<BK, F, A_TMA>;
     KF_CUDA_RET(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1283,7 +1362,7 @@ struct WgradLaunch {
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cudaLaunchConfig_t cfg = {};
-    cfg.blockDim = dim3(kWgradThreads);
+    cfg.blockDim = dim3(A_TMA ? kWgradTmaThreads : kWgradThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cfg.attrs = attr;
@@ -1294,6 +1373,21 @@ struct WgradLaunch {
     cfg.gridDim = dim3(2 * (unsigned)pairs);
     KF_CUDA_RET(cudaLaunchKernelEx(&cfg, kern, *tmap_dy, *tmap_x, p));
     return check_launch("kf_wgrad");
+  }
+};
+
+struct FeatureLaunch {
+  const __nv_bfloat16* x;
+  __nv_bfloat16* feat;
+  int64_t n;
+  int I;
+  BasisDev bd;
+  cudaStream_t stream;
+  template <int BK, int F>
+  int go() const {
+    const unsigned grid = (unsigned)std::min<int64_t>(cdiv(n * (F / 8), 256), (int64_t)sm_count() * 16);
+    feature_kernel<BK, F><<<grid, 256, 0, stream>>>(x, feat, n, I, bd);
+    return check_launch("kf_features");
   }
 };
 
@@ -1359,7 +1453,22 @@ extern "C" int kf_dgrad(const void* x, const void* dy, const void* packed, const
   return dispatch_fused(basis, f_pad, L);
 }
 
-extern "C" int kf_wgrad(const void* x, const void* dy, const float* knot_tab, const float* fold, const void* coef,
+extern "C" int kf_features(const void* x, const float* knot_tab, void* feat, int64_t B, int32_t I, int32_t nt,
+                           int32_t f_pad, int32_t has_base, const kf_basis_desc* basis, void* stream) {
+  using namespace kf;
+  clear_error();
+  KF_CHECK_ARG(x && feat, "kf_features: null tensor pointer");
+  if (int rc = bind_device(x)) return rc;
+  KF_CHECK_ARG(B >= 0 && I >= 1, "kf_features: bad sizes");
+  KF_CHECK_ARG(((uintptr_t)feat % 16) == 0, "kf_features: feat must be 16-byte aligned");
+  BasisDev bd{};
+  if (int rc = fill_basis(basis, knot_tab, nt, has_base, f_pad, bd)) return rc;
+  if (B == 0) return KF_OK;
+  FeatureLaunch L{(const __nv_bfloat16*)x, (__nv_bfloat16*)feat, B * (int64_t)I, I, bd, (cudaStream_t)stream};
+  return dispatch_fused(basis, f_pad, L);
+}
+
+extern "C" int kf_wgrad(const void* x, const void* feat, const void* dy, const float* knot_tab, const float* fold, const void* coef,
                         const void* edge_scale, const void* edge_mask, void* dcoef, void* dbase, void* dscale, int64_t B,
                         int32_t I, int32_t O, int32_t K, int32_t nt, int32_t f_pad, const kf_basis_desc* basis,
                         void* stream) {
@@ -1402,12 +1511,15 @@ extern "C" int kf_wgrad(const void* x, const void* dy, const float* knot_tab, co
   if (int rc = make_tmap_bf16(&tdy, dy, B, O, 64, kBK)) return rc;
   p.x_tma = (I % 8 == 0) && ((uintptr_t)x % 16 == 0);
   p.tab_stride = basis->kind == KF_BASIS_BSPLINE ? ((p.bd.nk + 15) & ~15) : 16;
-  if (p.x_tma) {
+  if (feat) {
+    KF_CHECK_ARG(((uintptr_t)feat % 16) == 0, "kf_wgrad: feat must be 16-byte aligned");
+    if (int rc = make_tmap_bf16(&tx, feat, B, (int64_t)I * f_pad, 64, kBK)) return rc;
+  } else if (p.x_tma) {
     if (int rc = make_tmap_bf16(&tx, x, B, I, 8, kBK, false)) return rc;
   } else {
     tx = tdy;  // unused
   }
-  WgradLaunch L{&tdy, &tx, p, s};
+  WgradLaunch L{&tdy, &tx, p, feat != nullptr, s};
   return dispatch_fused(basis, f_pad, L);
 }
 

@@ -256,6 +256,27 @@ def pack_coef(coef, base, edge_scale, edge_mask, plan: KernelPlan, f_pad: int) -
     return packed
 
 
+# The coefficient gradient reads the basis features from a (B, I * f_pad) bf16
+# matrix made by kf_features when it fits in this budget (2.1 GB at 16384
+# tokens x 4096 inputs); above it, or if the allocation fails, the kernel
+# evaluates the features itself (slower, no extra memory).
+WGRAD_FEATURE_BYTES_MAX = 16 << 30
+
+
+def wgrad_features(x, knot_tab, nt, f_pad, has_base, desc, stream):
+    """The feature matrix of x for kf_wgrad, or None for its self-evaluating path."""
+    nbytes = x.shape[0] * x.shape[1] * f_pad * 2
+    if nbytes > WGRAD_FEATURE_BYTES_MAX:
+        return None
+    try:
+        feat = torch.empty(x.shape[0], x.shape[1] * f_pad, device=x.device, dtype=_BF16)
+    except torch.cuda.OutOfMemoryError:
+        return None
+    _launch("kf_features", _ptr(x), _ptr(knot_tab), _ptr(feat), x.shape[0], x.shape[1], nt, f_pad, int(has_base),
+            ctypes.byref(desc), stream)
+    return feat
+
+
 class _FusedKANLinear(torch.autograd.Function):
     """y = sum_{i,j} feat_j(x_i) C_eff[o,i,j] + silu(x_i) W_eff[o,i] + b_o in one
     tcgen05 contraction per pass (forward, input gradient, coefficient gradient),
@@ -308,8 +329,10 @@ class _FusedKANLinear(torch.autograd.Function):
             if plan.folded and not plan.is_identity_fold():
                 fold = _fold_on(plan, 0, x.device)
             cf, sc, mk = _bf16_or_none(coef), _bf16_or_none(edge_scale), _bf16_or_none(edge_mask)
-            _launch("kf_wgrad", _ptr(x), _ptr(gy), _ptr(ctx.knot_tab), _ptr(fold), _ptr(cf), _ptr(sc), _ptr(mk), _ptr(gc),
-                    _ptr(gb), _ptr(gs), x.shape[0], n_in, n_out, k, nt, f_pad, ctypes.byref(desc), stream)
+            feat = wgrad_features(x, ctx.knot_tab, nt, f_pad, base_weight is not None, desc, stream)
+            _launch("kf_wgrad", _ptr(x), _ptr(feat), _ptr(gy), _ptr(ctx.knot_tab), _ptr(fold), _ptr(cf), _ptr(sc), _ptr(mk),
+                    _ptr(gc), _ptr(gb), _ptr(gs), x.shape[0], n_in, n_out, k, nt, f_pad, ctypes.byref(desc), stream)
+            del feat
             gc = gc.to(coef.dtype) if need[1] else None
             gb = gb.to(base_weight.dtype) if (gb is not None and need[2]) else None
             gs = gs.to(edge_scale.dtype) if gs is not None else None

@@ -312,6 +312,27 @@ def test_bf16_fused_layer_forward_and_gradients(basis, n_b, n_in, n_out, base, b
         close(gr, want[key[nme]], BF16_TOL, f"d{nme}")
 
 
+@pytest.mark.parametrize("case", [0, 1, 3, 5, 7])
+def test_bf16_wgrad_feature_matrix_path_equals_self_evaluating_path(monkeypatch, case):
+    """kf_wgrad reading the kf_features matrix by TMA and kf_wgrad evaluating the
+    features itself (no feature buffer) give bit-identical gradients: the same
+    bf16 features meet the same MMA accumulation order."""
+    basis, n_b, n_in, n_out, base, bias, scale = FUSED_CASES[case]
+    layer = make_bf16_layer(basis, n_in, n_out, base, bias, scale, seed=3)
+    x = (torch.randn(n_b, n_in, device=DEV) * 1.2).clamp(-3, 3).to(torch.bfloat16).requires_grad_()
+    dy = (torch.randn(n_b, n_out, device=DEV) * 0.5).to(torch.bfloat16)
+    params = [p for _, p in layer.named_parameters()]
+
+    def grads():
+        return torch.autograd.grad(layer(x), [x] + params, dy)
+
+    fast = grads()
+    monkeypatch.setattr(kb.kernels, "WGRAD_FEATURE_BYTES_MAX", 0)
+    slow = grads()
+    for a, b in zip(fast, slow):
+        assert torch.equal(a, b)
+
+
 def test_bf16_fused_multi_tile_persistent_against_float32_primitives():
     """Enough tiles that every persistent CTA runs several (both TMEM accumulators,
     every pipeline phase); checked against the float32 primitive kernels."""
