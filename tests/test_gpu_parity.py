@@ -167,9 +167,10 @@ def test_edge_derivative_matches_reference(case, order):
     close(d, LAYERS[f"{case}/edge{order}"], FP32_TOL, f"edge{order}")
 
 
-# (n_in, n_out, batch): one or several 32-input chunks, partial chunks, I < 32
-# (several outputs per warp, some idle when O is small), ragged row groups.
-EDGE_SHAPES = [(64, 24, 301), (37, 3, 133), (5, 7, 1000), (2, 1, 4096), (130, 9, 50)]
+# (n_in, n_out, batch): even I (two inputs per lane: one or several 64-input
+# chunks, I < 64 with several outputs per warp) and odd I (one input per lane:
+# partial 32-input chunks, I < 32), outputs idle when O is small, ragged row groups.
+EDGE_SHAPES = [(64, 24, 301), (37, 3, 133), (5, 7, 1000), (2, 1, 4096), (130, 9, 50), (24, 40, 99), (66, 5, 17)]
 
 
 @pytest.mark.parametrize("basis", [kb.Jacobi(6, 0.5, 0.5), kb.BSpline(8, 3), kb.Chebyshev(5)], ids=repr)
