@@ -1506,7 +1506,11 @@ extern "C" int kf_wgrad(const void* x, const void* feat, const void* dy, const f
   const int ipt = kBM / f_pad;  // inputs per CTA of a pair tile
   p.tiles.m_tiles = (int)cdiv(I, 2 * ipt);
   p.tiles.n_tiles = (int)cdiv(O, kBN);
-  p.tiles.gm = p.tiles.m_tiles;  // M fastest: concurrent pairs share the dy column block
+  // Without the feature matrix, M fastest: concurrent pairs share the dy column
+  // block and nothing else is read.  With it, super-rows of 8 M tiles: the
+  // pairs in flight share a few feature blocks and a few dy blocks, so neither
+  // the 2 B I f_pad-byte feature matrix nor dy is re-read per output block.
+  p.tiles.gm = feat ? std::min(p.tiles.m_tiles, 8) : p.tiles.m_tiles;
   CUtensorMap tdy, tx;
   if (int rc = make_tmap_bf16(&tdy, dy, B, O, 64, kBK)) return rc;
   p.x_tma = (I % 8 == 0) && ((uintptr_t)x % 16 == 0);
