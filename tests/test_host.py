@@ -61,6 +61,8 @@ def test_bad_arguments_fail_without_a_gpu():
     assert rc == 1 and "bad op" in _lib.last_error()
     rc = _lib.load().kf_fwd(None, None, None, None, None, 4, 2, 2, 4, 16, 1, ctypes.byref(d), None)
     assert rc == 1 and "null" in _lib.last_error()
+    rc = _lib.load().kf_features(None, None, None, 4, 2, 4, 16, 1, ctypes.byref(d), None)
+    assert rc == 1 and "null" in _lib.last_error()
 
 
 CHEB_CASES = [c for c in sorted({k.split("/")[0] for k in BASES}) if f"{c}/fold0" in BASES]
