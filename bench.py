@@ -39,9 +39,10 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # DRAM bytes (read + write) per launch, from one-pass ncu captures of the full
 # bench workload, summarised in profiles/ with the commands that made them.
 TRAFFIC_PER_LAUNCH: dict[tuple[int, str], float] = {
-    (2, "kf_fwd"): 2041462272 + 136227584,
-    (2, "kf_wgrad"): 2423913216 + 454517248,
-    (2, "kf_dgrad"): 4672861696 + 132950784,
+    (2, "kf_fwd"): 1909501440 + 134651136,
+    (2, "kf_wgrad"): 10327355136 + 464899584,
+    (2, "kf_dgrad"): 4572593664 + 132439296,
+    (2, "kf_features"): 134248192 + 2084940544,
     (4, "kf_edge_derivative"): 67622000 + 4231267968,  # mean of 16 launches
 }
 
