@@ -181,7 +181,7 @@ __device__ __forceinline__ void cheb_drow(float x, const BasisDev& bd, float (&f
     um2 = um1;
     um1 = u;
   }
-  f[F - 1] = bd.has_base ? dsilu_acc(x) : 0.0f;
+  f[F - 1] = bd.has_base ? dsilu_fast(x) : 0.0f;
 }
 
 // ===========================================================================
@@ -511,8 +511,9 @@ __global__ void __launch_bounds__(kDgradThreads, 1) fused_dgrad_kernel(const __g
   uint8_t* sa = base;
   uint8_t* sb = sa + kStages * kATile;                  // kStages x 16 KB (this CTA's half of B)
   Ctl* ctl = reinterpret_cast<Ctl*>(sb + kStages * kBHalf);
-  float* tabs = reinterpret_cast<float*>(ctl + 1);      // B-spline knots: [IPT][64]
-  float* stage = tabs + IPT * kTabStride;               // B-spline: per-warp [32][33]
+  float* xsm = reinterpret_cast<float*>(ctl + 1);       // x of each row's tile inputs [128][IPT + 1]
+  float* tabs = xsm + kBM * (IPT + 1);                  // B-spline knot tables [IPT][(BK+1) * 64]
+  float* stage = tabs + IPT * (BK + 1) * kTabStride;    // B-spline: per-warp [32][33]
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const uint32_t rank = cluster_ctarank();
   const int pair = blockIdx.x / 2, n_pairs = gridDim.x / 2;
@@ -628,9 +629,10 @@ __global__ void __launch_bounds__(kDgradThreads, 1) fused_dgrad_kernel(const __g
         // all four warps are past the previous tile (its table readers are done) and agree
         ok = named_bar_and(1, 128, ok);
         if (ok) {
-          for (int e = etid; e < IPT * kTabStride; e += 128) {
-            const int u = e / kTabStride, r = e % kTabStride;
-            tabs[e] = (i_base + u < p.I) ? __ldg(p.bd.tab + (size_t)(i_base + u) * ((BK + 1) * kTabStride) + r) : 0.0f;
+          constexpr int kTab = (BK + 1) * kTabStride;  // knots and reciprocal differences of one input
+          for (int e = etid; e < IPT * kTab; e += 128) {
+            const int u = e / kTab, r = e % kTab;
+            tabs[e] = (i_base + u < p.I) ? __ldg(p.bd.tab + (size_t)(i_base + u) * kTab + r) : 0.0f;
           }
         }
         named_bar(1, 128);
@@ -639,6 +641,23 @@ __global__ void __launch_bounds__(kDgradThreads, 1) fused_dgrad_kernel(const __g
       tc_fence_after();
       const int64_t b = (int64_t)m * kPairM + (int64_t)rank * kBM + row;
       const bool row_ok = b < p.B;
+      // this row's x for the tile's inputs, loaded once (vector loads when aligned)
+      float* xr = xsm + row * (IPT + 1);
+      if (row_ok && i_base + IPT <= p.I && (p.I % 8) == 0) {
+        const uint4* src = reinterpret_cast<const uint4*>(p.x + b * p.I + i_base);
+#pragma unroll
+        for (int v8 = 0; v8 < IPT / 8; ++v8) {
+          const uint4 pk = __ldg(src + v8);
+          const uint32_t w4[4] = {pk.x, pk.y, pk.z, pk.w};
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            xr[8 * v8 + 2 * h] = __uint_as_float(w4[h] << 16);
+            xr[8 * v8 + 2 * h + 1] = __uint_as_float(w4[h] & 0xffff0000u);
+          }
+        }
+      } else {
+        for (int u = 0; u < IPT; ++u) xr[u] = (row_ok && i_base + u < p.I) ? __bfloat162float(p.x[b * p.I + i_base + u]) : 0.0f;
+      }
       float dxv[IPT];
 #pragma unroll 1
       for (int c = 0; c < kBN / 32; ++c) {
@@ -654,8 +673,7 @@ __global__ void __launch_bounds__(kDgradThreads, 1) fused_dgrad_kernel(const __g
           for (int h = 0; h < 32 / F + (F > 32 ? 1 : 0); ++h) {
             // F == 16: two inputs per chunk; F == 32: one input per chunk
             const int u = (c * 32) / F + h;
-            const int i = i_base + u;
-            float xval = (row_ok && i < p.I) ? __bfloat162float(p.x[b * p.I + i]) : 0.0f;
+            const float xval = xr[u];
             float df[F];
             cheb_drow<F>(xval, p.bd, df);
             float s = 0.0f;
@@ -676,20 +694,20 @@ __global__ void __launch_bounds__(kDgradThreads, 1) fused_dgrad_kernel(const __g
             const int i = i_base + u;
             float s = 0.0f;
             if (row_ok && i < p.I) {
-              const float xval = __bfloat162float(p.x[b * p.I + i]);
-              const float* tu = tabs + u * kTabStride;
+              const float xval = xr[u];
+              const float* tu = tabs + u * ((BK + 1) * kTabStride);
               const int j0 = knot_interval(xval, tu, p.bd.nk);
               if (j0 >= 0) {
                 float dv[BK + 1];
-                // reference derivative step with plain division (spline.py:86-91)
-                bspline_local<BK>(xval, tu, p.bd.nk, j0, 1, dv);
+                // derivative step of kanforge/bases/spline.py:86-91 with the reciprocal differences of the table
+                bspline_local_tab<BK>(xval, tu, p.bd.nk, j0, 1, dv);
 #pragma unroll
                 for (int rp = 0; rp <= BK; ++rp) {
                   const int r = j0 - BK + rp;
                   if (r >= 0 && r < p.bd.nt) s = fmaf(wst[lane * 33 + h * F + r], dv[rp], s);
                 }
               }
-              if (p.bd.has_base) s = fmaf(wst[lane * 33 + h * F + F - 1], dsilu_acc(xval), s);
+              if (p.bd.has_base) s = fmaf(wst[lane * 33 + h * F + F - 1], dsilu_fast(xval), s);
             }
 #pragma unroll
             for (int uu = 0; uu < IPT; ++uu)
@@ -1313,7 +1331,7 @@ struct DgradLaunch {
   template <int BK, int F>
   int go() const {
     constexpr int IPT = kBN / F;
-    const size_t smem = kPairSmem + (BK > 0 ? sizeof(float) * (IPT * kTabStride + 4 * 32 * 33) : 0);
+    const size_t smem = kPairSmem + sizeof(float) * (kBM * (IPT + 1) + (BK > 0 ? IPT * (BK + 1) * kTabStride + 4 * 32 * 33 : 0));
     auto kern = fused_dgrad_kernel<BK, F>;
     KF_CUDA_RET(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     cudaLaunchAttribute attr[1];
