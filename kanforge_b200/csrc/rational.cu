@@ -40,11 +40,25 @@ __global__ void __launch_bounds__(kRatThreads) rational_act_kernel(const T* __re
     const int i = (int)(e % I);
     const float* th = sp + (i / p.in_per_group) * w;
     const float xv = to_f32(x[e]);
-    out[e] = from_f32<T>(rational_deriv(xv, th, p.na, th + p.na, p.nb, m));
+    if (m == 0) {  // R = P / (1 + |x Qs(x)|), Horner unrolled to the kernel limits (registers only)
+      float P = 0.0f, Qs = 0.0f;
+#pragma unroll
+      for (int j = KF_RAT_MAX_NUM - 1; j >= 0; --j)
+        if (j < p.na) P = P * xv + th[j];
+#pragma unroll
+      for (int j = KF_RAT_MAX_DEN - 1; j >= 0; --j)
+        if (j < p.nb) Qs = Qs * xv + th[p.na + j];
+      out[e] = from_f32<T>(P / (1.0f + fabsf(xv * Qs)));
+    } else {
+      out[e] = from_f32<T>(rational_deriv(xv, th, p.na, th + p.na, p.nb, m));
+    }
   }
 }
 
-// Partial sums per (CTA, input): workspace[blk][i][na + nb].
+// Partial sums per (row block, input): workspace[blk][i][na + nb].  Grid
+// (row blocks, 256-input chunks), one thread per input of the chunk walking the
+// block's rows; the accumulators and polynomial steps are unrolled to the
+// kernel limits with predicates, so they stay in registers.
 template <typename T>
 __global__ void __launch_bounds__(kRatThreads) rational_bwd_kernel(const T* __restrict__ x, const T* __restrict__ dr,
                                                                    const float* __restrict__ num, const float* __restrict__ den,
@@ -57,51 +71,67 @@ __global__ void __launch_bounds__(kRatThreads) rational_bwd_kernel(const T* __re
     sp[e] = c < p.na ? num[g * p.na + c] : den[g * p.nb + (c - p.na)];
   }
   __syncthreads();
+  const int i = blockIdx.y * kRatThreads + threadIdx.x;
+  if (i >= I) return;
   const int64_t r0 = (int64_t)blockIdx.x * rows_per_blk;
   const int64_t r1 = min(B, r0 + rows_per_blk);
-  for (int i = threadIdx.x; i < I; i += blockDim.x) {
-    const float* a = sp + (i / p.in_per_group) * w;
-    const float* bq = a + p.na;
-    float acc[KF_RAT_MAX_NUM + KF_RAT_MAX_DEN];
-    for (int c = 0; c < w; ++c) acc[c] = 0.0f;
-    for (int64_t b = r0; b < r1; ++b) {
-      const int64_t e = b * I + i;
-      const float xv = to_f32(x[e]);
-      const float g = to_f32(dr[e]);
-      // P, P', Q, Q' by Horner
-      float P = a[p.na - 1], dP = 0.0f;
-      for (int j = p.na - 2; j >= 0; --j) {
+  const float* a = sp + (i / p.in_per_group) * w;
+  const float* bq = a + p.na;
+  float acc_a[KF_RAT_MAX_NUM], acc_b[KF_RAT_MAX_DEN];
+#pragma unroll
+  for (int j = 0; j < KF_RAT_MAX_NUM; ++j) acc_a[j] = 0.0f;
+#pragma unroll
+  for (int j = 0; j < KF_RAT_MAX_DEN; ++j) acc_b[j] = 0.0f;
+  for (int64_t b = r0; b < r1; ++b) {
+    const int64_t e = b * I + i;
+    const float xv = to_f32(x[e]);
+    const float g = to_f32(dr[e]);
+    // P, P', Q, Q' by Horner (Q = x * Qs(x))
+    float P = 0.0f, dP = 0.0f;
+#pragma unroll
+    for (int j = KF_RAT_MAX_NUM - 1; j >= 0; --j) {
+      if (j < p.na) {
         dP = dP * xv + P;
         P = P * xv + a[j];
       }
-      float Qs = bq[p.nb - 1], dQs = 0.0f;  // Q = x * Qs(x)
-      for (int j = p.nb - 2; j >= 0; --j) {
+    }
+    float Qs = 0.0f, dQs = 0.0f;
+#pragma unroll
+    for (int j = KF_RAT_MAX_DEN - 1; j >= 0; --j) {
+      if (j < p.nb) {
         dQs = dQs * xv + Qs;
         Qs = Qs * xv + bq[j];
       }
-      const float Q = xv * Qs;
-      const float dQ = Qs + xv * dQs;
-      const float sg = Q > 0.0f ? 1.0f : (Q < 0.0f ? -1.0f : 0.0f);
-      const float D = 1.0f + fabsf(Q);
-      const float R = P / D;
-      const float dR = (dP - sg * dQ * R) / D;
-      dx[e] = from_f32<T>(g * dR);
-      const float u = g / D;
-      float xp = 1.0f;
-      for (int j = 0; j < p.na; ++j) {
-        acc[j] = fmaf(u, xp, acc[j]);
-        xp *= xv;
-      }
-      const float v = -u * R * sg;
-      xp = xv;
-      for (int j = 0; j < p.nb; ++j) {
-        acc[p.na + j] = fmaf(v, xp, acc[p.na + j]);
-        xp *= xv;
-      }
     }
-    float* dst = ws + ((size_t)blockIdx.x * I + i) * w;
-    for (int c = 0; c < w; ++c) dst[c] = acc[c];
+    const float Q = xv * Qs;
+    const float dQ = Qs + xv * dQs;
+    const float sg = Q > 0.0f ? 1.0f : (Q < 0.0f ? -1.0f : 0.0f);
+    const float D = 1.0f + fabsf(Q);
+    const float R = P / D;
+    const float dR = (dP - sg * dQ * R) / D;
+    dx[e] = from_f32<T>(g * dR);
+    const float u = g / D;
+    float xp = 1.0f;
+#pragma unroll
+    for (int j = 0; j < KF_RAT_MAX_NUM; ++j) {
+      if (j < p.na) acc_a[j] = fmaf(u, xp, acc_a[j]);
+      xp *= xv;
+    }
+    const float v = -u * R * sg;
+    xp = xv;
+#pragma unroll
+    for (int j = 0; j < KF_RAT_MAX_DEN; ++j) {
+      if (j < p.nb) acc_b[j] = fmaf(v, xp, acc_b[j]);
+      xp *= xv;
+    }
   }
+  float* dst = ws + ((size_t)blockIdx.x * I + i) * w;
+#pragma unroll
+  for (int j = 0; j < KF_RAT_MAX_NUM; ++j)
+    if (j < p.na) dst[j] = acc_a[j];
+#pragma unroll
+  for (int j = 0; j < KF_RAT_MAX_DEN; ++j)
+    if (j < p.nb) dst[p.na + j] = acc_b[j];
 }
 
 // dnum[g, j], dden[g, j] = sum over CTAs and the inputs of group g, in a fixed order.
@@ -140,7 +170,13 @@ int rat_params(const kf_basis_desc* d, int I, RatParams& p) {
   return KF_OK;
 }
 
-int64_t rat_blocks(int64_t B) { return B <= 0 ? 1 : std::min<int64_t>(kRatMaxBlocks, B); }
+// Row blocks of the backward: at least kRatMaxBlocks, more when I has few
+// 256-input chunks, so that the grid (row blocks x chunks) fills the GPU.
+int64_t rat_blocks(int64_t B, int I) {
+  const int64_t chunks = cdiv((int64_t)I, (int64_t)kRatThreads);
+  const int64_t target = std::max<int64_t>(kRatMaxBlocks, (148 * 8) / chunks);
+  return B <= 0 ? 1 : std::min<int64_t>(target, B);
+}
 
 // ---------------------------------------------------------------------------
 // Scratch for kf_rational_bwd_noalloc: a fixed array in device memory, one per
@@ -180,7 +216,7 @@ int rational_scratch(float** out) {
 
 extern "C" int64_t kf_rational_workspace(int64_t B, int32_t I, const kf_basis_desc* basis) {
   if (!basis || basis->kind != KF_BASIS_RATIONAL) return 0;
-  return kf::rat_blocks(B) * (int64_t)I * (basis->degree + 1 + basis->den_degree);
+  return kf::rat_blocks(B, I) * (int64_t)I * (basis->degree + 1 + basis->den_degree);
 }
 
 extern "C" int kf_rational_act(const void* x, const float* num, const float* den, void* out, int64_t B, int32_t I,
@@ -223,15 +259,15 @@ extern "C" int kf_rational_bwd(const void* x, const void* dr, const float* num, 
     KF_CUDA_RET(cudaMemsetAsync(dden, 0, sizeof(float) * p.groups * p.nb, s));
     return KF_OK;
   }
-  const int64_t nblk = rat_blocks(B);
+  const int64_t nblk = rat_blocks(B, I);
   const int64_t rows = cdiv(B, nblk);
   const int64_t used = cdiv(B, rows);
   const size_t smem = sizeof(float) * p.groups * (p.na + p.nb);
   if (dtype == KF_DTYPE_F32) {
-    rational_bwd_kernel<float><<<(unsigned)used, kRatThreads, smem, s>>>((const float*)x, (const float*)dr, num, den,
+    rational_bwd_kernel<float><<<dim3((unsigned)used, (unsigned)cdiv(I, kRatThreads)), kRatThreads, smem, s>>>((const float*)x, (const float*)dr, num, den,
                                                                          (float*)dx, workspace, B, I, rows, p);
   } else if (dtype == KF_DTYPE_BF16) {
-    rational_bwd_kernel<__nv_bfloat16><<<(unsigned)used, kRatThreads, smem, s>>>(
+    rational_bwd_kernel<__nv_bfloat16><<<dim3((unsigned)used, (unsigned)cdiv(I, kRatThreads)), kRatThreads, smem, s>>>(
         (const __nv_bfloat16*)x, (const __nv_bfloat16*)dr, num, den, (__nv_bfloat16*)dx, workspace, B, I, rows, p);
   } else {
     set_error("kf_rational_bwd: dtype %d unsupported", dtype);
@@ -271,15 +307,15 @@ extern "C" int kf_rational_bwd_noalloc(const void* x, const void* dr, const floa
     return KF_OK;
   }
   const int64_t cap = std::max<int64_t>(1, KF_RATIONAL_NOALLOC_MAX_FLOATS / row);
-  const int64_t nblk = std::min<int64_t>(rat_blocks(B), cap);
+  const int64_t nblk = std::min<int64_t>(rat_blocks(B, I), cap);
   const int64_t rows = cdiv(B, nblk);
   const int64_t used = cdiv(B, rows);
   const size_t smem = sizeof(float) * p.groups * (p.na + p.nb);
   if (dtype == KF_DTYPE_F32) {
-    rational_bwd_kernel<float><<<(unsigned)used, kRatThreads, smem, s>>>((const float*)x, (const float*)dr, num, den,
+    rational_bwd_kernel<float><<<dim3((unsigned)used, (unsigned)cdiv(I, kRatThreads)), kRatThreads, smem, s>>>((const float*)x, (const float*)dr, num, den,
                                                                          (float*)dx, ws, B, I, rows, p);
   } else if (dtype == KF_DTYPE_BF16) {
-    rational_bwd_kernel<__nv_bfloat16><<<(unsigned)used, kRatThreads, smem, s>>>(
+    rational_bwd_kernel<__nv_bfloat16><<<dim3((unsigned)used, (unsigned)cdiv(I, kRatThreads)), kRatThreads, smem, s>>>(
         (const __nv_bfloat16*)x, (const __nv_bfloat16*)dr, num, den, (__nv_bfloat16*)dx, ws, B, I, rows, p);
   } else {
     set_error("kf_rational_bwd_noalloc: dtype %d unsupported", dtype);
