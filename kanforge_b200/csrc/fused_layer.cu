@@ -13,14 +13,21 @@
 // w = 1; dx is P_1, the coefficient gradient G_0 followed by the fold
 // transpose of kanforge/torch/kernels.py:97-98).
 //
-// The basis operand feat is never written to HBM: producer warps evaluate it
-// from x into shared memory in the canonical 128-byte swizzled K-major layout
-// the tensor core reads, fence it into the async proxy and signal an mbarrier.
-// Coefficients / dy arrive by TMA (no multicast).  One thread issues
-// tcgen05.mma into one of two 128x256 f32 accumulators in tensor memory while
-// the epilogue warps drain the other (persistent CTAs, one per SM).
+// All three run on persistent 2-CTA clusters (one CTA per SM): one thread of
+// CTA 0 issues tcgen05.mma.cta_group::2 with M = 256 (rows 0-127 of A and of
+// the accumulator in CTA 0, rows 128-255 in CTA 1, B split by N between the
+// CTAs) into 256-column f32 accumulators in tensor memory while the epilogue
+// warps of both CTAs drain the accumulator of the previous tile.  The basis
+// operand is evaluated by producer warps from x into shared memory in the
+// canonical 128-byte swizzled layout the tensor core reads (fenced into the
+// async proxy, signalled on an mbarrier), or, for the coefficient gradient,
+// read by TMA from the feature matrix of kf_features; coefficients and dy
+// arrive by TMA (no multicast).  A CTA-1 stage completes on CTA 0's barriers
+// (remote arrives and cta_group::2 TMA), MMA completions are multicast to
+// both CTAs.
 //
-// Tiles: BM = 128 rows, BN = 256 columns, BK = 64 bf16 (128 B), 4 stages.
+// Tiles: pair M = 256 rows, N = 256 columns per accumulator (the forward uses
+// two: 512 outputs), K steps of 64 bf16 (128 B), 4 stages.
 #include "basis.cuh"
 #include "umma.cuh"
 

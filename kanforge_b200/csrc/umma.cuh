@@ -1,7 +1,8 @@
 // Blackwell (sm_100a) building blocks written as inline PTX: mbarriers with
-// bounded waits, TMA tile loads (never with cluster multicast), tcgen05 tensor
-// memory allocation, MMA issue/commit and accumulator loads, and the shared
-// memory matrix descriptors of the 128-byte swizzled canonical layouts.
+// bounded waits, TMA tile loads (never with cluster multicast), CTA-pair
+// (cta_group::2) tensor memory allocation, MMA issue/commit and accumulator
+// loads, and the shared memory matrix descriptors of the 128-byte swizzled
+// canonical layouts.
 #pragma once
 
 #include <cuda.h>
@@ -140,38 +141,8 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
 
 // ---- tensor memory -----------------------------------------------------------
 
-__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)), "r"(ncols)
-               : "memory");
-}
-
-__device__ __forceinline__ void tmem_relinquish() {
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// D[tmem] (+)= A[smem] * B[smem]^T, kind::f16 (bf16 inputs here), one thread issues.
-__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
-  const uint32_t mask0 = 0, mask1 = 0, mask2 = 0, mask3 = 0;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(mask0), "r"(mask1), "r"(mask2), "r"(mask3)
-      : "memory");
-}
-
-// Arrive once on `bar` when every tcgen05 op issued so far by this thread completes.
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
 
 // 32 lanes x 32 consecutive 32-bit columns: thread t of the warp gets lane
 // (warp % 4) * 32 + t, columns col .. col + 31.
