@@ -1144,38 +1144,21 @@ __global__ void __launch_bounds__(A_TMA ? kWgradTmaThreads : kWgradThreads, 1)
 
 // feat[b, i*F + j] = feature j of x[b,i], bf16: the forward's basis row
 // (Chebyshev T_j(g(x)) or the B-spline values, zero past nt) with silu(x) in
-// column F - 1.  One thread per 16-byte chunk (8 features) of the output, so
-// that a warp's store is 512 contiguous bytes; the F / 8 threads of one
-// (b, i) each evaluate its row and keep their own chunk.
-template <int BK, int F>
-__global__ void __launch_bounds__(256) feature_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ feat,
-                                                      int64_t n, int I, BasisDev bd) {
+// column F - 1.
+//
+// Chebyshev: one thread per 16-byte chunk (8 features) of the output, so that
+// a warp's store is 512 contiguous bytes; the F / 8 threads of one (b, i) each
+// evaluate its (cheap) row and keep their own chunk.
+template <int F>
+__global__ void __launch_bounds__(256) feature_cheb_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ feat,
+                                                           int64_t n, BasisDev bd) {
   constexpr int CH = F / 8;
   const int64_t n_chunks = n * CH;
   for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < n_chunks; c += (int64_t)gridDim.x * blockDim.x) {
     const int64_t e = c / CH;
     const int q = (int)(c % CH);
-    const float xv = __bfloat162float(x[e]);
     float f[F];
-    if constexpr (BK == 0) {
-      cheb_row<F>(xv, bd, f);
-    } else {
-      const float* tu = bd.tab + (size_t)(e % I) * ((BK + 1) * kTabStride);
-      const int j0 = knot_interval(xv, tu, bd.nk);
-      float vv[BK + 1];
-#pragma unroll
-      for (int rp = 0; rp <= BK; ++rp) vv[rp] = 0.0f;
-      if (j0 >= 0) bspline_local_tab<BK>(xv, tu, bd.nk, j0, 0, vv);
-#pragma unroll
-      for (int j = 0; j < F; ++j) {
-        float val = 0.0f;
-#pragma unroll
-        for (int rp = 0; rp <= BK; ++rp)
-          if (j == j0 - BK + rp) val = vv[rp];
-        f[j] = j < bd.nt ? val : 0.0f;
-      }
-      f[F - 1] = bd.has_base ? silu_fast(xv) : 0.0f;
-    }
+    cheb_row<F>(__bfloat162float(x[e]), bd, f);
     float g[8];
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
@@ -1190,6 +1173,77 @@ __global__ void __launch_bounds__(256) feature_kernel(const __nv_bfloat16* __res
     pk.z = pack_bf16x2(g[4], g[5]);
     pk.w = pack_bf16x2(g[6], g[7]);
     reinterpret_cast<uint4*>(feat)[c] = pk;
+  }
+}
+
+// B-splines: a CTA owns 32 consecutive inputs and stages their knot tables in
+// shared memory once (rows of ts >= nk floats, each lane's table at an odd
+// stride so that the 32 lanes, one input each, read without bank conflicts);
+// its warps walk the rows, each lane evaluating one (row, input) once (knot
+// search and Cox-de Boor from the table).  Warp shuffles then regroup the
+// F / 8 chunks of the 32 rows of features so that each store instruction
+// writes 512 contiguous bytes.
+template <int BK, int F>
+__global__ void __launch_bounds__(256) feature_spline_kernel(const __nv_bfloat16* __restrict__ x,
+                                                             __nv_bfloat16* __restrict__ feat, int64_t B, int I, BasisDev bd,
+                                                             int ts) {
+  constexpr int CH = F / 8;
+  extern __shared__ float tabs[];  // [32][ls]
+  const int ls = (BK + 1) * ts + 1;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int i0 = blockIdx.y * 32;
+  for (int e = threadIdx.x; e < 32 * (BK + 1) * ts; e += blockDim.x) {
+    const int u = e / ((BK + 1) * ts), rem = e % ((BK + 1) * ts);
+    const int q = rem / ts, r = rem % ts;
+    tabs[u * ls + rem] = (i0 + u < I) ? __ldg(bd.tab + (size_t)(i0 + u) * ((BK + 1) * kTabStride) + q * kTabStride + r) : 0.0f;
+  }
+  __syncthreads();
+  const int i = i0 + lane;
+  const bool in_ok = i < I;
+  const float* tu = tabs + lane * ls;
+  for (int64_t b = (int64_t)blockIdx.x * 8 + warp; b < B; b += (int64_t)gridDim.x * 8) {
+    float f[F];
+#pragma unroll
+    for (int j = 0; j < F; ++j) f[j] = 0.0f;
+    if (in_ok) {
+      const float xv = __bfloat162float(x[b * I + i]);
+      const int j0 = knot_interval(xv, tu, bd.nk);
+      float vv[BK + 1];
+#pragma unroll
+      for (int rp = 0; rp <= BK; ++rp) vv[rp] = 0.0f;
+      if (j0 >= 0) bspline_local_tab<BK>(xv, tu, bd.nk, j0, 0, vv, ts);
+#pragma unroll
+      for (int j = 0; j < F; ++j) {
+        float val = 0.0f;
+#pragma unroll
+        for (int rp = 0; rp <= BK; ++rp)
+          if (j == j0 - BK + rp) val = vv[rp];
+        f[j] = j < bd.nt ? val : 0.0f;
+      }
+      f[F - 1] = bd.has_base ? silu_fast(xv) : 0.0f;
+    }
+    uint32_t w[F / 2];  // the row as bf16 pairs
+#pragma unroll
+    for (int k = 0; k < F / 2; ++k) w[k] = pack_bf16x2(f[2 * k], f[2 * k + 1]);
+    const int q = lane % CH;  // chunk this lane stores
+#pragma unroll
+    for (int s2 = 0; s2 < CH; ++s2) {
+      const int src = s2 * (32 / CH) + lane / CH;  // input (lane) whose chunk q this lane stores
+      uint32_t v[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+      for (int k = 0; k < F / 2; ++k) {
+        const uint32_t t = __shfl_sync(0xffffffffu, w[k], src);
+        if (k / 4 == q) v[k % 4] = t;
+      }
+      if (i0 + src < I) {
+        uint4 pk;
+        pk.x = v[0];
+        pk.y = v[1];
+        pk.z = v[2];
+        pk.w = v[3];
+        reinterpret_cast<uint4*>(feat + (b * I + i0 + src) * F)[q] = pk;
+      }
+    }
   }
 }
 
@@ -1404,14 +1458,25 @@ struct WgradLaunch {
 struct FeatureLaunch {
   const __nv_bfloat16* x;
   __nv_bfloat16* feat;
-  int64_t n;
+  int64_t B;
   int I;
   BasisDev bd;
   cudaStream_t stream;
   template <int BK, int F>
   int go() const {
-    const unsigned grid = (unsigned)std::min<int64_t>(cdiv(n * (F / 8), 256), (int64_t)sm_count() * 16);
-    feature_kernel<BK, F><<<grid, 256, 0, stream>>>(x, feat, n, I, bd);
+    if constexpr (BK == 0) {
+      const int64_t n = B * (int64_t)I;
+      const unsigned grid = (unsigned)std::min<int64_t>(cdiv(n * (F / 8), 256), (int64_t)sm_count() * 16);
+      feature_cheb_kernel<F><<<grid, 256, 0, stream>>>(x, feat, n, bd);
+    } else {
+      const unsigned gy = (unsigned)cdiv(I, 32);
+      const int64_t want = std::max<int64_t>(1, (int64_t)sm_count() * 8 / gy);
+      const unsigned gx = (unsigned)std::max<int64_t>(1, std::min<int64_t>(cdiv(B, (int64_t)8), want));
+      const int ts = (bd.nk + 15) & ~15;  // table row stride in shared memory (>= nk)
+      const size_t smem = sizeof(float) * 32 * ((BK + 1) * ts + 1);
+      KF_CUDA_RET(cudaFuncSetAttribute(feature_spline_kernel<BK, F>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      feature_spline_kernel<BK, F><<<dim3(gx, gy), 256, smem, stream>>>(x, feat, B, I, bd, ts);
+    }
     return check_launch("kf_features");
   }
 };
@@ -1489,7 +1554,7 @@ extern "C" int kf_features(const void* x, const float* knot_tab, void* feat, int
   BasisDev bd{};
   if (int rc = fill_basis(basis, knot_tab, nt, has_base, f_pad, bd)) return rc;
   if (B == 0) return KF_OK;
-  FeatureLaunch L{(const __nv_bfloat16*)x, (__nv_bfloat16*)feat, B * (int64_t)I, I, bd, (cudaStream_t)stream};
+  FeatureLaunch L{(const __nv_bfloat16*)x, (__nv_bfloat16*)feat, B, I, bd, (cudaStream_t)stream};
   return dispatch_fused(basis, f_pad, L);
 }
 
