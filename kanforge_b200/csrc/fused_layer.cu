@@ -502,7 +502,7 @@ struct DgradParams {
   BasisDev bd;
 };
 
-constexpr int kDgradThreads = 256;  // w0 TMA, w1 MMA (CTA 0), w4-7 epilogue
+constexpr int kDgradThreads = 384;  // w0 TMA, w1 MMA (CTA 0), w4-11 epilogue (two sets of four)
 
 // The input gradient runs on CTA pairs: a tile is 256 tokens x 256 feature
 // columns, CTA r loads dy rows 128 r .. 128 r + 127 (its half of A) and
@@ -520,7 +520,7 @@ __global__ void __launch_bounds__(kDgradThreads, 1) fused_dgrad_kernel(const __g
   Ctl* ctl = reinterpret_cast<Ctl*>(sb + kStages * kBHalf);
   float* xsm = reinterpret_cast<float*>(ctl + 1);       // x of each row's tile inputs [128][IPT + 1]
   float* tabs = xsm + kBM * (IPT + 1);                  // B-spline knot tables [IPT][(BK+1) * 64]
-  float* stage = tabs + IPT * (BK + 1) * kTabStride;    // B-spline: per-warp [32][33]
+  float* stage = tabs + IPT * (BK + 1) * kTabStride;    // B-spline: per epilogue warp [32][33]
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const uint32_t rank = cluster_ctarank();
   const int pair = blockIdx.x / 2, n_pairs = gridDim.x / 2;
@@ -533,7 +533,7 @@ __global__ void __launch_bounds__(kDgradThreads, 1) fused_dgrad_kernel(const __g
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&ctl->acc_full[a], 1);
-      mbar_init(&ctl->acc_empty[a], 8);  // 4 epilogue warps of each CTA (used in CTA 0)
+      mbar_init(&ctl->acc_empty[a], 16);  // 8 epilogue warps of each CTA (used in CTA 0)
     }
     mbar_init(&ctl->drain, 1);
     ctl->abort = 0;
@@ -621,10 +621,14 @@ __global__ void __launch_bounds__(kDgradThreads, 1) fused_dgrad_kernel(const __g
       mbar_drain(&ctl->drain, 0);
     }
   } else if (warp >= 4) {
-    const int q = warp - 4;
+    // Two sets of four warps: set h2 reads TMEM lane quarter q (rows 32 q ..) of
+    // column chunks 4 h2 .. 4 h2 + 3, i.e. the inputs IPT/2 h2 .. of the tile,
+    // and writes those inputs' dx.
+    constexpr int kHalfIn = IPT / 2;
+    const int q = (warp - 4) % 4, h2 = (warp - 4) / 4;
     const int row = q * 32 + lane;
-    const int etid = q * 32 + lane;
-    float* wst = stage + q * (32 * 33);
+    const int etid = (warp - 4) * 32 + lane;  // 0 .. 255
+    float* wst = stage + (warp - 4) * (32 * 33);
     int tc = 0;
     for (int t = pair; t < n_tiles; t += n_pairs, ++tc) {
       int m, n;
@@ -633,44 +637,42 @@ __global__ void __launch_bounds__(kDgradThreads, 1) fused_dgrad_kernel(const __g
       const int acc = tc & 1;
       bool ok = mbar_wait_warp(&ctl->acc_full[acc], (tc >> 1) & 1, abort);
       if constexpr (BK > 0) {
-        // all four warps are past the previous tile (its table readers are done) and agree
-        ok = named_bar_and(1, 128, ok);
+        // all eight warps are past the previous tile (its table readers are done) and agree
+        ok = named_bar_and(1, 256, ok);
         if (ok) {
           constexpr int kTab = (BK + 1) * kTabStride;  // knots and reciprocal differences of one input
-          for (int e = etid; e < IPT * kTab; e += 128) {
+          for (int e = etid; e < IPT * kTab; e += 256) {
             const int u = e / kTab, r = e % kTab;
             tabs[e] = (i_base + u < p.I) ? __ldg(p.bd.tab + (size_t)(i_base + u) * kTab + r) : 0.0f;
           }
         }
-        named_bar(1, 128);
+        named_bar(1, 256);
       }
       if (!ok) break;
       tc_fence_after();
       const int64_t b = (int64_t)m * kPairM + (int64_t)rank * kBM + row;
       const bool row_ok = b < p.B;
-      // this row's x for the tile's inputs, loaded once (vector loads when aligned)
+      // this row's x for this set's inputs, loaded once (4-byte loads when aligned)
+      const int u0 = h2 * kHalfIn;
       float* xr = xsm + row * (IPT + 1);
-      if (row_ok && i_base + IPT <= p.I && (p.I % 8) == 0) {
-        const uint4* src = reinterpret_cast<const uint4*>(p.x + b * p.I + i_base);
+      if (row_ok && i_base + u0 + kHalfIn <= p.I && ((p.I | i_base) % 2) == 0) {
+        const uint32_t* src = reinterpret_cast<const uint32_t*>(p.x + b * p.I + i_base + u0);
 #pragma unroll
-        for (int v8 = 0; v8 < IPT / 8; ++v8) {
-          const uint4 pk = __ldg(src + v8);
-          const uint32_t w4[4] = {pk.x, pk.y, pk.z, pk.w};
-#pragma unroll
-          for (int h = 0; h < 4; ++h) {
-            xr[8 * v8 + 2 * h] = __uint_as_float(w4[h] << 16);
-            xr[8 * v8 + 2 * h + 1] = __uint_as_float(w4[h] & 0xffff0000u);
-          }
+        for (int k2 = 0; k2 < kHalfIn / 2; ++k2) {
+          const uint32_t wv = __ldg(src + k2);
+          xr[u0 + 2 * k2] = __uint_as_float(wv << 16);
+          xr[u0 + 2 * k2 + 1] = __uint_as_float(wv & 0xffff0000u);
         }
       } else {
-        for (int u = 0; u < IPT; ++u) xr[u] = (row_ok && i_base + u < p.I) ? __bfloat162float(p.x[b * p.I + i_base + u]) : 0.0f;
+        for (int u = u0; u < u0 + kHalfIn; ++u)
+          xr[u] = (row_ok && i_base + u < p.I) ? __bfloat162float(p.x[b * p.I + i_base + u]) : 0.0f;
       }
       float dxv[IPT];
 #pragma unroll 1
-      for (int c = 0; c < kBN / 32; ++c) {
+      for (int c = 4 * h2; c < 4 * h2 + 4; ++c) {
         float v[32];
         tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + acc * kBN + c * 32, v);
-        if (c == kBN / 32 - 1) {
+        if (c == 4 * h2 + 3) {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive_cluster(&ctl->acc_empty[acc], 0);
@@ -724,21 +726,22 @@ __global__ void __launch_bounds__(kDgradThreads, 1) fused_dgrad_kernel(const __g
         }
       }
       if (row_ok) {
-        __nv_bfloat16* dst = p.dx + b * p.I + i_base;
-        if (i_base + IPT <= p.I && (p.I % 8) == 0) {
+        __nv_bfloat16* dst = p.dx + b * p.I + i_base + u0;
+        if (i_base + u0 + kHalfIn <= p.I && ((p.I | i_base) % 2) == 0) {
 #pragma unroll
-          for (int u = 0; u < IPT / 8; ++u) {
-            uint4 pk;
-            pk.x = pack_bf16x2(dxv[8 * u + 0], dxv[8 * u + 1]);
-            pk.y = pack_bf16x2(dxv[8 * u + 2], dxv[8 * u + 3]);
-            pk.z = pack_bf16x2(dxv[8 * u + 4], dxv[8 * u + 5]);
-            pk.w = pack_bf16x2(dxv[8 * u + 6], dxv[8 * u + 7]);
-            *reinterpret_cast<uint4*>(dst + 8 * u) = pk;
+          for (int k2 = 0; k2 < kHalfIn / 2; ++k2) {
+            float lo = 0.0f, hi = 0.0f;
+#pragma unroll
+            for (int uu = 0; uu < IPT; ++uu) {
+              if (uu == u0 + 2 * k2) lo = dxv[uu];
+              if (uu == u0 + 2 * k2 + 1) hi = dxv[uu];
+            }
+            reinterpret_cast<uint32_t*>(dst)[k2] = pack_bf16x2(lo, hi);
           }
         } else {
 #pragma unroll
-          for (int u = 0; u < IPT; ++u)
-            if (i_base + u < p.I) dst[u] = __float2bfloat16_rn(dxv[u]);
+          for (int uu = 0; uu < IPT; ++uu)
+            if (uu >= u0 && uu < u0 + kHalfIn && i_base + uu < p.I) p.dx[b * p.I + i_base + uu] = __float2bfloat16_rn(dxv[uu]);
         }
       }
     }
@@ -1392,7 +1395,7 @@ struct DgradLaunch {
   template <int BK, int F>
   int go() const {
     constexpr int IPT = kBN / F;
-    const size_t smem = kPairSmem + sizeof(float) * (kBM * (IPT + 1) + (BK > 0 ? IPT * (BK + 1) * kTabStride + 4 * 32 * 33 : 0));
+    const size_t smem = kPairSmem + sizeof(float) * (kBM * (IPT + 1) + (BK > 0 ? IPT * (BK + 1) * kTabStride + 8 * 32 * 33 : 0));
     auto kern = fused_dgrad_kernel<BK, F>;
     KF_CUDA_RET(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     cudaLaunchAttribute attr[1];
