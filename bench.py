@@ -76,6 +76,15 @@ def dist_env():
 # ---------------------------------------------------------------------------
 
 
+def mean_square(y):
+    """Loss of the training steps: mean of y^2 accumulated in float32, one
+    reduction over the bf16 output (no float32 copy of y; the backward is one
+    elementwise kernel writing dy in y's dtype)."""
+    import torch
+
+    return torch.linalg.vector_norm(y, dtype=torch.float32).square() / y.numel()
+
+
 def build_workload(cfg: int, dtype_name: str, device, seed: int, tokens: int | None = None):
     """(model, x, step_fn, params, flops_per_step, unit_per_step, per-kernel work)."""
     import torch
@@ -101,7 +110,7 @@ def build_workload(cfg: int, dtype_name: str, device, seed: int, tokens: int | N
         model = model.to(dtype)
         nb = tokens or 65536
         x = torch.randn(nb, 1024, generator=g).clamp(-3, 3).to(device=device, dtype=dtype)
-        loss_fn = lambda y: y.float().square().mean()  # noqa: E731
+        loss_fn = mean_square
         flops = 6 * nb * 1024 * 1024 * 12
         kwork = {n: 2.0 * nb * 1024 * 1024 * 12 for n in ("kf_fwd", "kf_dgrad", "kf_wgrad")}
     elif cfg == 2:
@@ -112,14 +121,14 @@ def build_workload(cfg: int, dtype_name: str, device, seed: int, tokens: int | N
         model = model.to(dtype)
         nb = tokens or 16384
         x = torch.randn(nb, 4096, generator=g).to(device=device, dtype=dtype)
-        loss_fn = lambda y: y.float().square().mean()  # noqa: E731
+        loss_fn = mean_square
         flops = 6 * nb * 4096 * 4096 * 14
         kwork = {n: 2.0 * nb * 4096 * 4096 * 14 for n in ("kf_fwd", "kf_dgrad", "kf_wgrad")}
     elif cfg == 3:
         dtype = torch.bfloat16
         model = kb.KANFFN(768, 3072, kind="grkan", groups=8).to(device=device, dtype=dtype)
         x = torch.randn(32, 1024, 768, generator=g).to(device=device, dtype=dtype)
-        loss_fn = lambda y: y.float().square().mean()  # noqa: E731
+        loss_fn = mean_square
         flops = 6 * 32768 * (768 * 3072 * 2)
         n_el = 32768 * (768 + 3072)
         kwork = {"kf_rational_act": 4.0 * n_el, "kf_rational_bwd": 6.0 * n_el}  # bytes: read x + write r (bf16)
