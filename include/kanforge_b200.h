@@ -116,8 +116,10 @@ int kf_knot_tables(const float* grid, float* tab, int32_t I, int32_t grid_size, 
  * feat = basis features (B-spline values or T_j(g(x))) and, in the last
  * column f_pad-1, silu(x) when has_base.  x (B,I) bf16, y (B,O) bf16, bias (O) bf16 or null,
  * knot_tab: kf_knot_tables output for B-splines, else null.  Requires O % 8 == 0.
+ * feat: the kf_features matrix of x (the kernel then reads the features by
+ * TMA), or null (it evaluates them itself).
  * (kanforge/torch/layers.py:171-192 with kernels.py:143-150.) */
-int kf_fwd(const void* x, const void* packed, const void* bias, const float* knot_tab, void* y, int64_t B,
+int kf_fwd(const void* x, const void* feat, const void* packed, const void* bias, const float* knot_tab, void* y, int64_t B,
            int32_t I, int32_t O, int32_t nt, int32_t f_pad, int32_t has_base, const kf_basis_desc* basis,
            void* stream);
 
@@ -134,7 +136,7 @@ int kf_dgrad(const void* x, const void* dy, const void* packed, const float* kno
  *   columns 0..nt-1, zero up to f_pad-2, silu(x) in column f_pad-1 when has_base)
  * x (B,I) bf16, feat (B, I*f_pad) bf16, 16-byte aligned.  Input of the fast
  * path of kf_wgrad, which then reads the features by TMA instead of
- * evaluating them once per 256-output tile.  (No reference counterpart: the
+ * evaluating them once per output tile, and of kf_fwd.  (No reference counterpart: the
  * reference evaluates the basis inside each Triton launch,
  * kanforge/kernels/triton_kernels.py:122-124, 144, 166.) */
 int kf_features(const void* x, const float* knot_tab, void* feat, int64_t B, int32_t I, int32_t nt, int32_t f_pad,

@@ -51,7 +51,7 @@ PROTOTYPES = {
     "kf_pack_coef": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, ctypes.c_int, _vp]),
     "kf_fwd": (
         ctypes.c_int,
-        [_vp, _vp, _vp, _vp, _vp, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, ctypes.POINTER(BasisDesc), _vp],
+        [_vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, ctypes.POINTER(BasisDesc), _vp],
     ),
     "kf_dgrad": (
         ctypes.c_int,

@@ -224,8 +224,15 @@ constexpr int kFwdNB = 2;                 // forward: 256-column accumulator blo
 // tile's K loop at 4096 inputs).  The stage barriers that the MMA waits on live in CTA 0:
 // CTA 1's producers arrive there remotely and its coefficient TMA completes
 // there; the MMA completions are multicast to both CTAs' barriers.
-template <int BK, int F>
-__global__ void __launch_bounds__(kFwdThreads, 1) fused_fwd_kernel(const __grid_constant__ CUtensorMap tmap_c, FwdParams p) {
+//
+// A_TMA: the feature rows are not evaluated here but read by TMA from the
+// (B, I*F) feature matrix of kf_features (tmap_a, K-major 128 x 64 boxes);
+// the kernel then has no producer warps.
+constexpr int kFwdTmaThreads = 256;  // A_TMA: w0 TMA, w1 MMA (CTA 0), w4-7 epilogue
+
+template <int BK, int F, bool A_TMA>
+__global__ void __launch_bounds__(A_TMA ? kFwdTmaThreads : kFwdThreads, 1)
+    fused_fwd_kernel(const __grid_constant__ CUtensorMap tmap_c, const __grid_constant__ CUtensorMap tmap_a, FwdParams p) {
   constexpr int IPK = kBK / F;  // inputs per K-step
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = align1024(smem_raw);
@@ -258,7 +265,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fused_fwd_kernel(const __grid_
     tmem_alloc_pair(&ctl->tmem_base, 512);
     tmem_relinquish_pair();
   }
-  if (warp == 0 && lane == 0) prefetch_tmap(&tmap_c);
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmap_c);
+    if (A_TMA) prefetch_tmap(&tmap_a);
+  }
   tc_fence_before();
   __syncthreads();
   cluster_sync();  // both CTAs' barriers exist before any remote arrive
@@ -277,7 +287,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fused_fwd_kernel(const __grid_
           const int s = it % kStages;
           const uint32_t ph = (it / kStages) & 1;
           if (!mbar_wait(&ctl->empty[s], ph ^ 1, abort)) break;
-          if constexpr (BK > 0) {
+          if constexpr (BK > 0 && !A_TMA) {
             // the knot tables of the step's inputs, into this CTA
             const int n_in = min(IPK, p.I - k * IPK);
             const uint32_t tb = (uint32_t)(n_in * kTabIn * sizeof(float));
@@ -285,7 +295,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fused_fwd_kernel(const __grid_
             bulk_load(tabs + s * IPK * kTabIn, p.bd.tab + (size_t)k * IPK * kTabIn, tb, &ctl->tab_full[s]);
           }
           uint8_t* sbs = sb + s * (kFwdNB * kBHalf);
-          if (rank == 0) mbar_arrive_expect_tx(&ctl->full_b[s], 2 * p.nblk * kBHalf);  // both CTAs' halves complete here
+          // both CTAs' coefficient halves (and A_TMA: feature rows) complete here
+          if (rank == 0) mbar_arrive_expect_tx(&ctl->full_b[s], 2 * p.nblk * kBHalf + (A_TMA ? 2 * kATile : 0));
+          if constexpr (A_TMA) {
+            const int a_row = m * kPairM + (int)rank * kBM;
+            if (rank == 0)
+              tma_load_2d(sa + s * kATile, &tmap_a, &ctl->full_b[s], k * kBK, a_row);
+            else
+              tma_load_2d_pair(sa + s * kATile, &tmap_a, &ctl->full_b[s], 0, k * kBK, a_row);
+          }
           for (int nb = 0; nb < p.nblk; ++nb) {
             const int c_row = (n * p.nblk + nb) * kBN + (int)rank * (kBN / 2);
             if (rank == 0)
@@ -311,7 +329,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fused_fwd_kernel(const __grid_
         for (int k = 0; k < p.k_steps; ++k, ++it) {
           const int s = it % kStages;
           const uint32_t ph = (it / kStages) & 1;
-          if (!mbar_wait_cluster(&ctl->full_a[s], ph, abort) || !mbar_wait_cluster(&ctl->full_b[s], ph, abort)) {
+          if ((!A_TMA && !mbar_wait_cluster(&ctl->full_a[s], ph, abort)) || !mbar_wait_cluster(&ctl->full_b[s], ph, abort)) {
             ok = false;
             break;
           }
@@ -379,7 +397,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) fused_fwd_kernel(const __grid_
         }
       }
     }
-  } else if (warp >= 8) {
+  } else if (!A_TMA && warp >= 8) {
     // ---------------- feature producers: x -> basis rows in smem ----------------
     // Group grp owns the K-steps it with it % 4 == grp, i.e. always stage grp;
     // each thread owns one row.  The x values of a thread's next step are
@@ -1359,14 +1377,19 @@ int max_pairs(K kern, const cudaLaunchConfig_t& cfg, int (&cache)[64]) {
 }
 
 struct FwdLaunch {
-  const CUtensorMap* tmap;
+  const CUtensorMap *tmap, *tmap_a;  // tmap_a maps the feature matrix when a_tma
   FwdParams p;
+  bool a_tma;
   cudaStream_t stream;
   template <int BK, int F>
   int go() const {
+    return a_tma ? launch<BK, F, true>() : launch<BK, F, false>();
+  }
+  template <int BK, int F, bool A_TMA>
+  int launch() const {
     constexpr int IPK = kBK / F;
-    const size_t smem = kFwdSmem + (BK > 0 ? 1024 + sizeof(float) * kStages * IPK * (BK + 1) * kTabStride : 0);
-    auto kern = fused_fwd_kernel<BK, F>;
+    const size_t smem = kFwdSmem + (BK > 0 && !A_TMA ? 1024 + sizeof(float) * kStages * IPK * (BK + 1) * kTabStride : 0);
+    auto kern = fused_fwd_kernel<BK, F, A_TMA>;
     KF_CUDA_RET(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1374,7 +1397,7 @@ struct FwdLaunch {
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cudaLaunchConfig_t cfg = {};
-    cfg.blockDim = dim3(kFwdThreads);
+    cfg.blockDim = dim3(A_TMA ? kFwdTmaThreads : kFwdThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cfg.attrs = attr;
@@ -1383,7 +1406,7 @@ struct FwdLaunch {
     static int pair_cache[64] = {0};  // per instantiation
     const int pairs = (int)std::min<int64_t>(p.tiles.m_tiles * (int64_t)p.tiles.n_tiles, max_pairs(kern, cfg, pair_cache));
     cfg.gridDim = dim3(2 * (unsigned)pairs);
-    KF_CUDA_RET(cudaLaunchKernelEx(&cfg, kern, *tmap, p));
+    KF_CUDA_RET(cudaLaunchKernelEx(&cfg, kern, *tmap, *tmap_a, p));
     return check_launch("kf_fwd");
   }
 };
@@ -1488,7 +1511,7 @@ struct FeatureLaunch {
 
 }  // namespace kf
 
-extern "C" int kf_fwd(const void* x, const void* packed, const void* bias, const float* knot_tab, void* y, int64_t B,
+extern "C" int kf_fwd(const void* x, const void* feat, const void* packed, const void* bias, const float* knot_tab, void* y, int64_t B,
                       int32_t I, int32_t O, int32_t nt, int32_t f_pad, int32_t has_base, const kf_basis_desc* basis,
                       void* stream) {
   using namespace kf;
@@ -1511,10 +1534,19 @@ extern "C" int kf_fwd(const void* x, const void* packed, const void* bias, const
   p.tiles.m_tiles = (int)cdiv(B, kPairM);
   p.nblk = O > kBN ? kFwdNB : 1;
   p.tiles.n_tiles = (int)cdiv(O, p.nblk * kBN);
-  p.tiles.gm = p.tiles.m_tiles;  // M fastest: concurrent pairs share one coefficient column block
-  CUtensorMap tmap;
+  // Without the feature matrix, M fastest: concurrent pairs share one
+  // coefficient column block and nothing else is read.  With it, super-rows of
+  // 8 M tiles, so that the pairs in flight share feature and coefficient blocks.
+  p.tiles.gm = feat ? std::min(p.tiles.m_tiles, 8) : p.tiles.m_tiles;
+  CUtensorMap tmap, tmap_a;
   if (int rc = make_tmap_bf16(&tmap, packed, O, (int64_t)I * f_pad, kBK, kBN / 2)) return rc;
-  FwdLaunch L{&tmap, p, (cudaStream_t)stream};
+  if (feat) {
+    KF_CHECK_ARG(((uintptr_t)feat % 16) == 0, "kf_fwd: feat must be 16-byte aligned");
+    if (int rc = make_tmap_bf16(&tmap_a, feat, B, (int64_t)I * f_pad, kBK, kBM)) return rc;
+  } else {
+    tmap_a = tmap;  // unused
+  }
+  FwdLaunch L{&tmap, &tmap_a, p, feat != nullptr, (cudaStream_t)stream};
   return dispatch_fused(basis, f_pad, L);
 }
 

@@ -259,7 +259,11 @@ def pack_coef(coef, base, edge_scale, edge_mask, plan: KernelPlan, f_pad: int) -
 # The coefficient gradient reads the basis features from a (B, I * f_pad) bf16
 # matrix made by kf_features when it fits in this budget (2.1 GB at 16384
 # tokens x 4096 inputs); above it, or if the allocation fails, the kernel
-# evaluates the features itself (slower, no extra memory).
+# evaluates the features itself (slower, no extra memory).  For B-spline plans,
+# whose features are costly to evaluate inside the forward's producer warps,
+# the matrix is made in the forward, read there by TMA too, and kept until the
+# backward (activation memory traded for one evaluation instead of one per
+# output tile); Chebyshev-feature plans make it in the backward.
 WGRAD_FEATURE_BYTES_MAX = 16 << 30
 
 
@@ -299,10 +303,12 @@ class _FusedKANLinear(torch.autograd.Function):
         g = None if grid is None else grid.detach().float().contiguous()
         tab = None if grid is None else knot_tables(g, plan)
         desc = plan.desc()
-        _launch("kf_fwd", _ptr(x), _ptr(packed), _ptr(b), _ptr(tab), _ptr(y), x.shape[0], n_in, n_out, nt, f_pad,
-                int(has_base), ctypes.byref(desc), _stream(x))
+        feat = wgrad_features(x, tab, nt, f_pad, has_base, desc, _stream(x)) if plan.kind == "bspline" else None
+        _launch("kf_fwd", _ptr(x), _ptr(feat), _ptr(packed), _ptr(b), _ptr(tab), _ptr(y), x.shape[0], n_in, n_out, nt,
+                f_pad, int(has_base), ctypes.byref(desc), _stream(x))
         ctx.save_for_backward(x, coef, base_weight, edge_scale, edge_mask, g)
         ctx.packed, ctx.knot_tab, ctx.plan, ctx.has_bias = packed, tab, plan, bias is not None
+        ctx.feat = feat
         ctx.layout = (nt, f_pad)
         return y
 
@@ -312,7 +318,7 @@ class _FusedKANLinear(torch.autograd.Function):
         plan = ctx.plan
         need = ctx.needs_input_grad
         if torch.is_grad_enabled():
-            ctx.packed = ctx.knot_tab = None
+            ctx.packed = ctx.knot_tab = ctx.feat = None
             return _fused_backward_differentiable(x, gy, coef, base_weight, edge_scale, edge_mask, grid, plan, need,
                                                   ctx.has_bias)
         nt, f_pad = ctx.layout
@@ -329,7 +335,8 @@ class _FusedKANLinear(torch.autograd.Function):
             if plan.folded and not plan.is_identity_fold():
                 fold = _fold_on(plan, 0, x.device)
             cf, sc, mk = _bf16_or_none(coef), _bf16_or_none(edge_scale), _bf16_or_none(edge_mask)
-            feat = wgrad_features(x, ctx.knot_tab, nt, f_pad, base_weight is not None, desc, stream)
+            feat = ctx.feat if ctx.feat is not None else wgrad_features(x, ctx.knot_tab, nt, f_pad,
+                                                                         base_weight is not None, desc, stream)
             _launch("kf_wgrad", _ptr(x), _ptr(feat), _ptr(gy), _ptr(ctx.knot_tab), _ptr(fold), _ptr(cf), _ptr(sc), _ptr(mk),
                     _ptr(gc), _ptr(gb), _ptr(gs), x.shape[0], n_in, n_out, k, nt, f_pad, ctypes.byref(desc), stream)
             del feat
@@ -342,7 +349,7 @@ class _FusedKANLinear(torch.autograd.Function):
                     nt, f_pad, int(base_weight is not None), ctypes.byref(desc), stream)
         if need[3]:
             gbias = gy.sum(0, dtype=torch.float32)
-        ctx.packed = ctx.knot_tab = None
+        ctx.packed = ctx.knot_tab = ctx.feat = None
         return gx, gc, gb, gbias, gs, None, None, None
 
 

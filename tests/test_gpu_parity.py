@@ -315,21 +315,23 @@ def test_bf16_fused_layer_forward_and_gradients(basis, n_b, n_in, n_out, base, b
 
 @pytest.mark.parametrize("case", [0, 1, 3, 5, 7])
 def test_bf16_wgrad_feature_matrix_path_equals_self_evaluating_path(monkeypatch, case):
-    """kf_wgrad reading the kf_features matrix by TMA and kf_wgrad evaluating the
-    features itself (no feature buffer) give bit-identical gradients: the same
-    bf16 features meet the same MMA accumulation order."""
+    """kf_wgrad (and, for B-splines, kf_fwd) reading the kf_features matrix by
+    TMA and the same kernels evaluating the features themselves (no feature
+    buffer) give bit-identical outputs and gradients: the same bf16 features
+    meet the same MMA accumulation order."""
     basis, n_b, n_in, n_out, base, bias, scale = FUSED_CASES[case]
     layer = make_bf16_layer(basis, n_in, n_out, base, bias, scale, seed=3)
     x = (torch.randn(n_b, n_in, device=DEV) * 1.2).clamp(-3, 3).to(torch.bfloat16).requires_grad_()
     dy = (torch.randn(n_b, n_out, device=DEV) * 0.5).to(torch.bfloat16)
     params = [p for _, p in layer.named_parameters()]
 
-    def grads():
-        return torch.autograd.grad(layer(x), [x] + params, dy)
+    def run():
+        y = layer(x)
+        return (y.detach(),) + torch.autograd.grad(y, [x] + params, dy)
 
-    fast = grads()
+    fast = run()
     monkeypatch.setattr(kb.kernels, "WGRAD_FEATURE_BYTES_MAX", 0)
-    slow = grads()
+    slow = run()
     for a, b in zip(fast, slow):
         assert torch.equal(a, b)
 

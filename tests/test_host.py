@@ -59,7 +59,7 @@ def test_bad_arguments_fail_without_a_gpu():
     d = kb.plan_for(kb.Chebyshev(3)).desc()
     rc = _lib.load().kf_prim(7, 0, None, None, None, None, None, 4, 2, 2, 4, ctypes.byref(d), None)
     assert rc == 1 and "bad op" in _lib.last_error()
-    rc = _lib.load().kf_fwd(None, None, None, None, None, 4, 2, 2, 4, 16, 1, ctypes.byref(d), None)
+    rc = _lib.load().kf_fwd(None, None, None, None, None, None, 4, 2, 2, 4, 16, 1, ctypes.byref(d), None)
     assert rc == 1 and "null" in _lib.last_error()
     rc = _lib.load().kf_features(None, None, None, 4, 2, 4, 16, 1, ctypes.byref(d), None)
     assert rc == 1 and "null" in _lib.last_error()
