@@ -9,6 +9,7 @@
 // The parameter gradients are reduced deterministically: each CTA writes
 // per-(CTA, input) partial sums into the caller's workspace, a second kernel
 // sums them in a fixed order.
+#include <atomic>
 #include <mutex>
 
 #include "basis.cuh"
@@ -18,65 +19,188 @@ namespace kf {
 namespace {
 
 constexpr int kRatThreads = 256;
-constexpr int kRatMaxBlocks = 128;
+constexpr int kRatVecThreads = 128;  // vector backward: two adjacent inputs per thread, 256 per CTA
+constexpr int kRatRows = 4;          // rows whose loads one thread of the vector backward has in flight
+constexpr int kRatWave = 148 * 8;    // CTA cap of the forward grid (148 SMs x 8)
+constexpr int kRatBwdWave = 148 * 6; // CTAs of one wave of the vector backward (148 SMs x 6 resident)
 
 struct RatParams {
   int na, nb;          // numerator coefficients (p+1), denominator coefficients (q)
   int groups, in_per_group;
 };
 
+// Two adjacent elements of T, and their float32 values.
 template <typename T>
-__global__ void __launch_bounds__(kRatThreads) rational_act_kernel(const T* __restrict__ x, const float* __restrict__ num,
-                                                                   const float* __restrict__ den, T* __restrict__ out,
-                                                                   int64_t n, int I, int m, RatParams p) {
-  extern __shared__ float sp[];  // [groups][na + nb]
+struct Pair;
+template <>
+struct Pair<float> {
+  using type = float2;
+};
+template <>
+struct Pair<__nv_bfloat16> {
+  using type = __nv_bfloat162;
+};
+__device__ __forceinline__ float2 pair_f32(float2 v) { return v; }
+__device__ __forceinline__ float2 pair_f32(__nv_bfloat162 v) { return __bfloat1622float2(v); }
+template <typename T>
+__device__ __forceinline__ typename Pair<T>::type pair_from(float a, float b);
+template <>
+__device__ __forceinline__ float2 pair_from<float>(float a, float b) { return make_float2(a, b); }
+template <>
+__device__ __forceinline__ __nv_bfloat162 pair_from<__nv_bfloat16>(float a, float b) { return __floats2bfloat162_rn(a, b); }
+
+// Coefficient table of all groups in shared memory: sp[g][na + nb].
+__device__ __forceinline__ void load_rat_table(float* sp, const float* num, const float* den, const RatParams& p) {
   const int w = p.na + p.nb;
   for (int e = threadIdx.x; e < p.groups * w; e += blockDim.x) {
     const int g = e / w, c = e % w;
     sp[e] = c < p.na ? num[g * p.na + c] : den[g * p.nb + (c - p.na)];
   }
   __syncthreads();
+}
+
+// R(x) = P(x) / (1 + |x Qs(x)|) by Horner, MA / MB steps with the ones at or
+// beyond na / nb skipped (compile-time when the kernel fixes the degrees).
+template <int MA, int MB>
+__device__ __forceinline__ float rat_value(float xv, const float* a, const float* bq, int na, int nb) {
+  float P = 0.0f, Qs = 0.0f;
+#pragma unroll
+  for (int j = MA - 1; j >= 0; --j)
+    if (j < na) P = P * xv + a[j];
+#pragma unroll
+  for (int j = MB - 1; j >= 0; --j)
+    if (j < nb) Qs = Qs * xv + bq[j];
+  return P / (1.0f + fabsf(xv * Qs));
+}
+
+// One element of the backward: returns dx = g R'(x) and adds g dR/da_j,
+// g dR/db_j to the accumulators.  With D = 1 + |Q|, Q = x Qs(x):
+//   R' = (P' - sign(Q) Q' R) / D,  dR/da_j = x^j / D,  dR/db_j = -R sign(Q) x^(j+1) / D.
+template <int MA, int MB>
+__device__ __forceinline__ float rat_bwd_elem(float xv, float g, const float* a, const float* bq, int na, int nb,
+                                              float (&acc_a)[MA], float (&acc_b)[MB]) {
+  float P = 0.0f, dP = 0.0f;
+#pragma unroll
+  for (int j = MA - 1; j >= 0; --j) {
+    if (j < na) {
+      dP = dP * xv + P;
+      P = P * xv + a[j];
+    }
+  }
+  float Qs = 0.0f, dQs = 0.0f;
+#pragma unroll
+  for (int j = MB - 1; j >= 0; --j) {
+    if (j < nb) {
+      dQs = dQs * xv + Qs;
+      Qs = Qs * xv + bq[j];
+    }
+  }
+  const float Q = xv * Qs;
+  const float dQ = Qs + xv * dQs;
+  const float sg = Q > 0.0f ? 1.0f : (Q < 0.0f ? -1.0f : 0.0f);
+  const float rD = 1.0f / (1.0f + fabsf(Q));
+  const float R = P * rD;
+  const float u = g * rD;
+  float xp = 1.0f;
+#pragma unroll
+  for (int j = 0; j < MA; ++j) {
+    if (j < na) acc_a[j] = fmaf(u, xp, acc_a[j]);
+    xp *= xv;
+  }
+  const float v = -u * R * sg;
+  xp = xv;
+#pragma unroll
+  for (int j = 0; j < MB; ++j) {
+    if (j < nb) acc_b[j] = fmaf(v, xp, acc_b[j]);
+    xp *= xv;
+  }
+  return g * ((dP - sg * dQ * R) * rD);
+}
+
+// Forward (and PINN derivatives): one element per thread, any layout.
+template <typename T>
+__global__ void __launch_bounds__(kRatThreads) rational_act_kernel(const T* __restrict__ x, const float* __restrict__ num,
+                                                                   const float* __restrict__ den, T* __restrict__ out,
+                                                                   int64_t n, int I, int m, RatParams p) {
+  extern __shared__ float sp[];  // [groups][na + nb]
+  load_rat_table(sp, num, den, p);
+  const int w = p.na + p.nb;
   for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
     const int i = (int)(e % I);
     const float* th = sp + (i / p.in_per_group) * w;
     const float xv = to_f32(x[e]);
-    if (m == 0) {  // R = P / (1 + |x Qs(x)|), Horner unrolled to the kernel limits (registers only)
-      float P = 0.0f, Qs = 0.0f;
-#pragma unroll
-      for (int j = KF_RAT_MAX_NUM - 1; j >= 0; --j)
-        if (j < p.na) P = P * xv + th[j];
-#pragma unroll
-      for (int j = KF_RAT_MAX_DEN - 1; j >= 0; --j)
-        if (j < p.nb) Qs = Qs * xv + th[p.na + j];
-      out[e] = from_f32<T>(P / (1.0f + fabsf(xv * Qs)));
-    } else {
+    if (m == 0)
+      out[e] = from_f32<T>(rat_value<KF_RAT_MAX_NUM, KF_RAT_MAX_DEN>(xv, th, th + p.na, p.na, p.nb));
+    else
       out[e] = from_f32<T>(rational_deriv(xv, th, p.na, th + p.na, p.nb, m));
+  }
+}
+
+// Forward R(x) on 16-byte vectors (8 bf16 / 4 float32 elements of one group):
+// nvec vectors, ivec per row, vpg per group, two vectors per thread in flight.
+// NA = NB = 0: degrees from p (up to the kernel limits).
+template <typename T, int NA, int NB>
+__global__ void __launch_bounds__(kRatThreads) rational_act_vec_kernel(const T* __restrict__ x, const float* __restrict__ num,
+                                                                       const float* __restrict__ den, T* __restrict__ out,
+                                                                       uint32_t nvec, uint32_t ivec, uint32_t vpg,
+                                                                       RatParams p) {
+  constexpr int MA = NA > 0 ? NA : KF_RAT_MAX_NUM;
+  constexpr int MB = NB > 0 ? NB : KF_RAT_MAX_DEN;
+  constexpr int V = 16 / sizeof(T);
+  struct __align__(16) Vec {
+    T e[V];
+  };
+  extern __shared__ float sp[];
+  load_rat_table(sp, num, den, p);
+  const int na = NA > 0 ? NA : p.na, nb = NB > 0 ? NB : p.nb;
+  const int w = p.na + p.nb;
+  const Vec* xv = reinterpret_cast<const Vec*>(x);
+  Vec* ov = reinterpret_cast<Vec*>(out);
+  auto eval = [&](const Vec& in, uint32_t v) {
+    const float* th = sp + ((v % ivec) / vpg) * w;
+    float ca[MA], cb[MB];
+#pragma unroll
+    for (int j = 0; j < MA; ++j) ca[j] = j < na ? th[j] : 0.0f;
+#pragma unroll
+    for (int j = 0; j < MB; ++j) cb[j] = j < nb ? th[na + j] : 0.0f;
+    Vec r;
+#pragma unroll
+    for (int k = 0; k < V; ++k) r.e[k] = from_f32<T>(rat_value<MA, MB>(to_f32(in.e[k]), ca, cb, na, nb));
+    ov[v] = r;
+  };
+  const uint32_t stride = gridDim.x * blockDim.x;
+  for (uint32_t v = blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += 2 * stride) {
+    const uint32_t v1 = v + stride;
+    const Vec a0 = xv[v];
+    if (v1 < nvec) {
+      const Vec a1 = xv[v1];
+      eval(a0, v);
+      eval(a1, v1);
+    } else {
+      eval(a0, v);
     }
   }
 }
 
-// Partial sums per (row block, input): workspace[blk][i][na + nb].  Grid
-// (row blocks, 256-input chunks), one thread per input of the chunk walking the
-// block's rows; the accumulators and polynomial steps are unrolled to the
-// kernel limits with predicates, so they stay in registers.
+// Backward partial sums per (row block, input), workspace layout
+// ws[blk][c][i] (c < na: numerator, then denominator).  Grid (row blocks,
+// 256-input chunks); each thread walks its block's rows in order, so the
+// partial sums of both kernels below are the same.
+//
+// Any layout: one input per thread, degrees up to the kernel limits.
 template <typename T>
 __global__ void __launch_bounds__(kRatThreads) rational_bwd_kernel(const T* __restrict__ x, const T* __restrict__ dr,
                                                                    const float* __restrict__ num, const float* __restrict__ den,
                                                                    T* __restrict__ dx, float* __restrict__ ws, int64_t B, int I,
                                                                    int64_t rows_per_blk, RatParams p) {
   extern __shared__ float sp[];
-  const int w = p.na + p.nb;
-  for (int e = threadIdx.x; e < p.groups * w; e += blockDim.x) {
-    const int g = e / w, c = e % w;
-    sp[e] = c < p.na ? num[g * p.na + c] : den[g * p.nb + (c - p.na)];
-  }
-  __syncthreads();
+  load_rat_table(sp, num, den, p);
   const int i = blockIdx.y * kRatThreads + threadIdx.x;
   if (i >= I) return;
   const int64_t r0 = (int64_t)blockIdx.x * rows_per_blk;
   const int64_t r1 = min(B, r0 + rows_per_blk);
+  const int w = p.na + p.nb;
   const float* a = sp + (i / p.in_per_group) * w;
-  const float* bq = a + p.na;
   float acc_a[KF_RAT_MAX_NUM], acc_b[KF_RAT_MAX_DEN];
 #pragma unroll
   for (int j = 0; j < KF_RAT_MAX_NUM; ++j) acc_a[j] = 0.0f;
@@ -84,57 +208,82 @@ __global__ void __launch_bounds__(kRatThreads) rational_bwd_kernel(const T* __re
   for (int j = 0; j < KF_RAT_MAX_DEN; ++j) acc_b[j] = 0.0f;
   for (int64_t b = r0; b < r1; ++b) {
     const int64_t e = b * I + i;
-    const float xv = to_f32(x[e]);
-    const float g = to_f32(dr[e]);
-    // P, P', Q, Q' by Horner (Q = x * Qs(x))
-    float P = 0.0f, dP = 0.0f;
-#pragma unroll
-    for (int j = KF_RAT_MAX_NUM - 1; j >= 0; --j) {
-      if (j < p.na) {
-        dP = dP * xv + P;
-        P = P * xv + a[j];
-      }
-    }
-    float Qs = 0.0f, dQs = 0.0f;
-#pragma unroll
-    for (int j = KF_RAT_MAX_DEN - 1; j >= 0; --j) {
-      if (j < p.nb) {
-        dQs = dQs * xv + Qs;
-        Qs = Qs * xv + bq[j];
-      }
-    }
-    const float Q = xv * Qs;
-    const float dQ = Qs + xv * dQs;
-    const float sg = Q > 0.0f ? 1.0f : (Q < 0.0f ? -1.0f : 0.0f);
-    const float D = 1.0f + fabsf(Q);
-    const float R = P / D;
-    const float dR = (dP - sg * dQ * R) / D;
-    dx[e] = from_f32<T>(g * dR);
-    const float u = g / D;
-    float xp = 1.0f;
-#pragma unroll
-    for (int j = 0; j < KF_RAT_MAX_NUM; ++j) {
-      if (j < p.na) acc_a[j] = fmaf(u, xp, acc_a[j]);
-      xp *= xv;
-    }
-    const float v = -u * R * sg;
-    xp = xv;
-#pragma unroll
-    for (int j = 0; j < KF_RAT_MAX_DEN; ++j) {
-      if (j < p.nb) acc_b[j] = fmaf(v, xp, acc_b[j]);
-      xp *= xv;
-    }
+    dx[e] = from_f32<T>(rat_bwd_elem(to_f32(x[e]), to_f32(dr[e]), a, a + p.na, p.na, p.nb, acc_a, acc_b));
   }
-  float* dst = ws + ((size_t)blockIdx.x * I + i) * w;
+  float* dst = ws + (size_t)blockIdx.x * w * I + i;
 #pragma unroll
   for (int j = 0; j < KF_RAT_MAX_NUM; ++j)
-    if (j < p.na) dst[j] = acc_a[j];
+    if (j < p.na) dst[(size_t)j * I] = acc_a[j];
 #pragma unroll
   for (int j = 0; j < KF_RAT_MAX_DEN; ++j)
-    if (j < p.nb) dst[p.na + j] = acc_b[j];
+    if (j < p.nb) dst[(size_t)(p.na + j) * I] = acc_b[j];
 }
 
-// dnum[g, j], dden[g, j] = sum over CTAs and the inputs of group g, in a fixed order.
+// Pairs of inputs (in_per_group even, x / dr / dx aligned to two elements, ws
+// to two floats):
+// one bf16x2 / float2 load of x and of dr per row, kRatRows rows' loads in
+// flight before their arithmetic, the degrees fixed at compile time (the
+// accumulators of both inputs and the coefficients stay in registers).
+template <typename T, int NA, int NB>
+__global__ void __launch_bounds__(kRatVecThreads, 6) rational_bwd_vec_kernel(
+    const T* __restrict__ x, const T* __restrict__ dr, const float* __restrict__ num, const float* __restrict__ den,
+    T* __restrict__ dx, float* __restrict__ ws, int64_t B, int I, int64_t rows_per_blk, RatParams p) {
+  static_assert(NA > 0 && NB > 0, "the vector backward fixes the degrees");
+  constexpr int MA = NA, MB = NB;
+  using P2 = typename Pair<T>::type;
+  extern __shared__ float sp[];
+  load_rat_table(sp, num, den, p);
+  const int i0 = blockIdx.y * (2 * kRatVecThreads) + 2 * threadIdx.x;
+  if (i0 >= I) return;
+  constexpr int na = NA, nb = NB;
+  const int w = p.na + p.nb;
+  const float* th = sp + (i0 / p.in_per_group) * w;
+  float ca[MA], cb[MB], a0[MA], a1[MA], b0[MB], b1[MB];
+#pragma unroll
+  for (int j = 0; j < MA; ++j) {
+    ca[j] = j < na ? th[j] : 0.0f;
+    a0[j] = a1[j] = 0.0f;
+  }
+#pragma unroll
+  for (int j = 0; j < MB; ++j) {
+    cb[j] = j < nb ? th[na + j] : 0.0f;
+    b0[j] = b1[j] = 0.0f;
+  }
+  const int64_t ih = I / 2;
+  const P2* xp = reinterpret_cast<const P2*>(x) + i0 / 2;
+  const P2* gp = reinterpret_cast<const P2*>(dr) + i0 / 2;
+  P2* dp = reinterpret_cast<P2*>(dx) + i0 / 2;
+  const int64_t r0 = (int64_t)blockIdx.x * rows_per_blk;
+  const int64_t r1 = min(B, r0 + rows_per_blk);
+  auto row = [&](int64_t b, P2 xv2, P2 gv2) {
+    const float2 xf = pair_f32(xv2), gf = pair_f32(gv2);
+    const float d0 = rat_bwd_elem(xf.x, gf.x, ca, cb, na, nb, a0, b0);
+    const float d1 = rat_bwd_elem(xf.y, gf.y, ca, cb, na, nb, a1, b1);
+    dp[b * ih] = pair_from<T>(d0, d1);
+  };
+  int64_t b = r0;
+  for (; b + kRatRows <= r1; b += kRatRows) {
+    P2 xv[kRatRows], gv[kRatRows];
+#pragma unroll
+    for (int r = 0; r < kRatRows; ++r) {
+      xv[r] = xp[(b + r) * ih];
+      gv[r] = gp[(b + r) * ih];
+    }
+#pragma unroll
+    for (int r = 0; r < kRatRows; ++r) row(b + r, xv[r], gv[r]);
+  }
+  for (; b < r1; ++b) row(b, xp[b * ih], gp[b * ih]);
+  float* dst = ws + (size_t)blockIdx.x * w * I + i0;
+#pragma unroll
+  for (int j = 0; j < MA; ++j)
+    if (j < na) *reinterpret_cast<float2*>(dst + (size_t)j * I) = make_float2(a0[j], a1[j]);
+#pragma unroll
+  for (int j = 0; j < MB; ++j)
+    if (j < nb) *reinterpret_cast<float2*>(dst + (size_t)(na + j) * I) = make_float2(b0[j], b1[j]);
+}
+
+// dnum[g, j], dden[g, j] = sum over row blocks and the inputs of group g, in a
+// fixed order (row block major, then input), so the result is deterministic.
 __global__ void __launch_bounds__(kRatThreads) rational_reduce_kernel(const float* __restrict__ ws, float* __restrict__ dnum,
                                                                       float* __restrict__ dden, int nblk, int I, RatParams p) {
   __shared__ float red[kRatThreads];
@@ -144,7 +293,7 @@ __global__ void __launch_bounds__(kRatThreads) rational_reduce_kernel(const floa
   float acc = 0.0f;
   for (int e = threadIdx.x; e < n; e += blockDim.x) {
     const int blk = e / p.in_per_group, ii = e % p.in_per_group;
-    acc += ws[((size_t)blk * I + g * p.in_per_group + ii) * w + c];
+    acc += ws[((size_t)blk * w + c) * I + g * p.in_per_group + ii];
   }
   red[threadIdx.x] = acc;
   __syncthreads();
@@ -155,6 +304,62 @@ __global__ void __launch_bounds__(kRatThreads) rational_reduce_kernel(const floa
   if (threadIdx.x == 0) {
     if (c < p.na) dnum[g * p.na + c] = red[0];
     else dden[g * p.nb + (c - p.na)] = red[0];
+  }
+}
+
+bool aligned_to(const void* q, size_t n) { return ((uintptr_t)q % n) == 0; }
+
+// The backward kernel for one dtype: pairs of inputs for the degrees of the
+// GR-KAN default (5, 4) where the layout allows, else one input per thread.
+template <typename T>
+void launch_rational_bwd(int64_t used, int I, size_t smem, cudaStream_t s, const T* x, const T* dr, const float* num,
+                         const float* den, T* dx, float* ws, int64_t B, int64_t rows, const RatParams& p) {
+  const dim3 grid((unsigned)used, (unsigned)cdiv((int64_t)I, (int64_t)kRatThreads));
+  const size_t two = 2 * sizeof(T);
+  if (p.na == 6 && p.nb == 4 && p.in_per_group % 2 == 0 && aligned_to(x, two) && aligned_to(dr, two) &&
+      aligned_to(dx, two) && aligned_to(ws, 2 * sizeof(float))) {
+    rational_bwd_vec_kernel<T, 6, 4><<<grid, kRatVecThreads, smem, s>>>(x, dr, num, den, dx, ws, B, I, rows, p);
+  } else {
+    rational_bwd_kernel<T><<<grid, kRatThreads, smem, s>>>(x, dr, num, den, dx, ws, B, I, rows, p);
+  }
+}
+
+// CTAs of Kern that fit the GPU at once (queried once per kernel).
+template <auto Kern>
+int64_t resident_ctas(int threads, size_t smem, int64_t fallback) {
+  static std::atomic<int64_t> cached{0};
+  int64_t n = cached.load();
+  if (n > 0) return n;
+  int dev = 0, sms = 0, per_sm = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, Kern, threads, smem) != cudaSuccess || sms * per_sm <= 0) {
+    (void)cudaGetLastError();
+    return fallback;
+  }
+  n = (int64_t)sms * per_sm;
+  cached.store(n);
+  return n;
+}
+
+// The forward for one dtype: 16-byte vectors where the layout allows, one
+// wave of CTAs striding over the vectors.
+template <typename T>
+void launch_rational_act(int64_t B, int I, int m, size_t smem, cudaStream_t s, const T* x, const float* num,
+                         const float* den, T* out, const RatParams& p) {
+  constexpr int V = 16 / sizeof(T);
+  const int64_t n = B * I;
+  const int64_t nvec = n / V;
+  if (m == 0 && p.in_per_group % V == 0 && nvec < (int64_t(1) << 30) && aligned_to(x, 16) && aligned_to(out, 16)) {
+    const bool fixed = p.na == 6 && p.nb == 4;
+    auto kern = fixed ? rational_act_vec_kernel<T, 6, 4> : rational_act_vec_kernel<T, 0, 0>;
+    const int64_t wave = fixed ? resident_ctas<rational_act_vec_kernel<T, 6, 4>>(kRatThreads, smem, kRatWave)
+                               : resident_ctas<rational_act_vec_kernel<T, 0, 0>>(kRatThreads, smem, kRatWave);
+    const unsigned grid = (unsigned)std::min<int64_t>(cdiv(nvec, (int64_t)kRatThreads), wave);
+    kern<<<grid, kRatThreads, smem, s>>>(x, num, den, out, (uint32_t)nvec, (uint32_t)(I / V), (uint32_t)(p.in_per_group / V),
+                                         p);
+  } else {
+    const unsigned grid = (unsigned)std::min<int64_t>(cdiv(n, (int64_t)kRatThreads), kRatWave);
+    rational_act_kernel<T><<<grid, kRatThreads, smem, s>>>(x, num, den, out, n, I, m, p);
   }
 }
 
@@ -170,11 +375,11 @@ int rat_params(const kf_basis_desc* d, int I, RatParams& p) {
   return KF_OK;
 }
 
-// Row blocks of the backward: at least kRatMaxBlocks, more when I has few
-// 256-input chunks, so that the grid (row blocks x chunks) fills the GPU.
+// Row blocks of the backward: the grid (row blocks x 256-input chunks) is one
+// wave of the vector backward, each thread walking its block's rows.
 int64_t rat_blocks(int64_t B, int I) {
   const int64_t chunks = cdiv((int64_t)I, (int64_t)kRatThreads);
-  const int64_t target = std::max<int64_t>(kRatMaxBlocks, (148 * 8) / chunks);
+  const int64_t target = std::max<int64_t>(1, kRatBwdWave / chunks);
   return B <= 0 ? 1 : std::min<int64_t>(target, B);
 }
 
@@ -228,15 +433,12 @@ extern "C" int kf_rational_act(const void* x, const float* num, const float* den
   KF_CHECK_ARG(x && num && den && out && B >= 0 && m >= 0 && m <= KF_RAT_MAX_ORDER, "kf_rational_act: bad arguments");
   if (int rc = bind_device(x)) return rc;
   if (B == 0) return KF_OK;
-  const int64_t n = B * I;
   const size_t smem = sizeof(float) * p.groups * (p.na + p.nb);
-  const unsigned grid = (unsigned)std::min<int64_t>(cdiv(n, kRatThreads), 148 * 8);
   cudaStream_t s = (cudaStream_t)stream;
   if (dtype == KF_DTYPE_F32) {
-    rational_act_kernel<float><<<grid, kRatThreads, smem, s>>>((const float*)x, num, den, (float*)out, n, I, m, p);
+    launch_rational_act<float>(B, I, m, smem, s, (const float*)x, num, den, (float*)out, p);
   } else if (dtype == KF_DTYPE_BF16) {
-    rational_act_kernel<__nv_bfloat16><<<grid, kRatThreads, smem, s>>>((const __nv_bfloat16*)x, num, den,
-                                                                        (__nv_bfloat16*)out, n, I, m, p);
+    launch_rational_act<__nv_bfloat16>(B, I, m, smem, s, (const __nv_bfloat16*)x, num, den, (__nv_bfloat16*)out, p);
   } else {
     set_error("kf_rational_act: dtype %d unsupported", dtype);
     return KF_ERR_UNSUPPORTED;
@@ -264,11 +466,11 @@ extern "C" int kf_rational_bwd(const void* x, const void* dr, const float* num, 
   const int64_t used = cdiv(B, rows);
   const size_t smem = sizeof(float) * p.groups * (p.na + p.nb);
   if (dtype == KF_DTYPE_F32) {
-    rational_bwd_kernel<float><<<dim3((unsigned)used, (unsigned)cdiv(I, kRatThreads)), kRatThreads, smem, s>>>((const float*)x, (const float*)dr, num, den,
-                                                                         (float*)dx, workspace, B, I, rows, p);
+    launch_rational_bwd<float>(used, I, smem, s, (const float*)x, (const float*)dr, num, den, (float*)dx, workspace, B,
+                               rows, p);
   } else if (dtype == KF_DTYPE_BF16) {
-    rational_bwd_kernel<__nv_bfloat16><<<dim3((unsigned)used, (unsigned)cdiv(I, kRatThreads)), kRatThreads, smem, s>>>(
-        (const __nv_bfloat16*)x, (const __nv_bfloat16*)dr, num, den, (__nv_bfloat16*)dx, workspace, B, I, rows, p);
+    launch_rational_bwd<__nv_bfloat16>(used, I, smem, s, (const __nv_bfloat16*)x, (const __nv_bfloat16*)dr, num, den,
+                                       (__nv_bfloat16*)dx, workspace, B, rows, p);
   } else {
     set_error("kf_rational_bwd: dtype %d unsupported", dtype);
     return KF_ERR_UNSUPPORTED;
@@ -312,11 +514,11 @@ extern "C" int kf_rational_bwd_noalloc(const void* x, const void* dr, const floa
   const int64_t used = cdiv(B, rows);
   const size_t smem = sizeof(float) * p.groups * (p.na + p.nb);
   if (dtype == KF_DTYPE_F32) {
-    rational_bwd_kernel<float><<<dim3((unsigned)used, (unsigned)cdiv(I, kRatThreads)), kRatThreads, smem, s>>>((const float*)x, (const float*)dr, num, den,
-                                                                         (float*)dx, ws, B, I, rows, p);
+    launch_rational_bwd<float>(used, I, smem, s, (const float*)x, (const float*)dr, num, den, (float*)dx, ws, B,
+                               rows, p);
   } else if (dtype == KF_DTYPE_BF16) {
-    rational_bwd_kernel<__nv_bfloat16><<<dim3((unsigned)used, (unsigned)cdiv(I, kRatThreads)), kRatThreads, smem, s>>>(
-        (const __nv_bfloat16*)x, (const __nv_bfloat16*)dr, num, den, (__nv_bfloat16*)dx, ws, B, I, rows, p);
+    launch_rational_bwd<__nv_bfloat16>(used, I, smem, s, (const __nv_bfloat16*)x, (const __nv_bfloat16*)dr, num, den,
+                                       (__nv_bfloat16*)dx, ws, B, rows, p);
   } else {
     set_error("kf_rational_bwd_noalloc: dtype %d unsupported", dtype);
     return KF_ERR_UNSUPPORTED;

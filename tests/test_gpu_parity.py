@@ -409,6 +409,55 @@ def test_grkan_forward_and_gradients(dtype, tol):
         close(gr, want[key[nme]], tol if dtype == torch.float32 else 5e-2, f"d{nme}")
 
 
+# (B, I, groups, p, q, misaligned x): the vector kernels (16-byte forward, paired
+# backward for degrees (5, 4)), their row and chunk tails, and the one-element
+# kernels (odd inputs per group, other degrees, x one element off alignment).
+RATIONAL_CASES = [
+    (1003, 64, 8, 5, 4, False),
+    (4096, 768, 8, 5, 4, False),
+    (77, 320, 8, 5, 4, False),
+    (37, 24, 8, 5, 4, False),
+    (129, 64, 2, 3, 3, False),
+    (200, 520, 8, 5, 4, False),
+    (77, 64, 8, 5, 4, True),
+]
+
+
+@pytest.mark.parametrize("dtype,tol,ptol", [(torch.float32, FP32_TOL, FP32_TOL), (torch.bfloat16, BF16_TOL, 5e-2)])
+@pytest.mark.parametrize("n_b,n_in,groups,p,q,offset", RATIONAL_CASES)
+def test_rational_kernels_match_oracle_on_every_launch_path(n_b, n_in, groups, p, q, offset, dtype, tol, ptol):
+    g = torch.Generator(device="cpu").manual_seed(n_b + n_in)
+    a, b = kb.fit_rational("gelu", p, q)
+    num = torch.as_tensor(np.tile(a, (groups, 1)), dtype=torch.float32) + 0.05 * torch.randn(groups, p + 1, generator=g)
+    den = torch.as_tensor(np.tile(b, (groups, 1)), dtype=torch.float32) + 0.05 * torch.randn(groups, q, generator=g)
+    x0 = (torch.randn(n_b, n_in, generator=g) * 1.5).to(dtype)
+    dr = torch.randn(n_b, n_in, generator=g).to(dtype)
+    if offset:  # a view one element past an aligned allocation
+        buf = torch.empty(n_b * n_in + 1, device=DEV, dtype=dtype)
+        x = buf[1:].view(n_b, n_in)
+        x.copy_(x0)
+        assert x.data_ptr() % 16 != 0
+    else:
+        x = x0.to(DEV)
+    numd, dend = num.to(DEV).requires_grad_(), den.to(DEV).requires_grad_()
+    x.requires_grad_()
+    plan = kb.plan_for(kb.Rational(p, q))
+    r = kb.kernels.rational_act(x, numd, dend, plan, groups)
+    gx, gnum, gden = torch.autograd.grad(r, [x, numd, dend], dr.to(DEV))
+
+    xs = x0.double().numpy()
+    ipg = n_in // groups
+    num_i, den_i = np.repeat(num.double().numpy(), ipg, 0), np.repeat(den.double().numpy(), ipg, 0)
+    drs = dr.double().numpy()
+    close(r, ko.rational(xs, num_i, den_i, 0)[..., 0], tol, "R")
+    close(gx, drs * ko.rational(xs, num_i, den_i, 1)[..., 0], tol, "dx")
+    dn, dq = ko.rational_param_partials(xs, num_i, den_i)
+    want_n = (drs[..., None] * dn).sum(0).reshape(groups, ipg, p + 1).sum(1)
+    want_q = (drs[..., None] * dq).sum(0).reshape(groups, ipg, q).sum(1)
+    close(gnum, want_n, ptol, "dnum")
+    close(gden, want_q, ptol, "dden")
+
+
 def test_grkan_starts_as_gelu_and_keeps_variance():
     """reference tests/test_layers.py:84-96, on the CUDA kernels."""
     torch.manual_seed(0)
