@@ -59,18 +59,39 @@ __device__ __forceinline__ void load_rat_table(float* sp, const float* num, cons
   __syncthreads();
 }
 
-// R(x) = P(x) / (1 + |x Qs(x)|) by Horner, MA / MB steps with the ones at or
-// beyond na / nb skipped (compile-time when the kernel fixes the degrees).
+// The elementwise arithmetic below comes in two forms with the same sequence
+// of IEEE operations, so they give the same bits: one element (degrees up to
+// MA / MB, the steps at or beyond na / nb skipped) and a pair of elements in
+// float2 lanes (degrees fixed), two fp32 operations per instruction
+// (__ffma2_rn / __fmul2_rn / __fadd2_rn).  1 / D uses __fdividef (2 ulp;
+// D = 1 + |Q| >= 1 is far inside its range).
+
+__device__ __forceinline__ float rat_sign(float q) { return q > 0.0f ? 1.0f : (q < 0.0f ? -1.0f : 0.0f); }
+__device__ __forceinline__ float2 dup2(float v) { return make_float2(v, v); }
+__device__ __forceinline__ float2 neg2(float2 v) { return make_float2(-v.x, -v.y); }
+
+// R(x) = P(x) / (1 + |x Qs(x)|) by Horner.
 template <int MA, int MB>
 __device__ __forceinline__ float rat_value(float xv, const float* a, const float* bq, int na, int nb) {
-  float P = 0.0f, Qs = 0.0f;
+  float P = a[na - 1], Qs = bq[nb - 1];
 #pragma unroll
-  for (int j = MA - 1; j >= 0; --j)
-    if (j < na) P = P * xv + a[j];
+  for (int j = MA - 2; j >= 0; --j)
+    if (j < na - 1) P = fmaf(P, xv, a[j]);
 #pragma unroll
-  for (int j = MB - 1; j >= 0; --j)
-    if (j < nb) Qs = Qs * xv + bq[j];
-  return P / (1.0f + fabsf(xv * Qs));
+  for (int j = MB - 2; j >= 0; --j)
+    if (j < nb - 1) Qs = fmaf(Qs, xv, bq[j]);
+  return __fdividef(P, 1.0f + fabsf(xv * Qs));
+}
+
+template <int NA, int NB>
+__device__ __forceinline__ float2 rat_value2(float2 x, const float2 (&a)[NA], const float2 (&bq)[NB]) {
+  float2 P = a[NA - 1], Qs = bq[NB - 1];
+#pragma unroll
+  for (int j = NA - 2; j >= 0; --j) P = __ffma2_rn(P, x, a[j]);
+#pragma unroll
+  for (int j = NB - 2; j >= 0; --j) Qs = __ffma2_rn(Qs, x, bq[j]);
+  const float2 Q = __fmul2_rn(x, Qs);
+  return make_float2(__fdividef(P.x, 1.0f + fabsf(Q.x)), __fdividef(P.y, 1.0f + fabsf(Q.y)));
 }
 
 // One element of the backward: returns dx = g R'(x) and adds g dR/da_j,
@@ -79,42 +100,81 @@ __device__ __forceinline__ float rat_value(float xv, const float* a, const float
 template <int MA, int MB>
 __device__ __forceinline__ float rat_bwd_elem(float xv, float g, const float* a, const float* bq, int na, int nb,
                                               float (&acc_a)[MA], float (&acc_b)[MB]) {
-  float P = 0.0f, dP = 0.0f;
+  float P = a[na - 1], dP = 0.0f;
 #pragma unroll
-  for (int j = MA - 1; j >= 0; --j) {
-    if (j < na) {
-      dP = dP * xv + P;
-      P = P * xv + a[j];
+  for (int j = MA - 2; j >= 0; --j) {
+    if (j < na - 1) {
+      dP = fmaf(dP, xv, P);
+      P = fmaf(P, xv, a[j]);
     }
   }
-  float Qs = 0.0f, dQs = 0.0f;
+  float Qs = bq[nb - 1], dQs = 0.0f;
 #pragma unroll
-  for (int j = MB - 1; j >= 0; --j) {
-    if (j < nb) {
-      dQs = dQs * xv + Qs;
-      Qs = Qs * xv + bq[j];
+  for (int j = MB - 2; j >= 0; --j) {
+    if (j < nb - 1) {
+      dQs = fmaf(dQs, xv, Qs);
+      Qs = fmaf(Qs, xv, bq[j]);
     }
   }
   const float Q = xv * Qs;
-  const float dQ = Qs + xv * dQs;
-  const float sg = Q > 0.0f ? 1.0f : (Q < 0.0f ? -1.0f : 0.0f);
-  const float rD = 1.0f / (1.0f + fabsf(Q));
+  const float dQ = fmaf(xv, dQs, Qs);
+  const float sg = rat_sign(Q);
+  const float rD = __fdividef(1.0f, 1.0f + fabsf(Q));
   const float R = P * rD;
   const float u = g * rD;
-  float xp = 1.0f;
+  acc_a[0] += u;
+  float xp = xv;
 #pragma unroll
-  for (int j = 0; j < MA; ++j) {
+  for (int j = 1; j < MA; ++j) {
     if (j < na) acc_a[j] = fmaf(u, xp, acc_a[j]);
     xp *= xv;
   }
-  const float v = -u * R * sg;
+  const float v = (-u * R) * sg;
   xp = xv;
 #pragma unroll
   for (int j = 0; j < MB; ++j) {
     if (j < nb) acc_b[j] = fmaf(v, xp, acc_b[j]);
     xp *= xv;
   }
-  return g * ((dP - sg * dQ * R) * rD);
+  return g * (fmaf(-(sg * dQ), R, dP) * rD);
+}
+
+template <int NA, int NB>
+__device__ __forceinline__ float2 rat_bwd_pair(float2 x, float2 g, const float2 (&a)[NA], const float2 (&bq)[NB],
+                                               float2 (&acc_a)[NA], float2 (&acc_b)[NB]) {
+  float2 P = a[NA - 1], dP = make_float2(0.0f, 0.0f);
+#pragma unroll
+  for (int j = NA - 2; j >= 0; --j) {
+    dP = __ffma2_rn(dP, x, P);
+    P = __ffma2_rn(P, x, a[j]);
+  }
+  float2 Qs = bq[NB - 1], dQs = make_float2(0.0f, 0.0f);
+#pragma unroll
+  for (int j = NB - 2; j >= 0; --j) {
+    dQs = __ffma2_rn(dQs, x, Qs);
+    Qs = __ffma2_rn(Qs, x, bq[j]);
+  }
+  const float2 Q = __fmul2_rn(x, Qs);
+  const float2 dQ = __ffma2_rn(x, dQs, Qs);
+  const float2 sg = make_float2(rat_sign(Q.x), rat_sign(Q.y));
+  const float2 rD = make_float2(__fdividef(1.0f, 1.0f + fabsf(Q.x)), __fdividef(1.0f, 1.0f + fabsf(Q.y)));
+  const float2 R = __fmul2_rn(P, rD);
+  const float2 u = __fmul2_rn(g, rD);
+  acc_a[0] = __fadd2_rn(acc_a[0], u);
+  float2 xp = x;
+#pragma unroll
+  for (int j = 1; j < NA; ++j) {
+    acc_a[j] = __ffma2_rn(u, xp, acc_a[j]);
+    xp = __fmul2_rn(xp, x);
+  }
+  const float2 v = __fmul2_rn(__fmul2_rn(neg2(u), R), sg);
+  xp = x;
+#pragma unroll
+  for (int j = 0; j < NB; ++j) {
+    acc_b[j] = __ffma2_rn(v, xp, acc_b[j]);
+    xp = __fmul2_rn(xp, x);
+  }
+  return __fmul2_rn(g, __fmul2_rn(__ffma2_rn(neg2(__fmul2_rn(sg, dQ)), R, dP), rD));
 }
 
 // Forward (and PINN derivatives): one element per thread, any layout.
@@ -137,48 +197,54 @@ __global__ void __launch_bounds__(kRatThreads) rational_act_kernel(const T* __re
 }
 
 // Forward R(x) on 16-byte vectors (8 bf16 / 4 float32 elements of one group):
-// nvec vectors, ivec per row, vpg per group, two vectors per thread in flight.
+// nvec vectors, ivec per row, vpg per group, four vectors per thread in flight.
 // NA = NB = 0: degrees from p (up to the kernel limits).
 template <typename T, int NA, int NB>
 __global__ void __launch_bounds__(kRatThreads) rational_act_vec_kernel(const T* __restrict__ x, const float* __restrict__ num,
                                                                        const float* __restrict__ den, T* __restrict__ out,
                                                                        uint32_t nvec, uint32_t ivec, uint32_t vpg,
                                                                        RatParams p) {
-  constexpr int MA = NA > 0 ? NA : KF_RAT_MAX_NUM;
-  constexpr int MB = NB > 0 ? NB : KF_RAT_MAX_DEN;
   constexpr int V = 16 / sizeof(T);
   struct __align__(16) Vec {
     T e[V];
   };
   extern __shared__ float sp[];
   load_rat_table(sp, num, den, p);
-  const int na = NA > 0 ? NA : p.na, nb = NB > 0 ? NB : p.nb;
   const int w = p.na + p.nb;
   const Vec* xv = reinterpret_cast<const Vec*>(x);
   Vec* ov = reinterpret_cast<Vec*>(out);
   auto eval = [&](const Vec& in, uint32_t v) {
     const float* th = sp + ((v % ivec) / vpg) * w;
-    float ca[MA], cb[MB];
-#pragma unroll
-    for (int j = 0; j < MA; ++j) ca[j] = j < na ? th[j] : 0.0f;
-#pragma unroll
-    for (int j = 0; j < MB; ++j) cb[j] = j < nb ? th[na + j] : 0.0f;
     Vec r;
+    if constexpr (NA > 0) {  // pairs of elements in float2 lanes
+      float2 ca[NA], cb[NB];
 #pragma unroll
-    for (int k = 0; k < V; ++k) r.e[k] = from_f32<T>(rat_value<MA, MB>(to_f32(in.e[k]), ca, cb, na, nb));
+      for (int j = 0; j < NA; ++j) ca[j] = dup2(th[j]);
+#pragma unroll
+      for (int j = 0; j < NB; ++j) cb[j] = dup2(th[NA + j]);
+#pragma unroll
+      for (int k = 0; k < V; k += 2) {
+        const float2 y = rat_value2(make_float2(to_f32(in.e[k]), to_f32(in.e[k + 1])), ca, cb);
+        r.e[k] = from_f32<T>(y.x);
+        r.e[k + 1] = from_f32<T>(y.y);
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < V; ++k)
+        r.e[k] = from_f32<T>(rat_value<KF_RAT_MAX_NUM, KF_RAT_MAX_DEN>(to_f32(in.e[k]), th, th + p.na, p.na, p.nb));
+    }
     ov[v] = r;
   };
+  constexpr int kIn = 4;  // vectors per thread in flight
   const uint32_t stride = gridDim.x * blockDim.x;
-  for (uint32_t v = blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += 2 * stride) {
-    const uint32_t v1 = v + stride;
-    const Vec a0 = xv[v];
-    if (v1 < nvec) {
-      const Vec a1 = xv[v1];
-      eval(a0, v);
-      eval(a1, v1);
-    } else {
-      eval(a0, v);
-    }
+  for (uint32_t v = blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += kIn * stride) {
+    Vec in[kIn];
+#pragma unroll
+    for (int k = 0; k < kIn; ++k)
+      if (v + k * stride < nvec) in[k] = xv[v + k * stride];
+#pragma unroll
+    for (int k = 0; k < kIn; ++k)
+      if (v + k * stride < nvec) eval(in[k], v + k * stride);
   }
 }
 
@@ -221,8 +287,8 @@ __global__ void __launch_bounds__(kRatThreads) rational_bwd_kernel(const T* __re
 
 // Pairs of inputs (in_per_group even, x / dr / dx aligned to two elements, ws
 // to two floats):
-// one bf16x2 / float2 load of x and of dr per row, kRatRows rows' loads in
-// flight before their arithmetic, the degrees fixed at compile time (the
+// one bf16x2 / float2 load of x and of dr per row, loaded kRatRows rows at a
+// time one group ahead of the arithmetic, the degrees fixed at compile time (the
 // accumulators of both inputs and the coefficients stay in registers).
 template <typename T, int NA, int NB>
 __global__ void __launch_bounds__(kRatVecThreads, 6) rational_bwd_vec_kernel(
@@ -235,19 +301,19 @@ __global__ void __launch_bounds__(kRatVecThreads, 6) rational_bwd_vec_kernel(
   load_rat_table(sp, num, den, p);
   const int i0 = blockIdx.y * (2 * kRatVecThreads) + 2 * threadIdx.x;
   if (i0 >= I) return;
-  constexpr int na = NA, nb = NB;
   const int w = p.na + p.nb;
   const float* th = sp + (i0 / p.in_per_group) * w;
-  float ca[MA], cb[MB], a0[MA], a1[MA], b0[MB], b1[MB];
+  // coefficients duplicated into both lanes; accumulators (input i0, i0 + 1)
+  float2 ca[MA], cb[MB], acc_a[MA], acc_b[MB];
 #pragma unroll
   for (int j = 0; j < MA; ++j) {
-    ca[j] = j < na ? th[j] : 0.0f;
-    a0[j] = a1[j] = 0.0f;
+    ca[j] = dup2(th[j]);
+    acc_a[j] = make_float2(0.0f, 0.0f);
   }
 #pragma unroll
   for (int j = 0; j < MB; ++j) {
-    cb[j] = j < nb ? th[na + j] : 0.0f;
-    b0[j] = b1[j] = 0.0f;
+    cb[j] = dup2(th[MA + j]);
+    acc_b[j] = make_float2(0.0f, 0.0f);
   }
   const int64_t ih = I / 2;
   const P2* xp = reinterpret_cast<const P2*>(x) + i0 / 2;
@@ -256,10 +322,8 @@ __global__ void __launch_bounds__(kRatVecThreads, 6) rational_bwd_vec_kernel(
   const int64_t r0 = (int64_t)blockIdx.x * rows_per_blk;
   const int64_t r1 = min(B, r0 + rows_per_blk);
   auto row = [&](int64_t b, P2 xv2, P2 gv2) {
-    const float2 xf = pair_f32(xv2), gf = pair_f32(gv2);
-    const float d0 = rat_bwd_elem(xf.x, gf.x, ca, cb, na, nb, a0, b0);
-    const float d1 = rat_bwd_elem(xf.y, gf.y, ca, cb, na, nb, a1, b1);
-    dp[b * ih] = pair_from<T>(d0, d1);
+    const float2 d = rat_bwd_pair(pair_f32(xv2), pair_f32(gv2), ca, cb, acc_a, acc_b);
+    dp[b * ih] = pair_from<T>(d.x, d.y);
   };
   int64_t b = r0;
   for (; b + kRatRows <= r1; b += kRatRows) {
@@ -275,11 +339,9 @@ __global__ void __launch_bounds__(kRatVecThreads, 6) rational_bwd_vec_kernel(
   for (; b < r1; ++b) row(b, xp[b * ih], gp[b * ih]);
   float* dst = ws + (size_t)blockIdx.x * w * I + i0;
 #pragma unroll
-  for (int j = 0; j < MA; ++j)
-    if (j < na) *reinterpret_cast<float2*>(dst + (size_t)j * I) = make_float2(a0[j], a1[j]);
+  for (int j = 0; j < MA; ++j) *reinterpret_cast<float2*>(dst + (size_t)j * I) = acc_a[j];
 #pragma unroll
-  for (int j = 0; j < MB; ++j)
-    if (j < nb) *reinterpret_cast<float2*>(dst + (size_t)(na + j) * I) = make_float2(b0[j], b1[j]);
+  for (int j = 0; j < MB; ++j) *reinterpret_cast<float2*>(dst + (size_t)(MA + j) * I) = acc_b[j];
 }
 
 // dnum[g, j], dden[g, j] = sum over row blocks and the inputs of group g, in a
@@ -349,7 +411,7 @@ void launch_rational_act(int64_t B, int I, int m, size_t smem, cudaStream_t s, c
   constexpr int V = 16 / sizeof(T);
   const int64_t n = B * I;
   const int64_t nvec = n / V;
-  if (m == 0 && p.in_per_group % V == 0 && nvec < (int64_t(1) << 30) && aligned_to(x, 16) && aligned_to(out, 16)) {
+  if (m == 0 && p.in_per_group % V == 0 && nvec < (int64_t(1) << 29) && aligned_to(x, 16) && aligned_to(out, 16)) {
     const bool fixed = p.na == 6 && p.nb == 4;
     auto kern = fixed ? rational_act_vec_kernel<T, 6, 4> : rational_act_vec_kernel<T, 0, 0>;
     const int64_t wave = fixed ? resident_ctas<rational_act_vec_kernel<T, 6, 4>>(kRatThreads, smem, kRatWave)

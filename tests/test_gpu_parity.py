@@ -415,6 +415,8 @@ def test_grkan_forward_and_gradients(dtype, tol):
 RATIONAL_CASES = [
     (1003, 64, 8, 5, 4, False),
     (4096, 768, 8, 5, 4, False),
+    (20000, 256, 8, 5, 4, False),
+    (3, 64, 8, 5, 4, False),
     (77, 320, 8, 5, 4, False),
     (37, 24, 8, 5, 4, False),
     (129, 64, 2, 3, 3, False),
