@@ -1200,16 +1200,23 @@ __global__ void __launch_bounds__(256) feature_cheb_kernel(const __nv_bfloat16* 
 // B-splines: a CTA owns 32 consecutive inputs and stages their knot tables in
 // shared memory once (rows of ts >= nk floats, each lane's table at an odd
 // stride so that the 32 lanes, one input each, read without bank conflicts);
-// its warps walk the rows, each lane evaluating one (row, input) once (knot
-// search and Cox-de Boor from the table).  Warp shuffles then regroup the
-// F / 8 chunks of the 32 rows of features so that each store instruction
-// writes 512 contiguous bytes.
+// its warps walk the rows, kSplineRows rows' x loaded together, each lane
+// evaluating one (row, input) once (knot search and Cox-de Boor from the
+// table).  The BK + 1 non-zero values of a row start at feature s = j0 - BK:
+// packed as bf16 pairs from an even position, a funnel shift by 16 bits moves
+// them to an odd one, and the NW words they touch are placed among the row's
+// F / 2 words; silu(x) is the high half of the last word.  Each lane stores
+// its own row (F / 8 16-byte chunks).
+constexpr int kSplineRows = 4;
+
+__device__ __forceinline__ uint32_t bf16_bits(float v) { return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v)); }
+
 template <int BK, int F>
 __global__ void __launch_bounds__(256) feature_spline_kernel(const __nv_bfloat16* __restrict__ x,
                                                              __nv_bfloat16* __restrict__ feat, int64_t B, int I, BasisDev bd,
                                                              int ts) {
-  constexpr int CH = F / 8;
-  extern __shared__ float tabs[];  // [32][ls]
+  constexpr int NW = (BK + 3) / 2;  // words that BK + 1 consecutive bf16 values can touch
+  extern __shared__ float tabs[];   // [32][ls]
   const int ls = (BK + 1) * ts + 1;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int i0 = blockIdx.y * 32;
@@ -1220,50 +1227,57 @@ __global__ void __launch_bounds__(256) feature_spline_kernel(const __nv_bfloat16
   }
   __syncthreads();
   const int i = i0 + lane;
-  const bool in_ok = i < I;
+  if (i >= I) return;
   const float* tu = tabs + lane * ls;
-  for (int64_t b = (int64_t)blockIdx.x * 8 + warp; b < B; b += (int64_t)gridDim.x * 8) {
-    float f[F];
+  const int64_t stride = (int64_t)gridDim.x * 8;
+  for (int64_t b0 = (int64_t)blockIdx.x * 8 + warp; b0 < B; b0 += kSplineRows * stride) {
+    float xs[kSplineRows];
 #pragma unroll
-    for (int j = 0; j < F; ++j) f[j] = 0.0f;
-    if (in_ok) {
-      const float xv = __bfloat162float(x[b * I + i]);
-      const int j0 = knot_interval(xv, tu, bd.nk);
-      float vv[BK + 1];
-#pragma unroll
-      for (int rp = 0; rp <= BK; ++rp) vv[rp] = 0.0f;
-      if (j0 >= 0) bspline_local_tab<BK>(xv, tu, bd.nk, j0, 0, vv, ts);
-#pragma unroll
-      for (int j = 0; j < F; ++j) {
-        float val = 0.0f;
-#pragma unroll
-        for (int rp = 0; rp <= BK; ++rp)
-          if (j == j0 - BK + rp) val = vv[rp];
-        f[j] = j < bd.nt ? val : 0.0f;
-      }
-      f[F - 1] = bd.has_base ? silu_fast(xv) : 0.0f;
+    for (int u = 0; u < kSplineRows; ++u) {
+      const int64_t b = b0 + u * stride;
+      xs[u] = b < B ? __bfloat162float(x[b * I + i]) : 0.0f;
     }
-    uint32_t w[F / 2];  // the row as bf16 pairs
 #pragma unroll
-    for (int k = 0; k < F / 2; ++k) w[k] = pack_bf16x2(f[2 * k], f[2 * k + 1]);
-    const int q = lane % CH;  // chunk this lane stores
+    for (int u = 0; u < kSplineRows; ++u) {
+      const int64_t b = b0 + u * stride;
+      if (b >= B) break;
+      const float xv = xs[u];
+      uint32_t wd[F / 2];
 #pragma unroll
-    for (int s2 = 0; s2 < CH; ++s2) {
-      const int src = s2 * (32 / CH) + lane / CH;  // input (lane) whose chunk q this lane stores
-      uint32_t v[4] = {0u, 0u, 0u, 0u};
+      for (int k = 0; k < F / 2; ++k) wd[k] = 0u;
+      const int j0 = knot_interval(xv, tu, bd.nk);
+      if (j0 >= 0) {
+        float vv[BK + 1];
+        bspline_local_tab<BK>(xv, tu, bd.nk, j0, 0, vv, ts);
+        const int s0 = j0 - BK;
+        uint32_t h[2 * NW];
 #pragma unroll
-      for (int k = 0; k < F / 2; ++k) {
-        const uint32_t t = __shfl_sync(0xffffffffu, w[k], src);
-        if (k / 4 == q) v[k % 4] = t;
+        for (int rp = 0; rp < 2 * NW; ++rp) {
+          const int j = s0 + rp;
+          h[rp] = (rp <= BK && j >= 0 && j < bd.nt) ? bf16_bits(vv[rp <= BK ? rp : 0]) : 0u;
+        }
+        const int par = s0 & 1, a = s0 >> 1;  // word a holds feature 2a (floor for s0 < 0)
+        uint32_t w[NW];
+#pragma unroll
+        for (int m = 0; m < NW; ++m) {
+          const uint32_t e = h[2 * m] | (h[2 * m + 1] << 16);
+          const uint32_t ep = m > 0 ? (h[2 * m - 2] | (h[2 * m - 1] << 16)) : 0u;
+          w[m] = par ? __funnelshift_l(ep, e, 16) : e;
+        }
+#pragma unroll
+        for (int k = 0; k < F / 2; ++k) {
+          const int m = k - a;
+          uint32_t v = 0u;
+#pragma unroll
+          for (int mm = 0; mm < NW; ++mm)
+            if (m == mm) v = w[mm];
+          wd[k] = v;
+        }
       }
-      if (i0 + src < I) {
-        uint4 pk;
-        pk.x = v[0];
-        pk.y = v[1];
-        pk.z = v[2];
-        pk.w = v[3];
-        reinterpret_cast<uint4*>(feat + (b * I + i0 + src) * F)[q] = pk;
-      }
+      if (bd.has_base) wd[F / 2 - 1] |= bf16_bits(silu_fast(xv)) << 16;
+      uint4* dst = reinterpret_cast<uint4*>(feat + (b * I + i) * F);
+#pragma unroll
+      for (int c = 0; c < F / 8; ++c) dst[c] = make_uint4(wd[4 * c], wd[4 * c + 1], wd[4 * c + 2], wd[4 * c + 3]);
     }
   }
 }

@@ -268,6 +268,10 @@ FUSED_CASES = [
     (kb.BSpline(5, 3, (-2.0, 2.0)), 1030, 16, 520, True, True, False),
     (kb.BSpline(4, 1), 64, 8, 8, True, True, False),
     (kb.Chebyshev(4, input_map="identity"), 77, 12, 40, True, True, False),
+    (kb.BSpline(6, 2), 200, 24, 72, True, True, False),
+    (kb.BSpline(4, 4), 99, 10, 16, False, True, False),
+    (kb.BSpline(7, 5), 150, 20, 48, True, False, False),
+    (kb.BSpline(20, 3), 140, 12, 40, True, True, False),       # f_pad 32
 ]
 
 
@@ -313,7 +317,7 @@ def test_bf16_fused_layer_forward_and_gradients(basis, n_b, n_in, n_out, base, b
         close(gr, want[key[nme]], BF16_TOL, f"d{nme}")
 
 
-@pytest.mark.parametrize("case", [0, 1, 3, 5, 7])
+@pytest.mark.parametrize("case", [0, 1, 3, 5, 6, 7, 8, 9, 10, 11])
 def test_bf16_wgrad_feature_matrix_path_equals_self_evaluating_path(monkeypatch, case):
     """kf_wgrad (and, for B-splines, kf_fwd) reading the kf_features matrix by
     TMA and the same kernels evaluating the features themselves (no feature
