@@ -20,7 +20,7 @@ namespace {
 
 constexpr int kRatThreads = 256;
 constexpr int kRatVecThreads = 128;  // vector backward: two adjacent inputs per thread, 256 per CTA
-constexpr int kRatRows = 4;          // rows whose loads one thread of the vector backward has in flight
+constexpr int kRatRows = 8;          // rows whose loads one thread of the vector backward has in flight
 constexpr int kRatWave = 148 * 8;    // CTA cap of the forward grid (148 SMs x 8)
 constexpr int kRatBwdWave = 148 * 6; // CTAs of one wave of the vector backward (148 SMs x 6 resident)
 
