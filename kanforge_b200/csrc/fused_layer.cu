@@ -76,6 +76,7 @@ struct Ctl {
   uint32_t tmem_base;
   int abort;
 };
+static_assert(sizeof(Ctl) % 16 == 0, "the shared memory after Ctl must stay 16-byte aligned");
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
@@ -84,6 +85,18 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
 __device__ __forceinline__ void named_bar(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
+
+// 16-byte asynchronous global -> shared copy (zero-filled when !valid) and
+// the wait for all of this thread's copies.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
+  const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+
+// Largest power of two <= n (n >= 1): the first step of the fixed-step knot search.
+__device__ __forceinline__ int pow2_floor(int n) { return 1 << (31 - __clz(n)); }
 
 // Knot table of one input (kTabStride floats per row): row 0 = extended knots
 // t_r (r < nk), row q = 1 / (t_{r+q} - t_r) for r <= nk - 1 - q; zero elsewhere.
@@ -117,7 +130,7 @@ __device__ __forceinline__ void drain_tma(Ctl* ctl, int issued) {
 
 // Cox-de Boor / derivative levels of bspline_local (basis.cuh) with the
 // reciprocal knot differences read from the table.
-template <int K>
+template <int K, int ES = 1>
 __device__ __forceinline__ void bspline_local_tab(float x, const float* tab, int nk, int j, int m, float (&v)[K + 1],
                                                   int ts = kTabStride) {
   const float* t = tab;
@@ -136,8 +149,8 @@ __device__ __forceinline__ void bspline_local_tab(float x, const float* tab, int
       const float right = rp <= q - 1 ? v[rp] : 0.0f;
       float out = 0.0f;
       if (r >= 0 && r <= nk - 2 - q) {
-        const float i1 = inv[r], i2 = inv[r + 1];
-        out = deriv ? (float)q * (left * i1 - right * i2) : (x - t[r]) * i1 * left + (t[r + q + 1] - x) * i2 * right;
+        const float i1 = inv[r * ES], i2 = inv[(r + 1) * ES];
+        out = deriv ? (float)q * (left * i1 - right * i2) : (x - t[r * ES]) * i1 * left + (t[(r + q + 1) * ES] - x) * i2 * right;
       }
       nv[rp] = out;
     }
@@ -516,11 +529,16 @@ struct DgradParams {
   int64_t B;
   int I, O;
   int k_steps;
+  int tab_ts;  // B-spline: row stride of the staged knot tables (nk rounded up to 4)
   TileMap tiles;
   BasisDev bd;
 };
 
-constexpr int kDgradThreads = 384;  // w0 TMA, w1 MMA (CTA 0), w4-11 epilogue (two sets of four)
+// Threads of the input-gradient kernel: w0 TMA, w1 MMA (CTA 0), then the
+// epilogue warps from w4 on: two sets of four for Chebyshev features, four
+// sets of four for B-splines (whose per-input derivative windows are the
+// epilogue's main cost).
+constexpr int dgrad_threads(int bk) { return bk > 0 ? 640 : 384; }
 
 // The input gradient runs on CTA pairs: a tile is 256 tokens x 256 feature
 // columns, CTA r loads dy rows 128 r .. 128 r + 127 (its half of A) and
@@ -528,17 +546,19 @@ constexpr int kDgradThreads = 384;  // w0 TMA, w1 MMA (CTA 0), w4-11 epilogue (t
 // 0's barrier, and each CTA's epilogue contracts its own 128 accumulator rows
 // with the derivative features.
 template <int BK, int F>
-__global__ void __launch_bounds__(kDgradThreads, 1) fused_dgrad_kernel(const __grid_constant__ CUtensorMap tmap_dy,
-                                                                       const __grid_constant__ CUtensorMap tmap_c, DgradParams p) {
+__global__ void __launch_bounds__(dgrad_threads(BK), 1) fused_dgrad_kernel(const __grid_constant__ CUtensorMap tmap_dy,
+                                                                           const __grid_constant__ CUtensorMap tmap_c, DgradParams p) {
   constexpr int IPT = kBN / F;  // inputs per tile
+  constexpr int kEpiWarps = dgrad_threads(BK) / 32 - 4;
+  constexpr int kEpiThreads = 32 * kEpiWarps;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = align1024(smem_raw);
   uint8_t* sa = base;
   uint8_t* sb = sa + kStages * kATile;                  // kStages x 16 KB (this CTA's half of B)
   Ctl* ctl = reinterpret_cast<Ctl*>(sb + kStages * kBHalf);
-  float* xsm = reinterpret_cast<float*>(ctl + 1);       // x of each row's tile inputs [128][IPT + 1]
-  float* tabs = xsm + kBM * (IPT + 1);                  // B-spline knot tables [IPT][(BK+1) * 64]
-  float* stage = tabs + IPT * (BK + 1) * kTabStride;    // B-spline: per epilogue warp [32][33]
+  float* xsm = reinterpret_cast<float*>(ctl + 1);       // Chebyshev: x of each row's tile inputs [128][IPT + 1]
+  float* tabs = reinterpret_cast<float*>(ctl + 1);      // B-spline: knot tables [2][IPT][BK+1][tab_ts]
+  float* stage = tabs + 2 * IPT * (BK + 1) * p.tab_ts;  // B-spline: per epilogue warp [32][F + 1]
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const uint32_t rank = cluster_ctarank();
   const int pair = blockIdx.x / 2, n_pairs = gridDim.x / 2;
@@ -551,7 +571,7 @@ __global__ void __launch_bounds__(kDgradThreads, 1) fused_dgrad_kernel(const __g
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&ctl->acc_full[a], 1);
-      mbar_init(&ctl->acc_empty[a], 16);  // 8 epilogue warps of each CTA (used in CTA 0)
+      mbar_init(&ctl->acc_empty[a], 2 * kEpiWarps);  // the epilogue warps of both CTAs (used in CTA 0)
     }
     mbar_init(&ctl->drain, 1);
     ctl->abort = 0;
@@ -639,129 +659,263 @@ __global__ void __launch_bounds__(kDgradThreads, 1) fused_dgrad_kernel(const __g
       mbar_drain(&ctl->drain, 0);
     }
   } else if (warp >= 4) {
-    // Two sets of four warps: set h2 reads TMEM lane quarter q (rows 32 q ..) of
-    // column chunks 4 h2 .. 4 h2 + 3, i.e. the inputs IPT/2 h2 .. of the tile,
-    // and writes those inputs' dx.
-    constexpr int kHalfIn = IPT / 2;
-    const int q = (warp - 4) % 4, h2 = (warp - 4) / 4;
-    const int row = q * 32 + lane;
-    const int etid = (warp - 4) * 32 + lane;  // 0 .. 255
-    float* wst = stage + (warp - 4) * (32 * 33);
-    int tc = 0;
-    for (int t = pair; t < n_tiles; t += n_pairs, ++tc) {
-      int m, n;
-      p.tiles.get(t, m, n);
-      const int i_base = n * IPT;
-      const int acc = tc & 1;
-      bool ok = mbar_wait_warp(&ctl->acc_full[acc], (tc >> 1) & 1, abort);
-      if constexpr (BK > 0) {
-        // all eight warps are past the previous tile (its table readers are done) and agree
-        ok = named_bar_and(1, 256, ok);
-        if (ok) {
-          constexpr int kTab = (BK + 1) * kTabStride;  // knots and reciprocal differences of one input
-          for (int e = etid; e < IPT * kTab; e += 256) {
-            const int u = e / kTab, r = e % kTab;
-            tabs[e] = (i_base + u < p.I) ? __ldg(p.bd.tab + (size_t)(i_base + u) * kTab + r) : 0.0f;
-          }
-        }
-        named_bar(1, 256);
-      }
-      if (!ok) break;
-      tc_fence_after();
-      const int64_t b = (int64_t)m * kPairM + (int64_t)rank * kBM + row;
-      const bool row_ok = b < p.B;
-      // this row's x for this set's inputs, loaded once (4-byte loads when aligned)
-      const int u0 = h2 * kHalfIn;
-      float* xr = xsm + row * (IPT + 1);
-      if (row_ok && i_base + u0 + kHalfIn <= p.I && ((p.I | i_base) % 2) == 0) {
-        const uint32_t* src = reinterpret_cast<const uint32_t*>(p.x + b * p.I + i_base + u0);
-#pragma unroll
-        for (int k2 = 0; k2 < kHalfIn / 2; ++k2) {
-          const uint32_t wv = __ldg(src + k2);
-          xr[u0 + 2 * k2] = __uint_as_float(wv << 16);
-          xr[u0 + 2 * k2 + 1] = __uint_as_float(wv & 0xffff0000u);
-        }
-      } else {
-        for (int u = u0; u < u0 + kHalfIn; ++u)
-          xr[u] = (row_ok && i_base + u < p.I) ? __bfloat162float(p.x[b * p.I + i_base + u]) : 0.0f;
-      }
-      float dxv[IPT];
-#pragma unroll 1
-      for (int c = 4 * h2; c < 4 * h2 + 4; ++c) {
-        float v[32];
-        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + acc * kBN + c * 32, v);
-        if (c == 4 * h2 + 3) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(&ctl->acc_empty[acc], 0);
-        }
-        if constexpr (BK == 0) {
-#pragma unroll
-          for (int h = 0; h < 32 / F + (F > 32 ? 1 : 0); ++h) {
-            // F == 16: two inputs per chunk; F == 32: one input per chunk
-            const int u = (c * 32) / F + h;
-            const float xval = xr[u];
-            float df[F];
-            cheb_drow<F>(xval, p.bd, df);
-            float s = 0.0f;
-#pragma unroll
-            for (int j = 0; j < F; ++j) s = fmaf(v[h * F + j], df[j], s);
-#pragma unroll
-            for (int uu = 0; uu < IPT; ++uu)
-              if (uu == u) dxv[uu] = s;
-          }
-        } else {
-          // stage the 32 columns of this row, then dot with the local derivative window
-#pragma unroll
-          for (int j = 0; j < 32; ++j) wst[lane * 33 + j] = v[j];
-          __syncwarp();
-#pragma unroll
-          for (int h = 0; h < 32 / F; ++h) {
-            const int u = (c * 32) / F + h;
-            const int i = i_base + u;
-            float s = 0.0f;
-            if (row_ok && i < p.I) {
-              const float xval = xr[u];
-              const float* tu = tabs + u * ((BK + 1) * kTabStride);
-              const int j0 = knot_interval(xval, tu, p.bd.nk);
-              if (j0 >= 0) {
-                float dv[BK + 1];
-                // derivative step of kanforge/bases/spline.py:86-91 with the reciprocal differences of the table
-                bspline_local_tab<BK>(xval, tu, p.bd.nk, j0, 1, dv);
-#pragma unroll
-                for (int rp = 0; rp <= BK; ++rp) {
-                  const int r = j0 - BK + rp;
-                  if (r >= 0 && r < p.bd.nt) s = fmaf(wst[lane * 33 + h * F + r], dv[rp], s);
-                }
-              }
-              if (p.bd.has_base) s = fmaf(wst[lane * 33 + h * F + F - 1], dsilu_fast(xval), s);
+    if constexpr (BK == 0) {
+      // Two sets of four warps: set h2 reads TMEM lane quarter q (rows 32 q ..) of
+      // column chunks 4 h2 .. 4 h2 + 3, i.e. the inputs IPT/2 h2 .. of the tile,
+      // and writes those inputs' dx.
+      constexpr int kHalfIn = IPT / 2;
+      const int q = (warp - 4) % 4, h2 = (warp - 4) / 4;
+      const int row = q * 32 + lane;
+      const int etid = (warp - 4) * 32 + lane;  // 0 .. 255
+      float* wst = stage + (warp - 4) * (32 * 33);
+      int tc = 0;
+      for (int t = pair; t < n_tiles; t += n_pairs, ++tc) {
+        int m, n;
+        p.tiles.get(t, m, n);
+        const int i_base = n * IPT;
+        const int acc = tc & 1;
+        bool ok = mbar_wait_warp(&ctl->acc_full[acc], (tc >> 1) & 1, abort);
+        if constexpr (BK > 0) {
+          // all eight warps are past the previous tile (its table readers are done) and agree
+          ok = named_bar_and(1, 256, ok);
+          if (ok) {
+            constexpr int kTab = (BK + 1) * kTabStride;  // knots and reciprocal differences of one input
+            for (int e = etid; e < IPT * kTab; e += 256) {
+              const int u = e / kTab, r = e % kTab;
+              tabs[e] = (i_base + u < p.I) ? __ldg(p.bd.tab + (size_t)(i_base + u) * kTab + r) : 0.0f;
             }
-#pragma unroll
-            for (int uu = 0; uu < IPT; ++uu)
-              if (uu == u) dxv[uu] = s;
           }
-          __syncwarp();
+          named_bar(1, 256);
         }
-      }
-      if (row_ok) {
-        __nv_bfloat16* dst = p.dx + b * p.I + i_base + u0;
-        if (i_base + u0 + kHalfIn <= p.I && ((p.I | i_base) % 2) == 0) {
-#pragma unroll
+        if (!ok) break;
+        tc_fence_after();
+        const int64_t b = (int64_t)m * kPairM + (int64_t)rank * kBM + row;
+        const bool row_ok = b < p.B;
+        // this row's x for this set's inputs, loaded once (4-byte loads when aligned)
+        const int u0 = h2 * kHalfIn;
+        float* xr = xsm + row * (IPT + 1);
+        if (row_ok && i_base + u0 + kHalfIn <= p.I && ((p.I | i_base) % 2) == 0) {
+          const uint32_t* src = reinterpret_cast<const uint32_t*>(p.x + b * p.I + i_base + u0);
+  #pragma unroll
           for (int k2 = 0; k2 < kHalfIn / 2; ++k2) {
-            float lo = 0.0f, hi = 0.0f;
-#pragma unroll
-            for (int uu = 0; uu < IPT; ++uu) {
-              if (uu == u0 + 2 * k2) lo = dxv[uu];
-              if (uu == u0 + 2 * k2 + 1) hi = dxv[uu];
+            const uint32_t wv = __ldg(src + k2);
+            xr[u0 + 2 * k2] = __uint_as_float(wv << 16);
+            xr[u0 + 2 * k2 + 1] = __uint_as_float(wv & 0xffff0000u);
+          }
+        } else {
+          for (int u = u0; u < u0 + kHalfIn; ++u)
+            xr[u] = (row_ok && i_base + u < p.I) ? __bfloat162float(p.x[b * p.I + i_base + u]) : 0.0f;
+        }
+        float dxv[IPT];
+  #pragma unroll 1
+        for (int c = 4 * h2; c < 4 * h2 + 4; ++c) {
+          float v[32];
+          tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + acc * kBN + c * 32, v);
+          if (c == 4 * h2 + 3) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(&ctl->acc_empty[acc], 0);
+          }
+          if constexpr (BK == 0) {
+  #pragma unroll
+            for (int h = 0; h < 32 / F + (F > 32 ? 1 : 0); ++h) {
+              // F == 16: two inputs per chunk; F == 32: one input per chunk
+              const int u = (c * 32) / F + h;
+              const float xval = xr[u];
+              float df[F];
+              cheb_drow<F>(xval, p.bd, df);
+              float s = 0.0f;
+  #pragma unroll
+              for (int j = 0; j < F; ++j) s = fmaf(v[h * F + j], df[j], s);
+  #pragma unroll
+              for (int uu = 0; uu < IPT; ++uu)
+                if (uu == u) dxv[uu] = s;
             }
-            reinterpret_cast<uint32_t*>(dst)[k2] = pack_bf16x2(lo, hi);
+          } else {
+            // stage the 32 columns of this row, then dot with the local derivative window
+  #pragma unroll
+            for (int j = 0; j < 32; ++j) wst[lane * 33 + j] = v[j];
+            __syncwarp();
+  #pragma unroll
+            for (int h = 0; h < 32 / F; ++h) {
+              const int u = (c * 32) / F + h;
+              const int i = i_base + u;
+              float s = 0.0f;
+              if (row_ok && i < p.I) {
+                const float xval = xr[u];
+                const float* tu = tabs + u * ((BK + 1) * kTabStride);
+                const int j0 = knot_interval(xval, tu, p.bd.nk);
+                if (j0 >= 0) {
+                  float dv[BK + 1];
+                  // derivative step of kanforge/bases/spline.py:86-91 with the reciprocal differences of the table
+                  bspline_local_tab<BK>(xval, tu, p.bd.nk, j0, 1, dv);
+  #pragma unroll
+                  for (int rp = 0; rp <= BK; ++rp) {
+                    const int r = j0 - BK + rp;
+                    if (r >= 0 && r < p.bd.nt) s = fmaf(wst[lane * 33 + h * F + r], dv[rp], s);
+                  }
+                }
+                if (p.bd.has_base) s = fmaf(wst[lane * 33 + h * F + F - 1], dsilu_fast(xval), s);
+              }
+  #pragma unroll
+              for (int uu = 0; uu < IPT; ++uu)
+                if (uu == u) dxv[uu] = s;
+            }
+            __syncwarp();
+          }
+        }
+        if (row_ok) {
+          __nv_bfloat16* dst = p.dx + b * p.I + i_base + u0;
+          if (i_base + u0 + kHalfIn <= p.I && ((p.I | i_base) % 2) == 0) {
+  #pragma unroll
+            for (int k2 = 0; k2 < kHalfIn / 2; ++k2) {
+              float lo = 0.0f, hi = 0.0f;
+  #pragma unroll
+              for (int uu = 0; uu < IPT; ++uu) {
+                if (uu == u0 + 2 * k2) lo = dxv[uu];
+                if (uu == u0 + 2 * k2 + 1) hi = dxv[uu];
+              }
+              reinterpret_cast<uint32_t*>(dst)[k2] = pack_bf16x2(lo, hi);
+            }
+          } else {
+  #pragma unroll
+            for (int uu = 0; uu < IPT; ++uu)
+              if (uu >= u0 && uu < u0 + kHalfIn && i_base + uu < p.I) p.dx[b * p.I + i_base + uu] = __float2bfloat16_rn(dxv[uu]);
+          }
+        }
+      }
+    } else {
+      // B-spline: four sets of four warps; set `set` reads TMEM lane quarter q
+      // (rows 32 q ..) of column chunks 2 set, 2 set + 1, i.e. the kSetIn
+      // inputs IPT/4 set .. of the tile, and writes those inputs' dx.
+      constexpr int kSetIn = IPT / 4;  // inputs per set
+      constexpr int kIPC = 32 / F;     // inputs per 32-column chunk
+      const int q = (warp - 4) % 4, set = (warp - 4) / 4;
+      const int row = q * 32 + lane;
+      const int etid = (warp - 4) * 32 + lane;  // 0 .. 511
+      float* wst = stage + (warp - 4) * (32 * (F + 1));
+      // tile t's knot tables (IPT inputs x (BK + 1) rows x tab_ts floats, zero
+      // past I) go to buffer t % 2 by 16-byte cp.async, issued one tile ahead
+      // so that the copy overlaps the previous tile's epilogue
+      const int ts = p.tab_ts, tab_in = (BK + 1) * p.tab_ts;
+      auto stage_tables = [&](int t, int buf) {
+        int m2, n2;
+        p.tiles.get(t, m2, n2);
+        const int ib = n2 * IPT;
+        float* dstb = tabs + buf * (IPT * tab_in);
+        const int c4 = ts / 4, per_in = (BK + 1) * c4;
+        for (int e = etid; e < IPT * per_in; e += kEpiThreads) {
+          const int u = e / per_in, rem = e % per_in;
+          const int qq = rem / c4, cc = rem % c4;
+          const bool in_ok = ib + u < p.I;
+          const float* src = p.bd.tab + (size_t)(in_ok ? ib + u : 0) * ((BK + 1) * kTabStride) + qq * kTabStride + cc * 4;
+          cp_async16(dstb + u * tab_in + qq * ts + cc * 4, src, in_ok);
+        }
+        cp_async_commit();
+      };
+      if (pair < n_tiles) stage_tables(pair, 0);
+      int tc = 0;
+      for (int t = pair; t < n_tiles; t += n_pairs, ++tc) {
+        int m, n;
+        p.tiles.get(t, m, n);
+        const int i_base = n * IPT;
+        const int acc = tc & 1;
+        bool ok = mbar_wait_warp(&ctl->acc_full[acc], (tc >> 1) & 1, abort);
+        cp_async_wait_all();
+        // every warp's table copies for this tile have landed, every warp is
+        // past the previous tile (its buffer is free again), and all agree
+        ok = named_bar_and(1, kEpiThreads, ok);
+        if (ok && t + n_pairs < n_tiles) stage_tables(t + n_pairs, (tc + 1) & 1);
+        if (!ok) break;
+        tc_fence_after();
+        const int64_t b = (int64_t)m * kPairM + (int64_t)rank * kBM + row;
+        const bool row_ok = b < p.B;
+        const int u0 = set * kSetIn;
+        const bool pairs_ok = row_ok && i_base + u0 + kSetIn <= p.I && ((p.I | i_base) % 2) == 0;
+        // this row's x for the set's inputs (4-byte loads when aligned)
+        float xv[kSetIn];
+        if (pairs_ok) {
+          const uint32_t* src = reinterpret_cast<const uint32_t*>(p.x + b * p.I + i_base + u0);
+#pragma unroll
+          for (int k2 = 0; k2 < kSetIn / 2; ++k2) {
+            const uint32_t wv = __ldg(src + k2);
+            xv[2 * k2] = __uint_as_float(wv << 16);
+            xv[2 * k2 + 1] = __uint_as_float(wv & 0xffff0000u);
           }
         } else {
 #pragma unroll
-          for (int uu = 0; uu < IPT; ++uu)
-            if (uu >= u0 && uu < u0 + kHalfIn && i_base + uu < p.I) p.dx[b * p.I + i_base + uu] = __float2bfloat16_rn(dxv[uu]);
+          for (int u = 0; u < kSetIn; ++u)
+            xv[u] = (row_ok && i_base + u0 + u < p.I) ? __bfloat162float(p.x[b * p.I + i_base + u0 + u]) : 0.0f;
+        }
+        // the derivative windows of the set's inputs, side by side: a
+        // fixed-step knot search (the largest r <= nk - 2 with t_r <= x) and
+        // the derivative step of kanforge/bases/spline.py:86-91 from the staged
+        // reciprocal differences
+        const float* tb = tabs + (tc & 1) * (IPT * tab_in) + u0 * tab_in;
+        const int nk = p.bd.nk;
+        int pos[kSetIn];
+        bool live[kSetIn], in_ok[kSetIn];
+#pragma unroll
+        for (int u = 0; u < kSetIn; ++u) {
+          const float* tu = tb + u * tab_in;
+          in_ok[u] = row_ok && i_base + u0 + u < p.I;
+          live[u] = in_ok[u] && xv[u] >= tu[0] && xv[u] < tu[nk - 1];
+          pos[u] = 0;
+        }
+        for (int st = pow2_floor(nk - 2); st > 0; st >>= 1) {
+#pragma unroll
+          for (int u = 0; u < kSetIn; ++u) {
+            const int c = pos[u] + st;
+            if (c <= nk - 2 && tb[u * tab_in + c] <= xv[u]) pos[u] = c;
+          }
+        }
+        float dv[kSetIn][BK + 1], dsl[kSetIn];
+#pragma unroll
+        for (int u = 0; u < kSetIn; ++u) {
+          bspline_local_tab<BK>(xv[u], tb + u * tab_in, nk, pos[u], 1, dv[u], ts);
+          dsl[u] = (p.bd.has_base && in_ok[u]) ? dsilu_fast(xv[u]) : 0.0f;
+        }
+        float dxl[kSetIn];
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          float v[32];
+          tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + acc * kBN + (2 * set + cc) * 32, v);
+          if (cc == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(&ctl->acc_empty[acc], 0);
+          }
+#pragma unroll
+          for (int h = 0; h < kIPC; ++h) {
+            const int ul = cc * kIPC + h;
+            // stage this input's F columns of the row, then dot with its window
+#pragma unroll
+            for (int j = 0; j < F; ++j) wst[lane * (F + 1) + j] = v[h * F + j];
+            __syncwarp();
+            float s = 0.0f;
+#pragma unroll
+            for (int rp = 0; rp <= BK; ++rp) {
+              const int r = pos[ul] - BK + rp;
+              if (live[ul] && r >= 0 && r < p.bd.nt) s = fmaf(wst[lane * (F + 1) + r], dv[ul][rp], s);
+            }
+            if (p.bd.has_base && in_ok[ul]) s = fmaf(wst[lane * (F + 1) + F - 1], dsl[ul], s);
+            dxl[ul] = s;
+            __syncwarp();
+          }
+        }
+        if (row_ok) {
+          __nv_bfloat16* dst = p.dx + b * p.I + i_base + u0;
+          if (pairs_ok) {
+#pragma unroll
+            for (int k2 = 0; k2 < kSetIn / 2; ++k2) reinterpret_cast<uint32_t*>(dst)[k2] = pack_bf16x2(dxl[2 * k2], dxl[2 * k2 + 1]);
+          } else {
+#pragma unroll
+            for (int u = 0; u < kSetIn; ++u)
+              if (i_base + u0 + u < p.I) dst[u] = __float2bfloat16_rn(dxl[u]);
+          }
         }
       }
+      cp_async_wait_all();  // no table copy lands after the loop (abort path)
     }
   }
 
@@ -1198,11 +1352,12 @@ __global__ void __launch_bounds__(256) feature_cheb_kernel(const __nv_bfloat16* 
 }
 
 // B-splines: a CTA owns 32 consecutive inputs and stages their knot tables in
-// shared memory once (rows of ts >= nk floats, each lane's table at an odd
-// stride so that the 32 lanes, one input each, read without bank conflicts);
-// its warps walk the rows, kSplineRows rows' x loaded together, each lane
-// evaluating one (row, input) once (knot search and Cox-de Boor from the
-// table).  The BK + 1 non-zero values of a row start at feature s = j0 - BK:
+// shared memory once (rows of ts >= nk floats), element-major and lane-minor:
+// element k of lane L's table at tabs[32 k + L], so each lane reads only its
+// own bank whatever index it needs.  Its warps walk the rows, kSplineRows
+// rows' x loaded together, each lane evaluating one (row, input) once: the
+// kSplineRows knot searches side by side (fixed steps: the largest r <= nk - 2
+// with t_r <= x), then Cox-de Boor from the table.  The BK + 1 non-zero values of a row start at feature s = j0 - BK:
 // packed as bf16 pairs from an even position, a funnel shift by 16 bits moves
 // them to an odd one, and the NW words they touch are placed among the row's
 // F / 2 words; silu(x) is the high half of the last word.  Each lane stores
@@ -1216,19 +1371,20 @@ __global__ void __launch_bounds__(256) feature_spline_kernel(const __nv_bfloat16
                                                              __nv_bfloat16* __restrict__ feat, int64_t B, int I, BasisDev bd,
                                                              int ts) {
   constexpr int NW = (BK + 3) / 2;  // words that BK + 1 consecutive bf16 values can touch
-  extern __shared__ float tabs[];   // [32][ls]
-  const int ls = (BK + 1) * ts + 1;
+  extern __shared__ float tabs[];   // [(BK + 1) * ts][32]
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int i0 = blockIdx.y * 32;
   for (int e = threadIdx.x; e < 32 * (BK + 1) * ts; e += blockDim.x) {
     const int u = e / ((BK + 1) * ts), rem = e % ((BK + 1) * ts);
     const int q = rem / ts, r = rem % ts;
-    tabs[u * ls + rem] = (i0 + u < I) ? __ldg(bd.tab + (size_t)(i0 + u) * ((BK + 1) * kTabStride) + q * kTabStride + r) : 0.0f;
+    tabs[rem * 32 + u] = (i0 + u < I) ? __ldg(bd.tab + (size_t)(i0 + u) * ((BK + 1) * kTabStride) + q * kTabStride + r) : 0.0f;
   }
   __syncthreads();
   const int i = i0 + lane;
   if (i >= I) return;
-  const float* tu = tabs + lane * ls;
+  const float* tu = tabs + lane;  // element k at tu[32 k]
+  const int nk = bd.nk, top = pow2_floor(nk - 2);
+  const float t_lo = tu[0], t_hi = tu[32 * (nk - 1)];
   const int64_t stride = (int64_t)gridDim.x * 8;
   for (int64_t b0 = (int64_t)blockIdx.x * 8 + warp; b0 < B; b0 += kSplineRows * stride) {
     float xs[kSplineRows];
@@ -1236,6 +1392,16 @@ __global__ void __launch_bounds__(256) feature_spline_kernel(const __nv_bfloat16
     for (int u = 0; u < kSplineRows; ++u) {
       const int64_t b = b0 + u * stride;
       xs[u] = b < B ? __bfloat162float(x[b * I + i]) : 0.0f;
+    }
+    int pos[kSplineRows];
+#pragma unroll
+    for (int u = 0; u < kSplineRows; ++u) pos[u] = 0;
+    for (int st = top; st > 0; st >>= 1) {
+#pragma unroll
+      for (int u = 0; u < kSplineRows; ++u) {
+        const int c = pos[u] + st;
+        if (c <= nk - 2 && tu[32 * c] <= xs[u]) pos[u] = c;
+      }
     }
 #pragma unroll
     for (int u = 0; u < kSplineRows; ++u) {
@@ -1245,10 +1411,10 @@ __global__ void __launch_bounds__(256) feature_spline_kernel(const __nv_bfloat16
       uint32_t wd[F / 2];
 #pragma unroll
       for (int k = 0; k < F / 2; ++k) wd[k] = 0u;
-      const int j0 = knot_interval(xv, tu, bd.nk);
+      const int j0 = (xv >= t_lo && xv < t_hi) ? pos[u] : -1;
       if (j0 >= 0) {
         float vv[BK + 1];
-        bspline_local_tab<BK>(xv, tu, bd.nk, j0, 0, vv, ts);
+        bspline_local_tab<BK, 32>(xv, tu, nk, j0, 0, vv, 32 * ts);
         const int s0 = j0 - BK;
         uint32_t h[2 * NW];
 #pragma unroll
@@ -1432,7 +1598,7 @@ struct DgradLaunch {
   template <int BK, int F>
   int go() const {
     constexpr int IPT = kBN / F;
-    const size_t smem = kPairSmem + sizeof(float) * (kBM * (IPT + 1) + (BK > 0 ? IPT * (BK + 1) * kTabStride + 8 * 32 * 33 : 0));
+    const size_t smem = kPairSmem + sizeof(float) * (BK > 0 ? 2 * IPT * (BK + 1) * p.tab_ts + 16 * 32 * (F + 1) : kBM * (IPT + 1));
     auto kern = fused_dgrad_kernel<BK, F>;
     KF_CUDA_RET(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     cudaLaunchAttribute attr[1];
@@ -1441,7 +1607,7 @@ struct DgradLaunch {
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cudaLaunchConfig_t cfg = {};
-    cfg.blockDim = dim3(kDgradThreads);
+    cfg.blockDim = dim3(dgrad_threads(BK));
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cfg.attrs = attr;
@@ -1513,7 +1679,7 @@ struct FeatureLaunch {
       const int64_t want = std::max<int64_t>(1, (int64_t)sm_count() * 8 / gy);
       const unsigned gx = (unsigned)std::max<int64_t>(1, std::min<int64_t>(cdiv(B, (int64_t)8), want));
       const int ts = (bd.nk + 15) & ~15;  // table row stride in shared memory (>= nk)
-      const size_t smem = sizeof(float) * 32 * ((BK + 1) * ts + 1);
+      const size_t smem = sizeof(float) * 32 * (BK + 1) * ts;
       KF_CUDA_RET(cudaFuncSetAttribute(feature_spline_kernel<BK, F>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
       feature_spline_kernel<BK, F><<<dim3(gx, gy), 256, smem, stream>>>(x, feat, B, I, bd, ts);
     }
@@ -1585,6 +1751,7 @@ extern "C" int kf_dgrad(const void* x, const void* dy, const void* packed, const
   p.tiles.m_tiles = (int)cdiv(B, kPairM);
   p.tiles.n_tiles = (int)cdiv((int64_t)I * f_pad, kBN);
   p.tiles.gm = std::min(p.tiles.m_tiles, 8);
+  p.tab_ts = (p.bd.nk + 3) & ~3;
   CUtensorMap tdy, tc;
   if (int rc = make_tmap_bf16(&tdy, dy, B, O, kBK, kBM)) return rc;
   if (int rc = make_tmap_bf16(&tc, packed, O, (int64_t)I * f_pad, 64, kBK)) return rc;
