@@ -76,13 +76,34 @@ def dist_env():
 # ---------------------------------------------------------------------------
 
 
+_MEAN_SQUARE = None
+
+
 def mean_square(y):
     """Loss of the training steps: mean of y^2 accumulated in float32, one
-    reduction over the bf16 output (no float32 copy of y; the backward is one
-    elementwise kernel writing dy in y's dtype)."""
+    reduction over the bf16 output (no float32 copy of y).  Its backward,
+    dy = y * (2 g / N), is one vectorised kernel in y's dtype that reads the
+    scale from device memory (`torch._foreach_mul` with a 0-dim tensor): the
+    generic backward of `vector_norm` multiplies by a broadcast device scalar
+    on torch's non-vectorised path and adds a masked fill."""
+    global _MEAN_SQUARE
     import torch
 
-    return torch.linalg.vector_norm(y, dtype=torch.float32).square() / y.numel()
+    if _MEAN_SQUARE is None:
+
+        class MeanSquare(torch.autograd.Function):
+            @staticmethod
+            def forward(ctx, t):
+                ctx.save_for_backward(t)
+                return torch.linalg.vector_norm(t, dtype=torch.float32).square() / t.numel()
+
+            @staticmethod
+            def backward(ctx, g):
+                (t,) = ctx.saved_tensors
+                return torch._foreach_mul([t], g * (2.0 / t.numel()))[0]
+
+        _MEAN_SQUARE = MeanSquare
+    return _MEAN_SQUARE.apply(y)
 
 
 def build_workload(cfg: int, dtype_name: str, device, seed: int, tokens: int | None = None):
