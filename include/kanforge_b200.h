@@ -142,6 +142,36 @@ int kf_dgrad(const void* x, const void* dy, const void* packed, const float* kno
 int kf_features(const void* x, const float* knot_tab, void* feat, int64_t B, int32_t I, int32_t nt, int32_t f_pad,
                 int32_t has_base, const kf_basis_desc* basis, void* stream);
 
+/* Float32 GEMM on tcgen05 with three TF32 products (hi*hi + hi*lo + lo*hi,
+ * hi = tf32(v), lo = v - hi, split in shared memory), float32 accumulation:
+ *   C[m,n] = sum_k A[m,k] B[n,k] (+ bias[n])
+ * A is K-major (a_mn_major = 0: element (m,k) at a[m*lda + k]) or MN-major
+ * (element (m,k) at a[k*lda + m]); B likewise with n.  lda, ldb multiples of
+ * 4 floats, operands 16-byte aligned, K >= 1.  The float32 layer's three
+ * contractions: forward y = feat packed^T + b (the reference's F_0,
+ * kanforge/torch/kernels.py:143-150), feature gradient dfeat = dy packed
+ * (its P_1 before the derivative features, kernels.py:84) and coefficient
+ * gradient dpacked = dy^T feat (its G_0, kernels.py:85). */
+int kf_gemm_tf32x3(const float* a, int32_t a_mn_major, int64_t lda, const float* b, int32_t b_mn_major, int64_t ldb,
+                   const float* bias, float* c, int64_t ldc, int64_t M, int64_t N, int64_t K, void* stream);
+
+/* Float32 feature matrix of the float32 tensor-core path:
+ *   feat[b, i*F + j] = phi_j(x[b,i]) (j < nf), 0 up to F-2, silu(x[b,i]) at F-1
+ *   when has_base (the column layout of kf_pack_coef; F = 16 or 32).
+ * grid (I, G+1) float32 for B-splines, else ignored.  x (B,I) float32.
+ * (The reference evaluates these inside its Triton launches,
+ * kanforge/kernels/triton_kernels.py:32-108.) */
+int kf_features_f32(const float* x, const float* grid, float* feat, int64_t B, int32_t I, int32_t nf, int32_t F,
+                    int32_t has_base, const kf_basis_desc* basis, void* stream);
+
+/* Input gradient from the feature gradient of kf_gemm_tf32x3:
+ *   dx[b,i] = sum_{j<nf} dfeat[b, i*F + j] d phi_j / dx (x[b,i])
+ *           + dfeat[b, i*F + F-1] silu'(x[b,i])        (when has_base)
+ * (the reference's gx = w * P_1, kanforge/torch/kernels.py:84, with the base
+ * branch of layers.py:185-186.) */
+int kf_features_dot_f32(const float* x, const float* grid, const float* dfeat, float* dx, int64_t B, int32_t I,
+                        int32_t nf, int32_t F, int32_t has_base, const kf_basis_desc* basis, void* stream);
+
 /* Fused coefficient gradient on tcgen05, with the effective-coefficient chain rule:
  *   dpacked[o,i,j] = sum_b dy[b,o] feat_j(x[b,i])
  *   dC[o,i,k]      = sum_{j<nt} dpacked[o,i,j] fold[k,j]      (fold null: k = j)

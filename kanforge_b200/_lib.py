@@ -70,6 +70,18 @@ PROTOTYPES = {
         ctypes.c_int,
         [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, ctypes.POINTER(BasisDesc), _vp, _c_i32, _vp],
     ),
+    "kf_gemm_tf32x3": (
+        ctypes.c_int,
+        [_vp, _c_i32, _c_i64, _vp, _c_i32, _c_i64, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _vp],
+    ),
+    "kf_features_f32": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, ctypes.POINTER(BasisDesc), _vp],
+    ),
+    "kf_features_dot_f32": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _vp, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, ctypes.POINTER(BasisDesc), _vp],
+    ),
     "kf_rational_act": (ctypes.c_int, [_vp, _vp, _vp, _vp, _c_i64, _c_i32, _c_i32, ctypes.POINTER(BasisDesc), ctypes.c_int, _vp]),
     "kf_rational_bwd": (
         ctypes.c_int,

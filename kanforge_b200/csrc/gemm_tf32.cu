@@ -1,0 +1,434 @@
+// Float32 GEMM on the 5th-generation tensor cores with three TF32 products
+// (the float32 KANLinear path: feature matrix x packed coefficients, the
+// input-gradient features and the coefficient gradient, i.e. the reference's
+// F/G/P contractions of kanforge/kernels/__init__.py:5-13 at m = 0, w = 1):
+//
+//   C[m, n] = sum_k A[m, k] B[n, k]  (+ bias[n]),  all float32,
+//
+// A and B each stored K-major (row m / n contiguous in k) or MN-major (row k
+// contiguous in m / n).  Every operand tile is split in shared memory into
+// hi = tf32(v) (round to nearest) and lo = v - hi, and the accumulator takes
+// hi*hi + hi*lo + lo*hi (tcgen05.mma kind::tf32, float32 accumulation in
+// tensor memory): the dropped lo*lo term and the tf32 rounding of lo leave a
+// relative error near 2^-22 per product, float32 accuracy for these sums.
+//
+// The tensor core's float32 accumulation loses precision with the number of
+// MMAs accumulated into one tensor-memory accumulator (measured: the error
+// grows linearly with K, about 40x round-to-nearest at K = 3000), so each
+// tile's K loop runs in segments of kGSeg stages (256 floats of K, 96 MMAs):
+// every segment starts a fresh accumulator, and the epilogue adds the segment
+// sums in float32 registers (round to nearest).
+//
+// One persistent CTA per SM, 128 x 128 output tiles, K steps of 32 floats
+// (128-byte rows), 3 stages.  K-major tiles use the 128-byte swizzle (16-byte
+// chunks XOR row % 8); MN-major tiles of 32-bit elements must use the
+// 128-byte swizzle with 32-byte atoms (32-byte chunks XOR row % 4, descriptor
+// layout type 1), the only MN-major layout the tensor core takes for TF32.
+// Warp roles: w0 TMA, w1 MMA issue, w4-7 split (hi in place, lo into a second
+// buffer of the same layout, fenced into the async proxy), w8-15 epilogue in
+// two column halves (two 128-column accumulators in tensor memory, so a
+// segment's drain overlaps the next segment's MMAs).
+#include "umma.cuh"
+
+namespace kf {
+
+namespace {
+
+using namespace umma;
+
+constexpr int kGM = 128, kGN = 128, kGK = 32;  // tile rows, columns, K floats per stage
+constexpr int kGStages = 3;
+constexpr int kGSeg = 8;  // stages per accumulation segment
+constexpr int kGTile = kGM * kGK * 4;          // 16 KB: one operand tile of a stage
+constexpr int kGThreads = 512;
+constexpr int kGEpiWarps = 8;
+
+struct GemmCtl {
+  uint64_t full[kGStages];   // TMA landed (expect_tx)
+  uint64_t split[kGStages];  // hi / lo written (4 split warps)
+  uint64_t empty[kGStages];  // MMAs of the stage done (tcgen05.commit)
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];     // 8 epilogue warps
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+constexpr size_t kGSmem = 1024 + (size_t)kGStages * 4 * kGTile + sizeof(GemmCtl);
+
+struct GemmParams {
+  const float* bias;  // (N) or null
+  float* C;           // (M, ldc)
+  int64_t M, N, K, ldc;
+  int a_mn, b_mn;     // operand stored MN-major
+  int m_fast;         // tile order: M fastest (else N fastest)
+  int m_tiles, n_tiles, k_steps;
+};
+
+// ---- single-CTA tcgen05 forms ----------------------------------------------
+__device__ __forceinline__ void tmem_alloc1(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish1() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc1(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit1(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Instruction descriptor of kind::tf32 with f32 accumulation.
+__host__ __device__ constexpr uint32_t idesc_tf32_f32(int M, int N, bool a_mn_major, bool b_mn_major) {
+  return (1u << 4)                          // D format: f32
+         | (2u << 7)                        // A format: tf32
+         | (2u << 10)                       // B format: tf32
+         | ((a_mn_major ? 1u : 0u) << 15)   // A major
+         | ((b_mn_major ? 1u : 0u) << 16)   // B major
+         | ((uint32_t)(N >> 3) << 17)       // N / 8
+         | ((uint32_t)(M >> 4) << 24);      // M / 16
+}
+
+// Shared-memory descriptor, layout type 1: 128-byte swizzle with 32-byte
+// atoms (MN-major 32-bit operands).  128-byte MN chunks `lbo` apart, 4-row K
+// groups `sbo` apart.
+__device__ __forceinline__ uint64_t smem_desc_sw128_b32(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version (sm_100)
+  d |= (uint64_t)1 << 61;  // SWIZZLE_128B_BASE32B
+  return d;
+}
+
+__device__ __forceinline__ float tf32_rna(float v) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
+  return __uint_as_float(r);
+}
+
+// Descriptor of k-step j (8 floats) of a 128-row operand tile.  K-major: rows
+// of 128 B, 8-row groups 1 KB apart, a k-step is 32 B along the row.
+// MN-major: blocks of 32 MN-elements x 32 k-rows (4 KB apart), 4-row K groups
+// 512 B apart, a k-step is 8 rows = 1 KB.
+__device__ __forceinline__ uint64_t operand_desc(uint32_t base, bool mn_major, int j) {
+  return mn_major ? smem_desc_sw128_b32(base + 1024u * j, 4096, 512) : smem_desc_sw128(base + 32u * j, 16, 1024);
+}
+
+__global__ void __launch_bounds__(kGThreads, 1) gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                                                                   const __grid_constant__ CUtensorMap tmap_b, GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // stage s: A, B (TMA, then hi in place), A_lo, B_lo
+  auto tile = [&](int s, int which) { return base + ((size_t)s * 4 + which) * kGTile; };
+  GemmCtl* ctl = reinterpret_cast<GemmCtl*>(base + (size_t)kGStages * 4 * kGTile);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  volatile int* abort = &ctl->abort;
+  const int n_tiles = p.m_tiles * p.n_tiles;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kGStages; ++s) {
+      mbar_init(&ctl->full[s], 1);
+      mbar_init(&ctl->split[s], 4);
+      mbar_init(&ctl->empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&ctl->acc_full[a], 1);
+      mbar_init(&ctl->acc_empty[a], kGEpiWarps);
+    }
+    mbar_init(&ctl->drain, 1);
+    ctl->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc1(&ctl->tmem_base, 256);
+    tmem_relinquish1();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmap_a);
+    prefetch_tmap(&tmap_b);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+  auto tile_mn = [&](int t, int& m, int& n) {
+    if (p.m_fast) {
+      m = t % p.m_tiles;
+      n = t / p.m_tiles;
+    } else {
+      n = t % p.n_tiles;
+      m = t / p.n_tiles;
+    }
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int it = 0;
+      for (int t = blockIdx.x; t < n_tiles && !*abort; t += gridDim.x) {
+        int m, n;
+        tile_mn(t, m, n);
+        for (int k = 0; k < p.k_steps; ++k, ++it) {
+          const int s = it % kGStages;
+          if (!mbar_wait(&ctl->empty[s], ((it / kGStages) & 1) ^ 1, abort)) break;
+          mbar_arrive_expect_tx(&ctl->full[s], 2 * kGTile);
+          const int k0 = k * kGK;
+          if (p.a_mn) {
+#pragma unroll
+            for (int c = 0; c < kGM / 32; ++c) tma_load_2d(tile(s, 0) + c * 4096, &tmap_a, &ctl->full[s], m * kGM + 32 * c, k0);
+          } else {
+            tma_load_2d(tile(s, 0), &tmap_a, &ctl->full[s], k0, m * kGM);
+          }
+          if (p.b_mn) {
+#pragma unroll
+            for (int c = 0; c < kGN / 32; ++c) tma_load_2d(tile(s, 1) + c * 4096, &tmap_b, &ctl->full[s], n * kGN + 32 * c, k0);
+          } else {
+            tma_load_2d(tile(s, 1), &tmap_b, &ctl->full[s], k0, n * kGN);
+          }
+        }
+      }
+      if (*abort) {  // the loads issued on every stage land before the CTA exits
+        for (int s = 0; s < kGStages; ++s) {
+          const int last = it - 1 - ((it - 1 - s) % kGStages + kGStages) % kGStages;
+          if (it > 0 && last >= 0) mbar_drain(&ctl->full[s], (last / kGStages) & 1);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_tf32_f32(kGM, kGN, p.a_mn != 0, p.b_mn != 0);
+      int it = 0, sc = 0;  // stages and segments issued
+      bool ok = true;
+      for (int t = blockIdx.x; t < n_tiles && ok && !*abort; t += gridDim.x) {
+        for (int k0 = 0; k0 < p.k_steps && ok; k0 += kGSeg, ++sc) {
+          const int acc = sc & 1;
+          if (!mbar_wait(&ctl->acc_empty[acc], ((sc >> 1) & 1) ^ 1, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d = tmem + acc * kGN;
+          const int k1 = min(p.k_steps, k0 + kGSeg);
+          for (int k = k0; k < k1; ++k, ++it) {
+            const int s = it % kGStages;
+            if (!mbar_wait(&ctl->split[s], (it / kGStages) & 1, abort)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a_hi = smem_u32(tile(s, 0)), b_hi = smem_u32(tile(s, 1));
+            const uint32_t a_lo = smem_u32(tile(s, 2)), b_lo = smem_u32(tile(s, 3));
+#pragma unroll
+            for (int j = 0; j < kGK / 8; ++j) {
+              const uint64_t ah = operand_desc(a_hi, p.a_mn, j), al = operand_desc(a_lo, p.a_mn, j);
+              const uint64_t bh = operand_desc(b_hi, p.b_mn, j), bl = operand_desc(b_lo, p.b_mn, j);
+              mma_tf32(d, ah, bh, idesc, (k > k0 || j > 0) ? 1u : 0u);
+              mma_tf32(d, ah, bl, idesc, 1u);
+              mma_tf32(d, al, bh, idesc, 1u);
+            }
+            mma_commit1(&ctl->empty[s]);
+          }
+          if (!ok) break;
+          mma_commit1(&ctl->acc_full[acc]);
+        }
+      }
+      // every MMA issued above has completed once the drain barrier flips
+      mma_commit1(&ctl->drain);
+      mbar_drain(&ctl->drain, 0);
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // split: hi = tf32(v) in place, lo = v - hi at the same offset of the lo tile
+    const int st = (warp - 4) * 32 + lane;  // 0 .. 127
+    int it = 0;
+    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
+      bool ok = true;
+      for (int k = 0; k < p.k_steps; ++k, ++it) {
+        const int s = it % kGStages;
+        if (!mbar_wait_warp(&ctl->full[s], (it / kGStages) & 1, abort)) {
+          ok = false;
+          break;
+        }
+#pragma unroll
+        for (int w = 0; w < 2; ++w) {
+          float4* hi = reinterpret_cast<float4*>(tile(s, w));
+          float4* lo = reinterpret_cast<float4*>(tile(s, 2 + w));
+#pragma unroll 4
+          for (int e = st; e < kGTile / 16; e += 128) {
+            const float4 v = hi[e];
+            const float4 h = make_float4(tf32_rna(v.x), tf32_rna(v.y), tf32_rna(v.z), tf32_rna(v.w));
+            hi[e] = h;
+            lo[e] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ctl->split[s]);
+      }
+      if (!ok) break;
+    }
+  } else if (warp >= 8) {
+    // half e of the columns (64 of them), lane quarter q of the rows: each
+    // thread sums its row's 64 columns over the tile's segments in registers
+    const int q = warp % 4, e = (warp - 8) / 4;
+    int sc = 0;
+    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
+      int m, n;
+      tile_mn(t, m, n);
+      float r[64];
+#pragma unroll
+      for (int j = 0; j < 64; ++j) r[j] = 0.0f;
+      bool ok = true;
+      for (int k0 = 0; k0 < p.k_steps; k0 += kGSeg, ++sc) {
+        const int acc = sc & 1;
+        if (!mbar_wait_warp(&ctl->acc_full[acc], (sc >> 1) & 1, abort)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        float v[32];
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + acc * kGN + e * 64, v);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) r[j] += v[j];
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + acc * kGN + e * 64 + 32, v);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) r[32 + j] += v[j];
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ctl->acc_empty[acc]);
+      }
+      if (!ok) break;
+      const int64_t row = (int64_t)m * kGM + q * 32 + lane;
+      const int64_t n0 = (int64_t)n * kGN + e * 64;
+      if (row < p.M) {
+        float* crow = p.C + row * p.ldc;
+        if (p.bias) {
+#pragma unroll
+          for (int j = 0; j < 64; ++j)
+            if (n0 + j < p.N) r[j] += __ldg(p.bias + n0 + j);
+        }
+        if (n0 + 64 <= p.N && (p.ldc % 4) == 0 && ((uintptr_t)p.C % 16) == 0) {
+#pragma unroll
+          for (int j = 0; j < 64; j += 4)
+            *reinterpret_cast<float4*>(crow + n0 + j) = make_float4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 64; ++j)
+            if (n0 + j < p.N) crow[n0 + j] = r[j];
+        }
+      }
+      __syncwarp();
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc1(tmem, 256);
+  }
+}
+
+// ---- host ------------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// 2-D float32 tensor map, rows x cols (cols contiguous, row pitch ld floats),
+// box 32 columns (128 B) x box_rows rows; the 128-byte swizzle with 16-byte
+// chunks (K-major tiles) or 32-byte atoms (MN-major tiles).
+int make_tmap_f32(CUtensorMap* map, const float* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows, bool atom32) {
+  auto enc = encode_fn();
+  if (!enc) {
+    set_error("cuTensorMapEncodeTiled is not available from the driver");
+    return KF_ERR_CUDA;
+  }
+  KF_CHECK_ARG(((uintptr_t)ptr % 16) == 0, "kf_gemm_tf32x3: operands must be 16-byte aligned");
+  KF_CHECK_ARG(ld % 4 == 0 && ld >= cols, "kf_gemm_tf32x3: row pitch %lld must be a multiple of 4 floats and >= %lld",
+               (long long)ld, (long long)cols);
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 4)};
+  cuuint32_t box[2] = {32u, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d) for %lldx%lld", (int)r, (long long)rows, (long long)cols);
+    return KF_ERR_CUDA;
+  }
+  return KF_OK;
+}
+
+}  // namespace
+
+}  // namespace kf
+
+extern "C" int kf_gemm_tf32x3(const float* a, int32_t a_mn_major, int64_t lda, const float* b, int32_t b_mn_major,
+                              int64_t ldb, const float* bias, float* c, int64_t ldc, int64_t M, int64_t N, int64_t K,
+                              void* stream) {
+  using namespace kf;
+  clear_error();
+  KF_CHECK_ARG(a && b && c, "kf_gemm_tf32x3: null operand");
+  KF_CHECK_ARG(M >= 0 && N >= 0 && K >= 1 && ldc >= N, "kf_gemm_tf32x3: bad sizes (M %lld, N %lld, K %lld, ldc %lld)",
+               (long long)M, (long long)N, (long long)K, (long long)ldc);
+  KF_CHECK_ARG(M < (int64_t)kGM * 65536 && N < (int64_t)kGN * 65536 && K < ((int64_t)1 << 36),
+               "kf_gemm_tf32x3: sizes beyond the kernel limits");
+  if (int rc = bind_device(a)) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (M == 0 || N == 0) return KF_OK;
+  CUtensorMap ta, tb;
+  // A: K-major (M rows of K) or MN-major (K rows of M); B likewise with N.
+  if (int rc = a_mn_major ? make_tmap_f32(&ta, a, K, M, lda, 32, true) : make_tmap_f32(&ta, a, M, K, lda, kGM, false))
+    return rc;
+  if (int rc = b_mn_major ? make_tmap_f32(&tb, b, K, N, ldb, 32, true) : make_tmap_f32(&tb, b, N, K, ldb, kGN, false))
+    return rc;
+  GemmParams p{};
+  p.bias = bias;
+  p.C = c;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.ldc = ldc;
+  p.a_mn = a_mn_major ? 1 : 0;
+  p.b_mn = b_mn_major ? 1 : 0;
+  p.m_tiles = (int)cdiv(M, (int64_t)kGM);
+  p.n_tiles = (int)cdiv(N, (int64_t)kGN);
+  p.k_steps = (int)cdiv(K, (int64_t)kGK);
+  // Tiles in flight together share the operand that is not streamed: along
+  // the larger of M and N that is the other operand (the coefficients of the
+  // forward and input gradient, the features of the coefficient gradient).
+  p.m_fast = M <= N ? 1 : 0;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  KF_CUDA_RET(cudaGetDevice(&dev));
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    KF_CUDA_RET(cudaFuncSetAttribute(gemm_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGSmem));
+    attr_set[dev] = true;
+  }
+  int sms = 0;
+  KF_CUDA_RET(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const int64_t tiles = (int64_t)p.m_tiles * p.n_tiles;
+  const unsigned grid = (unsigned)std::min<int64_t>(tiles, sms > 0 ? sms : 148);
+  gemm_tf32x3_kernel<<<grid, kGThreads, kGSmem, s>>>(ta, tb, p);
+  return check_launch("kf_gemm_tf32x3");
+}

@@ -268,6 +268,111 @@ struct PrimLaunch {
   }
 };
 
+// ---------------------------------------------------------------------------
+// Float32 feature matrix and its input-gradient contraction, for the float32
+// tensor-core path (kf_gemm_tf32x3).  Column layout of input i: i * F + j,
+// phi_j(x) for j < nf, zero up to F - 2, silu(x) at F - 1 when the base branch
+// is fused (the layout of kf_pack_coef).  Threads run along the inputs (one
+// input's knots computed once per thread), CTAs along row blocks.
+// ---------------------------------------------------------------------------
+constexpr int kFeatRows = 64;  // rows per CTA row block
+
+template <int BK>
+__global__ void __launch_bounds__(kThreads) feature_f32_kernel(const float* __restrict__ x, float* __restrict__ feat,
+                                                               int64_t B, int I, int F, int has_base, FeatArgs fa) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= I) return;
+  float t[KF_NK_MAX];
+  load_knots<BK>(fa, i, t, 0, 1);
+  const int64_t b0 = (int64_t)blockIdx.y * kFeatRows;
+  const int64_t b1 = min(B, b0 + kFeatRows);
+  for (int64_t b = b0; b < b1; ++b) {
+    const float xv = x[b * I + i];
+    float* dst = feat + (b * I + i) * F;
+    eval_features<BK>(fa, xv, 1.0f, t, dst, 1);
+    for (int j = fa.nf; j < F - 1; ++j) dst[j] = 0.0f;
+    dst[F - 1] = has_base ? silu_acc(xv) : 0.0f;
+  }
+}
+
+// dx[b, i] = sum_j dfeat[b, i * F + j] d phi_j / dx + dfeat[b, i * F + F - 1] silu'(x).
+// B-splines: the native first-derivative window; Chebyshev features T_j(z):
+// dT_j/dz = j U_{j-1}(z) (U_0 = 1, U_1 = 2 z, U_j = 2 z U_{j-1} - U_{j-2}),
+// times dz/dx = 1 - z^2 under the tanh map.
+template <int BK>
+__global__ void __launch_bounds__(kThreads) feature_dot_f32_kernel(const float* __restrict__ x, const float* __restrict__ dfeat,
+                                                                   float* __restrict__ dx, int64_t B, int I, int F,
+                                                                   int has_base, FeatArgs fa) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= I) return;
+  float t[KF_NK_MAX];
+  load_knots<BK>(fa, i, t, 0, 1);
+  const int64_t b0 = (int64_t)blockIdx.y * kFeatRows;
+  const int64_t b1 = min(B, b0 + kFeatRows);
+  for (int64_t b = b0; b < b1; ++b) {
+    const float xv = x[b * I + i];
+    const float* h = dfeat + (b * I + i) * F;
+    float acc;
+    if constexpr (BK == 0) {
+      const bool tanh_map = fa.map == KF_MAP_TANH;
+      const float z = tanh_map ? tanhf(xv) : xv;
+      float um2 = 0.0f, um1 = 1.0f;  // U_{j-2}, U_{j-1} for j = 1
+      acc = 0.0f;
+      for (int j = 1; j < fa.nf; ++j) {
+        acc = fmaf(h[j] * (float)j, um1, acc);
+        const float uj = j == 1 ? 2.0f * z : 2.0f * z * um1 - um2;
+        um2 = um1;
+        um1 = uj;
+      }
+      if (tanh_map) acc *= 1.0f - z * z;
+    } else {
+      acc = dot_features<BK>(fa, xv, t, h, 1);
+    }
+    if (has_base) acc = fmaf(h[F - 1], dsilu_acc(xv), acc);
+    dx[b * I + i] = acc;
+  }
+}
+
+struct FeatureF32Launch {
+  bool dot;
+  const float *x, *dfeat;
+  float* out;
+  int64_t B;
+  int I, F, has_base;
+  FeatArgs fa;
+  cudaStream_t stream;
+  template <int BK>
+  int operator()() const {
+    const dim3 grid((unsigned)cdiv((int64_t)I, (int64_t)kThreads), (unsigned)cdiv(B, (int64_t)kFeatRows));
+    if (dot)
+      feature_dot_f32_kernel<BK><<<grid, kThreads, 0, stream>>>(x, dfeat, out, B, I, F, has_base, fa);
+    else
+      feature_f32_kernel<BK><<<grid, kThreads, 0, stream>>>(x, out, B, I, F, has_base, fa);
+    return check_launch(dot ? "kf_features_dot_f32" : "kf_features_f32");
+  }
+};
+
+int feature_args(const kf_basis_desc* basis, const float* grid, int nf, int F, int m, FeatArgs& fa) {
+  KF_CHECK_ARG(basis != nullptr, "basis is null");
+  KF_CHECK_ARG(F == 16 || F == 32, "F must be 16 or 32 (got %d)", F);
+  KF_CHECK_ARG(nf >= 1 && nf + 1 <= F, "nf %d (+ the SiLU column) exceeds F %d", nf, F);
+  fa.m = m;
+  fa.nf = nf;
+  fa.map = basis->input_map;
+  if (basis->kind == KF_BASIS_BSPLINE) {
+    KF_CHECK_ARG(grid != nullptr, "B-spline needs its grid");
+    fa.G = basis->grid_size;
+    fa.nk = basis->grid_size + 2 * basis->order + 1;
+    fa.grid = grid;
+    KF_CHECK_ARG(fa.nk <= KF_NK_MAX, "%d knots exceed the limit %d", fa.nk, KF_NK_MAX);
+    KF_CHECK_ARG(nf == basis->size, "B-spline nf %d != size %d", nf, basis->size);
+  } else if (basis->kind != KF_BASIS_CHEB) {
+    set_error("basis kind %d has no float32 feature kernel", basis->kind);
+    return KF_ERR_UNSUPPORTED;
+  }
+  return KF_OK;
+}
+
 }  // namespace kf
 
 extern "C" int kf_prim(int op, int m, const float* x, const float* a, const float* b, const float* grid, float* out,
@@ -301,5 +406,31 @@ extern "C" int kf_prim(int op, int m, const float* x, const float* a, const floa
     return KF_OK;
   }
   PrimLaunch L{op, x, a, b, out, B, I, O, fa, (cudaStream_t)stream};
+  return dispatch_bk(basis, L);
+}
+
+extern "C" int kf_features_f32(const float* x, const float* grid, float* feat, int64_t B, int32_t I, int32_t nf, int32_t F,
+                               int32_t has_base, const kf_basis_desc* basis, void* stream) {
+  using namespace kf;
+  clear_error();
+  KF_CHECK_ARG(x && feat && B >= 0 && I >= 1, "kf_features_f32: bad arguments");
+  FeatArgs fa{};
+  if (int rc = feature_args(basis, grid, nf, F, 0, fa)) return rc;
+  if (int rc = bind_device(x)) return rc;
+  if (B == 0) return KF_OK;
+  FeatureF32Launch L{false, x, nullptr, feat, B, I, F, has_base, fa, (cudaStream_t)stream};
+  return dispatch_bk(basis, L);
+}
+
+extern "C" int kf_features_dot_f32(const float* x, const float* grid, const float* dfeat, float* dx, int64_t B, int32_t I,
+                                   int32_t nf, int32_t F, int32_t has_base, const kf_basis_desc* basis, void* stream) {
+  using namespace kf;
+  clear_error();
+  KF_CHECK_ARG(x && dfeat && dx && B >= 0 && I >= 1, "kf_features_dot_f32: bad arguments");
+  FeatArgs fa{};
+  if (int rc = feature_args(basis, grid, nf, F, 1, fa)) return rc;
+  if (int rc = bind_device(x)) return rc;
+  if (B == 0) return KF_OK;
+  FeatureF32Launch L{true, x, dfeat, dx, B, I, F, has_base, fa, (cudaStream_t)stream};
   return dispatch_bk(basis, L);
 }

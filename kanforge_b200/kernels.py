@@ -389,6 +389,139 @@ def kan_linear_fused(x, coef, base_weight, bias, edge_scale, edge_mask, grid, pl
     return y.reshape(*lead, coef.shape[0])
 
 
+# --- float32 layers on the tensor cores (three TF32 products) ------------------
+
+# Float32 layers run their contractions on the tensor cores (kf_gemm_tf32x3);
+# False routes them through the closed float32 CUDA-core primitives instead.
+FP32_TENSOR_CORES = True
+
+
+def tf32_ok(plan: KernelPlan | None, x: torch.Tensor, n_out: int, has_base: bool, coef_dtype=None) -> bool:
+    """Whether the float32 tensor-core path serves this call: float32 inputs and
+    parameters on CUDA, a B-spline or Chebyshev-feature plan with <= 31 feature
+    columns, outputs a multiple of 4."""
+    if plan is None or plan.kind not in ("cheb", "bspline") or x.dtype != torch.float32 or x.device.type != "cuda":
+        return False
+    if coef_dtype is not None and coef_dtype != torch.float32:
+        return False
+    nt, _ = fused_layout(plan, has_base)
+    if nt + 1 > 32 or n_out % 4:
+        return False
+    return plan.supported(_lib.KF_OP_F, _lib.KF_DTYPE_F32)
+
+
+def gemm_tf32x3(a, a_mn: bool, b, b_mn: bool, out, m: int, n: int, k: int, bias=None):
+    """out (m, n) = A B^T (+ bias) through kf_gemm_tf32x3; A (m, k) stored K-major
+    (a_mn False) or as its (k, m) transpose, B (n, k) likewise."""
+    _launch("kf_gemm_tf32x3", _ptr(a), int(a_mn), a.stride(0), _ptr(b), int(b_mn), b.stride(0), _ptr(bias), _ptr(out),
+            out.stride(0), m, n, k, _stream(out))
+    return out
+
+
+def packed_f32(coef, base_weight, edge_scale, edge_mask, plan: KernelPlan, f_pad: int) -> torch.Tensor:
+    """The float32 operand (O, I * f_pad) of the layout of kf_pack_coef:
+    coef * edge_scale * edge_mask (folded into Chebyshev features), zero
+    padding, and base_weight * edge_mask in the last column."""
+    n_out, n_in, _ = coef.shape
+    nt = plan.n_features(0)
+    sm = edge_mask.float() if edge_mask is not None else None
+    if edge_scale is not None:
+        sm = edge_scale.float() if sm is None else edge_scale.float() * sm
+    ce = coef.float() if sm is None else coef.float() * sm[..., None]
+    if plan.folded and not plan.is_identity_fold():
+        ce = ce @ _fold_on(plan, 0, coef.device)
+    parts = [ce[..., :nt], ce.new_zeros(n_out, n_in, f_pad - nt - 1)]
+    if base_weight is not None:
+        bw = base_weight.float() if edge_mask is None else base_weight.float() * edge_mask.float()
+        parts.append(bw[..., None])
+    else:
+        parts.append(ce.new_zeros(n_out, n_in, 1))
+    return torch.cat(parts, -1).reshape(n_out, n_in * f_pad).contiguous()
+
+
+class _Tf32KANLinear(torch.autograd.Function):
+    """Float32 KANLinear as three tcgen05 contractions with TF32 hi/lo splits
+    (float32 accuracy): y = feat packed^T + b, dfeat = dy packed (then dx by
+    the feature derivatives), dpacked = dy^T feat, with the chain rule of
+    the packed operand (fold, edge_scale, edge_mask, base column) applied by
+    torch on the (O, I, f_pad) gradient.  Double backward falls back to the
+    closed float32 primitives, as in the bf16 path."""
+
+    @staticmethod
+    def forward(ctx, x, coef, base_weight, bias, edge_scale, edge_mask, grid, plan):
+        n_out, n_in, _ = coef.shape
+        has_base = base_weight is not None
+        nt, f_pad = fused_layout(plan, has_base)
+        x = x.contiguous()
+        n_b = x.shape[0]
+        det = lambda t: None if t is None else t.detach()  # noqa: E731
+        packed = packed_f32(coef.detach(), det(base_weight), det(edge_scale), det(edge_mask), plan, f_pad)
+        g = None if grid is None else grid.detach().float().contiguous()
+        desc = plan.desc()
+        feat = torch.empty(n_b, n_in * f_pad, device=x.device, dtype=torch.float32)
+        _launch("kf_features_f32", _ptr(x), _ptr(g), _ptr(feat), n_b, n_in, nt, f_pad, int(has_base), ctypes.byref(desc),
+                _stream(x))
+        y = torch.empty(n_b, n_out, device=x.device, dtype=torch.float32)
+        b = None if bias is None else bias.detach().float().contiguous()
+        gemm_tf32x3(feat, False, packed, False, y, n_b, n_out, n_in * f_pad, bias=b)
+        ctx.save_for_backward(x, coef, base_weight, edge_scale, edge_mask, g)
+        ctx.feat, ctx.packed, ctx.plan, ctx.has_bias, ctx.layout = feat, packed, plan, bias is not None, (nt, f_pad)
+        return y
+
+    @staticmethod
+    def backward(ctx, gy):
+        x, coef, base_weight, edge_scale, edge_mask, grid = ctx.saved_tensors
+        plan = ctx.plan
+        need = ctx.needs_input_grad
+        if torch.is_grad_enabled():
+            ctx.feat = ctx.packed = None
+            return _fused_backward_differentiable(x, gy, coef, base_weight, edge_scale, edge_mask, grid, plan, need,
+                                                  ctx.has_bias)
+        nt, f_pad = ctx.layout
+        n_out, n_in, k = coef.shape
+        n_b = x.shape[0]
+        gy = gy.float().contiguous()
+        desc = plan.desc()
+        gx = gc = gb = gbias = gs = None
+        if need[0]:
+            dfeat = torch.empty(n_b, n_in * f_pad, device=x.device, dtype=torch.float32)
+            gemm_tf32x3(gy, False, ctx.packed, True, dfeat, n_b, n_in * f_pad, n_out)
+            gx = torch.empty_like(x)
+            _launch("kf_features_dot_f32", _ptr(x), _ptr(grid), _ptr(dfeat), _ptr(gx), n_b, n_in, nt, f_pad,
+                    int(base_weight is not None), ctypes.byref(desc), _stream(x))
+            del dfeat
+        if need[1] or need[2] or need[4]:
+            dpacked = torch.empty(n_out, n_in * f_pad, device=x.device, dtype=torch.float32)
+            gemm_tf32x3(gy, True, ctx.feat, True, dpacked, n_out, n_in * f_pad, n_b)
+            dp = dpacked.view(n_out, n_in, f_pad)
+            dce = dp[..., :nt]
+            if plan.folded and not plan.is_identity_fold():
+                dce = dce @ _fold_on(plan, 0, x.device).T
+            mask = edge_mask.float() if edge_mask is not None else None
+            sm = mask
+            if edge_scale is not None:
+                sm = edge_scale.float() if sm is None else edge_scale.float() * sm
+            if need[1]:
+                gc = (dce if sm is None else dce * sm[..., None]).to(coef.dtype)
+            if need[4] and edge_scale is not None:
+                gsc = (dce * coef.float()).sum(-1)
+                gs = (gsc if mask is None else gsc * mask).to(edge_scale.dtype)
+            if need[2] and base_weight is not None:
+                gbv = dp[..., f_pad - 1]
+                gb = (gbv if mask is None else gbv * mask).to(base_weight.dtype)
+        if need[3] and ctx.has_bias:
+            gbias = gy.sum(0)
+        ctx.feat = ctx.packed = None
+        return gx, gc, gb, gbias, gs, None, None, None
+
+
+def kan_linear_tf32(x, coef, base_weight, bias, edge_scale, edge_mask, grid, plan):
+    """Float32 KANLinear on (..., I) inputs through the tensor cores; see ``_Tf32KANLinear``."""
+    lead = x.shape[:-1]
+    y = _Tf32KANLinear.apply(x.reshape(-1, x.shape[-1]), coef, base_weight, bias, edge_scale, edge_mask, grid, plan)
+    return y.reshape(*lead, coef.shape[0])
+
+
 # --- edge_derivative ---------------------------------------------------------
 
 

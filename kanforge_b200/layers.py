@@ -209,6 +209,11 @@ class KANLinear(nn.Module):
             # coef * edge_scale * edge_mask and base_weight * edge_mask are formed inside the kernels
             return _kernels.kan_linear_fused(x, self.coef, self.base_weight, self.bias, self.edge_scale, self.edge_mask,
                                              self._grid(), plan)
+        if plan.kind != "rational" and _kernels.FP32_TENSOR_CORES and _kernels.tf32_ok(
+                plan, x, self.out_features, self.base_weight is not None, self.coef.dtype):
+            # float32: three TF32 products per contraction on the tensor cores
+            return _kernels.kan_linear_tf32(x, self.coef, self.base_weight, self.bias, self.edge_scale, self.edge_mask,
+                                            self._grid(), plan)
         coef_eff = self.effective_coef()
         base_eff = self.effective_base_weight()
         if plan.kind == "rational":

@@ -340,6 +340,88 @@ def test_bf16_wgrad_feature_matrix_path_equals_self_evaluating_path(monkeypatch,
         assert torch.equal(a, b)
 
 
+# ---------------------------------------------------------------------------
+# float32 layers on the tensor cores (kf_gemm_tf32x3, three TF32 products)
+# ---------------------------------------------------------------------------
+
+# (M, N, K, A MN-major, B MN-major, bias): ragged tiles and K steps, every major
+# combination, several persistent tiles per CTA
+GEMM_CASES = [
+    (300, 200, 100, False, False, True),
+    (129, 260, 37, True, True, False),
+    (513, 64, 1000, False, True, True),
+    (64, 513, 999, True, False, False),
+    (1, 4, 1, False, False, True),
+    (9, 80, 4, False, True, False),
+    (4096, 1024, 512, False, False, False),
+    (1024, 4096, 3000, True, True, False),
+]
+
+
+@pytest.mark.parametrize("m,n,k,a_mn,b_mn,bias", GEMM_CASES)
+def test_gemm_tf32x3_matches_float64(m, n, k, a_mn, b_mn, bias):
+    g = torch.Generator(device="cpu").manual_seed(m + n + k)
+    a = torch.randn(m, k, generator=g, dtype=torch.float64)
+    b = torch.randn(n, k, generator=g, dtype=torch.float64)
+    bv = torch.randn(n, generator=g, dtype=torch.float64) if bias else None
+    pad4 = lambda v: (v + 3) // 4 * 4  # noqa: E731
+    # operands in padded storage (row pitch a multiple of 4 floats), as the kernel takes them
+    sa = torch.zeros((k, pad4(m)) if a_mn else (m, pad4(k)), dtype=torch.float32, device=DEV)
+    sb = torch.zeros((k, pad4(n)) if b_mn else (n, pad4(k)), dtype=torch.float32, device=DEV)
+    if a_mn:
+        sa[:, :m] = a.T.float().to(DEV)
+    else:
+        sa[:, :k] = a.float().to(DEV)
+    if b_mn:
+        sb[:, :n] = b.T.float().to(DEV)
+    else:
+        sb[:, :k] = b.float().to(DEV)
+    out = torch.full((m, pad4(n)), float("nan"), dtype=torch.float32, device=DEV)
+    bias_d = None if bv is None else bv.float().to(DEV)
+    kb.kernels.gemm_tf32x3(sa, a_mn, sb, b_mn, out, m, n, k, bias=bias_d)
+    want = a.float().double() @ b.float().double().T + (0 if bv is None else bv.float().double())
+    close(out[:, :n], want.numpy(), FP32_TOL, "C")
+    assert torch.isnan(out[:, n:]).all()  # nothing written past N
+
+
+FP32_LAYER_CASES = [
+    # basis, B, I, O, base, bias, edge_scale
+    (kb.BSpline(8, 3), 257, 37, 136, True, True, True),
+    (kb.Chebyshev(12), 300, 40, 264, True, True, False),
+    (kb.Jacobi(6, 0.5, 0.5), 130, 64, 256, True, True, False),
+    (kb.BSpline(5, 3, (-2.0, 2.0)), 1030, 16, 520, True, False, False),
+    (kb.BSpline(20, 3), 140, 12, 40, True, True, False),      # 32-wide feature rows
+    (kb.Chebyshev(5), 129, 9, 24, False, False, False),
+    (kb.Chebyshev(4, input_map="identity"), 77, 12, 40, True, True, True),
+]
+
+
+@pytest.mark.parametrize("basis,n_b,n_in,n_out,base,bias,scale", FP32_LAYER_CASES,
+                         ids=lambda v: repr(v) if isinstance(v, kb.Basis) else str(v))
+def test_float32_layer_on_tensor_cores_matches_oracle(basis, n_b, n_in, n_out, base, bias, scale):
+    layer = make_bf16_layer(basis, n_in, n_out, base, bias, scale).float()
+    x0 = (torch.randn(n_b, n_in, device=DEV) * 1.2).clamp(-3, 3)
+    assert kb.kernels.tf32_ok(layer._plan, x0, n_out, base, layer.coef.dtype)
+    x = x0.clone().requires_grad_()
+    y = layer(x)
+    nodes = [y.grad_fn] + [f for f, _ in y.grad_fn.next_functions if f is not None]
+    assert any("Tf32" in type(f).__name__ for f in nodes)  # the tensor-core path served the call
+    dy = torch.randn(n_b, n_out, device=DEV) * 0.5
+    params = [p for _, p in layer.named_parameters()]
+    names = [n for n, _ in layer.named_parameters()]
+    grads = torch.autograd.grad(y, [x] + params, dy)
+    n = layer_numpy(layer)
+    xs = x0.double().cpu().numpy()
+    kw = dict(coef=n["coef"], base_weight=n["base_weight"], bias=n["bias"], spec=n["spec"], params=n["params"],
+              edge_scale=n["edge_scale"], edge_mask=n["edge_mask"])
+    close(y, ko.kan_linear(xs, **kw), FP32_TOL, "y")
+    want = ko.kan_linear_backward(xs, dy.double().cpu().numpy(), **kw)
+    close(grads[0], want["dx"], FP32_TOL, "dx")
+    key = {"coef": "dcoef", "base_weight": "dbase_weight", "bias": "dbias", "edge_scale": "dedge_scale"}
+    for nme, gr in zip(names, grads[1:]):
+        close(gr, want[key[nme]], FP32_TOL, f"d{nme}")
+
+
 def test_bf16_fused_multi_tile_persistent_against_float32_primitives():
     """Enough tiles that every persistent CTA runs several (both TMEM accumulators,
     every pipeline phase); checked against the float32 primitive kernels."""
