@@ -158,7 +158,8 @@ int kf_gemm_tf32x3(const float* a, int32_t a_mn_major, int64_t lda, const float*
 /* Float32 feature matrix of the float32 tensor-core path:
  *   feat[b, i*F + j] = phi_j(x[b,i]) (j < nf), 0 up to F-2, silu(x[b,i]) at F-1
  *   when has_base (the column layout of kf_pack_coef; F = 16 or 32).
- * grid (I, G+1) float32 for B-splines, else ignored.  x (B,I) float32.
+ * grid (I, G+1) float32 for B-splines, else ignored.  x (B,I) float32; feat
+ * 16-byte aligned.
  * (The reference evaluates these inside its Triton launches,
  * kanforge/kernels/triton_kernels.py:32-108.) */
 int kf_features_f32(const float* x, const float* grid, float* feat, int64_t B, int32_t I, int32_t nf, int32_t F,
@@ -167,8 +168,8 @@ int kf_features_f32(const float* x, const float* grid, float* feat, int64_t B, i
 /* Input gradient from the feature gradient of kf_gemm_tf32x3:
  *   dx[b,i] = sum_{j<nf} dfeat[b, i*F + j] d phi_j / dx (x[b,i])
  *           + dfeat[b, i*F + F-1] silu'(x[b,i])        (when has_base)
- * (the reference's gx = w * P_1, kanforge/torch/kernels.py:84, with the base
- * branch of layers.py:185-186.) */
+ * dfeat 16-byte aligned.  (The reference's gx = w * P_1,
+ * kanforge/torch/kernels.py:84, with the base branch of layers.py:185-186.) */
 int kf_features_dot_f32(const float* x, const float* grid, const float* dfeat, float* dx, int64_t B, int32_t I,
                         int32_t nf, int32_t F, int32_t has_base, const kf_basis_desc* basis, void* stream);
 

@@ -277,9 +277,9 @@ struct PrimLaunch {
 // ---------------------------------------------------------------------------
 constexpr int kFeatRows = 64;  // rows per CTA row block
 
-template <int BK>
+template <int BK, int F>
 __global__ void __launch_bounds__(kThreads) feature_f32_kernel(const float* __restrict__ x, float* __restrict__ feat,
-                                                               int64_t B, int I, int F, int has_base, FeatArgs fa) {
+                                                               int64_t B, int I, int has_base, FeatArgs fa) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= I) return;
   float t[KF_NK_MAX];
@@ -288,10 +288,13 @@ __global__ void __launch_bounds__(kThreads) feature_f32_kernel(const float* __re
   const int64_t b1 = min(B, b0 + kFeatRows);
   for (int64_t b = b0; b < b1; ++b) {
     const float xv = x[b * I + i];
-    float* dst = feat + (b * I + i) * F;
-    eval_features<BK>(fa, xv, 1.0f, t, dst, 1);
-    for (int j = fa.nf; j < F - 1; ++j) dst[j] = 0.0f;
-    dst[F - 1] = has_base ? silu_acc(xv) : 0.0f;
+    float f[F];  // the row, written out as float4s
+    eval_features<BK>(fa, xv, 1.0f, t, f, 1);
+    for (int j = fa.nf; j < F - 1; ++j) f[j] = 0.0f;
+    f[F - 1] = has_base ? silu_acc(xv) : 0.0f;
+    float4* dst = reinterpret_cast<float4*>(feat + (b * I + i) * F);
+#pragma unroll
+    for (int c = 0; c < F / 4; ++c) dst[c] = make_float4(f[4 * c], f[4 * c + 1], f[4 * c + 2], f[4 * c + 3]);
   }
 }
 
@@ -299,10 +302,10 @@ __global__ void __launch_bounds__(kThreads) feature_f32_kernel(const float* __re
 // B-splines: the native first-derivative window; Chebyshev features T_j(z):
 // dT_j/dz = j U_{j-1}(z) (U_0 = 1, U_1 = 2 z, U_j = 2 z U_{j-1} - U_{j-2}),
 // times dz/dx = 1 - z^2 under the tanh map.
-template <int BK>
+template <int BK, int F>
 __global__ void __launch_bounds__(kThreads) feature_dot_f32_kernel(const float* __restrict__ x, const float* __restrict__ dfeat,
-                                                                   float* __restrict__ dx, int64_t B, int I, int F,
-                                                                   int has_base, FeatArgs fa) {
+                                                                   float* __restrict__ dx, int64_t B, int I, int has_base,
+                                                                   FeatArgs fa) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= I) return;
   float t[KF_NK_MAX];
@@ -344,10 +347,13 @@ struct FeatureF32Launch {
   template <int BK>
   int operator()() const {
     const dim3 grid((unsigned)cdiv((int64_t)I, (int64_t)kThreads), (unsigned)cdiv(B, (int64_t)kFeatRows));
-    if (dot)
-      feature_dot_f32_kernel<BK><<<grid, kThreads, 0, stream>>>(x, dfeat, out, B, I, F, has_base, fa);
-    else
-      feature_f32_kernel<BK><<<grid, kThreads, 0, stream>>>(x, out, B, I, F, has_base, fa);
+    if (dot) {
+      if (F == 16) feature_dot_f32_kernel<BK, 16><<<grid, kThreads, 0, stream>>>(x, dfeat, out, B, I, has_base, fa);
+      else feature_dot_f32_kernel<BK, 32><<<grid, kThreads, 0, stream>>>(x, dfeat, out, B, I, has_base, fa);
+    } else {
+      if (F == 16) feature_f32_kernel<BK, 16><<<grid, kThreads, 0, stream>>>(x, out, B, I, has_base, fa);
+      else feature_f32_kernel<BK, 32><<<grid, kThreads, 0, stream>>>(x, out, B, I, has_base, fa);
+    }
     return check_launch(dot ? "kf_features_dot_f32" : "kf_features_f32");
   }
 };
@@ -414,6 +420,7 @@ extern "C" int kf_features_f32(const float* x, const float* grid, float* feat, i
   using namespace kf;
   clear_error();
   KF_CHECK_ARG(x && feat && B >= 0 && I >= 1, "kf_features_f32: bad arguments");
+  KF_CHECK_ARG(((uintptr_t)feat % 16) == 0, "kf_features_f32: feat must be 16-byte aligned");
   FeatArgs fa{};
   if (int rc = feature_args(basis, grid, nf, F, 0, fa)) return rc;
   if (int rc = bind_device(x)) return rc;
@@ -427,6 +434,7 @@ extern "C" int kf_features_dot_f32(const float* x, const float* grid, const floa
   using namespace kf;
   clear_error();
   KF_CHECK_ARG(x && dfeat && dx && B >= 0 && I >= 1, "kf_features_dot_f32: bad arguments");
+  KF_CHECK_ARG(((uintptr_t)dfeat % 16) == 0, "kf_features_dot_f32: dfeat must be 16-byte aligned");
   FeatArgs fa{};
   if (int rc = feature_args(basis, grid, nf, F, 1, fa)) return rc;
   if (int rc = bind_device(x)) return rc;
