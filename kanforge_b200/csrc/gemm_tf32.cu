@@ -19,15 +19,20 @@
 // every segment starts a fresh accumulator, and the epilogue adds the segment
 // sums in float32 registers (round to nearest).
 //
-// One persistent CTA per SM, 128 x 128 output tiles, K steps of 32 floats
-// (128-byte rows), 3 stages.  K-major tiles use the 128-byte swizzle (16-byte
+// Persistent CTA pairs (clusters of 2, tcgen05 cta_group::2): a pair tile is
+// 256 x 128 outputs, CTA r holding A rows 128 r .. 128 r + 127 and B rows
+// 64 r .. 64 r + 63 (half of B per CTA, so that a stage of A, B and their lo
+// halves is 48 KB and 4 stages fit; each stage's loads, split and MMAs form a
+// latency chain, and more stages in flight raise its throughput).  K steps of
+// 32 floats (128-byte rows).  K-major tiles use the 128-byte swizzle (16-byte
 // chunks XOR row % 8); MN-major tiles of 32-bit elements must use the
 // 128-byte swizzle with 32-byte atoms (32-byte chunks XOR row % 4, descriptor
 // layout type 1), the only MN-major layout the tensor core takes for TF32.
-// Warp roles: w0 TMA, w1 MMA issue, w4-7 split (hi in place, lo into a second
-// buffer of the same layout, fenced into the async proxy), w8-15 epilogue in
-// two column halves (two 128-column accumulators in tensor memory, so a
-// segment's drain overlaps the next segment's MMAs).
+// Warp roles in each CTA: w0 TMA (its own halves, local barriers), w1 MMA
+// issue (CTA 0), w4-7 split (hi in place, lo into a second buffer of the same
+// layout, fenced into the async proxy, then an arrive on CTA 0's barrier),
+// w8-15 epilogue in two column halves (two 128-column accumulators in tensor
+// memory, so a segment's drain overlaps the next segment's MMAs).
 #include "umma.cuh"
 
 namespace kf {
@@ -36,25 +41,28 @@ namespace {
 
 using namespace umma;
 
-constexpr int kGM = 128, kGN = 128, kGK = 32;  // tile rows, columns, K floats per stage
-constexpr int kGStages = 3;
+constexpr int kGM = 128, kGN = 128, kGK = 32;  // rows per CTA, pair tile columns, K floats per stage
+constexpr int kGPairM = 2 * kGM;               // pair tile rows
+constexpr int kGStages = 4;
 constexpr int kGSeg = 8;  // stages per accumulation segment
-constexpr int kGTile = kGM * kGK * 4;          // 16 KB: one operand tile of a stage
+constexpr int kGTile = kGM * kGK * 4;          // 16 KB: A tile of a stage (this CTA's 128 rows)
+constexpr int kGBHalf = (kGN / 2) * kGK * 4;   // 8 KB: this CTA's 64 rows of B
+constexpr int kGStage = 2 * (kGTile + kGBHalf);  // 48 KB: A, B, A_lo, B_lo
 constexpr int kGThreads = 512;
 constexpr int kGEpiWarps = 8;
 
 struct GemmCtl {
   uint64_t full[kGStages];   // TMA landed (expect_tx)
-  uint64_t split[kGStages];  // hi / lo written (4 split warps)
+  uint64_t split[kGStages];  // hi / lo written (4 split warps of each CTA; used in CTA 0)
   uint64_t empty[kGStages];  // MMAs of the stage done (tcgen05.commit)
   uint64_t acc_full[2];
-  uint64_t acc_empty[2];     // 8 epilogue warps
+  uint64_t acc_empty[2];     // 8 epilogue warps of each CTA (used in CTA 0)
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
 };
 
-constexpr size_t kGSmem = 1024 + (size_t)kGStages * 4 * kGTile + sizeof(GemmCtl);
+constexpr size_t kGSmem = 1024 + (size_t)kGStages * kGStage + sizeof(GemmCtl);
 
 struct GemmParams {
   const float* bias;  // (N) or null
@@ -65,27 +73,17 @@ struct GemmParams {
   int m_tiles, n_tiles, k_steps;
 };
 
-// ---- single-CTA tcgen05 forms ----------------------------------------------
-__device__ __forceinline__ void tmem_alloc1(uint32_t* dst_smem, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)), "r"(ncols)
-               : "memory");
-}
-__device__ __forceinline__ void tmem_relinquish1() {
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc1(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+// D[tmem of both CTAs] (+)= A[smem of both] * B[smem of both]^T, issued by one thread of CTA 0.
+__device__ __forceinline__ void mma_tf32_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+  const uint32_t mask0 = 0, mask1 = 0, mask2 = 0, mask3 = 0, mask4 = 0, mask5 = 0, mask6 = 0, mask7 = 0;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8, %9, %10, %11, %12}, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(mask0), "r"(mask1), "r"(mask2), "r"(mask3), "r"(mask4),
+      "r"(mask5), "r"(mask6), "r"(mask7)
       : "memory");
-}
-__device__ __forceinline__ void mma_commit1(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 // Instruction descriptor of kind::tf32 with f32 accumulation.
@@ -130,30 +128,33 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tf32x3_kernel(const __grid_
                                                                    const __grid_constant__ CUtensorMap tmap_b, GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  // stage s: A, B (TMA, then hi in place), A_lo, B_lo
-  auto tile = [&](int s, int which) { return base + ((size_t)s * 4 + which) * kGTile; };
-  GemmCtl* ctl = reinterpret_cast<GemmCtl*>(base + (size_t)kGStages * 4 * kGTile);
+  // stage s: A (16 KB), B half (8 KB) -- TMA, then hi in place -- A_lo, B_lo
+  auto a_tile = [&](int s, bool lo) { return base + (size_t)s * kGStage + (lo ? kGTile + kGBHalf : 0); };
+  auto b_tile = [&](int s, bool lo) { return base + (size_t)s * kGStage + kGTile + (lo ? kGTile + kGBHalf : 0); };
+  GemmCtl* ctl = reinterpret_cast<GemmCtl*>(base + (size_t)kGStages * kGStage);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = blockIdx.x / 2, n_pairs = gridDim.x / 2;
   volatile int* abort = &ctl->abort;
   const int n_tiles = p.m_tiles * p.n_tiles;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kGStages; ++s) {
       mbar_init(&ctl->full[s], 1);
-      mbar_init(&ctl->split[s], 4);
+      mbar_init(&ctl->split[s], 8);
       mbar_init(&ctl->empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&ctl->acc_full[a], 1);
-      mbar_init(&ctl->acc_empty[a], kGEpiWarps);
+      mbar_init(&ctl->acc_empty[a], 2 * kGEpiWarps);
     }
     mbar_init(&ctl->drain, 1);
     ctl->abort = 0;
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc1(&ctl->tmem_base, 256);
-    tmem_relinquish1();
+    tmem_alloc_pair(&ctl->tmem_base, 256);
+    tmem_relinquish_pair();
   }
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmap_a);
@@ -161,6 +162,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tf32x3_kernel(const __grid_
   }
   tc_fence_before();
   __syncthreads();
+  cluster_sync();  // both CTAs' barriers exist before any remote arrive
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
   auto tile_mn = [&](int t, int& m, int& n) {
@@ -176,25 +178,27 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tf32x3_kernel(const __grid_
   if (warp == 0) {
     if (lane == 0) {
       int it = 0;
-      for (int t = blockIdx.x; t < n_tiles && !*abort; t += gridDim.x) {
+      for (int t = pair; t < n_tiles && !*abort; t += n_pairs) {
         int m, n;
         tile_mn(t, m, n);
+        const int a_row = m * kGPairM + (int)rank * kGM;      // this CTA's A rows
+        const int b_row = n * kGN + (int)rank * (kGN / 2);    // this CTA's B rows
         for (int k = 0; k < p.k_steps; ++k, ++it) {
           const int s = it % kGStages;
           if (!mbar_wait(&ctl->empty[s], ((it / kGStages) & 1) ^ 1, abort)) break;
-          mbar_arrive_expect_tx(&ctl->full[s], 2 * kGTile);
+          mbar_arrive_expect_tx(&ctl->full[s], kGTile + kGBHalf);
           const int k0 = k * kGK;
           if (p.a_mn) {
 #pragma unroll
-            for (int c = 0; c < kGM / 32; ++c) tma_load_2d(tile(s, 0) + c * 4096, &tmap_a, &ctl->full[s], m * kGM + 32 * c, k0);
+            for (int c = 0; c < kGM / 32; ++c) tma_load_2d(a_tile(s, false) + c * 4096, &tmap_a, &ctl->full[s], a_row + 32 * c, k0);
           } else {
-            tma_load_2d(tile(s, 0), &tmap_a, &ctl->full[s], k0, m * kGM);
+            tma_load_2d(a_tile(s, false), &tmap_a, &ctl->full[s], k0, a_row);
           }
           if (p.b_mn) {
 #pragma unroll
-            for (int c = 0; c < kGN / 32; ++c) tma_load_2d(tile(s, 1) + c * 4096, &tmap_b, &ctl->full[s], n * kGN + 32 * c, k0);
+            for (int c = 0; c < kGN / 64; ++c) tma_load_2d(b_tile(s, false) + c * 4096, &tmap_b, &ctl->full[s], b_row + 32 * c, k0);
           } else {
-            tma_load_2d(tile(s, 1), &tmap_b, &ctl->full[s], k0, n * kGN);
+            tma_load_2d(b_tile(s, false), &tmap_b, &ctl->full[s], k0, b_row);
           }
         }
       }
@@ -206,14 +210,14 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tf32x3_kernel(const __grid_
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      const uint32_t idesc = idesc_tf32_f32(kGM, kGN, p.a_mn != 0, p.b_mn != 0);
+    if (rank == 0 && lane == 0) {
+      const uint32_t idesc = idesc_tf32_f32(kGPairM, kGN, p.a_mn != 0, p.b_mn != 0);
       int it = 0, sc = 0;  // stages and segments issued
       bool ok = true;
-      for (int t = blockIdx.x; t < n_tiles && ok && !*abort; t += gridDim.x) {
+      for (int t = pair; t < n_tiles && ok && !*abort; t += n_pairs) {
         for (int k0 = 0; k0 < p.k_steps && ok; k0 += kGSeg, ++sc) {
           const int acc = sc & 1;
-          if (!mbar_wait(&ctl->acc_empty[acc], ((sc >> 1) & 1) ^ 1, abort)) {
+          if (!mbar_wait_cluster(&ctl->acc_empty[acc], ((sc >> 1) & 1) ^ 1, abort)) {
             ok = false;
             break;
           }
@@ -222,36 +226,36 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tf32x3_kernel(const __grid_
           const int k1 = min(p.k_steps, k0 + kGSeg);
           for (int k = k0; k < k1; ++k, ++it) {
             const int s = it % kGStages;
-            if (!mbar_wait(&ctl->split[s], (it / kGStages) & 1, abort)) {
+            if (!mbar_wait_cluster(&ctl->split[s], (it / kGStages) & 1, abort)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            const uint32_t a_hi = smem_u32(tile(s, 0)), b_hi = smem_u32(tile(s, 1));
-            const uint32_t a_lo = smem_u32(tile(s, 2)), b_lo = smem_u32(tile(s, 3));
+            const uint32_t a_hi = smem_u32(a_tile(s, false)), b_hi = smem_u32(b_tile(s, false));
+            const uint32_t a_lo = smem_u32(a_tile(s, true)), b_lo = smem_u32(b_tile(s, true));
 #pragma unroll
             for (int j = 0; j < kGK / 8; ++j) {
               const uint64_t ah = operand_desc(a_hi, p.a_mn, j), al = operand_desc(a_lo, p.a_mn, j);
               const uint64_t bh = operand_desc(b_hi, p.b_mn, j), bl = operand_desc(b_lo, p.b_mn, j);
-              mma_tf32(d, ah, bh, idesc, (k > k0 || j > 0) ? 1u : 0u);
-              mma_tf32(d, ah, bl, idesc, 1u);
-              mma_tf32(d, al, bh, idesc, 1u);
+              mma_tf32_pair(d, ah, bh, idesc, (k > k0 || j > 0) ? 1u : 0u);
+              mma_tf32_pair(d, ah, bl, idesc, 1u);
+              mma_tf32_pair(d, al, bh, idesc, 1u);
             }
-            mma_commit1(&ctl->empty[s]);
+            mma_commit_pair(&ctl->empty[s], 0x3);
           }
           if (!ok) break;
-          mma_commit1(&ctl->acc_full[acc]);
+          mma_commit_pair(&ctl->acc_full[acc], 0x3);
         }
       }
       // every MMA issued above has completed once the drain barrier flips
-      mma_commit1(&ctl->drain);
+      mma_commit_pair(&ctl->drain, 0x1);
       mbar_drain(&ctl->drain, 0);
     }
   } else if (warp >= 4 && warp < 8) {
     // split: hi = tf32(v) in place, lo = v - hi at the same offset of the lo tile
     const int st = (warp - 4) * 32 + lane;  // 0 .. 127
     int it = 0;
-    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
+    for (int t = pair; t < n_tiles; t += n_pairs) {
       bool ok = true;
       for (int k = 0; k < p.k_steps; ++k, ++it) {
         const int s = it % kGStages;
@@ -261,10 +265,11 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tf32x3_kernel(const __grid_
         }
 #pragma unroll
         for (int w = 0; w < 2; ++w) {
-          float4* hi = reinterpret_cast<float4*>(tile(s, w));
-          float4* lo = reinterpret_cast<float4*>(tile(s, 2 + w));
+          float4* hi = reinterpret_cast<float4*>(w ? b_tile(s, false) : a_tile(s, false));
+          float4* lo = reinterpret_cast<float4*>(w ? b_tile(s, true) : a_tile(s, true));
+          const int n4 = (w ? kGBHalf : kGTile) / 16;
 #pragma unroll 4
-          for (int e = st; e < kGTile / 16; e += 128) {
+          for (int e = st; e < n4; e += 128) {
             const float4 v = hi[e];
             const float4 h = make_float4(tf32_rna(v.x), tf32_rna(v.y), tf32_rna(v.z), tf32_rna(v.w));
             hi[e] = h;
@@ -273,16 +278,19 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tf32x3_kernel(const __grid_
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&ctl->split[s]);
+        if (lane == 0) {
+          if (rank == 0) mbar_arrive(&ctl->split[s]);
+          else mbar_arrive_peer(&ctl->split[s], 0);
+        }
       }
       if (!ok) break;
     }
   } else if (warp >= 8) {
-    // half e of the columns (64 of them), lane quarter q of the rows: each
-    // thread sums its row's 64 columns over the tile's segments in registers
+    // half e of the columns (64 of them), lane quarter q of this CTA's rows:
+    // each thread sums its row's 64 columns over the tile's segments in registers
     const int q = warp % 4, e = (warp - 8) / 4;
     int sc = 0;
-    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
+    for (int t = pair; t < n_tiles; t += n_pairs) {
       int m, n;
       tile_mn(t, m, n);
       float r[64];
@@ -305,10 +313,10 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tf32x3_kernel(const __grid_
         for (int j = 0; j < 32; ++j) r[32 + j] += v[j];
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&ctl->acc_empty[acc]);
+        if (lane == 0) mbar_arrive_cluster(&ctl->acc_empty[acc], 0);
       }
       if (!ok) break;
-      const int64_t row = (int64_t)m * kGM + q * 32 + lane;
+      const int64_t row = (int64_t)m * kGPairM + (int64_t)rank * kGM + q * 32 + lane;
       const int64_t n0 = (int64_t)n * kGN + e * 64;
       if (row < p.M) {
         float* crow = p.C + row * p.ldc;
@@ -333,9 +341,10 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tf32x3_kernel(const __grid_
 
   tc_fence_before();
   __syncthreads();
+  cluster_sync();  // no remote arrive or MMA of the pair is outstanding past this point
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc1(tmem, 256);
+    tmem_dealloc_pair(tmem, 256);
   }
 }
 
@@ -391,7 +400,7 @@ extern "C" int kf_gemm_tf32x3(const float* a, int32_t a_mn_major, int64_t lda, c
   KF_CHECK_ARG(a && b && c, "kf_gemm_tf32x3: null operand");
   KF_CHECK_ARG(M >= 0 && N >= 0 && K >= 1 && ldc >= N, "kf_gemm_tf32x3: bad sizes (M %lld, N %lld, K %lld, ldc %lld)",
                (long long)M, (long long)N, (long long)K, (long long)ldc);
-  KF_CHECK_ARG(M < (int64_t)kGM * 65536 && N < (int64_t)kGN * 65536 && K < ((int64_t)1 << 36),
+  KF_CHECK_ARG(M < (int64_t)kGPairM * 65536 && N < (int64_t)kGN * 65536 && K < ((int64_t)1 << 36),
                "kf_gemm_tf32x3: sizes beyond the kernel limits");
   if (int rc = bind_device(a)) return rc;
   cudaStream_t s = (cudaStream_t)stream;
@@ -400,7 +409,7 @@ extern "C" int kf_gemm_tf32x3(const float* a, int32_t a_mn_major, int64_t lda, c
   // A: K-major (M rows of K) or MN-major (K rows of M); B likewise with N.
   if (int rc = a_mn_major ? make_tmap_f32(&ta, a, K, M, lda, 32, true) : make_tmap_f32(&ta, a, M, K, lda, kGM, false))
     return rc;
-  if (int rc = b_mn_major ? make_tmap_f32(&tb, b, K, N, ldb, 32, true) : make_tmap_f32(&tb, b, N, K, ldb, kGN, false))
+  if (int rc = b_mn_major ? make_tmap_f32(&tb, b, K, N, ldb, 32, true) : make_tmap_f32(&tb, b, N, K, ldb, kGN / 2, false))
     return rc;
   GemmParams p{};
   p.bias = bias;
@@ -411,7 +420,7 @@ extern "C" int kf_gemm_tf32x3(const float* a, int32_t a_mn_major, int64_t lda, c
   p.ldc = ldc;
   p.a_mn = a_mn_major ? 1 : 0;
   p.b_mn = b_mn_major ? 1 : 0;
-  p.m_tiles = (int)cdiv(M, (int64_t)kGM);
+  p.m_tiles = (int)cdiv(M, (int64_t)kGPairM);
   p.n_tiles = (int)cdiv(N, (int64_t)kGN);
   p.k_steps = (int)cdiv(K, (int64_t)kGK);
   // Tiles in flight together share the operand that is not streamed: along
@@ -427,8 +436,30 @@ extern "C" int kf_gemm_tf32x3(const float* a, int32_t a_mn_major, int64_t lda, c
   }
   int sms = 0;
   KF_CUDA_RET(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(kGThreads);
+  cfg.dynamicSmemBytes = kGSmem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.gridDim = dim3(2 * (unsigned)((sms > 0 ? sms : 148) / 2));
+  static int pair_cache[64] = {0};  // clusters of 2 that fit at once, per device
+  if (dev >= 0 && dev < 64 && pair_cache[dev] <= 0) {
+    int nc = 0;
+    if (cudaOccupancyMaxActiveClusters(&nc, gemm_tf32x3_kernel, &cfg) != cudaSuccess || nc <= 0) {
+      (void)cudaGetLastError();
+      nc = (sms > 0 ? sms : 148) / 2;
+    }
+    pair_cache[dev] = nc;
+  }
   const int64_t tiles = (int64_t)p.m_tiles * p.n_tiles;
-  const unsigned grid = (unsigned)std::min<int64_t>(tiles, sms > 0 ? sms : 148);
-  gemm_tf32x3_kernel<<<grid, kGThreads, kGSmem, s>>>(ta, tb, p);
+  const int pairs = (int)std::min<int64_t>(tiles, dev >= 0 && dev < 64 ? pair_cache[dev] : 1);
+  cfg.gridDim = dim3(2 * (unsigned)pairs);
+  KF_CUDA_RET(cudaLaunchKernelEx(&cfg, gemm_tf32x3_kernel, ta, tb, p));
   return check_launch("kf_gemm_tf32x3");
 }
