@@ -209,18 +209,21 @@ def test_edge_derivative_many_features_scalar_kernel(order):
     close(d, want, FP32_TOL, "edge")
 
 
-def test_higher_order_input_derivatives_and_gradient_penalty():
+@pytest.mark.parametrize("n_out", [5, 8])
+def test_higher_order_input_derivatives_and_gradient_penalty(n_out):
     """Closure of F/G/P: 1st-3rd input derivatives and the double backward into
-    coef (reference tests/test_kernels.py:102-121), against the oracle."""
+    coef (reference tests/test_kernels.py:102-121), against the oracle.  With
+    8 outputs the float32 forward runs on the tensor cores and the
+    differentiable backward on the primitives."""
     torch.manual_seed(0)
     for basis in (kb.BSpline(5, 3), kb.Chebyshev(5), kb.Jacobi(4, 0.5, 1.5)):
-        layer = kb.KANLinear(4, 5, basis, edge_scale=True, device=DEV)
+        layer = kb.KANLinear(4, n_out, basis, edge_scale=True, device=DEV)
         with torch.no_grad():
             layer.coef.normal_(0, 0.5)
             layer.edge_scale.uniform_(0.5, 1.5)
             layer.bias.normal_()
         x0 = torch.rand(37, 4, device=DEV) * 1.8 - 0.9
-        wts = torch.linspace(-1, 1, 5, device=DEV)
+        wts = torch.linspace(-1, 1, n_out, device=DEV)
         x = x0.clone().requires_grad_()
         y = layer(x)
         loss = (y * wts).sum()

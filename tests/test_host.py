@@ -197,3 +197,36 @@ def test_backend_argument_and_errors():
     assert not layer.uses_kernel(torch.device("cpu"))
     with pytest.raises(RuntimeError, match="device"):
         kb.KANLinear(3, 2, "bspline", backend="kernel").uses_kernel(torch.device("cpu"))
+
+
+@pytest.mark.parametrize("basis", [kb.Chebyshev(12), kb.BSpline(8, 3), kb.Chebyshev(4, input_map="identity")], ids=repr)
+def test_float32_packed_operand_layout(basis):
+    """The float32 tensor-core operand has the column layout of kf_pack_coef:
+    per input, the basis columns (coef * edge_scale * edge_mask, folded into
+    Chebyshev features), zeros, and base_weight * edge_mask last."""
+    torch.manual_seed(0)
+    plan = kb.plan_for(basis)
+    n_out, n_in, k = 6, 5, basis.size
+    nt, f_pad = kb.kernels.fused_layout(plan, True)
+    coef = torch.randn(n_out, n_in, k)
+    base = torch.randn(n_out, n_in)
+    scale = torch.rand(n_out, n_in) + 0.5
+    mask = (torch.rand(n_out, n_in) > 0.3).float()
+    packed = kb.kernels.packed_f32(coef, base, scale, mask, plan, f_pad).view(n_out, n_in, f_pad)
+    ce = (coef * (scale * mask)[..., None]).double().numpy()
+    fold = plan.fold(0)
+    want = ce @ fold if (plan.folded and not plan.is_identity_fold()) else ce
+    np.testing.assert_allclose(packed[..., :nt].double().numpy(), want[..., :nt], rtol=1e-5, atol=1e-6)
+    assert torch.all(packed[..., nt:f_pad - 1] == 0)
+    np.testing.assert_allclose(packed[..., f_pad - 1].numpy(), (base * mask).numpy(), rtol=1e-6)
+
+
+def test_float32_tensor_core_dispatch_rules():
+    """CPU tensors, bf16 inputs, rational plans and outputs that are not a
+    multiple of 4 never take the float32 tensor-core path."""
+    plan = kb.plan_for(kb.BSpline(8, 3))
+    x = torch.zeros(3, 4)
+    assert not kb.kernels.tf32_ok(plan, x, 8, True, torch.float32)  # CPU
+    assert not kb.kernels.tf32_ok(plan, x.to(torch.bfloat16), 8, True)
+    assert not kb.kernels.tf32_ok(kb.plan_for(kb.Rational(5, 4)), x, 8, False)
+    assert not kb.kernels.tf32_ok(None, x, 8, False)
