@@ -39,10 +39,17 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # DRAM bytes (read + write) per launch, from one-pass ncu captures of the full
 # bench workload, summarised in profiles/ with the commands that made them.
 TRAFFIC_PER_LAUNCH: dict[tuple[int, str], float] = {
+    (1, "kf_fwd"): (2713.3 + 131.2) * 1e6,  # bf16
+    (1, "kf_dgrad"): (324.1 + 123.8) * 1e6,
+    (1, "kf_wgrad"): (3946.0 + 22.2) * 1e6,
+    (1, "kf_features"): (138.0 + 2085.2) * 1e6,
+    (1, "kf_gemm_tf32x3"): (6613.7 + 1529.3) * 1e6,  # float32, mean of the three contractions
     (2, "kf_fwd"): 1909501440 + 134651136,
     (2, "kf_wgrad"): 10327355136 + 464899584,
     (2, "kf_dgrad"): 4572593664 + 132439296,
     (2, "kf_features"): 134248192 + 2084940544,
+    (3, "kf_rational_act"): (125.9 + 78.8) * 1e6,  # mean of the two layers
+    (3, "kf_rational_bwd"): (251.7 + 99.6 + 9.1) * 1e6,  # with the reduction, mean of the two layers
     (4, "kf_edge_derivative"): 67622000 + 4231267968,  # mean of 16 launches
 }
 
@@ -154,7 +161,8 @@ def build_workload(cfg: int, dtype_name: str, device, seed: int, tokens: int | N
         loss_fn = mean_square
         flops = 6 * 32768 * (768 * 3072 * 2)
         n_el = 32768 * (768 + 3072)
-        kwork = {"kf_rational_act": 4.0 * n_el, "kf_rational_bwd": 6.0 * n_el}  # bytes: read x + write r (bf16)
+        # bytes per launch (read x + write r, bf16), the mean of the two layers' launches
+        kwork = {"kf_rational_act": 4.0 * n_el / 2, "kf_rational_bwd": 6.0 * n_el / 2}
     elif cfg == 4:
         dtype = torch.float32
         model = kb.KANLinear(64, 64, kb.Jacobi(6, 0.5, 0.5), device=device)
