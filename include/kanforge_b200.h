@@ -143,7 +143,8 @@ int kf_features(const void* x, const float* knot_tab, void* feat, int64_t B, int
                 int32_t has_base, const kf_basis_desc* basis, void* stream);
 
 /* Float32 GEMM on tcgen05 with three TF32 products (hi*hi + hi*lo + lo*hi,
- * hi = tf32(v), lo = v - hi, split in shared memory), float32 accumulation:
+ * hi = v truncated to TF32 as the tensor core reads it, lo = v - hi, formed in
+ * shared memory), float32 accumulation:
  *   C[m,n] = sum_k A[m,k] B[n,k] (+ bias[n])
  * A is K-major (a_mn_major = 0: element (m,k) at a[m*lda + k]) or MN-major
  * (element (m,k) at a[k*lda + m]); B likewise with n.  lda, ldb multiples of

@@ -6,11 +6,13 @@
 //   C[m, n] = sum_k A[m, k] B[n, k]  (+ bias[n]),  all float32,
 //
 // A and B each stored K-major (row m / n contiguous in k) or MN-major (row k
-// contiguous in m / n).  Every operand tile is split in shared memory into
-// hi = tf32(v) (round to nearest) and lo = v - hi, and the accumulator takes
-// hi*hi + hi*lo + lo*hi (tcgen05.mma kind::tf32, float32 accumulation in
-// tensor memory): the dropped lo*lo term and the tf32 rounding of lo leave a
-// relative error near 2^-22 per product, float32 accuracy for these sums.
+// contiguous in m / n).  tcgen05.mma kind::tf32 reads the upper 19 bits of
+// each 32-bit operand (the low 13 mantissa bits are dropped), so the tile as
+// loaded is hi = trunc(v); a second tile in shared memory holds lo = v - hi
+// (exact in float32), and the accumulator takes hi*hi + hi*lo + lo*hi
+// (float32 accumulation in tensor memory): the dropped lo*lo term and the
+// truncation of lo leave a relative error near 2^-21 per product, float32
+// accuracy for these sums (the tests hold every case to 1e-5 of float64).
 //
 // The tensor core's float32 accumulation loses precision with the number of
 // MMAs accumulated into one tensor-memory accumulator (measured: the error
@@ -29,8 +31,8 @@
 // 128-byte swizzle with 32-byte atoms (32-byte chunks XOR row % 4, descriptor
 // layout type 1), the only MN-major layout the tensor core takes for TF32.
 // Warp roles in each CTA: w0 TMA (its own halves, local barriers), w1 MMA
-// issue (CTA 0), w4-7 split (hi in place, lo into a second buffer of the same
-// layout, fenced into the async proxy, then an arrive on CTA 0's barrier),
+// issue (CTA 0), w4-7 split (lo into a second buffer of the same layout,
+// fenced into the async proxy, then an arrive on CTA 0's barrier),
 // w8-15 epilogue in two column halves (two 128-column accumulators in tensor
 // memory, so a segment's drain overlaps the next segment's MMAs).
 #include "umma.cuh"
@@ -110,11 +112,8 @@ __device__ __forceinline__ uint64_t smem_desc_sw128_b32(uint32_t saddr, uint32_t
   return d;
 }
 
-__device__ __forceinline__ float tf32_rna(float v) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
-  return __uint_as_float(r);
-}
+// The value the tensor core reads from a 32-bit operand: its upper 19 bits.
+__device__ __forceinline__ float tf32_trunc(float v) { return __uint_as_float(__float_as_uint(v) & 0xFFFFE000u); }
 
 // Descriptor of k-step j (8 floats) of a 128-row operand tile.  K-major: rows
 // of 128 B, 8-row groups 1 KB apart, a k-step is 32 B along the row.
@@ -252,7 +251,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tf32x3_kernel(const __grid_
       mbar_drain(&ctl->drain, 0);
     }
   } else if (warp >= 4 && warp < 8) {
-    // split: hi = tf32(v) in place, lo = v - hi at the same offset of the lo tile
+    // split: lo = v - trunc(v) at the same offset of the lo tile (hi is the tile as loaded)
     const int st = (warp - 4) * 32 + lane;  // 0 .. 127
     int it = 0;
     for (int t = pair; t < n_tiles; t += n_pairs) {
@@ -265,15 +264,13 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_tf32x3_kernel(const __grid_
         }
 #pragma unroll
         for (int w = 0; w < 2; ++w) {
-          float4* hi = reinterpret_cast<float4*>(w ? b_tile(s, false) : a_tile(s, false));
+          const float4* hi = reinterpret_cast<const float4*>(w ? b_tile(s, false) : a_tile(s, false));
           float4* lo = reinterpret_cast<float4*>(w ? b_tile(s, true) : a_tile(s, true));
           const int n4 = (w ? kGBHalf : kGTile) / 16;
 #pragma unroll 4
           for (int e = st; e < n4; e += 128) {
             const float4 v = hi[e];
-            const float4 h = make_float4(tf32_rna(v.x), tf32_rna(v.y), tf32_rna(v.z), tf32_rna(v.w));
-            hi[e] = h;
-            lo[e] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+            lo[e] = make_float4(v.x - tf32_trunc(v.x), v.y - tf32_trunc(v.y), v.z - tf32_trunc(v.z), v.w - tf32_trunc(v.w));
           }
         }
         fence_proxy_async_smem();
