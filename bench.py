@@ -396,6 +396,33 @@ def run_ours(args, world, rank, local):
     torch.cuda.synchronize()
     kb.kernels.check_device_errors()
 
+    # --graph: one step captured into a CUDA graph and replayed (launch-bound
+    # configurations); the library launches of a step are counted at capture.
+    graph = graph_out = None
+    graph_launches = 0
+    if args.graph:
+        if world > 1:
+            raise SystemExit("--graph runs on one GPU")
+        side = torch.cuda.Stream(device)
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                step()
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        launches_c0 = kb.kernels.LAUNCH_COUNT
+        with torch.cuda.graph(graph):
+            graph_out = step()
+        graph_launches = kb.kernels.LAUNCH_COUNT - launches_c0
+        for _ in range(args.warmup):
+            graph.replay()
+        torch.cuda.synchronize()
+        kb.kernels.check_device_errors()
+
+        def full_step():  # noqa: F811
+            graph.replay()
+            return graph_out
+
     timer = KernelTimer()
     kb.kernels.set_launch_observer(timer)
     uuid = None
@@ -418,6 +445,8 @@ def run_ours(args, world, rank, local):
     barrier()
     clocks = sampler.stop()
     launches = kb.kernels.LAUNCH_COUNT - launches0  # library kernels launched in the timed region
+    if graph is not None:
+        launches = graph_launches * args.steps
     elapsed_ms = start.elapsed_time(end)
     if pg is not None:
         elapsed_ms = max_over_ranks(elapsed_ms, device, pg)
@@ -469,6 +498,13 @@ def run_ours(args, world, rank, local):
         free[slot].record()
 
     def e2e_run(n_steps):
+        if graph is not None:  # the graph reads x and writes its output in place
+            for _ in range(n_steps):
+                x.detach().copy_(x_host, non_blocking=True)
+                graph.replay()
+                res = graph_out[0, 0, :1] if cfg == 4 else graph_out.detach().float().reshape(1)
+                loss_host.copy_(res, non_blocking=True)
+            return
         issue_copy(0)
         for k in range(n_steps):
             e2e_step(k, k == n_steps - 1)
@@ -516,7 +552,8 @@ def run_ours(args, world, rank, local):
         "scaling": "weak", "vs_baseline": None, "dtype": {torch.bfloat16: "bf16", torch.float32: "f32"}[dtype],
         "data": "synthetic",
         "config": {"workload": CONFIGS[cfg]["workload"], "index": cfg, "global_batch": world * units,
-                   "parallelism": f"dp{world}", "l2": "inputs larger than L2 (126 MB)" if cfg in (1, 2, 3, 4) else "small (latency case)"},
+                   "parallelism": f"dp{world}", "l2": "inputs larger than L2 (126 MB)" if cfg in (1, 2, 3, 4) else "small (latency case)",
+                   **({"cuda_graph": True} if graph is not None else {})},
         "tflops_per_step": None if flops is None else flops / 1e12,
         "achieved_tflops": None if flops is None else flops * world / (ms_per_step / 1e3) / 1e12,
         "roofline": roofline,
@@ -548,6 +585,8 @@ def main(argv=None):
     ap.add_argument("--dtype", default="bf16", choices=["bf16", "fp32"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--graph", action="store_true",
+                    help="replay one captured CUDA graph per step (launch-bound configurations, one GPU)")
     ap.add_argument("--tokens", type=int, default=None,
                     help="profiling case: override the batch of configs 1, 2, 4 (not a bench line)")
     args = ap.parse_args(argv)
