@@ -397,8 +397,10 @@ extern "C" int kf_gemm_tf32x3(const float* a, int32_t a_mn_major, int64_t lda, c
   KF_CHECK_ARG(a && b && c, "kf_gemm_tf32x3: null operand");
   KF_CHECK_ARG(M >= 0 && N >= 0 && K >= 1 && ldc >= N, "kf_gemm_tf32x3: bad sizes (M %lld, N %lld, K %lld, ldc %lld)",
                (long long)M, (long long)N, (long long)K, (long long)ldc);
-  KF_CHECK_ARG(M < (int64_t)kGPairM * 65536 && N < (int64_t)kGN * 65536 && K < ((int64_t)1 << 36),
-               "kf_gemm_tf32x3: sizes beyond the kernel limits");
+  // tile counts and TMA coordinates are 32-bit
+  KF_CHECK_ARG(M < (int64_t)kGPairM * 65536 && N < (int64_t)kGN * 65536 && K <= (int64_t)INT32_MAX - kGK,
+               "kf_gemm_tf32x3: sizes beyond the kernel limits (M %lld, N %lld, K %lld)", (long long)M, (long long)N,
+               (long long)K);
   if (int rc = bind_device(a)) return rc;
   cudaStream_t s = (cudaStream_t)stream;
   if (M == 0 || N == 0) return KF_OK;
