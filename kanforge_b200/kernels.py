@@ -395,6 +395,12 @@ def kan_linear_fused(x, coef, base_weight, bias, edge_scale, edge_mask, grid, pl
 # False routes them through the closed float32 CUDA-core primitives instead.
 FP32_TENSOR_CORES = True
 
+# The float32 tensor-core path holds a (B, I * f_pad) float32 feature matrix
+# from the forward to the backward and makes a second one (the feature
+# gradient) in the backward; above this many bytes for the two, calls take the
+# primitives, which need no such buffers.
+FP32_FEATURE_BYTES_MAX = 32 << 30
+
 
 def tf32_ok(plan: KernelPlan | None, x: torch.Tensor, n_out: int, has_base: bool, coef_dtype=None) -> bool:
     """Whether the float32 tensor-core path serves this call: float32 inputs and
@@ -404,8 +410,10 @@ def tf32_ok(plan: KernelPlan | None, x: torch.Tensor, n_out: int, has_base: bool
         return False
     if coef_dtype is not None and coef_dtype != torch.float32:
         return False
-    nt, _ = fused_layout(plan, has_base)
+    nt, f_pad = fused_layout(plan, has_base)
     if nt + 1 > 32 or n_out % 4:
+        return False
+    if 2 * 4 * x.numel() * f_pad > FP32_FEATURE_BYTES_MAX:
         return False
     return plan.supported(_lib.KF_OP_F, _lib.KF_DTYPE_F32)
 

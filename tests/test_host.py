@@ -230,3 +230,12 @@ def test_float32_tensor_core_dispatch_rules():
     assert not kb.kernels.tf32_ok(plan, x.to(torch.bfloat16), 8, True)
     assert not kb.kernels.tf32_ok(kb.plan_for(kb.Rational(5, 4)), x, 8, False)
     assert not kb.kernels.tf32_ok(None, x, 8, False)
+
+
+def test_float32_tensor_core_path_respects_its_memory_budget(monkeypatch):
+    """Above FP32_FEATURE_BYTES_MAX the float32 layer takes the primitives
+    (checked on the dispatch rule; the CPU tensor itself never qualifies)."""
+    plan = kb.plan_for(kb.BSpline(8, 3))
+    x = torch.zeros(1000, 64)
+    monkeypatch.setattr(kb.kernels, "FP32_FEATURE_BYTES_MAX", 0)
+    assert not kb.kernels.tf32_ok(plan, x, 8, True, torch.float32)
