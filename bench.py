@@ -27,6 +27,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 from pathlib import Path
 
@@ -237,7 +238,7 @@ class ClockSampler:
     def __init__(self, uuid: str | None):
         self.uuid = uuid
         self.proc = None
-        self.path = ROOT / "gpurun_out" / f"clocks_{os.getpid()}.csv"
+        self.path = Path(tempfile.gettempdir()) / f"kanforge_b200_clocks_{os.getpid()}.csv"
 
     def start(self):
         try:
@@ -256,7 +257,10 @@ class ClockSampler:
         self.proc.wait(timeout=10)
         self.fh.close()
         rows = []
-        for line in self.path.read_text().splitlines():
+        text = self.path.read_text()
+        with contextlib.suppress(OSError):
+            self.path.unlink()
+        for line in text.splitlines():
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 10:
                 continue
