@@ -166,6 +166,13 @@ int kf_gemm_tf32x3(const float* a, int32_t a_mn_major, int64_t lda, const float*
 int kf_features_f32(const float* x, const float* grid, float* feat, int64_t B, int32_t I, int32_t nf, int32_t F,
                     int32_t has_base, const kf_basis_desc* basis, void* stream);
 
+/* The same float32 feature matrix for B-spline bases from the knot tables of
+ * kf_knot_tables (knot_tab, 16-byte aligned) instead of the raw grid: the
+ * knot search and Cox-de Boor steps of kf_features, float32 output, silu(x)
+ * at F-1 when has_base.  nt = the basis size; F = 16 or 32. */
+int kf_features_spline_f32(const float* x, const float* knot_tab, float* feat, int64_t B, int32_t I, int32_t nt, int32_t F,
+                           int32_t has_base, const kf_basis_desc* basis, void* stream);
+
 /* Input gradient from the feature gradient of kf_gemm_tf32x3:
  *   dx[b,i] = sum_{j<nf} dfeat[b, i*F + j] d phi_j / dx (x[b,i])
  *           + dfeat[b, i*F + F-1] silu'(x[b,i])        (when has_base)

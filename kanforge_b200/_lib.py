@@ -78,6 +78,10 @@ PROTOTYPES = {
         ctypes.c_int,
         [_vp, _vp, _vp, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, ctypes.POINTER(BasisDesc), _vp],
     ),
+    "kf_features_spline_f32": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, ctypes.POINTER(BasisDesc), _vp],
+    ),
     "kf_features_dot_f32": (
         ctypes.c_int,
         [_vp, _vp, _vp, _vp, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, ctypes.POINTER(BasisDesc), _vp],

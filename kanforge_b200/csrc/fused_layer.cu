@@ -1448,6 +1448,77 @@ __global__ void __launch_bounds__(256) feature_spline_kernel(const __nv_bfloat16
   }
 }
 
+// Float32 rows of the same B-spline features for the float32 tensor-core
+// path: the tables, knot search and Cox-de Boor steps of
+// feature_spline_kernel, the values placed among the row's F floats by
+// selects, silu(x) (accurate exponential and division) in column F - 1, each
+// lane storing its own row as float4s.
+template <int BK, int F>
+__global__ void __launch_bounds__(256) feature_spline_f32_kernel(const float* __restrict__ x, float* __restrict__ feat,
+                                                                 int64_t B, int I, BasisDev bd, int ts) {
+  extern __shared__ float tabs[];  // [(BK + 1) * ts][32]
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int i0 = blockIdx.y * 32;
+  for (int e = threadIdx.x; e < 32 * (BK + 1) * ts; e += blockDim.x) {
+    const int u = e / ((BK + 1) * ts), rem = e % ((BK + 1) * ts);
+    const int q = rem / ts, r = rem % ts;
+    tabs[rem * 32 + u] = (i0 + u < I) ? __ldg(bd.tab + (size_t)(i0 + u) * ((BK + 1) * kTabStride) + q * kTabStride + r) : 0.0f;
+  }
+  __syncthreads();
+  const int i = i0 + lane;
+  if (i >= I) return;
+  const float* tu = tabs + lane;  // element k at tu[32 k]
+  const int nk = bd.nk, top = pow2_floor(nk - 2);
+  const float t_lo = tu[0], t_hi = tu[32 * (nk - 1)];
+  const int64_t stride = (int64_t)gridDim.x * 8;
+  for (int64_t b0 = (int64_t)blockIdx.x * 8 + warp; b0 < B; b0 += kSplineRows * stride) {
+    float xs[kSplineRows];
+#pragma unroll
+    for (int u = 0; u < kSplineRows; ++u) {
+      const int64_t b = b0 + u * stride;
+      xs[u] = b < B ? x[b * I + i] : 0.0f;
+    }
+    int pos[kSplineRows];
+#pragma unroll
+    for (int u = 0; u < kSplineRows; ++u) pos[u] = 0;
+    for (int st = top; st > 0; st >>= 1) {
+#pragma unroll
+      for (int u = 0; u < kSplineRows; ++u) {
+        const int c = pos[u] + st;
+        if (c <= nk - 2 && tu[32 * c] <= xs[u]) pos[u] = c;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kSplineRows; ++u) {
+      const int64_t b = b0 + u * stride;
+      if (b >= B) break;
+      const float xv = xs[u];
+      float f[F];
+#pragma unroll
+      for (int k = 0; k < F; ++k) f[k] = 0.0f;
+      const int j0 = (xv >= t_lo && xv < t_hi) ? pos[u] : -1;
+      if (j0 >= 0) {
+        float vv[BK + 1];
+        bspline_local_tab<BK, 32>(xv, tu, nk, j0, 0, vv, 32 * ts);
+        const int s0 = j0 - BK;
+#pragma unroll
+        for (int k = 0; k < F - 1; ++k) {
+          const int m = k - s0;
+          float v = 0.0f;
+#pragma unroll
+          for (int mm = 0; mm <= BK; ++mm)
+            if (m == mm) v = vv[mm];
+          f[k] = k < bd.nt ? v : 0.0f;
+        }
+      }
+      f[F - 1] = bd.has_base ? silu_acc(xv) : 0.0f;
+      float4* dst = reinterpret_cast<float4*>(feat + (b * I + i) * F);
+#pragma unroll
+      for (int c = 0; c < F / 4; ++c) dst[c] = make_float4(f[4 * c], f[4 * c + 1], f[4 * c + 2], f[4 * c + 3]);
+    }
+  }
+}
+
 // ===========================================================================
 // host side
 // ===========================================================================
@@ -1687,7 +1758,34 @@ struct FeatureLaunch {
   }
 };
 
+struct FeatureF32SplineLaunch {
+  const float* x;
+  float* feat;
+  int64_t B;
+  int I;
+  BasisDev bd;
+  cudaStream_t stream;
+  template <int BK, int F>
+  int go() const {
+    if constexpr (BK == 0) {
+      set_error("kf_features_f32: the knot-table kernel is for B-splines");
+      return KF_ERR_UNSUPPORTED;
+    } else {
+      const unsigned gy = (unsigned)cdiv(I, 32);
+      const int64_t want = std::max<int64_t>(1, (int64_t)sm_count() * 8 / gy);
+      const unsigned gx = (unsigned)std::max<int64_t>(1, std::min<int64_t>(cdiv(B, (int64_t)8), want));
+      const int ts = (bd.nk + 15) & ~15;  // table row stride in shared memory (>= nk)
+      const size_t smem = sizeof(float) * 32 * (BK + 1) * ts;
+      KF_CUDA_RET(cudaFuncSetAttribute(feature_spline_f32_kernel<BK, F>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem));
+      feature_spline_f32_kernel<BK, F><<<dim3(gx, gy), 256, smem, stream>>>(x, feat, B, I, bd, ts);
+      return check_launch("kf_features_f32");
+    }
+  }
+};
+
 }  // namespace
+
 
 }  // namespace kf
 
@@ -1756,6 +1854,22 @@ extern "C" int kf_dgrad(const void* x, const void* dy, const void* packed, const
   if (int rc = make_tmap_bf16(&tdy, dy, B, O, kBK, kBM)) return rc;
   if (int rc = make_tmap_bf16(&tc, packed, O, (int64_t)I * f_pad, 64, kBK)) return rc;
   DgradLaunch L{&tdy, &tc, p, (cudaStream_t)stream};
+  return dispatch_fused(basis, f_pad, L);
+}
+
+extern "C" int kf_features_spline_f32(const float* x, const float* knot_tab, float* feat, int64_t B, int32_t I, int32_t nt,
+                                      int32_t f_pad, int32_t has_base, const kf_basis_desc* basis, void* stream) {
+  using namespace kf;
+  clear_error();
+  KF_CHECK_ARG(x && feat, "kf_features_spline_f32: null tensor pointer");
+  KF_CHECK_ARG(basis && basis->kind == KF_BASIS_BSPLINE, "kf_features_spline_f32: B-spline bases only");
+  if (int rc = bind_device(x)) return rc;
+  KF_CHECK_ARG(B >= 0 && I >= 1, "kf_features_spline_f32: bad sizes");
+  KF_CHECK_ARG(((uintptr_t)feat % 16) == 0, "kf_features_spline_f32: feat must be 16-byte aligned");
+  BasisDev bd{};
+  if (int rc = fill_basis(basis, knot_tab, nt, has_base, f_pad, bd)) return rc;
+  if (B == 0) return KF_OK;
+  FeatureF32SplineLaunch L{x, feat, B, I, bd, (cudaStream_t)stream};
   return dispatch_fused(basis, f_pad, L);
 }
 

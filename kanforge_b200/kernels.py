@@ -467,8 +467,14 @@ class _Tf32KANLinear(torch.autograd.Function):
         g = None if grid is None else grid.detach().float().contiguous()
         desc = plan.desc()
         feat = torch.empty(n_b, n_in * f_pad, device=x.device, dtype=torch.float32)
-        _launch("kf_features_f32", _ptr(x), _ptr(g), _ptr(feat), n_b, n_in, nt, f_pad, int(has_base), ctypes.byref(desc),
-                _stream(x))
+        if plan.kind == "bspline":
+            tab = knot_tables(g, plan)
+            _launch("kf_features_spline_f32", _ptr(x), _ptr(tab), _ptr(feat), n_b, n_in, nt, f_pad, int(has_base),
+                    ctypes.byref(desc), _stream(x))
+            del tab
+        else:
+            _launch("kf_features_f32", _ptr(x), _ptr(g), _ptr(feat), n_b, n_in, nt, f_pad, int(has_base),
+                    ctypes.byref(desc), _stream(x))
         y = torch.empty(n_b, n_out, device=x.device, dtype=torch.float32)
         b = None if bias is None else bias.detach().float().contiguous()
         gemm_tf32x3(feat, False, packed, False, y, n_b, n_out, n_in * f_pad, bias=b)

@@ -9,6 +9,8 @@ Tolerances (metric max|a-b| / max(1, max|b|), reference tests/test_kernels.py:96
 
 from __future__ import annotations
 
+import ctypes
+
 import numpy as np
 import pytest
 import torch
@@ -423,6 +425,33 @@ def test_float32_layer_on_tensor_cores_matches_oracle(basis, n_b, n_in, n_out, b
     key = {"coef": "dcoef", "base_weight": "dbase_weight", "bias": "dbias", "edge_scale": "dedge_scale"}
     for nme, gr in zip(names, grads[1:]):
         close(gr, want[key[nme]], FP32_TOL, f"d{nme}")
+
+
+@pytest.mark.parametrize("order,grid_size,base", [(1, 6, True), (2, 9, False), (3, 8, True), (4, 5, True),
+                                                  (5, 7, False), (3, 20, True)])
+def test_float32_spline_features_from_knot_tables_match_grid_kernel(order, grid_size, base):
+    """kf_features_spline_f32 (knot tables) against kf_features_f32 (raw grid) on
+    non-uniform grids, with inputs on knots, outside the grid and at its ends."""
+    n_b, n_in = 1000, 37
+    layer = make_bf16_layer(kb.BSpline(grid_size, order), n_in, 8, base, False, False).float()
+    plan, g = layer._plan, layer.basis_grid.float().contiguous()
+    nt, f_pad = kb.kernels.fused_layout(plan, base)
+    x = (torch.randn(n_b, n_in, device=DEV) * 1.2).clamp(-3, 3)
+    x[:64] = g[:, torch.randint(0, g.shape[1], (64,))].T  # exactly on knots (ends included)
+    x[64:80] = 5.0
+    x[80:96] = -5.0
+    x = x.contiguous()
+    desc = plan.desc()
+    want = torch.full((n_b, n_in * f_pad), float("nan"), device=DEV)
+    got = torch.full_like(want, float("nan"))
+    kb.kernels._launch("kf_features_f32", x.data_ptr(), g.data_ptr(), want.data_ptr(), n_b, n_in, nt, f_pad, int(base),
+                       ctypes.byref(desc), kb.kernels._stream(x))
+    tab = kb.kernels.knot_tables(g, plan)
+    kb.kernels._launch("kf_features_spline_f32", x.data_ptr(), tab.data_ptr(), got.data_ptr(), n_b, n_in, nt, f_pad,
+                       int(base), ctypes.byref(desc), kb.kernels._stream(x))
+    torch.cuda.synchronize()
+    assert not torch.isnan(got).any()
+    torch.testing.assert_close(got, want, rtol=1e-5, atol=2e-6)
 
 
 def test_bf16_fused_multi_tile_persistent_against_float32_primitives():
