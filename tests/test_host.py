@@ -239,3 +239,27 @@ def test_float32_tensor_core_path_respects_its_memory_budget(monkeypatch):
     x = torch.zeros(1000, 64)
     monkeypatch.setattr(kb.kernels, "FP32_FEATURE_BYTES_MAX", 0)
     assert not kb.kernels.tf32_ok(plan, x, 8, True, torch.float32)
+
+
+@pytest.mark.parametrize("basis,first", [(kb.BSpline(8, 3), ["kf_knot_tables", "kf_features_spline_f32"]),
+                                         (kb.Chebyshev(12), ["kf_features_f32"])])
+def test_float32_tensor_core_forward_launch_sequence(monkeypatch, basis, first):
+    """The float32 layer's forward launches: B-spline features from the knot
+    tables, other bases from kf_features_f32, then one GEMM with the bias
+    (launches recorded, nothing executed)."""
+    calls = []
+    monkeypatch.setattr(kb.kernels, "_launch", lambda name, *args: calls.append((name, args)))
+    monkeypatch.setattr(kb.kernels, "_stream", lambda t: None)
+    layer = kb.KANLinear(16, 8, basis)
+    x = torch.zeros(5, 16)
+    with torch.no_grad():
+        y = kb.kernels.kan_linear_tf32(x, layer.coef, layer.base_weight, layer.bias, layer.edge_scale, layer.edge_mask,
+                                       layer._grid(), layer._plan)
+    assert y.shape == (5, 8)
+    assert [n for n, _ in calls] == first + ["kf_gemm_tf32x3"]
+    nt, f_pad = kb.kernels.fused_layout(layer._plan, True)
+    feat_args = calls[len(first) - 1][1]
+    assert feat_args[3:8] == (5, 16, nt, f_pad, 1)  # B, I, nt, f_pad, has_base
+    gemm = calls[-1][1]
+    assert gemm[-4:-1] == (5, 8, 16 * f_pad)  # M = tokens, N = outputs, K = I * f_pad
+    assert gemm[6].value == layer.bias.data_ptr()
