@@ -237,9 +237,13 @@ int64_t kf_rational_workspace(int64_t B, int32_t I, const kf_basis_desc* basis);
  * KF_RATIONAL_NOALLOC_MAX_FLOATS floats (4 MiB) that is part of the library's
  * device code, so every GPU that loads the library holds it until the process
  * exits.  Requires I * (p + 1 + q) <= KF_RATIONAL_NOALLOC_MAX_FLOATS (else
- * KF_ERR_ARG with a message) and allocates and frees nothing.  The first call
- * on a device looks up the array's device address (cudaGetSymbolAddress) and
- * must come before any stream capture.  All calls share the array: calls whose
+ * KF_ERR_ARG with a message) and allocates and frees nothing itself.  The first
+ * call on a device looks up the array's device address (cudaGetSymbolAddress)
+ * and must come before any stream capture.  With CUDA's lazy module loading
+ * (the default) that first call may also be what loads the library's device
+ * code onto the device, which places the array in device memory then; a host
+ * that must see no device allocation after start-up should make one call per
+ * device at start-up.  All calls share the array: calls whose
  * kernels overlap on the GPU race.  The caller still passes inputs and outputs.
  * Has no counterpart in the reference. */
 #define KF_RATIONAL_NOALLOC_MAX_FLOATS (1 << 20)

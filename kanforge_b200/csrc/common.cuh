@@ -6,6 +6,7 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <algorithm>
 #include <cstdio>
 #include <string>
 

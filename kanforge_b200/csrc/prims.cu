@@ -275,7 +275,8 @@ struct PrimLaunch {
 // is fused (the layout of kf_pack_coef).  Threads run along the inputs (one
 // input's knots computed once per thread), CTAs along row blocks.
 // ---------------------------------------------------------------------------
-constexpr int kFeatRows = 64;  // rows per CTA row block
+constexpr int kFeatRows = 64;      // rows per CTA row block
+constexpr int64_t kMaxGridY = 65535;  // gridDim.y limit: larger B strides over the row blocks
 
 template <int BK, int F>
 __global__ void __launch_bounds__(kThreads) feature_f32_kernel(const float* __restrict__ x, float* __restrict__ feat,
@@ -284,9 +285,9 @@ __global__ void __launch_bounds__(kThreads) feature_f32_kernel(const float* __re
   if (i >= I) return;
   float t[KF_NK_MAX];
   load_knots<BK>(fa, i, t, 0, 1);
-  const int64_t b0 = (int64_t)blockIdx.y * kFeatRows;
-  const int64_t b1 = min(B, b0 + kFeatRows);
-  for (int64_t b = b0; b < b1; ++b) {
+  // row blocks of kFeatRows, strided by gridDim.y (capped at 65535 by the launch)
+  for (int64_t b0 = (int64_t)blockIdx.y * kFeatRows; b0 < B; b0 += (int64_t)gridDim.y * kFeatRows)
+  for (int64_t b = b0, b1 = min(B, b0 + kFeatRows); b < b1; ++b) {
     const float xv = x[b * I + i];
     float f[F];  // the row, written out as float4s
     eval_features<BK>(fa, xv, 1.0f, t, f, 1);
@@ -310,9 +311,9 @@ __global__ void __launch_bounds__(kThreads) feature_dot_f32_kernel(const float* 
   if (i >= I) return;
   float t[KF_NK_MAX];
   load_knots<BK>(fa, i, t, 0, 1);
-  const int64_t b0 = (int64_t)blockIdx.y * kFeatRows;
-  const int64_t b1 = min(B, b0 + kFeatRows);
-  for (int64_t b = b0; b < b1; ++b) {
+  // row blocks of kFeatRows, strided by gridDim.y (capped at 65535 by the launch)
+  for (int64_t b0 = (int64_t)blockIdx.y * kFeatRows; b0 < B; b0 += (int64_t)gridDim.y * kFeatRows)
+  for (int64_t b = b0, b1 = min(B, b0 + kFeatRows); b < b1; ++b) {
     const float xv = x[b * I + i];
     const float* h = dfeat + (b * I + i) * F;
     float acc;
@@ -346,7 +347,8 @@ struct FeatureF32Launch {
   cudaStream_t stream;
   template <int BK>
   int operator()() const {
-    const dim3 grid((unsigned)cdiv((int64_t)I, (int64_t)kThreads), (unsigned)cdiv(B, (int64_t)kFeatRows));
+    const dim3 grid((unsigned)cdiv((int64_t)I, (int64_t)kThreads),
+                    (unsigned)std::min<int64_t>(cdiv(B, (int64_t)kFeatRows), kMaxGridY));
     if (dot) {
       if (F == 16) feature_dot_f32_kernel<BK, 16><<<grid, kThreads, 0, stream>>>(x, dfeat, out, B, I, has_base, fa);
       else feature_dot_f32_kernel<BK, 32><<<grid, kThreads, 0, stream>>>(x, dfeat, out, B, I, has_base, fa);

@@ -61,8 +61,9 @@ def bspline_features(x, grid, k):
     return phi.astype(np.float32), db.astype(np.float32)
 
 
-def kan_linear_step(x, coef, base_w, bias, feats):
-    """One fwd+bwd of loss = mean(y^2); returns (loss, grads)."""
+def kan_linear_step(x, coef, base_w, bias, feats, dy=None):
+    """One fwd+bwd of loss = mean(y^2), or of sum(dy * y) when dy is given;
+    returns (loss, grads) with grads["y"] the forward output."""
     bsz, n_in = x.shape
     n_out = coef.shape[0]
     phi, dphi = feats(x)
@@ -71,12 +72,15 @@ def kan_linear_step(x, coef, base_w, bias, feats):
         y += _silu(x) @ base_w.T
     if bias is not None:
         y += bias
-    loss = float(np.mean(y * y))
-    dy = (2.0 / y.size) * y
+    if dy is None:
+        loss = float(np.mean(y * y))
+        dy = (2.0 / y.size) * y
+    else:
+        loss = float(np.sum(dy * y))
     dphi_in = (dy @ coef.reshape(n_out, -1)).reshape(bsz, n_in, -1)
     dx = (dphi_in * dphi).sum(-1)
     dcoef = (dy.T @ phi.reshape(bsz, -1)).reshape(coef.shape)
-    grads = {"x": dx, "coef": dcoef}
+    grads = {"x": dx, "coef": dcoef, "y": y}
     if base_w is not None:
         dx += (dy @ base_w) * _dsilu(x)
         grads["base_weight"] = dy.T @ _silu(x)
@@ -120,7 +124,7 @@ def grkan_ffn_step(x, l1, l2, groups):
     dh = (dy @ l2["w"]) * dr2[..., 0]
     dw1 = dh.T @ r1[..., 0]
     dx = (dh @ l1["w"]) * dr1[..., 0]
-    return loss, {"x": dx, "w1": dw1, "w2": dw2}
+    return loss, {"x": dx, "w1": dw1, "w2": dw2, "y": y}
 
 
 def edge_derivative_order(x, coef_fold, base_w, m):

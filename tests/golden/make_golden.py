@@ -32,7 +32,9 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-REF = os.environ.get("KANFORGE_REFERENCE", "/root/reference")
+REF = os.environ.get("KANFORGE_REFERENCE")
+if not REF:
+    sys.exit("set KANFORGE_REFERENCE to the directory that holds the reference's kanforge package")
 sys.path.insert(0, REF)
 os.environ.setdefault("TRITON_INTERPRET", "1")
 

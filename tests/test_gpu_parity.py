@@ -427,12 +427,15 @@ def test_float32_layer_on_tensor_cores_matches_oracle(basis, n_b, n_in, n_out, b
         close(gr, want[key[nme]], FP32_TOL, f"d{nme}")
 
 
-@pytest.mark.parametrize("order,grid_size,base", [(1, 6, True), (2, 9, False), (3, 8, True), (4, 5, True),
-                                                  (5, 7, False), (3, 20, True)])
-def test_float32_spline_features_from_knot_tables_match_grid_kernel(order, grid_size, base):
+@pytest.mark.parametrize("order,grid_size,base,n_b", [(1, 6, True, 1000), (2, 9, False, 1000), (3, 8, True, 1000),
+                                                      (4, 5, True, 1000), (5, 7, False, 1000), (3, 20, True, 1000),
+                                                      (3, 8, True, 30011), (2, 9, False, 40003)])
+def test_float32_spline_features_from_knot_tables_match_grid_kernel(order, grid_size, base, n_b):
     """kf_features_spline_f32 (knot tables) against kf_features_f32 (raw grid) on
-    non-uniform grids, with inputs on knots, outside the grid and at its ends."""
-    n_b, n_in = 1000, 37
+    non-uniform grids, with inputs on knots, outside the grid and at its ends.
+    The 30011- and 40003-row cases run the row loop's later grid-stride passes
+    and end on a partial group of rows."""
+    n_in = 37
     layer = make_bf16_layer(kb.BSpline(grid_size, order), n_in, 8, base, False, False).float()
     plan, g = layer._plan, layer.basis_grid.float().contiguous()
     nt, f_pad = kb.kernels.fused_layout(plan, base)
@@ -452,6 +455,40 @@ def test_float32_spline_features_from_knot_tables_match_grid_kernel(order, grid_
     torch.cuda.synchronize()
     assert not torch.isnan(got).any()
     torch.testing.assert_close(got, want, rtol=1e-5, atol=2e-6)
+
+
+@pytest.mark.parametrize("basis", [kb.Chebyshev(6), kb.BSpline(5, 2)], ids=repr)
+def test_float32_feature_kernels_past_the_grid_y_limit(basis):
+    """More rows than 65535 row blocks of 64 (4,194,240): kf_features_f32 and
+    kf_features_dot_f32 stride over the row blocks; the rows past the limit
+    equal the same rows computed by a small launch."""
+    n_b, n_in = 65535 * 64 + 777, 1
+    plan = kb.plan_for(basis)
+    nt, f_pad = kb.kernels.fused_layout(plan, True)
+    g = torch.Generator(device=DEV).manual_seed(5)
+    x = (torch.randn(n_b, n_in, device=DEV, generator=g) * 1.2).clamp(-3, 3)
+    grid = torch.linspace(-1, 1, basis.size - plan.consts[1] + 1, device=DEV)[None] if plan.kind == "bspline" else \
+        x.new_zeros(1)
+    desc = plan.desc()
+    feat = torch.empty(n_b, n_in * f_pad, device=DEV)
+    kb.kernels._launch("kf_features_f32", x.data_ptr(), grid.data_ptr(), feat.data_ptr(), n_b, n_in, nt, f_pad, 1,
+                       ctypes.byref(desc), kb.kernels._stream(x))
+    dfeat = torch.randn(n_b, n_in * f_pad, device=DEV, generator=g)
+    dx = torch.empty_like(x)
+    kb.kernels._launch("kf_features_dot_f32", x.data_ptr(), grid.data_ptr(), dfeat.data_ptr(), dx.data_ptr(), n_b, n_in,
+                       nt, f_pad, 1, ctypes.byref(desc), kb.kernels._stream(x))
+    tail = slice(n_b - 5000, n_b)
+    xt = x[tail].contiguous()
+    ft = torch.empty(5000, n_in * f_pad, device=DEV)
+    kb.kernels._launch("kf_features_f32", xt.data_ptr(), grid.data_ptr(), ft.data_ptr(), 5000, n_in, nt, f_pad, 1,
+                       ctypes.byref(desc), kb.kernels._stream(x))
+    dft = dfeat[tail].contiguous()
+    dxt = torch.empty_like(xt)
+    kb.kernels._launch("kf_features_dot_f32", xt.data_ptr(), grid.data_ptr(), dft.data_ptr(), dxt.data_ptr(), 5000, n_in,
+                       nt, f_pad, 1, ctypes.byref(desc), kb.kernels._stream(x))
+    torch.cuda.synchronize()
+    assert torch.equal(feat[tail], ft)
+    assert torch.equal(dx[tail], dxt)
 
 
 def test_bf16_fused_multi_tile_persistent_against_float32_primitives():
