@@ -114,7 +114,8 @@ int kf_knot_tables(const float* grid, float* tab, int32_t I, int32_t grid_size, 
 /* Fused KANLinear forward on tcgen05 (bf16 operands, f32 accumulation):
  *   y[b,o] = sum_{i,j} feat_j(x[b,i]) packed[o,i,j] + bias[o]
  * feat = basis features (B-spline values or T_j(g(x))) and, in the last
- * column f_pad-1, silu(x) when has_base.  x (B,I) bf16, y (B,O) bf16, bias (O) bf16 or null,
+ * column f_pad-1, silu(x) when has_base.  x (B,I) bf16, y (B,O) bf16, bias (O) bf16 or null
+ * (y and bias 16-byte aligned),
  * knot_tab: kf_knot_tables output for B-splines, else null.  Requires O % 8 == 0.
  * feat: the kf_features matrix of x (the kernel then reads the features by
  * TMA), or null (it evaluates them itself).
@@ -226,6 +227,37 @@ int kf_rational_bwd(const void* x, const void* dr, const float* num, const float
 
 /* Workspace (float32 elements) that kf_rational_bwd needs. */
 int64_t kf_rational_workspace(int64_t B, int32_t I, const kf_basis_desc* basis);
+
+/* GR-KAN layer contractions on tcgen05 (bf16 operands, f32 accumulation):
+ * the linear map of a GRKAN layer, kanforge/torch/layers.py:335-363 (R = the
+ * group rational of kf_rational_act, W = coef[..., 0] of shape (O, I)).
+ *   kf_grkan_fwd:   y[b,o] = sum_i r[b,i] w[o,i] + bias[o]
+ *                   r = R(x) (B,I), w (O,I), bias (O) or null, y (B,O), all bf16;
+ *                   I % 16 == 0, O % 8 == 0, r, w, y and bias 16-byte aligned.
+ *   kf_grkan_dgrad: dR[b,i] = sum_o dy[b,o] w[o,i] on the tensor cores, then in
+ *                   the same kernel dx[b,i] = dR[b,i] R'(x[b,i]) and the partial
+ *                   sums of the per-group parameter gradients
+ *                   dnum[g,j] = sum dR dR/da_j, dden[g,j] = sum dR dR/db_j
+ *                   (float32, reduced in a fixed order through `workspace`,
+ *                   kf_grkan_workspace floats).  Rational degrees (5, 4), the
+ *                   inputs per group a multiple of 32, O % 8 == 0; x, dy, w, dx
+ *                   bf16 and 16-byte aligned; num (groups, 6), den (groups, 4).
+ *   kf_grkan_wgrad: dw[o,i] = sum_b dy[b,o] r[b,i], bf16; I % 16 == 0, O % 8 == 0.
+ *                   When the (I / 256) x (O / 256) output tiles are too few to
+ *                   fill the GPU, the batch is split and the float32 partial
+ *                   sums go through `workspace` (kf_grkan_wgrad_workspace
+ *                   floats, 16-byte aligned; 0 = none needed), summed in a
+ *                   fixed order.
+ * Replace Rational._eval + the torch linear map and its autograd
+ * (kanforge/bases/rational.py:84-101, kanforge/torch/layers.py:184-191). */
+int kf_grkan_fwd(const void* r, const void* w, const void* bias, void* y, int64_t B, int32_t I, int32_t O, void* stream);
+int kf_grkan_dgrad(const void* x, const void* dy, const void* w, const float* num, const float* den, void* dx, float* dnum,
+                   float* dden, float* workspace, int64_t B, int32_t I, int32_t O, const kf_basis_desc* basis,
+                   void* stream);
+int64_t kf_grkan_workspace(int64_t B, int32_t I, const kf_basis_desc* basis);
+int64_t kf_grkan_wgrad_workspace(int64_t B, int32_t I, int32_t O);
+int kf_grkan_wgrad(const void* r, const void* dy, void* dw, float* workspace, int64_t B, int32_t I, int32_t O,
+                   void* stream);
 
 /* kf_rational_bwd for callers that cannot allocate device memory.  Some hosts
  * of this library may not call cudaMalloc: code that runs inside a device

@@ -92,6 +92,14 @@ PROTOTYPES = {
         [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i32, ctypes.POINTER(BasisDesc), ctypes.c_int, _vp],
     ),
     "kf_rational_workspace": (_c_i64, [_c_i64, _c_i32, ctypes.POINTER(BasisDesc)]),
+    "kf_grkan_fwd": (ctypes.c_int, [_vp, _vp, _vp, _vp, _c_i64, _c_i32, _c_i32, _vp]),
+    "kf_grkan_dgrad": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i32, _c_i32, ctypes.POINTER(BasisDesc), _vp],
+    ),
+    "kf_grkan_workspace": (_c_i64, [_c_i64, _c_i32, ctypes.POINTER(BasisDesc)]),
+    "kf_grkan_wgrad_workspace": (_c_i64, [_c_i64, _c_i32, _c_i32]),
+    "kf_grkan_wgrad": (ctypes.c_int, [_vp, _vp, _vp, _vp, _c_i64, _c_i32, _c_i32, _vp]),
     "kf_rational_bwd_noalloc": (
         ctypes.c_int,
         [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i32, ctypes.POINTER(BasisDesc), ctypes.c_int, _vp],

@@ -197,4 +197,53 @@ __device__ __forceinline__ float rational_deriv(float x, const float* a, int na,
   return out[m];
 }
 
+// Two elements of the rational backward in float2 lanes (two fp32 operations
+// per instruction: __ffma2_rn / __fmul2_rn / __fadd2_rn), degrees fixed: returns
+// dx = g R'(x) and adds g dR/da_j, g dR/db_j to the accumulators.  With
+// D = 1 + |Q|, Q = x Qs(x):
+//   R' = (P' - sign(Q) Q' R) / D,  dR/da_j = x^j / D,  dR/db_j = -R sign(Q) x^(j+1) / D.
+// 1 / D uses __fdividef (2 ulp; D >= 1 is far inside its range).  Used by the
+// rational kernels and the GR-KAN input-gradient epilogue.
+__device__ __forceinline__ float rat_sign(float q) { return q > 0.0f ? 1.0f : (q < 0.0f ? -1.0f : 0.0f); }
+__device__ __forceinline__ float2 dup2(float v) { return make_float2(v, v); }
+__device__ __forceinline__ float2 neg2(float2 v) { return make_float2(-v.x, -v.y); }
+
+template <int NA, int NB>
+__device__ __forceinline__ float2 rat_bwd_pair(float2 x, float2 g, const float2 (&a)[NA], const float2 (&bq)[NB],
+                                               float2 (&acc_a)[NA], float2 (&acc_b)[NB]) {
+  float2 P = a[NA - 1], dP = make_float2(0.0f, 0.0f);
+#pragma unroll
+  for (int j = NA - 2; j >= 0; --j) {
+    dP = __ffma2_rn(dP, x, P);
+    P = __ffma2_rn(P, x, a[j]);
+  }
+  float2 Qs = bq[NB - 1], dQs = make_float2(0.0f, 0.0f);
+#pragma unroll
+  for (int j = NB - 2; j >= 0; --j) {
+    dQs = __ffma2_rn(dQs, x, Qs);
+    Qs = __ffma2_rn(Qs, x, bq[j]);
+  }
+  const float2 Q = __fmul2_rn(x, Qs);
+  const float2 dQ = __ffma2_rn(x, dQs, Qs);
+  const float2 sg = make_float2(rat_sign(Q.x), rat_sign(Q.y));
+  const float2 rD = make_float2(__fdividef(1.0f, 1.0f + fabsf(Q.x)), __fdividef(1.0f, 1.0f + fabsf(Q.y)));
+  const float2 R = __fmul2_rn(P, rD);
+  const float2 u = __fmul2_rn(g, rD);
+  acc_a[0] = __fadd2_rn(acc_a[0], u);
+  float2 xp = x;
+#pragma unroll
+  for (int j = 1; j < NA; ++j) {
+    acc_a[j] = __ffma2_rn(u, xp, acc_a[j]);
+    xp = __fmul2_rn(xp, x);
+  }
+  const float2 v = __fmul2_rn(__fmul2_rn(neg2(u), R), sg);
+  xp = x;
+#pragma unroll
+  for (int j = 0; j < NB; ++j) {
+    acc_b[j] = __ffma2_rn(v, xp, acc_b[j]);
+    xp = __fmul2_rn(xp, x);
+  }
+  return __fmul2_rn(g, __fmul2_rn(__ffma2_rn(neg2(__fmul2_rn(sg, dQ)), R, dP), rD));
+}
+
 }  // namespace kf

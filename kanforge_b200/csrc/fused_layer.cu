@@ -40,7 +40,8 @@ using namespace umma;
 constexpr int kBM = 128;
 constexpr int kBN = 256;
 constexpr int kBK = 64;  // bf16 elements per stage row = 128 bytes
-constexpr int kStages = 4;
+constexpr int kStages = 4;     // pipeline depth of the kernels with producer warps
+constexpr int kMaxStages = 6;  // deepest pipeline (TMA-fed kernels, where shared memory allows)
 constexpr int kATile = kBM * 128;  // 16 KB
 constexpr int kTabStride = 64;     // floats per knot/inverse-difference row
 constexpr int kMaxOrder = 5;
@@ -66,10 +67,10 @@ struct BasisDev {
 };
 
 struct Ctl {
-  uint64_t full_a[kStages];
-  uint64_t full_b[kStages];
-  uint64_t tab_full[kStages];   // CTA pairs: this CTA's knot tables of the stage landed
-  uint64_t empty[kStages];
+  uint64_t full_a[kMaxStages];
+  uint64_t full_b[kMaxStages];
+  uint64_t tab_full[kMaxStages];   // CTA pairs: this CTA's knot tables of the stage landed
+  uint64_t empty[kMaxStages];
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
   uint64_t drain;
@@ -120,11 +121,12 @@ __global__ void __launch_bounds__(256) knot_table_kernel(const float* __restrict
 
 // Abort path of the TMA thread: wait for the last load issued on every stage
 // (iterations < `issued`) so that no bulk copy targets shared memory after exit.
+template <int NS>
 __device__ __forceinline__ void drain_tma(Ctl* ctl, int issued) {
-  for (int s = 0; s < kStages; ++s) {
-    int last = issued - 1 - ((issued - 1 - s) % kStages + kStages) % kStages;
+  for (int s = 0; s < NS; ++s) {
+    int last = issued - 1 - ((issued - 1 - s) % NS + NS) % NS;
     if (issued <= 0 || last < 0) continue;
-    mbar_drain(&ctl->full_b[s], (last / kStages) & 1);
+    mbar_drain(&ctl->full_b[s], (last / NS) & 1);
   }
 }
 
@@ -243,15 +245,16 @@ constexpr int kFwdNB = 2;                 // forward: 256-column accumulator blo
 // the kernel then has no producer warps.
 constexpr int kFwdTmaThreads = 256;  // A_TMA: w0 TMA, w1 MMA (CTA 0), w4-7 epilogue
 
-template <int BK, int F, bool A_TMA>
+template <int BK, int F, bool A_TMA, int NS>
 __global__ void __launch_bounds__(A_TMA ? kFwdTmaThreads : kFwdThreads, 1)
     fused_fwd_kernel(const __grid_constant__ CUtensorMap tmap_c, const __grid_constant__ CUtensorMap tmap_a, FwdParams p) {
   constexpr int IPK = kBK / F;  // inputs per K-step
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = align1024(smem_raw);
-  uint8_t* sa = base;                                   // kStages x 16 KB
-  uint8_t* sb = sa + kStages * kATile;                  // kStages x kFwdNB x 16 KB (this CTA's halves of B)
-  Ctl* ctl = reinterpret_cast<Ctl*>(sb + kStages * kFwdNB * kBHalf);
+  const int b_stage = p.nblk * kBHalf;                  // bytes of B per stage (this CTA's halves)
+  uint8_t* sa = base;                                   // NS x 16 KB
+  uint8_t* sb = sa + NS * kATile;                       // NS x nblk x 16 KB
+  Ctl* ctl = reinterpret_cast<Ctl*>(sb + NS * b_stage);
   constexpr int kTabIn = (BK + 1) * kTabStride;          // floats of one input's knot table
   float* tabs = reinterpret_cast<float*>(align1024(reinterpret_cast<uint8_t*>(ctl + 1)));  // B-spline: [stage][IPK][kTabIn]
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -260,7 +263,7 @@ __global__ void __launch_bounds__(A_TMA ? kFwdTmaThreads : kFwdThreads, 1)
   volatile int* abort = &ctl->abort;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < NS; ++s) {
       mbar_init(&ctl->full_a[s], 8);    // 4 producer warps of each CTA (used in CTA 0)
       mbar_init(&ctl->full_b[s], 1);    // CTA 0's expect_tx for both halves (used in CTA 0)
       mbar_init(&ctl->tab_full[s], 1);  // this CTA's knot tables
@@ -297,8 +300,8 @@ __global__ void __launch_bounds__(A_TMA ? kFwdTmaThreads : kFwdThreads, 1)
         int m, n;
         p.tiles.get(t, m, n);
         for (int k = 0; k < p.k_steps; ++k, ++it) {
-          const int s = it % kStages;
-          const uint32_t ph = (it / kStages) & 1;
+          const int s = it % NS;
+          const uint32_t ph = (it / NS) & 1;
           if (!mbar_wait(&ctl->empty[s], ph ^ 1, abort)) break;
           if constexpr (BK > 0 && !A_TMA) {
             // the knot tables of the step's inputs, into this CTA
@@ -307,7 +310,7 @@ __global__ void __launch_bounds__(A_TMA ? kFwdTmaThreads : kFwdThreads, 1)
             mbar_arrive_expect_tx(&ctl->tab_full[s], tb);
             bulk_load(tabs + s * IPK * kTabIn, p.bd.tab + (size_t)k * IPK * kTabIn, tb, &ctl->tab_full[s]);
           }
-          uint8_t* sbs = sb + s * (kFwdNB * kBHalf);
+          uint8_t* sbs = sb + s * b_stage;
           // both CTAs' coefficient halves (and A_TMA: feature rows) complete here
           if (rank == 0) mbar_arrive_expect_tx(&ctl->full_b[s], 2 * p.nblk * kBHalf + (A_TMA ? 2 * kATile : 0));
           if constexpr (A_TMA) {
@@ -328,7 +331,7 @@ __global__ void __launch_bounds__(A_TMA ? kFwdTmaThreads : kFwdThreads, 1)
       }
       // Abort: CTA 0 drains the coefficient loads of both CTAs (they complete
       // on its barriers) before the pair's final cluster barrier.
-      if (*abort && rank == 0) drain_tma(ctl, it);
+      if (*abort && rank == 0) drain_tma<NS>(ctl, it);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer (CTA 0 of the pair) ----------------
@@ -336,29 +339,33 @@ __global__ void __launch_bounds__(A_TMA ? kFwdTmaThreads : kFwdThreads, 1)
       const uint32_t idesc = idesc_bf16_f32(kPairM, kBN, false, false);
       int it = 0, tc = 0;
       for (int t = pair; t < n_tiles && !*abort; t += n_pairs, ++tc) {
-        if (!mbar_wait_cluster(&ctl->acc_empty[0], (tc & 1) ^ 1, abort)) break;
+        // one 256-column block per tile: the two accumulators alternate, so the
+        // epilogue of a tile overlaps the MMAs of the next
+        const int acc = p.nblk == 1 ? (tc & 1) : 0;
+        const uint32_t par = p.nblk == 1 ? ((tc >> 1) & 1) : (tc & 1);
+        if (!mbar_wait_cluster(&ctl->acc_empty[acc], par ^ 1, abort)) break;
         tc_fence_after();
         bool ok = true;
         for (int k = 0; k < p.k_steps; ++k, ++it) {
-          const int s = it % kStages;
-          const uint32_t ph = (it / kStages) & 1;
+          const int s = it % NS;
+          const uint32_t ph = (it / NS) & 1;
           if ((!A_TMA && !mbar_wait_cluster(&ctl->full_a[s], ph, abort)) || !mbar_wait_cluster(&ctl->full_b[s], ph, abort)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(sa + s * kATile), b0 = smem_u32(sb + s * (kFwdNB * kBHalf));
+          const uint32_t a0 = smem_u32(sa + s * kATile), b0 = smem_u32(sb + s * b_stage);
 #pragma unroll
           for (int j = 0; j < kBK / 16; ++j) {
             const uint64_t adesc = smem_desc_sw128(a0 + 32 * j, 16, 1024);
             for (int nb = 0; nb < p.nblk; ++nb)
-              mma_bf16_pair(tmem + nb * kBN, adesc, smem_desc_sw128(b0 + nb * kBHalf + 32 * j, 16, 1024), idesc,
+              mma_bf16_pair(tmem + (acc + nb) * kBN, adesc, smem_desc_sw128(b0 + nb * kBHalf + 32 * j, 16, 1024), idesc,
                             (k > 0 || j > 0) ? 1u : 0u);
           }
           mma_commit_pair(&ctl->empty[s], 0x3);
         }
         if (!ok) break;
-        mma_commit_pair(&ctl->acc_full[0], 0x3);
+        mma_commit_pair(&ctl->acc_full[acc], 0x3);
       }
       // Every MMA of this CTA has completed (and every commit above has
       // arrived) once the drain barrier flips: the pair may then exit.
@@ -373,7 +380,9 @@ __global__ void __launch_bounds__(A_TMA ? kFwdTmaThreads : kFwdThreads, 1)
     for (int t = pair; t < n_tiles; t += n_pairs, ++tc) {
       int m, n;
       p.tiles.get(t, m, n);
-      if (!mbar_wait_warp(&ctl->acc_full[0], tc & 1, abort)) break;
+      const int acc = p.nblk == 1 ? (tc & 1) : 0;
+      const uint32_t par = p.nblk == 1 ? ((tc >> 1) & 1) : (tc & 1);
+      if (!mbar_wait_warp(&ctl->acc_full[acc], par, abort)) break;
       tc_fence_after();
       const int64_t b = (int64_t)m * kPairM + (int64_t)rank * kBM + row;
       const int o_base = n * (p.nblk * kBN);
@@ -381,22 +390,35 @@ __global__ void __launch_bounds__(A_TMA ? kFwdTmaThreads : kFwdThreads, 1)
 #pragma unroll 1
       for (int c = 0; c < n_chunks; ++c) {
         float v[32];
-        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + c * 32, v);
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + acc * kBN + c * 32, v);
         if (c == n_chunks - 1) {
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(&ctl->acc_empty[0], 0);
+          if (lane == 0) mbar_arrive_cluster(&ctl->acc_empty[acc], 0);
         }
         const int o0 = o_base + c * 32;
         if (b < p.B && o0 < p.O) {
+          // O % 8 == 0: the chunk's outputs are whole groups of 8 (one 16-byte
+          // vector of y and of the bias each)
           if (p.bias) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] += (o0 + j < p.O) ? __bfloat162float(p.bias[o0 + j]) : 0.0f;
-          }
-          __nv_bfloat16* dst = p.y + b * p.O + o0;
-          if (o0 + 32 <= p.O) {
+            const uint4* bv = reinterpret_cast<const uint4*>(p.bias + o0);
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
+              if (o0 + 8 * u < p.O) {
+                const uint4 w = __ldg(bv + u);
+                const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                  v[8 * u + 2 * h] += __uint_as_float(ws[h] << 16);
+                  v[8 * u + 2 * h + 1] += __uint_as_float(ws[h] & 0xffff0000u);
+                }
+              }
+            }
+          }
+          __nv_bfloat16* dst = p.y + b * p.O + o0;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            if (o0 + 8 * u < p.O) {
               uint4 pk;
               pk.x = pack_bf16x2(v[8 * u + 0], v[8 * u + 1]);
               pk.y = pack_bf16x2(v[8 * u + 2], v[8 * u + 3]);
@@ -404,8 +426,6 @@ __global__ void __launch_bounds__(A_TMA ? kFwdTmaThreads : kFwdThreads, 1)
               pk.w = pack_bf16x2(v[8 * u + 6], v[8 * u + 7]);
               *reinterpret_cast<uint4*>(dst + 8 * u) = pk;
             }
-          } else {
-            for (int j = 0; j < 32 && o0 + j < p.O; ++j) dst[j] = __float2bfloat16_rn(v[j]);
           }
         }
       }
@@ -415,7 +435,7 @@ __global__ void __launch_bounds__(A_TMA ? kFwdTmaThreads : kFwdThreads, 1)
     // Group grp owns the K-steps it with it % 4 == grp, i.e. always stage grp;
     // each thread owns one row.  The x values of a thread's next step are
     // loaded one step ahead so global latency overlaps the current step.
-    static_assert(kStages % kFwdGroups == 0, "each producer group owns whole stages");
+    static_assert(A_TMA || NS % kFwdGroups == 0, "each producer group owns whole stages");
     const int grp = (warp - 8) / 4;
     const int row = ((warp - 8) % 4) * 32 + lane;
     int it = 0;
@@ -432,8 +452,8 @@ __global__ void __launch_bounds__(A_TMA ? kFwdTmaThreads : kFwdThreads, 1)
       for (int u = 0; u < IPK; ++u) xa[u] = (row_ok && k < p.k_steps && k * IPK + u < p.I) ? __ldg(xrow + k * IPK + u) : 0;
       for (; k < p.k_steps; k += kFwdGroups) {
         const int git = it + k;
-        const int s = git % kStages;
-        const uint32_t ph = (git / kStages) & 1;
+        const int s = git % NS;
+        const uint32_t ph = (git / NS) & 1;
         const int i0 = k * IPK;
         const int inext = i0 + kFwdGroups * IPK;
 #pragma unroll
@@ -532,13 +552,32 @@ struct DgradParams {
   int tab_ts;  // B-spline: row stride of the staged knot tables (nk rounded up to 4)
   TileMap tiles;
   BasisDev bd;
+  // GR-KAN (BK = kRationalBK): R = P / (1 + |Q|) of degrees (5, 4), parameters
+  // shared by ipg consecutive inputs (ipg a multiple of 32)
+  const float* rnum;  // (groups, 6)
+  const float* rden;  // (groups, 4)
+  int ipg;
+  float* rws;  // parameter-gradient partial sums [10][I / 32][n_rq]
+  int n_rq;    // 32-row blocks: 8 per pair tile of 256 rows (those past B hold zeros)
 };
+
+// Template value of BK that selects the GR-KAN epilogue of the input-gradient
+// kernel: the accumulator holds dR = dy W (one column per input), the
+// epilogue writes dx = dR R'(x) and the per-group parameter-gradient partial
+// sums of R = P / (1 + |Q|) (kanforge/bases/rational.py:84-101,
+// kanforge/torch/layers.py:335-363).
+constexpr int kRationalBK = -1;
+constexpr int kRatNA = 6, kRatNB = 4;  // the GR-KAN degrees (5, 4)
 
 // Threads of the input-gradient kernel: w0 TMA, w1 MMA (CTA 0), then the
 // epilogue warps from w4 on: two sets of four for Chebyshev features, four
-// sets of four for B-splines (whose per-input derivative windows are the
-// epilogue's main cost).
-constexpr int dgrad_threads(int bk) { return bk > 0 ? 640 : 384; }
+// sets of four for B-splines and the GR-KAN rational (whose per-input
+// derivative windows / rational backward are the epilogue's main cost).
+constexpr int dgrad_threads(int bk) { return bk != 0 ? 640 : 384; }
+// Pipeline depth: six stages of 32 KB where the epilogue's shared memory
+// leaves room (deeper buffering hides the TMA latency of operands read from
+// DRAM); B-spline plans keep four for their knot tables and staging.
+constexpr int dgrad_stages(int bk) { return bk > 0 ? kStages : kMaxStages; }
 
 // The input gradient runs on CTA pairs: a tile is 256 tokens x 256 feature
 // columns, CTA r loads dy rows 128 r .. 128 r + 127 (its half of A) and
@@ -548,14 +587,15 @@ constexpr int dgrad_threads(int bk) { return bk > 0 ? 640 : 384; }
 template <int BK, int F>
 __global__ void __launch_bounds__(dgrad_threads(BK), 1) fused_dgrad_kernel(const __grid_constant__ CUtensorMap tmap_dy,
                                                                            const __grid_constant__ CUtensorMap tmap_c, DgradParams p) {
-  constexpr int IPT = kBN / F;  // inputs per tile
+  constexpr int NS = dgrad_stages(BK);
+  constexpr int IPT = BK < 0 ? kBN : kBN / F;  // inputs per tile
   constexpr int kEpiWarps = dgrad_threads(BK) / 32 - 4;
   constexpr int kEpiThreads = 32 * kEpiWarps;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = align1024(smem_raw);
   uint8_t* sa = base;
-  uint8_t* sb = sa + kStages * kATile;                  // kStages x 16 KB (this CTA's half of B)
-  Ctl* ctl = reinterpret_cast<Ctl*>(sb + kStages * kBHalf);
+  uint8_t* sb = sa + NS * kATile;                  // NS x 16 KB (this CTA's half of B)
+  Ctl* ctl = reinterpret_cast<Ctl*>(sb + NS * kBHalf);
   float* xsm = reinterpret_cast<float*>(ctl + 1);       // Chebyshev: x of each row's tile inputs [128][IPT + 1]
   float* tabs = reinterpret_cast<float*>(ctl + 1);      // B-spline: knot tables [2][IPT][BK+1][tab_ts]
   float* stage = tabs + 2 * IPT * (BK + 1) * p.tab_ts;  // B-spline: per epilogue warp [32][F + 1]
@@ -565,7 +605,7 @@ __global__ void __launch_bounds__(dgrad_threads(BK), 1) fused_dgrad_kernel(const
   volatile int* abort = &ctl->abort;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < NS; ++s) {
       mbar_init(&ctl->full_b[s], 1);  // CTA 0's expect_tx for both CTAs' A and B halves (used in CTA 0)
       mbar_init(&ctl->empty[s], 1);
     }
@@ -601,8 +641,8 @@ __global__ void __launch_bounds__(dgrad_threads(BK), 1) fused_dgrad_kernel(const
         const int a_row = m * kPairM + (int)rank * kBM;
         const int b_col = n * kBN + (int)rank * (kBN / 2);
         for (int k = 0; k < p.k_steps; ++k, ++it) {
-          const int s = it % kStages;
-          const uint32_t ph = (it / kStages) & 1;
+          const int s = it % NS;
+          const uint32_t ph = (it / NS) & 1;
           if (!mbar_wait(&ctl->empty[s], ph ^ 1, abort)) break;
           if (rank == 0) {
             mbar_arrive_expect_tx(&ctl->full_b[s], 2 * (kATile + kBHalf));  // both CTAs' loads complete here
@@ -622,7 +662,7 @@ __global__ void __launch_bounds__(dgrad_threads(BK), 1) fused_dgrad_kernel(const
       }
       // Abort: CTA 0 drains the loads of both CTAs (they complete on its
       // barriers) before the pair's final cluster barrier.
-      if (*abort && rank == 0) drain_tma(ctl, it);
+      if (*abort && rank == 0) drain_tma<NS>(ctl, it);
     }
   } else if (warp == 1) {
     if (rank == 0 && lane == 0) {
@@ -635,8 +675,8 @@ __global__ void __launch_bounds__(dgrad_threads(BK), 1) fused_dgrad_kernel(const
         const uint32_t d_tmem = tmem + acc * kBN;
         bool ok = true;
         for (int k = 0; k < p.k_steps; ++k, ++it) {
-          const int s = it % kStages;
-          const uint32_t ph = (it / kStages) & 1;
+          const int s = it % NS;
+          const uint32_t ph = (it / NS) & 1;
           if (!mbar_wait_cluster(&ctl->full_b[s], ph, abort)) {
             ok = false;
             break;
@@ -659,7 +699,92 @@ __global__ void __launch_bounds__(dgrad_threads(BK), 1) fused_dgrad_kernel(const
       mbar_drain(&ctl->drain, 0);
     }
   } else if (warp >= 4) {
-    if constexpr (BK == 0) {
+    if constexpr (BK < 0) {
+      // GR-KAN: four sets of four warps; set `set` reads TMEM lane quarter q
+      // (rows 32 q ..) of column chunks 2 set and 2 set + 1, each chunk 32
+      // inputs of one parameter group, in halves of 16 columns.  Per half a
+      // thread loads its row's 16 x values, evaluates the rational backward in
+      // float2 lanes and writes dx; per chunk the warp sums the parameter-
+      // gradient terms over its 32 rows (a fixed shuffle tree) into rws.
+      const int q = (warp - 4) % 4, set = (warp - 4) / 4;
+      const int row = q * 32 + lane;
+      const int n_chunks = p.I / 32;
+      int g_cur = -1;
+      float2 ca[kRatNA], cb[kRatNB];
+      int tc = 0;
+      for (int t = pair; t < n_tiles; t += n_pairs, ++tc) {
+        int m, n;
+        p.tiles.get(t, m, n);
+        const int acc = tc & 1;
+        const int64_t b = (int64_t)m * kPairM + (int64_t)rank * kBM + row;
+        const bool row_ok = b < p.B;
+        const int rq = (m * 2 + (int)rank) * 4 + q;  // this warp's 32-row block
+        const uint4* xrow = reinterpret_cast<const uint4*>(p.x + (row_ok ? b : 0) * p.I);
+        uint4* dxrow = reinterpret_cast<uint4*>(p.dx + (row_ok ? b : 0) * p.I);
+        if (!mbar_wait_warp(&ctl->acc_full[acc], (tc >> 1) & 1, abort)) break;
+        tc_fence_after();
+#pragma unroll 1
+        for (int cc = 0; cc < 2; ++cc) {
+          const int c = 2 * set + cc;
+          const int i0 = n * kBN + c * 32;
+          const bool chunk_ok = i0 < p.I;  // warp-uniform
+          if (chunk_ok && i0 / p.ipg != g_cur) {
+            g_cur = i0 / p.ipg;
+#pragma unroll
+            for (int j = 0; j < kRatNA; ++j) ca[j] = dup2(__ldg(p.rnum + g_cur * kRatNA + j));
+#pragma unroll
+            for (int j = 0; j < kRatNB; ++j) cb[j] = dup2(__ldg(p.rden + g_cur * kRatNB + j));
+          }
+          float2 acc_a[kRatNA], acc_b[kRatNB];
+#pragma unroll
+          for (int j = 0; j < kRatNA; ++j) acc_a[j] = make_float2(0.0f, 0.0f);
+#pragma unroll
+          for (int j = 0; j < kRatNB; ++j) acc_b[j] = make_float2(0.0f, 0.0f);
+#pragma unroll 1
+          for (int h = 0; h < 2; ++h) {
+            const int ih = i0 + 16 * h;
+            uint4 xq[2];
+#pragma unroll
+            for (int k = 0; k < 2; ++k) xq[k] = (row_ok && chunk_ok) ? __ldg(xrow + ih / 8 + k) : make_uint4(0, 0, 0, 0);
+            float v[16];
+            tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + acc * kBN + c * 32 + 16 * h, v);
+            if (cc == 1 && h == 1) {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive_cluster(&ctl->acc_empty[acc], 0);
+            }
+            if (!chunk_ok) continue;
+            const uint32_t* xw = reinterpret_cast<const uint32_t*>(xq);
+            uint32_t out[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const float2 xv = make_float2(__uint_as_float(xw[k] << 16), __uint_as_float(xw[k] & 0xffff0000u));
+              const float2 d = rat_bwd_pair(xv, make_float2(v[2 * k], v[2 * k + 1]), ca, cb, acc_a, acc_b);
+              out[k] = pack_bf16x2(d.x, d.y);
+            }
+            if (row_ok) {
+              dxrow[ih / 8] = make_uint4(out[0], out[1], out[2], out[3]);
+              dxrow[ih / 8 + 1] = make_uint4(out[4], out[5], out[6], out[7]);
+            }
+          }
+          if (!chunk_ok) continue;
+          float ps[kRatNA + kRatNB];
+#pragma unroll
+          for (int j = 0; j < kRatNA; ++j) ps[j] = acc_a[j].x + acc_a[j].y;
+#pragma unroll
+          for (int j = 0; j < kRatNB; ++j) ps[kRatNA + j] = acc_b[j].x + acc_b[j].y;
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) {
+#pragma unroll
+            for (int j = 0; j < kRatNA + kRatNB; ++j) ps[j] += __shfl_xor_sync(0xffffffffu, ps[j], off);
+          }
+          if (lane == 0) {
+#pragma unroll
+            for (int j = 0; j < kRatNA + kRatNB; ++j) p.rws[((size_t)j * n_chunks + i0 / 32) * p.n_rq + rq] = ps[j];
+          }
+        }
+      }
+    } else if constexpr (BK == 0) {
       // Two sets of four warps: set h2 reads TMEM lane quarter q (rows 32 q ..) of
       // column chunks 4 h2 .. 4 h2 + 3, i.e. the inputs IPT/2 h2 .. of the tile,
       // and writes those inputs' dx.
@@ -948,11 +1073,19 @@ struct WgradParams {
   int tab_stride;  // B-spline: row stride of the producers' private knot tables (>= nk)
   TileMap tiles;
   BasisDev bd;
+  // split K (feature matrix by TMA, no fold / mask / scale / base): tile t of
+  // split s = t / tiles.count() sums K steps [s ks, (s + 1) ks) and writes its
+  // float32 partial (O, I K) block s of `part`; 1 = no split
+  int n_split, ks;
+  float* part;
 };
 
 constexpr int kWgradThreads = 768;     // w0 TMA, w1 MMA (CTA 0), w4-7 epilogue, w8-23 producers (2 groups)
 constexpr int kWgradTmaThreads = 256;  // A_TMA: w0 TMA, w1 MMA (CTA 0), w4-7 epilogue
 constexpr int kXTile = kBK * 8 * 2;  // x tile per stage: 64 rows x 8 inputs bf16 = 1 KB
+// Pipeline depth: five stages when both operands arrive by TMA, four with
+// producer warps (their two groups own alternate K steps).
+constexpr int wgrad_stages(bool a_tma) { return a_tma ? 5 : kStages; }
 
 // The coefficient gradient runs on CTA pairs like the forward: a tile is 256
 // feature rows (CTA r evaluates the features of inputs IPT r .. IPT r + IPT - 1
@@ -969,14 +1102,15 @@ template <int BK, int F, bool A_TMA>
 __global__ void __launch_bounds__(A_TMA ? kWgradTmaThreads : kWgradThreads, 1)
     fused_wgrad_kernel(const __grid_constant__ CUtensorMap tmap_dy, const __grid_constant__ CUtensorMap tmap_x,
                        WgradParams p) {
+  constexpr int NS = wgrad_stages(A_TMA);
   constexpr int IPT = kBM / F;  // inputs per tile (rows of the feature operand)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = align1024(smem_raw);
   uint8_t* sa = base;
-  uint8_t* sb = sa + kStages * kATile;                           // kStages x 16 KB (this CTA's half of dy)
-  Ctl* ctl = reinterpret_cast<Ctl*>(sb + kStages * kBHalf);
+  uint8_t* sb = sa + NS * kATile;                           // NS x 16 KB (this CTA's half of dy)
+  Ctl* ctl = reinterpret_cast<Ctl*>(sb + NS * kBHalf);
   uint8_t* sx = align1024(reinterpret_cast<uint8_t*>(ctl + 1));  // x tiles [stage][64 rows][8 inputs]
-  float* stg = reinterpret_cast<float*>(sx + kStages * kXTile);  // epilogue staging [128][33]
+  float* stg = reinterpret_cast<float*>(sx + NS * kXTile);  // epilogue staging [128][33]
   float* tabs = stg + 128 * 33;                                   // B-spline: per producer warp [(BK+1) * ts]
   float* sfold = tabs + (BK > 0 ? 16 * (BK + 1) * p.tab_stride : 0);  // fold matrix [K][F], zero past nt
   __nv_bfloat16* sout = reinterpret_cast<__nv_bfloat16*>(sfold + 32 * 32);  // dcoef of a chunk [32][IPT * K]
@@ -986,7 +1120,7 @@ __global__ void __launch_bounds__(A_TMA ? kWgradTmaThreads : kWgradThreads, 1)
   volatile int* abort = &ctl->abort;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < NS; ++s) {
       mbar_init(&ctl->full_a[s], 16);   // the 8 warps of the owning producer group, in each CTA (used in CTA 0)
       mbar_init(&ctl->full_b[s], 1);    // CTA 0's expect_tx for both dy halves (and A_TMA: feature halves)
       mbar_init(&ctl->tab_full[s], 1);  // this CTA's x tile
@@ -1013,20 +1147,28 @@ __global__ void __launch_bounds__(A_TMA ? kWgradTmaThreads : kWgradThreads, 1)
   cluster_sync();  // both CTAs' barriers exist before any remote arrive
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
-  const int n_tiles = p.tiles.count();
+  const int n_mn = p.tiles.count();
+  const int n_tiles = n_mn * p.n_split;
+  // tile t: output tile (m, n) of split t / n_mn, K steps [k0, k1)
+  auto decode = [&](int t, int& m, int& n, int& k0, int& k1) {
+    const int sp = t / n_mn;
+    p.tiles.get(t - sp * n_mn, m, n);
+    k0 = sp * p.ks;
+    k1 = min(p.k_steps, k0 + p.ks);
+  };
 
   if (warp == 0) {
     if (lane == 0) {
       int it = 0;
       for (int t = pair; t < n_tiles && !*abort; t += n_pairs) {
-        int m, n;
-        p.tiles.get(t, m, n);
+        int m, n, k0, k1;
+        decode(t, m, n, k0, k1);
         const int x0 = ((m * 2 + (int)rank) * IPT) & ~7;  // TMA x coordinate rounded down to 16 bytes
         const int o0 = n * kBN + (int)rank * (kBN / 2);
         const int f0 = (m * 2 + (int)rank) * kBM;         // A_TMA: first feature column of this CTA
-        for (int k = 0; k < p.k_steps; ++k, ++it) {
-          const int s = it % kStages;
-          const uint32_t ph = (it / kStages) & 1;
+        for (int k = k0; k < k1; ++k, ++it) {
+          const int s = it % NS;
+          const uint32_t ph = (it / NS) & 1;
           if (!mbar_wait(&ctl->empty[s], ph ^ 1, abort)) break;
           if (!A_TMA && p.x_tma) {
             mbar_arrive_expect_tx(&ctl->tab_full[s], kXTile);
@@ -1058,11 +1200,11 @@ __global__ void __launch_bounds__(A_TMA ? kWgradTmaThreads : kWgradThreads, 1)
       // Abort: CTA 0 drains the dy loads of both CTAs (they complete on its
       // barriers); each CTA drains its own x tiles.
       if (*abort) {
-        if (rank == 0) drain_tma(ctl, it);
+        if (rank == 0) drain_tma<NS>(ctl, it);
         if (p.x_tma) {
-          for (int s = 0; s < kStages; ++s) {
-            const int last = it - 1 - ((it - 1 - s) % kStages + kStages) % kStages;
-            if (it > 0 && last >= 0) mbar_drain(&ctl->tab_full[s], (last / kStages) & 1);
+          for (int s = 0; s < NS; ++s) {
+            const int last = it - 1 - ((it - 1 - s) % NS + NS) % NS;
+            if (it > 0 && last >= 0) mbar_drain(&ctl->tab_full[s], (last / NS) & 1);
           }
         }
       }
@@ -1072,14 +1214,16 @@ __global__ void __launch_bounds__(A_TMA ? kWgradTmaThreads : kWgradThreads, 1)
       const uint32_t idesc = idesc_bf16_f32(kPairM, kBN, true, true);  // both operands MN-major
       int it = 0, tc = 0;
       for (int t = pair; t < n_tiles && !*abort; t += n_pairs, ++tc) {
+        int m, n, k0, k1;
+        decode(t, m, n, k0, k1);
         const int acc = tc & 1;
         if (!mbar_wait_cluster(&ctl->acc_empty[acc], ((tc >> 1) & 1) ^ 1, abort)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem + acc * kBN;
         bool ok = true;
-        for (int k = 0; k < p.k_steps; ++k, ++it) {
-          const int s = it % kStages;
-          const uint32_t ph = (it / kStages) & 1;
+        for (int k = k0; k < k1; ++k, ++it) {
+          const int s = it % NS;
+          const uint32_t ph = (it / NS) & 1;
           if ((!A_TMA && !mbar_wait_cluster(&ctl->full_a[s], ph, abort)) || !mbar_wait_cluster(&ctl->full_b[s], ph, abort)) {
             ok = false;
             break;
@@ -1089,7 +1233,7 @@ __global__ void __launch_bounds__(A_TMA ? kWgradTmaThreads : kWgradThreads, 1)
 #pragma unroll
           for (int j = 0; j < kBK / 16; ++j) {
             mma_bf16_pair(d_tmem, smem_desc_sw128(a0 + 2048 * j, 8192, 1024), smem_desc_sw128(b0 + 2048 * j, 8192, 1024), idesc,
-                          (k > 0 || j > 0) ? 1u : 0u);
+                          (k > k0 || j > 0) ? 1u : 0u);
           }
           mma_commit_pair(&ctl->empty[s], 0x3);
         }
@@ -1112,8 +1256,9 @@ __global__ void __launch_bounds__(A_TMA ? kWgradTmaThreads : kWgradThreads, 1)
     }
     int tc = 0;
     for (int t = pair; t < n_tiles; t += n_pairs, ++tc) {
-      int m, n;
-      p.tiles.get(t, m, n);
+      int m, n, k0, k1;
+      decode(t, m, n, k0, k1);
+      float* part = p.part ? p.part + (size_t)(t / n_mn) * p.O * ((size_t)p.I * p.K) : nullptr;
       const int i_base = (m * 2 + (int)rank) * IPT;
       const int n_u = min(IPT, p.I - i_base);  // inputs of this CTA's rows that exist
       const int row_len = n_u * K;              // bf16 of one output's contiguous dcoef slice
@@ -1143,6 +1288,11 @@ __global__ void __launch_bounds__(A_TMA ? kWgradTmaThreads : kWgradThreads, 1)
           if (o >= p.O || i >= p.I) continue;
           const float* dcol = stg + (u * F) * 33 + ol;  // dpacked[o, i, j] = dcol[j * 33]
           const int64_t e = (int64_t)o * p.I + i;
+          if (part) {  // split K: this split's float32 partial, reduced by the caller's kernel
+            float* dst = part + e * K;
+            for (int kk = 0; kk < K; ++kk) dst[kk] = dcol[kk * 33];
+            continue;
+          }
           __nv_bfloat16* so = sout + ol * (IPT * K) + u * K;
           // C_eff = coef * scale * mask  =>  dcoef = dC_eff * scale * mask,
           // dscale = sum_k dC_eff * coef * mask; base_eff = base * mask (kanforge/torch/layers.py:162-167)
@@ -1173,6 +1323,7 @@ __global__ void __launch_bounds__(A_TMA ? kWgradTmaThreads : kWgradThreads, 1)
           if (p.dbase) p.dbase[e] = __float2bfloat16_rn(dcol[(F - 1) * 33] * mk);
         }
         named_bar(1, 128);  // sout complete
+        if (part) continue;
         // each output's slice (o, i_base .. i_base + n_u - 1, 0 .. K - 1) is
         // contiguous in dcoef: warp q copies rows q, q + 4, ..., lanes along the
         // row, in bf16 pairs when the row starts 4-byte aligned and is even.
@@ -1221,8 +1372,8 @@ __global__ void __launch_bounds__(A_TMA ? kWgradTmaThreads : kWgradThreads, 1)
       int k = ((it & 1) == grp) ? 0 : 1;
       for (; k < p.k_steps; k += 2) {
         const int git = it + k;
-        const int s = git % kStages;
-        const uint32_t ph = (git / kStages) & 1;
+        const int s = git % NS;
+        const uint32_t ph = (git / NS) & 1;
         float xv[2] = {0.0f, 0.0f};
         if (!p.x_tma) {
 #pragma unroll
@@ -1608,8 +1759,8 @@ int dispatch_fused(const kf_basis_desc* d, int f_pad, Fn&& fn) {
 }
 
 
-constexpr size_t kFwdSmem = 1024 + kStages * (kATile + kFwdNB * kBHalf) + sizeof(Ctl);
-constexpr size_t kPairSmem = 1024 + kStages * (kATile + kBHalf) + sizeof(Ctl);
+// Shared memory of the pair kernels with ns stages of A (16 KB) and nb halves of B (16 KB each).
+constexpr size_t pair_smem(int ns, int nb) { return 1024 + (size_t)ns * (kATile + nb * kBHalf) + sizeof(Ctl); }
 
 // Largest number of co-resident CTA pairs for a cluster launch of `kern`
 // (clusters of 2), cached per device in the caller's `cache`.
@@ -1636,11 +1787,21 @@ struct FwdLaunch {
   int go() const {
     return a_tma ? launch<BK, F, true>() : launch<BK, F, false>();
   }
+  // Six stages when both operands arrive by TMA into 256-output tiles (the
+  // GR-KAN contractions), else four (producer groups own one stage each; a
+  // 512-output stage is 48 KB).
   template <int BK, int F, bool A_TMA>
   int launch() const {
+    if constexpr (A_TMA && BK == 0 && F == 16) {
+      if (p.nblk == 1) return launch_ns<BK, F, A_TMA, kMaxStages>();
+    }
+    return launch_ns<BK, F, A_TMA, kStages>();
+  }
+  template <int BK, int F, bool A_TMA, int NS>
+  int launch_ns() const {
     constexpr int IPK = kBK / F;
-    const size_t smem = kFwdSmem + (BK > 0 && !A_TMA ? 1024 + sizeof(float) * kStages * IPK * (BK + 1) * kTabStride : 0);
-    auto kern = fused_fwd_kernel<BK, F, A_TMA>;
+    const size_t smem = pair_smem(NS, p.nblk) + (BK > 0 && !A_TMA ? 1024 + sizeof(float) * NS * IPK * (BK + 1) * kTabStride : 0);
+    auto kern = fused_fwd_kernel<BK, F, A_TMA, NS>;
     KF_CUDA_RET(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1669,7 +1830,8 @@ struct DgradLaunch {
   template <int BK, int F>
   int go() const {
     constexpr int IPT = kBN / F;
-    const size_t smem = kPairSmem + sizeof(float) * (BK > 0 ? 2 * IPT * (BK + 1) * p.tab_ts + 16 * 32 * (F + 1) : kBM * (IPT + 1));
+    const size_t smem = pair_smem(dgrad_stages(BK), 1) + sizeof(float) * (BK > 0 ? 2 * IPT * (BK + 1) * p.tab_ts + 16 * 32 * (F + 1)
+                                                      : BK == 0 ? kBM * (IPT + 1) : 0);
     auto kern = fused_dgrad_kernel<BK, F>;
     KF_CUDA_RET(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     cudaLaunchAttribute attr[1];
@@ -1703,7 +1865,7 @@ struct WgradLaunch {
   }
   template <int BK, int F, bool A_TMA>
   int launch() const {
-    const size_t smem = kPairSmem + 1024 + kStages * kXTile +
+    const size_t smem = pair_smem(wgrad_stages(A_TMA), 1) + 1024 + wgrad_stages(A_TMA) * kXTile +
                         sizeof(float) * (128 * 33 + (BK > 0 ? 16 * (BK + 1) * p.tab_stride : 0) + 32 * 32) +
                         sizeof(__nv_bfloat16) * 32 * 128;
     if (smem > 232448) {
@@ -1725,7 +1887,8 @@ struct WgradLaunch {
     cfg.numAttrs = 1;
     cfg.gridDim = dim3(2 * (unsigned)(sm_count() / 2));
     static int pair_cache[64] = {0};  // per instantiation
-    const int pairs = (int)std::min<int64_t>(p.tiles.m_tiles * (int64_t)p.tiles.n_tiles, max_pairs(kern, cfg, pair_cache));
+    const int pairs = (int)std::min<int64_t>(p.tiles.m_tiles * (int64_t)p.tiles.n_tiles * p.n_split,
+                                             max_pairs(kern, cfg, pair_cache));
     cfg.gridDim = dim3(2 * (unsigned)pairs);
     KF_CUDA_RET(cudaLaunchKernelEx(&cfg, kern, *tmap_dy, *tmap_x, p));
     return check_launch("kf_wgrad");
@@ -1784,6 +1947,43 @@ struct FeatureF32SplineLaunch {
   }
 };
 
+// GR-KAN parameter gradients: dnum[g, j] (j < 6) and dden[g, j - 6] = the sum
+// of the input-gradient epilogue's partial sums rws[j][chunk][rq] over the 32-row
+// blocks rq and the group's 32-input chunks, which are cpg * n_rq consecutive
+// floats; one CTA per (group, coefficient), fixed per-thread strides and a fixed
+// tree, so the result is deterministic.
+__global__ void __launch_bounds__(256) grkan_reduce_kernel(const float* __restrict__ rws, float* __restrict__ dnum,
+                                                           float* __restrict__ dden, int n_chunks, int cpg, int n_rq) {
+  __shared__ float red[256];
+  constexpr int W = kRatNA + kRatNB;
+  const int g = blockIdx.x / W, j = blockIdx.x % W;
+  const float* src = rws + ((size_t)j * n_chunks + (size_t)g * cpg) * n_rq;
+  const int64_t n = (int64_t)cpg * n_rq;
+  float acc = 0.0f;
+  for (int64_t e = threadIdx.x; e < n; e += 256) acc += src[e];
+  red[threadIdx.x] = acc;
+  __syncthreads();
+  for (int st = 128; st > 0; st >>= 1) {
+    if (threadIdx.x < st) red[threadIdx.x] += red[threadIdx.x + st];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    if (j < kRatNA) dnum[g * kRatNA + j] = red[0];
+    else dden[g * kRatNB + (j - kRatNA)] = red[0];
+  }
+}
+
+int grkan_check(const kf_basis_desc* d, int64_t B, int I, int O, const char* who) {
+  KF_CHECK_ARG(d != nullptr && d->kind == KF_BASIS_RATIONAL, "%s: needs a rational basis", who);
+  KF_CHECK_ARG(d->degree == kRatNA - 1 && d->den_degree == kRatNB, "%s: rational degrees (%d, %d), the kernel takes (5, 4)", who,
+               d->degree, d->den_degree);
+  KF_CHECK_ARG(B >= 0 && I >= 1 && O >= 1, "%s: bad sizes", who);
+  KF_CHECK_ARG(d->groups >= 1 && I % d->groups == 0 && (I / d->groups) % 32 == 0,
+               "%s: inputs per group (I %d / groups %d) must be a multiple of 32", who, I, d->groups);
+  KF_CHECK_ARG(O % 8 == 0, "%s: O (%d) must be a multiple of 8", who, O);
+  return KF_OK;
+}
+
 }  // namespace
 
 
@@ -1798,6 +1998,7 @@ extern "C" int kf_fwd(const void* x, const void* feat, const void* packed, const
   if (int rc = bind_device(x)) return rc;
   KF_CHECK_ARG(B >= 0 && I >= 1 && O >= 1, "kf_fwd: bad sizes");
   KF_CHECK_ARG(O % 8 == 0, "kf_fwd: O (%d) must be a multiple of 8", O);
+  KF_CHECK_ARG(((uintptr_t)y % 16) == 0 && ((uintptr_t)bias % 16) == 0, "kf_fwd: y and bias must be 16-byte aligned");
   FwdParams p{};
   if (int rc = fill_basis(basis, knot_tab, nt, has_base, f_pad, p.bd)) return rc;
   if (B == 0) return KF_OK;
@@ -1923,6 +2124,8 @@ extern "C" int kf_wgrad(const void* x, const void* feat, const void* dy, const f
   p.O = O;
   p.K = K;
   p.k_steps = (int)cdiv(B, kBK);
+  p.n_split = 1;
+  p.ks = p.k_steps;
   const int ipt = kBM / f_pad;  // inputs per CTA of a pair tile
   p.tiles.m_tiles = (int)cdiv(I, 2 * ipt);
   p.tiles.n_tiles = (int)cdiv(O, kBN);
@@ -1965,4 +2168,178 @@ extern "C" int kf_knot_tables(const float* grid, float* tab, int32_t I, int32_t 
     default: knot_table_kernel<5><<<blocks, 256, 0, s>>>(grid, tab, I, grid_size); break;
   }
   return check_launch("kf_knot_tables");
+}
+
+// ---------------------------------------------------------------------------
+// GR-KAN layers (kanforge/torch/layers.py:335-363): the rational activation R
+// (kf_rational_act) followed by the linear map of coef[..., 0] = W (O, I),
+// the three contractions on the CTA-pair kernels above.
+// ---------------------------------------------------------------------------
+
+extern "C" int64_t kf_grkan_workspace(int64_t B, int32_t I, const kf_basis_desc* basis) {
+  (void)basis;
+  if (B <= 0 || I <= 0) return 0;
+  // one slot per 32-row block of every pair tile (rows past B included, they hold zeros)
+  return (int64_t)(kf::kRatNA + kf::kRatNB) * (I / 32) * 8 * kf::cdiv(B, (int64_t)kf::kPairM);
+}
+
+extern "C" int kf_grkan_fwd(const void* r, const void* w, const void* bias, void* y, int64_t B, int32_t I, int32_t O,
+                            void* stream) {
+  using namespace kf;
+  clear_error();
+  KF_CHECK_ARG(r && w && y, "kf_grkan_fwd: null tensor pointer");
+  if (int rc = bind_device(r)) return rc;
+  KF_CHECK_ARG(B >= 0 && I >= 1 && O >= 1, "kf_grkan_fwd: bad sizes");
+  KF_CHECK_ARG(I % 16 == 0 && O % 8 == 0, "kf_grkan_fwd: I (%d) must be a multiple of 16 and O (%d) of 8", I, O);
+  KF_CHECK_ARG(((uintptr_t)r % 16) == 0 && ((uintptr_t)w % 16) == 0 && ((uintptr_t)y % 16) == 0 && ((uintptr_t)bias % 16) == 0,
+               "kf_grkan_fwd: r, w, y and bias must be 16-byte aligned");
+  if (B == 0) return KF_OK;
+  FwdParams p{};
+  p.bias = (const __nv_bfloat16*)bias;
+  p.y = (__nv_bfloat16*)y;
+  p.B = B;
+  p.I = I / 16;  // the kernel's K extent is I * F with F = 16
+  p.O = O;
+  p.k_steps = (int)cdiv(I, kBK);
+  p.tiles.m_tiles = (int)cdiv(B, kPairM);
+  // 256-output tiles: the two accumulators alternate between tiles, so each
+  // tile's epilogue overlaps the next tile's MMAs (the K loops are short)
+  p.nblk = 1;
+  p.tiles.n_tiles = (int)cdiv(O, p.nblk * kBN);
+  p.tiles.gm = std::min(p.tiles.m_tiles, 8);
+  CUtensorMap tmap, tmap_a;
+  if (int rc = make_tmap_bf16(&tmap, w, O, I, kBK, kBN / 2)) return rc;
+  if (int rc = make_tmap_bf16(&tmap_a, r, B, I, kBK, kBM)) return rc;
+  FwdLaunch L{&tmap, &tmap_a, p, true, (cudaStream_t)stream};
+  return L.launch<0, 16, true>();
+}
+
+extern "C" int kf_grkan_dgrad(const void* x, const void* dy, const void* w, const float* num, const float* den, void* dx,
+                              float* dnum, float* dden, float* workspace, int64_t B, int32_t I, int32_t O,
+                              const kf_basis_desc* basis, void* stream) {
+  using namespace kf;
+  clear_error();
+  KF_CHECK_ARG(x && dy && w && num && den && dx && dnum && dden, "kf_grkan_dgrad: null tensor pointer");
+  if (int rc = grkan_check(basis, B, I, O, "kf_grkan_dgrad")) return rc;
+  if (int rc = bind_device(x)) return rc;
+  KF_CHECK_ARG(((uintptr_t)x % 16) == 0 && ((uintptr_t)dx % 16) == 0 && ((uintptr_t)dy % 16) == 0 && ((uintptr_t)w % 16) == 0,
+               "kf_grkan_dgrad: x, dx, dy and w must be 16-byte aligned");
+  cudaStream_t s = (cudaStream_t)stream;
+  const int groups = basis->groups;
+  if (B == 0) {
+    KF_CUDA_RET(cudaMemsetAsync(dnum, 0, sizeof(float) * groups * kRatNA, s));
+    KF_CUDA_RET(cudaMemsetAsync(dden, 0, sizeof(float) * groups * kRatNB, s));
+    return KF_OK;
+  }
+  KF_CHECK_ARG(workspace != nullptr, "kf_grkan_dgrad: null workspace (kf_grkan_workspace floats)");
+  DgradParams p{};
+  p.x = (const __nv_bfloat16*)x;
+  p.dx = (__nv_bfloat16*)dx;
+  p.B = B;
+  p.I = I;
+  p.O = O;
+  p.k_steps = (int)cdiv(O, kBK);
+  p.tiles.m_tiles = (int)cdiv(B, kPairM);
+  p.tiles.n_tiles = (int)cdiv(I, kBN);
+  p.tiles.gm = std::min(p.tiles.m_tiles, 8);
+  p.rnum = num;
+  p.rden = den;
+  p.ipg = I / groups;
+  p.rws = workspace;
+  p.n_rq = 8 * p.tiles.m_tiles;  // 32-row blocks of all pair tiles, rows past B included
+  CUtensorMap tdy, tc;
+  if (int rc = make_tmap_bf16(&tdy, dy, B, O, kBK, kBM)) return rc;
+  if (int rc = make_tmap_bf16(&tc, w, O, I, 64, kBK)) return rc;
+  DgradLaunch L{&tdy, &tc, p, s};
+  if (int rc = L.go<kRationalBK, 16>()) return rc;
+  grkan_reduce_kernel<<<groups * (kRatNA + kRatNB), 256, 0, s>>>(workspace, dnum, dden, I / 32, p.ipg / 32, p.n_rq);
+  return check_launch("kf_grkan_dgrad");
+}
+
+namespace kf {
+namespace {
+// K splits of the GR-KAN weight gradient: enough (pair tile, split) work items
+// to give every CTA pair of the GPU one, each split at least 16 K steps.
+int grkan_wgrad_splits(int64_t B, int I, int O) {
+  const int64_t tiles = cdiv(I, kPairM) * cdiv(O, kBN);
+  const int64_t k_steps = cdiv(B, kBK);
+  const int64_t pairs = sm_count() / 2;
+  const int64_t by_pairs = std::max<int64_t>(1, pairs / std::max<int64_t>(tiles, 1));
+  return (int)std::max<int64_t>(1, std::min<int64_t>({by_pairs, k_steps / 16, 16}));
+}
+
+// dw[e] = bf16(sum_s part[s][e]) in split order.
+__global__ void __launch_bounds__(256) split_sum_kernel(const float* __restrict__ part, __nv_bfloat16* __restrict__ dw, int64_t n,
+                                                        int n_split) {
+  for (int64_t e2 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; 2 * e2 < n; e2 += (int64_t)gridDim.x * blockDim.x) {
+    float2 acc = make_float2(0.0f, 0.0f);
+    for (int sp = 0; sp < n_split; ++sp) {
+      const float2 v = reinterpret_cast<const float2*>(part + (size_t)sp * n)[e2];
+      acc.x += v.x;
+      acc.y += v.y;
+    }
+    reinterpret_cast<uint32_t*>(dw)[e2] = pack_bf16x2(acc.x, acc.y);
+  }
+}
+}  // namespace
+}  // namespace kf
+
+extern "C" int64_t kf_grkan_wgrad_workspace(int64_t B, int32_t I, int32_t O) {
+  if (B <= 0 || I <= 0 || O <= 0) return 0;
+  const int ns = kf::grkan_wgrad_splits(B, I, O);
+  return ns > 1 ? (int64_t)ns * O * I : 0;
+}
+
+extern "C" int kf_grkan_wgrad(const void* r, const void* dy, void* dw, float* workspace, int64_t B, int32_t I, int32_t O,
+                              void* stream) {
+  using namespace kf;
+  clear_error();
+  KF_CHECK_ARG(r && dy && dw, "kf_grkan_wgrad: null tensor pointer");
+  if (int rc = bind_device(r)) return rc;
+  KF_CHECK_ARG(B >= 0 && I >= 1 && O >= 1, "kf_grkan_wgrad: bad sizes");
+  KF_CHECK_ARG(I % 16 == 0 && O % 8 == 0, "kf_grkan_wgrad: I (%d) must be a multiple of 16 and O (%d) of 8", I, O);
+  KF_CHECK_ARG(((uintptr_t)r % 16) == 0 && ((uintptr_t)dy % 16) == 0 && ((uintptr_t)dw % 4) == 0,
+               "kf_grkan_wgrad: r and dy must be 16-byte aligned, dw 4-byte aligned");
+  cudaStream_t s = (cudaStream_t)stream;
+  if (B == 0) {
+    KF_CUDA_RET(cudaMemsetAsync(dw, 0, sizeof(__nv_bfloat16) * (size_t)O * I, s));
+    return KF_OK;
+  }
+  // dW = dy^T R as the coefficient-gradient kernel with F = 16 feature columns
+  // per "input" (I / 16 of them), K = 16, no fold, mask, scale or base column:
+  // its (O, I / 16, 16) output is W's (O, I) layout.
+  WgradParams p{};
+  p.x = (const __nv_bfloat16*)r;
+  p.dcoef = (__nv_bfloat16*)dw;
+  p.B = B;
+  p.I = I / 16;
+  p.O = O;
+  p.K = 16;
+  p.k_steps = (int)cdiv(B, kBK);
+  p.n_split = grkan_wgrad_splits(B, I, O);
+  p.ks = (int)cdiv(p.k_steps, p.n_split);
+  p.n_split = (int)cdiv(p.k_steps, p.ks);  // no empty split
+  if (p.n_split > 1) {
+    KF_CHECK_ARG(workspace != nullptr && ((uintptr_t)workspace % 16) == 0,
+                 "kf_grkan_wgrad: needs a 16-byte aligned workspace of kf_grkan_wgrad_workspace floats");
+    p.part = workspace;
+  }
+  p.x_tma = 0;
+  p.tab_stride = 16;
+  p.bd.nt = 16;
+  p.tiles.m_tiles = (int)cdiv(I, kPairM);
+  p.tiles.n_tiles = (int)cdiv(O, kBN);
+  p.tiles.gm = std::min(p.tiles.m_tiles, 8);
+  CUtensorMap tdy, tx;
+  if (int rc = make_tmap_bf16(&tdy, dy, B, O, 64, kBK)) return rc;
+  if (int rc = make_tmap_bf16(&tx, r, B, I, 64, kBK)) return rc;
+  WgradLaunch L{&tdy, &tx, p, true, s};
+  if (int rc = L.launch<0, 16, true>()) return rc;
+  if (p.n_split > 1) {
+    const int64_t n = (int64_t)O * I;
+    const unsigned grid = (unsigned)std::min<int64_t>(cdiv(n / 2, 256), (int64_t)sm_count() * 8);
+    split_sum_kernel<<<grid, 256, 0, s>>>(workspace, (__nv_bfloat16*)dw, n, p.n_split);
+    return check_launch("kf_grkan_wgrad");
+  }
+  return KF_OK;
 }

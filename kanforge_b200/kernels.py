@@ -39,12 +39,13 @@ def set_launch_observer(fn) -> None:
 
 
 # Entry points that launch more than one kernel (partial sums + their reduction).
-_KERNELS_PER_CALL = {"kf_rational_bwd": 2, "kf_rational_bwd_noalloc": 2}
+_KERNELS_PER_CALL = {"kf_rational_bwd": 2, "kf_rational_bwd_noalloc": 2, "kf_grkan_dgrad": 2}
 
 
-def _launch(name: str, *args) -> None:
+def _launch(name: str, *args, kernels: int | None = None) -> None:
+    """Call entry point `name`; `kernels` overrides how many kernels it launches."""
     global LAUNCH_COUNT
-    LAUNCH_COUNT += _KERNELS_PER_CALL.get(name, 1)
+    LAUNCH_COUNT += kernels if kernels is not None else _KERNELS_PER_CALL.get(name, 1)
     if _observer is None:
         _lib.call(name, *args)
         return
@@ -232,7 +233,13 @@ def fused_ok(plan: KernelPlan | None, x: torch.Tensor, n_out: int, has_base: boo
 
 
 def _bf16_or_none(t):
-    return None if t is None else t.detach().to(_BF16).contiguous()
+    return None if t is None else _aligned16(t.detach().to(_BF16).contiguous())
+
+
+def _aligned16(t: torch.Tensor) -> torch.Tensor:
+    """t, or a copy of it when its data does not start on a 16-byte boundary
+    (a view into a larger tensor): the kernels read it in 16-byte vectors."""
+    return t if t.data_ptr() % 16 == 0 else t.clone()
 
 
 def pack_coef(coef, base, edge_scale, edge_mask, plan: KernelPlan, f_pad: int) -> torch.Tensor:
@@ -626,6 +633,124 @@ class _RationalAct(torch.autograd.Function):
 
 def rational_act(x2, num, den, plan, groups, m=0):
     return _RationalAct.apply(x2, num, den, plan, groups, m)
+
+
+# --- GR-KAN layers: the rational activation and the linear map on our GEMMs ---
+
+
+def grkan_ok(plan: KernelPlan | None, x: torch.Tensor, n_in: int, n_out: int, groups: int, coef_dtype) -> str | None:
+    """Which GEMM path serves a GR-KAN layer call: "bf16" (the tcgen05
+    contractions with the rational backward fused into the input gradient;
+    degrees (5, 4), inputs per group a multiple of 32, outputs a multiple of
+    8), "f32" (the rational kernels around three-TF32-product GEMMs; inputs and
+    outputs multiples of 4), or None."""
+    if plan is None or plan.kind != "rational" or x.device.type != "cuda" or coef_dtype != x.dtype:
+        return None
+    if n_in % groups:
+        return None
+    if x.dtype == _BF16:
+        num_deg, den_deg = plan.consts
+        if (num_deg, den_deg) == (5, 4) and (n_in // groups) % 32 == 0 and n_out % 8 == 0:
+            return "bf16"
+        return None
+    if x.dtype == torch.float32 and n_in % 4 == 0 and n_out % 4 == 0 and FP32_TENSOR_CORES:
+        return "f32"
+    return None
+
+
+def _grkan_reference_grads(x, num, den, w, bias, plan, groups, gy, need):
+    """Gradients of the GR-KAN layer as a differentiable graph (create_graph)."""
+    with torch.enable_grad():
+        leaves = [t.detach().requires_grad_(n) if t is not None else None for t, n in zip((x, num, den, w, bias), need)]
+        r = rational_act(leaves[0], leaves[1], leaves[2], plan, groups)
+        y = torch.nn.functional.linear(r.to(leaves[3].dtype), leaves[3], leaves[4])
+        want = [t for t, n in zip(leaves, need) if n and t is not None]
+        got = iter(torch.autograd.grad(y, want, gy, create_graph=True))
+    return tuple(next(got) if (n and t is not None) else None for t, n in zip(leaves, need))
+
+
+class _GRKANLinear(torch.autograd.Function):
+    """y = R(x) w^T + b for a GR-KAN layer (kanforge/torch/layers.py:335-363):
+    R = P / (1 + |Q|) per group (kf_rational_act), then the contraction on our
+    kernels.  bf16: kf_grkan_fwd / kf_grkan_dgrad (dR = dy w on the tensor
+    cores, dx = dR R'(x) and the rational parameter gradients in its epilogue)
+    / kf_grkan_wgrad.  float32: kf_gemm_tf32x3 for the three contractions and
+    kf_rational_bwd for dx and the parameter gradients.  Double backward builds
+    the gradients from differentiable pieces."""
+
+    @staticmethod
+    def forward(ctx, x, num, den, w, bias, plan, groups, path):
+        n_b, n_in = x.shape
+        n_out = w.shape[0]
+        x = x.contiguous()
+        w_c = w.detach().contiguous()
+        numf, denf = num.detach().float().contiguous(), den.detach().float().contiguous()
+        desc = plan.desc(groups)
+        r = torch.empty_like(x)
+        _launch("kf_rational_act", _ptr(x), _ptr(numf), _ptr(denf), _ptr(r), n_b, n_in, 0, ctypes.byref(desc),
+                _rat_dtype(x), _stream(x))
+        y = torch.empty(n_b, n_out, device=x.device, dtype=x.dtype)
+        b = None if bias is None else _aligned16(bias.detach().to(x.dtype).contiguous())
+        if path == "bf16":
+            _launch("kf_grkan_fwd", _ptr(r), _ptr(w_c), _ptr(b), _ptr(y), n_b, n_in, n_out, _stream(x))
+        else:
+            gemm_tf32x3(r, False, w_c, False, y, n_b, n_out, n_in, bias=b)
+        ctx.save_for_backward(x, num, den, w, bias)
+        ctx.r, ctx.w_c, ctx.numf, ctx.denf = r, w_c, numf, denf
+        ctx.plan, ctx.groups, ctx.path = plan, groups, path
+        return y
+
+    @staticmethod
+    def backward(ctx, gy):
+        x, num, den, w, bias = ctx.saved_tensors
+        plan, groups, path = ctx.plan, ctx.groups, ctx.path
+        need = ctx.needs_input_grad
+        r, w_c, numf, denf = ctx.r, ctx.w_c, ctx.numf, ctx.denf
+        ctx.r = ctx.w_c = ctx.numf = ctx.denf = None
+        if torch.is_grad_enabled():
+            grads = _grkan_reference_grads(x, num, den, w, bias, plan, groups, gy, need[:5])
+            return grads + (None, None, None)
+        n_b, n_in = x.shape
+        n_out = w.shape[0]
+        gy = gy.to(x.dtype).contiguous()
+        desc = plan.desc(groups)
+        stream = _stream(x)
+        dx = dnum = dden = dw = dbias = None
+        if need[0] or need[1] or need[2]:
+            dx = torch.empty_like(x)
+            dnum = torch.empty(num.shape, device=x.device, dtype=torch.float32)
+            dden = torch.empty(den.shape, device=x.device, dtype=torch.float32)
+            if path == "bf16":
+                ws_n = _lib.load().kf_grkan_workspace(n_b, n_in, ctypes.byref(desc))
+                ws = torch.empty(max(int(ws_n), 1), device=x.device, dtype=torch.float32)
+                _launch("kf_grkan_dgrad", _ptr(x), _ptr(gy), _ptr(w_c), _ptr(numf), _ptr(denf), _ptr(dx), _ptr(dnum),
+                        _ptr(dden), _ptr(ws), n_b, n_in, n_out, ctypes.byref(desc), stream)
+            else:
+                dr = torch.empty_like(x)
+                gemm_tf32x3(gy, False, w_c, True, dr, n_b, n_in, n_out)
+                ws_n = _lib.load().kf_rational_workspace(n_b, n_in, ctypes.byref(desc))
+                ws = torch.empty(max(int(ws_n), 1), device=x.device, dtype=torch.float32)
+                _launch("kf_rational_bwd", _ptr(x), _ptr(dr), _ptr(numf), _ptr(denf), _ptr(dx), _ptr(dnum), _ptr(dden),
+                        _ptr(ws), n_b, n_in, ctypes.byref(desc), _rat_dtype(x), stream)
+        if need[3]:
+            dw = torch.empty(n_out, n_in, device=x.device, dtype=x.dtype)
+            if path == "bf16":
+                ws_n = int(_lib.load().kf_grkan_wgrad_workspace(n_b, n_in, n_out))
+                ws = torch.empty(ws_n, device=x.device, dtype=torch.float32) if ws_n else None
+                _launch("kf_grkan_wgrad", _ptr(r), _ptr(gy), _ptr(dw), _ptr(ws), n_b, n_in, n_out, stream,
+                        kernels=2 if ws_n else 1)  # split K: the partial sums' reduction
+            else:
+                gemm_tf32x3(gy, True, r, True, dw, n_out, n_in, n_b)
+        if need[4] and bias is not None:
+            dbias = gy.sum(0, dtype=torch.float32).to(bias.dtype)
+        return (dx if need[0] else None, dnum.to(num.dtype) if (need[1] and dnum is not None) else None,
+                dden.to(den.dtype) if (need[2] and dden is not None) else None, dw.to(w.dtype) if dw is not None else None,
+                dbias, None, None, None)
+
+
+def grkan_linear(x2, num, den, w, bias, plan, groups, path):
+    """GR-KAN layer on (B, I) inputs; see ``_GRKANLinear``."""
+    return _GRKANLinear.apply(x2, num, den, w, bias, plan, groups, path)
 
 
 def check_device_errors() -> None:

@@ -564,6 +564,56 @@ def test_grkan_forward_and_gradients(dtype, tol):
         close(gr, want[key[nme]], tol if dtype == torch.float32 else 5e-2, f"d{nme}")
 
 
+# (B, I, O, groups): the bf16 GR-KAN tensor-core path (inputs per group a
+# multiple of 32): ragged row and output tiles, groups spanning several 256-input
+# tiles and several groups per tile, 512- and 256-output forward tiles
+GRKAN_TC_CASES = [(1000, 256, 136, 8), (513, 512, 64, 4), (300, 64, 24, 2), (4097, 768, 520, 8), (2048, 1024, 768, 8)]
+
+
+@pytest.mark.parametrize("n_b,n_in,n_out,groups", GRKAN_TC_CASES)
+def test_grkan_bf16_tensor_core_path_matches_oracle(n_b, n_in, n_out, groups):
+    torch.manual_seed(n_in)
+    layer = kb.GRKAN(n_in, n_out, groups=groups)
+    with torch.no_grad():
+        layer.basis_numerator.add_(0.05 * torch.randn_like(layer.basis_numerator))
+        layer.basis_denominator.add_(0.05 * torch.randn_like(layer.basis_denominator))
+        layer.bias.normal_(0, 0.1)
+        layer.edge_mask[1, 3] = 0
+    layer = layer.to(device=DEV, dtype=torch.bfloat16)
+    x0 = (torch.randn(n_b, n_in, device=DEV) * 1.5).to(torch.bfloat16)
+    assert kb.kernels.grkan_ok(layer._plan, x0, n_in, n_out, groups, layer.coef.dtype) == "bf16"
+    x = x0.clone().requires_grad_()
+    y = layer(x)
+    nodes = [y.grad_fn] + [f for f, _ in y.grad_fn.next_functions if f is not None]
+    assert any(type(f).__name__ == "_GRKANLinearBackward" for f in nodes)  # the tensor-core path served the call
+    dy = torch.randn_like(y)
+    names = [n for n, _ in layer.named_parameters()]
+    grads = torch.autograd.grad(y, [x] + [p for _, p in layer.named_parameters()], dy)
+    kb.kernels.check_device_errors()
+    n = layer_numpy(layer)
+    xs = x0.double().cpu().numpy()
+    kw = dict(coef=n["coef"], base_weight=None, bias=n["bias"], spec=n["spec"], params=n["params"], edge_scale=None,
+              edge_mask=n["edge_mask"])
+    close(y, ko.kan_linear(xs, **kw), BF16_TOL, "y")
+    want = ko.kan_linear_backward(xs, dy.double().cpu().numpy(), groups=groups, **kw)
+    close(grads[0], want["dx"], BF16_TOL, "dx")
+    key = {"coef": "dcoef", "bias": "dbias", "basis_numerator": "dnumerator", "basis_denominator": "ddenominator"}
+    for nme, gr in zip(names, grads[1:]):
+        close(gr, want[key[nme]], BF16_TOL if nme in ("coef", "bias") else 5e-2, f"d{nme}")
+
+
+def test_grkan_bf16_tensor_core_gradients_are_deterministic():
+    torch.manual_seed(1)
+    layer = kb.GRKAN(768, 520, groups=8).to(device=DEV, dtype=torch.bfloat16)
+    x = (torch.randn(3001, 768, device=DEV) * 1.5).to(torch.bfloat16).requires_grad_()
+    dy = torch.randn(3001, 520, device=DEV).to(torch.bfloat16)
+    params = [p for _, p in layer.named_parameters()]
+    first = torch.autograd.grad(layer(x), [x] + params, dy)
+    second = torch.autograd.grad(layer(x), [x] + params, dy)
+    for a, b in zip(first, second):
+        assert torch.equal(a, b)
+
+
 # (B, I, groups, p, q, misaligned x): the vector kernels (16-byte forward, paired
 # backward for degrees (5, 4)), their row and chunk tails, and the one-element
 # kernels (odd inputs per group, other degrees, x one element off alignment).
