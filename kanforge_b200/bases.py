@@ -182,10 +182,38 @@ class BSpline(Basis):
 INPUT_MAPS = ("tanh", "identity", "fractional")
 
 
+def chebyshev_gauss_nodes(n: int) -> np.ndarray:
+    """The n zeros of T_n, cos(pi (m + 1/2) / n)."""
+    return np.cos(np.pi * (np.arange(n) + 0.5) / n)
+
+
+def chebyshev_projection(values: np.ndarray) -> np.ndarray:
+    """Chebyshev coefficients (n, k) of k polynomials of degree < n from their
+    values (n, k) at the n Chebyshev-Gauss nodes, by the discrete orthogonality
+    of T_0 .. T_{n-1} on those nodes (exact for that degree: a DCT-II)."""
+    n = values.shape[0]
+    theta = np.pi * (np.arange(n) + 0.5) / n
+    t = np.cos(np.outer(np.arange(n), theta))  # t[j, m] = T_j(node m)
+    coef = (2.0 / n) * (t @ values)
+    coef[0] *= 0.5
+    return coef
+
+
+def _convert_to_chebyshev(series_cls, degree: int) -> np.ndarray:
+    """(degree+1, degree+1): column k = the Chebyshev coefficients of basis
+    polynomial k of a numpy polynomial series class (exact conversion)."""
+    out = np.zeros((degree + 1, degree + 1))
+    for k in range(degree + 1):
+        c = series_cls.basis(k).convert(kind=npcheb.Chebyshev).coef
+        out[: len(c), k] = c
+    return out
+
+
 class PolynomialBasis(Basis):
     """family_k(z) = sum_j T_j(z) A[j, k] of z = g(x), g = tanh or identity
-    (polynomial.py:30-111).  The kernels evaluate T_j(g(x)); A and every
-    derivative order are folded into the coefficients."""
+    (reference kanforge/bases/polynomial.py:30-111).  ``_cheb`` is A, built by
+    each family from its definition; the kernels evaluate T_j(g(x)) and fold
+    A and every derivative order into the coefficients."""
 
     default_input_map = "tanh"
     _is_chebyshev = False
@@ -193,30 +221,31 @@ class PolynomialBasis(Basis):
     def __init__(self, degree: int = 5, input_map: str | None = None):
         if degree < 0:
             raise ValueError("degree must be >= 0")
-        input_map = input_map or self.default_input_map
-        if input_map not in INPUT_MAPS:
-            raise ValueError(f"input_map must be one of {INPUT_MAPS}")
         self.degree = int(degree)
-        self.input_map = input_map
+        self.input_map = input_map or self.default_input_map
+        if self.input_map not in INPUT_MAPS:
+            raise ValueError(f"input_map must be one of {INPUT_MAPS}")
 
     @property
     def size(self) -> int:
         return self.degree + 1
 
-    def _family(self, z: np.ndarray) -> np.ndarray:
+    def family_values(self, z: np.ndarray) -> np.ndarray:
+        """(len(z), degree + 1) values of the family at float64 points z."""
         raise NotImplementedError
+
+    def _chebyshev_matrix(self) -> np.ndarray:
+        return chebyshev_projection(self.family_values(chebyshev_gauss_nodes(self.degree + 1)))
 
     @cached_property
     def _cheb(self) -> np.ndarray:
-        """Chebyshev coefficients (D+1, size): interpolation at the D+1 Chebyshev nodes."""
-        d = self.degree
-        nodes = np.cos(np.pi * (np.arange(d + 1) + 0.5) / (d + 1))
-        return np.linalg.solve(npcheb.chebvander(nodes, d), self._family(nodes))
+        """A, (degree + 1, size)."""
+        a = np.asarray(self._chebyshev_matrix(), dtype=np.float64)
+        a.setflags(write=False)
+        return a
 
     def param_specs(self):
-        if self.input_map == "fractional":
-            return {"exponent_logit": ParamSpec(np.zeros(1))}
-        return {}
+        return {"exponent_logit": ParamSpec(np.zeros(1))} if self.input_map == "fractional" else {}
 
     def config(self):
         return {"name": self.name, "degree": self.degree, "input_map": self.input_map}
@@ -224,40 +253,45 @@ class PolynomialBasis(Basis):
     def host_eval(self, x, params=None):
         x = np.asarray(x, dtype=np.float64)
         z = np.tanh(x) if self.input_map == "tanh" else x
-        return npcheb.chebvander(z, self.degree) @ self._cheb
+        return np.moveaxis(npcheb.chebval(z, self._cheb), 0, -1)
 
 
 class Chebyshev(PolynomialBasis):
-    """T_n(tanh x) (ChebyKAN)."""
+    """T_n(tanh x) (ChebyKAN): A is the identity."""
 
     name = "chebyshev"
     _is_chebyshev = True
 
-    def _family(self, z):
-        return npcheb.chebvander(z, self.degree)
+    def _chebyshev_matrix(self):
+        return np.eye(self.degree + 1)
 
 
 class Chebyshev2(PolynomialBasis):
-    """Chebyshev polynomials of the second kind U_n."""
+    """Chebyshev polynomials of the second kind:
+    U_n = 2 (T_n + T_{n-2} + ...) ending in T_1, or in T_0 counted once."""
 
     name = "chebyshev2"
 
-    def _family(self, z):
-        u = [np.ones_like(z), 2 * z]
-        for _ in range(2, self.degree + 1):
-            u.append(2 * z * u[-1] - u[-2])
-        return np.stack(u[: self.degree + 1], -1)
+    def _chebyshev_matrix(self):
+        d = self.degree
+        a = np.zeros((d + 1, d + 1))
+        for n in range(d + 1):
+            a[n % 2 : n + 1 : 2, n] = 2.0
+            if n % 2 == 0:
+                a[0, n] = 1.0
+        return a
 
 
 class Legendre(PolynomialBasis):
     name = "legendre"
 
-    def _family(self, z):
-        return nplegendre.legvander(z, self.degree)
+    def _chebyshev_matrix(self):
+        return _convert_to_chebyshev(np.polynomial.Legendre, self.degree)
 
 
 class Jacobi(PolynomialBasis):
-    """Jacobi polynomials P_n^(alpha, beta) by their three-term recurrence."""
+    """Jacobi polynomials P_n^(alpha, beta), P_n(1) = C(n + alpha, n), from the
+    three-term recurrence P_{n+1} = (a_n z + b_n) P_n - c_n P_{n-1} (DLMF 18.9.2)."""
 
     name = "jacobi"
 
@@ -267,21 +301,28 @@ class Jacobi(PolynomialBasis):
         super().__init__(degree, input_map)
         self.alpha, self.beta = float(alpha), float(beta)
 
-    def _family(self, z):
-        a, b = self.alpha, self.beta
-        vals = [np.ones_like(z), (a + 1) + (a + b + 2) * (z - 1) / 2]
-        for n in range(2, self.degree + 1):
-            c = 2 * n + a + b
-            num = (c - 1) * (c * (c - 2) * z + a * a - b * b) * vals[-1] - 2 * (n + a - 1) * (n + b - 1) * c * vals[-2]
-            vals.append(num / (2 * n * (n + a + b) * (c - 2)))
-        return np.stack(vals[: self.degree + 1], -1)
+    def family_values(self, z):
+        al, be = self.alpha, self.beta
+        out = np.empty(z.shape + (self.degree + 1,))
+        out[..., 0] = 1.0
+        if self.degree >= 1:
+            out[..., 1] = 0.5 * (al - be) + 0.5 * (al + be + 2.0) * z
+        for n in range(1, self.degree):
+            s = 2.0 * n + al + be
+            denom = 2.0 * (n + 1) * (n + al + be + 1) * s
+            a_n = (s + 1) * (s + 2) * s / denom
+            b_n = (s + 1) * (al * al - be * be) / denom
+            c_n = 2.0 * (n + al) * (n + be) * (s + 2) / denom
+            out[..., n + 1] = (a_n * z + b_n) * out[..., n] - c_n * out[..., n - 1]
+        return out
 
     def config(self):
         return {**super().config(), "alpha": self.alpha, "beta": self.beta}
 
 
 class Gegenbauer(PolynomialBasis):
-    """Gegenbauer polynomials C_n^(lam)."""
+    """Gegenbauer (ultraspherical) polynomials C_n^(lam):
+    (n + 1) C_{n+1} = 2 (n + lam) z C_n - (n + 2 lam - 1) C_{n-1}."""
 
     name = "gegenbauer"
 
@@ -291,12 +332,15 @@ class Gegenbauer(PolynomialBasis):
         super().__init__(degree, input_map)
         self.lam = float(lam)
 
-    def _family(self, z):
+    def family_values(self, z):
         lam = self.lam
-        vals = [np.ones_like(z), 2 * lam * z]
-        for n in range(2, self.degree + 1):
-            vals.append((2 * z * (n + lam - 1) * vals[-1] - (n + 2 * lam - 2) * vals[-2]) / n)
-        return np.stack(vals[: self.degree + 1], -1)
+        out = np.empty(z.shape + (self.degree + 1,))
+        out[..., 0] = 1.0
+        if self.degree >= 1:
+            out[..., 1] = 2.0 * lam * z
+        for n in range(1, self.degree):
+            out[..., n + 1] = (2.0 * (n + lam) * z * out[..., n] - (n + 2.0 * lam - 1.0) * out[..., n - 1]) / (n + 1)
+        return out
 
     def config(self):
         return {**super().config(), "lam": self.lam}
@@ -307,29 +351,35 @@ class Hermite(PolynomialBasis):
 
     name = "hermite"
 
-    def _family(self, z):
-        return nphermite.hermvander(z, self.degree)
+    def _chebyshev_matrix(self):
+        return _convert_to_chebyshev(np.polynomial.Hermite, self.degree)
 
 
 class Laguerre(PolynomialBasis):
     name = "laguerre"
 
-    def _family(self, z):
-        return nplaguerre.lagvander(z, self.degree)
+    def _chebyshev_matrix(self):
+        return _convert_to_chebyshev(np.polynomial.Laguerre, self.degree)
 
 
 class Bernstein(PolynomialBasis):
-    """C(n, j) t^j (1 - t)^(n - j) of t = (z + 1) / 2."""
+    """Bernstein polynomials C(n, j) t^j (1 - t)^(n - j) of t = (z + 1) / 2."""
 
     name = "bernstein"
 
-    def _family(self, z):
-        t, n = (z + 1) / 2, self.degree
-        return np.stack([math.comb(n, j) * t**j * (1 - t) ** (n - j) for j in range(n + 1)], -1)
+    def family_values(self, z):
+        n = self.degree
+        t = 0.5 * (z + 1.0)
+        j = np.arange(n + 1)
+        binom = np.array([math.comb(n, k) for k in j], dtype=np.float64)
+        return binom * t[..., None] ** j * (1.0 - t)[..., None] ** (n - j)
 
 
 class Gram(PolynomialBasis):
-    """Polynomials orthonormal on ``points`` equally spaced points of [-1, 1]."""
+    """Gram polynomials: orthonormal for the mean over ``points`` equally spaced
+    points of [-1, 1] (mean of each square = 1), positive leading coefficient;
+    built by Gram-Schmidt on z * p_k, carried on those points and the Chebyshev
+    nodes together."""
 
     name = "gram"
 
@@ -339,12 +389,18 @@ class Gram(PolynomialBasis):
         if self.points <= self.degree:
             raise ValueError("points must be > degree")
 
-    @cached_property
-    def _cheb(self):
-        grid = np.linspace(-1, 1, self.points)
-        _q, r = np.linalg.qr(npcheb.chebvander(grid, self.degree))
-        sign = np.sign(np.diag(r))
-        return np.linalg.inv(r) * sign * math.sqrt(self.points)
+    def _chebyshev_matrix(self):
+        d, n_pts = self.degree, self.points
+        z = np.concatenate([np.linspace(-1.0, 1.0, n_pts), chebyshev_gauss_nodes(d + 1)])
+        mean = lambda f, g: float(np.dot(f[:n_pts], g[:n_pts])) / n_pts  # noqa: E731
+        family = [np.ones_like(z)]
+        for _ in range(d):
+            q = z * family[-1]
+            for _sweep in range(2):  # re-orthogonalise once for accuracy
+                for p in family:
+                    q = q - mean(q, p) * p
+            family.append(q / math.sqrt(mean(q, q)))
+        return chebyshev_projection(np.stack(family, -1)[n_pts:])
 
     def config(self):
         return {**super().config(), "points": self.points}
@@ -356,8 +412,8 @@ class Taylor(PolynomialBasis):
     name = "taylor"
     default_input_map = "identity"
 
-    def _family(self, z):
-        return np.stack([z**j for j in range(self.degree + 1)], -1)
+    def _chebyshev_matrix(self):
+        return _convert_to_chebyshev(np.polynomial.Polynomial, self.degree)
 
 
 # ---------------------------------------------------------------------------
@@ -377,43 +433,64 @@ TARGETS = {
 }
 
 
+class _RationalLeastSquares:
+    """Least-squares fit of R = P / (1 + |Q|) to samples (x_n, y_n): P of degree
+    p (coefficients a_0..a_p), Q = sum_{j=1..q} b_j x^j; theta = (a, b)."""
+
+    def __init__(self, xs: np.ndarray, ys: np.ndarray, p: int, q: int):
+        self.ys = ys
+        self.n_num = p + 1
+        self.pow_num = xs[:, None] ** np.arange(p + 1)      # x^0 .. x^p
+        self.pow_den = xs[:, None] ** np.arange(1, q + 1)   # x^1 .. x^q
+
+    def linearised_start(self) -> np.ndarray:
+        """theta minimising |P - y Q - y|: the fit of P = y (1 + Q), which a
+        rational reaches exactly when it interpolates."""
+        design = np.concatenate([self.pow_num, -self.ys[:, None] * self.pow_den], axis=1)
+        return np.linalg.lstsq(design, self.ys, rcond=None)[0]
+
+    def evaluate(self, theta):
+        """(residual R - y, Q) at theta."""
+        q = self.pow_den @ theta[self.n_num:]
+        return (self.pow_num @ theta[: self.n_num]) / (1 + np.abs(q)) - self.ys, q
+
+    def jacobian(self, theta, q):
+        """dR/dtheta: x^j / D for a_j and -P sign(Q) x^j / D^2 for b_j, D = 1 + |Q|."""
+        d = 1 + np.abs(q)
+        p_val = self.pow_num @ theta[: self.n_num]
+        return np.concatenate([self.pow_num / d[:, None], (-p_val / d**2 * np.sign(q))[:, None] * self.pow_den], axis=1)
+
+
 @lru_cache(maxsize=None)
 def fit_rational(target: str, num_degree: int, den_degree: int, lim: float = 3.0):
-    """(a, b) of P/(1+|Q|) fitting ``target`` on [-lim, lim] (rational.py:27-61).
+    """(a, b) of the rational P / (1 + |Q|) closest to ``target`` on [-lim, lim].
 
-    Start from the linear least-squares solution of P - f Q = f, then
-    Levenberg-Marquardt on the true residual (damping x1/3 on success, x4 on
-    failure, stop above 1e8, at most 200 iterations).
+    The reference's initial fit (kanforge/bases/rational.py:27-61), whose
+    steps are kept so the coefficients agree to rounding: samples at 2001
+    evenly spaced points, the linearised least-squares start, then
+    Levenberg-Marquardt with Marquardt's diagonal scaling (system
+    J^T J + mu (diag(J^T J) + 1e-12)): mu starts at 1e-3, a step that lowers
+    the squared residual is taken and divides mu by 3, a rejected one
+    multiplies it by 4, and the search ends once mu exceeds 1e8 or after 200
+    trials.  Exact for ``identity``.
     """
-    f = TARGETS[target]
     xs = np.linspace(-lim, lim, 2001)
-    ys = f(xs)
-    vp = xs[:, None] ** np.arange(num_degree + 1)
-    vq = xs[:, None] ** np.arange(1, den_degree + 1)
-    theta = np.linalg.lstsq(np.hstack([vp, -ys[:, None] * vq]), ys, rcond=None)[0]
-    damping = 1e-3
-    npar = num_degree + 1
-
-    def resid(th):
-        s = vq @ th[npar:]
-        return (vp @ th[:npar]) / (1 + np.abs(s)) - ys, s
-
-    r, s = resid(theta)
-    for _ in range(200):
-        den = 1 + np.abs(s)
-        num = vp @ theta[:npar]
-        jac = np.hstack([vp / den[:, None], (-num / den**2 * np.sign(s))[:, None] * vq])
-        grad = jac.T @ r
-        jtj = jac.T @ jac
-        step = np.linalg.solve(jtj + damping * np.diag(np.diag(jtj) + 1e-12), -grad)
-        r_new, s_new = resid(theta + step)
-        if r_new @ r_new < r @ r:
-            theta, r, s, damping = theta + step, r_new, s_new, damping / 3
+    ls = _RationalLeastSquares(xs, TARGETS[target](xs), num_degree, den_degree)
+    theta = ls.linearised_start()
+    resid, q = ls.evaluate(theta)
+    mu, trials = 1e-3, 0
+    while trials < 200 and mu <= 1e8:
+        trials += 1
+        jac = ls.jacobian(theta, q)
+        normal = jac.T @ jac
+        delta = np.linalg.solve(normal + mu * np.diag(np.diag(normal) + 1e-12), -(jac.T @ resid))
+        cand_resid, cand_q = ls.evaluate(theta + delta)
+        if cand_resid @ cand_resid < resid @ resid:
+            theta, resid, q = theta + delta, cand_resid, cand_q
+            mu /= 3
         else:
-            damping *= 4
-        if damping > 1e8:
-            break
-    return theta[:npar].copy(), theta[npar:].copy()
+            mu *= 4
+    return theta[: num_degree + 1].copy(), theta[num_degree + 1:].copy()
 
 
 class Rational(Basis):

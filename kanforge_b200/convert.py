@@ -64,18 +64,18 @@ def _dtype_name(t: torch.Tensor) -> str:
 
 
 def _layer_spec(layer: KANLinear):
-    kw = layer._init_kwargs
+    opt = layer.options
     spec = {
         "type": "GRKAN" if isinstance(layer, GRKAN) else "KANLinear",
         "in": layer.in_features,
         "out": layer.out_features,
         "basis": layer.basis.config(),
-        "bias": bool(kw["bias"]),
-        "base_activation": activation_name(kw["base_activation"]),
-        "groups": kw["groups"],
-        "edge_scale": bool(kw["edge_scale"]),
-        "edge_dropout": float(kw["edge_dropout"]),
-        "backend": kw["backend"],
+        "bias": bool(opt.bias),
+        "base_activation": activation_name(opt.base_activation),
+        "groups": opt.groups,
+        "edge_scale": bool(opt.edge_scale),
+        "edge_dropout": float(opt.edge_dropout),
+        "backend": opt.backend,
         "dtype": _dtype_name(layer.coef),
     }
     return spec, {k: v for k, v in layer._export_full().items() if v is not None}

@@ -19,8 +19,10 @@ CPU tensors raise: there is no CPU fallback.
 
 from __future__ import annotations
 
+import functools
 import math
 from collections.abc import Callable, Sequence
+from dataclasses import dataclass
 
 import numpy as np
 import torch
@@ -28,7 +30,7 @@ import torch.nn.functional as F
 from torch import nn
 
 from . import kernels as _kernels
-from ._init import basis_param_values, init_stds, resolve_groups
+from ._init import init_stds, initial_basis_state, resolve_groups
 from .bases import Basis, Rational, make_basis
 from .plan import plan_for
 
@@ -54,13 +56,30 @@ class _EdgeDerivativeNoGrad(torch.autograd.Function):
         raise NotImplementedError("backward through KANLinear.edge_derivative is not available; use autograd on forward")
 
 
+@dataclass(frozen=True)
+class LayerOptions:
+    """The constructor choices a layer keeps for re-initialisation and export
+    (the ``.npz`` layer spec of kanforge/convert.py:108-160)."""
+
+    bias: bool
+    base_activation: Callable[[torch.Tensor], torch.Tensor] | None
+    groups: int | None  # as given: None = one group per input
+    edge_scale: bool
+    coef_init: str
+    coef_init_std: float
+    edge_dropout: float
+    backend: str
+    grid_ranges: object = None
+
+
 class KANLinear(nn.Module):
     """One KAN layer: y_o = sum_i s_oi phi_oi(x_i) + sum_i w_oi act(x_i) + b_o.
 
-    Parameters (reference names): ``coef`` (out, in, basis.size), ``base_weight``
-    (out, in), ``bias`` (out,), ``edge_scale`` (out, in), trainable basis
-    parameters ``basis_<name>`` (groups, *shape).  Buffers: ``basis_<name>``
-    grids (in, *shape), ``edge_mask``, ``sym_code``, ``sym_params``.
+    Parameters (reference names, kanforge/torch/layers.py:52-118): ``coef``
+    (out, in, basis.size), ``base_weight`` (out, in), ``bias`` (out,),
+    ``edge_scale`` (out, in), trainable basis parameters ``basis_<name>``
+    (groups, *shape).  Buffers: ``basis_<name>`` grids (in, *shape),
+    ``edge_mask``, ``sym_code``, ``sym_params``.
 
     ``backend`` is accepted for compatibility ("auto", "ops", "kernel"); every
     value runs the CUDA kernels.  ``"kernel"`` raises for a basis without one.
@@ -85,105 +104,102 @@ class KANLinear(nn.Module):
         dtype=None,
     ):
         super().__init__()
-        if not 0 <= edge_dropout < 1:
-            raise ValueError("edge_dropout must be in [0, 1)")
         if backend not in BACKENDS:
             raise ValueError(f"backend must be one of {BACKENDS}")
-        factory = {"device": device, "dtype": dtype}
-        self.in_features = in_features
-        self.out_features = out_features
+        if not 0.0 <= edge_dropout < 1.0:
+            raise ValueError("edge_dropout must be in [0, 1)")
+        self.options = LayerOptions(bias, base_activation, groups, edge_scale, coef_init, coef_init_std, edge_dropout,
+                                    backend, grid_ranges)
+        self.in_features, self.out_features = in_features, out_features
         self.basis = make_basis(basis)
         self.base_activation = base_activation
         self.groups = resolve_groups(in_features, groups)
-        self.coef_init = coef_init
-        self.coef_init_std = coef_init_std
-        self.edge_dropout = edge_dropout
-        self.backend = backend
-        self._grid_ranges = grid_ranges
-        self._init_kwargs = {
-            "basis": self.basis,
-            "bias": bias,
-            "base_activation": base_activation,
-            "groups": groups,
-            "edge_scale": edge_scale,
-            "coef_init": coef_init,
-            "coef_init_std": coef_init_std,
-            "edge_dropout": edge_dropout,
-            "backend": backend,
-        }
+        self.coef_init, self.coef_init_std = coef_init, coef_init_std
+        self.edge_dropout, self.backend = edge_dropout, backend
+        # rejects an unknown scheme before any tensor exists
         init_stds(self.basis, in_features, out_features, coef_init, coef_init_std, base_activation is not None)
-        self.coef = nn.Parameter(torch.empty(out_features, in_features, self.basis.size, **factory))
-        if base_activation is not None:
-            self.base_weight = nn.Parameter(torch.empty(out_features, in_features, **factory))
-        else:
-            self.register_parameter("base_weight", None)
-        if bias:
-            self.bias = nn.Parameter(torch.empty(out_features, **factory))
-        else:
-            self.register_parameter("bias", None)
-        if edge_scale:
-            self.edge_scale = nn.Parameter(torch.empty(out_features, in_features, **factory))
-        else:
-            self.register_parameter("edge_scale", None)
-        self.register_buffer("edge_mask", torch.empty(out_features, in_features, **factory))
-        self.register_buffer("sym_code", torch.empty(out_features, in_features, dtype=torch.int32, device=device))
-        self.register_buffer("sym_params", torch.empty(out_features, in_features, 4, **factory))
-        self._trainable_names: list[str] = []
-        self._buffer_names: list[str] = []
+
+        edge = (out_features, in_features)
+        tensor = functools.partial(torch.empty, device=device, dtype=dtype)
+        optional = {
+            "coef": edge + (self.basis.size,),
+            "base_weight": edge if base_activation is not None else None,
+            "bias": (out_features,) if bias else None,
+            "edge_scale": edge if edge_scale else None,
+        }
+        for name, shape in optional.items():
+            self.register_parameter(name, None if shape is None else nn.Parameter(tensor(shape)))
+        self.register_buffer("edge_mask", tensor(edge))
+        self.register_buffer("sym_code", torch.empty(edge, dtype=torch.int32, device=device))
+        self.register_buffer("sym_params", tensor(edge + (4,)))
+        self._basis_tensors: dict[str, bool] = {}  # basis_<name> -> trainable
         self.reset_parameters()
         if backend == "kernel" and self._plan is None:
             raise RuntimeError(f"no fused kernel for this basis: {self.basis!r}")
 
-    # --- parameters (reference layers.py:120-167) -----------------------------
+    # --- parameters ------------------------------------------------------------
 
-    def _set_basis_state(self, trainable: dict, buffers: dict) -> None:
-        for name in self._trainable_names + self._buffer_names:
+    def _install_basis_state(self, state) -> None:
+        """Registers the basis tensors of ``state`` (replacing the previous ones)
+        in the dtype and on the device of ``coef``."""
+        for name in self._basis_tensors:
             delattr(self, f"basis_{name}")
         like = {"dtype": self.coef.dtype, "device": self.coef.device}
-        for name, value in trainable.items():
-            self.register_parameter(f"basis_{name}", nn.Parameter(torch.as_tensor(np.ascontiguousarray(value), **like)))
-        for name, value in buffers.items():
-            self.register_buffer(f"basis_{name}", torch.as_tensor(np.ascontiguousarray(value), **like))
-        self._trainable_names, self._buffer_names = list(trainable), list(buffers)
+        self._basis_tensors = {}
+        for trainable, values in ((True, state.trainable), (False, state.buffers)):
+            for name, value in values.items():
+                t = torch.as_tensor(np.ascontiguousarray(value), **like)
+                if trainable:
+                    self.register_parameter(f"basis_{name}", nn.Parameter(t))
+                else:
+                    self.register_buffer(f"basis_{name}", t)
+                self._basis_tensors[name] = trainable
         self._plan = plan_for(self.basis)
 
+    @torch.no_grad()
     def reset_parameters(self) -> None:
-        coef_std, base_std = init_stds(
-            self.basis, self.in_features, self.out_features, self.coef_init, self.coef_init_std, self.base_weight is not None
-        )
-        nn.init.normal_(self.coef, std=coef_std) if coef_std else nn.init.zeros_(self.coef)
+        """Draws the coefficients and base weights of the layer's scheme
+        (reference kanforge/torch/layers.py:131-149) and resets the masks,
+        symbolic slots and basis state."""
+        opt = self.options
+        coef_std, base_std = init_stds(self.basis, self.in_features, self.out_features, opt.coef_init,
+                                       opt.coef_init_std, self.base_weight is not None)
+        if coef_std:
+            self.coef.normal_(0.0, coef_std)
+        else:
+            self.coef.zero_()
         if self.base_weight is not None:
             if base_std is None:
                 nn.init.kaiming_uniform_(self.base_weight, a=math.sqrt(5))
             else:
-                nn.init.normal_(self.base_weight, std=base_std)
-        if self.bias is not None:
-            nn.init.zeros_(self.bias)
-        if self.edge_scale is not None:
-            nn.init.ones_(self.edge_scale)
-        self.edge_mask.fill_(1.0)
-        self.sym_code.fill_(-1)
-        self.sym_params.zero_()
+                self.base_weight.normal_(0.0, base_std)
+        for t, value in ((self.bias, 0.0), (self.edge_scale, 1.0), (self.edge_mask, 1.0), (self.sym_code, -1),
+                         (self.sym_params, 0.0)):
+            if t is not None:
+                t.fill_(value)
         self._sym_codes = ()
-        self._set_basis_state(*basis_param_values(self.basis, self.groups, self.in_features, self._grid_ranges))
+        self._install_basis_state(initial_basis_state(self.basis, self.groups, self.in_features, opt.grid_ranges))
 
     def basis_params(self) -> dict[str, torch.Tensor]:
-        """Basis parameters and buffers expanded to (in, *shape) (layers.py:151-160)."""
-        rep = self.in_features // self.groups
+        """Every basis tensor with one row per input, (in, *shape): per-group
+        trainables repeated over their group's inputs (reference
+        kanforge/torch/layers.py:151-160; one group or one per input: as stored)."""
+        per_group = self.in_features // self.groups
+        expand = self.groups not in (1, self.in_features)
         out = {}
-        for name in self._trainable_names:
-            p = getattr(self, f"basis_{name}")
-            out[name] = p if self.groups in (1, self.in_features) else p.repeat_interleave(rep, dim=0)
-        for name in self._buffer_names:
-            out[name] = getattr(self, f"basis_{name}")
+        for name, trainable in self._basis_tensors.items():
+            t = getattr(self, f"basis_{name}")
+            out[name] = t.repeat_interleave(per_group, dim=0) if (trainable and expand) else t
         return out
 
     def effective_coef(self) -> torch.Tensor:
-        scale = self.edge_mask if self.edge_scale is None else self.edge_scale * self.edge_mask
-        return self.coef * scale[..., None]
+        """coef * edge_scale * edge_mask over the basis axis."""
+        gate = self.edge_mask if self.edge_scale is None else self.edge_mask * self.edge_scale
+        return self.coef * gate.unsqueeze(-1)
 
     def effective_base_weight(self) -> torch.Tensor | None:
-        return None if self.base_weight is None else self.base_weight * self.edge_mask
+        """base_weight * edge_mask (None without a base branch)."""
+        return None if self.base_weight is None else self.edge_mask * self.base_weight
 
     # --- computation ------------------------------------------------------------
 
@@ -219,6 +235,12 @@ class KANLinear(nn.Module):
         if plan.kind == "rational":
             lead = x.shape[:-1]
             x2 = x.reshape(-1, self.in_features)
+            path = None if base_eff is not None else _kernels.grkan_ok(plan, x2, self.in_features, self.out_features,
+                                                                      self.groups, self.coef.dtype)
+            if path is not None:
+                y = _kernels.grkan_linear(x2, self.basis_numerator, self.basis_denominator, coef_eff[..., 0], self.bias, plan,
+                                          self.groups, path)
+                return y.reshape(*lead, self.out_features)
             r = _kernels.rational_act(x2, self.basis_numerator, self.basis_denominator, plan, self.groups)
             y = F.linear(r.to(coef_eff.dtype), coef_eff[..., 0], self.bias)
             if base_eff is not None:

@@ -263,3 +263,38 @@ def test_float32_tensor_core_forward_launch_sequence(monkeypatch, basis, first):
     gemm = calls[-1][1]
     assert gemm[-4:-1] == (5, 8, 16 * f_pad)  # M = tokens, N = outputs, K = I * f_pad
     assert gemm[6].value == layer.bias.data_ptr()
+
+
+def test_polynomial_family_matrices_match_independent_evaluations():
+    """Every family's Chebyshev matrix A reproduces the family evaluated
+    independently (scipy.special, or the definition): family_k(z) =
+    sum_j T_j(z) A[j, k]; Gram polynomials are orthonormal on their points."""
+    from scipy import special
+
+    z = np.linspace(-1, 1, 41)
+    d = 7
+
+    def via_a(basis):
+        return np.polynomial.chebyshev.chebvander(z, basis.degree) @ basis._cheb
+
+    cases = [
+        (kb.Chebyshev(d), lambda n: special.eval_chebyt(n, z)),
+        (kb.Chebyshev2(d), lambda n: special.eval_chebyu(n, z)),
+        (kb.Legendre(d), lambda n: special.eval_legendre(n, z)),
+        (kb.Jacobi(d, 0.5, 1.5), lambda n: special.eval_jacobi(n, 0.5, 1.5, z)),
+        (kb.Jacobi(d, -0.3, 2.0), lambda n: special.eval_jacobi(n, -0.3, 2.0, z)),
+        (kb.Gegenbauer(d, 0.7), lambda n: special.eval_gegenbauer(n, 0.7, z)),
+        (kb.Hermite(d), lambda n: special.eval_hermite(n, z)),
+        (kb.Laguerre(d), lambda n: special.eval_genlaguerre(n, 0.0, z)),
+        (kb.Bernstein(d), lambda n: special.comb(d, n) * ((z + 1) / 2) ** n * ((1 - z) / 2) ** (d - n)),
+        (kb.Taylor(d), lambda n: z**n),
+    ]
+    for basis, fn in cases:
+        want = np.stack([fn(n) for n in range(d + 1)], -1)
+        np.testing.assert_allclose(via_a(basis), want, rtol=1e-11, atol=1e-11 * max(1.0, np.abs(want).max()),
+                                   err_msg=repr(basis))
+    g = kb.Gram(5, points=11)
+    pts = np.linspace(-1, 1, 11)
+    v = np.polynomial.chebyshev.chebvander(pts, 5) @ g._cheb
+    np.testing.assert_allclose(v.T @ v / 11, np.eye(6), atol=1e-12)
+    assert (np.diag(g._cheb) > 0).all()
