@@ -259,6 +259,52 @@ int64_t kf_grkan_wgrad_workspace(int64_t B, int32_t I, int32_t O);
 int kf_grkan_wgrad(const void* r, const void* dy, void* dw, float* workspace, int64_t B, int32_t I, int32_t O,
                    void* stream);
 
+/* ---- KAN convolutions (kanforge/torch/conv.py:57-85) ----
+ * A KANConvNd applies one KANLinear per channel group to every receptive
+ * field.  Its input is an implicit patch matrix of the image img (N, channels,
+ * size_0, size_1, size_2), channels-first, unused spatial dimensions of size
+ * 1: row (n, o_0, o_1, o_2) over the output positions, column (c, k_0, k_1,
+ * k_2) over the group's channels and the kernel offsets (the weight order of
+ * torch.nn.ConvNd), value img[n, channel0 + c, o_d stride_d - padding_d +
+ * k_d dilation_d] or 0 in the zero padding; out_d = (size_d + 2 padding_d -
+ * dilation_d (kernel_d - 1) - 1) / stride_d + 1.  rows = batch prod(out),
+ * cols = group_channels prod(kernel).  (Other padding modes: pad the image
+ * first and pass padding 0.) */
+typedef struct kf_conv_geom {
+  int32_t batch;          /* images N */
+  int32_t channels;       /* channels of img (all groups) */
+  int32_t group_channels; /* channels of this group */
+  int32_t channel0;       /* first channel of this group */
+  int32_t size[3];
+  int32_t kernel[3];
+  int32_t stride[3];
+  int32_t padding[3];
+  int32_t dilation[3];
+} kf_conv_geom;
+
+/* The patch matrix itself, (rows, cols) in `dtype` (for the float32 path and
+ * the primitives, which take a plain matrix). */
+int kf_conv_patches(const void* img, const kf_conv_geom* geom, void* patches, int dtype, void* stream);
+/* Its transpose: dimg[n, channel0 + c, p] = sum of dpatches over the
+ * (row, column) pairs that read img[n, channel0 + c, p], in a fixed order.
+ * Writes this group's channels of dimg only. */
+int kf_conv_fold(const void* dpatches, const kf_conv_geom* geom, void* dimg, int dtype, void* stream);
+/* kf_fwd / kf_features / kf_dgrad / kf_wgrad with x the implicit patch matrix
+ * of img (bf16): the kernels gather each receptive field from the image; no
+ * patch matrix is made.  kf_conv_dgrad writes the patch-matrix gradient
+ * dpatches (rows, cols), which kf_conv_fold turns into the image gradient. */
+int kf_conv_fwd(const void* img, const kf_conv_geom* geom, const void* feat, const void* packed, const void* bias,
+                const float* knot_tab, void* y, int32_t O, int32_t nt, int32_t f_pad, int32_t has_base,
+                const kf_basis_desc* basis, void* stream);
+int kf_conv_features(const void* img, const kf_conv_geom* geom, const float* knot_tab, void* feat, int32_t nt, int32_t f_pad,
+                     int32_t has_base, const kf_basis_desc* basis, void* stream);
+int kf_conv_dgrad(const void* img, const kf_conv_geom* geom, const void* dy, const void* packed, const float* knot_tab,
+                  void* dpatches, int32_t O, int32_t nt, int32_t f_pad, int32_t has_base, const kf_basis_desc* basis,
+                  void* stream);
+int kf_conv_wgrad(const void* img, const kf_conv_geom* geom, const void* feat, const void* dy, const float* knot_tab,
+                  const float* fold, const void* coef, const void* edge_scale, const void* edge_mask, void* dcoef, void* dbase,
+                  void* dscale, int32_t O, int32_t K, int32_t nt, int32_t f_pad, const kf_basis_desc* basis, void* stream);
+
 /* kf_rational_bwd for callers that cannot allocate device memory.  Some hosts
  * of this library may not call cudaMalloc: code that runs inside a device
  * memory allocator or pool callback (allocating there would re-enter the

@@ -37,8 +37,42 @@ class BasisDesc(ctypes.Structure):
     ]
 
 
+class ConvGeom(ctypes.Structure):
+    """``kf_conv_geom`` (include/kanforge_b200.h): the implicit patch matrix of a KAN convolution."""
+
+    _fields_ = [
+        ("batch", _c_i32),
+        ("channels", _c_i32),
+        ("group_channels", _c_i32),
+        ("channel0", _c_i32),
+        ("size", _c_i32 * 3),
+        ("kernel", _c_i32 * 3),
+        ("stride", _c_i32 * 3),
+        ("padding", _c_i32 * 3),
+        ("dilation", _c_i32 * 3),
+    ]
+
+
+_GEOM = ctypes.POINTER(ConvGeom)
+
 # name -> (restype, argtypes)
 PROTOTYPES = {
+    "kf_conv_patches": (ctypes.c_int, [_vp, _GEOM, _vp, ctypes.c_int, _vp]),
+    "kf_conv_fold": (ctypes.c_int, [_vp, _GEOM, _vp, ctypes.c_int, _vp]),
+    "kf_conv_fwd": (
+        ctypes.c_int,
+        [_vp, _GEOM, _vp, _vp, _vp, _vp, _vp, _c_i32, _c_i32, _c_i32, _c_i32, ctypes.POINTER(BasisDesc), _vp],
+    ),
+    "kf_conv_features": (ctypes.c_int, [_vp, _GEOM, _vp, _vp, _c_i32, _c_i32, _c_i32, ctypes.POINTER(BasisDesc), _vp]),
+    "kf_conv_dgrad": (
+        ctypes.c_int,
+        [_vp, _GEOM, _vp, _vp, _vp, _vp, _c_i32, _c_i32, _c_i32, _c_i32, ctypes.POINTER(BasisDesc), _vp],
+    ),
+    "kf_conv_wgrad": (
+        ctypes.c_int,
+        [_vp, _GEOM, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_i32, _c_i32, _c_i32, _c_i32,
+         ctypes.POINTER(BasisDesc), _vp],
+    ),
     "kf_version": (ctypes.c_int, []),
     "kf_last_error": (ctypes.c_char_p, []),
     "kf_query": (ctypes.c_int, [ctypes.POINTER(BasisDesc), ctypes.c_int, ctypes.c_int]),

@@ -29,6 +29,7 @@
 // Tiles: pair M = 256 rows, N = 256 columns per accumulator (the forward uses
 // two: 512 outputs), K steps of 64 bf16 (128 B), 4 stages.
 #include "basis.cuh"
+#include "conv.cuh"
 #include "umma.cuh"
 
 namespace kf {
@@ -220,6 +221,7 @@ struct FwdParams {
   int nblk;  // 256-output accumulator blocks per tile: kFwdNB, or 1 when O <= 256
   TileMap tiles;
   BasisDev bd;
+  ConvDev conv;  // active: x is an image read through the implicit patch matrix
 };
 
 constexpr int kFwdThreads = 768;  // w0 TMA, w1 MMA (CTA 0), w4-7 epilogue, w8-23 producers (4 groups)
@@ -449,7 +451,9 @@ __global__ void __launch_bounds__(A_TMA ? kFwdTmaThreads : kFwdThreads, 1)
       int k = ((grp - it) % kFwdGroups + kFwdGroups) % kFwdGroups;
       unsigned short xa[IPK], xb[IPK];
 #pragma unroll
-      for (int u = 0; u < IPK; ++u) xa[u] = (row_ok && k < p.k_steps && k * IPK + u < p.I) ? __ldg(xrow + k * IPK + u) : 0;
+      for (int u = 0; u < IPK; ++u)
+        xa[u] = (row_ok && k < p.k_steps && k * IPK + u < p.I)
+                    ? (p.conv.active ? x_bits(p.x, p.conv, b, k * IPK + u, p.I) : __ldg(xrow + k * IPK + u)) : 0;
       for (; k < p.k_steps; k += kFwdGroups) {
         const int git = it + k;
         const int s = git % NS;
@@ -457,7 +461,9 @@ __global__ void __launch_bounds__(A_TMA ? kFwdTmaThreads : kFwdThreads, 1)
         const int i0 = k * IPK;
         const int inext = i0 + kFwdGroups * IPK;
 #pragma unroll
-        for (int u = 0; u < IPK; ++u) xb[u] = (row_ok && k + kFwdGroups < p.k_steps && inext + u < p.I) ? __ldg(xrow + inext + u) : 0;
+        for (int u = 0; u < IPK; ++u)
+          xb[u] = (row_ok && k + kFwdGroups < p.k_steps && inext + u < p.I)
+                      ? (p.conv.active ? x_bits(p.x, p.conv, b, inext + u, p.I) : __ldg(xrow + inext + u)) : 0;
         bool ok = mbar_wait_warp(&ctl->empty[s], ph ^ 1, abort);
         if constexpr (BK > 0) ok = ok && mbar_wait_warp(&ctl->tab_full[s], ph, abort);  // tables landed
         if (!ok) {
@@ -559,6 +565,7 @@ struct DgradParams {
   int ipg;
   float* rws;  // parameter-gradient partial sums [10][I / 32][n_rq]
   int n_rq;    // 32-row blocks: 8 per pair tile of 256 rows (those past B hold zeros)
+  ConvDev conv;  // active: x is an image read through the implicit patch matrix (dx is still (B, I))
 };
 
 // Template value of BK that selects the GR-KAN epilogue of the input-gradient
@@ -819,7 +826,10 @@ __global__ void __launch_bounds__(dgrad_threads(BK), 1) fused_dgrad_kernel(const
         // this row's x for this set's inputs, loaded once (4-byte loads when aligned)
         const int u0 = h2 * kHalfIn;
         float* xr = xsm + row * (IPT + 1);
-        if (row_ok && i_base + u0 + kHalfIn <= p.I && ((p.I | i_base) % 2) == 0) {
+        if (p.conv.active) {
+          for (int u = u0; u < u0 + kHalfIn; ++u)
+            xr[u] = (row_ok && i_base + u < p.I) ? x_value(p.x, p.conv, b, i_base + u, p.I) : 0.0f;
+        } else if (row_ok && i_base + u0 + kHalfIn <= p.I && ((p.I | i_base) % 2) == 0) {
           const uint32_t* src = reinterpret_cast<const uint32_t*>(p.x + b * p.I + i_base + u0);
   #pragma unroll
           for (int k2 = 0; k2 < kHalfIn / 2; ++k2) {
@@ -959,7 +969,11 @@ __global__ void __launch_bounds__(dgrad_threads(BK), 1) fused_dgrad_kernel(const
         const bool pairs_ok = row_ok && i_base + u0 + kSetIn <= p.I && ((p.I | i_base) % 2) == 0;
         // this row's x for the set's inputs (4-byte loads when aligned)
         float xv[kSetIn];
-        if (pairs_ok) {
+        if (p.conv.active) {
+#pragma unroll
+          for (int u = 0; u < kSetIn; ++u)
+            xv[u] = (row_ok && i_base + u0 + u < p.I) ? x_value(p.x, p.conv, b, i_base + u0 + u, p.I) : 0.0f;
+        } else if (pairs_ok) {
           const uint32_t* src = reinterpret_cast<const uint32_t*>(p.x + b * p.I + i_base + u0);
 #pragma unroll
           for (int k2 = 0; k2 < kSetIn / 2; ++k2) {
@@ -1078,6 +1092,7 @@ struct WgradParams {
   // float32 partial (O, I K) block s of `part`; 1 = no split
   int n_split, ks;
   float* part;
+  ConvDev conv;  // active: x is an image read through the implicit patch matrix
 };
 
 constexpr int kWgradThreads = 768;     // w0 TMA, w1 MMA (CTA 0), w4-7 epilogue, w8-23 producers (2 groups)
@@ -1379,7 +1394,7 @@ __global__ void __launch_bounds__(A_TMA ? kWgradTmaThreads : kWgradThreads, 1)
 #pragma unroll
           for (int r = 0; r < NB; ++r) {
             const int64_t b = (int64_t)k * kBK + bsub + r;
-            if (b < p.B && i < p.I) xv[r] = __bfloat162float(p.x[b * p.I + i]);
+            if (b < p.B && i < p.I) xv[r] = x_value(p.x, p.conv, b, i, p.I);
           }
         }
         bool ok = mbar_wait_warp(&ctl->empty[s], ph ^ 1, abort);
@@ -1477,14 +1492,14 @@ __global__ void __launch_bounds__(A_TMA ? kWgradTmaThreads : kWgradThreads, 1)
 // evaluate its (cheap) row and keep their own chunk.
 template <int F>
 __global__ void __launch_bounds__(256) feature_cheb_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ feat,
-                                                           int64_t n, BasisDev bd) {
+                                                           int64_t n, int I, BasisDev bd, ConvDev conv) {
   constexpr int CH = F / 8;
   const int64_t n_chunks = n * CH;
   for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < n_chunks; c += (int64_t)gridDim.x * blockDim.x) {
     const int64_t e = c / CH;
     const int q = (int)(c % CH);
     float f[F];
-    cheb_row<F>(__bfloat162float(x[e]), bd, f);
+    cheb_row<F>(conv.active ? x_value(x, conv, e / I, (int)(e % I), I) : __bfloat162float(x[e]), bd, f);
     float g[8];
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
@@ -1520,7 +1535,7 @@ __device__ __forceinline__ uint32_t bf16_bits(float v) { return (uint32_t)__bflo
 template <int BK, int F>
 __global__ void __launch_bounds__(256) feature_spline_kernel(const __nv_bfloat16* __restrict__ x,
                                                              __nv_bfloat16* __restrict__ feat, int64_t B, int I, BasisDev bd,
-                                                             int ts) {
+                                                             int ts, ConvDev conv) {
   constexpr int NW = (BK + 3) / 2;  // words that BK + 1 consecutive bf16 values can touch
   extern __shared__ float tabs[];   // [(BK + 1) * ts][32]
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -1542,7 +1557,7 @@ __global__ void __launch_bounds__(256) feature_spline_kernel(const __nv_bfloat16
 #pragma unroll
     for (int u = 0; u < kSplineRows; ++u) {
       const int64_t b = b0 + u * stride;
-      xs[u] = b < B ? __bfloat162float(x[b * I + i]) : 0.0f;
+      xs[u] = b < B ? x_value(x, conv, b, i, I) : 0.0f;
     }
     int pos[kSplineRows];
 #pragma unroll
@@ -1902,12 +1917,13 @@ struct FeatureLaunch {
   int I;
   BasisDev bd;
   cudaStream_t stream;
+  ConvDev conv;
   template <int BK, int F>
   int go() const {
     if constexpr (BK == 0) {
       const int64_t n = B * (int64_t)I;
       const unsigned grid = (unsigned)std::min<int64_t>(cdiv(n * (F / 8), 256), (int64_t)sm_count() * 16);
-      feature_cheb_kernel<F><<<grid, 256, 0, stream>>>(x, feat, n, bd);
+      feature_cheb_kernel<F><<<grid, 256, 0, stream>>>(x, feat, n, I, bd, conv);
     } else {
       const unsigned gy = (unsigned)cdiv(I, 32);
       const int64_t want = std::max<int64_t>(1, (int64_t)sm_count() * 8 / gy);
@@ -1915,7 +1931,7 @@ struct FeatureLaunch {
       const int ts = (bd.nk + 15) & ~15;  // table row stride in shared memory (>= nk)
       const size_t smem = sizeof(float) * 32 * (BK + 1) * ts;
       KF_CUDA_RET(cudaFuncSetAttribute(feature_spline_kernel<BK, F>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-      feature_spline_kernel<BK, F><<<dim3(gx, gy), 256, smem, stream>>>(x, feat, B, I, bd, ts);
+      feature_spline_kernel<BK, F><<<dim3(gx, gy), 256, smem, stream>>>(x, feat, B, I, bd, ts, conv);
     }
     return check_launch("kf_features");
   }
@@ -1989,7 +2005,7 @@ int grkan_check(const kf_basis_desc* d, int64_t B, int I, int O, const char* who
 
 }  // namespace kf
 
-extern "C" int kf_fwd(const void* x, const void* feat, const void* packed, const void* bias, const float* knot_tab, void* y, int64_t B,
+static int kf_fwd_impl(const kf::ConvDev* conv, const void* x, const void* feat, const void* packed, const void* bias, const float* knot_tab, void* y, int64_t B,
                       int32_t I, int32_t O, int32_t nt, int32_t f_pad, int32_t has_base, const kf_basis_desc* basis,
                       void* stream) {
   using namespace kf;
@@ -2025,11 +2041,12 @@ extern "C" int kf_fwd(const void* x, const void* feat, const void* packed, const
   } else {
     tmap_a = tmap;  // unused
   }
+  if (conv) p.conv = *conv;
   FwdLaunch L{&tmap, &tmap_a, p, feat != nullptr, (cudaStream_t)stream};
   return dispatch_fused(basis, f_pad, L);
 }
 
-extern "C" int kf_dgrad(const void* x, const void* dy, const void* packed, const float* knot_tab, void* dx, int64_t B,
+static int kf_dgrad_impl(const kf::ConvDev* conv, const void* x, const void* dy, const void* packed, const float* knot_tab, void* dx, int64_t B,
                         int32_t I, int32_t O, int32_t nt, int32_t f_pad, int32_t has_base, const kf_basis_desc* basis,
                         void* stream) {
   using namespace kf;
@@ -2054,6 +2071,7 @@ extern "C" int kf_dgrad(const void* x, const void* dy, const void* packed, const
   CUtensorMap tdy, tc;
   if (int rc = make_tmap_bf16(&tdy, dy, B, O, kBK, kBM)) return rc;
   if (int rc = make_tmap_bf16(&tc, packed, O, (int64_t)I * f_pad, 64, kBK)) return rc;
+  if (conv) p.conv = *conv;
   DgradLaunch L{&tdy, &tc, p, (cudaStream_t)stream};
   return dispatch_fused(basis, f_pad, L);
 }
@@ -2074,7 +2092,7 @@ extern "C" int kf_features_spline_f32(const float* x, const float* knot_tab, flo
   return dispatch_fused(basis, f_pad, L);
 }
 
-extern "C" int kf_features(const void* x, const float* knot_tab, void* feat, int64_t B, int32_t I, int32_t nt,
+static int kf_features_impl(const kf::ConvDev* conv, const void* x, const float* knot_tab, void* feat, int64_t B, int32_t I, int32_t nt,
                            int32_t f_pad, int32_t has_base, const kf_basis_desc* basis, void* stream) {
   using namespace kf;
   clear_error();
@@ -2086,10 +2104,11 @@ extern "C" int kf_features(const void* x, const float* knot_tab, void* feat, int
   if (int rc = fill_basis(basis, knot_tab, nt, has_base, f_pad, bd)) return rc;
   if (B == 0) return KF_OK;
   FeatureLaunch L{(const __nv_bfloat16*)x, (__nv_bfloat16*)feat, B, I, bd, (cudaStream_t)stream};
+  if (conv) L.conv = *conv;
   return dispatch_fused(basis, f_pad, L);
 }
 
-extern "C" int kf_wgrad(const void* x, const void* feat, const void* dy, const float* knot_tab, const float* fold, const void* coef,
+static int kf_wgrad_impl(const kf::ConvDev* conv, const void* x, const void* feat, const void* dy, const float* knot_tab, const float* fold, const void* coef,
                         const void* edge_scale, const void* edge_mask, void* dcoef, void* dbase, void* dscale, int64_t B,
                         int32_t I, int32_t O, int32_t K, int32_t nt, int32_t f_pad, const kf_basis_desc* basis,
                         void* stream) {
@@ -2136,7 +2155,8 @@ extern "C" int kf_wgrad(const void* x, const void* feat, const void* dy, const f
   p.tiles.gm = feat ? std::min(p.tiles.m_tiles, 8) : p.tiles.m_tiles;
   CUtensorMap tdy, tx;
   if (int rc = make_tmap_bf16(&tdy, dy, B, O, 64, kBK)) return rc;
-  p.x_tma = (I % 8 == 0) && ((uintptr_t)x % 16 == 0);
+  if (conv) p.conv = *conv;
+  p.x_tma = !conv && (I % 8 == 0) && ((uintptr_t)x % 16 == 0);  // an image is gathered, not tiled
   p.tab_stride = basis->kind == KF_BASIS_BSPLINE ? ((p.bd.nk + 15) & ~15) : 16;
   if (feat) {
     KF_CHECK_ARG(((uintptr_t)feat % 16) == 0, "kf_wgrad: feat must be 16-byte aligned");
@@ -2342,4 +2362,209 @@ extern "C" int kf_grkan_wgrad(const void* r, const void* dy, void* dw, float* wo
     return check_launch("kf_grkan_wgrad");
   }
   return KF_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Entry points of the plain (rows, I) layer and of the KAN convolution, whose
+// x operand is an image read through the implicit patch matrix (conv.cuh).
+// ---------------------------------------------------------------------------
+
+extern "C" int kf_fwd(const void* x, const void* feat, const void* packed, const void* bias, const float* knot_tab, void* y,
+                      int64_t B, int32_t I, int32_t O, int32_t nt, int32_t f_pad, int32_t has_base, const kf_basis_desc* basis,
+                      void* stream) {
+  return kf_fwd_impl(nullptr, x, feat, packed, bias, knot_tab, y, B, I, O, nt, f_pad, has_base, basis, stream);
+}
+
+extern "C" int kf_dgrad(const void* x, const void* dy, const void* packed, const float* knot_tab, void* dx, int64_t B,
+                        int32_t I, int32_t O, int32_t nt, int32_t f_pad, int32_t has_base, const kf_basis_desc* basis,
+                        void* stream) {
+  return kf_dgrad_impl(nullptr, x, dy, packed, knot_tab, dx, B, I, O, nt, f_pad, has_base, basis, stream);
+}
+
+extern "C" int kf_features(const void* x, const float* knot_tab, void* feat, int64_t B, int32_t I, int32_t nt,
+                           int32_t f_pad, int32_t has_base, const kf_basis_desc* basis, void* stream) {
+  return kf_features_impl(nullptr, x, knot_tab, feat, B, I, nt, f_pad, has_base, basis, stream);
+}
+
+extern "C" int kf_wgrad(const void* x, const void* feat, const void* dy, const float* knot_tab, const float* fold,
+                        const void* coef, const void* edge_scale, const void* edge_mask, void* dcoef, void* dbase,
+                        void* dscale, int64_t B, int32_t I, int32_t O, int32_t K, int32_t nt, int32_t f_pad,
+                        const kf_basis_desc* basis, void* stream) {
+  return kf_wgrad_impl(nullptr, x, feat, dy, knot_tab, fold, coef, edge_scale, edge_mask, dcoef, dbase, dscale, B, I, O, K,
+                       nt, f_pad, basis, stream);
+}
+
+namespace kf {
+namespace {
+
+// The implicit patch matrix of `g`: its device description, rows and columns.
+int conv_geometry(const kf_conv_geom* g, ConvDev& d, int64_t& rows, int& cols, const char* who) {
+  KF_CHECK_ARG(g != nullptr, "%s: null geometry", who);
+  KF_CHECK_ARG(g->batch >= 0 && g->channels >= 1 && g->group_channels >= 1 && g->channel0 >= 0 &&
+                   g->channel0 + g->group_channels <= g->channels,
+               "%s: bad channel layout", who);
+  d = ConvDev{};
+  d.active = 1;
+  d.c0 = g->channel0;
+  int64_t per_image = g->channels, out_n = 1, ksz = 1;
+  for (int k = 0; k < 3; ++k) {
+    KF_CHECK_ARG(g->size[k] >= 1 && g->kernel[k] >= 1 && g->stride[k] >= 1 && g->dilation[k] >= 1 && g->padding[k] >= 0,
+                 "%s: bad size / kernel / stride / dilation / padding in dimension %d", who, k);
+    const int span = g->dilation[k] * (g->kernel[k] - 1) + 1;
+    const int padded = g->size[k] + 2 * g->padding[k];
+    KF_CHECK_ARG(padded >= span, "%s: kernel larger than the padded input in dimension %d", who, k);
+    d.size[k] = g->size[k];
+    d.kernel[k] = g->kernel[k];
+    d.stride[k] = g->stride[k];
+    d.pad[k] = g->padding[k];
+    d.dil[k] = g->dilation[k];
+    d.out[k] = (padded - span) / g->stride[k] + 1;
+    per_image *= g->size[k];
+    out_n *= d.out[k];
+    ksz *= g->kernel[k];
+  }
+  d.img_n_stride = per_image;
+  rows = (int64_t)g->batch * out_n;
+  KF_CHECK_ARG((int64_t)g->group_channels * ksz < (1 << 30), "%s: too many patch columns", who);
+  cols = (int)(g->group_channels * ksz);
+  return KF_OK;
+}
+
+// out[r, c] = the implicit patch matrix, row-major (rows, cols).
+template <typename T>
+__global__ void __launch_bounds__(256) conv_patches_kernel(const T* __restrict__ img, T* __restrict__ out, int64_t n, int cols,
+                                                           ConvDev g) {
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t src = conv_index(g, e / cols, (int)(e % cols));
+    out[e] = src >= 0 ? img[src] : from_f32<T>(0.0f);
+  }
+}
+
+// dimg[n, c0 + c, p] = sum over the kernel offsets k of dpatches[(n, o), (c, k)]
+// with o_d = (p_d + pad_d - k_d dil_d) / stride_d exact and inside the output:
+// the transpose of the patch gather, one thread per image element of the
+// group, offsets in a fixed order (deterministic).
+template <typename T>
+__global__ void __launch_bounds__(256) conv_fold_kernel(const T* __restrict__ dp, T* __restrict__ dimg, int64_t n_elem, int cg,
+                                                        int cols, ConvDev g) {
+  const int64_t plane = (int64_t)g.size[0] * g.size[1] * g.size[2];
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n_elem; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t pix = e % plane;
+    const int64_t nc = e / plane;
+    const int c = (int)(nc % cg);
+    const int64_t n = nc / cg;
+    const int p2 = (int)(pix % g.size[2]);
+    const int p1 = (int)((pix / g.size[2]) % g.size[1]);
+    const int p0 = (int)(pix / ((int64_t)g.size[2] * g.size[1]));
+    float acc = 0.0f;
+    for (int k0 = 0; k0 < g.kernel[0]; ++k0) {
+      const int a0 = p0 + g.pad[0] - k0 * g.dil[0];
+      if (a0 < 0 || a0 % g.stride[0] || a0 / g.stride[0] >= g.out[0]) continue;
+      for (int k1 = 0; k1 < g.kernel[1]; ++k1) {
+        const int a1 = p1 + g.pad[1] - k1 * g.dil[1];
+        if (a1 < 0 || a1 % g.stride[1] || a1 / g.stride[1] >= g.out[1]) continue;
+        for (int k2 = 0; k2 < g.kernel[2]; ++k2) {
+          const int a2 = p2 + g.pad[2] - k2 * g.dil[2];
+          if (a2 < 0 || a2 % g.stride[2] || a2 / g.stride[2] >= g.out[2]) continue;
+          const int64_t row = ((n * g.out[0] + a0 / g.stride[0]) * g.out[1] + a1 / g.stride[1]) * g.out[2] + a2 / g.stride[2];
+          const int col = ((c * g.kernel[0] + k0) * g.kernel[1] + k1) * g.kernel[2] + k2;
+          acc += to_f32(dp[row * cols + col]);
+        }
+      }
+    }
+    dimg[(n * g.img_n_stride / plane + g.c0 + c) * plane + pix] = from_f32<T>(acc);
+  }
+}
+
+unsigned elementwise_grid(int64_t n) { return (unsigned)std::max<int64_t>(1, std::min<int64_t>(cdiv(n, 256), (int64_t)sm_count() * 16)); }
+
+}  // namespace
+}  // namespace kf
+
+extern "C" int kf_conv_patches(const void* img, const kf_conv_geom* geom, void* patches, int dtype, void* stream) {
+  using namespace kf;
+  clear_error();
+  KF_CHECK_ARG(img && patches, "kf_conv_patches: null tensor pointer");
+  KF_CHECK_ARG(dtype == KF_DTYPE_F32 || dtype == KF_DTYPE_BF16, "kf_conv_patches: dtype %d", dtype);
+  ConvDev g;
+  int64_t rows;
+  int cols;
+  if (int rc = conv_geometry(geom, g, rows, cols, "kf_conv_patches")) return rc;
+  if (int rc = bind_device(img)) return rc;
+  const int64_t n = rows * cols;
+  if (n == 0) return KF_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (dtype == KF_DTYPE_F32)
+    conv_patches_kernel<float><<<elementwise_grid(n), 256, 0, s>>>((const float*)img, (float*)patches, n, cols, g);
+  else
+    conv_patches_kernel<__nv_bfloat16><<<elementwise_grid(n), 256, 0, s>>>((const __nv_bfloat16*)img, (__nv_bfloat16*)patches,
+                                                                          n, cols, g);
+  return check_launch("kf_conv_patches");
+}
+
+extern "C" int kf_conv_fold(const void* dpatches, const kf_conv_geom* geom, void* dimg, int dtype, void* stream) {
+  using namespace kf;
+  clear_error();
+  KF_CHECK_ARG(dpatches && dimg, "kf_conv_fold: null tensor pointer");
+  KF_CHECK_ARG(dtype == KF_DTYPE_F32 || dtype == KF_DTYPE_BF16, "kf_conv_fold: dtype %d", dtype);
+  ConvDev g;
+  int64_t rows;
+  int cols;
+  if (int rc = conv_geometry(geom, g, rows, cols, "kf_conv_fold")) return rc;
+  if (int rc = bind_device(dimg)) return rc;
+  const int64_t n = (int64_t)geom->batch * geom->group_channels * g.size[0] * g.size[1] * g.size[2];
+  if (n == 0) return KF_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (dtype == KF_DTYPE_F32)
+    conv_fold_kernel<float><<<elementwise_grid(n), 256, 0, s>>>((const float*)dpatches, (float*)dimg, n, geom->group_channels,
+                                                               cols, g);
+  else
+    conv_fold_kernel<__nv_bfloat16><<<elementwise_grid(n), 256, 0, s>>>((const __nv_bfloat16*)dpatches, (__nv_bfloat16*)dimg, n,
+                                                                       geom->group_channels, cols, g);
+  return check_launch("kf_conv_fold");
+}
+
+extern "C" int kf_conv_fwd(const void* img, const kf_conv_geom* geom, const void* feat, const void* packed, const void* bias,
+                           const float* knot_tab, void* y, int32_t O, int32_t nt, int32_t f_pad, int32_t has_base,
+                           const kf_basis_desc* basis, void* stream) {
+  kf::ConvDev g;
+  int64_t rows;
+  int cols;
+  kf::clear_error();
+  if (int rc = kf::conv_geometry(geom, g, rows, cols, "kf_conv_fwd")) return rc;
+  return kf_fwd_impl(&g, img, feat, packed, bias, knot_tab, y, rows, cols, O, nt, f_pad, has_base, basis, stream);
+}
+
+extern "C" int kf_conv_features(const void* img, const kf_conv_geom* geom, const float* knot_tab, void* feat, int32_t nt,
+                                int32_t f_pad, int32_t has_base, const kf_basis_desc* basis, void* stream) {
+  kf::ConvDev g;
+  int64_t rows;
+  int cols;
+  kf::clear_error();
+  if (int rc = kf::conv_geometry(geom, g, rows, cols, "kf_conv_features")) return rc;
+  return kf_features_impl(&g, img, knot_tab, feat, rows, cols, nt, f_pad, has_base, basis, stream);
+}
+
+extern "C" int kf_conv_dgrad(const void* img, const kf_conv_geom* geom, const void* dy, const void* packed,
+                             const float* knot_tab, void* dpatches, int32_t O, int32_t nt, int32_t f_pad, int32_t has_base,
+                             const kf_basis_desc* basis, void* stream) {
+  kf::ConvDev g;
+  int64_t rows;
+  int cols;
+  kf::clear_error();
+  if (int rc = kf::conv_geometry(geom, g, rows, cols, "kf_conv_dgrad")) return rc;
+  return kf_dgrad_impl(&g, img, dy, packed, knot_tab, dpatches, rows, cols, O, nt, f_pad, has_base, basis, stream);
+}
+
+extern "C" int kf_conv_wgrad(const void* img, const kf_conv_geom* geom, const void* feat, const void* dy, const float* knot_tab,
+                             const float* fold, const void* coef, const void* edge_scale, const void* edge_mask, void* dcoef,
+                             void* dbase, void* dscale, int32_t O, int32_t K, int32_t nt, int32_t f_pad,
+                             const kf_basis_desc* basis, void* stream) {
+  kf::ConvDev g;
+  int64_t rows;
+  int cols;
+  kf::clear_error();
+  if (int rc = kf::conv_geometry(geom, g, rows, cols, "kf_conv_wgrad")) return rc;
+  return kf_wgrad_impl(&g, img, feat, dy, knot_tab, fold, coef, edge_scale, edge_mask, dcoef, dbase, dscale, rows, cols, O, K,
+                       nt, f_pad, basis, stream);
 }

@@ -273,6 +273,11 @@ def pack_coef(coef, base, edge_scale, edge_mask, plan: KernelPlan, f_pad: int) -
 # output tile); Chebyshev-feature plans make it in the backward.
 WGRAD_FEATURE_BYTES_MAX = 16 << 30
 
+# Plan kinds whose bf16 forward makes the feature matrix and reads it by TMA
+# (kept for the coefficient gradient) instead of evaluating the features in
+# the forward kernel's producer warps.
+FEATURES_IN_FORWARD = ("bspline",)
+
 
 def wgrad_features(x, knot_tab, nt, f_pad, has_base, desc, stream):
     """The feature matrix of x for kf_wgrad, or None for its self-evaluating path."""
@@ -310,7 +315,7 @@ class _FusedKANLinear(torch.autograd.Function):
         g = None if grid is None else grid.detach().float().contiguous()
         tab = None if grid is None else knot_tables(g, plan)
         desc = plan.desc()
-        feat = wgrad_features(x, tab, nt, f_pad, has_base, desc, _stream(x)) if plan.kind == "bspline" else None
+        feat = wgrad_features(x, tab, nt, f_pad, has_base, desc, _stream(x)) if plan.kind in FEATURES_IN_FORWARD else None
         _launch("kf_fwd", _ptr(x), _ptr(feat), _ptr(packed), _ptr(b), _ptr(tab), _ptr(y), x.shape[0], n_in, n_out, nt,
                 f_pad, int(has_base), ctypes.byref(desc), _stream(x))
         ctx.save_for_backward(x, coef, base_weight, edge_scale, edge_mask, g)

@@ -206,32 +206,41 @@ class KANLinear(nn.Module):
     def _grid(self):
         return getattr(self, "basis_grid", None) if self._plan is not None and self._plan.grid else None
 
-    def _check_supported(self) -> None:
+    def _check_supported(self, derivatives: bool = False) -> None:
         if self._plan is None:
             raise RuntimeError(f"no fused kernel for this basis: {self.basis!r}")
         if self._sym_codes:
             raise NotImplementedError("symbolic edges are not part of the kanforge_b200 kernel path")
-        if self.base_weight is not None and self.base_activation is not F.silu:
-            raise NotImplementedError("the fused base branch is SiLU; other base activations are not supported")
+        if derivatives and self.base_weight is not None and self.base_activation is not F.silu:
+            raise NotImplementedError("edge derivatives take the SiLU base branch; other base activations are not supported")
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         _require_cuda(x)
         self._check_supported()
         if self.training and self.edge_dropout > 0:
             raise NotImplementedError("edge_dropout (DropKAN) is not part of the kanforge_b200 kernel path")
+        if self.base_weight is None or self.base_activation is F.silu:
+            return self._edges(x, self.base_weight)
+        # another base activation: the kernels compute the basis part, the base
+        # branch act(x) (W * mask)^T is added as a plain linear map
+        y = self._edges(x, None)
+        return y + F.linear(self.base_activation(x), self.effective_base_weight()).to(y.dtype)
+
+    def _edges(self, x: torch.Tensor, silu_weight: torch.Tensor | None) -> torch.Tensor:
+        """sum_i phi_oi(x_i) + bias, plus the SiLU base branch of ``silu_weight``."""
         plan = self._plan
-        if plan.kind != "rational" and _kernels.fused_ok(plan, x, self.out_features, self.base_weight is not None,
-                                                          self.coef.dtype):
+        has_base = silu_weight is not None
+        if plan.kind != "rational" and _kernels.fused_ok(plan, x, self.out_features, has_base, self.coef.dtype):
             # coef * edge_scale * edge_mask and base_weight * edge_mask are formed inside the kernels
-            return _kernels.kan_linear_fused(x, self.coef, self.base_weight, self.bias, self.edge_scale, self.edge_mask,
+            return _kernels.kan_linear_fused(x, self.coef, silu_weight, self.bias, self.edge_scale, self.edge_mask,
                                              self._grid(), plan)
         if plan.kind != "rational" and _kernels.FP32_TENSOR_CORES and _kernels.tf32_ok(
-                plan, x, self.out_features, self.base_weight is not None, self.coef.dtype):
+                plan, x, self.out_features, has_base, self.coef.dtype):
             # float32: three TF32 products per contraction on the tensor cores
-            return _kernels.kan_linear_tf32(x, self.coef, self.base_weight, self.bias, self.edge_scale, self.edge_mask,
+            return _kernels.kan_linear_tf32(x, self.coef, silu_weight, self.bias, self.edge_scale, self.edge_mask,
                                             self._grid(), plan)
         coef_eff = self.effective_coef()
-        base_eff = self.effective_base_weight()
+        base_eff = None if silu_weight is None else silu_weight * self.edge_mask
         if plan.kind == "rational":
             lead = x.shape[:-1]
             x2 = x.reshape(-1, self.in_features)
@@ -266,7 +275,7 @@ class KANLinear(nn.Module):
         if order < 0:
             raise ValueError("order must be >= 0")
         _require_cuda(x)
-        self._check_supported()
+        self._check_supported(derivatives=True)
         plan = self._plan
         coef_eff = self.effective_coef()
         base_eff = self.effective_base_weight()
