@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define KF_ABI_VERSION 1
+#define KF_ABI_VERSION 2
 
 /* status codes */
 #define KF_OK 0
@@ -41,6 +41,12 @@ extern "C" {
 #define KF_BASIS_BSPLINE 1   /* native derivative order, per-input grid */
 #define KF_BASIS_CHEB 2      /* Chebyshev features T_j(g(x)), derivatives folded */
 #define KF_BASIS_RATIONAL 3  /* KAT P(x) / (1 + |Q(x)|), per-group parameters */
+#define KF_BASIS_FOURIER 4   /* cos(w_j x), sin(w_j x), w_j = 2 pi j / period; derivatives folded */
+#define KF_BASIS_BUMP 5      /* bumps on a per-input grid of centres (RBF, wavelets, RSWAF), native order */
+
+#define KF_BUMP_GAUSS 0      /* norm P_m(u) exp(-u^2/2) k^m, u = (x - c_j) k, k = u_scale (count-1) / (c_last - c_first) */
+#define KF_BUMP_TANH 1       /* P_m(t) / h^m, t = tanh((x - c_j) / h), h = (c_last - c_first) / (count - 1) */
+#define KF_BUMP_MAX_ORDER 5  /* derivative orders with a polynomial in the descriptor */
 
 #define KF_MAP_TANH 0
 #define KF_MAP_IDENTITY 1
@@ -62,6 +68,11 @@ typedef struct kf_basis_desc {
   int32_t den_degree; /* rational: denominator degree */
   int32_t input_map;  /* Chebyshev: KF_MAP_* */
   int32_t groups;     /* rational: parameter groups (inputs per group = I / groups) */
+  float period;       /* Fourier: period (size = 2 frequencies) */
+  int32_t bump_mode;  /* bumps: KF_BUMP_*; size = count (grid (I, count) of centres) */
+  float u_scale;      /* bumps: scale of u (gauss) */
+  float norm;         /* bumps: constant factor (gauss) */
+  float bump_poly[KF_BUMP_MAX_ORDER + 1][8]; /* bumps: P_m, coefficients lowest first, m = 0..5 */
 } kf_basis_desc;
 
 /* Library ABI version (KF_ABI_VERSION). */

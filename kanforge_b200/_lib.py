@@ -13,7 +13,9 @@ from pathlib import Path
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libkanb200.so"
 
 KF_OK = 0
-KF_BASIS_BSPLINE, KF_BASIS_CHEB, KF_BASIS_RATIONAL = 1, 2, 3
+KF_BASIS_BSPLINE, KF_BASIS_CHEB, KF_BASIS_RATIONAL, KF_BASIS_FOURIER, KF_BASIS_BUMP = 1, 2, 3, 4, 5
+KF_BUMP_GAUSS, KF_BUMP_TANH = 0, 1
+KF_BUMP_MAX_ORDER = 5
 KF_MAP_TANH, KF_MAP_IDENTITY = 0, 1
 KF_DTYPE_F32, KF_DTYPE_BF16 = 0, 1
 KF_OP_F, KF_OP_G, KF_OP_P = 0, 1, 2
@@ -34,6 +36,11 @@ class BasisDesc(ctypes.Structure):
         ("den_degree", _c_i32),
         ("input_map", _c_i32),
         ("groups", _c_i32),
+        ("period", ctypes.c_float),
+        ("bump_mode", _c_i32),
+        ("u_scale", ctypes.c_float),
+        ("norm", ctypes.c_float),
+        ("bump_poly", (ctypes.c_float * 8) * (KF_BUMP_MAX_ORDER + 1)),
     ]
 
 

@@ -529,6 +529,158 @@ class Rational(Basis):
         return (p / (1 + np.abs(q)))[..., None]
 
 
+# ---------------------------------------------------------------------------
+# periodic and bump bases (the reference's "fourier" and "bump" kernel plans)
+# ---------------------------------------------------------------------------
+
+
+class Fourier(Basis):
+    """cos(w_j x), then sin(w_j x), w_j = 2 pi j / period, j = 1..frequencies
+    (FourierKAN; the constant term is the layer bias), reference
+    kanforge/bases/fourier.py:13-52.  ``learnable_frequency`` adds a trainable
+    per-group frequency scale (no kernel plan then)."""
+
+    name = "fourier"
+
+    def __init__(self, frequencies: int = 5, period: float = 2 * math.pi, learnable_frequency: bool = False):
+        if frequencies < 1 or not period > 0:
+            raise ValueError("frequencies must be >= 1 and period > 0")
+        self.frequencies = int(frequencies)
+        self.period = float(period)
+        self.learnable_frequency = bool(learnable_frequency)
+
+    @property
+    def size(self) -> int:
+        return 2 * self.frequencies
+
+    def param_specs(self):
+        return {"frequency_scale": ParamSpec(np.ones(1))} if self.learnable_frequency else {}
+
+    def config(self):
+        return {"name": self.name, "frequencies": self.frequencies, "period": self.period,
+                "learnable_frequency": self.learnable_frequency}
+
+    def host_eval(self, x, params=None):
+        w = (2.0 * math.pi / self.period) * np.arange(1, self.frequencies + 1)
+        arg = np.asarray(x, dtype=np.float64)[..., None] * w
+        return np.concatenate([np.cos(arg), np.sin(arg)], axis=-1)
+
+
+def gaussian_bump_polys(p, max_order: int) -> list[np.ndarray]:
+    """P_0 .. P_max_order with d^m/du^m [p(u) exp(-u^2/2)] = P_m(u) exp(-u^2/2):
+    P_{m+1} = P_m' - u P_m."""
+    out = [np.asarray(p, dtype=np.float64)]
+    for _ in range(max_order):
+        q = out[-1]
+        out.append(np.polynomial.polynomial.polysub(np.polynomial.polynomial.polyder(q),
+                                                    np.polynomial.polynomial.polymulx(q)))
+    return out
+
+
+def tanh_bump_polys(max_order: int) -> list[np.ndarray]:
+    """P_0 .. P_max_order in t = tanh(v) with d^m/dv^m (1 - tanh(v)^2) = P_m(t):
+    P_0 = 1 - t^2, P_{m+1} = P_m'(t) (1 - t^2)."""
+    sech2 = np.array([1.0, 0.0, -1.0])
+    out = [sech2]
+    for _ in range(max_order):
+        out.append(np.polynomial.polynomial.polymul(np.polynomial.polynomial.polyder(out[-1]), sech2))
+    return out
+
+
+class _Bump(Basis):
+    """psi(u_scale (x - c_j) / h) on ``count`` centres spread over ``grid_range``,
+    h = the centre spacing, psi(u) = norm p(u) exp(-u^2/2) (reference
+    kanforge/bases/radial.py:35-74).  Fixed centres are a per-input grid
+    buffer; ``learnable`` centres and width are trainable (no kernel plan)."""
+
+    p: tuple = (1.0,)
+    norm = 1.0
+    u_scale = 1.0
+
+    def __init__(self, count: int = 8, grid_range: tuple[float, float] = (-1.0, 1.0), learnable: bool = False):
+        if count < 2:
+            raise ValueError("count must be >= 2")
+        self.count = int(count)
+        self.grid_range = _check_range(grid_range)
+        self.learnable = bool(learnable)
+
+    @property
+    def size(self) -> int:
+        return self.count
+
+    def param_specs(self):
+        lo, hi = self.grid_range
+        centres = np.linspace(lo, hi, self.count)
+        if not self.learnable:
+            return {"grid": ParamSpec(centres, trainable=False)}
+        return {"centers": ParamSpec(centres), "log_scale": ParamSpec(np.array([math.log((hi - lo) / (self.count - 1))]))}
+
+    def config(self) -> dict[str, Any]:
+        return {"name": self.name, "count": self.count, "grid_range": self.grid_range, "learnable": self.learnable}
+
+    def host_eval(self, x, params=None):
+        c = np.linspace(*self.grid_range, self.count) if params is None else np.asarray(params["grid"])
+        k = self.u_scale * (self.count - 1) / (c[..., -1:] - c[..., :1])
+        u = (np.asarray(x, dtype=np.float64)[..., None] - c) * k
+        return self.norm * np.polynomial.polynomial.polyval(u, np.asarray(self.p)) * np.exp(-0.5 * u * u)
+
+
+class RBF(_Bump):
+    """Gaussian RBF exp(-((x - c) / h)^2) on a uniform grid of centres (FastKAN)."""
+
+    name = "rbf"
+    u_scale = math.sqrt(2.0)
+
+
+class MexicanHat(_Bump):
+    """Mexican-hat wavelet 2 / (sqrt(3) pi^(1/4)) (1 - u^2) exp(-u^2 / 2)."""
+
+    name = "mexican_hat"
+    p = (1.0, 0.0, -1.0)
+    norm = 2.0 / (math.sqrt(3.0) * math.pi**0.25)
+
+    def __init__(self, count: int = 8, grid_range: tuple[float, float] = (-1.0, 1.0), learnable: bool = True):
+        super().__init__(count, grid_range, learnable)
+
+
+class DoG(_Bump):
+    """Derivative-of-Gaussian wavelet -u exp(-u^2 / 2)."""
+
+    name = "dog"
+    p = (0.0, -1.0)
+
+    def __init__(self, count: int = 8, grid_range: tuple[float, float] = (-1.0, 1.0), learnable: bool = True):
+        super().__init__(count, grid_range, learnable)
+
+
+class RSWAF(Basis):
+    """Reflectional switch activation 1 - tanh((x - c) / h)^2 on a uniform grid
+    of centres, h = their spacing (FasterKAN), reference kanforge/bases/radial.py:120-147."""
+
+    name = "rswaf"
+
+    def __init__(self, count: int = 8, grid_range: tuple[float, float] = (-1.0, 1.0)):
+        if count < 2:
+            raise ValueError("count must be >= 2")
+        self.count = int(count)
+        self.grid_range = _check_range(grid_range)
+
+    @property
+    def size(self) -> int:
+        return self.count
+
+    def param_specs(self):
+        return {"grid": ParamSpec(np.linspace(*self.grid_range, self.count), trainable=False)}
+
+    def config(self):
+        return {"name": self.name, "count": self.count, "grid_range": self.grid_range}
+
+    def host_eval(self, x, params=None):
+        c = np.linspace(*self.grid_range, self.count) if params is None else np.asarray(params["grid"])
+        h = (c[..., -1:] - c[..., :1]) / (self.count - 1)
+        return 1.0 - np.tanh((np.asarray(x, dtype=np.float64)[..., None] - c) / h) ** 2
+
+
 __all__ = [
     "BASES",
     "Basis",
@@ -536,6 +688,11 @@ __all__ = [
     "Bernstein",
     "Chebyshev",
     "Chebyshev2",
+    "DoG",
+    "Fourier",
+    "MexicanHat",
+    "RBF",
+    "RSWAF",
     "Gegenbauer",
     "Gram",
     "Hermite",

@@ -78,8 +78,16 @@ extern "C" int kf_device_status(int32_t* flags) {
 
 // Fused tensor-core kernels: the feature vector of one input (basis features
 // plus the SiLU column) must fit the padded width; B-splines up to order 5.
+static int closed_family_ok(const kf_basis_desc* d) {
+  if (d->kind == KF_BASIS_FOURIER) return d->size >= 2 && d->size % 2 == 0 && d->size <= 32 && d->period > 0.0f;
+  if (d->kind == KF_BASIS_BUMP)
+    return d->size >= 2 && d->size <= 32 && (d->bump_mode == KF_BUMP_GAUSS || d->bump_mode == KF_BUMP_TANH);
+  return 0;
+}
+
 static int fused_supported(const kf_basis_desc* d) {
   if (d->kind == KF_BASIS_CHEB) return d->degree + 2 <= 32;
+  if (d->kind == KF_BASIS_FOURIER) return closed_family_ok(d) && d->size + 1 <= 32;
   if (d->kind == KF_BASIS_BSPLINE) return d->order >= 1 && d->order <= 5 && d->size + 1 <= 32 && d->grid_size + 2 * d->order + 1 <= 64;
   return 0;
 }
@@ -94,7 +102,7 @@ extern "C" int kf_query(const kf_basis_desc* d, int op, int dtype) {
       if (d->kind == KF_BASIS_CHEB) return d->degree + 1 <= 32;
       if (d->kind == KF_BASIS_BSPLINE)
         return d->order >= 1 && d->order <= 5 && d->size <= 32 && d->grid_size + 2 * d->order + 1 <= 64;
-      return 0;
+      return closed_family_ok(d);
     case 16:
       return dtype == KF_DTYPE_BF16 && fused_supported(d);
     case 17:
@@ -103,7 +111,7 @@ extern "C" int kf_query(const kf_basis_desc* d, int op, int dtype) {
       if (d->kind == KF_BASIS_CHEB) return d->degree + 1 <= 32;
       if (d->kind == KF_BASIS_BSPLINE)
         return d->order >= 1 && d->order <= 5 && d->size <= 32 && d->grid_size + 2 * d->order + 1 <= 64;
-      return 0;
+      return closed_family_ok(d);
     default:
       return 0;
   }

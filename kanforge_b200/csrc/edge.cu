@@ -37,7 +37,14 @@ struct EdgeArgs {
 // Features j < nf of order m at x for input i; t: knots of input i (B-splines).
 __device__ __forceinline__ void edge_features_rt(const EdgeArgs& A, int i, float x, const float* t, float* f,
                                                  int stride = 1) {
-  switch (A.kind == KF_BASIS_BSPLINE ? A.order : (A.kind == KF_BASIS_RATIONAL ? -1 : 0)) {
+  const int sel = A.kind == KF_BASIS_BSPLINE ? A.order
+                  : A.kind == KF_BASIS_RATIONAL ? -1
+                  : A.kind == KF_BASIS_FOURIER ? kFourierBK
+                  : A.kind == KF_BASIS_BUMP    ? kBumpBK
+                                               : 0;
+  switch (sel) {
+    case kFourierBK: eval_features<kFourierBK>(A.fa, x, 1.0f, t, f, stride); break;
+    case kBumpBK: eval_features<kBumpBK>(A.fa, x, 1.0f, t, f, stride); break;
     case -1: {
       const int g = i / A.in_per_group;
       f[0] = rational_deriv(x, A.num + (size_t)g * A.na, A.na, A.den + (size_t)g * A.nb, A.nb, A.m);
@@ -53,6 +60,10 @@ __device__ __forceinline__ void edge_features_rt(const EdgeArgs& A, int i, float
 }
 
 __device__ __forceinline__ void load_knots_rt(const EdgeArgs& A, int i, float* t) {
+  if (A.kind == KF_BASIS_BUMP) {
+    for (int r = 0; r < A.fa.nk; ++r) t[r] = A.fa.grid[(size_t)i * A.fa.nk + r];
+    return;
+  }
   if (A.kind != KF_BASIS_BSPLINE) return;
   const float* g = A.fa.grid + (size_t)i * (A.fa.G + 1);
   for (int r = 0; r < A.fa.nk; ++r) t[r] = extended_knot(g, A.fa.G, A.order, r);
@@ -102,11 +113,13 @@ __global__ void __launch_bounds__(kEdgeThreads, 1) edge_vec_kernel(const __grid_
   const int i = blockIdx.y * il + (lane & (il - 1));
   const int lo = lane >> il_log2;
   const int i_base = blockIdx.y * il;
-  if (A.kind == KF_BASIS_BSPLINE) {
+  if (A.kind == KF_BASIS_BSPLINE || A.kind == KF_BASIS_BUMP) {
     const int n_in = min(il, A.I - i_base);
     for (int e = threadIdx.x; e < n_in * A.fa.nk; e += blockDim.x) {
       const int ii = e / A.fa.nk, r = e % A.fa.nk;
-      Ts[ii * KF_NK_MAX + r] = extended_knot(A.fa.grid + (size_t)(i_base + ii) * (A.fa.G + 1), A.fa.G, A.order, r);
+      Ts[ii * KF_NK_MAX + r] = A.kind == KF_BASIS_BUMP
+                                   ? A.fa.grid[(size_t)(i_base + ii) * A.fa.nk + r]
+                                   : extended_knot(A.fa.grid + (size_t)(i_base + ii) * (A.fa.G + 1), A.fa.G, A.order, r);
     }
     __syncthreads();
   }
@@ -215,7 +228,7 @@ int launch_vec(const EdgeArgs& A, cudaStream_t stream) {
   int il_log2 = 5;
   while (il_log2 > 0 && (1 << (il_log2 - 1)) >= A.I) --il_log2;
   const size_t smem = ((size_t)(edge_chunk(NB) * (NF + 1) + NB) * kEdgeThreads +
-                       (A.kind == KF_BASIS_BSPLINE ? (32 * KF_NK_MAX) : 0)) * sizeof(float);
+                       ((A.kind == KF_BASIS_BSPLINE || A.kind == KF_BASIS_BUMP) ? (32 * KF_NK_MAX) : 0)) * sizeof(float);
   int dev = 0, n_sm = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
   // The coefficients are read through L1: keep the shared-memory carve-out small.
@@ -314,6 +327,9 @@ extern "C" int kf_edge_derivative(const float* x, const float* coefT, const floa
     A.fa.nk = basis->grid_size + 2 * basis->order + 1;
     A.fa.grid = grid;
     KF_CHECK_ARG(A.fa.nk <= KF_NK_MAX, "kf_edge_derivative: too many knots");
+  } else if (basis->kind == KF_BASIS_FOURIER || basis->kind == KF_BASIS_BUMP) {
+    KF_CHECK_ARG(nf == basis->size, "kf_edge_derivative: nf %d != basis size %d", nf, basis->size);
+    if (!fill_closed_family(basis, grid, basis->kind == KF_BASIS_BUMP ? order : 0, A.fa)) return KF_ERR_ARG;
   } else if (basis->kind != KF_BASIS_CHEB) {
     set_error("kf_edge_derivative: basis kind %d unsupported", basis->kind);
     return KF_ERR_UNSUPPORTED;

@@ -30,6 +30,7 @@
 // two: 512 outputs), K steps of 64 bf16 (128 B), 4 stages.
 #include "basis.cuh"
 #include "conv.cuh"
+#include "features.cuh"
 #include "umma.cuh"
 
 namespace kf {
@@ -59,7 +60,14 @@ struct TileMap {
   __device__ __forceinline__ int count() const { return m_tiles * n_tiles; }
 };
 
+// Template values of BK: 1..5 B-spline order; 0 Chebyshev features;
+// kFourierBK Fourier features (closed-form rows like Chebyshev: no per-input
+// data); kRationalBK the GR-KAN rational (input-gradient kernel only).
+constexpr bool is_closed(int bk) { return bk == 0 || bk == kFourierBK; }
+
 struct BasisDev {
+  float w1;      // Fourier: 2 pi / period
+  int nfreq;     // Fourier: frequencies (nt = 2 nfreq)
   int map;       // KF_MAP_* (Chebyshev)
   int nt;        // basis feature columns (Chebyshev: T_0..T_{nt-1}; B-spline: size)
   int has_base;  // SiLU column at index F - 1 (the last padded column)
@@ -205,6 +213,69 @@ __device__ __forceinline__ void cheb_drow(float x, const BasisDev& bd, float (&f
     um1 = u;
   }
   f[F - 1] = bd.has_base ? dsilu_fast(x) : 0.0f;
+}
+
+// Fourier feature row: cos(j w1 x) in columns 0..n-1, sin(j w1 x) in n..2n-1
+// (kanforge/bases/fourier.py:36-44), zero up to F-2, silu(x) in the last column.
+template <int F>
+__device__ __forceinline__ void fourier_row(float x, const BasisDev& bd, float (&f)[F]) {
+  float s1, c1;
+  sincosf(bd.w1 * x, &s1, &c1);
+  float c = c1, s = s1;
+#pragma unroll
+  for (int j = 0; j < F; ++j) f[j] = 0.0f;
+#pragma unroll
+  for (int j = 0; j < (F - 1) / 2; ++j) {
+    if (j < bd.nfreq) {
+      // columns j and nfreq + j: a compile-time loop over possible positions keeps f in registers
+#pragma unroll
+      for (int q = 0; q < F - 1; ++q) {
+        if (q == j) f[q] = c;
+        if (q == bd.nfreq + j) f[q] = s;
+      }
+    }
+    const float cn = c * c1 - s * s1;
+    s = s * c1 + c * s1;
+    c = cn;
+  }
+  f[F - 1] = bd.has_base ? silu_fast(x) : 0.0f;
+}
+
+// d/dx of the Fourier row: -j w1 sin(j w1 x), j w1 cos(j w1 x), and silu'.
+template <int F>
+__device__ __forceinline__ void fourier_drow(float x, const BasisDev& bd, float (&f)[F]) {
+  float s1, c1;
+  sincosf(bd.w1 * x, &s1, &c1);
+  float c = c1, s = s1;
+#pragma unroll
+  for (int j = 0; j < F; ++j) f[j] = 0.0f;
+#pragma unroll
+  for (int j = 0; j < (F - 1) / 2; ++j) {
+    if (j < bd.nfreq) {
+      const float w = (float)(j + 1) * bd.w1;
+#pragma unroll
+      for (int q = 0; q < F - 1; ++q) {
+        if (q == j) f[q] = -w * s;
+        if (q == bd.nfreq + j) f[q] = w * c;
+      }
+    }
+    const float cn = c * c1 - s * s1;
+    s = s * c1 + c * s1;
+    c = cn;
+  }
+  f[F - 1] = bd.has_base ? dsilu_fast(x) : 0.0f;
+}
+
+template <int BK, int F>
+__device__ __forceinline__ void closed_row(float x, const BasisDev& bd, float (&f)[F]) {
+  if constexpr (BK == kFourierBK) fourier_row<F>(x, bd, f);
+  else cheb_row<F>(x, bd, f);
+}
+
+template <int BK, int F>
+__device__ __forceinline__ void closed_drow(float x, const BasisDev& bd, float (&f)[F]) {
+  if constexpr (BK == kFourierBK) fourier_drow<F>(x, bd, f);
+  else cheb_drow<F>(x, bd, f);
 }
 
 // ===========================================================================
@@ -474,11 +545,11 @@ __global__ void __launch_bounds__(A_TMA ? kFwdTmaThreads : kFwdThreads, 1)
 #pragma unroll
         for (int u = 0; u < IPK; ++u) xv[u] = __uint_as_float((uint32_t)xa[u] << 16);
         uint8_t* arow = sa + s * kATile;
-        if constexpr (BK == 0) {
+        if constexpr (is_closed(BK)) {
 #pragma unroll
           for (int u = 0; u < IPK; ++u) {
             float f[F];
-            cheb_row<F>(xv[u], p.bd, f);
+            closed_row<BK, F>(xv[u], p.bd, f);
             if (i0 + IPK > p.I && i0 + u >= p.I) {  // tail step only
 #pragma unroll
               for (int j = 0; j < F; ++j) f[j] = 0.0f;
@@ -580,7 +651,7 @@ constexpr int kRatNA = 6, kRatNB = 4;  // the GR-KAN degrees (5, 4)
 // epilogue warps from w4 on: two sets of four for Chebyshev features, four
 // sets of four for B-splines and the GR-KAN rational (whose per-input
 // derivative windows / rational backward are the epilogue's main cost).
-constexpr int dgrad_threads(int bk) { return bk != 0 ? 640 : 384; }
+constexpr int dgrad_threads(int bk) { return (bk > 0 || bk == kRationalBK) ? 640 : 384; }
 // Pipeline depth: six stages of 32 KB where the epilogue's shared memory
 // leaves room (deeper buffering hides the TMA latency of operands read from
 // DRAM); B-spline plans keep four for their knot tables and staging.
@@ -595,7 +666,7 @@ template <int BK, int F>
 __global__ void __launch_bounds__(dgrad_threads(BK), 1) fused_dgrad_kernel(const __grid_constant__ CUtensorMap tmap_dy,
                                                                            const __grid_constant__ CUtensorMap tmap_c, DgradParams p) {
   constexpr int NS = dgrad_stages(BK);
-  constexpr int IPT = BK < 0 ? kBN : kBN / F;  // inputs per tile
+  constexpr int IPT = BK == kRationalBK ? kBN : kBN / F;  // inputs per tile
   constexpr int kEpiWarps = dgrad_threads(BK) / 32 - 4;
   constexpr int kEpiThreads = 32 * kEpiWarps;
   extern __shared__ uint8_t smem_raw[];
@@ -706,7 +777,7 @@ __global__ void __launch_bounds__(dgrad_threads(BK), 1) fused_dgrad_kernel(const
       mbar_drain(&ctl->drain, 0);
     }
   } else if (warp >= 4) {
-    if constexpr (BK < 0) {
+    if constexpr (BK == kRationalBK) {
       // GR-KAN: four sets of four warps; set `set` reads TMEM lane quarter q
       // (rows 32 q ..) of column chunks 2 set and 2 set + 1, each chunk 32
       // inputs of one parameter group, in halves of 16 columns.  Per half a
@@ -791,7 +862,7 @@ __global__ void __launch_bounds__(dgrad_threads(BK), 1) fused_dgrad_kernel(const
           }
         }
       }
-    } else if constexpr (BK == 0) {
+    } else if constexpr (is_closed(BK)) {
       // Two sets of four warps: set h2 reads TMEM lane quarter q (rows 32 q ..) of
       // column chunks 4 h2 .. 4 h2 + 3, i.e. the inputs IPT/2 h2 .. of the tile,
       // and writes those inputs' dx.
@@ -851,14 +922,14 @@ __global__ void __launch_bounds__(dgrad_threads(BK), 1) fused_dgrad_kernel(const
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(&ctl->acc_empty[acc], 0);
           }
-          if constexpr (BK == 0) {
+          if constexpr (is_closed(BK)) {
   #pragma unroll
             for (int h = 0; h < 32 / F + (F > 32 ? 1 : 0); ++h) {
               // F == 16: two inputs per chunk; F == 32: one input per chunk
               const int u = (c * 32) / F + h;
               const float xval = xr[u];
               float df[F];
-              cheb_drow<F>(xval, p.bd, df);
+              closed_drow<BK, F>(xval, p.bd, df);
               float s = 0.0f;
   #pragma unroll
               for (int j = 0; j < F; ++j) s = fmaf(v[h * F + j], df[j], s);
@@ -1315,7 +1386,7 @@ __global__ void __launch_bounds__(A_TMA ? kWgradTmaThreads : kWgradThreads, 1)
           const float sm = mk * (p.scale ? __bfloat162float(p.scale[e]) : 1.0f);
           const __nv_bfloat16* ce = p.coef + e * K;
           float dsc = 0.0f;
-          if (BK == 0 && p.fold) {  // only Chebyshev-feature plans fold
+          if (is_closed(BK) && p.fold) {  // only Chebyshev-feature plans fold
             float d[F - 1];
 #pragma unroll
             for (int j = 0; j < F - 1; ++j) d[j] = dcol[j * 33];
@@ -1417,8 +1488,8 @@ __global__ void __launch_bounds__(A_TMA ? kWgradTmaThreads : kWgradThreads, 1)
 #pragma unroll
           for (int j = 0; j < F; ++j) f[r][j] = 0.0f;
           if (!okr) continue;
-          if constexpr (BK == 0) {
-            cheb_row<F>(xv[r], p.bd, f[r]);
+          if constexpr (is_closed(BK)) {
+            closed_row<BK, F>(xv[r], p.bd, f[r]);
           } else {
             const int j0 = knot_interval(xv[r], tab, p.bd.nk);
             float vv[BK + 1];
@@ -1490,7 +1561,7 @@ __global__ void __launch_bounds__(A_TMA ? kWgradTmaThreads : kWgradThreads, 1)
 // Chebyshev: one thread per 16-byte chunk (8 features) of the output, so that
 // a warp's store is 512 contiguous bytes; the F / 8 threads of one (b, i) each
 // evaluate its (cheap) row and keep their own chunk.
-template <int F>
+template <int BK, int F>
 __global__ void __launch_bounds__(256) feature_cheb_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ feat,
                                                            int64_t n, int I, BasisDev bd, ConvDev conv) {
   constexpr int CH = F / 8;
@@ -1499,7 +1570,7 @@ __global__ void __launch_bounds__(256) feature_cheb_kernel(const __nv_bfloat16* 
     const int64_t e = c / CH;
     const int q = (int)(c % CH);
     float f[F];
-    cheb_row<F>(conv.active ? x_value(x, conv, e / I, (int)(e % I), I) : __bfloat162float(x[e]), bd, f);
+    closed_row<BK, F>(conv.active ? x_value(x, conv, e / I, (int)(e % I), I) : __bfloat162float(x[e]), bd, f);
     float g[8];
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
@@ -1751,8 +1822,12 @@ int fill_basis(const kf_basis_desc* d, const float* knot_tab, int nt, int has_ba
     bd.nk = d->grid_size + 2 * d->order + 1;
     KF_CHECK_ARG(bd.nk <= kTabStride, "B-spline with %d knots exceeds %d", bd.nk, kTabStride);
     KF_CHECK_ARG(nt == d->size, "B-spline nt %d must equal the basis size %d", nt, d->size);
+  } else if (d->kind == KF_BASIS_FOURIER) {
+    KF_CHECK_ARG(d->period > 0.0f && d->size % 2 == 0 && nt == d->size, "Fourier: period > 0 and nt = size (even)");
+    bd.w1 = 6.283185307179586f / d->period;
+    bd.nfreq = d->size / 2;
   } else if (d->kind != KF_BASIS_CHEB) {
-    set_error("fused kernels support B-spline and Chebyshev-feature bases");
+    set_error("fused kernels support B-spline, Chebyshev-feature and Fourier bases");
     return KF_ERR_UNSUPPORTED;
   }
   return KF_OK;
@@ -1761,6 +1836,12 @@ int fill_basis(const kf_basis_desc* d, const float* knot_tab, int nt, int has_ba
 template <typename Fn>
 int dispatch_fused(const kf_basis_desc* d, int f_pad, Fn&& fn) {
   if (d->kind == KF_BASIS_CHEB) return f_pad == 16 ? fn.template go<0, 16>() : fn.template go<0, 32>();
+  if (d->kind == KF_BASIS_FOURIER)
+    return f_pad == 16 ? fn.template go<kFourierBK, 16>() : fn.template go<kFourierBK, 32>();
+  if (d->kind != KF_BASIS_BSPLINE) {
+    set_error("fused kernels: basis kind %d unsupported", d->kind);
+    return KF_ERR_UNSUPPORTED;
+  }
   switch (d->order) {
     case 1: return f_pad == 16 ? fn.template go<1, 16>() : fn.template go<1, 32>();
     case 2: return f_pad == 16 ? fn.template go<2, 16>() : fn.template go<2, 32>();
@@ -1846,7 +1927,7 @@ struct DgradLaunch {
   int go() const {
     constexpr int IPT = kBN / F;
     const size_t smem = pair_smem(dgrad_stages(BK), 1) + sizeof(float) * (BK > 0 ? 2 * IPT * (BK + 1) * p.tab_ts + 16 * 32 * (F + 1)
-                                                      : BK == 0 ? kBM * (IPT + 1) : 0);
+                                                      : is_closed(BK) ? kBM * (IPT + 1) : 0);
     auto kern = fused_dgrad_kernel<BK, F>;
     KF_CUDA_RET(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     cudaLaunchAttribute attr[1];
@@ -1920,10 +2001,10 @@ struct FeatureLaunch {
   ConvDev conv;
   template <int BK, int F>
   int go() const {
-    if constexpr (BK == 0) {
+    if constexpr (is_closed(BK)) {
       const int64_t n = B * (int64_t)I;
       const unsigned grid = (unsigned)std::min<int64_t>(cdiv(n * (F / 8), 256), (int64_t)sm_count() * 16);
-      feature_cheb_kernel<F><<<grid, 256, 0, stream>>>(x, feat, n, I, bd, conv);
+      feature_cheb_kernel<BK, F><<<grid, 256, 0, stream>>>(x, feat, n, I, bd, conv);
     } else {
       const unsigned gy = (unsigned)cdiv(I, 32);
       const int64_t want = std::max<int64_t>(1, (int64_t)sm_count() * 8 / gy);
@@ -1946,7 +2027,7 @@ struct FeatureF32SplineLaunch {
   cudaStream_t stream;
   template <int BK, int F>
   int go() const {
-    if constexpr (BK == 0) {
+    if constexpr (BK <= 0) {
       set_error("kf_features_f32: the knot-table kernel is for B-splines");
       return KF_ERR_UNSUPPORTED;
     } else {

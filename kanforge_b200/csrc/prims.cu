@@ -39,7 +39,7 @@ __global__ void __launch_bounds__(kThreads) prim_f_kernel(const float* __restric
   float acc[4][4] = {};
 
   for (int i0 = 0; i0 < I; i0 += kChunk) {
-    if constexpr (BK > 0) {
+    if constexpr (BK > 0 || BK == kBumpBK) {
       for (int ii = 0; ii < kChunk; ++ii)
         if (i0 + ii < I) load_knots<BK>(fa, i0 + ii, Ts + ii * KF_NK_MAX, tid, kThreads);
       __syncthreads();
@@ -110,7 +110,7 @@ __global__ void __launch_bounds__(kThreads) prim_g_kernel(const float* __restric
   const int tx = tid % 16, ty = tid / 16;
   const int i0 = blockIdx.x * kChunk;
   const int o0 = blockIdx.y * kTile;
-  if constexpr (BK > 0) {
+  if constexpr (BK > 0 || BK == kBumpBK) {
     for (int ii = 0; ii < kChunk; ++ii)
       if (i0 + ii < I) load_knots<BK>(fa, i0 + ii, Ts + ii * KF_NK_MAX, tid, kThreads);
     __syncthreads();
@@ -217,7 +217,7 @@ __global__ void __launch_bounds__(kThreads) prim_p_kernel(const float* __restric
       const int n = tx + 16 * u;
       if (n < nn) Hs[(ty * 4 + r) * nn + n] = acc[r][u];
     }
-  if constexpr (BK > 0) {
+  if constexpr (BK > 0 || BK == kBumpBK) {
     for (int ii = 0; ii < kChunk; ++ii)
       if (i0 + ii < I) load_knots<BK>(fa, i0 + ii, Ts + ii * KF_NK_MAX, tid, kThreads);
   }
@@ -317,7 +317,21 @@ __global__ void __launch_bounds__(kThreads) feature_dot_f32_kernel(const float* 
     const float xv = x[b * I + i];
     const float* h = dfeat + (b * I + i) * F;
     float acc;
-    if constexpr (BK == 0) {
+    if constexpr (BK == kFourierBK) {
+      // d/dx cos(j w1 x) = -j w1 sin(j w1 x), d/dx sin(j w1 x) = j w1 cos(j w1 x)
+      const int n = fa.nf / 2;
+      float s1, c1;
+      sincosf(fa.w1 * xv, &s1, &c1);
+      float c = c1, sn = s1;
+      acc = 0.0f;
+      for (int j = 0; j < n; ++j) {
+        const float w = (float)(j + 1) * fa.w1;
+        acc = fmaf(w, fmaf(h[n + j], c, -h[j] * sn), acc);
+        const float cn = c * c1 - sn * s1;
+        sn = sn * c1 + c * s1;
+        c = cn;
+      }
+    } else if constexpr (BK == 0) {
       const bool tanh_map = fa.map == KF_MAP_TANH;
       const float z = tanh_map ? tanhf(xv) : xv;
       float um2 = 0.0f, um1 = 1.0f;  // U_{j-2}, U_{j-1} for j = 1
@@ -374,6 +388,9 @@ int feature_args(const kf_basis_desc* basis, const float* grid, int nf, int F, i
     fa.grid = grid;
     KF_CHECK_ARG(fa.nk <= KF_NK_MAX, "%d knots exceed the limit %d", fa.nk, KF_NK_MAX);
     KF_CHECK_ARG(nf == basis->size, "B-spline nf %d != size %d", nf, basis->size);
+  } else if (basis->kind == KF_BASIS_FOURIER || basis->kind == KF_BASIS_BUMP) {
+    KF_CHECK_ARG(nf == basis->size, "nf %d != basis size %d", nf, basis->size);
+    if (!fill_closed_family(basis, grid, m, fa)) return KF_ERR_ARG;
   } else if (basis->kind != KF_BASIS_CHEB) {
     set_error("basis kind %d has no float32 feature kernel", basis->kind);
     return KF_ERR_UNSUPPORTED;
@@ -405,6 +422,9 @@ extern "C" int kf_prim(int op, int m, const float* x, const float* a, const floa
     fa.grid = grid;
     KF_CHECK_ARG(fa.nk <= KF_NK_MAX, "kf_prim: %d knots exceed the limit %d", fa.nk, KF_NK_MAX);
     KF_CHECK_ARG(nf == basis->size, "kf_prim: B-spline nf %d != size %d", nf, basis->size);
+  } else if (basis->kind == KF_BASIS_FOURIER || basis->kind == KF_BASIS_BUMP) {
+    KF_CHECK_ARG(nf == basis->size, "kf_prim: nf %d != basis size %d", nf, basis->size);
+    if (!fill_closed_family(basis, grid, m, fa)) return KF_ERR_ARG;
   } else if (basis->kind != KF_BASIS_CHEB) {
     set_error("kf_prim: basis kind %d has no primitive kernel", basis->kind);
     return KF_ERR_UNSUPPORTED;

@@ -222,7 +222,7 @@ def fused_ok(plan: KernelPlan | None, x: torch.Tensor, n_out: int, has_base: boo
     """Whether the tensor-core path serves this call: bf16 inputs and parameters,
     CUDA, a B-spline or Chebyshev-feature plan with <= 31 feature columns,
     outputs a multiple of 8."""
-    if plan is None or plan.kind not in ("cheb", "bspline") or x.dtype != _BF16 or x.device.type != "cuda":
+    if plan is None or plan.kind not in ("cheb", "bspline", "fourier") or x.dtype != _BF16 or x.device.type != "cuda":
         return False
     if coef_dtype is not None and coef_dtype != _BF16:
         return False
@@ -418,7 +418,7 @@ def tf32_ok(plan: KernelPlan | None, x: torch.Tensor, n_out: int, has_base: bool
     """Whether the float32 tensor-core path serves this call: float32 inputs and
     parameters on CUDA, a B-spline or Chebyshev-feature plan with <= 31 feature
     columns, outputs a multiple of 4."""
-    if plan is None or plan.kind not in ("cheb", "bspline") or x.dtype != torch.float32 or x.device.type != "cuda":
+    if plan is None or plan.kind not in ("cheb", "bspline", "fourier", "bump") or x.dtype != torch.float32 or x.device.type != "cuda":
         return False
     if coef_dtype is not None and coef_dtype != torch.float32:
         return False
@@ -560,7 +560,7 @@ def edge_derivative(x, coef_eff, base_eff, grid, plan: KernelPlan, order: int, b
     n_out, n_in, _ = coef_eff.shape
     c = coef_eff.detach().float()
     num = den = None
-    if plan.kind == "cheb":
+    if plan.folded:
         c = c @ _fold_on(plan, order, x.device)
     elif plan.kind == "rational":
         num = basis_params["numerator"].detach().float().contiguous()

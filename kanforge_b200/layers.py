@@ -239,6 +239,13 @@ class KANLinear(nn.Module):
             # float32: three TF32 products per contraction on the tensor cores
             return _kernels.kan_linear_tf32(x, self.coef, silu_weight, self.bias, self.edge_scale, self.edge_mask,
                                             self._grid(), plan)
+        if plan.kind == "bump" and x.dtype == torch.bfloat16 and _kernels.FP32_TENSOR_CORES:
+            # bf16 bump layers (centres per input) compute in float32 on the three-TF32 GEMM
+            f = lambda t: None if t is None else t.float()  # noqa: E731
+            if _kernels.tf32_ok(plan, x.float(), self.out_features, has_base, torch.float32):
+                y = _kernels.kan_linear_tf32(x.float(), self.coef.float(), f(silu_weight), f(self.bias),
+                                             f(self.edge_scale), f(self.edge_mask), self._grid(), plan)
+                return y.to(x.dtype)
         coef_eff = self.effective_coef()
         base_eff = None if silu_weight is None else silu_weight * self.edge_mask
         if plan.kind == "rational":

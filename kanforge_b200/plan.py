@@ -7,7 +7,12 @@ derivatives are obtained:
   evaluated as Chebyshev features T_j(g(x)); the family matrix and the m-th
   x-derivative are *folded* into the coefficients, phi_k^(m) = sum_j R_m[k,j] T_j,
   so kernels never differentiate (kanforge/kernels/plan.py:75-101).
+* ``fourier``: cos / sin features of the harmonics; the m-th derivative of
+  every feature is a rotation of its (cos, sin) pair scaled by w^m, folded into
+  the coefficients like ``cheb`` (kanforge/kernels/plan.py:76-87);
 * ``bspline``: the derivative order is evaluated natively from the per-input grid.
+* ``bump``: RBF / wavelet / RSWAF bumps on a per-input grid of centres,
+  natively at every order from derivative polynomials (plan.py:33-73, 112-120).
 * ``rational``: the KAT group rational; trainable per-group parameters, so the
   reference has no fused plan for it (plan.py:107-108).  This package runs it on
   its own elementwise kernels plus the layer contraction.
@@ -23,22 +28,23 @@ import numpy as np
 from numpy.polynomial import chebyshev as npcheb
 
 from . import _lib
-from .bases import BSpline, PolynomialBasis, Rational
+from .bases import RBF, RSWAF, BSpline, DoG, Fourier, MexicanHat, PolynomialBasis, Rational, gaussian_bump_polys, tanh_bump_polys
 
 ONE_MINUS_Z2 = np.array([0.5, 0.0, -0.5])  # 1 - z^2 in the Chebyshev basis
 
 
 @dataclass(frozen=True)
 class KernelPlan:
-    kind: str             # "cheb" | "bspline" | "rational"
-    consts: tuple         # cheb: (degree, input_map); bspline: (grid_size, order); rational: (p, q)
+    kind: str             # "cheb" | "fourier" | "bspline" | "bump" | "rational"
+    consts: tuple         # cheb: (degree, input_map); fourier: (frequencies, period); bspline: (grid_size, order);
+                          # bump: (mode, count, u_scale, norm, p); rational: (p, q)
     size: int             # basis functions per edge
     fold_key: tuple = ()  # cheb: the Chebyshev coefficient matrix, flattened
     grid: bool = False    # the kernels read the per-input grid
 
     @property
     def folded(self) -> bool:
-        return self.kind == "cheb"
+        return self.kind in ("cheb", "fourier")
 
     def n_features(self, m: int) -> int:
         """Features evaluated for derivative order m (plan.py:52-56)."""
@@ -54,7 +60,15 @@ class KernelPlan:
         """R_m (size, n_features(m)) for folded plans, else None."""
         if not self.folded:
             return None
+        if self.kind == "fourier":
+            return _fourier_fold(self.consts, m)
         return _fold(self.consts, self.fold_key, m)
+
+    def bump_poly(self, m: int) -> np.ndarray:
+        """Coefficients (lowest first) of the bump's m-th derivative polynomial:
+        in u for gauss bumps, in tanh for RSWAF."""
+        mode, _count, _u_scale, _norm, p = self.consts
+        return (gaussian_bump_polys(p, m) if mode == "gauss" else tanh_bump_polys(m))[m]
 
     def is_identity_fold(self) -> bool:
         """R_0 is the identity (plain Chebyshev): the coefficients need no fold."""
@@ -75,6 +89,19 @@ class KernelPlan:
         elif self.kind == "bspline":
             d.kind = _lib.KF_BASIS_BSPLINE
             d.grid_size, d.order = self.consts
+        elif self.kind == "fourier":
+            d.kind = _lib.KF_BASIS_FOURIER
+            d.degree, d.period = self.consts
+        elif self.kind == "bump":
+            d.kind = _lib.KF_BASIS_BUMP
+            mode, _count, d.u_scale, d.norm, _p = self.consts
+            d.bump_mode = _lib.KF_BUMP_GAUSS if mode == "gauss" else _lib.KF_BUMP_TANH
+            for m in range(_lib.KF_BUMP_MAX_ORDER + 1):
+                poly = self.bump_poly(m)
+                if len(poly) > 8:
+                    raise ValueError(f"bump derivative polynomial of order {m} has more than 8 coefficients")
+                for e, v in enumerate(poly):
+                    d.bump_poly[m][e] = float(v)
         else:
             d.kind = _lib.KF_BASIS_RATIONAL
             d.degree, d.den_degree = self.consts
@@ -105,6 +132,19 @@ def _fold(consts, fold_key, m):
     return r
 
 
+@lru_cache(maxsize=None)
+def _fourier_fold(consts, m):
+    """R_m (2n, 2n): cos(w x)^(m) = w^m (cos(m pi/2) cos(w x) - sin(m pi/2) sin(w x)),
+    sin(w x)^(m) = w^m (sin(m pi/2) cos(w x) + cos(m pi/2) sin(w x))."""
+    n, period = consts
+    wm = (2.0 * np.pi / period * np.arange(1, n + 1)) ** m
+    c, s = (1.0, 0.0, -1.0, 0.0)[m % 4], (0.0, 1.0, 0.0, -1.0)[m % 4]
+    eye = np.eye(n)
+    r = np.block([[eye * (wm * c), eye * (-wm * s)], [eye * (wm * s), eye * (wm * c)]])
+    r.setflags(write=False)
+    return r
+
+
 def plan_for(basis) -> KernelPlan | None:
     """The kernel plan of ``basis``, or None when no kernel exists (plan.py:104-121)."""
     if isinstance(basis, PolynomialBasis) and basis.input_map in ("tanh", "identity"):
@@ -113,4 +153,12 @@ def plan_for(basis) -> KernelPlan | None:
         return KernelPlan("bspline", (basis.grid_size, basis.order), basis.size, grid=True)
     if type(basis) is Rational:
         return KernelPlan("rational", (basis.num_degree, basis.den_degree), 1)
+    if any(spec.trainable for spec in basis.param_specs().values()):
+        return None  # learnable frequencies / centres: no kernel plan (plan.py:107-108)
+    if type(basis) is Fourier:
+        return KernelPlan("fourier", (basis.frequencies, basis.period), basis.size)
+    if type(basis) in (RBF, MexicanHat, DoG):
+        return KernelPlan("bump", ("gauss", basis.count, basis.u_scale, basis.norm, tuple(basis.p)), basis.size, grid=True)
+    if type(basis) is RSWAF:
+        return KernelPlan("bump", ("tanh", basis.count, 1.0, 1.0, (1.0, 0.0, -1.0)), basis.size, grid=True)
     return None

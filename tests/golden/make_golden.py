@@ -60,6 +60,13 @@ BASIS_CASES = [
     ("taylor_3", kf.Taylor(3), {"kind": "poly", "family": "taylor", "degree": 3, "input_map": "identity"}),
     ("rational_gelu", kf.Rational(5, 4, "gelu"), {"kind": "rational", "num_degree": 5, "den_degree": 4}),
     ("rational_identity", kf.Rational(5, 4, "identity"), {"kind": "rational", "num_degree": 5, "den_degree": 4}),
+    ("fourier_3", kf.Fourier(3), {"kind": "fourier", "frequencies": 3, "period": 2 * np.pi}),
+    ("fourier_4_p3", kf.Fourier(4, 3.0), {"kind": "fourier", "frequencies": 4, "period": 3.0}),
+    ("rbf_6", kf.RBF(6), {"kind": "bump", "family": "rbf", "count": 6, "grid_range": (-1.0, 1.0)}),
+    ("mexican_hat_5", kf.MexicanHat(5, learnable=False),
+     {"kind": "bump", "family": "mexican_hat", "count": 5, "grid_range": (-1.0, 1.0)}),
+    ("dog_5", kf.DoG(5, (-2.0, 2.0), learnable=False), {"kind": "bump", "family": "dog", "count": 5, "grid_range": (-2.0, 2.0)}),
+    ("rswaf_6", kf.RSWAF(6), {"kind": "bump", "family": "rswaf", "count": 6, "grid_range": (-1.0, 1.0)}),
 ]
 
 
@@ -101,7 +108,8 @@ def make_bases():
             rec[f"{name}/d{m}"] = np.asarray(basis.derivative(x, m, params))
         plan = plan_for(basis)
         if plan is not None and plan.folded:
-            rec[f"{name}/cheb"] = basis._cheb
+            if plan.kind == "cheb":
+                rec[f"{name}/cheb"] = basis._cheb
             for m in range(4):
                 rec[f"{name}/fold{m}"] = plan.fold(m)
     np.savez_compressed(HERE / "bases.npz", **rec)
@@ -116,6 +124,10 @@ LAYER_CASES = [
     ("chebyshev_4_id_nobase", kf.Chebyshev(4, input_map="identity"), 3, 2, None, False, True, 0.9),
     ("rational_gelu_g2", kf.Rational(5, 4, "gelu"), 4, 3, 2, False, False, 2.5),
     ("rational_identity_g1", kf.Rational(5, 4, "identity"), 4, 2, 1, False, True, 2.0),
+    ("fourier_3", kf.Fourier(3), 4, 3, None, True, True, 2.5),
+    ("rbf_6", kf.RBF(6), 4, 3, None, True, False, 1.4),
+    ("mexican_hat_5", kf.MexicanHat(5, learnable=False), 3, 4, None, False, True, 1.2),
+    ("rswaf_6", kf.RSWAF(6), 4, 2, None, True, False, 1.3),
 ]
 
 
@@ -160,7 +172,9 @@ def make_layers():
     np.savez_compressed(HERE / "layers.npz", **rec)
 
 
-PRIM_CASES = [("bspline_5_3", kf.BSpline(5, 3)), ("chebyshev_5", kf.Chebyshev(5)), ("jacobi_4", kf.Jacobi(4, 0.5, 1.5))]
+PRIM_CASES = [("bspline_5_3", kf.BSpline(5, 3)), ("chebyshev_5", kf.Chebyshev(5)), ("jacobi_4", kf.Jacobi(4, 0.5, 1.5)),
+              ("fourier_3", kf.Fourier(3)), ("rbf_6", kf.RBF(6)), ("dog_5", kf.DoG(5, learnable=False)),
+              ("rswaf_6", kf.RSWAF(6))]
 
 
 def make_prims():

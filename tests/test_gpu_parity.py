@@ -39,6 +39,10 @@ def spec_of_basis(basis) -> dict:
         return {"kind": "bspline", "grid_size": cfg["grid_size"], "order": cfg["order"], "grid_range": cfg["grid_range"]}
     if cfg["name"] == "rational":
         return {"kind": "rational", "num_degree": cfg["num_degree"], "den_degree": cfg["den_degree"]}
+    if cfg["name"] == "fourier":
+        return {"kind": "fourier", "frequencies": cfg["frequencies"], "period": cfg["period"]}
+    if cfg["name"] in ("rbf", "mexican_hat", "dog", "rswaf"):
+        return {"kind": "bump", "family": cfg["name"], "count": cfg["count"], "grid_range": cfg["grid_range"]}
     out = {"kind": "poly", "family": cfg["name"], "degree": cfg["degree"], "input_map": cfg["input_map"]}
     for k in ("alpha", "beta", "lam"):
         if k in cfg:
@@ -62,7 +66,8 @@ def layer_numpy(layer) -> dict:
 # ---------------------------------------------------------------------------
 
 PRIMS = load_golden("prims.npz")
-PRIM_BASES = {"bspline_5_3": kb.BSpline(5, 3), "chebyshev_5": kb.Chebyshev(5), "jacobi_4": kb.Jacobi(4, 0.5, 1.5)}
+PRIM_BASES = {"bspline_5_3": kb.BSpline(5, 3), "chebyshev_5": kb.Chebyshev(5), "jacobi_4": kb.Jacobi(4, 0.5, 1.5),
+              "fourier_3": kb.Fourier(3), "rbf_6": kb.RBF(6), "dog_5": kb.DoG(5, learnable=False), "rswaf_6": kb.RSWAF(6)}
 
 
 @pytest.mark.parametrize("case", sorted(PRIM_BASES))
@@ -86,6 +91,11 @@ PRIM_SWEEP = [
     (kb.Chebyshev(12), 200, 33, 66),
     (kb.Chebyshev(4, input_map="identity"), 17, 3, 2),
     (kb.Jacobi(6, 0.5, 0.5), 99, 12, 31),
+    (kb.Fourier(5, 3.0), 150, 11, 20),
+    (kb.RBF(8), 100, 9, 17),
+    (kb.MexicanHat(6, learnable=False), 77, 5, 9),
+    (kb.DoG(5, (-2.0, 2.0), learnable=False), 64, 7, 5),
+    (kb.RSWAF(7), 64, 10, 12),
 ]
 
 
@@ -102,7 +112,7 @@ def test_primitives_match_oracle_ragged_shapes(basis, n_b, n_in, n_out, m):
     c = rng.standard_normal((n_out, n_in, basis.size)) * 0.3
     params = None
     grid = np.zeros(1)
-    if spec["kind"] == "bspline":
+    if spec["kind"] in ("bspline", "bump"):  # non-uniform per-input grids / centres
         grid = ko.default_grid(spec, n_in)
         grid[:, 1:-1] += rng.uniform(-0.2, 0.2, (n_in, grid.shape[1] - 2)) * (grid[0, 1] - grid[0, 0])
         params = {"grid": grid}
@@ -132,6 +142,10 @@ LAYER_BASES = {
     "chebyshev_4_id_nobase": (kb.Chebyshev(4, input_map="identity"), {"base_activation": None}),
     "rational_gelu_g2": (kb.Rational(5, 4, "gelu"), {"base_activation": None, "groups": 2}),
     "rational_identity_g1": (kb.Rational(5, 4, "identity"), {"base_activation": None, "groups": 1}),
+    "fourier_3": (kb.Fourier(3), {}),
+    "rbf_6": (kb.RBF(6), {}),
+    "mexican_hat_5": (kb.MexicanHat(5, learnable=False), {"base_activation": None}),
+    "rswaf_6": (kb.RSWAF(6), {}),
 }
 
 
@@ -175,7 +189,7 @@ def test_edge_derivative_matches_reference(case, order):
 EDGE_SHAPES = [(64, 24, 301), (37, 3, 133), (5, 7, 1000), (2, 1, 4096), (130, 9, 50), (24, 40, 99), (66, 5, 17)]
 
 
-@pytest.mark.parametrize("basis", [kb.Jacobi(6, 0.5, 0.5), kb.BSpline(8, 3), kb.Chebyshev(5)], ids=repr)
+@pytest.mark.parametrize("basis", [kb.Jacobi(6, 0.5, 0.5), kb.BSpline(8, 3), kb.Chebyshev(5), kb.Fourier(4), kb.RBF(6), kb.RSWAF(5)], ids=repr)
 @pytest.mark.parametrize("order", [0, 2, 3])
 @pytest.mark.parametrize("shape", EDGE_SHAPES, ids=str)
 def test_edge_derivative_streaming_kernel_matches_oracle(basis, order, shape):
@@ -277,6 +291,9 @@ FUSED_CASES = [
     (kb.BSpline(4, 4), 99, 10, 16, False, True, False),
     (kb.BSpline(7, 5), 150, 20, 48, True, False, False),
     (kb.BSpline(20, 3), 140, 12, 40, True, True, False),       # f_pad 32
+    (kb.Fourier(4), 300, 40, 264, True, True, False),
+    (kb.Fourier(7), 257, 37, 136, True, False, True),
+    (kb.Fourier(12, 3.0), 129, 9, 24, True, True, False),        # f_pad 32
 ]
 
 
@@ -398,6 +415,10 @@ FP32_LAYER_CASES = [
     (kb.BSpline(20, 3), 140, 12, 40, True, True, False),      # 32-wide feature rows
     (kb.Chebyshev(5), 129, 9, 24, False, False, False),
     (kb.Chebyshev(4, input_map="identity"), 77, 12, 40, True, True, True),
+    (kb.Fourier(5), 257, 37, 136, True, True, True),
+    (kb.RBF(8), 300, 24, 64, True, True, False),
+    (kb.RSWAF(6), 129, 9, 24, False, False, False),
+    (kb.MexicanHat(5, learnable=False), 77, 12, 40, True, True, True),
 ]
 
 
@@ -753,3 +774,27 @@ def test_training_step_in_cuda_graph_matches_eager(kind):
     for got, w in zip([x.grad] + [p.grad for p in params], want):
         same(got, w)
     del graph
+
+
+@pytest.mark.parametrize("basis", [kb.RBF(8), kb.RSWAF(6)], ids=repr)
+def test_bf16_bump_layer_on_float32_tensor_cores_matches_oracle(basis):
+    """bf16 bump layers (centres per input) run the float32 three-TF32 path."""
+    layer = make_bf16_layer(basis, 24, 64, True, True, True)
+    x0 = (torch.randn(300, 24, device=DEV) * 1.2).clamp(-3, 3).to(torch.bfloat16)
+    x = x0.clone().requires_grad_()
+    y = layer(x)
+    assert y.dtype == torch.bfloat16
+    dy = (torch.randn(300, 64, device=DEV) * 0.5).to(torch.bfloat16)
+    params = [p for _, p in layer.named_parameters()]
+    names = [n for n, _ in layer.named_parameters()]
+    grads = torch.autograd.grad(y, [x] + params, dy)
+    n = layer_numpy(layer)
+    xs = x0.double().cpu().numpy()
+    kw = dict(coef=n["coef"], base_weight=n["base_weight"], bias=n["bias"], spec=n["spec"], params=n["params"],
+              edge_scale=n["edge_scale"], edge_mask=n["edge_mask"])
+    close(y, ko.kan_linear(xs, **kw), BF16_TOL, "y")
+    want = ko.kan_linear_backward(xs, dy.double().cpu().numpy(), **kw)
+    close(grads[0], want["dx"], BF16_TOL, "dx")
+    key = {"coef": "dcoef", "base_weight": "dbase_weight", "bias": "dbias", "edge_scale": "dedge_scale"}
+    for nme, gr in zip(names, grads[1:]):
+        close(gr, want[key[nme]], BF16_TOL, f"d{nme}")
