@@ -382,11 +382,19 @@ def run_ours(args, world, rank, local):
                                                                         tokens=args.tokens)
     loss_of = getattr(step, "loss_fn", None)
 
-    from kanforge_b200.data_parallel import allreduce_gradients, max_over_ranks
+    from kanforge_b200.data_parallel import GradientSync, allreduce_gradients, max_over_ranks
+
+    def grad_sync():
+        """The gradient all-reduce of a step: overlapped with the backward
+        (default), or after it (--no-overlap); nothing on one GPU."""
+        if pg is None or not params or args.no_overlap:
+            return contextlib.nullcontext()
+        return GradientSync(params, group=pg, reserved_sms=args.reserve_sms)
 
     def full_step():
-        out = step()
-        if pg is not None and params:
+        with grad_sync():
+            out = step()
+        if pg is not None and params and args.no_overlap:
             allreduce_gradients(params, group=pg)
         return out
 
@@ -495,8 +503,9 @@ def run_ours(args, world, rank, local):
             p.grad = None
         y = model(x_dev)
         loss = loss_of(y)
-        loss.backward()
-        if pg is not None and params:
+        with grad_sync():
+            loss.backward()
+        if pg is not None and params and args.no_overlap:
             allreduce_gradients(params, group=pg)
         loss_host.copy_(loss.detach().float().reshape(1), non_blocking=True)
         x_dev.requires_grad_(False)
@@ -592,6 +601,10 @@ def main(argv=None):
     ap.add_argument("--dtype", default="bf16", choices=["bf16", "fp32"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="multi-GPU: all-reduce the gradients after the backward instead of beside it")
+    ap.add_argument("--reserve-sms", type=int, default=0,
+                    help="multi-GPU: SMs the persistent kernels leave to NCCL while the all-reduce overlaps")
     ap.add_argument("--graph", action="store_true",
                     help="replay one captured CUDA graph per step (launch-bound configurations, one GPU)")
     ap.add_argument("--tokens", type=int, default=None,

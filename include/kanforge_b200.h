@@ -87,6 +87,13 @@ const char* kf_last_error(void);
  * kanforge/kernels/plan.py:104-121). */
 int kf_query(const kf_basis_desc* basis, int op, int dtype);
 
+/* SMs that the persistent tensor-core kernels leave free (default 0: they
+ * take every SM), so that a kernel launched beside them on another stream --
+ * the gradient all-reduce of data parallelism overlapping the backward --
+ * finds SMs to run on.  Process-wide; 0 <= n < the SM count.  (No counterpart
+ * in the reference, which has no distributed code.) */
+int kf_set_reserved_sms(int32_t n);
+
 /* Reads and clears the device-side error word of the current device (set by a
  * kernel whose bounded wait ran out).  Synchronises the device.  *flags = 0 when
  * clean. */

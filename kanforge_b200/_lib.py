@@ -81,6 +81,7 @@ PROTOTYPES = {
          ctypes.POINTER(BasisDesc), _vp],
     ),
     "kf_version": (ctypes.c_int, []),
+    "kf_set_reserved_sms": (ctypes.c_int, [_c_i32]),
     "kf_last_error": (ctypes.c_char_p, []),
     "kf_query": (ctypes.c_int, [ctypes.POINTER(BasisDesc), ctypes.c_int, ctypes.c_int]),
     "kf_device_status": (ctypes.c_int, [ctypes.POINTER(_c_i32)]),

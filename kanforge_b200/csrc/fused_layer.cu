@@ -28,6 +28,8 @@
 //
 // Tiles: pair M = 256 rows, N = 256 columns per accumulator (the forward uses
 // two: 512 outputs), K steps of 64 bf16 (128 B), 4 stages.
+#include <atomic>
+
 #include "basis.cuh"
 #include "conv.cuh"
 #include "features.cuh"
@@ -1860,17 +1862,24 @@ constexpr size_t pair_smem(int ns, int nb) { return 1024 + (size_t)ns * (kATile 
 
 // Largest number of co-resident CTA pairs for a cluster launch of `kern`
 // (clusters of 2), cached per device in the caller's `cache`.
+std::atomic<int> g_reserved_sms{0};
+
 template <typename K>
 int max_pairs(K kern, const cudaLaunchConfig_t& cfg, int (&cache)[64]) {
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && cache[dev] > 0) return cache[dev];
-  int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
-    cudaGetLastError();
-    n = sm_count() / 2;
+  int n = (dev >= 0 && dev < 64) ? cache[dev] : 0;
+  if (n <= 0) {
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = sm_count() / 2;
+    }
+    if (dev >= 0 && dev < 64) cache[dev] = n;
   }
-  if (dev >= 0 && dev < 64) cache[dev] = n;
+  // SMs left to kernels that run beside the persistent grids (a collective
+  // overlapping the backward): kf_set_reserved_sms
+  const int reserved = g_reserved_sms.load(std::memory_order_relaxed);
+  if (reserved > 0) n = std::max(1, std::min(n, (sm_count() - reserved) / 2));
   return n;
 }
 
@@ -2648,4 +2657,11 @@ extern "C" int kf_conv_wgrad(const void* img, const kf_conv_geom* geom, const vo
   if (int rc = kf::conv_geometry(geom, g, rows, cols, "kf_conv_wgrad")) return rc;
   return kf_wgrad_impl(&g, img, feat, dy, knot_tab, fold, coef, edge_scale, edge_mask, dcoef, dbase, dscale, rows, cols, O, K,
                        nt, f_pad, basis, stream);
+}
+
+extern "C" int kf_set_reserved_sms(int32_t n) {
+  kf::clear_error();
+  KF_CHECK_ARG(n >= 0 && n < kf::sm_count(), "kf_set_reserved_sms: %d out of range", n);
+  kf::g_reserved_sms.store(n, std::memory_order_relaxed);
+  return KF_OK;
 }

@@ -53,6 +53,30 @@ def _launch(name: str, *args, kernels: int | None = None) -> None:
         _lib.call(name, *args)
 
 
+# Gradient-ready hook of data parallelism: a callable([(param, grad), ...])
+# returning waitables, called by the tensor-core backward passes as soon as
+# their parameter gradients are written and before the input-gradient kernel,
+# so that the all-reduce of those gradients overlaps it (data_parallel.py).
+_grad_hook = None
+
+
+def set_grad_ready_hook(fn) -> None:
+    global _grad_hook
+    _grad_hook = fn
+
+
+def _grads_ready(pairs) -> list:
+    if _grad_hook is None:
+        return []
+    return _grad_hook([(p, g) for p, g in pairs if p is not None and g is not None])
+
+
+def set_reserved_sms(n: int) -> None:
+    """SMs the persistent tensor-core kernels leave to kernels on other streams
+    (kf_set_reserved_sms); 0 restores every SM to them."""
+    _lib.call("kf_set_reserved_sms", int(n))
+
+
 def available(device: torch.device) -> bool:
     """True on CUDA devices with the library loaded (kanforge/torch/kernels.py:19-28)."""
     if torch.device(device).type != "cuda":
@@ -355,12 +379,17 @@ class _FusedKANLinear(torch.autograd.Function):
             gc = gc.to(coef.dtype) if need[1] else None
             gb = gb.to(base_weight.dtype) if (gb is not None and need[2]) else None
             gs = gs.to(edge_scale.dtype) if gs is not None else None
+        # the parameter gradients are complete: a registered hook (data
+        # parallelism) can start their all-reduce now, beside the input gradient
+        pending = _grads_ready([(coef, gc), (base_weight, gb), (edge_scale, gs)])
         if need[0]:
             gx = torch.empty_like(x)
             _launch("kf_dgrad", _ptr(x), _ptr(gy), _ptr(ctx.packed), _ptr(ctx.knot_tab), _ptr(gx), x.shape[0], n_in, n_out,
                     nt, f_pad, int(base_weight is not None), ctypes.byref(desc), stream)
         if need[3]:
             gbias = gy.sum(0, dtype=torch.float32)
+        for work in pending:
+            work.wait()
         ctx.packed = ctx.knot_tab = ctx.feat = None
         return gx, gc, gb, gbias, gs, None, None, None
 

@@ -85,3 +85,38 @@ def test_lost_rank_is_an_error_not_a_hang():
             pytest.fail("a rank hung on the collective of a lost peer")
     assert out[1] == "left"
     assert str(out[0]).startswith("error"), out[0]
+
+
+def _sync_worker(rank, world, port, out):
+    """GradientSync: gradients handed over during the backward are reduced once
+    (there), the others when the context exits; the hook is removed after."""
+    _init(rank, world, port)
+    try:
+        import kanforge_b200.kernels as kk
+        from kanforge_b200.data_parallel import GradientSync
+
+        early = torch.nn.Parameter(torch.zeros(3))
+        late = torch.nn.Parameter(torch.zeros(2))
+        sync = GradientSync([early, late])
+        with sync:
+            g = torch.full((3,), float(rank + 1))
+            works = kk._grads_ready([(early, g), (None, None)])  # as the fused backward does
+            for w in works:
+                w.wait()
+            kk._grads_ready([(early, g)])  # a second hand-over of the same parameter is ignored
+            early.grad = g
+            late.grad = torch.full((2,), 10.0 * (rank + 1))
+        out[rank] = (early.grad.clone(), late.grad.clone(), kk._grad_hook is None)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gradient_sync_reduces_every_gradient_once():
+    world, port = 2, _free_port()
+    out = mp.Manager().dict()
+    mp.spawn(_sync_worker, args=(world, port, out), nprocs=world, join=True)
+    for rank in range(world):
+        e, l_, unhooked = out[rank]
+        assert torch.equal(e, torch.full((3,), 3.0))
+        assert torch.equal(l_, torch.full((2,), 30.0))
+        assert unhooked
