@@ -229,6 +229,27 @@ int kf_edge_derivative(const float* x, const float* coefT, const float* base_eff
                        int32_t O, int32_t nf, int32_t order, const kf_basis_desc* basis,
                        const float* silu_poly, int32_t n_poly, void* stream);
 
+/* Backward of kf_edge_derivative: the reference's edge_derivative is an
+ * autograd graph (kanforge/torch/layers.py:206-226), so a loss on the edge
+ * derivatives trains the layer.  With g = dL/dout (B, O, I) float32:
+ *   kf_edge_derivative_dx:    dx[b,i] = sum_o g[b,o,i] (sum_j phi_j^(order)(x) coefT[o,j,i] + s(x) base_eff[o,i])
+ *                             -- called with the order, coefficients (coefT of that order, nf features) and
+ *                             SiLU polynomials of the forward's order + 1;
+ *   kf_edge_derivative_dcoef: dcoefT[o,j,i] = sum_b g[b,o,i] phi_j^(order)(x[b,i]) (O, nf, I) and, when dbase
+ *                             is given, dbase[o,i] = sum_b g[b,o,i] s(x[b,i]), s = silu^(order) from silu_poly;
+ *                             summed over row splits in a fixed order through `workspace`
+ *                             (kf_edge_derivative_workspace floats).
+ * The caller applies the fold (Chebyshev, Fourier) and edge_scale / edge_mask chain rule. */
+int kf_edge_derivative_dx(const float* x, const float* g, const float* coefT, const float* base_eff, const float* grid,
+                          const float* basis_num, const float* basis_den, float* dx, int64_t B, int32_t I, int32_t O,
+                          int32_t nf, int32_t order, const kf_basis_desc* basis, const float* silu_poly, int32_t n_poly,
+                          void* stream);
+int kf_edge_derivative_dcoef(const float* x, const float* g, const float* grid, const float* basis_num,
+                             const float* basis_den, float* dcoefT, float* dbase, float* workspace, int64_t B, int32_t I,
+                             int32_t O, int32_t nf, int32_t order, const kf_basis_desc* basis, const float* silu_poly,
+                             int32_t n_poly, void* stream);
+int64_t kf_edge_derivative_workspace(int64_t B, int32_t I, int32_t O, int32_t nf);
+
 /* KAT group rational activation and its order-m derivative, elementwise
  * (kanforge/bases/rational.py:84-101):  out[b,i] = R_g(i)^(m)(x[b,i]).
  * num (groups, p+1), den (groups, q) float32; x, out in `dtype`. */

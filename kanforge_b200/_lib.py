@@ -112,6 +112,17 @@ PROTOTYPES = {
         ctypes.c_int,
         [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, ctypes.POINTER(BasisDesc), _vp, _c_i32, _vp],
     ),
+    "kf_edge_derivative_dx": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, ctypes.POINTER(BasisDesc), _vp,
+         _c_i32, _vp],
+    ),
+    "kf_edge_derivative_dcoef": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, ctypes.POINTER(BasisDesc), _vp,
+         _c_i32, _vp],
+    ),
+    "kf_edge_derivative_workspace": (_c_i64, [_c_i64, _c_i32, _c_i32, _c_i32]),
     "kf_gemm_tf32x3": (
         ctypes.c_int,
         [_vp, _c_i32, _c_i64, _vp, _c_i32, _c_i64, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _vp],

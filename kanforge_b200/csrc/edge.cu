@@ -25,6 +25,7 @@ struct EdgeArgs {
   const float* num;    // rational: (groups, na)
   const float* den;    // rational: (groups, nb)
   float* out;
+  const float* g;      // backward: the output gradient (B, O, I)
   int64_t B;
   int I, O, nf, m;
   int kind, order;     // KF_BASIS_*, B-spline order
@@ -222,6 +223,112 @@ __global__ void __launch_bounds__(256) edge_scalar_kernel(EdgeArgs A) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Backward of edge_derivative (the reference's is an autograd graph,
+// kanforge/torch/layers.py:206-226): with g = dL/dout (B, O, I),
+//   dx[b,i]       = sum_o g[b,o,i] (sum_j phi_j^(m+1)(x) coefT1[o,j,i] + s_(m+1)(x) base[o,i])
+//   dcoefT[o,j,i] = sum_b g[b,o,i] phi_j^(m)(x[b,i]),   dbase[o,i] = sum_b g[b,o,i] s_m(x[b,i]).
+// Both read g once, lanes along i (a warp's load is one 128-byte line).
+// ---------------------------------------------------------------------------
+
+// dx: one thread per (b, i); A holds the order-(m+1) features, coefficients
+// and SiLU polynomials, A.out = dx (B, I).
+__global__ void __launch_bounds__(256) edge_dx_kernel(EdgeArgs A) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= A.B * A.I) return;
+  const int64_t b = e / A.I;
+  const int i = (int)(e % A.I);
+  float t[KF_NK_MAX];
+  load_knots_rt(A, i, t);
+  const float x = A.x[e];
+  float f[KF_NF_MAX];
+  edge_features_rt(A, i, x, t, f);
+  const float sb = A.base ? silu_deriv(x, A.m, A.poly, A.n_poly) : 0.0f;
+  float dx = 0.0f;
+  const float* gp = A.g + b * A.O * A.I + i;
+  for (int o = 0; o < A.O; ++o) {
+    float v = A.base ? sb * A.base[(size_t)o * A.I + i] : 0.0f;
+    const float* c = A.coef + (size_t)o * A.nf * A.I + i;
+    for (int j = 0; j < A.nf; ++j) v = fmaf(f[j], c[(size_t)j * A.I], v);
+    dx = fmaf(__ldcs(gp + (size_t)o * A.I), v, dx);
+  }
+  A.out[e] = dx;
+}
+
+// dcoefT / dbase partial sums: block (32 inputs) x (OC outputs) x (one of
+// gridDim.z row splits); warp w takes the split's rows w, w + 8, ...; each
+// thread keeps OC x NJ sums (NJ >= nf + 1: the features and the SiLU term),
+// the 8 warps add theirs in shared memory in a fixed order, and the block
+// writes ws[split][o][j][i] (j = nf: the base term).
+template <int NJ, int OC>
+__global__ void __launch_bounds__(256) edge_dcoef_kernel(EdgeArgs A, float* __restrict__ ws, int64_t rows_per_split) {
+  __shared__ float red[8][NJ][32];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int i = blockIdx.x * 32 + lane;
+  const int o0 = blockIdx.y * OC;
+  const int nj = A.nf + 1;
+  float acc[OC][NJ];
+#pragma unroll
+  for (int q = 0; q < OC; ++q)
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) acc[q][j] = 0.0f;
+  float t[KF_NK_MAX];
+  if (i < A.I) load_knots_rt(A, i, t);
+  const int64_t r0 = (int64_t)blockIdx.z * rows_per_split;
+  const int64_t r1 = min(A.B, r0 + rows_per_split);
+  if (i < A.I) {
+    for (int64_t b = r0 + warp; b < r1; b += 8) {
+      const float x = A.x[b * A.I + i];
+      float f[NJ];
+      edge_features_rt(A, i, x, t, f);
+      const float sterm = A.n_poly ? silu_deriv(x, A.m, A.poly, A.n_poly) : 0.0f;
+      const float* gp = A.g + (b * A.O + o0) * A.I + i;
+#pragma unroll
+      for (int q = 0; q < OC; ++q) {
+        if (o0 + q < A.O) {
+          const float gv = __ldcs(gp + (size_t)q * A.I);
+#pragma unroll
+          for (int j = 0; j < NJ; ++j)
+            if (j < nj) acc[q][j] = fmaf(gv, j < A.nf ? f[j] : sterm, acc[q][j]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < OC; ++q) {
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) red[warp][j][lane] = acc[q][j];
+    __syncthreads();
+    for (int e = threadIdx.x; e < NJ * 32; e += 256) {
+      const int l = e % 32, j = e / 32;
+      const int ii = blockIdx.x * 32 + l;
+      if (ii < A.I && o0 + q < A.O && j < nj) {
+        float sum = 0.0f;
+        for (int w = 0; w < 8; ++w) sum += red[w][j][l];
+        ws[(((size_t)blockIdx.z * A.O + o0 + q) * nj + j) * A.I + ii] = sum;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// Sum of the splits in order: dcoefT[o,j,i] (j < nf) and dbase[o,i] (j = nf).
+__global__ void __launch_bounds__(256) edge_dcoef_reduce_kernel(const float* __restrict__ ws, float* __restrict__ dcoefT,
+                                                                float* __restrict__ dbase, int splits, int O, int nf, int I) {
+  const int nj = nf + 1;
+  const int64_t n = (int64_t)O * nj * I;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
+    float sum = 0.0f;
+    for (int z = 0; z < splits; ++z) sum += ws[(size_t)z * n + e];
+    const int i = (int)(e % I);
+    const int64_t oj = e / I;
+    const int j = (int)(oj % nj);
+    const int64_t o = oj / nj;
+    if (j < nf) dcoefT[(o * nf + j) * I + i] = sum;
+    else if (dbase) dbase[o * I + i] = sum;
+  }
+}
+
 template <int NF>
 int launch_vec(const EdgeArgs& A, cudaStream_t stream) {
   constexpr int NB = edge_rows(NF);
@@ -278,20 +385,22 @@ int launch_edge(const EdgeArgs& A, bool vec, cudaStream_t stream) {
 
 }  // namespace kf
 
-extern "C" int kf_edge_derivative(const float* x, const float* coefT, const float* base_eff, const float* grid,
-                                  const float* basis_num, const float* basis_den, float* out, int64_t B, int32_t I,
-                                  int32_t O, int32_t nf, int32_t order, const kf_basis_desc* basis,
-                                  const float* silu_poly, int32_t n_poly, void* stream) {
-  using namespace kf;
-  clear_error();
+namespace kf {
+namespace {
+// EdgeArgs of an edge-derivative launch (shared by the forward and backward
+// entry points); coefT may be null where the launch reads no coefficients.
+int fill_edge_args(EdgeArgs& A, const float* x, const float* coefT, const float* base_eff, const float* grid,
+                   const float* basis_num, const float* basis_den, float* out, int64_t B, int32_t I, int32_t O,
+                   int32_t nf, int32_t order, const kf_basis_desc* basis, const float* silu_poly, int32_t n_poly,
+                   bool need_coef) {
   KF_CHECK_ARG(basis != nullptr, "kf_edge_derivative: basis is null");
   KF_CHECK_ARG(B >= 0 && I >= 1 && O >= 1 && nf >= 1 && order >= 0, "kf_edge_derivative: bad sizes");
   KF_CHECK_ARG(nf <= KF_NF_MAX, "kf_edge_derivative: %d features exceed the limit %d", nf, KF_NF_MAX);
-  KF_CHECK_ARG(x && coefT && out, "kf_edge_derivative: null tensor pointer");
+  KF_CHECK_ARG(x && out && (coefT || !need_coef), "kf_edge_derivative: null tensor pointer");
   if (int rc = bind_device(x)) return rc;
   KF_CHECK_ARG(base_eff == nullptr || (silu_poly != nullptr && n_poly >= 1 && n_poly <= 8),
                "kf_edge_derivative: the base term needs 1..8 SiLU polynomial coefficients");
-  EdgeArgs A{};
+  A = EdgeArgs{};
   A.x = x;
   A.coef = coefT;
   A.base = base_eff;
@@ -308,7 +417,6 @@ extern "C" int kf_edge_derivative(const float* x, const float* coefT, const floa
   A.fa.m = order;
   A.fa.nf = nf;
   A.fa.map = basis->input_map;
-  if (B == 0) return KF_OK;
   if (basis->kind == KF_BASIS_RATIONAL) {
     KF_CHECK_ARG(basis_num && basis_den, "kf_edge_derivative: rational needs its parameters");
     KF_CHECK_ARG(nf == 1, "kf_edge_derivative: rational has one feature");
@@ -334,6 +442,94 @@ extern "C" int kf_edge_derivative(const float* x, const float* coefT, const floa
     set_error("kf_edge_derivative: basis kind %d unsupported", basis->kind);
     return KF_ERR_UNSUPPORTED;
   }
+  return KF_OK;
+}
+}  // namespace
+}  // namespace kf
+
+extern "C" int kf_edge_derivative(const float* x, const float* coefT, const float* base_eff, const float* grid,
+                                  const float* basis_num, const float* basis_den, float* out, int64_t B, int32_t I,
+                                  int32_t O, int32_t nf, int32_t order, const kf_basis_desc* basis,
+                                  const float* silu_poly, int32_t n_poly, void* stream) {
+  using namespace kf;
+  clear_error();
+  EdgeArgs A;
+  if (int rc = fill_edge_args(A, x, coefT, base_eff, grid, basis_num, basis_den, out, B, I, O, nf, order, basis, silu_poly,
+                              n_poly, true))
+    return rc;
+  if (B == 0) return KF_OK;
   const bool vec = nf <= kEdgeMaxNF;
   return launch_edge(A, vec, (cudaStream_t)stream);
+}
+
+namespace kf {
+namespace {
+// Row splits of the coefficient-gradient kernel: about four CTAs per SM.
+int edge_splits(int64_t B, int I, int O, int oc) {
+  const int64_t blocks = cdiv((int64_t)I, (int64_t)32) * cdiv((int64_t)O, (int64_t)oc);
+  return (int)std::max<int64_t>(1, std::min<int64_t>(cdiv((int64_t)148 * 4, blocks), cdiv(B, (int64_t)64)));
+}
+int edge_oc(int nf) { return nf + 1 <= 10 ? 8 : (nf + 1 <= 17 ? 4 : 2); }
+}  // namespace
+}  // namespace kf
+
+extern "C" int64_t kf_edge_derivative_workspace(int64_t B, int32_t I, int32_t O, int32_t nf) {
+  if (B <= 0 || I <= 0 || O <= 0 || nf <= 0) return 0;
+  const int oc = kf::edge_oc(nf);
+  return (int64_t)kf::edge_splits(B, I, O, oc) * O * (nf + 1) * I;
+}
+
+extern "C" int kf_edge_derivative_dx(const float* x, const float* g, const float* coefT, const float* base_eff,
+                                     const float* grid, const float* basis_num, const float* basis_den, float* dx,
+                                     int64_t B, int32_t I, int32_t O, int32_t nf, int32_t order,
+                                     const kf_basis_desc* basis, const float* silu_poly, int32_t n_poly, void* stream) {
+  using namespace kf;
+  clear_error();
+  KF_CHECK_ARG(g != nullptr, "kf_edge_derivative_dx: null gradient");
+  EdgeArgs A;
+  if (int rc = fill_edge_args(A, x, coefT, base_eff, grid, basis_num, basis_den, dx, B, I, O, nf, order, basis, silu_poly,
+                              n_poly, true))
+    return rc;
+  if (B == 0) return KF_OK;
+  A.g = g;
+  const int64_t n = B * (int64_t)I;
+  edge_dx_kernel<<<(unsigned)cdiv(n, (int64_t)256), 256, 0, (cudaStream_t)stream>>>(A);
+  return check_launch("kf_edge_derivative_dx");
+}
+
+extern "C" int kf_edge_derivative_dcoef(const float* x, const float* g, const float* grid, const float* basis_num,
+                                        const float* basis_den, float* dcoefT, float* dbase, float* workspace, int64_t B,
+                                        int32_t I, int32_t O, int32_t nf, int32_t order, const kf_basis_desc* basis,
+                                        const float* silu_poly, int32_t n_poly, void* stream) {
+  using namespace kf;
+  clear_error();
+  KF_CHECK_ARG(g && dcoefT, "kf_edge_derivative_dcoef: null tensor pointer");
+  KF_CHECK_ARG(dbase == nullptr || (silu_poly != nullptr && n_poly >= 1 && n_poly <= 8),
+               "kf_edge_derivative_dcoef: the base gradient needs 1..8 SiLU polynomial coefficients");
+  EdgeArgs A;
+  if (int rc = fill_edge_args(A, x, nullptr, nullptr, grid, basis_num, basis_den, dcoefT, B, I, O, nf, order, basis,
+                              nullptr, 0, false))
+    return rc;
+  A.g = g;
+  A.n_poly = dbase ? n_poly : 0;
+  for (int e = 0; e < 2 * A.n_poly; ++e) A.poly[e] = silu_poly[e];
+  cudaStream_t s = (cudaStream_t)stream;
+  if (B == 0) {
+    KF_CUDA_RET(cudaMemsetAsync(dcoefT, 0, sizeof(float) * (size_t)O * nf * I, s));
+    if (dbase) KF_CUDA_RET(cudaMemsetAsync(dbase, 0, sizeof(float) * (size_t)O * I, s));
+    return KF_OK;
+  }
+  KF_CHECK_ARG(workspace != nullptr, "kf_edge_derivative_dcoef: null workspace (kf_edge_derivative_workspace floats)");
+  const int oc = edge_oc(nf);
+  const int splits = edge_splits(B, I, O, oc);
+  const int64_t rows = cdiv(B, (int64_t)splits);
+  const dim3 grid3((unsigned)cdiv((int64_t)I, (int64_t)32), (unsigned)cdiv((int64_t)O, (int64_t)oc), (unsigned)splits);
+  if (nf + 1 <= 10) edge_dcoef_kernel<10, 8><<<grid3, 256, 0, s>>>(A, workspace, rows);
+  else if (nf + 1 <= 17) edge_dcoef_kernel<17, 4><<<grid3, 256, 0, s>>>(A, workspace, rows);
+  else edge_dcoef_kernel<KF_NF_MAX + 1, 2><<<grid3, 256, 0, s>>>(A, workspace, rows);
+  if (int rc = check_launch("kf_edge_derivative_dcoef")) return rc;
+  const int64_t n = (int64_t)O * (nf + 1) * I;
+  const unsigned blocks = (unsigned)std::max<int64_t>(1, std::min<int64_t>(cdiv(n, (int64_t)256), 148 * 8));
+  edge_dcoef_reduce_kernel<<<blocks, 256, 0, s>>>(workspace, dcoefT, dbase, splits, O, nf, I);
+  return check_launch("kf_edge_derivative_dcoef");
 }

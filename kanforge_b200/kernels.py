@@ -580,32 +580,99 @@ def kan_linear_tf32(x, coef, base_weight, bias, edge_scale, edge_mask, grid, pla
 # --- edge_derivative ---------------------------------------------------------
 
 
+def _silu_polys(order: int):
+    """(ctypes float array, n): silu^(order) as [h_m, h_{m-1}] polynomials in sigmoid."""
+    polys = silu_derivative_polys(order).astype("float32").ravel()
+    return (ctypes.c_float * polys.size)(*polys.tolist()), polys.size // 2
+
+
+def _edge_coef(coef_eff: torch.Tensor, plan: KernelPlan, order: int) -> torch.Tensor:
+    """(O, nf, I) float32 coefficients of the order-`order` features: folded
+    into the kernel features for Chebyshev / Fourier plans."""
+    c = coef_eff.detach().float()
+    if plan.folded:
+        c = c @ _fold_on(plan, order, c.device)
+    return c.permute(0, 2, 1).contiguous()
+
+
+class _EdgeDerivative(torch.autograd.Function):
+    """out[b,o,i] = d^m/dx^m (phi_oi(x_i) + W_eff[o,i] silu(x_i)) (kanforge/torch/layers.py:206-226),
+    differentiable in x, the effective coefficients and the base weight like
+    the reference's autograd graph: dx from the order-(m+1) edges contracted
+    with the output gradient (kf_edge_derivative_dx), the coefficient and base
+    gradients from the order-m features (kf_edge_derivative_dcoef)."""
+
+    @staticmethod
+    def forward(ctx, x2, coef_eff, base_eff, num, den, grid, plan, order, groups):
+        n_out, n_in, _ = coef_eff.shape
+        coef_c = _edge_coef(coef_eff, plan, order)
+        base = None if base_eff is None else base_eff.detach().float().contiguous()
+        g = None if grid is None else grid.detach().float().contiguous()
+        numf = None if num is None else num.detach().float().contiguous()
+        denf = None if den is None else den.detach().float().contiguous()
+        poly_buf, n_poly = _silu_polys(order)
+        out = torch.empty(x2.shape[0], n_out, n_in, device=x2.device, dtype=torch.float32)
+        desc = plan.desc(groups)
+        _launch("kf_edge_derivative", _ptr(x2), _ptr(coef_c), _ptr(base), _ptr(g), _ptr(numf), _ptr(denf), _ptr(out),
+                x2.shape[0], n_in, n_out, coef_c.shape[1], order, ctypes.byref(desc), ctypes.cast(poly_buf, ctypes.c_void_p),
+                n_poly, _stream(x2))
+        ctx.save_for_backward(x2, coef_eff, base_eff)
+        ctx.extra = (numf, denf, g, plan, order, groups)
+        return out
+
+    @staticmethod
+    def backward(ctx, gout):
+        x2, coef_eff, base_eff = ctx.saved_tensors
+        numf, denf, g, plan, order, groups = ctx.extra
+        need = ctx.needs_input_grad
+        if need[3] or need[4]:
+            raise NotImplementedError("gradients of edge derivatives into the rational parameters are not available")
+        gout = gout.float().contiguous()
+        n_b, n_in = x2.shape
+        n_out = coef_eff.shape[0]
+        desc = plan.desc(groups)
+        stream = _stream(x2)
+        dx = dcoef = dbase = None
+        if need[0]:
+            coef1 = _edge_coef(coef_eff, plan, order + 1)
+            base = None if base_eff is None else base_eff.detach().float().contiguous()
+            poly_buf, n_poly = _silu_polys(order + 1)
+            dx = torch.empty_like(x2)
+            _launch("kf_edge_derivative_dx", _ptr(x2), _ptr(gout), _ptr(coef1), _ptr(base), _ptr(g), _ptr(numf), _ptr(denf),
+                    _ptr(dx), n_b, n_in, n_out, coef1.shape[1], order + 1, ctypes.byref(desc),
+                    ctypes.cast(poly_buf, ctypes.c_void_p), n_poly, stream)
+        if need[1] or need[2]:
+            nf = plan.n_features(order) if plan.kind != "rational" else 1
+            dct = torch.empty(n_out, nf, n_in, device=x2.device, dtype=torch.float32)
+            db = torch.empty(n_out, n_in, device=x2.device, dtype=torch.float32) if (need[2] and base_eff is not None) else None
+            ws_n = int(_lib.load().kf_edge_derivative_workspace(n_b, n_in, n_out, nf))
+            ws = torch.empty(max(ws_n, 1), device=x2.device, dtype=torch.float32)
+            poly_buf, n_poly = _silu_polys(order)
+            _launch("kf_edge_derivative_dcoef", _ptr(x2), _ptr(gout), _ptr(g), _ptr(numf), _ptr(denf), _ptr(dct), _ptr(db),
+                    _ptr(ws), n_b, n_in, n_out, nf, order, ctypes.byref(desc), ctypes.cast(poly_buf, ctypes.c_void_p),
+                    n_poly, stream, kernels=2)
+            if need[1]:
+                d = dct.permute(0, 2, 1)  # (O, I, nf)
+                if plan.folded:
+                    d = d @ _fold_on(plan, order, x2.device).T  # features -> basis functions
+                dcoef = d.to(coef_eff.dtype)
+            if db is not None:
+                dbase = db.to(base_eff.dtype)
+        return dx, dcoef, dbase, None, None, None, None, None, None
+
+
 def edge_derivative(x, coef_eff, base_eff, grid, plan: KernelPlan, order: int, basis_params: dict | None = None,
                     groups: int = 1) -> torch.Tensor:
-    """(B, O, I) d^m phi_oi / dx_i^m + silu^(m) W_eff, float32 (kanforge/torch/layers.py:206-226)."""
+    """(..., O, I) d^m phi_oi / dx_i^m + silu^(m) W_eff, float32 (kanforge/torch/layers.py:206-226);
+    differentiable in x, coef_eff and base_eff."""
     _check_cuda(x)
     lead = x.shape[:-1]
     x2 = x.reshape(-1, x.shape[-1]).float().contiguous()
-    n_out, n_in, _ = coef_eff.shape
-    c = coef_eff.detach().float()
     num = den = None
-    if plan.folded:
-        c = c @ _fold_on(plan, order, x.device)
-    elif plan.kind == "rational":
-        num = basis_params["numerator"].detach().float().contiguous()
-        den = basis_params["denominator"].detach().float().contiguous()
-    nf = c.shape[-1]
-    coef_c = c.permute(0, 2, 1).contiguous()  # (O, nf, I): the kernel's coalesced layout
-    base = None if base_eff is None else base_eff.detach().float().contiguous()
-    g = None if grid is None else grid.detach().float().contiguous()
-    polys = torch.as_tensor(silu_derivative_polys(order), dtype=torch.float32).flatten().contiguous()
-    out = torch.empty(x2.shape[0], n_out, n_in, device=x.device, dtype=torch.float32)
-    desc = plan.desc(groups)
-    poly_buf = (ctypes.c_float * polys.numel())(*polys.tolist())
-    _launch("kf_edge_derivative", _ptr(x2), _ptr(coef_c), _ptr(base), _ptr(g), _ptr(num), _ptr(den), _ptr(out),
-              x2.shape[0], n_in, n_out, nf, order, ctypes.byref(desc), ctypes.cast(poly_buf, ctypes.c_void_p),
-              polys.numel() // 2, _stream(x2))
-    return out.reshape(*lead, n_out, n_in)
+    if plan.kind == "rational":
+        num, den = basis_params["numerator"], basis_params["denominator"]
+    out = _EdgeDerivative.apply(x2, coef_eff, base_eff, num, den, grid, plan, order, groups)
+    return out.reshape(*lead, coef_eff.shape[0], coef_eff.shape[1])
 
 
 # --- KAT rational ------------------------------------------------------------

@@ -44,18 +44,6 @@ def _require_cuda(x: torch.Tensor) -> None:
         )
 
 
-class _EdgeDerivativeNoGrad(torch.autograd.Function):
-    """Marks a kernel-computed edge derivative as non-differentiable, loudly."""
-
-    @staticmethod
-    def forward(ctx, out, *inputs):
-        return out
-
-    @staticmethod
-    def backward(ctx, *grads):
-        raise NotImplementedError("backward through KANLinear.edge_derivative is not available; use autograd on forward")
-
-
 @dataclass(frozen=True)
 class LayerOptions:
     """The constructor choices a layer keeps for re-initialisation and export
@@ -290,10 +278,7 @@ class KANLinear(nn.Module):
         if plan.kind == "rational":
             params = {"numerator": self.basis_numerator, "denominator": self.basis_denominator}
         out = _kernels.edge_derivative(x, coef_eff, base_eff, self._grid(), plan, order, params, self.groups)
-        out = out.to(x.dtype) if x.dtype != torch.float32 else out
-        if torch.is_grad_enabled() and (x.requires_grad or any(p.requires_grad for p in self.parameters())):
-            out = _EdgeDerivativeNoGrad.apply(out, x)
-        return out
+        return out.to(x.dtype) if x.dtype != torch.float32 else out
 
     # --- state export / import (.npz layout, layers.py:230-267) -----------------
 
