@@ -18,6 +18,9 @@
  *   kanforge/torch/layers.py:206-226   edge_derivative        -> kf_edge_derivative
  *   kanforge/bases/rational.py:84-101  Rational._eval (GRKAN) -> kf_rational_act,
  *                                                               kf_rational_bwd
+ *   kanforge/grid.py:19-31             adaptive_grid          -> kf_adaptive_grid
+ *   kanforge/grid.py:34-38             resample_grid          -> kf_resample_grid
+ *   kanforge/grid.py:55-85             refit                  -> kf_refit
  */
 #ifndef KANFORGE_B200_H
 #define KANFORGE_B200_H
@@ -366,6 +369,78 @@ int kf_conv_wgrad(const void* img, const kf_conv_geom* geom, const void* feat, c
 #define KF_RATIONAL_NOALLOC_MAX_FLOATS (1 << 20)
 int kf_rational_bwd_noalloc(const void* x, const void* dr, const float* num, const float* den, void* dx, float* dnum,
                             float* dden, int64_t B, int32_t I, const kf_basis_desc* basis, int dtype, void* stream);
+
+/* ---- grid tools (kanforge/grid.py:19-85; kanforge/_layer.py:107-183) -------
+ * GridToolsMixin.update_grid / refine_grid / change_basis run on the device:
+ * the samples never leave it and the (samples x inputs x outputs) refit
+ * targets are never formed. */
+
+#define KF_GRID_MAX_POINTS 192 /* grid points per input of kf_adaptive_grid */
+#define KF_FIT_MAX_SIZE 64     /* basis functions per edge of kf_refit (old and new) */
+
+/* Samples x (n, I) row-major in `dtype` -> xt (I, n) float32, one column per
+ * input: the sample layout of kf_adaptive_grid and kf_refit. */
+int kf_samples_transpose(const void* x, int dtype, int64_t n, int32_t I, float* xt, void* stream);
+
+/* Bytes of workspace kf_adaptive_grid needs. */
+int64_t kf_grid_workspace(int64_t n, int32_t I, int32_t n_points);
+
+/* Per-input adaptive grids (I, n_points) float64 from the samples xt (I, n)
+ * (kanforge/grid.py:19-31, pykan's update_grid_from_samples):
+ *   q_t   = the sample of rank round(linspace(0, n-1, n_points)[t]) (halves to even)
+ *   u_t   = lo + (hi - lo) t / (n_points - 1),  lo = min - margin, hi = max + margin
+ *           (hi - lo < 1e-8: lo -= 0.5, hi += 0.5 and q = u)
+ *   grid  = grid_eps u + (1 - grid_eps) q
+ * Equal to the reference's float64 result on the same float32 samples.  NaN
+ * samples sort last.  2 <= n_points <= KF_GRID_MAX_POINTS, n >= 1,
+ * 0 < grid_eps <= 1. */
+int kf_adaptive_grid(const float* xt, int64_t n, int32_t I, int32_t n_points, double margin, double grid_eps,
+                     double* grid, void* workspace, void* stream);
+
+/* out (I, n_new) = np.interp(linspace(0, 1, n_new), linspace(0, 1, n_old), grid[i])
+ * for every row of grid (I, n_old), float64 (kanforge/grid.py:34-38). */
+int kf_resample_grid(const double* grid, int32_t I, int32_t n_old, int32_t n_new, double* out, void* stream);
+
+/* A basis as kf_refit evaluates it (order 0, float64).  Constants are the
+ * reference's float64 values (kf_basis_desc holds float32 copies). */
+typedef struct kf_fit_basis {
+  int32_t kind;        /* KF_BASIS_BSPLINE, KF_BASIS_CHEB, KF_BASIS_FOURIER, KF_BASIS_BUMP */
+  int32_t size;        /* basis functions per edge, <= KF_FIT_MAX_SIZE */
+  int32_t order;       /* B-spline order k */
+  int32_t degree;      /* Chebyshev: features T_0..T_degree; Fourier: frequencies */
+  int32_t input_map;   /* Chebyshev: KF_MAP_* */
+  int32_t bump_mode;   /* bumps: KF_BUMP_* */
+  int32_t n_grid;      /* B-spline: G + 1 grid points; bumps: count; else 0 */
+  int32_t n_poly;      /* bumps: coefficients in poly */
+  const double* grid;  /* (I, n_grid) per-input grid / centres (device), or null */
+  const double* fold;  /* Chebyshev: (size, degree + 1), phi_k = sum_j fold[k, j] T_j (device) */
+  double freq;         /* Fourier: 2 pi / period */
+  double u_scale;      /* gauss bumps */
+  double norm;         /* gauss bumps */
+  double poly[8];      /* bumps: order-0 polynomial, lowest coefficient first */
+} kf_fit_basis;
+
+/* Bytes of workspace kf_refit needs. */
+int64_t kf_refit_workspace(int64_t n, int32_t I, int32_t k_old, int32_t k_new);
+
+/* Refit of a layer onto `new_basis` (kanforge/grid.py:55-85 refit and
+ * kanforge/_layer.py:120-137 _refit_to):
+ *   samples  xt (I, n) float32 (kf_samples_transpose), or, with xt null,
+ *            n evenly spaced points per input over ranges (I, 2) float64
+ *            (grid.py:49-52 sample_inputs);
+ *   targets  the old edge functions sum_k c_eff[o,i,k] phi_k(x), c_eff = coef * edge_scale;
+ *   solution per input the least-squares coefficients in the new basis,
+ *            minimum-norm where the samples leave them undetermined
+ *            (eigenvalues of the Gram matrix below 1e-13 of the largest are
+ *            dropped); ridge > 0 adds ridge * mean(phi_new^2) * n to the Gram
+ *            diagonal (the reference's appended damping rows);
+ *   outputs  coef_out (O, I, new size) = solution / s and scale_out (O, I) = s,
+ *            s = edge_scale where |edge_scale| > 1e-12 else 1, float64.
+ * coef (O, I, old size) and edge_scale (O, I, or null) in `dtype`; scale_out
+ * is written when edge_scale is given.  Deterministic. */
+int kf_refit(const float* xt, const double* ranges, int64_t n, int32_t I, int32_t O, const kf_fit_basis* old_basis,
+             const kf_fit_basis* new_basis, const void* coef, const void* edge_scale, int dtype, double ridge,
+             double* coef_out, double* scale_out, void* workspace, void* stream);
 
 #ifdef __cplusplus
 }

@@ -50,10 +50,12 @@ class BasisState:
 
 
 def _uniform_grids(ranges, n_inputs: int, n_knots: int) -> np.ndarray:
-    """(n_inputs, n_knots) knots spread evenly over each input's [lo, hi]."""
+    """(n_inputs, n_knots) knots spread evenly over each input's [lo, hi]:
+    lo + (hi - lo) t, t = linspace(0, 1, n_knots), the reference's rounding
+    (kanforge/_layer.py:40-42)."""
     lo_hi = np.broadcast_to(np.asarray(ranges, dtype=np.float64), (n_inputs, 2))
     frac = np.linspace(0.0, 1.0, n_knots)
-    return lo_hi[:, 0:1] * (1.0 - frac) + lo_hi[:, 1:2] * frac
+    return lo_hi[:, 0:1] + (lo_hi[:, 1:2] - lo_hi[:, 0:1]) * frac
 
 
 def initial_basis_state(basis: Basis, groups: int, in_features: int, grid_ranges=None) -> BasisState:

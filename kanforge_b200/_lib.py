@@ -60,7 +60,32 @@ class ConvGeom(ctypes.Structure):
     ]
 
 
+class FitBasis(ctypes.Structure):
+    """``kf_fit_basis`` (include/kanforge_b200.h): a basis as the refit evaluates it."""
+
+    _fields_ = [
+        ("kind", _c_i32),
+        ("size", _c_i32),
+        ("order", _c_i32),
+        ("degree", _c_i32),
+        ("input_map", _c_i32),
+        ("bump_mode", _c_i32),
+        ("n_grid", _c_i32),
+        ("n_poly", _c_i32),
+        ("grid", _vp),
+        ("fold", _vp),
+        ("freq", ctypes.c_double),
+        ("u_scale", ctypes.c_double),
+        ("norm", ctypes.c_double),
+        ("poly", ctypes.c_double * 8),
+    ]
+
+
+KF_GRID_MAX_POINTS, KF_FIT_MAX_SIZE = 192, 64
+
 _GEOM = ctypes.POINTER(ConvGeom)
+_FIT = ctypes.POINTER(FitBasis)
+_f64 = ctypes.c_double
 
 # name -> (restype, argtypes)
 PROTOTYPES = {
@@ -153,6 +178,15 @@ PROTOTYPES = {
     "kf_grkan_workspace": (_c_i64, [_c_i64, _c_i32, ctypes.POINTER(BasisDesc)]),
     "kf_grkan_wgrad_workspace": (_c_i64, [_c_i64, _c_i32, _c_i32]),
     "kf_grkan_wgrad": (ctypes.c_int, [_vp, _vp, _vp, _vp, _c_i64, _c_i32, _c_i32, _vp]),
+    "kf_samples_transpose": (ctypes.c_int, [_vp, ctypes.c_int, _c_i64, _c_i32, _vp, _vp]),
+    "kf_grid_workspace": (_c_i64, [_c_i64, _c_i32, _c_i32]),
+    "kf_adaptive_grid": (ctypes.c_int, [_vp, _c_i64, _c_i32, _c_i32, _f64, _f64, _vp, _vp, _vp]),
+    "kf_resample_grid": (ctypes.c_int, [_vp, _c_i32, _c_i32, _c_i32, _vp, _vp]),
+    "kf_refit_workspace": (_c_i64, [_c_i64, _c_i32, _c_i32, _c_i32]),
+    "kf_refit": (
+        ctypes.c_int,
+        [_vp, _vp, _c_i64, _c_i32, _c_i32, _FIT, _FIT, _vp, _vp, ctypes.c_int, _f64, _vp, _vp, _vp, _vp],
+    ),
     "kf_rational_bwd_noalloc": (
         ctypes.c_int,
         [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i32, ctypes.POINTER(BasisDesc), ctypes.c_int, _vp],

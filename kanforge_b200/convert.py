@@ -5,6 +5,14 @@ string ``{"format": 1, "source": ..., "model": spec}``.  Files written by the
 reference load here and files written here load in the reference, for the
 layer types of the hot path: ``KANLinear``, ``GRKAN``, ``KAN`` and sequences of
 those with ``Linear`` layers and standard activations.
+
+Arrays are float64 in the file, as the reference writes them.  Device
+parameters move in one batch: ``save`` widens every tensor to float64 on the
+GPU and copies all of them into one pinned host buffer with asynchronous
+copies and a single synchronisation; ``load(..., device=cuda)`` gathers the
+file's arrays into one pinned buffer, sends it with one copy and narrows each
+array to its parameter's dtype on the GPU.  No per-tensor pageable copies and
+no float64 casts on the CPU.
 """
 
 from __future__ import annotations
@@ -63,6 +71,55 @@ def _dtype_name(t: torch.Tensor) -> str:
     return str(t.dtype).replace("torch.", "")
 
 
+def _host_float64(tensors: dict[str, torch.Tensor]) -> dict[str, np.ndarray]:
+    """float64 NumPy copies of tensors; CUDA tensors are widened on their device
+    and land in one pinned buffer per device after a single synchronisation."""
+    out: dict[str, np.ndarray] = {}
+    by_device: dict[torch.device, list[str]] = {}
+    for name, t in tensors.items():
+        if t.device.type == "cuda":
+            by_device.setdefault(t.device, []).append(name)
+        else:
+            out[name] = t.detach().to(torch.float64).numpy().copy()
+    for device, names in by_device.items():
+        total = sum(tensors[n].numel() for n in names)
+        staging = torch.empty(total, dtype=torch.float64, pin_memory=True)
+        stream = torch.cuda.Stream(device)
+        stream.wait_stream(torch.cuda.current_stream(device))
+        views, at = {}, 0
+        with torch.cuda.stream(stream):
+            for n in names:
+                t = tensors[n].detach()
+                k = t.numel()
+                wide = t.to(torch.float64).reshape(-1)
+                staging[at:at + k].copy_(wide, non_blocking=True)
+                wide.record_stream(stream)
+                views[n] = (at, k, tuple(t.shape))
+                at += k
+        stream.synchronize()
+        host = staging.numpy()
+        for n, (a, k, shape) in views.items():
+            out[n] = host[a:a + k].reshape(shape)
+    return out
+
+
+def _device_float64(arrays: dict[str, np.ndarray], device: torch.device) -> dict[str, torch.Tensor]:
+    """The arrays as float64 tensors on a CUDA device: one pinned staging buffer,
+    one host-to-device copy."""
+    names = list(arrays)
+    total = sum(int(np.asarray(arrays[n]).size) for n in names)
+    staging = torch.empty(total, dtype=torch.float64, pin_memory=True)
+    host = staging.numpy()
+    views, at = {}, 0
+    for n in names:
+        a = np.asarray(arrays[n], dtype=np.float64)
+        host[at:at + a.size] = a.reshape(-1)
+        views[n] = (at, a.size, a.shape)
+        at += a.size
+    dev = staging.to(device, non_blocking=True)
+    return {n: dev[a:a + k].view(shape) for n, (a, k, shape) in views.items()}
+
+
 def _layer_spec(layer: KANLinear):
     opt = layer.options
     spec = {
@@ -78,31 +135,33 @@ def _layer_spec(layer: KANLinear):
         "backend": opt.backend,
         "dtype": _dtype_name(layer.coef),
     }
-    return spec, {k: v for k, v in layer._export_full().items() if v is not None}
+    own = {**dict(layer.named_parameters(recurse=False)), **dict(layer.named_buffers(recurse=False))}
+    return spec, own
 
 
 def to_spec(model):
-    """(spec, arrays) of a model."""
-    arrays: dict[str, np.ndarray] = {}
+    """(spec, arrays) of a model, arrays float64 NumPy (convert.py:141-172)."""
+    tensors: dict[str, torch.Tensor] = {}
 
     def walk(m, prefix):
         if isinstance(m, KANLinear):
-            spec, arr = _layer_spec(m)
-            arrays.update({prefix + k: v for k, v in arr.items()})
+            spec, own = _layer_spec(m)
+            tensors.update({prefix + k: v for k, v in own.items()})
             return spec
         if isinstance(m, KAN):
             return {"type": "KAN", "widths": list(m.widths), "layers": [walk(c, f"{prefix}{k}.") for k, c in enumerate(m)]}
         if isinstance(m, nn.Sequential):
             return {"type": "Sequential", "layers": [walk(c, f"{prefix}{k}.") for k, c in enumerate(m)]}
         if isinstance(m, nn.Linear):
-            arrays[prefix + "weight"] = m.weight.detach().cpu().double().numpy()
+            tensors[prefix + "weight"] = m.weight
             if m.bias is not None:
-                arrays[prefix + "bias"] = m.bias.detach().cpu().double().numpy()
+                tensors[prefix + "bias"] = m.bias
             return {"type": "Linear", "in": m.in_features, "out": m.out_features, "bias": m.bias is not None,
                     "dtype": _dtype_name(m.weight)}
         return {"type": "Activation", "name": activation_name(m)}
 
-    return walk(model, ""), arrays
+    spec = walk(model, "")
+    return spec, _host_float64(tensors)
 
 
 class _Lambda(nn.Module):
@@ -114,22 +173,23 @@ class _Lambda(nn.Module):
         return self.fn(x)
 
 
-def _build(spec, arrays, prefix=""):
+def _build(spec, arrays, prefix="", device=None):
     t = spec["type"]
     if t in ("KANLinear", "GRKAN"):
         layer = KANLinear(
             spec["in"], spec["out"], spec["basis"], bias=spec["bias"], base_activation=make_activation(spec["base_activation"]),
             groups=spec["groups"], edge_scale=spec["edge_scale"], edge_dropout=spec["edge_dropout"],
-            backend=spec["backend"], dtype=getattr(torch, spec.get("dtype", "float32")),
+            backend=spec["backend"], dtype=getattr(torch, spec.get("dtype", "float32")), device=device,
         )
         state = {k[len(prefix):]: v for k, v in arrays.items() if k.startswith(prefix) and "." not in k[len(prefix):]}
         layer._import_full(state)
         return layer
     if t in ("KAN", "Sequential"):
-        children = [_build(c, arrays, f"{prefix}{k}.") for k, c in enumerate(spec["layers"])]
+        children = [_build(c, arrays, f"{prefix}{k}.", device) for k, c in enumerate(spec["layers"])]
         return rebuild_kan(children) if t == "KAN" else nn.Sequential(*children)
     if t == "Linear":
-        lin = nn.Linear(spec["in"], spec["out"], bias=spec["bias"], dtype=getattr(torch, spec.get("dtype", "float32")))
+        lin = nn.Linear(spec["in"], spec["out"], bias=spec["bias"], dtype=getattr(torch, spec.get("dtype", "float32")),
+                        device=device)
         with torch.no_grad():
             lin.weight.copy_(torch.as_tensor(arrays[prefix + "weight"]))
             if spec["bias"]:
@@ -141,8 +201,12 @@ def _build(spec, arrays, prefix=""):
     raise ValueError(f"layer type {t!r} is not part of the kanforge_b200 hot path")
 
 
-def from_spec(spec, arrays):
-    return _build(spec, arrays)
+def from_spec(spec, arrays, device=None):
+    """The model of ``spec`` with ``arrays`` loaded, on ``device`` (default CPU)."""
+    device = None if device is None else torch.device(device)
+    if device is not None and device.type == "cuda":
+        arrays = _device_float64(arrays, device)
+    return _build(spec, arrays, device=device)
 
 
 def save(model, path) -> None:
@@ -151,11 +215,12 @@ def save(model, path) -> None:
     np.savez(path, __spec__=np.array(json.dumps({"format": 1, "source": "torch", "model": spec})), **arrays)
 
 
-def load(path, backend: str = "torch"):
-    """Load a file written by ``save`` here or by the reference (convert.py:319-325)."""
+def load(path, backend: str = "torch", device=None):
+    """Load a file written by ``save`` here or by the reference (convert.py:319-325),
+    onto ``device`` (default CPU, like the reference)."""
     if backend != "torch":
         raise ValueError("kanforge_b200 loads models for torch only")
     with np.load(path, allow_pickle=False) as data:
         meta = json.loads(str(data["__spec__"]))
         arrays = {k: data[k] for k in data.files if k != "__spec__"}
-    return from_spec(meta["model"], arrays)
+    return from_spec(meta["model"], arrays, device)

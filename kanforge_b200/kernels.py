@@ -17,6 +17,7 @@ from __future__ import annotations
 
 import ctypes
 import functools
+import math
 
 import torch
 
@@ -852,6 +853,112 @@ class _GRKANLinear(torch.autograd.Function):
 def grkan_linear(x2, num, den, w, bias, plan, groups, path):
     """GR-KAN layer on (B, I) inputs; see ``_GRKANLinear``."""
     return _GRKANLinear.apply(x2, num, den, w, bias, plan, groups, path)
+
+
+# --- grid tools (kanforge/grid.py, kanforge/_layer.py:107-183) ----------------
+
+
+def sample_columns(x2: torch.Tensor) -> torch.Tensor:
+    """Samples (n, I) -> (I, n) float32, one column per input (kf_samples_transpose)."""
+    _check_cuda(x2)
+    x2 = x2.contiguous()
+    if x2.dtype not in (torch.float32, _BF16):
+        x2 = x2.float()
+    n, n_in = x2.shape
+    xt = torch.empty(n_in, n, device=x2.device, dtype=torch.float32)
+    _launch("kf_samples_transpose", _ptr(x2), _rat_dtype(x2), n, n_in, _ptr(xt), _stream(x2))
+    return xt
+
+
+def _bytes(n: int, device) -> torch.Tensor:
+    return torch.empty(max(int(n), 16), dtype=torch.uint8, device=device)
+
+
+def adaptive_grid(xt: torch.Tensor, n_points: int, margin: float = 0.0, grid_eps: float = 0.02) -> torch.Tensor:
+    """Per-input adaptive grids (I, n_points) float64 from sample columns xt (I, n)
+    (kanforge/grid.py:19-31), equal to the reference's float64 grid."""
+    if not 0 < grid_eps <= 1:
+        raise ValueError("grid_eps must be in (0, 1]: some uniform part keeps the grid increasing")
+    n_in, n = xt.shape
+    if n < 1:
+        raise ValueError("adaptive_grid needs at least one sample")
+    if not 2 <= n_points <= _lib.KF_GRID_MAX_POINTS:
+        raise ValueError(f"grids of {n_points} points are outside [2, {_lib.KF_GRID_MAX_POINTS}]")
+    ws = _bytes(_lib.load().kf_grid_workspace(n, n_in, n_points), xt.device)
+    grid = torch.empty(n_in, n_points, dtype=torch.float64, device=xt.device)
+    _launch("kf_adaptive_grid", _ptr(xt), n, n_in, n_points, float(margin), float(grid_eps), _ptr(grid), _ptr(ws),
+            _stream(xt), kernels=8)
+    return grid
+
+
+def resample_grid(grid: torch.Tensor, n_points: int) -> torch.Tensor:
+    """Rows of grid (I, n) linearly interpolated to n_points (kanforge/grid.py:34-38), float64."""
+    _check_cuda(grid)
+    g = grid.detach().to(torch.float64).contiguous()
+    out = torch.empty(g.shape[0], n_points, dtype=torch.float64, device=g.device)
+    _launch("kf_resample_grid", _ptr(g), g.shape[0], g.shape[1], n_points, _ptr(out), _stream(g))
+    return out
+
+
+def fit_basis(plan: KernelPlan, grid: torch.Tensor | None, device) -> tuple[_lib.FitBasis, list]:
+    """The ``kf_fit_basis`` of a plan (float64 constants) and the tensors it points to."""
+    b = _lib.FitBasis()
+    keep = []
+    b.size = plan.size
+    if plan.size > _lib.KF_FIT_MAX_SIZE:
+        raise ValueError(f"refit handles bases of up to {_lib.KF_FIT_MAX_SIZE} functions per edge, not {plan.size}")
+    if plan.kind in ("bspline", "bump"):
+        g = grid.detach().to(torch.float64).contiguous()
+        keep.append(g)
+        b.grid = g.data_ptr()
+        b.n_grid = g.shape[-1]
+    if plan.kind == "bspline":
+        b.kind = _lib.KF_BASIS_BSPLINE
+        b.order = plan.consts[1]
+    elif plan.kind == "cheb":
+        b.kind = _lib.KF_BASIS_CHEB
+        b.degree = plan.consts[0]
+        b.input_map = _lib.KF_MAP_TANH if plan.consts[1] == "tanh" else _lib.KF_MAP_IDENTITY
+        fold = torch.tensor(plan.fold(0), dtype=torch.float64, device=device)
+        keep.append(fold)
+        b.fold = fold.data_ptr()
+    elif plan.kind == "fourier":
+        b.kind = _lib.KF_BASIS_FOURIER
+        n, period = plan.consts
+        b.degree = n
+        b.freq = 2 * math.pi / period
+    elif plan.kind == "bump":
+        b.kind = _lib.KF_BASIS_BUMP
+        mode, _count, u_scale, norm, _p = plan.consts
+        b.bump_mode = _lib.KF_BUMP_GAUSS if mode == "gauss" else _lib.KF_BUMP_TANH
+        b.u_scale, b.norm = float(u_scale), float(norm)
+        poly = [float(v) for v in plan.bump_poly(0)]
+        b.n_poly = len(poly)
+        for j, v in enumerate(poly):
+            b.poly[j] = v
+    else:
+        raise NotImplementedError(f"no refit for {plan.kind} bases")
+    return b, keep
+
+
+def refit(xt, ranges, n: int, old: _lib.FitBasis, new: _lib.FitBasis, coef: torch.Tensor, edge_scale, ridge: float):
+    """(coef_out (O, I, new size), scale_out (O, I) or None), float64: the refit of
+    kanforge/grid.py:55-85 and the edge_scale handling of kanforge/_layer.py:120-137.
+    Samples are the columns xt (I, n), or n points per input over ranges (I, 2)."""
+    coef = coef.detach().contiguous()
+    if coef.dtype not in (torch.float32, _BF16):
+        coef = coef.float()
+    scale = None if edge_scale is None else edge_scale.detach().to(coef.dtype).contiguous()
+    n_out, n_in, k_old = coef.shape
+    if k_old != old.size:
+        raise ValueError(f"coef has {k_old} basis functions, the old basis {old.size}")
+    ws = _bytes(_lib.load().kf_refit_workspace(n, n_in, old.size, new.size), coef.device)
+    out = torch.empty(n_out, n_in, new.size, dtype=torch.float64, device=coef.device)
+    scale_out = None if scale is None else torch.empty(n_out, n_in, dtype=torch.float64, device=coef.device)
+    _launch("kf_refit", _ptr(xt), _ptr(ranges), n, n_in, n_out, ctypes.byref(old), ctypes.byref(new), _ptr(coef),
+            _ptr(scale), _rat_dtype(coef), float(ridge), _ptr(out), _ptr(scale_out), _ptr(ws), _stream(coef),
+            kernels=3)
+    return out, scale_out
 
 
 def check_device_errors() -> None:

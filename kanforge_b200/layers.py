@@ -136,7 +136,10 @@ class KANLinear(nn.Module):
         self._basis_tensors = {}
         for trainable, values in ((True, state.trainable), (False, state.buffers)):
             for name, value in values.items():
-                t = torch.as_tensor(np.ascontiguousarray(value), **like)
+                if isinstance(value, torch.Tensor):
+                    t = value.detach().to(**like).contiguous()
+                else:
+                    t = torch.as_tensor(np.ascontiguousarray(value), **like)
                 if trainable:
                     self.register_parameter(f"basis_{name}", nn.Parameter(t))
                 else:
@@ -280,6 +283,103 @@ class KANLinear(nn.Module):
         out = _kernels.edge_derivative(x, coef_eff, base_eff, self._grid(), plan, order, params, self.groups)
         return out.to(x.dtype) if x.dtype != torch.float32 else out
 
+    # --- grid tools (reference kanforge/_layer.py:107-183, kanforge/grid.py) ------
+    # Adaptive grids, resampled grids and the least-squares refit run on the
+    # device (kf_adaptive_grid, kf_resample_grid, kf_refit); the samples stay
+    # there.  Samples are taken in float32.  Parameter shapes can change:
+    # re-create the optimizer afterwards.
+
+    @staticmethod
+    def _refit_plan(basis: Basis):
+        plan = plan_for(basis)
+        if plan is None or plan.kind == "rational":
+            raise NotImplementedError(f"no device refit for {basis!r}: it has no kernel plan with fixed features")
+        return plan
+
+    def _grid64(self) -> torch.Tensor | None:
+        return self.basis_grid.detach().to(torch.float64) if "grid" in self._basis_tensors else None
+
+    def _sample_columns(self, x) -> torch.Tensor:
+        x = x if isinstance(x, torch.Tensor) else torch.as_tensor(np.asarray(x), dtype=torch.float32)
+        x = x.detach().to(self.coef.device)
+        _require_cuda(x)
+        return _kernels.sample_columns(x.reshape(-1, self.in_features))
+
+    def _ranges(self, grid: torch.Tensor) -> torch.Tensor:
+        return torch.stack([grid[:, 0], grid[:, -1]], -1).to(torch.float64).contiguous()
+
+    @torch.no_grad()
+    def _refit_to(self, new_basis: Basis, new_grid, samples, ridge: float) -> None:
+        """Move to new_basis (grid new_grid, float64) keeping the edge functions on
+        samples: (xt, None, n) sample columns or (None, ranges, n) evenly spaced
+        points (_layer.py:120-137)."""
+        old_fb, keep_old = _kernels.fit_basis(self._refit_plan(self.basis), self._grid64(), self.coef.device)
+        new_fb, keep_new = _kernels.fit_basis(self._refit_plan(new_basis), new_grid, self.coef.device)
+        xt, ranges, n = samples
+        coef, scale = _kernels.refit(xt, ranges, n, old_fb, new_fb, self.coef, self.edge_scale, ridge)
+        like = {"dtype": self.coef.dtype, "device": self.coef.device}
+        self.basis = new_basis
+        self.coef = nn.Parameter(coef.to(**like).contiguous())
+        if scale is not None:
+            self.edge_scale = nn.Parameter(scale.to(**like).contiguous())
+        state = initial_basis_state(new_basis, self.groups, self.in_features)
+        if new_grid is not None:
+            state.buffers["grid"] = new_grid
+        self._install_basis_state(state)
+        del keep_old, keep_new
+
+    def update_grid(self, x, *, margin: float = 0.0, grid_eps: float = 0.02, ridge: float = 0.0) -> None:
+        """Adapt every input's grid to the samples x (pykan's update_grid_from_samples)
+        and refit the edge functions on x (_layer.py:148-164).  Like pykan this
+        only approximates the old functions on the new grid."""
+        if x is None:
+            raise ValueError("update_grid needs input samples x")
+        if not self.basis.grid_names():
+            raise TypeError(f"{type(self.basis).__name__} has no grid")
+        xt = self._sample_columns(x)
+        grid = _kernels.adaptive_grid(xt, self.basis_grid.shape[-1], margin, grid_eps)
+        self._refit_to(self.basis, grid, (xt, None, xt.shape[1]), ridge)
+
+    def refine_grid(self, grid_size: int, x=None, *, ridge: float = 0.0) -> None:
+        """The same basis with grid_size intervals (or centres); each grid keeps
+        its per-input shape (_layer.py:166-175)."""
+        cfg = self.basis.config()
+        key = next((k for k in ("grid_size", "count", "num_knots") if k in cfg), None)
+        if key is None:
+            raise TypeError(f"{type(self.basis).__name__} has no grid size to refine")
+        new_basis = make_basis({**cfg, key: grid_size})
+        old_grid = self._grid64()
+        new_grid = None
+        if old_grid is not None and "grid" in new_basis.grid_names():
+            n_new = initial_basis_state(new_basis, self.groups, self.in_features).buffers["grid"].shape[-1]
+            new_grid = _kernels.resample_grid(old_grid, n_new)
+        samples = self._fit_samples(x, old_grid, 8 * new_basis.size + 64)
+        self._refit_to(new_basis, new_grid, samples, ridge)
+
+    def change_basis(self, basis, x=None, *, ridge: float = 0.0) -> None:
+        """Convert to another basis by least squares (_layer.py:177-183): a new
+        grid spans each input's old grid range; without x the fit uses evenly
+        spaced points over the old grid (else the new basis' grid)."""
+        new_basis = make_basis(basis)
+        old_grid = self._grid64()
+        ranges = None if old_grid is None else self._ranges(old_grid)
+        state = initial_basis_state(new_basis, self.groups, self.in_features,
+                                    None if ranges is None else ranges.cpu().numpy())
+        new_grid = state.buffers.get("grid")
+        if new_grid is not None:
+            new_grid = torch.as_tensor(new_grid, dtype=torch.float64, device=self.coef.device)
+        src = old_grid if old_grid is not None else new_grid
+        samples = self._fit_samples(x, src, 8 * max(new_basis.size, self.basis.size) + 64)
+        self._refit_to(new_basis, new_grid, samples, ridge)
+
+    def _fit_samples(self, x, grid, n: int):
+        if x is not None:
+            xt = self._sample_columns(x)
+            return xt, None, xt.shape[1]
+        if grid is None:
+            raise ValueError(f"{type(self.basis).__name__} has no grid: pass samples x")
+        return None, self._ranges(grid), n
+
     # --- state export / import (.npz layout, layers.py:230-267) -----------------
 
     @staticmethod
@@ -363,6 +463,18 @@ class KAN(nn.Sequential):
     def edge_derivative(self, x: torch.Tensor, order: int = 1) -> list[torch.Tensor]:
         """Per-layer edge derivatives at the activations each layer receives."""
         return [layer.edge_derivative(h, order) for layer, h in layer_inputs(self, x)]
+
+    @torch.no_grad()
+    def update_grid(self, x: torch.Tensor, **kwargs) -> None:
+        """Update every layer's grid from the activations it receives, each layer
+        after the ones before it (kanforge/torch/layers.py:389-393)."""
+        for layer in self:
+            layer.update_grid(x, **kwargs)
+            x = layer(x)
+
+    def refine_grid(self, grid_size: int, **kwargs) -> None:
+        for layer in self:
+            layer.refine_grid(grid_size, **kwargs)
 
 
 def rebuild_kan(layers: Sequence[KANLinear]) -> KAN:

@@ -1,6 +1,6 @@
 """Generate the golden fixtures in this folder by running the REFERENCE package.
 
-    KANFORGE_REFERENCE=/path/to/kanforge TRITON_INTERPRET=1 python tests/golden/make_golden.py
+    KANFORGE_REFERENCE=/path/to/kanforge TRITON_INTERPRET=1 python tests/golden/make_golden.py [names]
 
 Imports fx-xf/kanforge v0.8.0 from the directory in ``KANFORGE_REFERENCE`` and
 records, on small seeded inputs:
@@ -17,7 +17,13 @@ records, on small seeded inputs:
 * ``init.npz``     -- ``fit_rational`` coefficients, basis second moments and
                       ``init_stds`` (kanforge/bases/rational.py:27-61, _layer.py:47-83);
 * ``ref_model.npz`` + ``ref_model_io.npz`` -- a model file written by
-                      ``kanforge.save`` and its outputs (kanforge/convert.py:313-325).
+                      ``kanforge.save`` and its outputs (kanforge/convert.py:313-325);
+* ``grid.npz``     -- the grid tools: ``adaptive_grid``, ``resample_grid``,
+                      ``sample_inputs``, ``refit`` (kanforge/grid.py) and float32
+                      layers before and after ``update_grid`` / ``refine_grid`` /
+                      ``change_basis`` (kanforge/_layer.py:148-183).
+
+Pass file names (``bases layers prims init model_file grid``) to regenerate a subset.
 
 The fixtures are committed; nothing at test time reads the reference.
 """
@@ -235,11 +241,124 @@ def make_model_file():
     np.savez(HERE / "ref_model_io.npz", x=x.numpy(), y=y.numpy())
 
 
+GRID_REFITS = [
+    # name, old basis, new basis (None = same basis on an adaptive grid), ridge, with edge_scale
+    ("bspline_adapt", kf.BSpline(5, 3), None, 0.0, False),
+    ("bspline_adapt_ridge", kf.BSpline(5, 3), None, 0.1, True),
+    ("bspline_to_cheb", kf.BSpline(5, 3), kf.Chebyshev(8), 0.0, False),
+    ("bspline_refine", kf.BSpline(4, 2), kf.BSpline(9, 2), 0.0, True),
+    ("rbf_adapt", kf.RBF(6), None, 0.0, False),
+    ("cheb_to_legendre", kf.Chebyshev(4), kf.Legendre(6, input_map="identity"), 0.0, False),
+    ("fourier_to_bspline", kf.Fourier(2), kf.BSpline(6, 3), 0.01, False),
+    ("rswaf_to_mexican_hat", kf.RSWAF(5), kf.MexicanHat(7, learnable=False), 0.0, False),
+]
+
+
+def make_grid():
+    """``grid.npz``: the reference grid tools (kanforge/grid.py) on float32-valued
+    samples, and float32 KANLinear layers after update_grid / refine_grid /
+    change_basis (kanforge/_layer.py:148-183)."""
+    from kanforge import grid as gridlib
+    from kanforge._layer import basis_param_values
+    from kanforge.torch import KAN, KANLinear
+
+    rec = {}
+    rng = np.random.default_rng(7)
+    x = rng.standard_normal((1000, 6)).astype(np.float32)
+    x[:, 1] = np.round(x[:, 1] * 2) / 2  # many ties
+    x[:, 2] = 0.375  # flat column
+    x[:, 3] = rng.uniform(3, 5, 1000).astype(np.float32)
+    x[:7, 4] = -0.0
+    cases = [(9, 0.0, 0.02), (12, 0.1, 0.5), (2, 0.0, 1.0), (6, 0.0, 0.02)]
+    rec["adaptive/x"] = x
+    for j, (n, margin, eps) in enumerate(cases):
+        rec[f"adaptive/{j}/args"] = np.array([n, margin, eps])
+        rec[f"adaptive/{j}/grid"] = gridlib.adaptive_grid(x.astype(np.float64), n, margin, eps)
+    rec["adaptive/x1"] = x[:1]
+    rec["adaptive/x1/grid"] = gridlib.adaptive_grid(x[:1].astype(np.float64), 5, 0.0, 0.02)
+    g = gridlib.adaptive_grid(x.astype(np.float64), 9, 0.0, 0.02)
+    rec["resample/grid"] = g
+    for n in (5, 9, 17, 33):
+        rec[f"resample/{n}"] = gridlib.resample_grid(g, n)
+    rec["samples/ranges"] = np.stack([g[:, 0], g[:, -1]], -1)
+    rec["samples/100"] = gridlib.sample_inputs(rec["samples/ranges"], 100)
+
+    for name, old, new, ridge, scaled in GRID_REFITS:
+        n_in, n_out = 4, 3
+        xs = (rng.standard_normal((400, n_in)) * 0.6).astype(np.float32).astype(np.float64)
+        _, old_buf = basis_param_values(old, n_in, n_in)
+        coef = rng.standard_normal((n_out, n_in, old.size)) * 0.3
+        if new is None:
+            new_basis, new_buf = old, {k: gridlib.adaptive_grid(xs, v.shape[-1], 0.0, 0.02) for k, v in old_buf.items()}
+        else:
+            ranges = gridlib.grid_ranges(old, old_buf)
+            new_basis = new
+            _, new_buf = basis_param_values(new, n_in, n_in, ranges)
+        out = gridlib.refit(old, old_buf, coef, new_basis, new_buf, xs, ridge)
+        rec[f"refit/{name}/x"] = xs
+        rec[f"refit/{name}/coef"] = coef
+        rec[f"refit/{name}/ridge"] = np.array(ridge)
+        rec[f"refit/{name}/old_config"] = np.array(json.dumps(old.config()))
+        rec[f"refit/{name}/new_config"] = np.array(json.dumps(new_basis.config()))
+        for k, v in old_buf.items():
+            rec[f"refit/{name}/old/{k}"] = v
+        for k, v in new_buf.items():
+            rec[f"refit/{name}/new/{k}"] = v
+        rec[f"refit/{name}/out"] = out
+
+    # float32 layers through the reference's own methods
+    def layer(basis, scaled, seed):
+        torch.manual_seed(seed)
+        lay = KANLinear(5, 4, basis, edge_scale=scaled)
+        with torch.no_grad():
+            lay.coef.normal_(0, 0.4)
+            if scaled:
+                lay.edge_scale.uniform_(0.5, 1.5)
+                lay.edge_scale[1, 2] = 0.0
+        return lay
+
+    def dump(prefix, lay):
+        for k, v in lay.state_dict().items():
+            rec[f"{prefix}/state/{k}"] = v.detach().numpy()
+        rec[f"{prefix}/config"] = np.array(json.dumps(lay.basis.config()))
+
+    xl = (torch.randn(3000, 5) * 0.7 + 0.2).float()
+    xl[:, 4] = xl[:, 4] * 4
+    ops = [
+        ("update_bspline", kf.BSpline(6, 3), True, lambda m: m.update_grid(xl)),
+        ("update_bspline_margin", kf.BSpline(4, 2), False, lambda m: m.update_grid(xl, margin=0.05, grid_eps=0.2, ridge=0.01)),
+        ("update_rbf", kf.RBF(8), False, lambda m: m.update_grid(xl)),
+        ("update_rswaf", kf.RSWAF(6), True, lambda m: m.update_grid(xl)),
+        ("refine_bspline", kf.BSpline(5, 3), True, lambda m: m.refine_grid(10)),
+        ("refine_bspline_x", kf.BSpline(5, 3), False, lambda m: m.refine_grid(7, xl)),
+        ("refine_rbf", kf.RBF(5), False, lambda m: m.refine_grid(9)),
+        ("change_bspline_cheb", kf.BSpline(5, 3), True, lambda m: m.change_basis(kf.Chebyshev(8))),
+        ("change_cheb_bspline_x", kf.Chebyshev(5), False, lambda m: m.change_basis(kf.BSpline(6, 3), xl)),
+        ("change_bspline_rbf", kf.BSpline(5, 3), False, lambda m: m.change_basis(kf.RBF(10))),
+    ]
+    rec["layer/x"] = xl.numpy()
+    for j, (name, basis, scaled, op) in enumerate(ops):
+        lay = layer(basis, scaled, 20 + j)
+        dump(f"layer/{name}/before", lay)
+        op(lay)
+        dump(f"layer/{name}/after", lay)
+
+    torch.manual_seed(5)
+    model = KAN([5, 4, 3], kf.BSpline(5, 3))
+    rec["kan/x"] = xl.numpy()
+    for j, lay in enumerate(model):
+        for k, v in lay.state_dict().items():
+            rec[f"kan/before/{j}/{k}"] = v.detach().numpy()
+    model.update_grid(xl)
+    for j, lay in enumerate(model):
+        for k, v in lay.state_dict().items():
+            rec[f"kan/after/{j}/{k}"] = v.detach().numpy()
+    np.savez_compressed(HERE / "grid.npz", **rec)
+
+
 if __name__ == "__main__":
-    make_bases()
-    make_layers()
-    make_prims()
-    make_init()
-    make_model_file()
+    which = sys.argv[1:] or ["bases", "layers", "prims", "init", "model_file", "grid"]
+    for name in which:
+        globals()[f"make_{name}"]()
     for f in sorted(HERE.glob("*.npz")):
         print(f.name, f.stat().st_size)

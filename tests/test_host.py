@@ -309,3 +309,36 @@ def test_polynomial_family_matrices_match_independent_evaluations():
     v = np.polynomial.chebyshev.chebvander(pts, 5) @ g._cheb
     np.testing.assert_allclose(v.T @ v / 11, np.eye(6), atol=1e-12)
     assert (np.diag(g._cheb) > 0).all()
+
+
+def test_grid_tools_validate_arguments_without_a_gpu():
+    """kf_adaptive_grid / kf_refit reject bad sizes on the host, before any CUDA call."""
+    lib = _lib.load()
+    ws = ctypes.c_void_p(16)
+    rc = lib.kf_adaptive_grid(ws, 10, 3, 1, 0.0, 0.02, ws, ws, None)
+    assert rc == 1 and "n_points" in _lib.last_error()
+    rc = lib.kf_adaptive_grid(ws, 10, 3, 9, 0.0, 0.0, ws, ws, None)
+    assert rc == 1 and "grid_eps" in _lib.last_error()
+    rc = lib.kf_adaptive_grid(ws, 0, 3, 9, 0.0, 0.02, ws, ws, None)
+    assert rc == 1 and "samples" in _lib.last_error()
+    assert lib.kf_grid_workspace(1000, 6, 9) == 6 * 9 * (8 + 1024)
+    big, keep = kb.kernels.fit_basis(kb.plan_for(kb.Chebyshev(5)), None, "cpu")
+    rat = _lib.FitBasis(kind=_lib.KF_BASIS_RATIONAL, size=1)
+    rc = lib.kf_refit(ws, None, 10, 3, 2, ctypes.byref(rat), ctypes.byref(big), ws, None, 0, 0.0, ws, None, ws, None)
+    assert rc == 2 and "no refit" in _lib.last_error()
+    with pytest.raises(ValueError, match="up to 64"):
+        kb.kernels.fit_basis(kb.plan_for(kb.BSpline(70, 3)), torch.zeros(3, 71, dtype=torch.float64), "cpu")
+
+
+def test_grid_tools_fail_loudly_on_cpu():
+    layer = kb.KANLinear(3, 2, kb.BSpline(5, 3))
+    with pytest.raises(ValueError, match="samples"):
+        layer.update_grid(None)
+    with pytest.raises(TypeError, match="no grid"):
+        kb.KANLinear(3, 2, kb.Chebyshev(4)).update_grid(torch.zeros(8, 3))
+    with pytest.raises(TypeError, match="grid size"):
+        kb.KANLinear(3, 2, kb.Chebyshev(4)).refine_grid(8)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        layer.update_grid(torch.zeros(8, 3))
+    with pytest.raises(ValueError, match="pass samples"):
+        kb.KANLinear(3, 2, kb.Chebyshev(4)).change_basis(kb.Legendre(4))
