@@ -21,6 +21,8 @@
  *   kanforge/grid.py:19-31             adaptive_grid          -> kf_adaptive_grid
  *   kanforge/grid.py:34-38             resample_grid          -> kf_resample_grid
  *   kanforge/grid.py:55-85             refit                  -> kf_refit
+ *   kanforge/bases/base.py:15-16       local / support (sparse gather, the
+ *                                      reference's planned kernel) -> kf_sparse_*
  */
 #ifndef KANFORGE_B200_H
 #define KANFORGE_B200_H
@@ -441,6 +443,33 @@ int64_t kf_refit_workspace(int64_t n, int32_t I, int32_t k_old, int32_t k_new);
 int kf_refit(const float* xt, const double* ranges, int64_t n, int32_t I, int32_t O, const kf_fit_basis* old_basis,
              const kf_fit_basis* new_basis, const void* coef, const void* edge_scale, int dtype, double ridge,
              double* coef_out, double* scale_out, void* workspace, void* stream);
+
+/* ---- sparse B-spline layers (kanforge/bases/base.py:15-16 local / support) --
+ * A B-spline of order k has at most k+1 non-zero functions at any input, so
+ * a float32 B-spline KANLinear needs k+1 coefficients per (token, input):
+ * these kernels gather them on the CUDA cores instead of running the dense
+ * (G+k+1)-wide contraction, for narrow layers whose few outputs would leave a
+ * tensor-core tile idle.  Same inputs and results as the dense layer
+ * (kanforge/torch/layers.py:171-192 and its autograd):
+ *   kf_sparse_fwd   y = sum_i phi_oi(x_i) + sum_i base[o,i] m silu(x_i) + bias
+ *   kf_sparse_dgrad dx[b,i] = sum_o dy[b,o] dphi_oi/dx (x_bi)   (base branch included)
+ *   kf_sparse_wgrad dcoef = sum_b dy B_j s m, dbase = sum_b dy silu m,
+ *                   dscale = sum_j coef sum_b dy B_j m, dbias = sum_b dy
+ *                   (fixed-order sums through `workspace`, kf_sparse_wgrad_workspace floats)
+ * phi_oi(x) = sum_j coef[o,i,j] s m B_j(x), s = edge_scale, m = edge_mask (null: 1).
+ * x (B, I), coef (O, I, G+k), edge_scale / edge_mask / base (O, I), bias (O),
+ * grid (I, G+1), y / dy (B, O), dx (B, I): float32.  Outputs of wgrad may be
+ * null when not wanted.  basis: KF_BASIS_BSPLINE, order 1..5. */
+int kf_sparse_fwd(const float* x, const float* coef, const float* edge_scale, const float* edge_mask, const float* base,
+                  const float* bias, const float* grid, float* y, int64_t B, int32_t I, int32_t O,
+                  const kf_basis_desc* basis, void* stream);
+int kf_sparse_dgrad(const float* x, const float* dy, const float* coef, const float* edge_scale, const float* edge_mask,
+                    const float* base, const float* grid, float* dx, int64_t B, int32_t I, int32_t O,
+                    const kf_basis_desc* basis, void* stream);
+int64_t kf_sparse_wgrad_workspace(int64_t B, int32_t I, int32_t O, const kf_basis_desc* basis);
+int kf_sparse_wgrad(const float* x, const float* dy, const float* coef, const float* edge_scale, const float* edge_mask,
+                    const float* grid, float* dcoef, float* dbase, float* dscale, float* dbias, float* workspace,
+                    int64_t B, int32_t I, int32_t O, const kf_basis_desc* basis, void* stream);
 
 #ifdef __cplusplus
 }

@@ -187,6 +187,17 @@ PROTOTYPES = {
         ctypes.c_int,
         [_vp, _vp, _c_i64, _c_i32, _c_i32, _FIT, _FIT, _vp, _vp, ctypes.c_int, _f64, _vp, _vp, _vp, _vp],
     ),
+    "kf_sparse_fwd": (
+        ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i32, _c_i32, ctypes.POINTER(BasisDesc), _vp],
+    ),
+    "kf_sparse_dgrad": (
+        ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i32, _c_i32, ctypes.POINTER(BasisDesc), _vp],
+    ),
+    "kf_sparse_wgrad_workspace": (_c_i64, [_c_i64, _c_i32, _c_i32, ctypes.POINTER(BasisDesc)]),
+    "kf_sparse_wgrad": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i32, _c_i32, ctypes.POINTER(BasisDesc), _vp],
+    ),
     "kf_rational_bwd_noalloc": (
         ctypes.c_int,
         [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i32, ctypes.POINTER(BasisDesc), ctypes.c_int, _vp],

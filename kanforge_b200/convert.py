@@ -7,12 +7,12 @@ layer types of the hot path: ``KANLinear``, ``GRKAN``, ``KAN`` and sequences of
 those with ``Linear`` layers and standard activations.
 
 Arrays are float64 in the file, as the reference writes them.  Device
-parameters move in one batch: ``save`` widens every tensor to float64 on the
-GPU and copies all of them into one pinned host buffer with asynchronous
-copies and a single synchronisation; ``load(..., device=cuda)`` gathers the
-file's arrays into one pinned buffer, sends it with one copy and narrows each
-array to its parameter's dtype on the GPU.  No per-tensor pageable copies and
-no float64 casts on the CPU.
+parameters stream through two alternating 64 MiB pinned buffers: ``save``
+widens every tensor to float64 on the GPU and copies it out chunk by chunk
+while the previous chunk is copied into its NumPy array; ``load(...,
+device=cuda)`` does the reverse and narrows each array to its parameter's
+dtype on the GPU.  No pageable device copies, no float64 casts on the CPU,
+and host memory beyond the arrays themselves stays at 128 MiB.
 """
 
 from __future__ import annotations
@@ -71,53 +71,98 @@ def _dtype_name(t: torch.Tensor) -> str:
     return str(t.dtype).replace("torch.", "")
 
 
+STAGING_BYTES = 64 << 20  # each of the two pinned staging buffers of the device copies
+
+
+class _Staging:
+    """Two pinned host buffers that alternate: while one chunk crosses PCIe
+    asynchronously on a side stream, the other is copied to or from NumPy."""
+
+    def __init__(self, device: torch.device):
+        n = STAGING_BYTES // 8
+        self.bufs = [torch.empty(n, dtype=torch.float64, pin_memory=True) for _ in range(2)]
+        self.host = [b.numpy() for b in self.bufs]
+        self.events: list = [None, None]
+        self.stream = torch.cuda.Stream(device)
+        self.stream.wait_stream(torch.cuda.current_stream(device))
+        self.n = n
+
+    def wait(self, k: int) -> None:
+        if self.events[k] is not None:
+            self.events[k].synchronize()
+            self.events[k] = None
+
+    def record(self, k: int) -> None:
+        ev = torch.cuda.Event()
+        ev.record(self.stream)
+        self.events[k] = ev
+
+
 def _host_float64(tensors: dict[str, torch.Tensor]) -> dict[str, np.ndarray]:
-    """float64 NumPy copies of tensors; CUDA tensors are widened on their device
-    and land in one pinned buffer per device after a single synchronisation."""
+    """float64 NumPy copies of tensors.  CUDA tensors are widened on their device
+    and streamed through the two pinned buffers chunk by chunk."""
     out: dict[str, np.ndarray] = {}
+    for name, t in tensors.items():
+        if t.device.type != "cuda":
+            out[name] = t.detach().to(torch.float64).numpy().copy()
     by_device: dict[torch.device, list[str]] = {}
     for name, t in tensors.items():
         if t.device.type == "cuda":
             by_device.setdefault(t.device, []).append(name)
-        else:
-            out[name] = t.detach().to(torch.float64).numpy().copy()
     for device, names in by_device.items():
-        total = sum(tensors[n].numel() for n in names)
-        staging = torch.empty(total, dtype=torch.float64, pin_memory=True)
-        stream = torch.cuda.Stream(device)
-        stream.wait_stream(torch.cuda.current_stream(device))
-        views, at = {}, 0
-        with torch.cuda.stream(stream):
-            for n in names:
-                t = tensors[n].detach()
-                k = t.numel()
+        st = _Staging(device)
+        pending: list = [None, None]
+        k = 0
+        for name in names:
+            t = tensors[name].detach()
+            dst = np.empty(tuple(t.shape), dtype=np.float64)
+            out[name] = dst
+            flat_dst = dst.reshape(-1)
+            with torch.cuda.stream(st.stream):
                 wide = t.to(torch.float64).reshape(-1)
-                staging[at:at + k].copy_(wide, non_blocking=True)
-                wide.record_stream(stream)
-                views[n] = (at, k, tuple(t.shape))
-                at += k
-        stream.synchronize()
-        host = staging.numpy()
-        for n, (a, k, shape) in views.items():
-            out[n] = host[a:a + k].reshape(shape)
+            for off in range(0, wide.numel(), st.n):
+                m = min(st.n, wide.numel() - off)
+                st.wait(k)
+                if pending[k] is not None:
+                    view, mm = pending[k]
+                    view[:] = st.host[k][:mm]
+                with torch.cuda.stream(st.stream):
+                    st.bufs[k][:m].copy_(wide[off:off + m], non_blocking=True)
+                st.record(k)
+                pending[k] = (flat_dst[off:off + m], m)
+                k ^= 1
+            wide.record_stream(st.stream)
+        for k in (0, 1):
+            st.wait(k)
+            if pending[k] is not None:
+                view, mm = pending[k]
+                view[:] = st.host[k][:mm]
     return out
 
 
 def _device_float64(arrays: dict[str, np.ndarray], device: torch.device) -> dict[str, torch.Tensor]:
-    """The arrays as float64 tensors on a CUDA device: one pinned staging buffer,
-    one host-to-device copy."""
-    names = list(arrays)
-    total = sum(int(np.asarray(arrays[n]).size) for n in names)
-    staging = torch.empty(total, dtype=torch.float64, pin_memory=True)
-    host = staging.numpy()
-    views, at = {}, 0
-    for n in names:
-        a = np.asarray(arrays[n], dtype=np.float64)
-        host[at:at + a.size] = a.reshape(-1)
-        views[n] = (at, a.size, a.shape)
-        at += a.size
-    dev = staging.to(device, non_blocking=True)
-    return {n: dev[a:a + k].view(shape) for n, (a, k, shape) in views.items()}
+    """The arrays as float64 tensors on a CUDA device, streamed through the two
+    pinned buffers chunk by chunk."""
+    st = _Staging(device)
+    out = {}
+    k = 0
+    for name, arr in arrays.items():
+        a = np.ascontiguousarray(arr, dtype=np.float64)
+        flat = a.reshape(-1)
+        dev = torch.empty(a.size, dtype=torch.float64, device=device)
+        for off in range(0, a.size, st.n):
+            m = min(st.n, a.size - off)
+            st.wait(k)
+            st.host[k][:m] = flat[off:off + m]
+            with torch.cuda.stream(st.stream):
+                dev[off:off + m].copy_(st.bufs[k][:m], non_blocking=True)
+            st.record(k)
+            k ^= 1
+        out[name] = dev.view(a.shape)
+    torch.cuda.current_stream(device).wait_stream(st.stream)
+    for k in (0, 1):
+        st.wait(k)
+    return out
 
 
 def _layer_spec(layer: KANLinear):

@@ -121,6 +121,41 @@ __device__ __forceinline__ void bspline_local(float x, const float* t, int nk, i
   }
 }
 
+// Row stride (floats) of the per-input knot tables: row 0 the extended knots,
+// row q the reciprocals 1 / (t_{r+q} - t_r).
+constexpr int kKnotTableStride = 64;
+
+// Cox-de Boor / derivative levels of bspline_local (basis.cuh) with the
+// reciprocal knot differences read from the table.
+template <int K, int ES = 1>
+__device__ __forceinline__ void bspline_local_tab(float x, const float* tab, int nk, int j, int m, float (&v)[K + 1],
+                                                  int ts = kKnotTableStride) {
+  const float* t = tab;
+#pragma unroll
+  for (int r = 0; r <= K; ++r) v[r] = 0.0f;
+  v[0] = 1.0f;
+#pragma unroll
+  for (int q = 1; q <= K; ++q) {
+    float nv[K + 1];
+    const bool deriv = q > K - m;
+    const float* inv = tab + q * ts;
+#pragma unroll
+    for (int rp = 0; rp <= q; ++rp) {
+      const int r = j - q + rp;
+      const float left = rp >= 1 ? v[rp - 1] : 0.0f;
+      const float right = rp <= q - 1 ? v[rp] : 0.0f;
+      float out = 0.0f;
+      if (r >= 0 && r <= nk - 2 - q) {
+        const float i1 = inv[r * ES], i2 = inv[(r + 1) * ES];
+        out = deriv ? (float)q * (left * i1 - right * i2) : (x - t[r * ES]) * i1 * left + (t[(r + q + 1) * ES] - x) * i2 * right;
+      }
+      nv[rp] = out;
+    }
+#pragma unroll
+    for (int rp = 0; rp <= K; ++rp) v[rp] = rp <= q ? nv[rp] : 0.0f;
+  }
+}
+
 // Dense B-spline feature vector: f[0..size) = m-th derivatives of every basis
 // function at x (zero where not supported).  t: extended knots (nk of them).
 template <int K>

@@ -47,7 +47,7 @@ constexpr int kBK = 64;  // bf16 elements per stage row = 128 bytes
 constexpr int kStages = 4;     // pipeline depth of the kernels with producer warps
 constexpr int kMaxStages = 6;  // deepest pipeline (TMA-fed kernels, where shared memory allows)
 constexpr int kATile = kBM * 128;  // 16 KB
-constexpr int kTabStride = 64;     // floats per knot/inverse-difference row
+constexpr int kTabStride = kKnotTableStride;  // floats per knot/inverse-difference row
 constexpr int kMaxOrder = 5;
 
 struct TileMap {
@@ -138,37 +138,6 @@ __device__ __forceinline__ void drain_tma(Ctl* ctl, int issued) {
     int last = issued - 1 - ((issued - 1 - s) % NS + NS) % NS;
     if (issued <= 0 || last < 0) continue;
     mbar_drain(&ctl->full_b[s], (last / NS) & 1);
-  }
-}
-
-// Cox-de Boor / derivative levels of bspline_local (basis.cuh) with the
-// reciprocal knot differences read from the table.
-template <int K, int ES = 1>
-__device__ __forceinline__ void bspline_local_tab(float x, const float* tab, int nk, int j, int m, float (&v)[K + 1],
-                                                  int ts = kTabStride) {
-  const float* t = tab;
-#pragma unroll
-  for (int r = 0; r <= K; ++r) v[r] = 0.0f;
-  v[0] = 1.0f;
-#pragma unroll
-  for (int q = 1; q <= K; ++q) {
-    float nv[K + 1];
-    const bool deriv = q > K - m;
-    const float* inv = tab + q * ts;
-#pragma unroll
-    for (int rp = 0; rp <= q; ++rp) {
-      const int r = j - q + rp;
-      const float left = rp >= 1 ? v[rp - 1] : 0.0f;
-      const float right = rp <= q - 1 ? v[rp] : 0.0f;
-      float out = 0.0f;
-      if (r >= 0 && r <= nk - 2 - q) {
-        const float i1 = inv[r * ES], i2 = inv[(r + 1) * ES];
-        out = deriv ? (float)q * (left * i1 - right * i2) : (x - t[r * ES]) * i1 * left + (t[(r + q + 1) * ES] - x) * i2 * right;
-      }
-      nv[rp] = out;
-    }
-#pragma unroll
-    for (int rp = 0; rp <= K; ++rp) v[rp] = rp <= q ? nv[rp] : 0.0f;
   }
 }
 
@@ -521,31 +490,28 @@ __global__ void __launch_bounds__(A_TMA ? kFwdTmaThreads : kFwdThreads, 1)
       const int64_t b = (int64_t)m * kPairM + (int64_t)rank * kBM + row;
       const bool row_ok = b < p.B;
       const unsigned short* xrow = reinterpret_cast<const unsigned short*>(p.x) + (row_ok ? b : 0) * p.I;
-      int k = ((grp - it) % kFwdGroups + kFwdGroups) % kFwdGroups;
-      unsigned short xa[IPK], xb[IPK];
+      auto load_x = [&](int kk, unsigned short (&dst)[IPK]) {
 #pragma unroll
-      for (int u = 0; u < IPK; ++u)
-        xa[u] = (row_ok && k < p.k_steps && k * IPK + u < p.I)
-                    ? (p.conv.active ? x_bits(p.x, p.conv, b, k * IPK + u, p.I) : __ldg(xrow + k * IPK + u)) : 0;
-      for (; k < p.k_steps; k += kFwdGroups) {
+        for (int u = 0; u < IPK; ++u)
+          dst[u] = (row_ok && kk < p.k_steps && kk * IPK + u < p.I)
+                       ? (p.conv.active ? x_bits(p.x, p.conv, b, kk * IPK + u, p.I) : __ldg(xrow + kk * IPK + u)) : 0;
+      };
+      // One K-step of this group: prefetch the x of the group's step after it
+      // into `nxt`, then fill the stage from `cur`.  Two calls alternate the
+      // buffers, so a prefetched value is first read one full step later and
+      // never copied (a copy would wait for the load right away).
+      auto produce = [&](int k, const unsigned short (&cur)[IPK], unsigned short (&nxt)[IPK]) -> bool {
         const int git = it + k;
         const int s = git % NS;
         const uint32_t ph = (git / NS) & 1;
         const int i0 = k * IPK;
-        const int inext = i0 + kFwdGroups * IPK;
-#pragma unroll
-        for (int u = 0; u < IPK; ++u)
-          xb[u] = (row_ok && k + kFwdGroups < p.k_steps && inext + u < p.I)
-                      ? (p.conv.active ? x_bits(p.x, p.conv, b, inext + u, p.I) : __ldg(xrow + inext + u)) : 0;
+        load_x(k + kFwdGroups, nxt);
         bool ok = mbar_wait_warp(&ctl->empty[s], ph ^ 1, abort);
         if constexpr (BK > 0) ok = ok && mbar_wait_warp(&ctl->tab_full[s], ph, abort);  // tables landed
-        if (!ok) {
-          alive = false;
-          break;
-        }
+        if (!ok) return false;
         float xv[IPK];
 #pragma unroll
-        for (int u = 0; u < IPK; ++u) xv[u] = __uint_as_float((uint32_t)xa[u] << 16);
+        for (int u = 0; u < IPK; ++u) xv[u] = __uint_as_float((uint32_t)cur[u] << 16);
         uint8_t* arow = sa + s * kATile;
         if constexpr (is_closed(BK)) {
 #pragma unroll
@@ -602,8 +568,21 @@ __global__ void __launch_bounds__(A_TMA ? kFwdTmaThreads : kFwdThreads, 1)
           else
             mbar_arrive_peer(&ctl->full_a[s], 0);
         }
-#pragma unroll
-        for (int u = 0; u < IPK; ++u) xa[u] = xb[u];
+        return true;
+      };
+      int k = ((grp - it) % kFwdGroups + kFwdGroups) % kFwdGroups;
+      unsigned short xa[IPK], xb[IPK];
+      load_x(k, xa);
+      for (; k < p.k_steps; k += 2 * kFwdGroups) {
+        if (!produce(k, xa, xb)) {
+          alive = false;
+          break;
+        }
+        if (k + kFwdGroups >= p.k_steps) break;
+        if (!produce(k + kFwdGroups, xb, xa)) {
+          alive = false;
+          break;
+        }
       }
       it += p.k_steps;
     }

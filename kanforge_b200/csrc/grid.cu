@@ -35,7 +35,6 @@ namespace {
 
 constexpr int kGridThreads = 256;      // = the 256 digit values of one radix pass
 constexpr int kFitThreads = 256;
-constexpr int kFitChunk = 64;          // samples per feature tile of the Gram kernel
 constexpr int kJacobiMaxSweeps = 40;
 constexpr double kEigenCut = 1e-13;    // eigenvalues below kEigenCut * max are dropped
 
@@ -267,32 +266,45 @@ __global__ void resample_grid_kernel(const double* __restrict__ grid, int32_t I,
 
 // ---- refit: float64 basis functions of one sample ---------------------------
 
-// Knots (B-spline: extended grid, kanforge/bases/spline.py:22-30) or centres
-// (bumps) of one input, staged in shared memory.
-__device__ int stage_knots(const kf_fit_basis& b, int i, double* out) {
-  if (b.kind != KF_BASIS_BSPLINE && b.kind != KF_BASIS_BUMP) return 0;
+// Per-input tables of a basis in shared memory: B-splines the extended knots
+// (kanforge/bases/spline.py:22-30) t[0..nt) followed by, for q = 1..k, the
+// reciprocals 1 / (t[j+q] - t[j]) (j < nt - q) in rows of nt; bumps the centres.
+__host__ __device__ inline int fit_table_len(const kf_fit_basis& b) {
+  if (b.kind == KF_BASIS_BSPLINE) return (b.n_grid + 2 * b.order) * (b.order + 1);
+  if (b.kind == KF_BASIS_BUMP) return b.n_grid;
+  return 0;
+}
+
+__device__ void stage_table(const kf_fit_basis& b, int i, double* out) {
+  if (b.kind != KF_BASIS_BSPLINE && b.kind != KF_BASIS_BUMP) return;
   const double* g = b.grid + (int64_t)i * b.n_grid;
   if (b.kind == KF_BASIS_BUMP) {
     for (int j = threadIdx.x; j < b.n_grid; j += blockDim.x) out[j] = g[j];
-    return b.n_grid;
+    return;
   }
-  const int k = b.order, ng = b.n_grid;
+  const int k = b.order, ng = b.n_grid, nt = ng + 2 * k;
   const double g0 = g[0], gl = g[ng - 1];
   const double h = __ddiv_rn(__dsub_rn(gl, g0), (double)(ng - 1));
-  for (int j = threadIdx.x; j < ng + 2 * k; j += blockDim.x) {
+  for (int j = threadIdx.x; j < nt; j += blockDim.x) {
     double t;
     if (j < k) t = __dsub_rn(g0, __dmul_rn(h, (double)(k - j)));
     else if (j < k + ng) t = g[j - k];
     else t = __dadd_rn(gl, __dmul_rn(h, (double)(j - k - ng + 1)));
     out[j] = t;
   }
-  return ng + 2 * k;
+  __syncthreads();
+  for (int e = threadIdx.x; e < k * nt; e += blockDim.x) {
+    const int q = e / nt + 1, j = e % nt;
+    out[q * nt + j] = j + q < nt ? 1.0 / (out[j + q] - out[j]) : 0.0;
+  }
 }
 
 // B-splines of order k at x: Cox-de Boor on the half-open knot interval that
-// holds x, evaluating only its k+1 non-zero functions (the same products and
-// sums as the full recursion of kanforge/bases/spline.py:74-85).
-__device__ void fit_bspline(const double* t, int nt, int k, int size, double x, double* out) {
+// holds x, evaluating only its k+1 non-zero functions (the products and sums of
+// the full recursion of kanforge/bases/spline.py:74-85, with the knot-difference
+// divisions as products with the staged reciprocals).
+__device__ void fit_bspline(const double* tab, int nt, int k, int size, double x, double* out) {
+  const double* t = tab;
   for (int j = 0; j < size; ++j) out[j] = 0.0;
   if (!(x >= t[0] && x < t[nt - 1])) return;
   int lo = 0, hi = nt - 2, m = 0;  // largest m with t[m] <= x
@@ -307,6 +319,8 @@ __device__ void fit_bspline(const double* t, int nt, int k, int size, double x, 
   }
   double nv[6] = {1.0, 0.0, 0.0, 0.0, 0.0, 0.0};  // nv[r] = B_{m-q+r, q}
   for (int q = 1; q <= k; ++q) {
+    const double* rq = tab + q * nt;        // 1 / (t[j+q] - t[j])
+    const double* rq1 = tab + q * nt + 1;   // 1 / (t[j+q+1] - t[j+1])
     double nw[6];
     for (int r = 0; r <= q; ++r) {
       const int j = m - q + r;
@@ -315,17 +329,8 @@ __device__ void fit_bspline(const double* t, int nt, int k, int size, double x, 
         continue;
       }
       double v = 0.0;
-      bool any = false;
-      if (r >= 1) {  // left term from B_{j, q-1}
-        const double left = __ddiv_rn(__dsub_rn(x, t[j]), __dsub_rn(t[j + q], t[j]));
-        v = __dmul_rn(left, nv[r - 1]);
-        any = true;
-      }
-      if (r <= q - 1) {  // right term from B_{j+1, q-1}
-        const double right = __ddiv_rn(__dsub_rn(t[j + q + 1], x), __dsub_rn(t[j + q + 1], t[j + 1]));
-        const double w = __dmul_rn(right, nv[r]);
-        v = any ? __dadd_rn(v, w) : w;
-      }
+      if (r >= 1) v = (x - t[j]) * rq[j] * nv[r - 1];                 // left term, from B_{j, q-1}
+      if (r <= q - 1) v = fma((t[j + q + 1] - x) * rq1[j], nv[r], v);  // right term, from B_{j+1, q-1}
       nw[r] = v;
     }
     for (int r = 0; r <= q; ++r) nv[r] = nw[r];
@@ -338,25 +343,24 @@ __device__ void fit_bspline(const double* t, int nt, int k, int size, double x, 
 
 __device__ __forceinline__ double fit_polyval(const double* c, int n, double x) {
   double y = c[n - 1];
-  for (int j = n - 2; j >= 0; --j) y = __dadd_rn(c[j], __dmul_rn(y, x));
+  for (int j = n - 2; j >= 0; --j) y = fma(y, x, c[j]);
   return y;
 }
 
 // Order-0 basis functions of input sample x (kanforge/bases/*.py _eval, m = 0).
-__device__ void fit_eval(const kf_fit_basis& b, const double* knots, int n_knots, double x, double* out) {
+__device__ void fit_eval(const kf_fit_basis& b, const double* tab, double x, double* out) {
   switch (b.kind) {
     case KF_BASIS_BSPLINE:
-      fit_bspline(knots, n_knots, b.order, b.size, x, out);
+      fit_bspline(tab, b.n_grid + 2 * b.order, b.order, b.size, x, out);
       return;
     case KF_BASIS_CHEB: {
-      // T_j(g(x)) by NumPy's chebvander recurrence, then phi_k = sum_j fold[k, j] T_j
+      // T_j(g(x)) by the three-term recurrence into out[], then phi_k = sum_j fold[k, j] T_j
       const double u = b.input_map == KF_MAP_TANH ? tanh(x) : x;
       const int nt = b.degree + 1;
       double tv[KF_FIT_MAX_SIZE];
       tv[0] = 1.0;
       if (nt > 1) tv[1] = u;
-      const double u2 = __dmul_rn(2.0, u);
-      for (int j = 2; j < nt; ++j) tv[j] = __dsub_rn(__dmul_rn(tv[j - 1], u2), tv[j - 2]);
+      for (int j = 2; j < nt; ++j) tv[j] = fma(2.0 * u, tv[j - 1], -tv[j - 2]);
       for (int k = 0; k < b.size; ++k) {
         const double* f = b.fold + (int64_t)k * nt;
         double acc = 0.0;
@@ -368,26 +372,25 @@ __device__ void fit_eval(const kf_fit_basis& b, const double* knots, int n_knots
     case KF_BASIS_FOURIER: {
       const int nfreq = b.degree;
       for (int j = 0; j < nfreq; ++j) {
-        double s, c;
-        sincos(__dmul_rn(x, __dmul_rn(b.freq, (double)(j + 1))), &s, &c);
-        out[j] = c;
-        out[nfreq + j] = s;
+        double sn, cs;
+        sincos(x * (b.freq * (double)(j + 1)), &sn, &cs);
+        out[j] = cs;
+        out[nfreq + j] = sn;
       }
       return;
     }
     case KF_BASIS_BUMP: {
       const int n = b.n_grid;
-      const double span = __dsub_rn(knots[n - 1], knots[0]);
+      const double span = tab[n - 1] - tab[0];
       if (b.bump_mode == KF_BUMP_GAUSS) {
-        const double kk = __ddiv_rn(__dmul_rn(b.u_scale, (double)(n - 1)), span);
+        const double kk = b.u_scale * (double)(n - 1) / span;
         for (int j = 0; j < n; ++j) {
-          const double u = __dmul_rn(__dsub_rn(x, knots[j]), kk);
-          const double p = fit_polyval(b.poly, b.n_poly, u);
-          out[j] = __dmul_rn(__dmul_rn(b.norm, p), exp(__dmul_rn(__dmul_rn(-0.5, u), u)));
+          const double u = (x - tab[j]) * kk;
+          out[j] = b.norm * fit_polyval(b.poly, b.n_poly, u) * exp(-0.5 * u * u);
         }
       } else {
-        const double h = __ddiv_rn(span, (double)(n - 1));
-        for (int j = 0; j < n; ++j) out[j] = fit_polyval(b.poly, b.n_poly, tanh(__ddiv_rn(__dsub_rn(x, knots[j]), h)));
+        const double inv_h = (double)(n - 1) / span;
+        for (int j = 0; j < n; ++j) out[j] = fit_polyval(b.poly, b.n_poly, tanh((x - tab[j]) * inv_h));
       }
       return;
     }
@@ -398,39 +401,58 @@ __device__ void fit_eval(const kf_fit_basis& b, const double* knots, int n_knots
 
 // ---- refit: Gram and cross matrices -----------------------------------------
 
+constexpr int kFitSamples = 128;  // samples per feature tile: one per thread and basis
+
 struct FitShape {
-  int kn, ko, kt, ld;  // new size, old size, kn + ko, feature row stride (multiple of 4)
-  int n_knots_max;     // knot slots per basis in shared memory
+  int kn, ko, kt, ld;      // new size, old size, kn + ko, feature row stride (multiple of 4)
+  int tab_new, tab_old;    // table lengths (doubles) of the two bases
+  int n_tiles, n_groups;   // 4x4 result tiles; sample groups (threads per tile)
 };
 
-__host__ __device__ inline FitShape fit_shape(int kn, int ko, int ng_new, int ng_old) {
+__host__ inline FitShape fit_shape(const kf_fit_basis& nb, const kf_fit_basis& ob) {
   FitShape s;
-  s.kn = kn;
-  s.ko = ko;
-  s.kt = kn + ko;
+  s.kn = nb.size;
+  s.ko = ob.size;
+  s.kt = s.kn + s.ko;
   s.ld = (s.kt + 3) & ~3;
-  s.n_knots_max = std::max(ng_new, ng_old) + 2 * 5 + 2;
+  s.tab_new = fit_table_len(nb);
+  s.tab_old = fit_table_len(ob);
+  s.n_tiles = ((s.kn + 3) / 4) * (s.ld / 4);
+  s.n_groups = std::max(1, kFitThreads / s.n_tiles);
   return s;
 }
 
+__host__ inline size_t fit_gram_smem(const FitShape& s) {
+  const size_t red = s.n_tiles <= kFitThreads ? (size_t)s.n_groups * s.n_tiles * 16 : 0;
+  return sizeof(double) * ((size_t)kFitSamples * s.ld + s.tab_new + s.tab_old + red);
+}
+
 // One CTA per (sample split, input): part[i, split] = sum over its samples of
-// b (b, a)^T, b the new and a the old basis functions, float64.  Each thread owns
-// up to two 4x4 tiles of the (kn x kt) result.
+// b (b, a)^T, b the new and a the old basis functions, float64.  Each feature
+// tile of 128 samples is evaluated by all threads (one sample and basis each);
+// the (kn x kt) result is cut into 4x4 register tiles, each owned by n_groups
+// threads that take every n_groups-th sample, reduced in a fixed order at the
+// end (with more than 256 tiles each thread owns two tiles and all samples).
 __global__ void __launch_bounds__(kFitThreads) refit_gram_kernel(const float* __restrict__ xt,
                                                                   const double* __restrict__ ranges, int64_t n,
                                                                   kf_fit_basis nb, kf_fit_basis ob, FitShape fs,
                                                                   int n_split, int64_t per_split,
                                                                   double* __restrict__ part) {
   extern __shared__ double fsm[];
-  double* feat = fsm;                                // [kFitChunk][ld]
-  double* knots_new = feat + kFitChunk * fs.ld;      // [n_knots_max]
-  double* knots_old = knots_new + fs.n_knots_max;    // [n_knots_max]
+  double* feat = fsm;                             // [kFitSamples][ld]
+  double* tab_new = feat + kFitSamples * fs.ld;   // [tab_new]
+  double* tab_old = tab_new + fs.tab_new;         // [tab_old]
+  double* red = tab_old + fs.tab_old;             // [n_groups][n_tiles][16]
   const int i = blockIdx.y, split = blockIdx.x, tid = threadIdx.x;
-  const int nk_new = stage_knots(nb, i, knots_new);
-  const int nk_old = stage_knots(ob, i, knots_old);
-  for (int j = tid; j < kFitChunk * fs.ld; j += blockDim.x) feat[j] = 0.0;
+  stage_table(nb, i, tab_new);
+  stage_table(ob, i, tab_old);
+  for (int j = tid; j < kFitSamples * fs.ld; j += blockDim.x) feat[j] = 0.0;
+  const bool wide = fs.n_tiles > kFitThreads;
   const int tq = fs.ld / 4;
-  const int n_tiles = ((fs.kn + 3) / 4) * tq;
+  const int grp = wide ? 0 : tid / fs.n_tiles;
+  const int my_tile = wide ? tid : tid % fs.n_tiles;
+  const bool active = wide || grp < fs.n_groups;
+  const int step = wide ? 1 : fs.n_groups;
   double acc[2][4][4];
 #pragma unroll
   for (int u = 0; u < 2; ++u)
@@ -446,28 +468,29 @@ __global__ void __launch_bounds__(kFitThreads) refit_gram_kernel(const float* __
   const int64_t s_begin = (int64_t)split * per_split;
   const int64_t s_end = min(n, s_begin + per_split);
   __syncthreads();
-  for (int64_t c0 = s_begin; c0 < s_end; c0 += kFitChunk) {
-    if (tid < 2 * kFitChunk) {
-      const int row = tid % kFitChunk;
-      const bool is_new = tid < kFitChunk;
+  for (int64_t c0 = s_begin; c0 < s_end; c0 += kFitSamples) {
+    {
+      const int row = tid % kFitSamples;
+      const bool is_new = tid < kFitSamples;
       const int64_t s = c0 + row;
       double* dst = feat + row * fs.ld + (is_new ? 0 : fs.kn);
-      const int size = is_new ? fs.kn : fs.ko;
       if (s < s_end) {
         const double x = xt ? (double)xt[(int64_t)i * n + s] : __dadd_rn(lo, __dmul_rn(unit_linspace(s, n), span));
-        if (is_new) fit_eval(nb, knots_new, nk_new, x, dst);
-        else fit_eval(ob, knots_old, nk_old, x, dst);
+        if (is_new) fit_eval(nb, tab_new, x, dst);
+        else fit_eval(ob, tab_old, x, dst);
       } else {
+        const int size = is_new ? fs.kn : fs.ko;
         for (int j = 0; j < size; ++j) dst[j] = 0.0;
       }
     }
     __syncthreads();
+    if (active) {
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int tile = tid + u * kFitThreads;
-      if (tile < n_tiles) {
+      for (int u = 0; u < 2; ++u) {
+        const int tile = my_tile + u * kFitThreads;
+        if (tile >= fs.n_tiles || (u == 1 && !wide)) continue;
         const int p0 = (tile / tq) * 4, q0 = (tile % tq) * 4;
-        for (int c = 0; c < kFitChunk; ++c) {
+        for (int c = grp; c < kFitSamples; c += step) {
           const double* row = feat + c * fs.ld;
           const double2 a01 = *reinterpret_cast<const double2*>(row + p0);
           const double2 a23 = *reinterpret_cast<const double2*>(row + p0 + 2);
@@ -485,16 +508,33 @@ __global__ void __launch_bounds__(kFitThreads) refit_gram_kernel(const float* __
     __syncthreads();
   }
   double* out = part + ((int64_t)i * n_split + split) * fs.kn * fs.kt;
+  if (wide) {
 #pragma unroll
-  for (int u = 0; u < 2; ++u) {
-    const int tile = tid + u * kFitThreads;
-    if (tile >= n_tiles) continue;
-    const int p0 = (tile / tq) * 4, q0 = (tile % tq) * 4;
+    for (int u = 0; u < 2; ++u) {
+      const int tile = tid + u * kFitThreads;
+      if (tile >= fs.n_tiles) continue;
+      const int p0 = (tile / tq) * 4, q0 = (tile % tq) * 4;
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          if (p0 + r < fs.kn && q0 + c < fs.kt) out[(p0 + r) * fs.kt + q0 + c] = acc[u][r][c];
+    }
+    return;
+  }
+  if (active) {
 #pragma unroll
     for (int r = 0; r < 4; ++r)
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
-        if (p0 + r < fs.kn && q0 + c < fs.kt) out[(p0 + r) * fs.kt + q0 + c] = acc[u][r][c];
+      for (int c = 0; c < 4; ++c) red[((int64_t)grp * fs.n_tiles + my_tile) * 16 + r * 4 + c] = acc[0][r][c];
+  }
+  __syncthreads();
+  for (int e = tid; e < fs.n_tiles * 16; e += blockDim.x) {  // sample groups summed in order
+    const int tile = e / 16, r = (e % 16) / 4, c = e % 4;
+    double v = 0.0;
+    for (int g = 0; g < fs.n_groups; ++g) v += red[((int64_t)g * fs.n_tiles + tile) * 16 + r * 4 + c];
+    const int p = (tile / tq) * 4 + r, q = (tile % tq) * 4 + c;
+    if (p < fs.kn && q < fs.kt) out[p * fs.kt + q] = v;
   }
 }
 
@@ -828,12 +868,12 @@ extern "C" int kf_refit(const float* xt, const double* ranges, int64_t n, int32_
   KF_CHECK_ARG(dtype == KF_DTYPE_F32 || dtype == KF_DTYPE_BF16, "kf_refit: dtype %d unsupported", dtype);
   if (int rc = bind_device(coef)) return rc;
   cudaStream_t s = (cudaStream_t)stream;
-  const FitShape fs = fit_shape(new_basis->size, old_basis->size, new_basis->n_grid, old_basis->n_grid);
+  const FitShape fs = fit_shape(*new_basis, *old_basis);
   const int64_t splits = fit_splits(n, I);
   const int64_t per_split = cdiv(n, splits);
   double* part = (double*)workspace;
   double* xmap = part + (int64_t)I * splits * fs.kn * fs.kt;
-  const size_t gram_smem = sizeof(double) * ((size_t)kFitChunk * fs.ld + 2 * (size_t)fs.n_knots_max);
+  const size_t gram_smem = fit_gram_smem(fs);
   if (int rc = set_smem((const void*)refit_gram_kernel, gram_smem)) return rc;
   refit_gram_kernel<<<dim3((unsigned)splits, (unsigned)I), kFitThreads, gram_smem, s>>>(
       xt, ranges, n, *new_basis, *old_basis, fs, (int)splits, per_split, part);

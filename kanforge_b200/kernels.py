@@ -581,6 +581,82 @@ def kan_linear_tf32(x, coef, base_weight, bias, edge_scale, edge_mask, grid, pla
 # --- edge_derivative ---------------------------------------------------------
 
 
+# --- sparse B-spline (kanforge/bases/base.py:15-16 local / support) ------------
+
+# float32 B-spline layers with at most this many outputs gather the k+1 non-zero
+# coefficients per (token, input) on the CUDA cores (kf_sparse_*); wider layers
+# run the dense three-TF32 tensor-core contraction.
+SPARSE_MAX_OUT = 64
+
+
+def sparse_ok(plan: KernelPlan | None, x: torch.Tensor, n_out: int, coef_dtype, has_tf32: bool) -> bool:
+    """Whether a float32 B-spline layer takes the sparse kernels: narrow layers,
+    and shapes the tensor-core path does not take."""
+    if plan is None or plan.kind != "bspline" or not 1 <= plan.consts[1] <= 5:
+        return False
+    if x.dtype != torch.float32 or coef_dtype != torch.float32 or x.device.type != "cuda":
+        return False
+    return n_out <= SPARSE_MAX_OUT or not has_tf32
+
+
+class _SparseKANLinear(torch.autograd.Function):
+    """Float32 B-spline KANLinear on the sparse gather kernels: forward, input
+    gradient and parameter gradients (fixed-order sums) each one library call.
+    Double backward falls back to the closed float32 primitives."""
+
+    @staticmethod
+    def forward(ctx, x, coef, base_weight, bias, edge_scale, edge_mask, grid, plan):
+        x = x.contiguous()
+        n_b, n_in = x.shape
+        n_out = coef.shape[0]
+        f = lambda t: None if t is None else t.detach().float().contiguous()  # noqa: E731
+        y = torch.empty(n_b, n_out, device=x.device, dtype=torch.float32)
+        desc = plan.desc()
+        _launch("kf_sparse_fwd", _ptr(x), _ptr(f(coef)), _ptr(f(edge_scale)), _ptr(f(edge_mask)), _ptr(f(base_weight)),
+                _ptr(f(bias)), _ptr(f(grid)), _ptr(y), n_b, n_in, n_out, ctypes.byref(desc), _stream(x))
+        ctx.save_for_backward(x, coef, base_weight, edge_scale, edge_mask, grid)
+        ctx.plan, ctx.has_bias = plan, bias is not None
+        return y
+
+    @staticmethod
+    def backward(ctx, gy):
+        x, coef, base_weight, edge_scale, edge_mask, grid = ctx.saved_tensors
+        plan, need = ctx.plan, ctx.needs_input_grad
+        if torch.is_grad_enabled():
+            return _fused_backward_differentiable(x, gy, coef, base_weight, edge_scale, edge_mask, grid, plan, need,
+                                                  ctx.has_bias)
+        f = lambda t: None if t is None else t.detach().float().contiguous()  # noqa: E731
+        gy = gy.float().contiguous()
+        n_b, n_in = x.shape
+        n_out = coef.shape[0]
+        desc = plan.desc()
+        c, s, m, w, g = f(coef), f(edge_scale), f(edge_mask), f(base_weight), f(grid)
+        gx = gc = gb = gbias = gs = None
+        if need[0]:
+            gx = torch.empty_like(x)
+            _launch("kf_sparse_dgrad", _ptr(x), _ptr(gy), _ptr(c), _ptr(s), _ptr(m), _ptr(w), _ptr(g), _ptr(gx), n_b,
+                    n_in, n_out, ctypes.byref(desc), _stream(x))
+        want_c, want_b = need[1], need[2] and base_weight is not None
+        want_bias, want_s = need[3] and ctx.has_bias, need[4] and edge_scale is not None
+        if want_c or want_b or want_bias or want_s:
+            n_ws = _lib.load().kf_sparse_wgrad_workspace(n_b, n_in, n_out, ctypes.byref(desc))
+            ws = torch.empty(max(n_ws, 1), device=x.device, dtype=torch.float32)
+            gc = torch.empty_like(c) if want_c else None
+            gb = torch.empty_like(w) if want_b else None
+            gbias = torch.empty(n_out, device=x.device, dtype=torch.float32) if want_bias else None
+            gs = torch.empty_like(s) if want_s else None
+            _launch("kf_sparse_wgrad", _ptr(x), _ptr(gy), _ptr(c), _ptr(s), _ptr(m), _ptr(g), _ptr(gc), _ptr(gb),
+                    _ptr(gs), _ptr(gbias), _ptr(ws), n_b, n_in, n_out, ctypes.byref(desc), _stream(x), kernels=2)
+        return gx, gc, gb, gbias, gs, None, None, None
+
+
+def kan_linear_sparse(x, coef, base_weight, bias, edge_scale, edge_mask, grid, plan):
+    """Float32 B-spline KANLinear on (..., I) inputs by the sparse kernels; see ``_SparseKANLinear``."""
+    lead = x.shape[:-1]
+    y = _SparseKANLinear.apply(x.reshape(-1, x.shape[-1]), coef, base_weight, bias, edge_scale, edge_mask, grid, plan)
+    return y.reshape(*lead, coef.shape[0])
+
+
 def _silu_polys(order: int):
     """(ctypes float array, n): silu^(order) as [h_m, h_{m-1}] polynomials in sigmoid."""
     polys = silu_derivative_polys(order).astype("float32").ravel()

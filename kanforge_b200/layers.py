@@ -225,8 +225,13 @@ class KANLinear(nn.Module):
             # coef * edge_scale * edge_mask and base_weight * edge_mask are formed inside the kernels
             return _kernels.kan_linear_fused(x, self.coef, silu_weight, self.bias, self.edge_scale, self.edge_mask,
                                              self._grid(), plan)
-        if plan.kind != "rational" and _kernels.FP32_TENSOR_CORES and _kernels.tf32_ok(
-                plan, x, self.out_features, has_base, self.coef.dtype):
+        tf32 = plan.kind != "rational" and _kernels.FP32_TENSOR_CORES and _kernels.tf32_ok(
+            plan, x, self.out_features, has_base, self.coef.dtype)
+        if _kernels.sparse_ok(plan, x, self.out_features, self.coef.dtype, tf32):
+            # float32 B-spline, narrow layer: gather the k+1 non-zero coefficients per (token, input)
+            return _kernels.kan_linear_sparse(x, self.coef, silu_weight, self.bias, self.edge_scale, self.edge_mask,
+                                              self._grid(), plan)
+        if tf32:
             # float32: three TF32 products per contraction on the tensor cores
             return _kernels.kan_linear_tf32(x, self.coef, silu_weight, self.bias, self.edge_scale, self.edge_mask,
                                             self._grid(), plan)
