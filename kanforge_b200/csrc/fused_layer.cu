@@ -490,28 +490,31 @@ __global__ void __launch_bounds__(A_TMA ? kFwdTmaThreads : kFwdThreads, 1)
       const int64_t b = (int64_t)m * kPairM + (int64_t)rank * kBM + row;
       const bool row_ok = b < p.B;
       const unsigned short* xrow = reinterpret_cast<const unsigned short*>(p.x) + (row_ok ? b : 0) * p.I;
-      auto load_x = [&](int kk, unsigned short (&dst)[IPK]) {
+      int k = ((grp - it) % kFwdGroups + kFwdGroups) % kFwdGroups;
+      unsigned short xa[IPK], xb[IPK];
 #pragma unroll
-        for (int u = 0; u < IPK; ++u)
-          dst[u] = (row_ok && kk < p.k_steps && kk * IPK + u < p.I)
-                       ? (p.conv.active ? x_bits(p.x, p.conv, b, kk * IPK + u, p.I) : __ldg(xrow + kk * IPK + u)) : 0;
-      };
-      // One K-step of this group: prefetch the x of the group's step after it
-      // into `nxt`, then fill the stage from `cur`.  Two calls alternate the
-      // buffers, so a prefetched value is first read one full step later and
-      // never copied (a copy would wait for the load right away).
-      auto produce = [&](int k, const unsigned short (&cur)[IPK], unsigned short (&nxt)[IPK]) -> bool {
+      for (int u = 0; u < IPK; ++u)
+        xa[u] = (row_ok && k < p.k_steps && k * IPK + u < p.I)
+                    ? (p.conv.active ? x_bits(p.x, p.conv, b, k * IPK + u, p.I) : __ldg(xrow + k * IPK + u)) : 0;
+      for (; k < p.k_steps; k += kFwdGroups) {
         const int git = it + k;
         const int s = git % NS;
         const uint32_t ph = (git / NS) & 1;
         const int i0 = k * IPK;
-        load_x(k + kFwdGroups, nxt);
+        const int inext = i0 + kFwdGroups * IPK;
+#pragma unroll
+        for (int u = 0; u < IPK; ++u)
+          xb[u] = (row_ok && k + kFwdGroups < p.k_steps && inext + u < p.I)
+                      ? (p.conv.active ? x_bits(p.x, p.conv, b, inext + u, p.I) : __ldg(xrow + inext + u)) : 0;
         bool ok = mbar_wait_warp(&ctl->empty[s], ph ^ 1, abort);
         if constexpr (BK > 0) ok = ok && mbar_wait_warp(&ctl->tab_full[s], ph, abort);  // tables landed
-        if (!ok) return false;
+        if (!ok) {
+          alive = false;
+          break;
+        }
         float xv[IPK];
 #pragma unroll
-        for (int u = 0; u < IPK; ++u) xv[u] = __uint_as_float((uint32_t)cur[u] << 16);
+        for (int u = 0; u < IPK; ++u) xv[u] = __uint_as_float((uint32_t)xa[u] << 16);
         uint8_t* arow = sa + s * kATile;
         if constexpr (is_closed(BK)) {
 #pragma unroll
@@ -568,21 +571,8 @@ __global__ void __launch_bounds__(A_TMA ? kFwdTmaThreads : kFwdThreads, 1)
           else
             mbar_arrive_peer(&ctl->full_a[s], 0);
         }
-        return true;
-      };
-      int k = ((grp - it) % kFwdGroups + kFwdGroups) % kFwdGroups;
-      unsigned short xa[IPK], xb[IPK];
-      load_x(k, xa);
-      for (; k < p.k_steps; k += 2 * kFwdGroups) {
-        if (!produce(k, xa, xb)) {
-          alive = false;
-          break;
-        }
-        if (k + kFwdGroups >= p.k_steps) break;
-        if (!produce(k + kFwdGroups, xb, xa)) {
-          alive = false;
-          break;
-        }
+#pragma unroll
+        for (int u = 0; u < IPK; ++u) xa[u] = xb[u];
       }
       it += p.k_steps;
     }

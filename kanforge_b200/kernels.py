@@ -585,8 +585,10 @@ def kan_linear_tf32(x, coef, base_weight, bias, edge_scale, edge_mask, grid, pla
 
 # float32 B-spline layers with at most this many outputs gather the k+1 non-zero
 # coefficients per (token, input) on the CUDA cores (kf_sparse_*); wider layers
-# run the dense three-TF32 tensor-core contraction.
-SPARSE_MAX_OUT = 64
+# run the dense three-TF32 tensor-core contraction (measured crossover between
+# 16 and 32 outputs: 65536 x 1024 -> 8 fwd+bwd 7.5 against 9.5 ms, -> 32 15.9
+# against 9.6 ms).
+SPARSE_MAX_OUT = 16
 
 
 def sparse_ok(plan: KernelPlan | None, x: torch.Tensor, n_out: int, coef_dtype, has_tf32: bool) -> bool:

@@ -51,7 +51,8 @@ CASES = [
 
 
 @pytest.mark.parametrize("case", CASES, ids=lambda c: f"{c[0]}x{c[1]}->{c[2]}_{c[3]!r}")
-def test_sparse_layer_matches_oracle(case):
+def test_sparse_layer_matches_oracle(case, monkeypatch):
+    monkeypatch.setattr(K, "SPARSE_MAX_OUT", 1 << 30)  # every output tile width, whatever the dispatch threshold
     n_b, n_in, n_out, basis, base, scaled, rng_x = case
     torch.manual_seed(n_in * 7 + n_out)
     layer = kb.KANLinear(n_in, n_out, basis, edge_scale=scaled, base_activation=torch.nn.functional.silu if base else None,
@@ -87,9 +88,9 @@ def test_sparse_layer_matches_oracle(case):
 
 def test_sparse_gradients_are_deterministic():
     torch.manual_seed(0)
-    layer = kb.KANLinear(48, 32, kb.BSpline(8, 3), edge_scale=True, device=DEV)
+    layer = kb.KANLinear(48, 12, kb.BSpline(8, 3), edge_scale=True, device=DEV)
     x = torch.randn(20000, 48, device=DEV).requires_grad_()
-    g = torch.randn(20000, 32, device=DEV)
+    g = torch.randn(20000, 12, device=DEV)
     a = torch.autograd.grad(layer(x), [x, layer.coef, layer.base_weight, layer.edge_scale, layer.bias], g)
     b = torch.autograd.grad(layer(x), [x, layer.coef, layer.base_weight, layer.edge_scale, layer.bias], g)
     for u, v in zip(a, b):
@@ -101,6 +102,10 @@ def test_dispatch_wide_layers_stay_on_the_tensor_cores():
     with launches() as names:
         layer(torch.randn(256, 64, device=DEV))
     assert "kf_sparse_fwd" not in names and "kf_gemm_tf32x3" in names, names
+    narrow = kb.KANLinear(64, K.SPARSE_MAX_OUT, kb.BSpline(8, 3), device=DEV)
+    with launches() as names:
+        narrow(torch.randn(256, 64, device=DEV))
+    assert "kf_sparse_fwd" in names, names
 
 
 def test_config0_training_step_matches_oracle():
