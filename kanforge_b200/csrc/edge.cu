@@ -17,6 +17,8 @@ namespace {
 
 constexpr int kEdgeThreads = 256;
 constexpr int kEdgeMaxNF = 16;  // features per input of the streaming kernel
+constexpr int kEdgeFeatRegs = 168;   // feature registers per thread of the streaming kernel
+constexpr int kEdgeBlocksPerSM = 1;  // resident CTAs per SM the streaming kernel is built for
 
 struct EdgeArgs {
   const float* x;
@@ -87,7 +89,7 @@ __host__ __device__ constexpr int edge_chunk(int nb) { return nb % 4 == 0 ? 4 : 
 // that keeps NB x (NF + 1) feature registers near 170, so that the
 // coefficients of one output (NF + 1 loads) serve NB outputs.
 __host__ __device__ constexpr int edge_rows(int nf) {
-  return (168 / (nf + 1) < 2 ? 2 : (168 / (nf + 1) > 16 ? 16 : 168 / (nf + 1))) & ~1;
+  return (kEdgeFeatRegs / (nf + 1) < 2 ? 2 : (kEdgeFeatRegs / (nf + 1) > 16 ? 16 : kEdgeFeatRegs / (nf + 1))) & ~1;
 }
 
 // One lane per input; a warp covers il consecutive inputs (il = 32, or the
@@ -102,7 +104,7 @@ __host__ __device__ constexpr int edge_rows(int nf) {
 // independently (persistent, no barrier after the knot table), so one warp's
 // feature prologue overlaps the others' stores.
 template <int NF, int NB>
-__global__ void __launch_bounds__(kEdgeThreads, 1) edge_vec_kernel(const __grid_constant__ EdgeArgs A, int il_log2) {
+__global__ void __launch_bounds__(kEdgeThreads, kEdgeBlocksPerSM) edge_vec_kernel(const __grid_constant__ EdgeArgs A, int il_log2) {
   constexpr int NJ = NF + 1, NP = NB / 2, CH = edge_chunk(NB);
   static_assert(NB % 2 == 0 && NB % CH == 0, "rows are processed in pairs and chunks");
   extern __shared__ float smem[];
@@ -173,11 +175,20 @@ __global__ void __launch_bounds__(kEdgeThreads, 1) edge_vec_kernel(const __grid_
     const float* cp = A.coef + (size_t)lo * NF * A.I + i;  // (O, NF, I)
     const float* bp = A.base ? A.base + (size_t)lo * A.I + i : nullptr;
     float* op = A.out + (b0 * A.O + lo) * A.I + i;
-    for (int o = lo; o < A.O; o += ol) {
-      float q[NJ];
+    // The coefficients of output o + ol are loaded while output o is computed.
+    float q[NJ];
+    if (lo < A.O) {
 #pragma unroll
       for (int j = 0; j < NF; ++j) q[j] = __ldg(cp + (size_t)j * A.I);
       q[NF] = bp ? __ldg(bp) : 0.0f;
+    }
+    for (int o = lo; o < A.O; o += ol) {
+      float qn[NJ];
+      if (o + ol < A.O) {
+#pragma unroll
+        for (int j = 0; j < NF; ++j) qn[j] = __ldg(cp + c_step + (size_t)j * A.I);
+        qn[NF] = bp ? __ldg(bp + o_step) : 0.0f;
+      }
       float2 acc[NP];
       {
         const float2 qq = make_float2(q[NF], q[NF]);
@@ -195,6 +206,8 @@ __global__ void __launch_bounds__(kEdgeThreads, 1) edge_vec_kernel(const __grid_
         if (2 * p < nrows) __stcs(op + (2 * p) * row_step, acc[p].x);
         if (2 * p + 1 < nrows) __stcs(op + (2 * p + 1) * row_step, acc[p].y);
       }
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) q[j] = qn[j];
       cp += c_step;
       if (bp) bp += o_step;
       op += o_step;
@@ -350,7 +363,7 @@ int launch_vec(const EdgeArgs& A, cudaStream_t stream) {
   const unsigned gy = (unsigned)cdiv(A.I, 1 << il_log2);
   const int64_t n_groups = cdiv(A.B, (int64_t)NB);
   const int64_t gx_need = cdiv(n_groups, (int64_t)(kEdgeThreads / 32));
-  const unsigned gx = (unsigned)std::max<int64_t>(1, std::min<int64_t>(gx_need, std::max(1, n_sm / (int)std::min<unsigned>(gy, n_sm))));
+  const unsigned gx = (unsigned)std::max<int64_t>(1, std::min<int64_t>(gx_need, std::max(1, kEdgeBlocksPerSM * n_sm / (int)std::min<unsigned>(gy, kEdgeBlocksPerSM * n_sm))));
   edge_vec_kernel<NF, NB><<<dim3(gx, gy), kEdgeThreads, smem, stream>>>(A, il_log2);
   return check_launch("kf_edge_derivative");
 }
