@@ -378,7 +378,7 @@ int kf_rational_bwd_noalloc(const void* x, const void* dr, const float* num, con
  * targets are never formed. */
 
 #define KF_GRID_MAX_POINTS 192 /* grid points per input of kf_adaptive_grid */
-#define KF_FIT_MAX_SIZE 64     /* basis functions per edge of kf_refit (old and new) */
+#define KF_FIT_MAX_SIZE 256    /* basis functions per edge of kf_refit (old and new) */
 
 /* Samples x (n, I) row-major in `dtype` -> xt (I, n) float32, one column per
  * input: the sample layout of kf_adaptive_grid and kf_refit. */
@@ -431,11 +431,14 @@ int64_t kf_refit_workspace(int64_t n, int32_t I, int32_t k_old, int32_t k_new);
  *            n evenly spaced points per input over ranges (I, 2) float64
  *            (grid.py:49-52 sample_inputs);
  *   targets  the old edge functions sum_k c_eff[o,i,k] phi_k(x), c_eff = coef * edge_scale;
- *   solution per input the least-squares coefficients in the new basis,
- *            minimum-norm where the samples leave them undetermined
- *            (eigenvalues of the Gram matrix below 1e-13 of the largest are
- *            dropped); ridge > 0 adds ridge * mean(phi_new^2) * n to the Gram
- *            diagonal (the reference's appended damping rows);
+ *   solution per input the least-squares coefficients in the new basis:
+ *            with both sizes <= 64 the minimum-norm solution where the samples
+ *            leave them undetermined (eigenvalues of the Gram matrix below 1e-13
+ *            of the largest are dropped); above, a Cholesky factorisation whose
+ *            pivots below 1e-13 of the largest diagonal entry drop that basis
+ *            function (coefficient 0: the minimum-norm choice for functions no
+ *            sample reaches); ridge > 0 adds ridge * mean(phi_new^2) * n to the
+ *            Gram diagonal (the reference's appended damping rows);
  *   outputs  coef_out (O, I, new size) = solution / s and scale_out (O, I) = s,
  *            s = edge_scale where |edge_scale| > 1e-12 else 1, float64.
  * coef (O, I, old size) and edge_scale (O, I, or null) in `dtype`; scale_out

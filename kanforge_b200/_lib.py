@@ -81,7 +81,7 @@ class FitBasis(ctypes.Structure):
     ]
 
 
-KF_GRID_MAX_POINTS, KF_FIT_MAX_SIZE = 192, 64
+KF_GRID_MAX_POINTS, KF_FIT_MAX_SIZE = 192, 256
 
 _GEOM = ctypes.POINTER(ConvGeom)
 _FIT = ctypes.POINTER(FitBasis)

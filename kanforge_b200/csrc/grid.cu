@@ -36,6 +36,7 @@ namespace {
 constexpr int kGridThreads = 256;      // = the 256 digit values of one radix pass
 constexpr int kFitThreads = 256;
 constexpr int kJacobiMaxSweeps = 40;
+constexpr int kFitSmall = 64;          // both sizes up to this: shared-memory Jacobi solve (exact minimum norm)
 constexpr double kEigenCut = 1e-13;    // eigenvalues below kEigenCut * max are dropped
 
 struct GridState {
@@ -347,7 +348,9 @@ __device__ __forceinline__ double fit_polyval(const double* c, int n, double x) 
   return y;
 }
 
-// Order-0 basis functions of input sample x (kanforge/bases/*.py _eval, m = 0).
+// Order-0 basis functions of input sample x (kanforge/bases/*.py _eval, m = 0);
+// MAXT bounds the Chebyshev features held per thread.
+template <int MAXT>
 __device__ void fit_eval(const kf_fit_basis& b, const double* tab, double x, double* out) {
   switch (b.kind) {
     case KF_BASIS_BSPLINE:
@@ -357,7 +360,7 @@ __device__ void fit_eval(const kf_fit_basis& b, const double* tab, double x, dou
       // T_j(g(x)) by the three-term recurrence into out[], then phi_k = sum_j fold[k, j] T_j
       const double u = b.input_map == KF_MAP_TANH ? tanh(x) : x;
       const int nt = b.degree + 1;
-      double tv[KF_FIT_MAX_SIZE];
+      double tv[MAXT];
       tv[0] = 1.0;
       if (nt > 1) tv[1] = u;
       for (int j = 2; j < nt; ++j) tv[j] = fma(2.0 * u, tv[j - 1], -tv[j - 2]);
@@ -401,12 +404,15 @@ __device__ void fit_eval(const kf_fit_basis& b, const double* tab, double x, dou
 
 // ---- refit: Gram and cross matrices -----------------------------------------
 
-constexpr int kFitSamples = 128;  // samples per feature tile: one per thread and basis
+constexpr int kFitTileGroup = 2 * kFitThreads;  // 4x4 result tiles per CTA when they are many (two per thread)
 
 struct FitShape {
   int kn, ko, kt, ld;      // new size, old size, kn + ko, feature row stride (multiple of 4)
   int tab_new, tab_old;    // table lengths (doubles) of the two bases
   int n_tiles, n_groups;   // 4x4 result tiles; sample groups (threads per tile)
+  int chunk;               // samples per feature tile (128, or 32 for wide feature rows)
+  int tile_groups;         // CTAs that share one (split, input)'s result tiles
+  bool small;              // both sizes <= kFitSmall
 };
 
 __host__ inline FitShape fit_shape(const kf_fit_basis& nb, const kf_fit_basis& ob) {
@@ -419,38 +425,44 @@ __host__ inline FitShape fit_shape(const kf_fit_basis& nb, const kf_fit_basis& o
   s.tab_old = fit_table_len(ob);
   s.n_tiles = ((s.kn + 3) / 4) * (s.ld / 4);
   s.n_groups = std::max(1, kFitThreads / s.n_tiles);
+  s.chunk = s.ld <= 128 ? 128 : 32;
+  s.tile_groups = s.n_tiles <= kFitThreads ? 1 : (s.n_tiles + kFitTileGroup - 1) / kFitTileGroup;
+  s.small = s.kn <= kFitSmall && s.ko <= kFitSmall;
   return s;
 }
 
 __host__ inline size_t fit_gram_smem(const FitShape& s) {
   const size_t red = s.n_tiles <= kFitThreads ? (size_t)s.n_groups * s.n_tiles * 16 : 0;
-  return sizeof(double) * ((size_t)kFitSamples * s.ld + s.tab_new + s.tab_old + red);
+  return sizeof(double) * ((size_t)s.chunk * s.ld + s.tab_new + s.tab_old + red);
 }
 
-// One CTA per (sample split, input): part[i, split] = sum over its samples of
-// b (b, a)^T, b the new and a the old basis functions, float64.  Each feature
-// tile of 128 samples is evaluated by all threads (one sample and basis each);
-// the (kn x kt) result is cut into 4x4 register tiles, each owned by n_groups
-// threads that take every n_groups-th sample, reduced in a fixed order at the
-// end (with more than 256 tiles each thread owns two tiles and all samples).
+// One CTA per (sample split, input, tile group): part[i, split] = sum over its
+// samples of b (b, a)^T, b the new and a the old basis functions, float64.  Each
+// feature tile of CHUNK samples is evaluated by 2 CHUNK threads (one sample and
+// basis each); the (kn x kt) result is cut into 4x4 register tiles.  With at
+// most 256 tiles each is owned by n_groups threads that take every n_groups-th
+// sample, reduced in a fixed order at the end; with more, each thread owns two
+// tiles of its CTA's tile group and all samples.
+template <int CHUNK, int MAXT>
 __global__ void __launch_bounds__(kFitThreads) refit_gram_kernel(const float* __restrict__ xt,
                                                                   const double* __restrict__ ranges, int64_t n,
                                                                   kf_fit_basis nb, kf_fit_basis ob, FitShape fs,
                                                                   int n_split, int64_t per_split,
                                                                   double* __restrict__ part) {
   extern __shared__ double fsm[];
-  double* feat = fsm;                             // [kFitSamples][ld]
-  double* tab_new = feat + kFitSamples * fs.ld;   // [tab_new]
-  double* tab_old = tab_new + fs.tab_new;         // [tab_old]
-  double* red = tab_old + fs.tab_old;             // [n_groups][n_tiles][16]
+  double* feat = fsm;                        // [CHUNK][ld]
+  double* tab_new = feat + CHUNK * fs.ld;    // [tab_new]
+  double* tab_old = tab_new + fs.tab_new;    // [tab_old]
+  double* red = tab_old + fs.tab_old;        // [n_groups][n_tiles][16]
   const int i = blockIdx.y, split = blockIdx.x, tid = threadIdx.x;
   stage_table(nb, i, tab_new);
   stage_table(ob, i, tab_old);
-  for (int j = tid; j < kFitSamples * fs.ld; j += blockDim.x) feat[j] = 0.0;
+  for (int j = tid; j < CHUNK * fs.ld; j += blockDim.x) feat[j] = 0.0;
   const bool wide = fs.n_tiles > kFitThreads;
+  const int tile0 = blockIdx.z * kFitTileGroup;
   const int tq = fs.ld / 4;
   const int grp = wide ? 0 : tid / fs.n_tiles;
-  const int my_tile = wide ? tid : tid % fs.n_tiles;
+  const int my_tile = wide ? tile0 + tid : tid % fs.n_tiles;
   const bool active = wide || grp < fs.n_groups;
   const int step = wide ? 1 : fs.n_groups;
   double acc[2][4][4];
@@ -468,16 +480,16 @@ __global__ void __launch_bounds__(kFitThreads) refit_gram_kernel(const float* __
   const int64_t s_begin = (int64_t)split * per_split;
   const int64_t s_end = min(n, s_begin + per_split);
   __syncthreads();
-  for (int64_t c0 = s_begin; c0 < s_end; c0 += kFitSamples) {
-    {
-      const int row = tid % kFitSamples;
-      const bool is_new = tid < kFitSamples;
+  for (int64_t c0 = s_begin; c0 < s_end; c0 += CHUNK) {
+    if (tid < 2 * CHUNK) {
+      const int row = tid % CHUNK;
+      const bool is_new = tid < CHUNK;
       const int64_t s = c0 + row;
       double* dst = feat + row * fs.ld + (is_new ? 0 : fs.kn);
       if (s < s_end) {
         const double x = xt ? (double)xt[(int64_t)i * n + s] : __dadd_rn(lo, __dmul_rn(unit_linspace(s, n), span));
-        if (is_new) fit_eval(nb, tab_new, x, dst);
-        else fit_eval(ob, tab_old, x, dst);
+        if (is_new) fit_eval<MAXT>(nb, tab_new, x, dst);
+        else fit_eval<MAXT>(ob, tab_old, x, dst);
       } else {
         const int size = is_new ? fs.kn : fs.ko;
         for (int j = 0; j < size; ++j) dst[j] = 0.0;
@@ -488,9 +500,9 @@ __global__ void __launch_bounds__(kFitThreads) refit_gram_kernel(const float* __
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
         const int tile = my_tile + u * kFitThreads;
-        if (tile >= fs.n_tiles || (u == 1 && !wide)) continue;
+        if ((u == 1 && !wide) || tile >= fs.n_tiles || (wide && tile >= tile0 + kFitTileGroup)) continue;
         const int p0 = (tile / tq) * 4, q0 = (tile % tq) * 4;
-        for (int c = grp; c < kFitSamples; c += step) {
+        for (int c = grp; c < CHUNK; c += step) {
           const double* row = feat + c * fs.ld;
           const double2 a01 = *reinterpret_cast<const double2*>(row + p0);
           const double2 a23 = *reinterpret_cast<const double2*>(row + p0 + 2);
@@ -511,8 +523,8 @@ __global__ void __launch_bounds__(kFitThreads) refit_gram_kernel(const float* __
   if (wide) {
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
-      const int tile = tid + u * kFitThreads;
-      if (tile >= fs.n_tiles) continue;
+      const int tile = my_tile + u * kFitThreads;
+      if (tile >= fs.n_tiles || tile >= tile0 + kFitTileGroup) continue;
       const int p0 = (tile / tq) * 4, q0 = (tile % tq) * 4;
 #pragma unroll
       for (int r = 0; r < 4; ++r)
@@ -561,7 +573,7 @@ __global__ void __launch_bounds__(kFitThreads) refit_solve_kernel(const double* 
   double* V = A + kn * la;     // [kn][la]
   double* M = V + kn * la;     // [kn][ko]
   double* W = M + kn * ko;     // [kn][ko]
-  __shared__ double rot_c[KF_FIT_MAX_SIZE / 2], rot_s[KF_FIT_MAX_SIZE / 2], red[kFitThreads / 32];
+  __shared__ double rot_c[kFitSmall / 2], rot_s[kFitSmall / 2], red[kFitThreads / 32];
   __shared__ int stop;
   const int i = blockIdx.x, tid = threadIdx.x;
   const double* src = part + (int64_t)i * n_split * kn * kt;
@@ -684,20 +696,103 @@ __global__ void __launch_bounds__(kFitThreads) refit_solve_kernel(const double* 
   }
 }
 
+// Sizes above kFitSmall: G = sum of the split partials (+ ridge) factored in
+// place as L L^T (one CTA per input, G in the global workspace `gwork`), then
+// X = G^-1 M by forward and back substitution, one right-hand side per thread.
+// A pivot below kEigenCut of the largest diagonal entry marks a basis function
+// the samples do not determine: its row and column are dropped and its row of
+// X is zero (for functions no sample reaches, as in the minimum-norm solution).
+__global__ void __launch_bounds__(kFitThreads) refit_chol_kernel(const double* __restrict__ part, int n_split,
+                                                                  int64_t n, FitShape fs, double ridge,
+                                                                  double* __restrict__ gwork,
+                                                                  double* __restrict__ xmap) {
+  const int kn = fs.kn, ko = fs.ko, kt = fs.kt;
+  const int i = blockIdx.x, tid = threadIdx.x;
+  double* G = gwork + (int64_t)i * kn * kn;
+  double* X = xmap + (int64_t)i * kn * ko;
+  __shared__ double diag_max, pivot;
+  __shared__ unsigned char dropped[KF_FIT_MAX_SIZE];
+  const double* src = part + (int64_t)i * n_split * kn * kt;
+  for (int e = tid; e < kn * kt; e += blockDim.x) {
+    double v = 0.0;
+    for (int sp = 0; sp < n_split; ++sp) v += src[(int64_t)sp * kn * kt + e];
+    const int p = e / kt, q = e % kt;
+    if (q < kn) G[p * kn + q] = v;
+    else X[p * ko + (q - kn)] = v;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    double tr = 0.0, mx = 0.0;
+    for (int p = 0; p < kn; ++p) {
+      tr += G[p * kn + p];
+      mx = fmax(mx, G[p * kn + p]);
+    }
+    double lam2 = 0.0;
+    if (ridge > 0.0) {
+      const double lam = sqrt(ridge * (tr / ((double)n * kn)) * (double)n);
+      lam2 = lam * lam;
+      for (int p = 0; p < kn; ++p) G[p * kn + p] += lam2;
+    }
+    diag_max = mx + lam2;
+  }
+  __syncthreads();
+  const double cut = kEigenCut * diag_max;
+  for (int j = 0; j < kn; ++j) {
+    if (tid == 0) {
+      const double d = G[j * kn + j];
+      const bool drop = !(d > cut);
+      dropped[j] = drop;
+      pivot = drop ? 0.0 : sqrt(d);
+      G[j * kn + j] = pivot;
+    }
+    __syncthreads();
+    const double piv = pivot;
+    for (int r = j + 1 + tid; r < kn; r += blockDim.x) G[r * kn + j] = piv > 0.0 ? G[r * kn + j] / piv : 0.0;
+    __syncthreads();
+    // trailing update of the lower triangle: G[r][c] -= L[r][j] L[c][j], j < c <= r
+    const int m = kn - j - 1;
+    for (int e = tid; e < m * (m + 1) / 2; e += blockDim.x) {
+      int r = (int)((sqrt(8.0 * e + 1.0) - 1.0) * 0.5);
+      while ((r + 1) * (r + 2) / 2 <= e) ++r;
+      while (r * (r + 1) / 2 > e) --r;
+      const int c = e - r * (r + 1) / 2;
+      const int rr = j + 1 + r, cc = j + 1 + c;
+      G[rr * kn + cc] -= G[rr * kn + j] * G[cc * kn + j];
+    }
+    __syncthreads();
+  }
+  // forward substitution L y = m, then back substitution L^T x = y, per column
+  for (int c = tid; c < ko; c += blockDim.x) {
+    for (int r = 0; r < kn; ++r) {
+      double v = X[r * ko + c];
+      for (int q = 0; q < r; ++q) v -= G[r * kn + q] * X[q * ko + c];
+      X[r * ko + c] = dropped[r] ? 0.0 : v / G[r * kn + r];
+    }
+    for (int r = kn - 1; r >= 0; --r) {
+      double v = X[r * ko + c];
+      for (int q = r + 1; q < kn; ++q) v -= G[q * kn + r] * X[q * ko + c];
+      X[r * ko + c] = dropped[r] ? 0.0 : v / G[r * kn + r];
+    }
+  }
+}
+
 // coef_out[o, i, :] = X_i (coef[o, i, :] s) / safe(s), scale_out[o, i] = safe(s)
-// (kanforge/_layer.py:122-137).  One CTA per (32 outputs, input).
-template <typename T>
+// (kanforge/_layer.py:122-137).  One CTA per (32 outputs, input); X_i staged in
+// shared memory when it fits (XSMEM), else read through the caches.
+template <typename T, bool XSMEM>
 __global__ void __launch_bounds__(kFitThreads) refit_apply_kernel(const double* __restrict__ xmap,
                                                                    const T* __restrict__ coef,
                                                                    const T* __restrict__ scale, int32_t O, int32_t I,
                                                                    int kn, int ko, double* __restrict__ coef_out,
                                                                    double* __restrict__ scale_out) {
   extern __shared__ double asm_[];
-  double* X = asm_;                // [kn][ko]
-  double* ce = X + kn * ko;        // [32][ko]
+  double* ce = asm_;                          // [32][ko]
+  double* Xs = ce + 32 * ko;                  // [kn][ko] (XSMEM)
   __shared__ double safe[32];
   const int i = blockIdx.y, o0 = blockIdx.x * 32, tid = threadIdx.x;
-  for (int e = tid; e < kn * ko; e += blockDim.x) X[e] = xmap[(int64_t)i * kn * ko + e];
+  const double* X = XSMEM ? Xs : xmap + (int64_t)i * kn * ko;
+  if (XSMEM)
+    for (int e = tid; e < kn * ko; e += blockDim.x) Xs[e] = xmap[(int64_t)i * kn * ko + e];
   if (tid < 32) {
     const int o = o0 + tid;
     double s = 1.0;
@@ -850,8 +945,43 @@ extern "C" int kf_resample_grid(const double* grid, int32_t I, int32_t n_old, in
 extern "C" int64_t kf_refit_workspace(int64_t n, int32_t I, int32_t k_old, int32_t k_new) {
   if (n < 1 || I < 1 || k_old < 1 || k_new < 1) return 0;
   const int64_t splits = kf::fit_splits(n, I);
-  return (int64_t)sizeof(double) * I * ((int64_t)splits * k_new * (k_new + k_old) + (int64_t)k_new * k_old);
+  const bool small = k_old <= kf::kFitSmall && k_new <= kf::kFitSmall;
+  return (int64_t)sizeof(double) * I *
+         ((int64_t)splits * k_new * (k_new + k_old) + (int64_t)k_new * k_old + (small ? 0 : (int64_t)k_new * k_new));
 }
+
+namespace kf {
+namespace {
+
+template <typename T>
+int launch_apply(const FitShape& fs, const double* xmap, const void* coef, const void* scale, int32_t O, int32_t I,
+                 double* coef_out, double* scale_out, cudaStream_t s) {
+  const size_t ce = sizeof(double) * 32 * (size_t)fs.ko;
+  const size_t with_x = ce + sizeof(double) * (size_t)fs.kn * fs.ko;
+  const dim3 agrid((unsigned)cdiv(O, 32), (unsigned)I);
+  if (with_x <= 200 * 1024) {
+    if (int rc = set_smem((const void*)refit_apply_kernel<T, true>, with_x)) return rc;
+    refit_apply_kernel<T, true><<<agrid, kFitThreads, with_x, s>>>(xmap, (const T*)coef, (const T*)scale, O, I, fs.kn,
+                                                                    fs.ko, coef_out, scale_out);
+  } else {
+    if (int rc = set_smem((const void*)refit_apply_kernel<T, false>, ce)) return rc;
+    refit_apply_kernel<T, false><<<agrid, kFitThreads, ce, s>>>(xmap, (const T*)coef, (const T*)scale, O, I, fs.kn,
+                                                                 fs.ko, coef_out, scale_out);
+  }
+  return check_launch("kf_refit (apply)");
+}
+
+template <int CHUNK, int MAXT>
+int launch_gram(const FitShape& fs, dim3 grid, cudaStream_t s, const float* xt, const double* ranges, int64_t n,
+                const kf_fit_basis& nb, const kf_fit_basis& ob, int splits, int64_t per_split, double* part) {
+  const size_t smem = fit_gram_smem(fs);
+  if (int rc = set_smem((const void*)refit_gram_kernel<CHUNK, MAXT>, smem)) return rc;
+  refit_gram_kernel<CHUNK, MAXT><<<grid, kFitThreads, smem, s>>>(xt, ranges, n, nb, ob, fs, splits, per_split, part);
+  return check_launch("kf_refit (gram)");
+}
+
+}  // namespace
+}  // namespace kf
 
 extern "C" int kf_refit(const float* xt, const double* ranges, int64_t n, int32_t I, int32_t O,
                         const kf_fit_basis* old_basis, const kf_fit_basis* new_basis, const void* coef,
@@ -869,30 +999,27 @@ extern "C" int kf_refit(const float* xt, const double* ranges, int64_t n, int32_
   if (int rc = bind_device(coef)) return rc;
   cudaStream_t s = (cudaStream_t)stream;
   const FitShape fs = fit_shape(*new_basis, *old_basis);
+  KF_CHECK_ARG(fit_gram_smem(fs) <= 200 * 1024, "kf_refit: basis tables too large for shared memory");
   const int64_t splits = fit_splits(n, I);
   const int64_t per_split = cdiv(n, splits);
   double* part = (double*)workspace;
   double* xmap = part + (int64_t)I * splits * fs.kn * fs.kt;
-  const size_t gram_smem = fit_gram_smem(fs);
-  if (int rc = set_smem((const void*)refit_gram_kernel, gram_smem)) return rc;
-  refit_gram_kernel<<<dim3((unsigned)splits, (unsigned)I), kFitThreads, gram_smem, s>>>(
-      xt, ranges, n, *new_basis, *old_basis, fs, (int)splits, per_split, part);
-  if (int rc = check_launch("kf_refit (gram)")) return rc;
-  const size_t solve_smem = sizeof(double) * (2 * (size_t)fs.kn * (fs.kn + 1) + 2 * (size_t)fs.kn * fs.ko);
-  if (int rc = set_smem((const void*)refit_solve_kernel, solve_smem)) return rc;
-  refit_solve_kernel<<<(unsigned)I, kFitThreads, solve_smem, s>>>(part, (int)splits, n, fs, ridge, xmap);
-  if (int rc = check_launch("kf_refit (solve)")) return rc;
-  if (O == 0) return KF_OK;
-  const size_t apply_smem = sizeof(double) * ((size_t)fs.kn * fs.ko + 32 * (size_t)fs.ko);
-  const dim3 agrid((unsigned)cdiv(O, 32), (unsigned)I);
-  if (dtype == KF_DTYPE_F32) {
-    if (int rc = set_smem((const void*)refit_apply_kernel<float>, apply_smem)) return rc;
-    refit_apply_kernel<float><<<agrid, kFitThreads, apply_smem, s>>>(xmap, (const float*)coef, (const float*)edge_scale,
-                                                                     O, I, fs.kn, fs.ko, coef_out, scale_out);
+  double* gwork = xmap + (int64_t)I * fs.kn * fs.ko;
+  const dim3 ggrid((unsigned)splits, (unsigned)I, (unsigned)fs.tile_groups);
+  int rc;
+  if (fs.small) rc = launch_gram<128, kFitSmall>(fs, ggrid, s, xt, ranges, n, *new_basis, *old_basis, (int)splits, per_split, part);
+  else if (fs.chunk == 128) rc = launch_gram<128, KF_FIT_MAX_SIZE>(fs, ggrid, s, xt, ranges, n, *new_basis, *old_basis, (int)splits, per_split, part);
+  else rc = launch_gram<32, KF_FIT_MAX_SIZE>(fs, ggrid, s, xt, ranges, n, *new_basis, *old_basis, (int)splits, per_split, part);
+  if (rc) return rc;
+  if (fs.small) {
+    const size_t solve_smem = sizeof(double) * (2 * (size_t)fs.kn * (fs.kn + 1) + 2 * (size_t)fs.kn * fs.ko);
+    if (int r2 = set_smem((const void*)refit_solve_kernel, solve_smem)) return r2;
+    refit_solve_kernel<<<(unsigned)I, kFitThreads, solve_smem, s>>>(part, (int)splits, n, fs, ridge, xmap);
   } else {
-    if (int rc = set_smem((const void*)refit_apply_kernel<__nv_bfloat16>, apply_smem)) return rc;
-    refit_apply_kernel<__nv_bfloat16><<<agrid, kFitThreads, apply_smem, s>>>(
-        xmap, (const __nv_bfloat16*)coef, (const __nv_bfloat16*)edge_scale, O, I, fs.kn, fs.ko, coef_out, scale_out);
+    refit_chol_kernel<<<(unsigned)I, kFitThreads, 0, s>>>(part, (int)splits, n, fs, ridge, gwork, xmap);
   }
-  return check_launch("kf_refit (apply)");
+  if (int r2 = check_launch("kf_refit (solve)")) return r2;
+  if (O == 0) return KF_OK;
+  if (dtype == KF_DTYPE_F32) return launch_apply<float>(fs, xmap, coef, edge_scale, O, I, coef_out, scale_out, s);
+  return launch_apply<__nv_bfloat16>(fs, xmap, coef, edge_scale, O, I, coef_out, scale_out, s);
 }

@@ -240,3 +240,68 @@ def test_grid_tool_errors():
         kb.KANLinear(3, 2, kb.BSpline(4, 3), device=DEV).update_grid(x, grid_eps=0.0)
     with pytest.raises(NotImplementedError):
         kb.GRKAN(8, 8, groups=2, device=DEV).change_basis(kb.Chebyshev(3), torch.rand(10, 8, device=DEV))
+
+
+def _bspline_spec(g, k, rng=(-1.0, 1.0)):
+    return {"kind": "bspline", "grid_size": g, "order": k, "grid_range": rng}
+
+
+def test_refine_to_a_fine_grid_uses_the_large_solver():
+    """Grid extension 5 -> 100 intervals (103 functions per edge: the Cholesky
+    path above 64): nested grids keep the function, coefficients match lstsq."""
+    torch.manual_seed(4)
+    layer = kb.KANLinear(6, 5, kb.BSpline(5, 3), edge_scale=True, device=DEV)
+    with torch.no_grad():
+        layer.coef.normal_(0, 0.5)
+        layer.edge_scale.uniform_(0.5, 2)
+    old_grid = layer.basis_grid.double().cpu().numpy()
+    coef0 = layer.coef.detach().double().cpu().numpy()
+    scale0 = layer.edge_scale.detach().double().cpu().numpy()
+    x = torch.linspace(-1, 1, 401, device=DEV)[:, None].repeat(1, 6)
+    before = layer(x)
+    layer.refine_grid(100)
+    kb.kernels.check_device_errors()
+    assert layer.coef.shape == (5, 6, 103)
+    assert ko.max_rel_err(layer(x).detach().cpu().numpy(), before.detach().cpu().numpy()) <= FP32_TOL
+    new_grid = ko.resample_grid(old_grid, 101)
+    xs = ko.sample_inputs(np.stack([old_grid[:, 0], old_grid[:, -1]], -1), 8 * 103 + 64)
+    want, _ = ko.refit_layer(_bspline_spec(5, 3), {"grid": old_grid}, coef0, scale0, _bspline_spec(100, 3),
+                             {"grid": new_grid}, xs)
+    assert ko.max_rel_err(layer.coef.detach().double().cpu().numpy(), want) <= FP32_TOL
+
+
+def test_large_refit_drops_functions_no_sample_reaches():
+    """Samples in [-0.5, 0.5] only: the B-splines of a 150-interval grid outside
+    that range get coefficient 0, as in the reference's minimum-norm lstsq."""
+    torch.manual_seed(5)
+    layer = kb.KANLinear(3, 2, kb.BSpline(6, 3), device=DEV)
+    with torch.no_grad():
+        layer.coef.normal_(0, 0.5)
+    old_grid = layer.basis_grid.double().cpu().numpy()
+    coef0 = layer.coef.detach().double().cpu().numpy()
+    x = torch.rand(6000, 3, device=DEV) - 0.5
+    layer.refine_grid(150, x)
+    kb.kernels.check_device_errors()
+    got = layer.coef.detach().double().cpu().numpy()
+    want, _ = ko.refit_layer(_bspline_spec(6, 3), {"grid": old_grid}, coef0, None, _bspline_spec(150, 3),
+                             {"grid": ko.resample_grid(old_grid, 151)}, x.double().cpu().numpy())
+    assert ko.max_rel_err(got, want) <= FP32_TOL
+    assert (got[..., :30] == 0).all() and (got[..., -30:] == 0).all()
+
+
+def test_update_grid_on_a_fine_grid_matches_oracle():
+    torch.manual_seed(6)
+    layer = kb.KANLinear(8, 4, kb.BSpline(120, 3), device=DEV)
+    with torch.no_grad():
+        layer.coef.normal_(0, 0.3)
+    old_grid = layer.basis_grid.double().cpu().numpy()
+    coef0 = layer.coef.detach().double().cpu().numpy()
+    x = torch.randn(20000, 8, device=DEV) * 0.5
+    layer.update_grid(x)
+    kb.kernels.check_device_errors()
+    xs = x.double().cpu().numpy()
+    grid = ko.adaptive_grid(xs, 121)
+    assert torch.equal(layer.basis_grid.cpu(), torch.as_tensor(grid).float())
+    want, _ = ko.refit_layer(_bspline_spec(120, 3), {"grid": old_grid}, coef0, None, _bspline_spec(120, 3),
+                             {"grid": grid}, xs)
+    assert ko.max_rel_err(layer.coef.detach().double().cpu().numpy(), want) <= FP32_TOL

@@ -326,8 +326,8 @@ def test_grid_tools_validate_arguments_without_a_gpu():
     rat = _lib.FitBasis(kind=_lib.KF_BASIS_RATIONAL, size=1)
     rc = lib.kf_refit(ws, None, 10, 3, 2, ctypes.byref(rat), ctypes.byref(big), ws, None, 0, 0.0, ws, None, ws, None)
     assert rc == 2 and "no refit" in _lib.last_error()
-    with pytest.raises(ValueError, match="up to 64"):
-        kb.kernels.fit_basis(kb.plan_for(kb.BSpline(70, 3)), torch.zeros(3, 71, dtype=torch.float64), "cpu")
+    with pytest.raises(ValueError, match="up to 256"):
+        kb.kernels.fit_basis(kb.plan_for(kb.BSpline(300, 3)), torch.zeros(3, 301, dtype=torch.float64), "cpu")
 
 
 def test_grid_tools_fail_loudly_on_cpu():
