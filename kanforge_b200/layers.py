@@ -235,6 +235,15 @@ class KANLinear(nn.Module):
             # float32: three TF32 products per contraction on the tensor cores
             return _kernels.kan_linear_tf32(x, self.coef, silu_weight, self.bias, self.edge_scale, self.edge_mask,
                                             self._grid(), plan)
+        if plan.kind == "bspline" and x.dtype == torch.bfloat16 and self.coef.dtype == torch.bfloat16:
+            # bf16 B-spline layers the fused kernels do not take (more than 31
+            # features per input, or output counts they do not tile) compute in
+            # float32 on the sparse gather kernels
+            f = lambda t: None if t is None else t.float()  # noqa: E731
+            if _kernels.sparse_ok(plan, x.float(), self.out_features, torch.float32, False):
+                y = _kernels.kan_linear_sparse(x.float(), self.coef.float(), f(silu_weight), f(self.bias),
+                                               f(self.edge_scale), f(self.edge_mask), self._grid(), plan)
+                return y.to(x.dtype)
         if plan.kind == "bump" and x.dtype == torch.bfloat16 and _kernels.FP32_TENSOR_CORES:
             # bf16 bump layers (centres per input) compute in float32 on the three-TF32 GEMM
             f = lambda t: None if t is None else t.float()  # noqa: E731

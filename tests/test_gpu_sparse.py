@@ -150,3 +150,26 @@ def test_sparse_double_backward_matches_primitives():
     ed2 = ko.edge_derivative(xs, n["coef"], n["base_weight"], n["spec"], n["params"], 2, None, n["edge_mask"])
     close(gx, ed1.sum(-2), FP32_TOL, "dx")
     close(gxx, ed2.sum(-2), FP32_TOL, "d2x")
+
+
+@pytest.mark.parametrize("grid_size,n_out", [(40, 64), (100, 24), (5, 5)])
+def test_bf16_layers_outside_the_fused_kernels_run_sparse(grid_size, n_out):
+    """bf16 B-spline layers with more than 31 features per input or an output
+    count the fused kernels do not tile compute in float32 on the sparse
+    kernels (tolerance: bf16, 2e-2, against the oracle on the bf16 values)."""
+    torch.manual_seed(grid_size)
+    layer = kb.KANLinear(12, n_out, kb.BSpline(grid_size, 3), device=DEV, dtype=torch.bfloat16)
+    x = ((torch.rand(2000, 12, device=DEV) * 2.4 - 1.2).bfloat16()).requires_grad_()
+    with launches() as names:
+        y = layer(x)
+        g = torch.randn_like(y)
+        gx, gc = torch.autograd.grad(y, [x, layer.coef], g)
+    assert "kf_sparse_fwd" in names and y.dtype == torch.bfloat16, names
+    n = layer_numpy(layer)
+    xs, gs = x.detach().double().cpu().numpy(), g.double().cpu().numpy()
+    close(y, ko.kan_linear(xs, n["coef"], n["base_weight"], n["bias"], n["spec"], n["params"], None, n["edge_mask"]),
+          2e-2, "y")
+    want = ko.kan_linear_backward(xs, gs, n["coef"], n["base_weight"], n["bias"], n["spec"], n["params"], None,
+                                  n["edge_mask"])
+    close(gx, want["dx"], 2e-2, "dx")
+    close(gc, want["dcoef"], 2e-2, "dcoef")
