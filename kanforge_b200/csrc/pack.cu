@@ -32,9 +32,25 @@ __global__ void __launch_bounds__(kPackThreads) pack_kernel(const T* __restrict_
     // effective coefficients coef * edge_scale * edge_mask (kanforge/torch/layers.py:162-167)
     const float mk = mask ? to_f32(mask[e]) : 1.0f;
     const float sm = mk * (scale ? to_f32(scale[e]) : 1.0f);
+    __nv_bfloat16* dst = packed + e * f_pad;
+    if (!has_fold) {
+      // no fold: column j is coefficient j (read straight from memory, no per-thread array)
+      for (int j0 = 0; j0 < f_pad; j0 += 8) {
+        __align__(16) __nv_bfloat16 tmp[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int j = j0 + u;
+          float v = 0.0f;
+          if (j < nt) v = j < K ? to_f32(c[j]) * sm : 0.0f;
+          else if (j == f_pad - 1 && base != nullptr) v = to_f32(base[e]) * mk;
+          tmp[u] = __float2bfloat16_rn(v);
+        }
+        *reinterpret_cast<uint4*>(dst + j0) = *reinterpret_cast<const uint4*>(tmp);
+      }
+      continue;
+    }
     float cv[kMaxFold];
     for (int k = 0; k < K; ++k) cv[k] = to_f32(c[k]) * sm;
-    __nv_bfloat16* dst = packed + e * f_pad;
     for (int j0 = 0; j0 < f_pad; j0 += 8) {
       __align__(16) __nv_bfloat16 tmp[8];
 #pragma unroll
