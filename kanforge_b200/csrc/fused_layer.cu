@@ -883,12 +883,13 @@ __global__ void __launch_bounds__(dgrad_threads(BK), 1) fused_dgrad_kernel(const
           for (int u = u0; u < u0 + kHalfIn; ++u)
             xr[u] = (row_ok && i_base + u < p.I) ? __bfloat162float(p.x[b * p.I + i_base + u]) : 0.0f;
         }
-        float dxv[IPT];
-  #pragma unroll 1
-        for (int c = 4 * h2; c < 4 * h2 + 4; ++c) {
+        float dxv[kHalfIn];  // this set's inputs u0 .. u0 + kHalfIn - 1 (static indices: the chunk loop unrolls)
+  #pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          const int c = 4 * h2 + cc;
           float v[32];
           tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + acc * kBN + c * 32, v);
-          if (c == 4 * h2 + 3) {
+          if (cc == 3) {
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(&ctl->acc_empty[acc], 0);
@@ -904,9 +905,7 @@ __global__ void __launch_bounds__(dgrad_threads(BK), 1) fused_dgrad_kernel(const
               float s = 0.0f;
   #pragma unroll
               for (int j = 0; j < F; ++j) s = fmaf(v[h * F + j], df[j], s);
-  #pragma unroll
-              for (int uu = 0; uu < IPT; ++uu)
-                if (uu == u) dxv[uu] = s;
+              dxv[(cc * 32) / F + h] = s;
             }
           } else {
             // stage the 32 columns of this row, then dot with the local derivative window
@@ -934,9 +933,7 @@ __global__ void __launch_bounds__(dgrad_threads(BK), 1) fused_dgrad_kernel(const
                 }
                 if (p.bd.has_base) s = fmaf(wst[lane * 33 + h * F + F - 1], dsilu_fast(xval), s);
               }
-  #pragma unroll
-              for (int uu = 0; uu < IPT; ++uu)
-                if (uu == u) dxv[uu] = s;
+              dxv[(cc * 32) / F + h] = s;
             }
             __syncwarp();
           }
@@ -946,18 +943,13 @@ __global__ void __launch_bounds__(dgrad_threads(BK), 1) fused_dgrad_kernel(const
           if (i_base + u0 + kHalfIn <= p.I && ((p.I | i_base) % 2) == 0) {
   #pragma unroll
             for (int k2 = 0; k2 < kHalfIn / 2; ++k2) {
-              float lo = 0.0f, hi = 0.0f;
-  #pragma unroll
-              for (int uu = 0; uu < IPT; ++uu) {
-                if (uu == u0 + 2 * k2) lo = dxv[uu];
-                if (uu == u0 + 2 * k2 + 1) hi = dxv[uu];
-              }
+              const float lo = dxv[2 * k2], hi = dxv[2 * k2 + 1];
               reinterpret_cast<uint32_t*>(dst)[k2] = pack_bf16x2(lo, hi);
             }
           } else {
   #pragma unroll
-            for (int uu = 0; uu < IPT; ++uu)
-              if (uu >= u0 && uu < u0 + kHalfIn && i_base + uu < p.I) p.dx[b * p.I + i_base + uu] = __float2bfloat16_rn(dxv[uu]);
+            for (int k = 0; k < kHalfIn; ++k)
+              if (i_base + u0 + k < p.I) p.dx[b * p.I + i_base + u0 + k] = __float2bfloat16_rn(dxv[k]);
           }
         }
       }
