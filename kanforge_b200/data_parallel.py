@@ -22,6 +22,11 @@ The sum runs in the gradients' dtype (bf16 for bf16 layers): NCCL adds the
 ranks' bf16 values, so each element carries about one bf16 rounding per rank
 of relative error; the 2-GPU test holds the result to 2e-2 of the one-GPU
 full-batch gradient.
+
+Grid updates (``update_grid``) adapt each layer's grid to its input samples;
+on sharded batches every rank would adapt to its own shard and the replicas
+would drift apart.  ``update_grid(model, x)`` gathers the ranks' samples
+first, so every rank computes the same grids and refit from the whole batch.
 """
 
 from __future__ import annotations
@@ -81,6 +86,22 @@ class GradientSync:
         rest = [p for p in self.params if p.grad is not None and id(p) not in self._done]
         allreduce_gradients(rest, group=self.group)
         return False
+
+
+def gather_samples(x: torch.Tensor, group=None) -> torch.Tensor:
+    """The ranks' sample batches concatenated along the first dimension, in rank
+    order, on every rank (one all-gather; every rank passes the same shape)."""
+    world = dist.get_world_size(group)
+    x = x.contiguous()
+    out = torch.empty((world * x.shape[0],) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
+    dist.all_gather_into_tensor(out, x, group=group)
+    return out
+
+
+def update_grid(model, x: torch.Tensor, group=None, **kwargs) -> None:
+    """``model.update_grid`` on the samples of all ranks (a KANLinear or a KAN):
+    the replicas keep identical grids and coefficients."""
+    model.update_grid(gather_samples(x, group), **kwargs)
 
 
 def max_over_ranks(value: float, device, group=None) -> float:

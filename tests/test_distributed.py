@@ -1,7 +1,8 @@
 """Multi-rank plumbing on CPU (gloo, world size 2): the gradient all-reduce and
-the max-over-ranks timing used by bench.py, and a rank that fails before the
-collective, which the other rank must see as an error within the process-group
-timeout instead of hanging."""
+the max-over-ranks timing used by bench.py, the sample gather of the
+data-parallel grid update, and a rank that fails before the collective, which
+the other rank must see as an error within the process-group timeout instead
+of hanging."""
 
 from __future__ import annotations
 
@@ -120,3 +121,44 @@ def test_gradient_sync_reduces_every_gradient_once():
         assert torch.equal(e, torch.full((3,), 3.0))
         assert torch.equal(l_, torch.full((2,), 30.0))
         assert unhooked
+
+
+class _RecordingModel:
+    """Stands in for a KAN model: records the samples its grid update sees."""
+
+    def __init__(self):
+        self.seen = None
+        self.kwargs = None
+
+    def update_grid(self, x, **kwargs):
+        self.seen = x.clone()
+        self.kwargs = kwargs
+
+
+def _gather_worker(rank, world, port, out):
+    """update_grid on sharded batches: every rank adapts to all ranks' samples,
+    in rank order, so the replicas keep identical grids."""
+    _init(rank, world, port)
+    try:
+        from kanforge_b200.data_parallel import gather_samples, update_grid
+
+        x = torch.arange(12, dtype=torch.float32).reshape(3, 4) + 100.0 * rank
+        full = gather_samples(x)
+        model = _RecordingModel()
+        update_grid(model, x[:, :2], margin=0.5)
+        out[rank] = (full.clone(), model.seen, model.kwargs)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_update_grid_gathers_every_ranks_samples():
+    world, port = 2, _free_port()
+    out = mp.Manager().dict()
+    mp.spawn(_gather_worker, args=(world, port, out), nprocs=world, join=True)
+    base = torch.arange(12, dtype=torch.float32).reshape(3, 4)
+    want = torch.cat([base + 100.0 * r for r in range(world)])
+    for rank in range(world):
+        full, seen, kwargs = out[rank]
+        assert torch.equal(full, want)
+        assert torch.equal(seen, want[:, :2])
+        assert kwargs == {"margin": 0.5}

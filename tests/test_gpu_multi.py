@@ -96,3 +96,43 @@ def test_two_gpu_gradients_equal_full_batch(kind, reserve):
                 assert err <= 2e-2, f"rank {rank} {name} ({how}): max rel err {err:.3e}"
         for name in full:  # both ranks hold the same sum
             assert torch.equal(out[0][0][name], out[1][0][name])
+
+
+def _grid_worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev, timeout=datetime.timedelta(seconds=60))
+    try:
+        import kanforge_b200 as kb
+        from kanforge_b200.data_parallel import update_grid
+
+        def model():
+            torch.manual_seed(0)
+            return kb.KAN([64, 32, 16], kb.BSpline(8, 3), device=dev)
+
+        g = torch.Generator().manual_seed(2)
+        x = (torch.randn(4096, 64, generator=g) * 1.5).to(dev)
+        dp = model()
+        update_grid(dp, x[rank * 2048:(rank + 1) * 2048])
+        out[rank] = {n: t.detach().cpu().clone() for n, t in dp.state_dict().items()}
+        if rank == 0:
+            full = model()
+            full.update_grid(x)
+            out["full"] = {n: t.detach().cpu().clone() for n, t in full.state_dict().items()}
+        torch.cuda.synchronize()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(600)
+def test_two_gpu_grid_update_equals_full_batch():
+    """data_parallel.update_grid on a batch split over two ranks leaves both
+    replicas with the grids and coefficients of the whole-batch update on one
+    GPU, bit for bit (the device update is deterministic)."""
+    out = mp.Manager().dict()
+    mp.spawn(_grid_worker, args=(2, _free_port(), out), nprocs=2, join=True)
+    full = out["full"]
+    for rank in range(2):
+        for name, want in full.items():
+            assert torch.equal(out[rank][name], want), f"rank {rank} {name}"
