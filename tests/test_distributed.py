@@ -47,7 +47,7 @@ def _allreduce_worker(rank, world, port, out):
 
 def test_gradient_allreduce_and_max_over_ranks():
     world, port = 2, _free_port()
-    out = mp.Manager().dict()
+    out = mp.get_context("spawn").Manager().dict()  # no fork after CUDA is up
     mp.spawn(_allreduce_worker, args=(world, port, out), nprocs=world, join=True)
     for rank in range(world):
         g1, g2, g3, t = out[rank]
@@ -73,7 +73,7 @@ def _failing_worker(rank, world, port, out):
 
 def test_lost_rank_is_an_error_not_a_hang():
     world, port = 2, _free_port()
-    out = mp.Manager().dict()
+    out = mp.get_context("spawn").Manager().dict()  # no fork after CUDA is up
     ctx = mp.get_context("spawn")
     procs = [ctx.Process(target=_failing_worker, args=(r, world, port, out)) for r in range(world)]
     for p in procs:
@@ -114,7 +114,7 @@ def _sync_worker(rank, world, port, out):
 
 def test_gradient_sync_reduces_every_gradient_once():
     world, port = 2, _free_port()
-    out = mp.Manager().dict()
+    out = mp.get_context("spawn").Manager().dict()  # no fork after CUDA is up
     mp.spawn(_sync_worker, args=(world, port, out), nprocs=world, join=True)
     for rank in range(world):
         e, l_, unhooked = out[rank]
@@ -153,7 +153,7 @@ def _gather_worker(rank, world, port, out):
 
 def test_update_grid_gathers_every_ranks_samples():
     world, port = 2, _free_port()
-    out = mp.Manager().dict()
+    out = mp.get_context("spawn").Manager().dict()  # no fork after CUDA is up
     mp.spawn(_gather_worker, args=(world, port, out), nprocs=world, join=True)
     base = torch.arange(12, dtype=torch.float32).reshape(3, 4)
     want = torch.cat([base + 100.0 * r for r in range(world)])

@@ -85,7 +85,7 @@ def _worker(rank, world, port, kind, reserve, out):
 @pytest.mark.timeout(600)
 @pytest.mark.parametrize("kind,reserve", [("cheb", 0), ("cheb", 16), ("bspline", 0), ("grkan", 0)])
 def test_two_gpu_gradients_equal_full_batch(kind, reserve):
-    out = mp.Manager().dict()
+    out = mp.get_context("spawn").Manager().dict()  # no fork after CUDA is up
     mp.spawn(_worker, args=(2, _free_port(), kind, reserve, out), nprocs=2, join=True)
     full = out["full"]
     for rank in range(2):
@@ -130,7 +130,7 @@ def test_two_gpu_grid_update_equals_full_batch():
     """data_parallel.update_grid on a batch split over two ranks leaves both
     replicas with the grids and coefficients of the whole-batch update on one
     GPU, bit for bit (the device update is deterministic)."""
-    out = mp.Manager().dict()
+    out = mp.get_context("spawn").Manager().dict()  # no fork after CUDA is up
     mp.spawn(_grid_worker, args=(2, _free_port(), out), nprocs=2, join=True)
     full = out["full"]
     for rank in range(2):
