@@ -2117,7 +2117,11 @@ static int kf_dgrad_impl(const kf::ConvDev* conv, const void* x, const void* dy,
   p.k_steps = (int)cdiv(O, kBK);
   p.tiles.m_tiles = (int)cdiv(B, kPairM);
   p.tiles.n_tiles = (int)cdiv((int64_t)I * f_pad, kBN);
-  p.tiles.gm = std::min(p.tiles.m_tiles, 8);
+  // Super-rows of 16 pair M tiles: their dy panels (16 x 256 rows x O) stay
+  // in L2 while the super-row streams every coefficient block once.  At the
+  // 4096 Chebyshev layer (2 MB panels) 16 measured faster than 8, 32 and 64
+  // (the L2 serves data shared by both dies at about half its capacity).
+  p.tiles.gm = std::min(p.tiles.m_tiles, 16);
   p.tab_ts = (p.bd.nk + 3) & ~3;
   CUtensorMap tdy, tc;
   if (int rc = make_tmap_bf16(&tdy, dy, B, O, kBK, kBM)) return rc;
