@@ -14,8 +14,10 @@ Two ways to sum the gradients, both in place (no flattened copy):
   has written them, and their all-reduce runs on NCCL's stream while the
   input-gradient kernel runs (kernels.set_grad_ready_hook); what no layer
   handed over is reduced when the context exits.  With
-  ``reserved_sms`` the persistent kernels leave that many SMs to NCCL
-  (kernels.set_reserved_sms).  It needs ``p.grad is None`` at the start of the
+  ``reserved_sms`` the persistent kernels launched after the first all-reduce
+  was issued (the input gradients) leave that many SMs to NCCL
+  (kernels.set_reserved_sms); a persistent kernel holding every SM would
+  otherwise keep NCCL's kernel waiting until it ends.  It needs ``p.grad is None`` at the start of the
   backward (no gradient accumulation across micro-batches).
 
 The sum runs in the gradients' dtype (bf16 for bf16 layers): NCCL adds the
@@ -68,13 +70,13 @@ class GradientSync:
                 continue  # reduced already, or will accumulate into an existing gradient: left to the exit
             self._done.add(id(p))
             works.append(dist.all_reduce(g, op=dist.ReduceOp.SUM, group=self.group, async_op=True))
+        if works and self.reserved_sms:
+            _kernels.set_reserved_sms(self.reserved_sms)  # from the next launch on, beside the all-reduce
         return works
 
     def __enter__(self):
         self._done.clear()
         _kernels.set_grad_ready_hook(self._ready)
-        if self.reserved_sms:
-            _kernels.set_reserved_sms(self.reserved_sms)
         return self
 
     def __exit__(self, exc_type, exc, tb):
