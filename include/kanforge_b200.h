@@ -147,6 +147,17 @@ int kf_fwd(const void* x, const void* feat, const void* packed, const void* bias
            int32_t I, int32_t O, int32_t nt, int32_t f_pad, int32_t has_base, const kf_basis_desc* basis,
            void* stream);
 
+/* kf_fwd (feat null) that also writes the basis feature matrix of x, (B, I * f_pad)
+ * bf16 as kf_features lays it out, for the coefficient gradient: the forward's
+ * producer warps evaluate every feature row anyway, so the backward need not
+ * evaluate them again.  KF_BASIS_CHEB and KF_BASIS_FOURIER only.  Same reference
+ * interface as kf_fwd (kanforge/torch/layers.py:177-191); the kept matrix is
+ * this library's (the reference evaluates the basis in each Triton launch,
+ * kanforge/kernels/triton_kernels.py:122-124). */
+int kf_fwd_emit_features(const void* x, const void* packed, const void* bias, const float* knot_tab, void* y,
+                         void* feat_out, int64_t B, int32_t I, int32_t O, int32_t nt, int32_t f_pad, int32_t has_base,
+                         const kf_basis_desc* basis, void* stream);
+
 /* Fused input gradient on tcgen05:
  *   dx[b,i] = sum_j (sum_o dy[b,o] packed[o,i,j]) dfeat_j(x[b,i])
  * dfeat = d/dx of the forward features (the SiLU column included).

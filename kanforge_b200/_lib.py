@@ -120,6 +120,10 @@ PROTOTYPES = {
         ctypes.c_int,
         [_vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, ctypes.POINTER(BasisDesc), _vp],
     ),
+    "kf_fwd_emit_features": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, ctypes.POINTER(BasisDesc), _vp],
+    ),
     "kf_dgrad": (
         ctypes.c_int,
         [_vp, _vp, _vp, _vp, _vp, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, ctypes.POINTER(BasisDesc), _vp],

@@ -264,6 +264,11 @@ struct FwdParams {
   TileMap tiles;
   BasisDev bd;
   ConvDev conv;  // active: x is an image read through the implicit patch matrix
+  // Closed-form plans, optional: for the first output tile of each token tile
+  // the producers also store their feature stages here (TMA, by tmap_a),
+  // (B, I * F) bf16 row-major, the layout kf_features writes for the
+  // coefficient gradient.
+  __nv_bfloat16* feat_out;
 };
 
 constexpr int kFwdThreads = 768;  // w0 TMA, w1 MMA (CTA 0), w4-7 epilogue, w8-23 producers (4 groups)
@@ -482,6 +487,8 @@ __global__ void __launch_bounds__(A_TMA ? kFwdTmaThreads : kFwdThreads, 1)
     static_assert(A_TMA || NS % kFwdGroups == 0, "each producer group owns whole stages");
     const int grp = (warp - 8) / 4;
     const int row = ((warp - 8) % 4) * 32 + lane;
+    const bool group_lead = row == 0;  // issues the group's feature stores (kf_fwd_emit_features)
+    bool store_pending = false;        // a store from the group's stage may still be reading it
     int it = 0;
     bool alive = true;
     for (int t = pair; t < n_tiles && alive; t += n_pairs) {  // abort is seen (warp-uniformly) by the waits
@@ -490,6 +497,8 @@ __global__ void __launch_bounds__(A_TMA ? kFwdTmaThreads : kFwdThreads, 1)
       const int64_t b = (int64_t)m * kPairM + (int64_t)rank * kBM + row;
       const bool row_ok = b < p.B;
       const unsigned short* xrow = reinterpret_cast<const unsigned short*>(p.x) + (row_ok ? b : 0) * p.I;
+      // the token tile's features go to the feature matrix once: from its tile of output block 0
+      const bool emit = is_closed(BK) && !A_TMA && p.feat_out != nullptr && n == 0;
       int k = ((grp - it) % kFwdGroups + kFwdGroups) % kFwdGroups;
       unsigned short xa[IPK], xb[IPK];
 #pragma unroll
@@ -508,6 +517,12 @@ __global__ void __launch_bounds__(A_TMA ? kFwdTmaThreads : kFwdThreads, 1)
                       ? (p.conv.active ? x_bits(p.x, p.conv, b, inext + u, p.I) : __ldg(xrow + inext + u)) : 0;
         bool ok = mbar_wait_warp(&ctl->empty[s], ph ^ 1, abort);
         if constexpr (BK > 0) ok = ok && mbar_wait_warp(&ctl->tab_full[s], ph, abort);  // tables landed
+        if (emit || store_pending) {
+          // the group's last store from this stage has read it; the four warps agree on ok
+          if (group_lead) bulk_wait_read_all();
+          ok = named_bar_and(2 + grp, 128, ok);
+          store_pending = false;
+        }
         if (!ok) {
           alive = false;
           break;
@@ -565,6 +580,13 @@ __global__ void __launch_bounds__(A_TMA ? kFwdTmaThreads : kFwdThreads, 1)
         }
         fence_proxy_async_smem();
         __syncwarp();
+        if (emit) {
+          // the stage as the four warps wrote it (128 rows x 64 columns, 128-byte
+          // swizzle, the layout of tmap_a's box); rows past B are not stored
+          named_bar(2 + grp, 128);
+          if (group_lead) tma_store_2d(&tmap_a, arow, k * kBK, (int)((int64_t)m * kPairM + rank * kBM));
+          store_pending = true;
+        }
         if (lane == 0) {
           if (rank == 0)
             mbar_arrive(&ctl->full_a[s]);
@@ -576,6 +598,7 @@ __global__ void __launch_bounds__(A_TMA ? kFwdTmaThreads : kFwdThreads, 1)
       }
       it += p.k_steps;
     }
+    if (group_lead && p.feat_out != nullptr) bulk_wait_all();  // shared memory stays until the stores are done
   }
 
   tc_fence_before();
@@ -2058,7 +2081,7 @@ int grkan_check(const kf_basis_desc* d, int64_t B, int I, int O, const char* who
 
 static int kf_fwd_impl(const kf::ConvDev* conv, const void* x, const void* feat, const void* packed, const void* bias, const float* knot_tab, void* y, int64_t B,
                       int32_t I, int32_t O, int32_t nt, int32_t f_pad, int32_t has_base, const kf_basis_desc* basis,
-                      void* stream) {
+                      void* stream, void* feat_out = nullptr) {
   using namespace kf;
   clear_error();
   KF_CHECK_ARG(x && packed && y, "kf_fwd: null tensor pointer");
@@ -2093,6 +2116,14 @@ static int kf_fwd_impl(const kf::ConvDev* conv, const void* x, const void* feat,
     tmap_a = tmap;  // unused
   }
   if (conv) p.conv = *conv;
+  if (feat_out) {
+    KF_CHECK_ARG(!conv && !feat && (basis->kind == KF_BASIS_CHEB || basis->kind == KF_BASIS_FOURIER),
+                 "kf_fwd_emit_features: Chebyshev-feature or Fourier plans of the plain layer only");
+    KF_CHECK_ARG(((uintptr_t)feat_out % 16) == 0, "kf_fwd_emit_features: feat_out must be 16-byte aligned");
+    p.feat_out = (__nv_bfloat16*)feat_out;
+    // the producers store their A stages through this map (the box the TMA-fed forward loads)
+    if (int rc = make_tmap_bf16(&tmap_a, feat_out, B, (int64_t)I * f_pad, kBK, kBM)) return rc;
+  }
   FwdLaunch L{&tmap, &tmap_a, p, feat != nullptr, (cudaStream_t)stream};
   return dispatch_fused(basis, f_pad, L);
 }
@@ -2428,6 +2459,14 @@ extern "C" int kf_fwd(const void* x, const void* feat, const void* packed, const
                       int64_t B, int32_t I, int32_t O, int32_t nt, int32_t f_pad, int32_t has_base, const kf_basis_desc* basis,
                       void* stream) {
   return kf_fwd_impl(nullptr, x, feat, packed, bias, knot_tab, y, B, I, O, nt, f_pad, has_base, basis, stream);
+}
+
+extern "C" int kf_fwd_emit_features(const void* x, const void* packed, const void* bias, const float* knot_tab, void* y,
+                                    void* feat_out, int64_t B, int32_t I, int32_t O, int32_t nt, int32_t f_pad,
+                                    int32_t has_base, const kf_basis_desc* basis, void* stream) {
+  kf::clear_error();
+  KF_CHECK_ARG(feat_out && basis, "kf_fwd_emit_features: null pointer");
+  return kf_fwd_impl(nullptr, x, nullptr, packed, bias, knot_tab, y, B, I, O, nt, f_pad, has_base, basis, stream, feat_out);
 }
 
 extern "C" int kf_dgrad(const void* x, const void* dy, const void* packed, const float* knot_tab, void* dx, int64_t B,

@@ -43,14 +43,15 @@ def set_launch_observer(fn) -> None:
 _KERNELS_PER_CALL = {"kf_rational_bwd": 2, "kf_rational_bwd_noalloc": 2, "kf_grkan_dgrad": 2}
 
 
-def _launch(name: str, *args, kernels: int | None = None) -> None:
-    """Call entry point `name`; `kernels` overrides how many kernels it launches."""
+def _launch(name: str, *args, kernels: int | None = None, label: str | None = None) -> None:
+    """Call entry point `name`; `kernels` overrides how many kernels it launches,
+    `label` the name the launch observer records (a variant of another entry)."""
     global LAUNCH_COUNT
     LAUNCH_COUNT += kernels if kernels is not None else _KERNELS_PER_CALL.get(name, 1)
     if _observer is None:
         _lib.call(name, *args)
         return
-    with _observer(name):
+    with _observer(label or name):
         _lib.call(name, *args)
 
 
@@ -303,6 +304,24 @@ WGRAD_FEATURE_BYTES_MAX = 16 << 30
 # the forward kernel's producer warps.
 FEATURES_IN_FORWARD = ("bspline",)
 
+# Plan kinds whose forward producer warps, which evaluate every feature row,
+# also write the feature matrix (kf_fwd_emit_features) when the coefficient
+# gradient will need it and it fits this budget: the backward then skips
+# kf_features.  The matrix is held from the forward to the backward, like an
+# activation (2.1 GB at 16384 tokens x 4096 inputs).
+FEATURES_EMITTED_BY_FORWARD = ("cheb", "fourier")
+FORWARD_FEATURE_BYTES_MAX = 4 << 30
+
+
+def _emitted_features(x, f_pad):
+    """An empty (B, I * f_pad) bf16 matrix for the forward to fill, or None."""
+    if x.shape[0] * x.shape[1] * f_pad * 2 > FORWARD_FEATURE_BYTES_MAX:
+        return None
+    try:
+        return torch.empty(x.shape[0], x.shape[1] * f_pad, device=x.device, dtype=_BF16)
+    except torch.cuda.OutOfMemoryError:
+        return None
+
 
 def wgrad_features(x, knot_tab, nt, f_pad, has_base, desc, stream):
     """The feature matrix of x for kf_wgrad, or None for its self-evaluating path."""
@@ -340,9 +359,18 @@ class _FusedKANLinear(torch.autograd.Function):
         g = None if grid is None else grid.detach().float().contiguous()
         tab = None if grid is None else knot_tables(g, plan)
         desc = plan.desc()
-        feat = wgrad_features(x, tab, nt, f_pad, has_base, desc, _stream(x)) if plan.kind in FEATURES_IN_FORWARD else None
-        _launch("kf_fwd", _ptr(x), _ptr(feat), _ptr(packed), _ptr(b), _ptr(tab), _ptr(y), x.shape[0], n_in, n_out, nt,
-                f_pad, int(has_base), ctypes.byref(desc), _stream(x))
+        need = ctx.needs_input_grad
+        feat = None
+        if plan.kind in FEATURES_IN_FORWARD:
+            feat = wgrad_features(x, tab, nt, f_pad, has_base, desc, _stream(x))
+        elif plan.kind in FEATURES_EMITTED_BY_FORWARD and (need[1] or need[2] or need[4]):
+            feat = _emitted_features(x, f_pad)
+        if feat is not None and plan.kind in FEATURES_EMITTED_BY_FORWARD:
+            _launch("kf_fwd_emit_features", _ptr(x), _ptr(packed), _ptr(b), _ptr(tab), _ptr(y), _ptr(feat), x.shape[0],
+                    n_in, n_out, nt, f_pad, int(has_base), ctypes.byref(desc), _stream(x), label="kf_fwd")
+        else:
+            _launch("kf_fwd", _ptr(x), _ptr(feat), _ptr(packed), _ptr(b), _ptr(tab), _ptr(y), x.shape[0], n_in, n_out, nt,
+                    f_pad, int(has_base), ctypes.byref(desc), _stream(x))
         ctx.save_for_backward(x, coef, base_weight, edge_scale, edge_mask, g)
         ctx.packed, ctx.knot_tab, ctx.plan, ctx.has_bias = packed, tab, plan, bias is not None
         ctx.feat = feat
