@@ -45,9 +45,9 @@ TRAFFIC_PER_LAUNCH: dict[tuple[int, str], float] = {
     (1, "kf_wgrad"): (3946.0 + 22.2) * 1e6,
     (1, "kf_features"): (138.0 + 2085.2) * 1e6,
     (1, "kf_gemm_tf32x3"): (6613.7 + 1529.3) * 1e6,  # float32, mean of the three contractions
-    (2, "kf_fwd"): 2059422208 + 118561536,
-    (2, "kf_wgrad"): (15260092672 + 15981035008) / 2 + (467704064 + 464687616) / 2,  # mean of two launches
-    (2, "kf_dgrad"): 3311955456 + 132527360,
+    (2, "kf_fwd"): 1968659712 + 2267541760,  # the forward also writes the 2.15 GB feature matrix
+    (2, "kf_wgrad"): 11694444544 + 464463872,
+    (2, "kf_dgrad"): 2874828800 + 132429824,
     (2, "kf_features"): 134248192 + 2084940544,
     (3, "kf_rational_act"): (125.9 + 78.8) * 1e6,  # mean of the two layers
     (3, "kf_rational_bwd"): (251.7 + 99.6 + 9.1) * 1e6,  # with the reduction, mean of the two layers
