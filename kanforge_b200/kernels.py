@@ -296,7 +296,8 @@ def pack_coef(coef, base, edge_scale, edge_mask, plan: KernelPlan, f_pad: int) -
 # whose features are costly to evaluate inside the forward's producer warps,
 # the matrix is made in the forward, read there by TMA too, and kept until the
 # backward (activation memory traded for one evaluation instead of one per
-# output tile); Chebyshev-feature plans make it in the backward.
+# output tile); Chebyshev-feature and Fourier plans have the forward kernel
+# write it (FEATURES_EMITTED_BY_FORWARD below), or make it in the backward.
 WGRAD_FEATURE_BYTES_MAX = 16 << 30
 
 # Plan kinds whose bf16 forward makes the feature matrix and reads it by TMA
