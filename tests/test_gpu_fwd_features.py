@@ -27,9 +27,9 @@ def _layer(basis, n_in, n_out):
 
 
 @pytest.mark.parametrize("basis,n_in,n_out,batch", [
-    (kb.Chebyshev(12), 256, 512, 777),   # ragged token tile, two 512-output tiles... of one
+    (kb.Chebyshev(12), 256, 512, 777),   # a ragged last token tile, one 512-output tile
     (kb.Chebyshev(5), 100, 264, 300),    # tail K step (inputs not a multiple of 4)
-    (kb.Fourier(6), 128, 1024, 513),
+    (kb.Fourier(6), 128, 1024, 513),     # two output tiles: only the first stores features
 ])
 def test_emitted_features_equal_kf_features_and_y_equals_kf_fwd(basis, n_in, n_out, batch):
     layer = _layer(basis, n_in, n_out)
